@@ -1,0 +1,793 @@
+/* TEST INFRASTRUCTURE ONLY (see ppocr_oracle.h): the CPU oracle.
+ *
+ * Arithmetic follows the reference's tier 3 (AVX2+FMA) scalar definitions:
+ * every convolution output adds its taps in kernel row-major order, each
+ * tap's channels in order, one fused multiply-add each
+ * (`kernels/dense.rs:104-141`, `kernels/depthwise.rs:12-45`,
+ * `kernels/pointwise.rs:20-44`), with the bias first or last where the
+ * reference's tiles put it (`bias_first` below). One detail is not
+ * restated: the reference's pointwise kernels also add the bias last on the
+ * few pixels a call leaves after its 12- and 4-pixel tiles
+ * (`pointwise.rs:131-185`), which depends on how its executor splits rows;
+ * those outputs differ from this restatement by at most one rounding.
+ *
+ * Compiled with -ffp-contract=off: a product and a sum written apart stay two
+ * roundings, as Rust keeps them; fmaf() marks every fused one.
+ */
+#include "ppocr_oracle.h"
+
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+enum {
+    K_CONV, K_DWCONV, K_ADD, K_MAXPOOL, K_AVGPOOL, K_CHANNELMUL, K_CONCATC,
+    K_LAYERNORM, K_ATTENTION, K_MEAN, K_CTCHEAD, K_CTCARGMAX, K_UPSAMPLE,
+    K_UPSAMPLEADD, K_CONVTRANSPOSE, K_COUNT
+};
+enum { A_NONE, A_RELU, A_SIGMOID, A_GELU, A_SWISH, A_HARDSIGMOID, A_HARDSIGMOIDFIFTH,
+       A_HARDSWISH, A_COUNT };
+
+#define OP_FIELDS 20
+#define MAX_SCRATCH_FLOATS ((size_t)1 << 30) /* plan.rs:73 */
+#define MAX_WINDOW ((size_t)1 << 16)         /* plan.rs:77 */
+
+typedef struct {
+    int kind, fused;
+    size_t x, x2, y, ih, iw, ic, oh, ow, oc, kh, kw, sh, sw;
+    long pt, pb, pl, pr;
+    size_t n2, w0, w1, b0, b1;
+} orc_op;
+
+struct orc_plan {
+    size_t slot, h, w, c;
+    size_t nbuf, nout, nops;
+    size_t *outputs, *out_n, *pool;
+    orc_op *ops;
+    float *weights;
+    size_t nweights;
+};
+
+/* ---------------------------------------------------------------- errors */
+
+static int fail(char *err, size_t len, const char *fmt, ...) {
+    if (err && len) {
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(err, len, fmt, ap);
+        va_end(ap);
+    }
+    return -1;
+}
+
+/* ------------------------------------------------------------ activations */
+
+static inline float f_of(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline uint32_t u_of(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+
+/* XNNPACK f32-vsigmoid "p5-div" exp constants, kernels/activation.rs:10-21. */
+#define EXP_MAGIC_BIAS f_of(0x4b40007fu)
+#define LOG2E f_of(0x3fb8aa3bu)
+#define MINUS_LN2 f_of(0xbf317218u)
+#define EXP_C5 f_of(0x3c07cfceu)
+#define EXP_C4 f_of(0x3d2b9d0du)
+#define EXP_C3 f_of(0x3e2aad40u)
+#define EXP_C2 f_of(0x3efffee3u)
+#define EXP_C1 f_of(0x3f7ffffbu)
+#define EXP_CUTOFF f_of(0xc2aeac4fu)
+
+/* exp(z) for z <= 0, the FMA (tier 3) form: activation.rs:37-60. */
+float orc_exp_neg(float z) {
+    float n = fmaf(z, LOG2E, EXP_MAGIC_BIAS);
+    float s = f_of(u_of(n) << 23);
+    n = n - EXP_MAGIC_BIAS;
+    float t = fmaf(n, MINUS_LN2, z);
+    float p = fmaf(fmaf(fmaf(fmaf(EXP_C5, t, EXP_C4), t, EXP_C3), t, EXP_C2), t, EXP_C1);
+    if (z < EXP_CUTOFF) return 0.0f;
+    return fmaf(t * s, p, s);
+}
+
+/* Rust's f32::clamp: NaN passes through. */
+static inline float clampf(float v, float lo, float hi) {
+    if (v < lo) v = lo;
+    if (v > hi) v = hi;
+    return v;
+}
+
+/* activation.rs:151-159 */
+static inline float sigmoid_one(float x) {
+    float e = orc_exp_neg(f_of(u_of(x) | 0x80000000u));
+    float f = e / (e + 1.0f);
+    return (u_of(x) >> 31) ? f : 1.0f - f;
+}
+
+/* layers.rs:20-40, 54-67 */
+static const uint32_t PHI_P[6] = {0x3ecc4228u, 0x3d0aa93cu, 0x3b9943c9u,
+                                  0x39310738u, 0x36d52462u, 0x32c36a3cu};
+static const uint32_t PHI_Q[5] = {0x3e80c788u, 0x3ceaaaeeu, 0x3af6ffc6u,
+                                  0x389a737au, 0x35a0b9e3u};
+static inline float gelu_one(float x) {
+    float c = clampf(x, -5.5f, 5.5f);
+    float s = c * c;
+    float p = f_of(PHI_P[5]);
+    for (int k = 4; k >= 0; k--) p = fmaf(p, s, f_of(PHI_P[k]));
+    float q = f_of(PHI_Q[4]);
+    for (int k = 3; k >= 0; k--) q = fmaf(q, s, f_of(PHI_Q[k]));
+    q = fmaf(q, s, 1.0f);
+    return x * clampf(fmaf(c, p / q, 0.5f), 0.0f, 1.0f);
+}
+
+#define HARDSIGMOID_ALPHA f_of(0x3e2aaaadu) /* layers.rs:42 */
+
+/* conv.rs:36-72 (Tail::apply) with the clamp of relu folded in. */
+float orc_activation(int code, float v) {
+    switch (code) {
+    case A_RELU: return clampf(v, 0.0f, INFINITY);
+    case A_SIGMOID: return sigmoid_one(v);
+    case A_GELU: return gelu_one(v);
+    case A_SWISH: return v * sigmoid_one(v); /* layers.rs:70 */
+    case A_HARDSIGMOID: return clampf(v * HARDSIGMOID_ALPHA + 0.5f, 0.0f, 1.0f); /* :215 */
+    case A_HARDSIGMOIDFIFTH: return clampf(v * 0.2f + 0.5f, 0.0f, 1.0f);        /* :222 */
+    case A_HARDSWISH: /* extension code 7: x * hardsigmoid(x) */
+        return v * clampf(v * HARDSIGMOID_ALPHA + 0.5f, 0.0f, 1.0f);
+    default: return v;
+    }
+}
+
+static void tail(float *y, size_t n, int code) {
+    if (code == A_NONE) return;
+    for (size_t i = 0; i < n; i++) y[i] = orc_activation(code, y[i]);
+}
+
+/* ------------------------------------------------------------------ parse */
+
+static int shape_len(size_t a, size_t b, size_t c, size_t *out) {
+    if (!a || !b || !c) return 0;
+    if (a > SIZE_MAX / b) return 0;
+    size_t ab = a * b;
+    if (ab > SIZE_MAX / c) return 0;
+    *out = ab * c;
+    return 1;
+}
+
+static int produced(const orc_plan *p, size_t before, size_t slot, size_t *h, size_t *w, size_t *c) {
+    for (size_t i = before; i-- > 0;) {
+        if (p->ops[i].y == slot) {
+            *h = p->ops[i].oh; *w = p->ops[i].ow; *c = p->ops[i].oc;
+            return 1;
+        }
+    }
+    if (slot == p->slot) { *h = p->h; *w = p->w; *c = p->c; return 1; }
+    return 0;
+}
+
+static int window_len(size_t n, long before, long after, size_t k, size_t s, size_t *out) {
+    if (before < 0 || after < 0 || s == 0) return 0;
+    size_t span = n + (size_t)before + (size_t)after;
+    if (span < k) return 0;
+    *out = (span - k) / s + 1;
+    return 1;
+}
+
+/* plan.rs:414-494 */
+static int derive_shapes(orc_plan *p, size_t height, size_t width, char *err, size_t el) {
+    p->h = height; p->w = width;
+    for (size_t i = 0; i < p->nops; i++) {
+        size_t h, w, c;
+        if (!produced(p, i, p->ops[i].x, &h, &w, &c))
+            return fail(err, el, "op %zu reads a buffer nothing wrote", i);
+        orc_op *op = &p->ops[i];
+        if (c != op->ic) return fail(err, el, "op %zu reads a tensor of another shape", i);
+        size_t oh = h, ow = w;
+        switch (op->kind) {
+        case K_CONV: case K_DWCONV: case K_MAXPOOL: case K_AVGPOOL:
+            if (!window_len(h, op->pt, op->pb, op->kh, op->sh, &oh) ||
+                !window_len(w, op->pl, op->pr, op->kw, op->sw, &ow))
+                return fail(err, el, "op %zu has a window larger than its padded input", i);
+            break;
+        case K_UPSAMPLE: case K_UPSAMPLEADD:
+            if ((op->sh && h > SIZE_MAX / op->sh) || (op->sw && w > SIZE_MAX / op->sw))
+                return fail(err, el, "op %zu output size overflows", i);
+            oh = h * op->sh; ow = w * op->sw; break;
+        case K_CONVTRANSPOSE:
+            if ((op->kh && h > SIZE_MAX / op->kh) || (op->kw && w > SIZE_MAX / op->kw))
+                return fail(err, el, "op %zu output size overflows", i);
+            oh = h * op->kh; ow = w * op->kw; break;
+        case K_MEAN: oh = 1; ow = 1; break;
+        default: break;
+        }
+        int has2 = 1;
+        size_t wh = 0, ww = 0, wc = 0;
+        switch (op->kind) {
+        case K_ADD: case K_UPSAMPLEADD: wh = oh; ww = ow; wc = op->oc; break;
+        case K_CONCATC: wh = oh; ww = ow; wc = op->n2; break;
+        case K_CHANNELMUL: wh = 1; ww = 1; wc = op->oc; break;
+        case K_CONV: if (op->n2 > 0) { wh = h; ww = w; wc = op->n2; } else has2 = 0; break;
+        default: has2 = 0;
+        }
+        if (has2) {
+            size_t h2, w2, c2;
+            if (!produced(p, i, op->x2, &h2, &w2, &c2) || h2 != wh || w2 != ww || c2 != wc)
+                return fail(err, el, "op %zu reads a second tensor of another shape", i);
+        }
+        op->ih = h; op->iw = w; op->oh = oh; op->ow = ow;
+    }
+    memset(p->pool, 0, p->nbuf * sizeof(size_t));
+    size_t image;
+    if (!shape_len(height, width, p->c, &image)) return fail(err, el, "input shape is zero or overflows");
+    if (p->slot >= p->nbuf) return fail(err, el, "buffer %zu does not exist", p->slot);
+    if (p->pool[p->slot] < image) p->pool[p->slot] = image;
+    for (size_t i = 0; i < p->nops; i++) {
+        size_t n;
+        if (!shape_len(p->ops[i].oh, p->ops[i].ow, p->ops[i].oc, &n))
+            return fail(err, el, "op %zu output shape is zero or overflows", i);
+        if (p->ops[i].y >= p->nbuf) return fail(err, el, "buffer %zu does not exist", p->ops[i].y);
+        if (p->pool[p->ops[i].y] < n) p->pool[p->ops[i].y] = n;
+    }
+    for (size_t k = 0; k < p->nout; k++) {
+        size_t h, w, c;
+        if (!produced(p, p->nops, p->outputs[k], &h, &w, &c))
+            return fail(err, el, "output %zu is never written", k);
+        p->out_n[k] = h * w * c;
+    }
+    return 0;
+}
+
+static int has_second(const orc_op *op) {
+    return op->kind == K_ADD || op->kind == K_CHANNELMUL || op->kind == K_CONCATC ||
+           op->kind == K_UPSAMPLEADD || (op->kind == K_CONV && op->n2 > 0);
+}
+static int is_pointwise(const orc_op *op) {
+    return op->kind == K_CONV && op->kh == 1 && op->kw == 1 && op->sh == 1 && op->sw == 1 &&
+           !op->pt && !op->pb && !op->pl && !op->pr;
+}
+
+/* plan.rs:498-767, the rules the executor relies on. */
+static int check(const orc_plan *p, char *err, size_t el) {
+    for (size_t b = 0; b < p->nbuf; b++)
+        if (p->pool[b] > MAX_SCRATCH_FLOATS)
+            return fail(err, el, "a buffer wants %zu floats", p->pool[b]);
+    size_t input_len;
+    if (!shape_len(p->h, p->w, p->c, &input_len)) return fail(err, el, "input shape is zero");
+    if (p->pool[p->slot] < input_len) return fail(err, el, "input buffer smaller than the image");
+    for (size_t k = 0; k < p->nout; k++) {
+        if (p->outputs[k] >= p->nbuf) return fail(err, el, "an output names a missing buffer");
+        if (p->pool[p->outputs[k]] < p->out_n[k]) return fail(err, el, "output %zu too large", k);
+    }
+    for (size_t i = 0; i < p->nops; i++) {
+        const orc_op *op = &p->ops[i];
+        size_t in_len, out_len;
+        if (!shape_len(op->ih, op->iw, op->ic, &in_len)) return fail(err, el, "op %zu input shape is zero", i);
+        if (!shape_len(op->oh, op->ow, op->oc, &out_len)) return fail(err, el, "op %zu output shape is zero", i);
+        switch (op->kind) {
+        case K_CONV: case K_DWCONV: case K_AVGPOOL: case K_MAXPOOL:
+            if (!op->kh || !op->kw || !op->sh || !op->sw || op->kh > MAX_WINDOW || op->kw > MAX_WINDOW ||
+                op->sh > MAX_WINDOW || op->sw > MAX_WINDOW || op->pt < 0 || op->pb < 0 || op->pl < 0 ||
+                op->pr < 0 || (size_t)op->pt > MAX_WINDOW || (size_t)op->pb > MAX_WINDOW ||
+                (size_t)op->pl > MAX_WINDOW || (size_t)op->pr > MAX_WINDOW)
+                return fail(err, el, "op %zu has an unsupported kernel, stride or padding", i);
+            break;
+        case K_MEAN:
+            if (op->oh != 1 || op->ow != 1 || op->ic != op->oc) return fail(err, el, "op %zu invalid mean", i);
+            break;
+        case K_CONCATC:
+            if (op->ih != op->oh || op->iw != op->ow || op->ic + op->n2 != op->oc)
+                return fail(err, el, "op %zu invalid concatenation", i);
+            break;
+        case K_CTCHEAD: case K_CTCARGMAX: {
+            size_t vocab = op->kind == K_CTCHEAD ? op->oc : op->n2;
+            size_t cols = (vocab + 15) / 16 * 16;
+            if (op->ih != 1 || op->oh != 1 || op->iw != op->ow || !vocab ||
+                (op->kind == K_CTCARGMAX && op->oc != 2) || cols * op->ic != op->w1 || op->b1 != cols)
+                return fail(err, el, "op %zu invalid CTC head", i);
+            break;
+        }
+        case K_LAYERNORM:
+            if (op->oc * 2 + 1 != op->w1) return fail(err, el, "op %zu needs gamma, beta and epsilon", i);
+            break;
+        case K_ATTENTION:
+            if (op->ih != 1 || op->oh != 1 || op->iw != op->ow || op->oc * 3 != op->ic || !op->n2 ||
+                op->oc % op->n2 || op->w1 != 1 || op->iw * op->iw > MAX_SCRATCH_FLOATS)
+                return fail(err, el, "op %zu invalid attention shape", i);
+            break;
+        case K_UPSAMPLE: case K_UPSAMPLEADD:
+            if (op->ic != op->oc || !op->sh || !op->sw || op->ih * op->sh != op->oh || op->iw * op->sw != op->ow)
+                return fail(err, el, "op %zu invalid upsampling", i);
+            break;
+        case K_CONVTRANSPOSE: {
+            size_t cols = op->kh * op->kw * op->oc;
+            if (!op->kh || !op->kw || op->sh != op->kh || op->sw != op->kw || op->pt || op->pb || op->pl ||
+                op->pr || op->ih * op->kh != op->oh || op->iw * op->kw != op->ow || cols * op->ic != op->w1 ||
+                (op->b1 && op->b1 != cols))
+                return fail(err, el, "op %zu invalid transposed convolution", i);
+            break;
+        }
+        default: break;
+        }
+        if ((op->kind == K_ADD || op->kind == K_CHANNELMUL || op->kind == K_LAYERNORM) &&
+            (op->ih != op->oh || op->iw != op->ow || op->ic != op->oc))
+            return fail(err, el, "op %zu elementwise shapes differ", i);
+        if (op->kind == K_AVGPOOL &&
+            (op->ic != op->oc || op->pt || op->pb || op->pl || op->pr || op->kh > op->ih || op->kw > op->iw ||
+             op->oh != (op->ih - op->kh) / op->sh + 1 || op->ow != (op->iw - op->kw) / op->sw + 1))
+            return fail(err, el, "op %zu average pool requires complete valid windows", i);
+        if (op->kind == K_MAXPOOL) {
+            if (op->ic != op->oc || op->pt || op->pl) return fail(err, el, "op %zu maxpool padding", i);
+            if ((op->oh - 1) * op->sh >= op->ih || (op->ow - 1) * op->sw >= op->iw)
+                return fail(err, el, "op %zu maxpool contains an empty output window", i);
+        }
+        if (is_pointwise(op) && (op->ih != op->oh || op->iw != op->ow))
+            return fail(err, el, "op %zu pointwise changes spatial dimensions", i);
+        if (op->x >= p->nbuf || p->pool[op->x] < in_len) return fail(err, el, "op %zu reads past its input", i);
+        if (op->y >= p->nbuf || p->pool[op->y] < out_len) return fail(err, el, "op %zu writes past its output", i);
+        if (op->y == op->x || (has_second(op) && op->x2 == op->y))
+            return fail(err, el, "op %zu writes the buffer it reads", i);
+        if (has_second(op)) {
+            size_t need = op->oc;
+            if (op->kind == K_ADD || op->kind == K_UPSAMPLEADD) need = out_len;
+            else if (op->kind == K_CONCATC) need = op->oh * op->ow * op->n2;
+            else if (op->kind == K_CONV) need = op->ih * op->iw * op->n2;
+            if (op->x2 >= p->nbuf || p->pool[op->x2] < need) return fail(err, el, "op %zu reads past its second input", i);
+        }
+        if (op->kind == K_CONV || op->kind == K_DWCONV) {
+            size_t taps = op->kh * op->kw, want;
+            if (op->n2 > 0 && (op->kind == K_DWCONV || is_pointwise(op)))
+                return fail(err, el, "op %zu reads a second input it cannot", i);
+            if (op->kind == K_DWCONV) {
+                if (op->ic != op->oc) return fail(err, el, "op %zu depthwise changes channels", i);
+                want = taps * op->oc;
+            } else {
+                want = (op->ic + op->n2) * taps * op->oc;
+            }
+            if (op->w1 != want) return fail(err, el, "op %zu: %zu weights for a shape needing %zu", i, op->w1, want);
+            if (op->b1 && op->b1 != op->oc) return fail(err, el, "op %zu has a bias of the wrong length", i);
+        }
+        int weighted = op->kind == K_CONV || op->kind == K_DWCONV || op->kind == K_LAYERNORM ||
+                       op->kind == K_ATTENTION || op->kind == K_CTCHEAD || op->kind == K_CTCARGMAX ||
+                       op->kind == K_CONVTRANSPOSE;
+        if (!weighted && (op->w1 || op->b1)) return fail(err, el, "op %zu has weights it does not use", i);
+        if (op->fused != A_NONE && !(op->kind == K_CONV || op->kind == K_DWCONV || op->kind == K_ADD ||
+                                     op->kind == K_CONVTRANSPOSE))
+            return fail(err, el, "op %zu has an invalid folded activation", i);
+        if (op->w1 && op->w0 + op->w1 > p->nweights) return fail(err, el, "op %zu weights past the end", i);
+        if (op->b1 && op->b0 + op->b1 > p->nweights) return fail(err, el, "op %zu bias past the end", i);
+    }
+    return 0;
+}
+
+orc_plan *orc_load(const uint8_t *bytes, size_t len, char *err, size_t el) {
+    if (len < 8 || memcmp(bytes, "PPOCRPL1", 8)) { fail(err, el, "not a ppocr-native plan"); return NULL; }
+    size_t at = 8;
+#define NEXT(v)                                                              \
+    do {                                                                     \
+        if (at + 4 > len) { fail(err, el, "the description is truncated"); goto bad; } \
+        uint32_t w_; memcpy(&w_, bytes + at, 4); at += 4; (v) = w_;          \
+    } while (0)
+    orc_plan *p = calloc(1, sizeof *p);
+    if (!p) return NULL;
+    size_t nops;
+    NEXT(p->slot); NEXT(p->h); NEXT(p->w); NEXT(p->c); NEXT(p->nbuf); NEXT(p->nout); NEXT(nops);
+    if (p->nout > len / 4 || nops > len / 80) { fail(err, el, "the description is truncated"); goto bad; }
+    p->outputs = calloc(p->nout + 1, sizeof(size_t));
+    p->out_n = calloc(p->nout + 1, sizeof(size_t));
+    p->ops = calloc(nops + 1, sizeof(orc_op));
+    if (!p->outputs || !p->out_n || !p->ops) goto bad;
+    for (size_t k = 0; k < p->nout; k++) NEXT(p->outputs[k]);
+    for (size_t i = 0; i < nops; i++) {
+        size_t f[OP_FIELDS];
+        for (int j = 0; j < OP_FIELDS; j++) NEXT(f[j]);
+        if (f[0] >= K_COUNT) { fail(err, el, "operation kind %zu is unknown", f[0]); goto bad; }
+        if (f[1] >= A_COUNT) { fail(err, el, "activation %zu is unknown", f[1]); goto bad; }
+        orc_op *op = &p->ops[i];
+        op->kind = (int)f[0]; op->fused = (int)f[1];
+        op->x = f[2]; op->x2 = f[3]; op->y = f[4]; op->ic = f[5]; op->oc = f[6];
+        op->kh = f[7]; op->kw = f[8]; op->sh = f[9]; op->sw = f[10];
+        op->pt = (long)f[11]; op->pb = (long)f[12]; op->pl = (long)f[13]; op->pr = (long)f[14];
+        op->n2 = f[15]; op->w0 = f[16]; op->w1 = f[17]; op->b0 = f[18]; op->b1 = f[19];
+    }
+#undef NEXT
+    p->nops = nops;
+    if (p->nbuf == 0 || p->nbuf > nops + 1) { fail(err, el, "%zu buffers for %zu operations", p->nbuf, nops); goto bad; }
+    size_t start = (at + 63) / 64 * 64;
+    if (start > len) { fail(err, el, "the plan ends before its weights"); goto bad; }
+    size_t raw = len - start;
+    if (raw % 4) { fail(err, el, "the weights are not a whole number of floats"); goto bad; }
+    p->nweights = raw / 4;
+    p->weights = malloc((p->nweights + 1) * sizeof(float));
+    p->pool = calloc(p->nbuf, sizeof(size_t));
+    if (!p->weights || !p->pool) goto bad;
+    for (size_t i = 0; i < p->nweights; i++) {
+        float v;
+        memcpy(&v, bytes + start + 4 * i, 4);
+        if (isnan(v) || isinf(v)) { fail(err, el, "the weights hold a non-finite value at float %zu", i); goto bad; }
+        if (fpclassify(v) == FP_SUBNORMAL) v = copysignf(0.0f, v); /* plan.rs:819-842 */
+        p->weights[i] = v;
+    }
+    if (derive_shapes(p, p->h, p->w, err, el) || check(p, err, el)) goto bad;
+    for (size_t i = 0; i < p->nops; i++)
+        if (p->ops[i].kind == K_LAYERNORM && p->weights[p->ops[i].w0 + 2 * p->ops[i].oc] <= 0.0f) {
+            fail(err, el, "layer normalization epsilon is not positive");
+            goto bad;
+        }
+    return p;
+bad:
+    orc_free(p);
+    return NULL;
+}
+
+void orc_free(orc_plan *p) {
+    if (!p) return;
+    free(p->outputs); free(p->out_n); free(p->pool); free(p->ops); free(p->weights);
+    free(p);
+}
+
+int orc_set_size(orc_plan *p, size_t h, size_t w, char *err, size_t el) {
+    size_t oh = p->h, ow = p->w;
+    if (derive_shapes(p, h, w, err, el) == 0 && check(p, err, el) == 0) return 0;
+    char scratch[8];
+    derive_shapes(p, oh, ow, scratch, sizeof scratch);
+    return -1;
+}
+
+size_t orc_input_len(const orc_plan *p) { return p->h * p->w * p->c; }
+size_t orc_output_count(const orc_plan *p) { return p->nout; }
+size_t orc_output_len(const orc_plan *p, size_t k) { return k < p->nout ? p->out_n[k] : 0; }
+
+/* ------------------------------------------------------------------ layers */
+
+static const float *W(const orc_plan *p, size_t at) { return p->weights + at; }
+
+/* Where the reference's tier-3 kernels add a convolution's bias: first for
+ * RGB stems (conv.rs:171-177), for pointwise layers whose output width is a
+ * multiple of 16 (pointwise.rs:77-102) and for windowed ones of such width
+ * except the last `ow % 4` pixels of each row (dense.rs:60-66); last
+ * otherwise (pointwise.rs:33-35, dense.rs:127-130). */
+static int bias_first(const orc_op *op, size_t ox) {
+    if (!is_pointwise(op) && op->ic == 3 && op->n2 == 0) return 1;
+    if (op->oc % 16) return 0;
+    if (is_pointwise(op)) return 1;
+    return ox < op->ow - op->ow % 4;
+}
+
+/* Dense convolution of any window over the channel concatenation of x (ic
+ * channels) and x2 (n2 channels): kernels/dense.rs:20-141 and the stem path
+ * conv.rs:146-236. Weights [kh][kw][ic+n2][oc]; padded taps are skipped (the
+ * reference multiplies them by zeros, which leaves every sum unchanged). */
+static void conv(const orc_plan *p, const orc_op *op, const float *x, const float *x2, float *y) {
+    const float *w = W(p, op->w0), *b = op->b1 ? W(p, op->b0) : NULL;
+    size_t co = op->oc, ch = op->ic + op->n2;
+    long rows = (long)op->oh;
+#pragma omp parallel for schedule(static)
+    for (long oy = 0; oy < rows; oy++) {
+        for (size_t ox = 0; ox < op->ow; ox++) {
+            float *acc = y + ((size_t)oy * op->ow + ox) * co;
+            int first = bias_first(op, ox);
+            for (size_t o = 0; o < co; o++) acc[o] = (b && first) ? b[o] : 0.0f;
+            for (size_t ky = 0; ky < op->kh; ky++) {
+                long iy = oy * (long)op->sh + (long)ky - op->pt;
+                if (iy < 0 || iy >= (long)op->ih) continue;
+                for (size_t kx = 0; kx < op->kw; kx++) {
+                    long ix = (long)(ox * op->sw + kx) - op->pl;
+                    if (ix < 0 || ix >= (long)op->iw) continue;
+                    const float *tap = w + (ky * op->kw + kx) * ch * co;
+                    const float *px = x + ((size_t)iy * op->iw + (size_t)ix) * op->ic;
+                    for (size_t i = 0; i < op->ic; i++) {
+                        float v = px[i];
+                        const float *row = tap + i * co;
+                        for (size_t o = 0; o < co; o++) acc[o] = fmaf(row[o], v, acc[o]);
+                    }
+                    if (op->n2) {
+                        const float *px2 = x2 + ((size_t)iy * op->iw + (size_t)ix) * op->n2;
+                        for (size_t i = 0; i < op->n2; i++) {
+                            float v = px2[i];
+                            const float *row = tap + (op->ic + i) * co;
+                            for (size_t o = 0; o < co; o++) acc[o] = fmaf(row[o], v, acc[o]);
+                        }
+                    }
+                }
+            }
+            if (b && !first)
+                for (size_t o = 0; o < co; o++) acc[o] += b[o];
+            tail(acc, co, op->fused);
+        }
+    }
+}
+
+/* Depthwise convolution: conv.rs:244-339, kernels/depthwise.rs:12-45 —
+ * bias first, taps in row-major order, one fused multiply-add per tap. */
+static void dwconv(const orc_plan *p, const orc_op *op, const float *x, float *y) {
+    const float *w = W(p, op->w0), *b = op->b1 ? W(p, op->b0) : NULL;
+    size_t c = op->oc;
+    long rows = (long)op->oh;
+#pragma omp parallel for schedule(static)
+    for (long oy = 0; oy < rows; oy++) {
+        for (size_t ox = 0; ox < op->ow; ox++) {
+            float *acc = y + ((size_t)oy * op->ow + ox) * c;
+            for (size_t k = 0; k < c; k++) acc[k] = b ? b[k] : 0.0f;
+            for (size_t ky = 0; ky < op->kh; ky++) {
+                long iy = oy * (long)op->sh + (long)ky - op->pt;
+                if (iy < 0 || iy >= (long)op->ih) continue;
+                for (size_t kx = 0; kx < op->kw; kx++) {
+                    long ix = (long)(ox * op->sw + kx) - op->pl;
+                    if (ix < 0 || ix >= (long)op->iw) continue;
+                    const float *tap = w + (ky * op->kw + kx) * c;
+                    const float *px = x + ((size_t)iy * op->iw + (size_t)ix) * c;
+                    for (size_t k = 0; k < c; k++) acc[k] = fmaf(tap[k], px[k], acc[k]);
+                }
+            }
+            tail(acc, c, op->fused);
+        }
+    }
+}
+
+/* conv.rs:404-440: windows cut short at the bottom and right edges; the
+ * first tap is copied, later ones kept only when greater
+ * (kernels/elementwise.rs:101-115). */
+static void maxpool(const orc_op *op, const float *x, float *y) {
+    size_t c = op->oc;
+    for (size_t oy = 0; oy < op->oh; oy++)
+        for (size_t ox = 0; ox < op->ow; ox++) {
+            float *out = y + (oy * op->ow + ox) * c;
+            int seeded = 0;
+            for (size_t ky = 0; ky < op->kh; ky++) {
+                size_t iy = oy * op->sh + ky;
+                if (iy >= op->ih) continue;
+                for (size_t kx = 0; kx < op->kw; kx++) {
+                    size_t ix = ox * op->sw + kx;
+                    if (ix >= op->iw) continue;
+                    const float *src = x + (iy * op->iw + ix) * c;
+                    if (!seeded) { memcpy(out, src, c * sizeof(float)); seeded = 1; }
+                    else for (size_t k = 0; k < c; k++) if (src[k] > out[k]) out[k] = src[k];
+                }
+            }
+        }
+}
+
+/* layers.rs:443-463: taps summed in row-major order, then divided. */
+static void avgpool(const orc_op *op, const float *x, float *y) {
+    float divisor = (float)(op->kh * op->kw);
+    for (size_t oy = 0; oy < op->oh; oy++)
+        for (size_t ox = 0; ox < op->ow; ox++) {
+            float *out = y + (oy * op->ow + ox) * op->oc;
+            for (size_t k = 0; k < op->oc; k++) out[k] = 0.0f;
+            for (size_t ky = 0; ky < op->kh; ky++)
+                for (size_t kx = 0; kx < op->kw; kx++) {
+                    const float *src = x + ((oy * op->sh + ky) * op->iw + ox * op->sw + kx) * op->ic;
+                    for (size_t k = 0; k < op->ic; k++) out[k] += src[k];
+                }
+            for (size_t k = 0; k < op->oc; k++) out[k] /= divisor;
+        }
+}
+
+/* layers.rs:391-406: pixels summed in order in f64, then divided. */
+static void mean(const orc_op *op, const float *x, float *y) {
+    size_t c = op->ic, pixels = op->ih * op->iw;
+    double *sums = calloc(c, sizeof(double));
+    for (size_t px = 0; px < pixels; px++)
+        for (size_t k = 0; k < c; k++) sums[k] += (double)x[px * c + k];
+    for (size_t k = 0; k < c; k++) y[k] = (float)(sums[k] / (double)pixels);
+    free(sums);
+}
+
+/* layers.rs:467-479 */
+static void layernorm(const orc_plan *p, const orc_op *op, const float *x, float *y) {
+    size_t c = op->oc;
+    const float *gamma = W(p, op->w0), *beta = gamma + c;
+    float eps = gamma[2 * c];
+    for (size_t px = 0; px < op->oh * op->ow; px++) {
+        const float *v = x + px * c;
+        float s = 0.0f;
+        for (size_t k = 0; k < c; k++) s += v[k];
+        float m = s / (float)c;
+        float q = 0.0f;
+        for (size_t k = 0; k < c; k++) { float d = v[k] - m; q += d * d; }
+        float var = q / (float)c;
+        float r = sqrtf(var + eps);
+        for (size_t k = 0; k < c; k++) y[px * c + k] = (v[k] - m) / r * gamma[k] + beta[k];
+    }
+}
+
+/* layers.rs:254-294 (softmax_scalar, tier 3): maximum and sum in 8 lanes over
+ * the whole groups of eight, the lanes then folded in order, the rest added
+ * one value at a time; then multiplied by the reciprocal of the sum. */
+static void softmax_row(float *v, size_t n) {
+    size_t body = n / 8 * 8;
+    float lanes[8];
+    for (int l = 0; l < 8; l++) lanes[l] = -INFINITY;
+    for (size_t j = 0; j < body; j++) { float a = lanes[j % 8]; lanes[j % 8] = a > v[j] ? a : v[j]; }
+    float mx = -INFINITY;
+    for (int l = 0; l < 8; l++) mx = fmaxf(mx, lanes[l]);
+    for (size_t j = body; j < n; j++) mx = fmaxf(mx, v[j]);
+    float sums[8] = {0};
+    for (size_t j = 0; j < body; j++) { v[j] = orc_exp_neg(v[j] - mx); sums[j % 8] += v[j]; }
+    float sum = 0.0f;
+    for (int l = 0; l < 8; l++) sum += sums[l];
+    for (size_t j = body; j < n; j++) { v[j] = orc_exp_neg(v[j] - mx); sum += v[j]; }
+    float r = 1.0f / sum;
+    for (size_t j = 0; j < n; j++) v[j] *= r;
+}
+
+/* layers.rs:494-522: per head, scores (Q * scale) K^T with sums over the
+ * head dimension in order, a softmax per row, then S V with sums over the
+ * keys in order (both products through pointwise_with, no bias). */
+static void attention(const orc_plan *p, const orc_op *op, const float *x, float *y) {
+    size_t t = op->iw, c = op->oc, heads = op->n2, hd = c / heads;
+    float scale = *W(p, op->w0);
+    float *q = malloc(t * hd * sizeof(float)), *scores = malloc(t * t * sizeof(float));
+    for (size_t h = 0; h < heads; h++) {
+        for (size_t s = 0; s < t; s++)
+            for (size_t d = 0; d < hd; d++) q[s * hd + d] = x[s * 3 * c + h * hd + d] * scale;
+        for (size_t s = 0; s < t; s++) {
+            float *row = scores + s * t;
+            for (size_t j = 0; j < t; j++) {
+                float acc = 0.0f;
+                for (size_t d = 0; d < hd; d++) acc = fmaf(x[j * 3 * c + c + h * hd + d], q[s * hd + d], acc);
+                row[j] = acc;
+            }
+            softmax_row(row, t);
+        }
+        for (size_t i = 0; i < t; i++)
+            for (size_t d = 0; d < hd; d++) {
+                float acc = 0.0f;
+                for (size_t j = 0; j < t; j++) acc = fmaf(x[j * 3 * c + 2 * c + h * hd + d], scores[i * t + j], acc);
+                y[i * c + h * hd + d] = acc;
+            }
+    }
+    free(q); free(scores);
+}
+
+/* layers.rs:692-832 (head_scalar, tier 3): logits from the bias, inputs
+ * added in order; an online softmax in 8 lanes, lane l holding columns
+ * 16j+l and 16j+8+l of panel j; the best column the first to reach the
+ * maximum. probs: y = [t][vocab] probabilities; else [t][2] = (class, 1/sum). */
+static void ctc_head(const orc_plan *p, const orc_op *op, const float *x, float *y, int probs) {
+    size_t t = op->iw, ci = op->ic, vocab = probs ? op->oc : op->n2;
+    size_t npanels = (vocab + 15) / 16;
+    const float *w = W(p, op->w0), *b = W(p, op->b0);
+    long tl = (long)t;
+#pragma omp parallel for schedule(static)
+    for (long pp = 0; pp < tl; pp++) {
+        float m[8], sum[8], best[8], logits[16];
+        for (int l = 0; l < 8; l++) { m[l] = -INFINITY; sum[l] = 0.0f; best[l] = 0.0f; }
+        const float *xv = x + (size_t)pp * ci;
+        for (size_t j = 0; j < npanels; j++) {
+            const float *panel = w + j * ci * 16;
+            for (int col = 0; col < 16; col++) {
+                float acc = b[j * 16 + col];
+                for (size_t i = 0; i < ci; i++) acc = fmaf(panel[i * 16 + col], xv[i], acc);
+                logits[col] = acc;
+            }
+            for (int l = 0; l < 8; l++) {
+                float a0 = logits[l], a1 = logits[8 + l], mm = m[l];
+                float top = a0 > a1 ? a0 : a1;
+                float grown = mm > top ? mm : top;
+                float s = sum[l] * orc_exp_neg(mm - grown);
+                s += orc_exp_neg(a0 - grown);
+                s += orc_exp_neg(a1 - grown);
+                m[l] = grown; sum[l] = s;
+                if (top > mm) best[l] = (float)(j * 16 + l + (a1 > a0 ? 8 : 0));
+            }
+            if (probs) {
+                size_t n = vocab - j * 16 < 16 ? vocab - j * 16 : 16;
+                memcpy(y + (size_t)pp * vocab + j * 16, logits, n * sizeof(float));
+            }
+        }
+        float mx = -INFINITY;
+        for (int l = 0; l < 8; l++) mx = fmaxf(mx, m[l]);
+        float total = 0.0f;
+        for (int l = 0; l < 8; l++) total += sum[l] * orc_exp_neg(m[l] - mx);
+        float r = 1.0f / total;
+        if (probs) {
+            for (size_t k = 0; k < vocab; k++) y[(size_t)pp * vocab + k] = orc_exp_neg(y[(size_t)pp * vocab + k] - mx) * r;
+        } else {
+            float bc = INFINITY;
+            for (int l = 0; l < 8; l++) if (m[l] == mx && best[l] < bc) bc = best[l];
+            y[2 * pp] = bc;
+            y[2 * pp + 1] = r;
+        }
+    }
+}
+
+/* layers.rs:595-680: each input pixel's channels times w [ic][kh][kw][oc]
+ * give its kh x kw block of outputs (bias per tap, placed as a pointwise
+ * layer of kh*kw*oc columns places it), then the tail. */
+static void convtranspose(const orc_plan *p, const orc_op *op, const float *x, float *y) {
+    const float *w = W(p, op->w0), *b = op->b1 ? W(p, op->b0) : NULL;
+    size_t cols = op->kh * op->kw * op->oc;
+    long rows = (long)op->ih;
+#pragma omp parallel for schedule(static)
+    for (long iy = 0; iy < rows; iy++) {
+        float *block = malloc(cols * sizeof(float));
+        for (size_t ix = 0; ix < op->iw; ix++) {
+            const float *px = x + ((size_t)iy * op->iw + ix) * op->ic;
+            int first = cols % 16 == 0;
+            for (size_t o = 0; o < cols; o++) block[o] = (b && first) ? b[o] : 0.0f;
+            for (size_t i = 0; i < op->ic; i++)
+                for (size_t o = 0; o < cols; o++) block[o] = fmaf(w[i * cols + o], px[i], block[o]);
+            if (b && !first)
+                for (size_t o = 0; o < cols; o++) block[o] += b[o];
+            tail(block, cols, op->fused);
+            for (size_t ky = 0; ky < op->kh; ky++)
+                for (size_t kx = 0; kx < op->kw; kx++) {
+                    size_t oy = (size_t)iy * op->kh + ky, ox = ix * op->kw + kx;
+                    memcpy(y + (oy * op->ow + ox) * op->oc, block + (ky * op->kw + kx) * op->oc,
+                           op->oc * sizeof(float));
+                }
+        }
+        free(block);
+    }
+}
+
+/* ----------------------------------------------------------------- execute */
+
+int orc_run(orc_plan *p, const float *input, float *const *outputs, int threads) {
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+    float **buf = calloc(p->nbuf, sizeof(float *));
+    if (!buf) return -1;
+    int rc = 0;
+    for (size_t b = 0; b < p->nbuf; b++) {
+        buf[b] = malloc((p->pool[b] ? p->pool[b] : 1) * sizeof(float));
+        if (!buf[b]) { rc = -1; goto done; }
+    }
+    memcpy(buf[p->slot], input, orc_input_len(p) * sizeof(float));
+    for (size_t i = 0; i < p->nops; i++) {
+        const orc_op *op = &p->ops[i];
+        const float *x = buf[op->x], *x2 = has_second(op) ? buf[op->x2] : NULL;
+        float *y = buf[op->y];
+        size_t n = op->oh * op->ow * op->oc;
+        switch (op->kind) {
+        case K_CONV: conv(p, op, x, x2, y); break;
+        case K_DWCONV: dwconv(p, op, x, y); break;
+        case K_ADD: /* conv.rs:74-79 */
+            for (size_t k = 0; k < n; k++) y[k] = x[k] + x2[k];
+            tail(y, n, op->fused);
+            break;
+        case K_MAXPOOL: maxpool(op, x, y); break;
+        case K_AVGPOOL: avgpool(op, x, y); break;
+        case K_CHANNELMUL: /* kernels/elementwise.rs:178-200 */
+            for (size_t px = 0; px < op->oh * op->ow; px++)
+                for (size_t k = 0; k < op->oc; k++) y[px * op->oc + k] = x[px * op->oc + k] * x2[k];
+            break;
+        case K_CONCATC: /* layers.rs:375-381 */
+            for (size_t px = 0; px < op->oh * op->ow; px++) {
+                memcpy(y + px * op->oc, x + px * op->ic, op->ic * sizeof(float));
+                memcpy(y + px * op->oc + op->ic, x2 + px * op->n2, op->n2 * sizeof(float));
+            }
+            break;
+        case K_LAYERNORM: layernorm(p, op, x, y); break;
+        case K_ATTENTION: attention(p, op, x, y); break;
+        case K_MEAN: mean(op, x, y); break;
+        case K_CTCHEAD: ctc_head(p, op, x, y, 1); break;
+        case K_CTCARGMAX: ctc_head(p, op, x, y, 0); break;
+        case K_UPSAMPLE: case K_UPSAMPLEADD: /* layers.rs:526-565 */
+            for (size_t oy = 0; oy < op->oh; oy++)
+                for (size_t ox = 0; ox < op->ow; ox++) {
+                    const float *src = x + ((oy / op->sh) * op->iw + ox / op->sw) * op->oc;
+                    float *dst = y + (oy * op->ow + ox) * op->oc;
+                    if (op->kind == K_UPSAMPLE) memcpy(dst, src, op->oc * sizeof(float));
+                    else {
+                        const float *add = x2 + (oy * op->ow + ox) * op->oc;
+                        for (size_t k = 0; k < op->oc; k++) dst[k] = add[k] + src[k];
+                    }
+                }
+            break;
+        case K_CONVTRANSPOSE: convtranspose(p, op, x, y); break;
+        default: rc = -1; goto done;
+        }
+    }
+    for (size_t k = 0; k < p->nout; k++) memcpy(outputs[k], buf[p->outputs[k]], p->out_n[k] * sizeof(float));
+done:
+    for (size_t b = 0; b < p->nbuf; b++) free(buf[b]);
+    free(buf);
+    return rc;
+}

@@ -1,0 +1,462 @@
+"""Benchmark: synthetic 300-dpi pages through the PP-OCRv6 detector and
+recogniser on B200, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload page|det|rec|layer]
+
+A step is one page's neural hot path: the detector at 1984 x 1536 and the
+recogniser over the page's 44 lines (runs of up to 16 lanes, each line at
+its own width). `value` is pages/s over all ranks with every input already
+in HBM; `e2e` the same through the public C ABI from page-locked host
+buffers, copies in and out included. With N > 1 each rank reads its own
+pages (weak scaling); ranks exchange nothing but the timing.
+
+`--impl reference` times the reference CPU path on this host: the C
+restatement of ppocr-native's CPU engine (oracle/, the reference itself is
+Rust and cannot be built here), all host threads, bounded samples.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+PKG_DIR = ROOT / "ppocr-native_b200"
+sys.path.insert(0, str(ROOT))
+
+L2_FLUSH_BYTES = 256 << 20  # larger than the 126 MB L2
+
+
+def package():
+    name = "ppocr_native_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, PKG_DIR / "__init__.py",
+                                                  submodule_search_locations=[str(PKG_DIR)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+# ----------------------------------------------------------------- plumbing
+
+class Dist:
+    def __init__(self):
+        self.rank = int(os.environ.get("RANK", 0))
+        self.world = int(os.environ.get("WORLD_SIZE", 1))
+        self.local = int(os.environ.get("LOCAL_RANK", 0))
+        self.pg = None
+
+    def init(self, backend: str):
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_threads() -> int:
+    return len(os.sched_getaffinity(0))
+
+
+# -------------------------------------------------------------- our path
+
+class PagePipeline:
+    """The detector and the recogniser runs of one page, queued on one stream."""
+
+    def __init__(self, cuda, synth, page, device: int):
+        self.det = cuda.Model(synth.det_plan(seed=0), device=device)
+        h, w = page.det.shape[:2]
+        self.det.set_input_size(h, w)
+        rec = cuda.Model(synth.rec_plan(seed=1), device=device)
+        self.recs = [rec] + [rec.share_weights() for _ in page.runs[1:]]
+        self.stream = self.det.stream
+        for m, run in zip(self.recs, page.runs):
+            m.set_stream(self.stream)
+            m.set_sizes([(48, page.widths[i]) for i in run])
+        self.page = page
+
+    def models(self):
+        return [self.det, *self.recs]
+
+    def fill_host(self):
+        """Copy the page into the page-locked lane inputs."""
+        np.copyto(self.det.input_mut(), self.page.det.reshape(-1))
+        for m, run in zip(self.recs, self.page.runs):
+            for lane, i in enumerate(run):
+                np.copyto(m.lane_input_mut(lane), self.page.lines[i].reshape(-1))
+
+    def run_host(self):
+        """The public call sequence: every run copies its inputs in and its
+        outputs out; the host reads each result."""
+        outs = []
+        for m in self.models():
+            m.enqueue()
+        for m in self.models():
+            m.wait(0)
+        outs.append(self.det.output())
+        for m, run in zip(self.recs, self.page.runs):
+            for lane in range(len(run)):
+                outs.append(m.lane_output(lane))
+        return outs
+
+    def enqueue_device(self):
+        for m in self.models():
+            m.enqueue_device()
+
+    def launches(self) -> int:
+        return sum(m.launches for m in self.models())
+
+    def io_bytes(self):
+        h2d = self.page.input_bytes()
+        d2h = self.det.output().nbytes
+        for m, run in zip(self.recs, self.page.runs):
+            d2h += sum(m.lane_output(lane).nbytes for lane in range(len(run)))
+        return h2d, d2h
+
+    def close(self):
+        for m in self.models():
+            m.close()
+
+
+def probe_kernel(cuda, torch, device: int, reps: int = 20) -> dict:
+    """Time the detector's dominant kernel alone with CUDA events: the 3x3
+    96 -> 24 convolution of the RSE neck at a quarter of a 1984 x 1536 page
+    (496 x 384 pixels), the layer class with the most FLOPs of the page
+    (18 of its 35 detector GFLOP with the DB head's)."""
+    from ppocr_native_b200.plan import Op, encode, window
+
+    h, w, ic, oc = 496, 384, 96, 24
+    rng = np.random.default_rng(0)
+    wt = rng.normal(0, 0.02, 9 * ic * oc).astype(np.float32)
+    b = rng.normal(0, 0.02, oc).astype(np.float32)
+    op = window(Op("conv", x=0, y=1, ic=ic, oc=oc, w=(0, wt.size), b=(wt.size, oc)), (3, 3), 1, 1, 1)
+    plan = encode((0, h, w, ic), 2, [1], [op], np.concatenate([wt, b]))
+    m = cuda.Model(plan, device=device)
+    x = rng.standard_normal(h * w * ic).astype(np.float32)
+    m.input_mut()[:] = x
+    m.run(60_000)
+    stream = torch.cuda.ExternalStream(m.stream)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
+    times = []
+    for i in range(reps + 3):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        m.enqueue_device()
+        with torch.cuda.stream(stream):
+            e1.record(stream)
+        e1.synchronize()
+        if i >= 3:
+            times.append(e0.elapsed_time(e1) / 1e3)
+    m.close()
+    t = statistics.median(times)
+    flops = 2 * h * w * 9 * ic * oc
+    algo_bytes = 4 * (h * w * ic + h * w * oc + 9 * ic * oc + oc)
+    return {"kernel": "conv_gemm 3x3 96->24 @ 496x384 (RSE neck / DB head class)", "seconds": t,
+            "flops": flops, "bytes": algo_bytes}
+
+
+def fp32_peak(torch, device: int) -> float:
+    """Measured FP32 CUDA-core peak: cuBLAS SGEMM 8192^3 with TF32 off."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    n = 8192
+    a = torch.randn(n, n, device=f"cuda:{device}")
+    b = torch.randn(n, n, device=f"cuda:{device}")
+    for _ in range(2):
+        a @ b
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        a @ b
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1) / 1e3)
+    del a, b
+    return 2 * n ** 3 / best / 1e12
+
+
+def cpu_baseline(widths_seed: int = 0, budget_s: float = 20.0) -> dict:
+    """The reference CPU path (C restatement, all host threads) on a bounded
+    sample: one page's detector and as many of its lines as fit the budget,
+    scaled to pages/s."""
+    pkg = package()
+    from oracle.oracle import Oracle, build
+
+    build()
+    synth, workload = pkg.synth, pkg.workload
+    page = workload.Page(widths_seed)
+    threads = cpu_threads()
+    det = Oracle(synth.det_plan(seed=0))
+    det.set_size(*page.det.shape[:2])
+    t0 = time.perf_counter()
+    det.run(page.det.reshape(-1), threads=threads)
+    t_det = time.perf_counter() - t0
+    rec = Oracle(synth.rec_plan(seed=1))
+    t_rec, done = 0.0, 0
+    for i, wd in enumerate(page.widths):
+        rec.set_size(48, wd)
+        t0 = time.perf_counter()
+        rec.run(page.lines[i].reshape(-1), threads=threads)
+        t_rec += time.perf_counter() - t0
+        done += 1
+        if t_det + t_rec > budget_s:
+            break
+    page_s = t_det + t_rec * len(page.widths) / done
+    return {"value": 1.0 / page_s, "unit": "pages/s", "cores": threads, "kind": "port",
+            "sample": f"1 page: detector 1984x1536 ({t_det:.2f} s) + {done} of {len(page.widths)} lines "
+                      f"({t_rec:.2f} s, scaled to all); C restatement of the reference CPU engine "
+                      "(tier-3 FMA order), OpenMP over output rows"}
+
+
+def run_ours(args, d: Dist) -> dict | None:
+    import torch
+
+    pkg = package()
+    cuda, synth, workload = pkg.cuda, pkg.synth, pkg.workload
+    device = d.local
+    torch.cuda.set_device(device)
+    d.init("nccl")
+    page = workload.Page(seed=1000 + d.rank)
+    pipe = PagePipeline(cuda, synth, page, device)
+    stream = torch.cuda.ExternalStream(pipe.stream)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
+
+    # Inputs into HBM once through the public path (copies included).
+    pipe.fill_host()
+    pipe.run_host()
+    for _ in range(args.warmup):
+        pipe.enqueue_device()
+    torch.cuda.synchronize()
+
+    # value: device-resident inputs, K steps, L2 flushed before each.
+    events = []
+    d.barrier()
+    torch.cuda.synchronize()
+    with Clocks(device) as clocks:
+        for _ in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            pipe.enqueue_device()
+            with torch.cuda.stream(stream):
+                e1.record(stream)
+            events.append((e0, e1))
+        torch.cuda.synchronize()
+    d.barrier()
+    local_s = sum(a.elapsed_time(b) for a, b in events) / 1e3
+    total_s = d.max(local_s)
+    value = d.world * args.steps / total_s
+
+    # e2e: the public call sequence with host buffers.
+    d.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        pipe.fill_host()
+        outs = pipe.run_host()
+        _ = [float(o[0]) for o in outs[:1]]
+    torch.cuda.synchronize()
+    e2e_local = time.perf_counter() - t0
+    e2e_s = d.max(e2e_local)
+    e2e = d.world * args.steps / e2e_s
+    h2d, d2h = pipe.io_bytes()
+    launches = pipe.launches()
+
+    # det alone (ms), for the metric's "det fwd ms"
+    det_times = []
+    for _ in range(5):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        pipe.det.enqueue_device()
+        with torch.cuda.stream(stream):
+            e1.record(stream)
+        e1.synchronize()
+        det_times.append(e0.elapsed_time(e1))
+    pipe.close()
+    d.barrier()
+
+    result = None
+    if d.rank == 0:
+        probe = probe_kernel(cuda, torch, device)
+        peak = fp32_peak(torch, device)
+        achieved = probe["flops"] / probe["seconds"] / 1e12
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        hbm = peaks.get("hbm_gbs", 6650.0)
+        result = {
+            "metric": "synthetic-page pages/s (det 1984x1536 + rec 44 lines) per B200 job",
+            "value": value,
+            "unit": "pages/s",
+            "n_gpus": d.world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": total_s / args.steps * 1e3,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic: seeded N(0,1) page tensors with the reference's page/line shapes; "
+                    "random-init weights N(0,0.02) of the synthetic PP-OCRv6-shaped det/rec plans",
+            "config": {"workload": "page: det 1984x1536 + rec 44 lines (48 x 320..1600, runs of 16)",
+                       "det_fwd_ms": statistics.median(det_times),
+                       "l2": "flushed (256 MB write) before every timed step, outside the step's events",
+                       "parallelism": f"replicas x{d.world} (pages sharded by rank, no collective)"},
+            "e2e": {"value": e2e, "unit": "pages/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches * args.steps,
+            "roofline": {"bound": "fp32", "kernel": probe["kernel"], "achieved": achieved,
+                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "peak_source": "measured in this run: cuBLAS SGEMM 8192^3, TF32 off (FP32 CUDA cores)",
+                         "traffic": None,
+                         "hbm_achieved_gbs": probe["bytes"] / probe["seconds"] / 1e9,
+                         "hbm_peak_gbs": hbm, "seconds_per_launch": probe["seconds"]},
+            "clocks": clocks.summary(),
+        }
+    return result
+
+
+def run_reference(args, d: Dist) -> dict | None:
+    if d.rank != 0:
+        return None
+    samples = []
+    base = None
+    for step in range(args.warmup + args.steps):
+        b = cpu_baseline(widths_seed=step, budget_s=8.0)
+        if step >= args.warmup:
+            samples.append(b["value"])
+            base = b
+    value = statistics.median(samples)
+    return {
+        "impl": "reference",
+        "metric": "synthetic-page pages/s (det 1984x1536 + rec 44 lines) per B200 job",
+        "value": value, "unit": "pages/s", "n_gpus": d.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 / value, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (same pages and weights as the GPU arm)",
+        "config": {"workload": "page: det 1984x1536 + rec 44 lines (48 x 320..1600, runs of 16)"},
+        "cpu_baseline": {"value": value, "unit": "pages/s", "cores": base["cores"], "kind": "port",
+                         "sample": base["sample"]},
+        "e2e": {"value": value, "unit": "pages/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    d = Dist()
+    if args.impl == "reference":
+        result = run_reference(args, d)
+    else:
+        result = run_ours(args, d)
+        if result is not None:
+            if args.no_cpu_baseline:
+                result["cpu_baseline"] = None
+            else:
+                result["cpu_baseline"] = cpu_baseline()
+    d.close()
+    if result is not None:
+        print(json.dumps(result))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,117 @@
+/* ppocr_cuda.h — C ABI of libppocr_cuda.so, the B200 (sm_100a) backend of
+ * the ppocr-native engine.
+ *
+ * It replaces the Vulkan `GpuModel` of ppocr-native
+ * (`src/engine/gpu/mod.rs:81-291`) behind the same calls: a model is a
+ * PPOCRPL1 plan loaded onto one GPU, run over one or more images ("lanes")
+ * at a time, each lane with its own input height and width. Lanes of equal
+ * size run as one batch. The library owns page-locked host buffers for
+ * every lane's input and outputs; their pointers stay valid until the next
+ * ppocr_model_set_sizes / ppocr_model_free.
+ *
+ * Every call returns a status (PPOCR_OK = 0) and never throws or aborts; the
+ * reason for the last failure on the calling thread is ppocr_last_error().
+ * On a failed resize the model keeps its previous sizes
+ * (`src/engine/mod.rs:425-446`). Calls on one model are not thread-safe;
+ * different models are independent.
+ *
+ * No PyTorch, Vulkan or CPU fallback sits on this path: a model that cannot
+ * run on the GPU returns an error, and the caller decides what to do.
+ */
+#ifndef PPOCR_CUDA_H
+#define PPOCR_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct ppocr_model ppocr_model;
+
+enum {
+    PPOCR_OK = 0,
+    PPOCR_E_PLAN = 1,        /* the plan file is unreadable, malformed or inconsistent */
+    PPOCR_E_SIZE = 2,        /* the requested input size does not fit the plan */
+    PPOCR_E_NOMEM = 3,       /* device or page-locked host memory ran out */
+    PPOCR_E_DEVICE = 4,      /* a CUDA call failed or no usable device */
+    PPOCR_E_TIMEOUT = 5,     /* the GPU did not finish within the timeout */
+    PPOCR_E_UNSUPPORTED = 6, /* an operation this backend does not run */
+    PPOCR_E_ARG = 7          /* a bad argument (null pointer, lane out of range) */
+};
+
+/* Bits of ppocr_model_set_options. */
+enum {
+    PPOCR_OPT_NO_FUSION = 1, /* run every plan operation as its own kernel */
+    PPOCR_OPT_NO_GRAPH = 2   /* launch kernels directly instead of replaying a CUDA graph */
+};
+
+/* Number of CUDA devices this process can use (0 when none). */
+int ppocr_device_count(void);
+
+/* Reason for the last failed call on this thread ("" after success). */
+const char *ppocr_last_error(void);
+
+/* Load and check a plan (replaces `GpuModel::load`, gpu/mod.rs:113-163),
+ * with one lane at the size the plan was exported at. */
+int ppocr_model_load(const char *plan_path, int device, ppocr_model **out);
+/* The same from a plan held in memory. */
+int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_model **out);
+/* A second model on the same device sharing the first one's weights
+ * (`Model::try_clone`, src/engine/mod.rs:318). */
+int ppocr_model_share_weights(const ppocr_model *src, ppocr_model **out);
+void ppocr_model_free(ppocr_model *model);
+
+/* The GPU's name (`GpuModel::device`, gpu/mod.rs:165-168). */
+const char *ppocr_model_device_name(const ppocr_model *model);
+/* 1 when the GPU shares memory with the CPU (`GpuModel::integrated`, :170-173). */
+int ppocr_model_integrated(const ppocr_model *model);
+/* Most lanes one run takes (`GpuModel::max_lanes`, :177-181). */
+size_t ppocr_model_max_lanes(const ppocr_model *model);
+size_t ppocr_model_output_count(const ppocr_model *model);
+
+/* One lane of height x width (`GpuModel::set_input_size`, :175-177). */
+int ppocr_model_set_input_size(ppocr_model *model, uint32_t height, uint32_t width);
+/* One lane per (height, width) pair in hw_pairs[2*i], hw_pairs[2*i+1]
+ * (`GpuModel::set_sizes`, :184-230). */
+int ppocr_model_set_sizes(ppocr_model *model, const uint32_t *hw_pairs, size_t lanes);
+
+/* The lane's HWC input in page-locked host memory, to be filled before each
+ * run (`GpuModel::lane_input_mut`, :240-246); *len receives its floats. */
+float *ppocr_model_lane_input(ppocr_model *model, size_t lane, size_t *len);
+/* Output `index` of the lane's last run (`GpuModel::lane_output`, :255-259). */
+const float *ppocr_model_lane_output(const ppocr_model *model, size_t lane, size_t index, size_t *len);
+
+/* Copy every lane's input to the GPU, run the network, copy the outputs
+ * back and wait at most timeout_ms (0 = no limit) (`GpuModel::run`,
+ * :262-290, whose fence wait has no limit, vk.rs:373-378). */
+int ppocr_model_run(ppocr_model *model, uint32_t timeout_ms);
+/* ppocr_model_run split in two, so that the host can prepare the next
+ * batch while the GPU runs this one. */
+int ppocr_model_enqueue(ppocr_model *model);
+int ppocr_model_wait(ppocr_model *model, uint32_t timeout_ms);
+
+/* Device-resident use, for callers whose inputs are produced on the GPU:
+ * the lane's input / output tensors in device memory, and a run that copies
+ * nothing (the outputs stay on the device). */
+float *ppocr_model_lane_device_input(ppocr_model *model, size_t lane, size_t *len);
+const float *ppocr_model_lane_device_output(const ppocr_model *model, size_t lane, size_t index, size_t *len);
+int ppocr_model_enqueue_device(ppocr_model *model);
+/* The cudaStream_t every kernel of this model runs on. */
+void *ppocr_model_stream(ppocr_model *model);
+/* Run this model on the caller's cudaStream_t (NULL: its own again), e.g.
+ * to queue several models behind one another without host waits. */
+int ppocr_model_set_stream(ppocr_model *model, void *stream);
+
+/* PPOCR_OPT_* bits; takes effect at the next run. */
+int ppocr_model_set_options(ppocr_model *model, uint32_t options);
+/* Kernel launches one run makes at the current sizes (copies excluded). */
+size_t ppocr_model_launches(const ppocr_model *model);
+/* A text line describing step `i` of the fused schedule (NULL past the end). */
+const char *ppocr_model_step_name(const ppocr_model *model, size_t i);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

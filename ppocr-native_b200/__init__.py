@@ -3,17 +3,10 @@ PP-OCRv6 detector and recogniser executed from PPOCRPL1 plans) as
 hand-written sm_100a CUDA kernels behind a C ABI (`include/ppocr_cuda.h`).
 
 Python here is the binding and the test/bench harness: `cuda` wraps the C ABI
-with ctypes, `plan` writes plan files, `synth` builds the synthetic networks.
+with ctypes (the library is opened on first use), `plan` writes plan files,
+`synth` builds the synthetic networks.
 """
 
-from . import plan, synth  # noqa: F401
+from . import cuda, plan, synth  # noqa: F401
 
-__all__ = ["plan", "synth", "cuda"]
-
-
-def __getattr__(name):
-    if name == "cuda":
-        from . import cuda
-
-        return cuda
-    raise AttributeError(name)
+__all__ = ["cuda", "plan", "synth"]

@@ -1,0 +1,263 @@
+// Depthwise convolution, alone and feeding a pointwise GEMM tile from shared
+// memory (sm_100a, FP32 pipes).
+//
+// Each depthwise output starts from its bias and adds its taps in kernel
+// row-major order, one fused multiply-add each (reference
+// `src/engine/conv.rs:244-339`, `kernels/depthwise.rs:12-45`), skipping taps
+// that fall in the padding. In the fused kernel a block computes the
+// depthwise outputs of BM consecutive pixels for every channel into shared
+// memory, then runs the pointwise GEMM over them for every output channel:
+// the depthwise map never reaches HBM.
+#include "devmath.cuh"
+#include "kernels.hpp"
+
+namespace ppocr {
+
+namespace {
+
+// Depthwise outputs of `count` channels (1 or 4) of one pixel, into v.
+template <int VEC>
+__device__ __forceinline__ void dw_pixel(const DwArgs &a, int n, int oy, int ox, int c, float v[VEC]) {
+#pragma unroll
+    for (int e = 0; e < VEC; e++) v[e] = a.b ? __ldg(a.b + c + e) : 0.0f;
+    const float *xn = a.x + (long)n * a.ih * a.iw * a.c;
+    for (int ky = 0; ky < a.kh; ky++) {
+        int iy = oy * a.sh - a.pt + ky;
+        if (iy < 0 || iy >= a.ih) continue;
+        for (int kx = 0; kx < a.kw; kx++) {
+            int ix = ox * a.sw - a.pl + kx;
+            if (ix < 0 || ix >= a.iw) continue;
+            const float *src = xn + ((long)iy * a.iw + ix) * a.c + c;
+            const float *w = a.w + (ky * a.kw + kx) * a.c + c;
+            if (VEC == 4) {
+                float4 q = __ldg(reinterpret_cast<const float4 *>(src));
+                float4 g = __ldg(reinterpret_cast<const float4 *>(w));
+                v[0] = ffma(g.x, q.x, v[0]);
+                v[1] = ffma(g.y, q.y, v[1]);
+                v[2] = ffma(g.z, q.z, v[2]);
+                v[3] = ffma(g.w, q.w, v[3]);
+            } else {
+                v[0] = ffma(__ldg(w), __ldg(src), v[0]);
+            }
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < VEC; e++) v[e] = activate(a.act, v[e]);
+}
+
+template <int VEC>
+__global__ void __launch_bounds__(256) dw_kernel(const DwArgs a) {
+    long groups = (long)a.N * a.oh * a.ow * (a.c / VEC);
+    for (long g = (long)blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += (long)gridDim.x * blockDim.x) {
+        int cg = a.c / VEC;
+        long m = g / cg;
+        int c = int(g - m * cg) * VEC;
+        int hw = a.oh * a.ow;
+        int n = int(m / hw), r = int(m - (long)n * hw);
+        int oy = r / a.ow, ox = r - oy * a.ow;
+        float v[VEC];
+        dw_pixel<VEC>(a, n, oy, ox, c, v);
+        float *dst = a.y + m * a.c + c;
+        if (VEC == 4)
+            *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+        else
+            dst[0] = v[0];
+    }
+}
+
+constexpr int BK = 8;
+constexpr int DPAD = 4;
+
+// Fused depthwise -> pointwise. Threads TX x TY, each TM pixels x TN output
+// channels of the current BN-wide output slice; BM = TM*TY pixels per block.
+template <int TM, int TN, int TX, int TY>
+__global__ void __launch_bounds__(TX *TY) dw_pw_kernel(const DwPwArgs a) {
+    constexpr int BM = TM * TY, BN = TN * TX, THREADS = TX * TY;
+    constexpr int BELEMS = BK * BN;
+    constexpr int BLOADS = (BELEMS + THREADS - 1) / THREADS;
+    extern __shared__ __align__(16) float smem[];
+    const DwArgs &d = a.dw;
+    const int C = d.c;
+    float *Ds = smem;                              // [C][BM + DPAD]
+    float *Bs = smem + (long)C * (BM + DPAD);      // [2][BK][BN]
+
+    const int tid = threadIdx.x;
+    const int tx = tid % TX, ty = tid / TX;
+    const long M = (long)d.N * d.oh * d.ow;
+    const long m0 = (long)blockIdx.x * BM;
+    const int hw = d.oh * d.ow;
+
+    // Phase 1: the depthwise tile, [channel][pixel].
+    const bool vec = (C % 4) == 0;
+    const int cg = vec ? C / 4 : C;
+    for (int g = tid; g < BM * cg; g += THREADS) {
+        int p = g / cg, c = (g - p * cg) * (vec ? 4 : 1);
+        long m = m0 + p;
+        if (m < M) {
+            int n = int(m / hw), r = int(m - (long)n * hw);
+            int oy = r / d.ow, ox = r - oy * d.ow;
+            if (vec) {
+                float v[4];
+                dw_pixel<4>(d, n, oy, ox, c, v);
+#pragma unroll
+                for (int e = 0; e < 4; e++) Ds[(c + e) * (BM + DPAD) + p] = v[e];
+            } else {
+                float v[1];
+                dw_pixel<1>(d, n, oy, ox, c, v);
+                Ds[c * (BM + DPAD) + p] = v[0];
+            }
+        } else {
+            for (int e = 0; e < (vec ? 4 : 1); e++) Ds[(c + e) * (BM + DPAD) + p] = 0.0f;
+        }
+    }
+
+    // Phase 2: pointwise GEMM over the tile, one BN slice at a time.
+    const int ktiles = (C + BK - 1) / BK;
+    float rb[BLOADS];
+    for (int n0 = 0; n0 < a.oc; n0 += BN) {
+        auto fetch = [&](int t) {
+            int c0 = t * BK;
+#pragma unroll
+            for (int l = 0; l < BLOADS; l++) {
+                int e = tid + l * THREADS;
+                int kk = e / BN, nn = e - kk * BN;
+                int c = c0 + kk, n = n0 + nn;
+                rb[l] = (e < BELEMS && c < C && n < a.oc) ? __ldg(a.w2 + (long)c * a.oc + n) : 0.0f;
+            }
+        };
+        auto stash = [&](int buf) {
+#pragma unroll
+            for (int l = 0; l < BLOADS; l++) {
+                int e = tid + l * THREADS;
+                if (e < BELEMS) Bs[buf * BELEMS + e] = rb[l];
+            }
+        };
+        float acc[TM][TN];
+        bool first[TM];
+#pragma unroll
+        for (int i = 0; i < TM; i++) {
+            long m = m0 + ty * TM + i;
+            bool f = a.bias_mode2 == BIAS_FIRST;
+            if (a.bias_mode2 == BIAS_FIRST_BUT_ROW_TAIL && m < M) {
+                int ox = int(m % d.ow);
+                f = ox < d.ow - d.ow % 4;
+            }
+            first[i] = f;
+#pragma unroll
+            for (int j = 0; j < TN; j++) {
+                int n = n0 + tx * TN + j;
+                acc[i][j] = (f && a.b2 && n < a.oc) ? __ldg(a.b2 + n) : 0.0f;
+            }
+        }
+        __syncthreads();  // the depthwise tile is complete; Bs is free
+        fetch(0);
+        stash(0);
+        __syncthreads();
+        for (int t = 0; t < ktiles; t++) {
+            int buf = t & 1;
+            if (t + 1 < ktiles) fetch(t + 1);
+            int c0 = t * BK;
+#pragma unroll
+            for (int kk = 0; kk < BK; kk++) {
+                if (c0 + kk >= C) break;
+                float fa[TM], fb[TN];
+                const float *arow = Ds + (c0 + kk) * (BM + DPAD) + ty * TM;
+#pragma unroll
+                for (int i = 0; i < TM; i++) fa[i] = arow[i];
+#pragma unroll
+                for (int j = 0; j < TN; j++) fb[j] = Bs[buf * BELEMS + kk * BN + tx * TN + j];
+#pragma unroll
+                for (int i = 0; i < TM; i++)
+#pragma unroll
+                    for (int j = 0; j < TN; j++) acc[i][j] = ffma(fb[j], fa[i], acc[i][j]);
+            }
+            if (t + 1 < ktiles) stash(buf ^ 1);
+            __syncthreads();
+        }
+#pragma unroll
+        for (int i = 0; i < TM; i++) {
+            long m = m0 + ty * TM + i;
+            if (m >= M) continue;
+#pragma unroll
+            for (int j = 0; j < TN; j++) {
+                int n = n0 + tx * TN + j;
+                if (n >= a.oc) continue;
+                float v = acc[i][j];
+                if (!first[i] && a.b2) v = fadd(v, __ldg(a.b2 + n));
+                v = activate(a.act2, v);
+                if (a.res) v = activate(a.act3, fadd(v, __ldg(a.res + m * a.oc + n)));
+                a.y[m * a.oc + n] = v;
+            }
+        }
+    }
+}
+
+template <int TM, int TN, int TX, int TY>
+size_t dw_pw_smem(int C) {
+    constexpr int BM = TM * TY, BN = TN * TX;
+    return sizeof(float) * ((size_t)C * (BM + DPAD) + 2 * BK * BN);
+}
+
+template <int TM, int TN, int TX, int TY>
+int run_dw_pw(const DwPwArgs &a, cudaStream_t s) {
+    constexpr int BM = TM * TY;
+    size_t smem = dw_pw_smem<TM, TN, TX, TY>(a.dw.c);
+    long M = (long)a.dw.N * a.dw.oh * a.dw.ow;
+    dw_pw_kernel<TM, TN, TX, TY><<<(unsigned)((M + BM - 1) / BM), TX * TY, smem, s>>>(a);
+    return 1;
+}
+
+}  // namespace
+
+int launch_dw(const DwArgs &a, cudaStream_t s) {
+    long work = (long)a.N * a.oh * a.ow * (a.c % 4 == 0 ? a.c / 4 : a.c);
+    long blocks = (work + 255) / 256;
+    if (blocks > 148L * 64) blocks = 148L * 64;
+    if (blocks < 1) blocks = 1;
+    if (a.c % 4 == 0)
+        dw_kernel<4><<<(unsigned)blocks, 256, 0, s>>>(a);
+    else
+        dw_kernel<1><<<(unsigned)blocks, 256, 0, s>>>(a);
+    return 1;
+}
+
+template <int TM, int TN, int TX, int TY>
+void allow_smem() {
+    cudaFuncSetAttribute(dw_pw_kernel<TM, TN, TX, TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+}
+
+// Raise the dynamic shared-memory ceiling of every fused instance; once per
+// device, with that device current.
+void configure_dw_kernels() {
+    allow_smem<8, 6, 16, 16>();
+    allow_smem<8, 4, 16, 16>();
+    allow_smem<8, 3, 16, 16>();
+    allow_smem<8, 3, 8, 16>();
+    allow_smem<8, 2, 16, 16>();
+    allow_smem<8, 4, 32, 8>();
+    allow_smem<8, 3, 32, 8>();
+    allow_smem<8, 2, 32, 8>();
+}
+
+bool dw_pw_supported(const DwPwArgs &a) {
+    // The depthwise tile of 128 (or 64) pixels x C channels must fit.
+    size_t smem = a.dw.c <= 192 ? dw_pw_smem<8, 4, 16, 16>(a.dw.c) : dw_pw_smem<8, 4, 32, 8>(a.dw.c);
+    return smem <= 200 * 1024;
+}
+
+int launch_dw_pw(const DwPwArgs &a, cudaStream_t s) {
+    // 128 pixels per block up to 192 channels, else 64; the output slice is
+    // 16 (or 32) threads x TN channels.
+    if (a.dw.c <= 192) {
+        if (a.oc % 96 == 0) return run_dw_pw<8, 6, 16, 16>(a, s);
+        if (a.oc % 64 == 0) return run_dw_pw<8, 4, 16, 16>(a, s);
+        if (a.oc % 48 == 0) return run_dw_pw<8, 3, 16, 16>(a, s);
+        if (a.oc % 24 == 0) return run_dw_pw<8, 3, 8, 16>(a, s);
+        return run_dw_pw<8, 2, 16, 16>(a, s);
+    }
+    if (a.oc % 128 == 0) return run_dw_pw<8, 4, 32, 8>(a, s);
+    if (a.oc % 96 == 0) return run_dw_pw<8, 3, 32, 8>(a, s);
+    return run_dw_pw<8, 2, 32, 8>(a, s);
+}
+
+}  // namespace ppocr

@@ -1,0 +1,470 @@
+// The layers around the convolutions (sm_100a): elementwise passes, pools,
+// the f64 channel mean, LayerNorm, multi-head attention, the CTC head and
+// the transposed convolution. Each follows the reference's arithmetic
+// (`src/engine/layers.rs`, `kernels/elementwise.rs`); where a reduction is
+// split across threads the split is noted.
+#include <cfloat>
+
+#include "devmath.cuh"
+#include "kernels.hpp"
+
+namespace ppocr {
+
+namespace {
+
+unsigned grid_for(long work, int threads = 256) {
+    long blocks = (work + threads - 1) / threads;
+    if (blocks > 148L * 32) blocks = 148L * 32;
+    return (unsigned)(blocks < 1 ? 1 : blocks);
+}
+
+// ----------------------------------------------------------------- eltwise
+
+template <int VEC>
+__global__ void __launch_bounds__(256) elt_kernel(const EltArgs a) {
+    const int cout = a.mode == ELT_CONCAT ? a.c + a.c2 : a.c;
+    const long total = (long)a.N * a.oh * a.ow * cout / VEC;
+    const int hw = a.oh * a.ow;
+    for (long g = (long)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (long)gridDim.x * blockDim.x) {
+        long e = g * VEC;
+        long m = e / cout;
+        int c = int(e - m * cout);
+        float v[VEC];
+        switch (a.mode) {
+        case ELT_ADD:
+#pragma unroll
+            for (int k = 0; k < VEC; k++) v[k] = activate(a.act, fadd(a.x[e + k], a.x2[e + k]));
+            break;
+        case ELT_CHANNELMUL:
+        case ELT_GATE_ADD: {
+            int n = int(m / hw);
+            const float *g = a.x2 + (long)n * a.c + c;
+#pragma unroll
+            for (int k = 0; k < VEC; k++) {
+                float x = a.x[e + k];
+                float p = fmul(x, g[k]);
+                v[k] = a.mode == ELT_CHANNELMUL ? p : activate(a.act, fadd(p, x));
+            }
+            break;
+        }
+        case ELT_UPSAMPLE:
+        case ELT_UPSAMPLE_ADD: {
+            int n = int(m / hw), r = int(m - (long)n * hw);
+            int oy = r / a.ow, ox = r - oy * a.ow;
+            const float *src = a.x + (((long)n * a.ih + oy / a.sh) * a.iw + ox / a.sw) * a.c + c;
+#pragma unroll
+            for (int k = 0; k < VEC; k++) v[k] = a.mode == ELT_UPSAMPLE ? src[k] : fadd(a.x2[e + k], src[k]);
+            break;
+        }
+        default: {  // ELT_CONCAT
+#pragma unroll
+            for (int k = 0; k < VEC; k++) {
+                int ck = c + k;
+                v[k] = ck < a.c ? a.x[m * a.c + ck] : a.x2[m * a.c2 + (ck - a.c)];
+            }
+        }
+        }
+        if (VEC == 4)
+            *reinterpret_cast<float4 *>(a.y + e) = make_float4(v[0], v[1], v[2], v[3]);
+        else
+            a.y[e] = v[0];
+    }
+}
+
+// ------------------------------------------------------------------- pools
+
+// Max pool: windows cut short at the bottom and right edges, the first tap
+// copied and later ones kept only when greater (conv.rs:404-440). Average
+// pool: whole windows, taps summed in row-major order then divided
+// (layers.rs:443-463).
+__global__ void __launch_bounds__(256) pool_kernel(const PoolArgs a) {
+    const long total = (long)a.N * a.oh * a.ow * a.c;
+    for (long g = (long)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (long)gridDim.x * blockDim.x) {
+        long m = g / a.c;
+        int c = int(g - m * a.c);
+        int hw = a.oh * a.ow;
+        int n = int(m / hw), r = int(m - (long)n * hw);
+        int oy = r / a.ow, ox = r - oy * a.ow;
+        const float *xn = a.x + (long)n * a.ih * a.iw * a.c + c;
+        float v = 0.0f;
+        bool seeded = false;
+        for (int ky = 0; ky < a.kh; ky++) {
+            int iy = oy * a.sh + ky;
+            if (iy >= a.ih) continue;
+            for (int kx = 0; kx < a.kw; kx++) {
+                int ix = ox * a.sw + kx;
+                if (ix >= a.iw) continue;
+                float x = xn[((long)iy * a.iw + ix) * a.c];
+                if (a.average) {
+                    v = fadd(v, x);
+                } else if (!seeded || x > v) {
+                    v = x;
+                    seeded = true;
+                }
+            }
+        }
+        if (a.average) v = fdiv(v, float(a.kh * a.kw));
+        a.y[g] = v;
+    }
+}
+
+// -------------------------------------------------------------------- mean
+
+// Stage 1: each block sums a run of pixels of one lane, per channel, in f64.
+// The reference sums all pixels in order in f64 (layers.rs:387-406); the
+// split into runs changes only f64 rounding, far below the f32 result's.
+__global__ void __launch_bounds__(256) mean_partial_kernel(const MeanArgs a) {
+    extern __shared__ double sums[];  // [rows][c]
+    const int n = blockIdx.y, chunk = blockIdx.x;
+    const int rows = blockDim.x / a.c;  // pixels summed side by side
+    const int t = threadIdx.x;
+    const int per = (a.hw + a.chunks - 1) / a.chunks;
+    const int p0 = chunk * per, p1 = min(a.hw, p0 + per);
+    const float *x = a.x + (long)n * a.hw * a.c;
+    if (rows >= 1) {
+        int row = t / a.c, c = t - row * a.c;
+        double s = 0.0;
+        if (row < rows)
+            for (int p = p0 + row; p < p1; p += rows) s += (double)x[(long)p * a.c + c];
+        if (row < rows) sums[row * a.c + c] = s;
+        __syncthreads();
+        if (t < a.c) {
+            double total = 0.0;
+            for (int r = 0; r < rows; r++) total += sums[r * a.c + t];
+            a.partial[((long)n * a.chunks + chunk) * a.c + t] = total;
+        }
+    } else {
+        for (int c = t; c < a.c; c += blockDim.x) {
+            double s = 0.0;
+            for (int p = p0; p < p1; p++) s += (double)x[(long)p * a.c + c];
+            a.partial[((long)n * a.chunks + chunk) * a.c + c] = s;
+        }
+    }
+}
+
+__global__ void mean_final_kernel(const MeanArgs a) {
+    int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= a.N * a.c) return;
+    int n = g / a.c, c = g - n * a.c;
+    double s = 0.0;
+    for (int k = 0; k < a.chunks; k++) s += a.partial[((long)n * a.chunks + k) * a.c + c];
+    a.y[g] = (float)(s / (double)a.hw);
+}
+
+// --------------------------------------------------------------- layernorm
+
+// One warp per pixel. The pixel's values go through shared memory and every
+// lane then forms the same sums in channel order, as the reference does
+// (layers.rs:467-479), so the result carries its bits.
+__global__ void __launch_bounds__(128) layernorm_kernel(const LayerNormArgs a) {
+    extern __shared__ float vals[];  // [4 warps][c]
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const long p = (long)blockIdx.x * 4 + warp;
+    if (p >= a.pixels) return;
+    float *v = vals + warp * a.c;
+    const float *x = a.x + p * a.c;
+    for (int k = lane; k < a.c; k += 32) v[k] = x[k];
+    __syncwarp();
+    float s = 0.0f;
+    for (int k = 0; k < a.c; k++) s = fadd(s, v[k]);
+    float m = fdiv(s, float(a.c));
+    float q = 0.0f;
+    for (int k = 0; k < a.c; k++) {
+        float d = fsub(v[k], m);
+        q = fadd(q, fmul(d, d));
+    }
+    float var = fdiv(q, float(a.c));
+    float r = __fsqrt_rn(fadd(var, a.w[2 * a.c]));
+    for (int k = lane; k < a.c; k += 32)
+        a.y[p * a.c + k] = fadd(fmul(fdiv(fsub(v[k], m), r), a.w[k]), a.w[a.c + k]);
+}
+
+// --------------------------------------------------------------- attention
+
+// One block per (lane, head), one thread per query. Per query, as the
+// reference (layers.rs:488-522 with softmax_row :254-294): scores
+// (q * scale) . k summed over the head dimension in order; the maximum; the
+// exponentials summed in 8 lanes (element j in lane j % 8) over whole groups
+// of eight, the lanes folded in order, the rest added one at a time; each
+// probability e * (1 / sum); the output sum of v * p over the keys in order.
+// Scores and exponentials are recomputed per pass instead of stored: the
+// same operations give the same bits.
+__global__ void attention_kernel(const AttentionArgs a) {
+    extern __shared__ float kv[];  // K [t][hd], V [t][hd]
+    const int n = blockIdx.x / a.heads, h = blockIdx.x % a.heads;
+    const int hd = a.c / a.heads, t = a.t, c = a.c;
+    float *K = kv, *V = kv + t * hd;
+    const float *x = a.x + (long)n * t * 3 * c;
+    for (int i = threadIdx.x; i < t * hd; i += blockDim.x) {
+        int j = i / hd, d = i - j * hd;
+        K[i] = x[(long)j * 3 * c + c + h * hd + d];
+        V[i] = x[(long)j * 3 * c + 2 * c + h * hd + d];
+    }
+    __syncthreads();
+    const float scale = a.scale[0];
+    constexpr int MAXHD = 64;
+    for (int s = threadIdx.x; s < t; s += blockDim.x) {
+        float q[MAXHD];
+        for (int d = 0; d < hd; d++) q[d] = fmul(x[(long)s * 3 * c + h * hd + d], scale);
+        auto score = [&](int j) {
+            float acc = 0.0f;
+            for (int d = 0; d < hd; d++) acc = ffma(K[j * hd + d], q[d], acc);
+            return acc;
+        };
+        float mx = -FLT_MAX;
+        bool any = false;
+        for (int j = 0; j < t; j++) {
+            float v = score(j);
+            if (!any || v > mx) mx = v;
+            any = true;
+        }
+        const int body = t / 8 * 8;
+        float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int j = 0; j < body; j++) lanes[j % 8] = fadd(lanes[j % 8], exp_neg(fsub(score(j), mx)));
+        float sum = 0.0f;
+        for (int l = 0; l < 8; l++) sum = fadd(sum, lanes[l]);
+        for (int j = body; j < t; j++) sum = fadd(sum, exp_neg(fsub(score(j), mx)));
+        float r = fdiv(1.0f, sum);
+        float out[MAXHD];
+        for (int d = 0; d < hd; d++) out[d] = 0.0f;
+        for (int j = 0; j < t; j++) {
+            float p = fmul(exp_neg(fsub(score(j), mx)), r);
+            for (int d = 0; d < hd; d++) out[d] = ffma(V[j * hd + d], p, out[d]);
+        }
+        float *y = a.y + ((long)n * t + s) * c + h * hd;
+        for (int d = 0; d < hd; d++) y[d] = out[d];
+    }
+}
+
+// --------------------------------------------------------------------- ctc
+
+constexpr int CTC_PX = 32;    // pixels per block
+constexpr int CTC_COLS = 256; // columns (16 panels) per block
+constexpr int CTC_THREADS = 256;
+
+// Logits of CTC_PX pixels x CTC_COLS columns: each starts from its bias and
+// adds the inputs in order (layers.rs:771-777), so they carry the
+// reference's bits. Each thread holds 4 pixels x 8 columns; the block then
+// reduces its columns per pixel to (max, sum exp(logit - max), first column
+// reaching max). The reference runs one online softmax per pixel over all
+// panels in order; merging per-block states instead changes only the
+// rounding of the sum (argmax and maximum are exact).
+__global__ void __launch_bounds__(CTC_THREADS) ctc_logits_kernel(const CtcArgs a) {
+    extern __shared__ float sm[];
+    float *xs = sm;                         // [ci][CTC_PX]
+    __shared__ float red_m[CTC_PX][32], red_s[CTC_PX][32];
+    __shared__ int red_b[CTC_PX][32];
+    const int p0 = blockIdx.x * CTC_PX, cb = blockIdx.y;
+    const int col0 = cb * CTC_COLS;
+    for (int i = threadIdx.x; i < a.ci * CTC_PX; i += CTC_THREADS) {
+        int k = i / CTC_PX, p = i - k * CTC_PX;
+        xs[i] = p0 + p < a.pixels ? a.x[(long)(p0 + p) * a.ci + k] : 0.0f;
+    }
+    __syncthreads();
+    const int tc = threadIdx.x % 32, tp = threadIdx.x / 32;  // 32 column groups x 8 pixel groups
+    float acc[4][8];
+    int cols[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        // column group tc holds columns tc*4 .. +4 of the first and of the
+        // second 128-column half, so a warp reads 512 contiguous bytes.
+        int col = col0 + (j < 4 ? tc * 4 + j : 128 + tc * 4 + (j - 4));
+        cols[j] = col;
+        float b = col < a.cols ? a.b[col] : -FLT_MAX;
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[i][j] = b;
+    }
+    for (int k = 0; k < a.ci; k++) {
+        float w[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            int col = cols[j];
+            w[j] = col < a.cols ? __ldg(a.w + ((long)(col >> 4) * a.ci + k) * 16 + (col & 15)) : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float xv = xs[k * CTC_PX + tp * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 8; j++) acc[i][j] = ffma(w[j], xv, acc[i][j]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        int p = p0 + tp * 4 + i;
+        float m = -FLT_MAX;
+        int best = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            bool live = cols[j] < a.vocab;
+            float v = acc[i][j];
+            if (live && (v > m || (v == m && cols[j] < best))) { m = v; best = cols[j]; }
+            if (a.probs && live && p < a.pixels) a.y[(long)p * a.vocab + cols[j]] = v;
+        }
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (cols[j] < a.vocab) s = fadd(s, exp_neg(fsub(acc[i][j], m)));
+        red_m[tp * 4 + i][tc] = m;
+        red_s[tp * 4 + i][tc] = s;
+        red_b[tp * 4 + i][tc] = best;
+    }
+    __syncthreads();
+    if (threadIdx.x < CTC_PX) {
+        int pl = threadIdx.x, p = p0 + pl;
+        float m = -FLT_MAX;
+        int best = 0x7fffffff;
+        for (int g = 0; g < 32; g++) {
+            float v = red_m[pl][g];
+            if (v > m || (v == m && red_b[pl][g] < best)) { m = v; best = red_b[pl][g]; }
+        }
+        float s = 0.0f;
+        for (int g = 0; g < 32; g++)
+            if (red_m[pl][g] > -FLT_MAX) s = fadd(s, fmul(red_s[pl][g], exp_neg(fsub(red_m[pl][g], m))));
+        if (p < a.pixels) {
+            float *st = a.partial + ((long)p * a.col_blocks + cb) * 3;
+            st[0] = m;
+            st[1] = s;
+            st[2] = __int_as_float(best);
+        }
+    }
+}
+
+// Merge the column blocks of each pixel in order: the largest maximum, the
+// rescaled sums, the smallest column holding the maximum (layers.rs:813-832).
+__global__ void ctc_merge_kernel(const CtcArgs a) {
+    int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= a.pixels) return;
+    const float *st = a.partial + (long)p * a.col_blocks * 3;
+    float m = -FLT_MAX;
+    int best = 0x7fffffff;
+    for (int b = 0; b < a.col_blocks; b++) {
+        float v = st[b * 3];
+        int col = __float_as_int(st[b * 3 + 2]);
+        if (v > m || (v == m && col < best)) { m = v; best = col; }
+    }
+    float s = 0.0f;
+    for (int b = 0; b < a.col_blocks; b++)
+        if (st[b * 3] > -FLT_MAX) s = fadd(s, fmul(st[b * 3 + 1], exp_neg(fsub(st[b * 3], m))));
+    float r = fdiv(1.0f, s);
+    if (a.probs) {
+        for (int c = 0; c < a.vocab; c++) {
+            float *v = a.y + (long)p * a.vocab + c;
+            *v = fmul(exp_neg(fsub(*v, m)), r);
+        }
+    } else {
+        a.y[2 * p] = (float)best;
+        a.y[2 * p + 1] = r;
+    }
+}
+
+// ------------------------------------------------------------ convtranspose
+
+// Non-overlapping transposed convolution (layers.rs:595-680): each input
+// pixel's channels times w [ic][kh][kw][oc] give its kh x kw block of
+// outputs. One thread per (input pixel, 4 output columns of the block); the
+// bias first or last as a pointwise layer of kh*kw*oc columns takes it.
+__global__ void __launch_bounds__(256) convt_kernel(const ConvTArgs a) {
+    const int cols = a.kh * a.kw * a.oc;
+    const int cg = (cols + 3) / 4;
+    const long total = (long)a.N * a.ih * a.iw * cg;
+    const int ow = a.iw * a.kw;
+    for (long g = (long)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (long)gridDim.x * blockDim.x) {
+        long pix = g / cg;
+        int c0 = int(g - pix * cg) * 4;
+        const float *x = a.x + pix * a.ic;
+        float acc[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[j] = (a.b && a.bias_first && c0 + j < cols) ? a.b[c0 + j] : 0.0f;
+        for (int i = 0; i < a.ic; i++) {
+            float xv = x[i];
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (c0 + j < cols) acc[j] = ffma(a.w[(long)i * cols + c0 + j], xv, acc[j]);
+        }
+        int hw = a.ih * a.iw;
+        int n = int(pix / hw), r = int(pix - (long)n * hw);
+        int iy = r / a.iw, ix = r - iy * a.iw;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int col = c0 + j;
+            if (col >= cols) break;
+            float v = acc[j];
+            if (a.b && !a.bias_first) v = fadd(v, a.b[col]);
+            v = activate(a.act, v);
+            int tap = col / a.oc, o = col - tap * a.oc;
+            int ky = tap / a.kw, kx = tap - ky * a.kw;
+            long oy = (long)iy * a.kh + ky, ox = (long)ix * a.kw + kx;
+            a.y[(((long)n * a.ih * a.kh + oy) * ow + ox) * a.oc + o] = v;
+        }
+    }
+}
+
+}  // namespace
+
+int launch_elt(const EltArgs &a, cudaStream_t s) {
+    int cout = a.mode == ELT_CONCAT ? a.c + a.c2 : a.c;
+    bool vec = cout % 4 == 0 && a.c % 4 == 0 && (a.mode != ELT_CONCAT || a.c2 % 4 == 0);
+    long total = (long)a.N * a.oh * a.ow * cout;
+    if (vec)
+        elt_kernel<4><<<grid_for(total / 4), 256, 0, s>>>(a);
+    else
+        elt_kernel<1><<<grid_for(total), 256, 0, s>>>(a);
+    return 1;
+}
+
+int launch_pool(const PoolArgs &a, cudaStream_t s) {
+    pool_kernel<<<grid_for((long)a.N * a.oh * a.ow * a.c), 256, 0, s>>>(a);
+    return 1;
+}
+
+int mean_chunks(int N, int hw, int c) {
+    (void)N;
+    (void)c;
+    int chunks = (hw + 511) / 512;
+    return chunks < 1 ? 1 : (chunks > 1024 ? 1024 : chunks);
+}
+
+int launch_mean(const MeanArgs &a, cudaStream_t s) {
+    int threads = 256;
+    int rows = a.c <= threads ? threads / a.c : 0;
+    size_t smem = rows ? sizeof(double) * rows * a.c : 0;
+    mean_partial_kernel<<<dim3(a.chunks, a.N), threads, smem, s>>>(a);
+    mean_final_kernel<<<(a.N * a.c + 255) / 256, 256, 0, s>>>(a);
+    return 2;
+}
+
+int launch_layernorm(const LayerNormArgs &a, cudaStream_t s) {
+    layernorm_kernel<<<(a.pixels + 3) / 4, 128, sizeof(float) * 4 * a.c, s>>>(a);
+    return 1;
+}
+
+bool attention_supported(int t, int c, int heads) {
+    int hd = c / heads;
+    return hd <= 64 && (size_t)2 * t * hd * sizeof(float) <= 160 * 1024;
+}
+
+int launch_attention(const AttentionArgs &a, cudaStream_t s) {
+    int hd = a.c / a.heads;
+    size_t smem = sizeof(float) * 2 * a.t * hd;
+    int threads = a.t < 32 ? 32 : (a.t > 256 ? 256 : (a.t + 31) / 32 * 32);
+    attention_kernel<<<a.N * a.heads, threads, smem, s>>>(a);
+    return 1;
+}
+
+int ctc_col_blocks(int cols) { return (cols + CTC_COLS - 1) / CTC_COLS; }
+
+int launch_ctc(const CtcArgs &a, cudaStream_t s) {
+    dim3 grid((a.pixels + CTC_PX - 1) / CTC_PX, a.col_blocks);
+    ctc_logits_kernel<<<grid, CTC_THREADS, sizeof(float) * a.ci * CTC_PX, s>>>(a);
+    ctc_merge_kernel<<<(a.pixels + 127) / 128, 128, 0, s>>>(a);
+    return 2;
+}
+
+int launch_convt(const ConvTArgs &a, cudaStream_t s) {
+    int cols = a.kh * a.kw * a.oc;
+    long total = (long)a.N * a.ih * a.iw * ((cols + 3) / 4);
+    convt_kernel<<<grid_for(total), 256, 0, s>>>(a);
+    return 1;
+}
+
+}  // namespace ppocr

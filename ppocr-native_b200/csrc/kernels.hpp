@@ -1,0 +1,167 @@
+// Launch arguments and entry points of every CUDA kernel of the backend.
+// Shared by the host runtime (model.cpp) and the kernels (*.cu). Tensors are
+// NHWC f32, lanes of one batch stored back to back ([N][H][W][C]).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+namespace ppocr {
+
+// Where a convolution adds its bias (the reference's tier-3 tiles decide it,
+// see Model::bias_mode): before the taps, after them, or before them except
+// on the last `ow % 4` pixels of each output row.
+enum BiasMode : int { BIAS_FIRST = 0, BIAS_LAST = 1, BIAS_FIRST_BUT_ROW_TAIL = 2 };
+
+// One input of a dense convolution: `c` channels of an image 2^shift times
+// smaller than the convolution's input along both axes, read as if
+// nearest-upsampled (the neck's upsample + concat, never written out;
+// reference `src/engine/kernels/dense.rs:7-19`).
+struct ConvSource {
+    const float *p = nullptr;
+    int c = 0;
+    int shift = 0;
+};
+
+constexpr int MAX_SOURCES = 4;
+
+struct ConvArgs {
+    ConvSource src[MAX_SOURCES];
+    int nsrc = 1;
+    int C = 0;                 // channels of all sources together
+    const float *w = nullptr;  // [kh][kw][C][oc]
+    const float *b = nullptr;  // [oc] or null
+    float *y = nullptr;        // [N][oh][ow][oc]
+    int N = 1, ih = 0, iw = 0, oh = 0, ow = 0, oc = 0;
+    int kh = 1, kw = 1, sh = 1, sw = 1, pt = 0, pl = 0;
+    int act = 0;
+    int bias_mode = BIAS_FIRST;
+    const float *gate = nullptr;  // [N][C]: input channel c of lane n is x * gate[n][c]
+    const float *res = nullptr;   // [N][oh][ow][oc]: y = act2(act(conv) + res)
+    int act2 = 0;
+};
+
+struct DwArgs {
+    const float *x = nullptr;  // [N][ih][iw][c]
+    const float *w = nullptr;  // [kh][kw][c]
+    const float *b = nullptr;  // [c] or null
+    float *y = nullptr;        // [N][oh][ow][c]
+    int N = 1, ih = 0, iw = 0, c = 0, oh = 0, ow = 0;
+    int kh = 3, kw = 3, sh = 1, sw = 1, pt = 0, pl = 0;
+    int act = 0;
+    double *mean_partial = nullptr;  // optional: per-block f64 channel sums of y
+};
+
+// Depthwise convolution whose output feeds a pointwise one straight from
+// shared memory.
+struct DwPwArgs {
+    DwArgs dw;                  // dw.y unused
+    const float *w2 = nullptr;  // [c][oc]
+    const float *b2 = nullptr;  // [oc] or null
+    float *y = nullptr;         // [N][oh][ow][oc]
+    int oc = 0;
+    int act2 = 0;
+    int bias_mode2 = BIAS_FIRST;
+    const float *res = nullptr;  // optional residual, y = act3(act2(pw) + res)
+    int act3 = 0;
+};
+
+enum EltMode : int {
+    ELT_ADD = 0,        // y = act(x + x2)
+    ELT_CHANNELMUL,     // y = x * g[n][c]
+    ELT_GATE_ADD,       // y = act(x * g[n][c] + x)
+    ELT_UPSAMPLE,       // y[r][c] = x[r/sh][c/sw]
+    ELT_UPSAMPLE_ADD,   // y = x2 + upsample(x)
+    ELT_CONCAT,         // y = [x | x2] per pixel
+};
+
+struct EltArgs {
+    int mode = ELT_ADD;
+    const float *x = nullptr, *x2 = nullptr;
+    float *y = nullptr;
+    int N = 1, ih = 0, iw = 0, oh = 0, ow = 0, c = 0, c2 = 0;
+    int sh = 1, sw = 1;
+    int act = 0;
+};
+
+struct PoolArgs {
+    const float *x = nullptr;
+    float *y = nullptr;
+    int N = 1, ih = 0, iw = 0, c = 0, oh = 0, ow = 0, kh = 1, kw = 1, sh = 1, sw = 1;
+    bool average = false;
+};
+
+struct MeanArgs {
+    const float *x = nullptr;  // [N][hw][c]
+    float *y = nullptr;        // [N][c]
+    double *partial = nullptr; // [N][chunks][c] scratch
+    int N = 1, hw = 0, c = 0, chunks = 1;
+};
+
+struct LayerNormArgs {
+    const float *x = nullptr, *w = nullptr;  // w = [gamma | beta | eps]
+    float *y = nullptr;
+    int pixels = 0, c = 0;
+};
+
+struct AttentionArgs {
+    const float *x = nullptr;  // [N][t][3c]
+    float *y = nullptr;        // [N][t][c]
+    const float *scale = nullptr;
+    int N = 1, t = 0, c = 0, heads = 1;
+};
+
+// CTC head over `cols` = 16 * ceil(vocab / 16) panel columns: each block
+// reduces a range of columns to a (max, sum of exp, best column) state per
+// pixel in `partial`; the merge turns them into the output.
+struct CtcArgs {
+    const float *x = nullptr;  // [pixels][ci]
+    const float *w = nullptr;  // [cols/16][ci][16]
+    const float *b = nullptr;  // [cols]
+    float *y = nullptr;        // argmax: [pixels][2]; probs: [pixels][vocab]
+    float *partial = nullptr;  // [pixels][col_blocks][3]
+    int pixels = 0, ci = 0, vocab = 0, cols = 0, col_blocks = 0;
+    bool probs = false;
+};
+
+struct ConvTArgs {
+    const float *x = nullptr;  // [N][ih][iw][ic]
+    const float *w = nullptr;  // [ic][kh][kw][oc]
+    const float *b = nullptr;  // [kh*kw*oc] or null
+    float *y = nullptr;        // [N][ih*kh][iw*kw][oc]
+    int N = 1, ih = 0, iw = 0, ic = 0, oc = 0, kh = 2, kw = 2;
+    int act = 0;
+    bool bias_first = true;
+    // A second transposed convolution fed from the first one's output
+    // block on chip (the DB head's pair); w2 null when absent.
+    const float *w2 = nullptr, *b2 = nullptr;
+    int oc2 = 0, kh2 = 2, kw2 = 2, act2 = 0;
+    bool bias_first2 = true;
+};
+
+// Each returns the number of kernels it launched.
+int launch_conv(const ConvArgs &a, cudaStream_t s);
+int launch_dw(const DwArgs &a, cudaStream_t s);
+int launch_dw_pw(const DwPwArgs &a, cudaStream_t s);
+int launch_elt(const EltArgs &a, cudaStream_t s);
+int launch_pool(const PoolArgs &a, cudaStream_t s);
+int launch_mean(const MeanArgs &a, cudaStream_t s);
+int launch_layernorm(const LayerNormArgs &a, cudaStream_t s);
+int launch_attention(const AttentionArgs &a, cudaStream_t s);
+int launch_ctc(const CtcArgs &a, cudaStream_t s);
+int launch_convt(const ConvTArgs &a, cudaStream_t s);
+
+// Per-device set-up (shared-memory ceilings); call with the device current.
+void configure_dw_kernels();
+
+// Scratch sizes (elements) the launches above need.
+int mean_chunks(int N, int hw, int c);
+int ctc_col_blocks(int cols);
+// Largest shared-memory need of launch_dw_pw for `c` input channels; 0 when
+// that kernel cannot take them.
+bool dw_pw_supported(const DwPwArgs &a);
+bool attention_supported(int t, int c, int heads);
+
+}  // namespace ppocr

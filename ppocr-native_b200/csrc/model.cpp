@@ -1,0 +1,969 @@
+// The CUDA backend of the ppocr-native engine: a PPOCRPL1 plan on one GPU,
+// run over lanes of images (the Vulkan `GpuModel` it replaces is ppocr-native
+// `src/engine/gpu/mod.rs:81-291`).
+//
+// Layout in device memory. Weights: every operation's weight and bias blocks
+// re-packed into one arena, each block on a 256-byte boundary, so kernels may
+// read them as float4. Tensors: lanes of equal size form a group that runs
+// as one batch; each plan buffer of a group is one allocation of
+// lanes x (the most floats any operation writes there), tensors stored NHWC
+// with the lanes back to back. Scratch: per group, the f64 partial sums of
+// the channel means and the per-column-block states of the CTC head.
+//
+// Schedule. The plan's operations are grouped into steps by `fuse`: a
+// depthwise layer and the pointwise one it feeds run as one kernel; a
+// squeeze-and-excite gate is folded into the next pointwise layer's input
+// load; a residual add into the epilogue of the layer that produces one of
+// its terms; the RSE gate and its residual add into one pass; nearest
+// upsampling and channel concatenation into the sources of the dense
+// convolution that reads them (the reference's own GPU fusion rules,
+// gpu/mod.rs:458-533, and CPU ones, schedule.rs:273-466). Each step is a
+// closure that launches its kernels on the model's stream; the whole run is
+// captured once per set of sizes into a CUDA graph and replayed.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <functional>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <set>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/ppocr_cuda.h"
+#include "kernels.hpp"
+#include "plan.hpp"
+
+using namespace ppocr;
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const std::string &msg) {
+    g_error = msg;
+    return code;
+}
+
+bool cuda_ok(cudaError_t e, const char *what, int *code = nullptr) {
+    if (e == cudaSuccess) return true;
+    g_error = std::string(what) + ": " + cudaGetErrorString(e);
+    if (code) *code = e == cudaErrorMemoryAllocation ? PPOCR_E_NOMEM : PPOCR_E_DEVICE;
+    return false;
+}
+
+// Raise per-kernel limits once per device.
+void configure_device(int device) {
+    static std::mutex mu;
+    static std::set<int> done;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count(device)) return;
+    configure_dw_kernels();
+    done.insert(device);
+}
+
+struct DeviceBuffer {
+    void *p = nullptr;
+    size_t bytes = 0;
+    DeviceBuffer() = default;
+    DeviceBuffer(const DeviceBuffer &) = delete;
+    DeviceBuffer &operator=(const DeviceBuffer &) = delete;
+    ~DeviceBuffer() {
+        if (p) cudaFree(p);
+    }
+};
+
+struct HostBuffer {
+    void *p = nullptr;
+    size_t bytes = 0;
+    HostBuffer() = default;
+    HostBuffer(const HostBuffer &) = delete;
+    HostBuffer &operator=(const HostBuffer &) = delete;
+    ~HostBuffer() {
+        if (p) cudaFreeHost(p);
+    }
+};
+
+// Weights on one device, shared by the models made with share_weights.
+struct Weights {
+    int device = 0;
+    DeviceBuffer arena;
+    std::vector<size_t> w_at, b_at;  // per op: float offset of its blocks in the arena (or SIZE_MAX)
+    const float *w(size_t op) const {
+        return w_at[op] == SIZE_MAX ? nullptr : static_cast<const float *>(arena.p) + w_at[op];
+    }
+    const float *b(size_t op) const {
+        return b_at[op] == SIZE_MAX ? nullptr : static_cast<const float *>(arena.p) + b_at[op];
+    }
+};
+
+// ------------------------------------------------------------- fusion plan
+
+enum StepKind {
+    S_OP,        // one plan operation, its own kernel(s)
+    S_DW_PW,     // depthwise `a` feeding pointwise `b` [+ residual add `c`]
+    S_CONV,      // a dense convolution with optional gate, sources, residual
+    S_GATE_ADD,  // channelmul `a` and add `b`: y = act(x * g + x)
+    S_SKIP,      // folded into another step
+};
+
+struct Step {
+    StepKind kind = S_OP;
+    size_t op = 0;              // the operation whose output this step writes (its position)
+    size_t a = 0, b = 0, c = 0; // ops involved (dw, pw, add / channelmul, add)
+    bool has_add = false;       // residual add folded in (op `c`)
+    bool gated = false;         // SE gate folded in: the conv reads channelmul `a`'s inputs
+    // Sources of a dense conv: (buffer, channels, shift), in channel order.
+    struct Src {
+        size_t slot, c;
+        int shift;
+    };
+    std::vector<Src> srcs;
+    std::string name;
+};
+
+// Which later operations read the value op `i` writes, until the buffer is
+// written again; `out` when that value is a plan output.
+struct Uses {
+    std::vector<size_t> readers;
+    bool out = false;
+};
+
+std::vector<Uses> find_uses(const Plan &p) {
+    std::vector<Uses> u(p.ops.size());
+    for (size_t i = 0; i < p.ops.size(); i++) {
+        size_t y = p.ops[i].y;
+        size_t j = i + 1;
+        for (; j < p.ops.size(); j++) {
+            const Op &o = p.ops[j];
+            if (o.x == y || (o.has_second() && o.x2 == y)) u[i].readers.push_back(j);
+            if (o.y == y) break;
+        }
+        if (j == p.ops.size())
+            for (size_t s : p.outputs)
+                if (s == y) u[i].out = true;
+    }
+    return u;
+}
+
+bool only_reader(const Uses &u, size_t j) { return !u.out && u.readers.size() == 1 && u.readers[0] == j; }
+
+// No op strictly between i and j writes buffer `slot`.
+bool intact(const Plan &p, size_t slot, size_t i, size_t j) {
+    for (size_t k = i + 1; k < j; k++)
+        if (p.ops[k].y == slot) return false;
+    return true;
+}
+
+bool is_pow2(size_t v, int &shift) {
+    shift = 0;
+    while ((size_t(1) << shift) < v) shift++;
+    return (size_t(1) << shift) == v && shift < 16;
+}
+
+// The channel sources of a dense windowed conv reading a chain of
+// concatenations of (nearest-upsampled) tensors; false when it is not one.
+bool chain_sources(const Plan &p, const std::vector<Uses> &u, size_t conv, size_t slot, size_t before, int shift,
+                   std::vector<Step::Src> &out, std::vector<size_t> &folded) {
+    // The op before `before` that wrote `slot`.
+    size_t w = SIZE_MAX;
+    for (size_t k = before; k-- > 0;)
+        if (p.ops[k].y == slot) { w = k; break; }
+    if (w != SIZE_MAX && only_reader(u[w], before) && intact(p, slot, w, conv)) {
+        const Op &o = p.ops[w];
+        int s;
+        if (o.kind == K_UPSAMPLE && o.sh == o.sw && is_pow2(o.sh, s) && s > 0 && shift + s < 16) {
+            folded.push_back(w);
+            return chain_sources(p, u, conv, o.x, w, shift + s, out, folded);
+        }
+        if (o.kind == K_CONCATC) {
+            folded.push_back(w);
+            return chain_sources(p, u, conv, o.x, w, shift, out, folded) &&
+                   chain_sources(p, u, conv, o.x2, w, shift, out, folded);
+        }
+    }
+    // A plain tensor: it must still hold its value when the conv runs.
+    size_t c = 0;
+    {
+        size_t k = before;
+        for (; k-- > 0;)
+            if (p.ops[k].y == slot) { c = p.ops[k].oc; break; }
+        if (k == SIZE_MAX) {
+            if (slot != p.slot) return false;
+            c = p.c;
+        }
+    }
+    if (!intact(p, slot, before, conv)) return false;
+    out.push_back({slot, c, shift});
+    return out.size() <= MAX_SOURCES;
+}
+
+std::vector<Step> fuse(const Plan &p, bool enabled) {
+    std::vector<Step> steps(p.ops.size());
+    for (size_t i = 0; i < p.ops.size(); i++) {
+        steps[i].kind = S_OP;
+        steps[i].op = i;
+        steps[i].a = i;
+        steps[i].name = kind_name(p.ops[i].kind);
+    }
+    if (!enabled) return steps;
+    std::vector<Uses> u = find_uses(p);
+    // A fused kernel must not write a buffer it reads: the plan rules that
+    // out per operation (plan.rs:680-685), not across the ones fused here.
+    auto disjoint = [](const std::vector<size_t> &reads, size_t write) {
+        return std::find(reads.begin(), reads.end(), write) == reads.end();
+    };
+    auto residual = [&](Step &st, size_t producer, size_t pos, std::vector<size_t> reads) {
+        // An add right after `pos` reading the producer's output once.
+        size_t j = pos + 1;
+        if (j >= p.ops.size() || !only_reader(u[producer], j)) return;
+        const Op &add = p.ops[j];
+        if (add.kind != K_ADD || add.x == add.x2) return;
+        size_t other = add.x == p.ops[producer].y ? add.x2 : add.x;
+        reads.push_back(other);
+        if (!disjoint(reads, add.y)) return;
+        st.has_add = true;
+        st.c = j;
+        st.op = j;
+        steps[j].kind = S_SKIP;
+        st.name += "+add";
+    };
+    for (size_t i = 0; i < p.ops.size(); i++) {
+        if (steps[i].kind == S_SKIP) continue;
+        const Op &op = p.ops[i];
+        // depthwise -> pointwise
+        if (op.kind == K_DWCONV && i + 1 < p.ops.size() && only_reader(u[i], i + 1)) {
+            const Op &pw = p.ops[i + 1];
+            if (pw.pointwise() && pw.x == op.y && pw.y != op.x) {
+                DwPwArgs probe;
+                probe.dw.c = int(op.oc);
+                probe.oc = int(pw.oc);
+                if (dw_pw_supported(probe)) {
+                    Step &st = steps[i];
+                    st.kind = S_DW_PW;
+                    st.a = i;
+                    st.b = i + 1;
+                    st.op = i + 1;
+                    st.name = "dw+pw";
+                    steps[i + 1].kind = S_SKIP;
+                    residual(st, i + 1, i + 1, {op.x});
+                    continue;
+                }
+            }
+        }
+        // channelmul feeding a pointwise conv: the gate joins its input load
+        if (op.kind == K_CHANNELMUL && i + 1 < p.ops.size() && only_reader(u[i], i + 1)) {
+            const Op &pw = p.ops[i + 1];
+            if (pw.pointwise() && pw.x == op.y && pw.n2 == 0 && disjoint({op.x, op.x2}, pw.y)) {
+                Step &st = steps[i];
+                st.kind = S_CONV;
+                st.gated = true;
+                st.a = i;
+                st.b = i + 1;
+                st.op = i + 1;
+                st.srcs = {{op.x, op.ic, 0}};
+                st.name = "gate+conv";
+                steps[i + 1].kind = S_SKIP;
+                residual(st, i + 1, i + 1, {op.x, op.x2});
+                continue;
+            }
+        }
+        // channelmul + add of its input: the RSE gate
+        if (op.kind == K_CHANNELMUL && i + 1 < p.ops.size() && only_reader(u[i], i + 1)) {
+            const Op &add = p.ops[i + 1];
+            if (add.kind == K_ADD && ((add.x == op.y && add.x2 == op.x) || (add.x2 == op.y && add.x == op.x)) &&
+                disjoint({op.x, op.x2}, add.y)) {
+                Step &st = steps[i];
+                st.kind = S_GATE_ADD;
+                st.a = i;
+                st.b = i + 1;
+                st.op = i + 1;
+                st.name = "gate_add";
+                steps[i + 1].kind = S_SKIP;
+                continue;
+            }
+        }
+        if (op.kind == K_CONV) {
+            Step &st = steps[i];
+            st.kind = S_CONV;
+            st.b = i;
+            std::vector<size_t> folded;
+            std::vector<Step::Src> srcs;
+            bool chained = false;
+            if (!op.pointwise()) {
+                chained = chain_sources(p, u, i, op.x, i, 0, srcs, folded);
+                if (chained && op.n2 > 0) {
+                    if (intact(p, op.x2, i, i)) srcs.push_back({op.x2, op.n2, 0});
+                    chained = srcs.size() <= MAX_SOURCES;
+                }
+                if (chained && folded.empty()) chained = false;
+                for (const Step::Src &src : srcs)
+                    if (src.slot == op.y) chained = false;
+            }
+            if (chained) {
+                st.srcs = srcs;
+                for (size_t f : folded) steps[f].kind = S_SKIP;
+                st.name = "conv(" + std::to_string(srcs.size()) + " sources)";
+            } else {
+                st.srcs = {{op.x, op.ic, 0}};
+                if (op.n2) st.srcs.push_back({op.x2, op.n2, 0});
+                st.name = "conv";
+            }
+            std::vector<size_t> reads;
+            for (const Step::Src &src : st.srcs) reads.push_back(src.slot);
+            residual(st, i, i, reads);
+        }
+    }
+    return steps;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------- model
+
+struct Group {
+    size_t h = 0, w = 0;
+    std::vector<size_t> lanes;  // model lane indices, in batch order
+    Plan plan;
+    std::vector<std::unique_ptr<DeviceBuffer>> slots;
+    DeviceBuffer mean_scratch, ctc_scratch;
+    HostBuffer in_host;                  // [N][h][w][c]
+    std::vector<std::unique_ptr<HostBuffer>> out_host;  // per output: [N][n]
+    std::vector<std::function<int(cudaStream_t)>> launches;
+    float *slot_ptr(size_t s) const { return static_cast<float *>(slots[s]->p); }
+};
+
+struct ppocr_model {
+    int device = 0;
+    std::string name;
+    bool integrated = false;
+    cudaStream_t stream = nullptr;      // where the model runs
+    cudaStream_t own_stream = nullptr;  // the stream it made
+    cudaEvent_t done = nullptr;
+    Plan plan;  // at the load size
+    std::shared_ptr<Weights> weights;
+    size_t weight_floats = 0;
+    uint32_t options = 0;
+    std::vector<Step> steps;
+    bool steps_fused = false;
+    std::vector<std::pair<size_t, size_t>> sizes;  // per lane (h, w)
+    std::vector<std::pair<size_t, size_t>> where;  // per lane (group, index in group)
+    std::vector<std::unique_ptr<Group>> groups;
+    cudaGraphExec_t graph_host = nullptr, graph_device = nullptr;
+    size_t launches = 0;
+    bool pending = false;
+
+    ~ppocr_model() {
+        if (device >= 0) cudaSetDevice(device);
+        if (stream) cudaStreamSynchronize(stream);
+        drop_graphs();
+        groups.clear();
+        if (done) cudaEventDestroy(done);
+        if (own_stream) cudaStreamDestroy(own_stream);
+    }
+
+    void drop_graphs() {
+        if (graph_host) cudaGraphExecDestroy(graph_host);
+        if (graph_device) cudaGraphExecDestroy(graph_device);
+        graph_host = graph_device = nullptr;
+    }
+
+    int bias_mode(const Op &op) const;
+    int build_group(Group &g, std::string &err);
+    int record(bool copies);
+    int enqueue(bool copies);
+};
+
+// Where the reference's tier-3 kernels add a convolution's bias: first for
+// RGB stems (conv.rs:171-177), for pointwise layers with a multiple of 16
+// output channels (pointwise.rs:77-102), for windowed ones of such width but
+// the last `ow % 4` pixels of each row (dense.rs:60-66); last otherwise
+// (pointwise.rs:33-35, dense.rs:127-130).
+int ppocr_model::bias_mode(const Op &op) const {
+    if (!op.pointwise() && op.ic == 3 && op.n2 == 0) return BIAS_FIRST;
+    if (op.oc % 16) return BIAS_LAST;
+    if (op.pointwise()) return BIAS_FIRST;
+    return BIAS_FIRST_BUT_ROW_TAIL;
+}
+
+int ppocr_model::build_group(Group &g, std::string &err) {
+    Plan &p = g.plan;
+    const size_t N = g.lanes.size();
+    int code = PPOCR_OK;
+    // Tensors.
+    g.slots.clear();
+    for (size_t s = 0; s < p.pool.size(); s++) {
+        auto b = std::make_unique<DeviceBuffer>();
+        b->bytes = std::max<size_t>(p.pool[s], 1) * N * sizeof(float);
+        if (!cuda_ok(cudaMalloc(&b->p, b->bytes), "allocating a tensor", &code)) {
+            err = g_error;
+            return code;
+        }
+        g.slots.push_back(std::move(b));
+    }
+    // Scratch.
+    size_t mean_doubles = 1, ctc_floats = 1;
+    for (const Op &op : p.ops) {
+        if (op.kind == K_MEAN)
+            mean_doubles = std::max(mean_doubles, N * mean_chunks(int(N), int(op.ih * op.iw), int(op.ic)) * op.ic);
+        if (op.kind == K_CTCHEAD || op.kind == K_CTCARGMAX) {
+            size_t vocab = op.kind == K_CTCHEAD ? op.oc : op.n2;
+            size_t cols = (vocab + 15) / 16 * 16;
+            ctc_floats = std::max(ctc_floats, N * op.iw * ctc_col_blocks(int(cols)) * 3);
+        }
+    }
+    g.mean_scratch.bytes = mean_doubles * sizeof(double);
+    g.ctc_scratch.bytes = ctc_floats * sizeof(float);
+    if (!cuda_ok(cudaMalloc(&g.mean_scratch.p, g.mean_scratch.bytes), "allocating scratch", &code) ||
+        !cuda_ok(cudaMalloc(&g.ctc_scratch.p, g.ctc_scratch.bytes), "allocating scratch", &code)) {
+        err = g_error;
+        return code;
+    }
+    // Page-locked host staging.
+    g.in_host.bytes = N * p.h * p.w * p.c * sizeof(float);
+    if (!cuda_ok(cudaHostAlloc(&g.in_host.p, g.in_host.bytes, cudaHostAllocDefault), "allocating host input", &code)) {
+        err = g_error;
+        return code;
+    }
+    std::memset(g.in_host.p, 0, g.in_host.bytes);
+    g.out_host.clear();
+    for (size_t k = 0; k < p.outputs.size(); k++) {
+        auto hb = std::make_unique<HostBuffer>();
+        hb->bytes = std::max<size_t>(p.out_n[k], 1) * N * sizeof(float);
+        if (!cuda_ok(cudaHostAlloc(&hb->p, hb->bytes, cudaHostAllocDefault), "allocating host output", &code)) {
+            err = g_error;
+            return code;
+        }
+        std::memset(hb->p, 0, hb->bytes);
+        g.out_host.push_back(std::move(hb));
+    }
+
+    // Launches.
+    g.launches.clear();
+    const Weights &W = *weights;
+    const int n = int(N);
+    auto buf = [&g](size_t s) { return g.slot_ptr(s); };
+    for (const Step &st : steps) {
+        if (st.kind == S_SKIP) continue;
+        if (st.kind == S_DW_PW) {
+            const Op &dw = p.ops[st.a], &pw = p.ops[st.b];
+            DwPwArgs a;
+            a.dw.x = buf(dw.x); a.dw.w = W.w(st.a); a.dw.b = W.b(st.a);
+            a.dw.N = n; a.dw.ih = int(dw.ih); a.dw.iw = int(dw.iw); a.dw.c = int(dw.ic);
+            a.dw.oh = int(dw.oh); a.dw.ow = int(dw.ow); a.dw.kh = int(dw.kh); a.dw.kw = int(dw.kw);
+            a.dw.sh = int(dw.sh); a.dw.sw = int(dw.sw); a.dw.pt = int(dw.pt); a.dw.pl = int(dw.pl);
+            a.dw.act = dw.fused;
+            a.w2 = W.w(st.b); a.b2 = W.b(st.b); a.oc = int(pw.oc); a.act2 = pw.fused;
+            a.bias_mode2 = bias_mode(pw);
+            a.y = buf(pw.y);
+            if (st.has_add) {
+                const Op &add = p.ops[st.c];
+                a.res = buf(add.x == pw.y ? add.x2 : add.x);
+                a.act3 = add.fused;
+                a.y = buf(add.y);
+            }
+            g.launches.push_back([a](cudaStream_t s) { return launch_dw_pw(a, s); });
+            continue;
+        }
+        if (st.kind == S_CONV) {
+            const Op &op = p.ops[st.b];
+            ConvArgs a;
+            a.nsrc = int(st.srcs.size());
+            a.C = 0;
+            for (size_t k = 0; k < st.srcs.size(); k++) {
+                a.src[k].p = buf(st.srcs[k].slot);
+                a.src[k].c = int(st.srcs[k].c);
+                a.src[k].shift = st.srcs[k].shift;
+                a.C += int(st.srcs[k].c);
+            }
+            if (st.gated) a.gate = buf(p.ops[st.a].x2);
+            a.w = W.w(st.b); a.b = W.b(st.b);
+            a.N = n; a.ih = int(op.ih); a.iw = int(op.iw); a.oh = int(op.oh); a.ow = int(op.ow); a.oc = int(op.oc);
+            a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
+            a.pt = int(op.pt); a.pl = int(op.pl);
+            a.act = op.fused;
+            a.bias_mode = bias_mode(op);
+            a.y = buf(op.y);
+            if (st.has_add) {
+                const Op &add = p.ops[st.c];
+                a.res = buf(add.x == op.y ? add.x2 : add.x);
+                a.act2 = add.fused;
+                a.y = buf(add.y);
+            }
+            g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
+            continue;
+        }
+        if (st.kind == S_GATE_ADD) {
+            const Op &cm = p.ops[st.a], &add = p.ops[st.b];
+            EltArgs a;
+            a.mode = ELT_GATE_ADD;
+            a.x = buf(cm.x); a.x2 = buf(cm.x2); a.y = buf(add.y);
+            a.N = n; a.oh = int(cm.oh); a.ow = int(cm.ow); a.c = int(cm.oc); a.act = add.fused;
+            g.launches.push_back([a](cudaStream_t s) { return launch_elt(a, s); });
+            continue;
+        }
+        // One operation alone.
+        const size_t i = st.a;
+        const Op &op = p.ops[i];
+        switch (op.kind) {
+        case K_CONV: {
+            ConvArgs a;
+            a.src[0] = {buf(op.x), int(op.ic), 0};
+            a.nsrc = 1;
+            if (op.n2) { a.src[1] = {buf(op.x2), int(op.n2), 0}; a.nsrc = 2; }
+            a.C = int(op.ic + op.n2);
+            a.w = W.w(i); a.b = W.b(i);
+            a.N = n; a.ih = int(op.ih); a.iw = int(op.iw); a.oh = int(op.oh); a.ow = int(op.ow); a.oc = int(op.oc);
+            a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
+            a.pt = int(op.pt); a.pl = int(op.pl); a.act = op.fused; a.bias_mode = bias_mode(op);
+            a.y = buf(op.y);
+            g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
+            break;
+        }
+        case K_DWCONV: {
+            DwArgs a;
+            a.x = buf(op.x); a.w = W.w(i); a.b = W.b(i); a.y = buf(op.y);
+            a.N = n; a.ih = int(op.ih); a.iw = int(op.iw); a.c = int(op.ic); a.oh = int(op.oh); a.ow = int(op.ow);
+            a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
+            a.pt = int(op.pt); a.pl = int(op.pl); a.act = op.fused;
+            g.launches.push_back([a](cudaStream_t s) { return launch_dw(a, s); });
+            break;
+        }
+        case K_ADD: case K_CHANNELMUL: case K_CONCATC: case K_UPSAMPLE: case K_UPSAMPLEADD: {
+            EltArgs a;
+            a.mode = op.kind == K_ADD ? ELT_ADD : op.kind == K_CHANNELMUL ? ELT_CHANNELMUL
+                     : op.kind == K_CONCATC ? ELT_CONCAT : op.kind == K_UPSAMPLE ? ELT_UPSAMPLE : ELT_UPSAMPLE_ADD;
+            a.x = buf(op.x); a.x2 = op.has_second() ? buf(op.x2) : nullptr; a.y = buf(op.y);
+            a.N = n; a.ih = int(op.ih); a.iw = int(op.iw); a.oh = int(op.oh); a.ow = int(op.ow);
+            a.c = int(op.kind == K_CONCATC ? op.ic : op.oc); a.c2 = int(op.n2);
+            a.sh = int(std::max<size_t>(op.sh, 1)); a.sw = int(std::max<size_t>(op.sw, 1)); a.act = op.fused;
+            g.launches.push_back([a](cudaStream_t s) { return launch_elt(a, s); });
+            break;
+        }
+        case K_MAXPOOL: case K_AVGPOOL: {
+            PoolArgs a;
+            a.x = buf(op.x); a.y = buf(op.y);
+            a.N = n; a.ih = int(op.ih); a.iw = int(op.iw); a.c = int(op.ic); a.oh = int(op.oh); a.ow = int(op.ow);
+            a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
+            a.average = op.kind == K_AVGPOOL;
+            g.launches.push_back([a](cudaStream_t s) { return launch_pool(a, s); });
+            break;
+        }
+        case K_MEAN: {
+            MeanArgs a;
+            a.x = buf(op.x); a.y = buf(op.y); a.partial = static_cast<double *>(g.mean_scratch.p);
+            a.N = n; a.hw = int(op.ih * op.iw); a.c = int(op.ic); a.chunks = mean_chunks(n, a.hw, a.c);
+            g.launches.push_back([a](cudaStream_t s) { return launch_mean(a, s); });
+            break;
+        }
+        case K_LAYERNORM: {
+            LayerNormArgs a;
+            a.x = buf(op.x); a.w = W.w(i); a.y = buf(op.y);
+            a.pixels = int(N * op.oh * op.ow); a.c = int(op.oc);
+            g.launches.push_back([a](cudaStream_t s) { return launch_layernorm(a, s); });
+            break;
+        }
+        case K_ATTENTION: {
+            if (!attention_supported(int(op.iw), int(op.oc), int(op.n2))) {
+                err = "attention over " + std::to_string(op.iw) + " steps with head size " +
+                      std::to_string(op.oc / op.n2) + " exceeds this backend";
+                return PPOCR_E_UNSUPPORTED;
+            }
+            AttentionArgs a;
+            a.x = buf(op.x); a.y = buf(op.y); a.scale = W.w(i);
+            a.N = n; a.t = int(op.iw); a.c = int(op.oc); a.heads = int(op.n2);
+            g.launches.push_back([a](cudaStream_t s) { return launch_attention(a, s); });
+            break;
+        }
+        case K_CTCHEAD: case K_CTCARGMAX: {
+            CtcArgs a;
+            a.x = buf(op.x); a.w = W.w(i); a.b = W.b(i); a.y = buf(op.y);
+            a.partial = static_cast<float *>(g.ctc_scratch.p);
+            a.pixels = int(N * op.iw); a.ci = int(op.ic);
+            a.probs = op.kind == K_CTCHEAD;
+            a.vocab = int(a.probs ? op.oc : op.n2);
+            a.cols = (a.vocab + 15) / 16 * 16;
+            a.col_blocks = ctc_col_blocks(a.cols);
+            g.launches.push_back([a](cudaStream_t s) { return launch_ctc(a, s); });
+            break;
+        }
+        case K_CONVTRANSPOSE: {
+            ConvTArgs a;
+            a.x = buf(op.x); a.w = W.w(i); a.b = W.b(i); a.y = buf(op.y);
+            a.N = n; a.ih = int(op.ih); a.iw = int(op.iw); a.ic = int(op.ic); a.oc = int(op.oc);
+            a.kh = int(op.kh); a.kw = int(op.kw); a.act = op.fused;
+            a.bias_first = (op.kh * op.kw * op.oc) % 16 == 0;
+            g.launches.push_back([a](cudaStream_t s) { return launch_convt(a, s); });
+            break;
+        }
+        default:
+            err = std::string("operation kind ") + kind_name(op.kind) + " is not supported";
+            return PPOCR_E_UNSUPPORTED;
+        }
+    }
+    return PPOCR_OK;
+}
+
+// Record one run on the stream: the input copies (when `copies`), every
+// step's kernels, the output copies.
+int ppocr_model::record(bool copies) {
+    size_t count = 0;
+    for (auto &gp : groups) {
+        Group &g = *gp;
+        if (copies) {
+            if (!cuda_ok(cudaMemcpyAsync(g.slot_ptr(g.plan.slot), g.in_host.p, g.in_host.bytes,
+                                         cudaMemcpyHostToDevice, stream), "copying the input"))
+                return PPOCR_E_DEVICE;
+        }
+        for (auto &l : g.launches) count += size_t(l(stream));
+        if (copies) {
+            for (size_t k = 0; k < g.plan.outputs.size(); k++) {
+                size_t bytes = g.lanes.size() * g.plan.out_n[k] * sizeof(float);
+                if (!cuda_ok(cudaMemcpyAsync(g.out_host[k]->p, g.slot_ptr(g.plan.outputs[k]), bytes,
+                                             cudaMemcpyDeviceToHost, stream), "copying an output"))
+                    return PPOCR_E_DEVICE;
+            }
+        }
+    }
+    launches = count;
+    if (!cuda_ok(cudaGetLastError(), "launching a kernel")) return PPOCR_E_DEVICE;
+    return PPOCR_OK;
+}
+
+int ppocr_model::enqueue(bool copies) {
+    if (!cuda_ok(cudaSetDevice(device), "selecting the device")) return PPOCR_E_DEVICE;
+    if (groups.empty()) return fail(PPOCR_E_SIZE, "the model has no lanes");
+    int rc;
+    if (options & PPOCR_OPT_NO_GRAPH) {
+        rc = record(copies);
+        if (rc) return rc;
+    } else {
+        cudaGraphExec_t &exec = copies ? graph_host : graph_device;
+        if (!exec) {
+            cudaGraph_t graph = nullptr;
+            if (!cuda_ok(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "capturing the run"))
+                return PPOCR_E_DEVICE;
+            rc = record(copies);
+            cudaError_t e = cudaStreamEndCapture(stream, &graph);
+            if (rc) {
+                if (graph) cudaGraphDestroy(graph);
+                return rc;
+            }
+            if (!cuda_ok(e, "capturing the run")) return PPOCR_E_DEVICE;
+            e = cudaGraphInstantiate(&exec, graph, 0);
+            cudaGraphDestroy(graph);
+            if (!cuda_ok(e, "instantiating the run")) return PPOCR_E_DEVICE;
+        }
+        if (!cuda_ok(cudaGraphLaunch(exec, stream), "launching the run")) return PPOCR_E_DEVICE;
+    }
+    if (!cuda_ok(cudaEventRecord(done, stream), "recording completion")) return PPOCR_E_DEVICE;
+    pending = true;
+    return PPOCR_OK;
+}
+
+// ------------------------------------------------------------------- C ABI
+
+namespace {
+
+int make_model(Plan &&plan, std::shared_ptr<Weights> weights, size_t weight_floats, int device, ppocr_model **out) {
+    auto m = std::make_unique<ppocr_model>();
+    m->device = device;
+    m->plan = std::move(plan);
+    m->weights = std::move(weights);
+    m->weight_floats = weight_floats;
+    cudaDeviceProp prop;
+    if (!cuda_ok(cudaSetDevice(device), "selecting the device") ||
+        !cuda_ok(cudaGetDeviceProperties(&prop, device), "reading the device"))
+        return PPOCR_E_DEVICE;
+    m->name = prop.name;
+    m->integrated = prop.integrated != 0;
+    configure_device(device);
+    if (!cuda_ok(cudaStreamCreateWithFlags(&m->own_stream, cudaStreamNonBlocking), "creating a stream") ||
+        !cuda_ok(cudaEventCreateWithFlags(&m->done, cudaEventDisableTiming), "creating an event"))
+        return PPOCR_E_DEVICE;
+    m->stream = m->own_stream;
+    uint32_t hw[2] = {uint32_t(m->plan.h), uint32_t(m->plan.w)};
+    int rc = ppocr_model_set_sizes(m.get(), hw, 1);
+    if (rc) return rc;
+    *out = m.release();
+    return PPOCR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ppocr_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+const char *ppocr_last_error(void) { return g_error.c_str(); }
+
+int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_model **out) {
+    g_error.clear();
+    if (!bytes || !out) return fail(PPOCR_E_ARG, "null argument");
+    *out = nullptr;
+    // The plan is checked before any device is touched.
+    Plan plan;
+    std::vector<float> values;
+    std::string err;
+    if (!Plan::parse(static_cast<const uint8_t *>(bytes), len, plan, values, err)) return fail(PPOCR_E_PLAN, err);
+    int count = ppocr_device_count();
+    if (device < 0 || device >= count)
+        return fail(PPOCR_E_DEVICE, "device " + std::to_string(device) + " of " + std::to_string(count));
+    if (!cuda_ok(cudaSetDevice(device), "selecting the device")) return PPOCR_E_DEVICE;
+    // Re-pack every block on a 256-byte boundary.
+    auto w = std::make_shared<Weights>();
+    w->device = device;
+    std::vector<float> arena;
+    auto place = [&](size_t at, size_t n) {
+        if (!n) return SIZE_MAX;
+        while (arena.size() % 64) arena.push_back(0.0f);
+        size_t where = arena.size();
+        arena.insert(arena.end(), values.begin() + at, values.begin() + at + n);
+        return where;
+    };
+    for (const Op &op : plan.ops) {
+        w->w_at.push_back(place(op.w0, op.w1));
+        w->b_at.push_back(place(op.b0, op.b1));
+    }
+    arena.resize(std::max<size_t>(arena.size(), 1) + 64, 0.0f);
+    int code = PPOCR_E_DEVICE;
+    w->arena.bytes = arena.size() * sizeof(float);
+    if (!cuda_ok(cudaMalloc(&w->arena.p, w->arena.bytes), "allocating weights", &code)) return code;
+    if (!cuda_ok(cudaMemcpy(w->arena.p, arena.data(), w->arena.bytes, cudaMemcpyHostToDevice), "uploading weights"))
+        return PPOCR_E_DEVICE;
+    return make_model(std::move(plan), w, values.size(), device, out);
+}
+
+int ppocr_model_load(const char *plan_path, int device, ppocr_model **out) {
+    g_error.clear();
+    if (!plan_path || !out) return fail(PPOCR_E_ARG, "null argument");
+    std::ifstream f(plan_path, std::ios::binary);
+    if (!f) return fail(PPOCR_E_PLAN, std::string("reading the plan: cannot open ") + plan_path);
+    std::vector<char> bytes((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+    return ppocr_model_load_bytes(bytes.data(), bytes.size(), device, out);
+}
+
+int ppocr_model_share_weights(const ppocr_model *src, ppocr_model **out) {
+    g_error.clear();
+    if (!src || !out) return fail(PPOCR_E_ARG, "null argument");
+    *out = nullptr;
+    Plan plan = src->plan;
+    std::string err;
+    return make_model(std::move(plan), src->weights, src->weight_floats, src->device, out);
+}
+
+void ppocr_model_free(ppocr_model *model) { delete model; }
+
+const char *ppocr_model_device_name(const ppocr_model *m) { return m ? m->name.c_str() : ""; }
+int ppocr_model_integrated(const ppocr_model *m) { return m && m->integrated ? 1 : 0; }
+size_t ppocr_model_max_lanes(const ppocr_model *m) { return m ? 256 : 0; }
+size_t ppocr_model_output_count(const ppocr_model *m) { return m ? m->plan.outputs.size() : 0; }
+
+int ppocr_model_set_input_size(ppocr_model *m, uint32_t height, uint32_t width) {
+    uint32_t hw[2] = {height, width};
+    return ppocr_model_set_sizes(m, hw, 1);
+}
+
+int ppocr_model_set_sizes(ppocr_model *m, const uint32_t *hw, size_t lanes) {
+    g_error.clear();
+    if (!m || (!hw && lanes)) return fail(PPOCR_E_ARG, "null argument");
+    if (lanes == 0) return fail(PPOCR_E_SIZE, "no lanes");
+    if (lanes > ppocr_model_max_lanes(m))
+        return fail(PPOCR_E_SIZE, std::to_string(lanes) + " lanes, more than the " +
+                                      std::to_string(ppocr_model_max_lanes(m)) + " a run takes");
+    if (!cuda_ok(cudaSetDevice(m->device), "selecting the device")) return PPOCR_E_DEVICE;
+    if (m->pending) {
+        cudaStreamSynchronize(m->stream);
+        m->pending = false;
+    }
+    // Validate every size first, so that a refusal leaves the model as it was.
+    std::map<std::pair<size_t, size_t>, size_t> group_of;
+    std::vector<std::pair<size_t, size_t>> sizes, where;
+    std::vector<std::unique_ptr<Group>> groups;
+    for (size_t l = 0; l < lanes; l++) {
+        std::pair<size_t, size_t> s{hw[2 * l], hw[2 * l + 1]};
+        auto it = group_of.find(s);
+        if (it == group_of.end()) {
+            auto g = std::make_unique<Group>();
+            g->h = s.first;
+            g->w = s.second;
+            g->plan = m->plan;
+            std::string err;
+            if (!g->plan.set_size(s.first, s.second, m->weight_floats, err)) return fail(PPOCR_E_SIZE, err);
+            it = group_of.emplace(s, groups.size()).first;
+            groups.push_back(std::move(g));
+        }
+        Group &g = *groups[it->second];
+        where.push_back({it->second, g.lanes.size()});
+        g.lanes.push_back(l);
+        sizes.push_back(s);
+    }
+    bool fused = !(m->options & PPOCR_OPT_NO_FUSION);
+    if (m->steps.empty() || m->steps_fused != fused) {
+        m->steps = fuse(m->plan, fused);
+        m->steps_fused = fused;
+    }
+    m->drop_graphs();
+    for (auto &g : groups) {
+        std::string err;
+        int rc = m->build_group(*g, err);
+        if (rc) return fail(rc, err);
+    }
+    m->groups = std::move(groups);
+    m->sizes = std::move(sizes);
+    m->where = std::move(where);
+    return PPOCR_OK;
+}
+
+float *ppocr_model_lane_input(ppocr_model *m, size_t lane, size_t *len) {
+    if (!m || lane >= m->where.size()) {
+        fail(PPOCR_E_ARG, "no such lane");
+        return nullptr;
+    }
+    Group &g = *m->groups[m->where[lane].first];
+    size_t n = g.plan.h * g.plan.w * g.plan.c;
+    if (len) *len = n;
+    return static_cast<float *>(g.in_host.p) + m->where[lane].second * n;
+}
+
+const float *ppocr_model_lane_output(const ppocr_model *m, size_t lane, size_t index, size_t *len) {
+    if (!m || lane >= m->where.size() || index >= m->plan.outputs.size()) {
+        fail(PPOCR_E_ARG, "no such lane or output");
+        return nullptr;
+    }
+    const Group &g = *m->groups[m->where[lane].first];
+    size_t n = g.plan.out_n[index];
+    if (len) *len = n;
+    return static_cast<const float *>(g.out_host[index]->p) + m->where[lane].second * n;
+}
+
+float *ppocr_model_lane_device_input(ppocr_model *m, size_t lane, size_t *len) {
+    if (!m || lane >= m->where.size()) {
+        fail(PPOCR_E_ARG, "no such lane");
+        return nullptr;
+    }
+    Group &g = *m->groups[m->where[lane].first];
+    size_t n = g.plan.h * g.plan.w * g.plan.c;
+    if (len) *len = n;
+    return g.slot_ptr(g.plan.slot) + m->where[lane].second * n;
+}
+
+const float *ppocr_model_lane_device_output(const ppocr_model *m, size_t lane, size_t index, size_t *len) {
+    if (!m || lane >= m->where.size() || index >= m->plan.outputs.size()) {
+        fail(PPOCR_E_ARG, "no such lane or output");
+        return nullptr;
+    }
+    const Group &g = *m->groups[m->where[lane].first];
+    size_t n = g.plan.out_n[index];
+    if (len) *len = n;
+    return g.slot_ptr(g.plan.outputs[index]) + m->where[lane].second * n;
+}
+
+int ppocr_model_enqueue(ppocr_model *m) {
+    g_error.clear();
+    if (!m) return fail(PPOCR_E_ARG, "null model");
+    return m->enqueue(true);
+}
+
+int ppocr_model_enqueue_device(ppocr_model *m) {
+    g_error.clear();
+    if (!m) return fail(PPOCR_E_ARG, "null model");
+    return m->enqueue(false);
+}
+
+// Poll the completion event until it fires or the deadline passes; the
+// reference waits forever (vk.rs:373-378).
+int ppocr_model_wait(ppocr_model *m, uint32_t timeout_ms) {
+    g_error.clear();
+    if (!m) return fail(PPOCR_E_ARG, "null model");
+    if (!m->pending) return PPOCR_OK;
+    auto start = std::chrono::steady_clock::now();
+    for (unsigned spin = 0;; spin++) {
+        cudaError_t e = cudaEventQuery(m->done);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) {
+            m->pending = false;
+            return cuda_ok(e, "running the network") ? PPOCR_OK : PPOCR_E_DEVICE;
+        }
+        if (timeout_ms) {
+            auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - start);
+            if (ms.count() >= timeout_ms)
+                return fail(PPOCR_E_TIMEOUT, "the GPU did not finish within " + std::to_string(timeout_ms) + " ms");
+        }
+        if (spin < 2000)
+            std::this_thread::yield();
+        else
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    m->pending = false;
+    return PPOCR_OK;
+}
+
+int ppocr_model_run(ppocr_model *m, uint32_t timeout_ms) {
+    int rc = ppocr_model_enqueue(m);
+    if (rc) return rc;
+    return ppocr_model_wait(m, timeout_ms);
+}
+
+void *ppocr_model_stream(ppocr_model *m) { return m ? static_cast<void *>(m->stream) : nullptr; }
+
+int ppocr_model_set_stream(ppocr_model *m, void *stream) {
+    g_error.clear();
+    if (!m) return fail(PPOCR_E_ARG, "null model");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->own_stream;
+    if (s == m->stream) return PPOCR_OK;
+    if (m->pending) {
+        cudaStreamSynchronize(m->stream);
+        m->pending = false;
+    }
+    m->stream = s;
+    m->drop_graphs();
+    return PPOCR_OK;
+}
+
+int ppocr_model_set_options(ppocr_model *m, uint32_t options) {
+    g_error.clear();
+    if (!m) return fail(PPOCR_E_ARG, "null model");
+    if (options == m->options) return PPOCR_OK;
+    bool refuse = (options ^ m->options) & PPOCR_OPT_NO_FUSION;
+    m->options = options;
+    m->drop_graphs();
+    if (refuse && !m->sizes.empty()) {
+        std::vector<uint32_t> hw;
+        for (auto &s : m->sizes) {
+            hw.push_back(uint32_t(s.first));
+            hw.push_back(uint32_t(s.second));
+        }
+        return ppocr_model_set_sizes(m, hw.data(), m->sizes.size());
+    }
+    return PPOCR_OK;
+}
+
+// Counted when the run is recorded (each launch function returns how many
+// kernels it started); 0 before the first run at the current sizes.
+size_t ppocr_model_launches(const ppocr_model *m) { return m ? m->launches : 0; }
+
+const char *ppocr_model_step_name(const ppocr_model *m, size_t i) {
+    if (!m) return nullptr;
+    size_t k = 0;
+    for (const Step &st : m->steps) {
+        if (st.kind == S_SKIP) continue;
+        if (k++ == i) return st.name.c_str();
+    }
+    return nullptr;
+}
+
+}  // extern "C"

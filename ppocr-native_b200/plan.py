@@ -335,3 +335,53 @@ class Builder:
     def build(self, outputs: list[int]) -> bytes:
         weights = np.concatenate(self.blob) if self.blob else np.zeros(0, np.float32)
         return encode(self.input, self.buffers, outputs, self.ops, weights)
+
+
+def shapes(data: bytes, h: int, w: int) -> list[Op]:
+    """Every op of a plan with its sizes at an input of h x w, as
+    `plan.rs:414-494` derives them (no checks: for cost accounting). Each
+    returned op carries ih, iw, oh, ow attributes."""
+    d = describe(data)
+    slot, _, _, c = d["input"]
+    ops = d["ops"]
+    made: dict[int, tuple[int, int, int]] = {slot: (h, w, c)}
+    for op in ops:
+        ih, iw, _ = made[op.x]
+        if op.kind in ("conv", "dwconv", "maxpool", "avgpool"):
+            oh = (ih + op.pt + op.pb - op.kh) // op.sh + 1
+            ow = (iw + op.pl + op.pr - op.kw) // op.sw + 1
+        elif op.kind in ("upsample", "upsampleadd"):
+            oh, ow = ih * op.sh, iw * op.sw
+        elif op.kind == "convtranspose":
+            oh, ow = ih * op.kh, iw * op.kw
+        elif op.kind == "mean":
+            oh, ow = 1, 1
+        else:
+            oh, ow = ih, iw
+        op.ih, op.iw, op.oh, op.ow = ih, iw, oh, ow
+        made[op.y] = (oh, ow, op.oc)
+    return ops
+
+
+def macs(op: Op) -> int:
+    """Multiply-adds of one op, as the reference's profiler counts them
+    (`examples/plan.rs:140-152`)."""
+    spatial = op.oh * op.ow
+    if op.kind == "conv":
+        return op.kh * op.kw * (op.ic + op.n2) * op.oc * spatial
+    if op.kind == "dwconv":
+        return op.kh * op.kw * op.oc * spatial
+    if op.kind == "attention":
+        return 2 * op.iw * op.iw * op.oc
+    if op.kind == "ctchead":
+        return op.iw * op.ic * op.oc
+    if op.kind == "ctcargmax":
+        return op.iw * op.ic * -(-op.n2 // 16) * 16
+    if op.kind == "convtranspose":
+        return op.kh * op.kw * op.ic * op.oc * op.ih * op.iw
+    return 0
+
+
+def flops(data: bytes, h: int, w: int) -> int:
+    """Floating-point operations (2 per multiply-add) of a whole plan."""
+    return 2 * sum(macs(op) for op in shapes(data, h, w))

@@ -1,0 +1,70 @@
+"""The C ABI without a GPU: the library builds, loads, exports every entry
+point `include/ppocr_cuda.h` declares, and checks plans on the host exactly
+as the reference does before touching a device."""
+
+from __future__ import annotations
+
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from ppocr_native_b200 import cuda, synth
+from test_oracle import good_file, malformed_files
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared() -> set[str]:
+    text = (ROOT / "include" / "ppocr_cuda.h").read_text()
+    return set(re.findall(r"\b(ppocr_[a-z_0-9]+)\s*\(", text))
+
+
+def test_library_exports_every_declared_entry_point():
+    lib = cuda.lib()
+    names = declared()
+    assert len(names) >= 20
+    for name in names:
+        assert hasattr(lib, name), name
+    assert names <= set(cuda._SIG), names - set(cuda._SIG)
+
+
+@pytest.mark.parametrize("what,data", malformed_files(), ids=[c[0] for c in malformed_files()])
+def test_malformed_plans_refused_before_any_device(what, data):
+    with pytest.raises(cuda.PpocrError) as e:
+        cuda.Model(data)
+    assert e.value.code == cuda.E_PLAN, (what, str(e.value))
+
+
+def test_plans_that_parse_reach_the_device_check():
+    for plan in (good_file(), synth.page_model_plan(16, 16), synth.line_model_plan(40),
+                 synth.fused_layer_plan(h=8, w=8)):
+        if cuda.device_count() == 0:
+            with pytest.raises(cuda.PpocrError) as e:
+                cuda.Model(plan, device=0)
+            assert e.value.code == cuda.E_DEVICE
+        with pytest.raises(cuda.PpocrError) as e:
+            cuda.Model(plan, device=99)
+        assert e.value.code == cuda.E_DEVICE
+
+
+def test_plan_file_path_errors():
+    with pytest.raises(cuda.PpocrError) as e:
+        cuda.Model("/nonexistent/plan")
+    assert e.value.code == cuda.E_PLAN
+
+
+def test_det_and_rec_plans_parse(tmp_path):
+    # the synthetic networks are valid PPOCRPL1 files with codes 0-6 only
+    from ppocr_native_b200.plan import describe
+
+    for plan in (synth.det_plan(), synth.rec_plan()):
+        d = describe(plan)
+        assert all(op.fused != "hardswish" for op in d["ops"])
+        p = tmp_path / "x.plan"
+        p.write_bytes(plan)
+        with pytest.raises(cuda.PpocrError) as e:
+            cuda.Model(p, device=99)
+        assert e.value.code == cuda.E_DEVICE
+    assert np.isfinite(describe(synth.det_plan())["weights"]).all()

@@ -1,0 +1,421 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle.
+
+The kernels accumulate every convolution output in the oracle's order (bias
+first or last as the reference's tiles do, taps and channels in order, one
+fused multiply-add each) and evaluate the activations with the same IEEE
+operations, so most outputs are expected to be bit-identical; the bar
+`north_star` sets is 1e-4 absolute on probabilities and recogniser values
+and identical CTC classes. Each test asserts the bar and, where the kernel
+is built to be exact, exact equality too.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from common import Op, encode, max_gap, noise, single, window
+from ppocr_native_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4  # north_star: probabilities and recogniser values within 1e-4
+
+
+def gpu_run(cuda, plan, x, hw=None, options=0):
+    with cuda.Model(plan) as m:
+        if options:
+            m.set_options(options)
+        if hw is not None:
+            m.set_input_size(*hw)
+        m.input_mut()[:] = x
+        m.run(60_000)
+        return [m.output(k).copy() for k in range(m.output_count())], m.steps()
+
+
+def oracle_run(oracle_mod, plan, x, hw=None):
+    o = oracle_mod.Oracle(plan)
+    if hw is not None:
+        o.set_size(*hw)
+    return o.run(x)
+
+
+def check(got, want, exact=True, tol=TOL):
+    assert got.shape == want.shape
+    gap = max_gap(got, want)
+    assert gap <= tol, gap
+    if exact:
+        assert np.array_equal(got, want), f"max gap {gap}, {int(np.sum(got != want))} of {got.size} differ"
+
+
+# ---------------------------------------------------------------- one op each
+
+CONV_CASES = [
+    # k, s, pads (t,b,l,r), ic, oc, fused
+    (3, 2, (1, 1, 1, 1), 3, 24, "swish"),   # det stem
+    (3, 2, (1, 1, 1, 1), 3, 48, "swish"),   # rec stem
+    (3, 1, (1, 1, 1, 1), 96, 24, "none"),   # RSE 3x3
+    (1, 1, (0, 0, 0, 0), 96, 192, "swish"),
+    (1, 1, (0, 0, 0, 0), 192, 384, "relu"),
+    (1, 1, (0, 0, 0, 0), 384, 96, "none"),
+    (1, 1, (0, 0, 0, 0), 24, 48, "hardswish"),
+    (1, 1, (0, 0, 0, 0), 120, 360, "none"),
+    (1, 1, (0, 0, 0, 0), 20, 36, "gelu"),    # oc % 16 != 0: bias last
+    (1, 1, (0, 0, 0, 0), 5, 4, "hardsigmoid"),
+    (2, 1, (0, 1, 0, 1), 8, 8, "gelu"),
+    (5, 2, (2, 2, 2, 2), 6, 10, "sigmoid"),
+    (3, 1, (1, 1, 1, 1), 16, 64, "hardsigmoidfifth"),
+    (3, 1, (1, 1, 1, 1), 7, 13, "none"),
+]
+
+
+@pytest.mark.parametrize("k,s,pads,ic,oc,fused", CONV_CASES)
+def test_conv(cuda_mod, oracle_mod, k, s, pads, ic, oc, fused):
+    h, w = 19, 23
+    x = noise(h * w * ic, 3, 1.0)
+    wt = noise(k * k * ic * oc, 5, 0.3)
+    b = noise(oc, 7, 0.5)
+    op = Op("conv", x=0, y=1, ic=ic, oc=oc, fused=fused, w=(0, wt.size), b=(wt.size, oc), kh=k, kw=k, sh=s, sw=s,
+            pt=pads[0], pb=pads[1], pl=pads[2], pr=pads[3])
+    plan = single(op, (h, w, ic), np.concatenate([wt, b]))
+    got, _ = gpu_run(cuda_mod, plan, x)
+    check(got[0], oracle_run(oracle_mod, plan, x)[0])
+
+
+def test_conv_two_inputs(cuda_mod, oracle_mod):
+    # a windowed conv over the concatenation of its input and a second one
+    h, w, c1, c2, oc = 11, 9, 8, 12, 16
+    first = window(Op("conv", x=0, y=1, ic=c1, oc=c2, w=(0, c1 * c2), b=(c1 * c2, c2)), (1, 1), 1, 0, 0)
+    at = c1 * c2 + c2
+    conv = window(Op("conv", x=0, y=2, ic=c1, oc=oc, x2=1, n2=c2), (3, 3), 1, 1, 1)
+    conv.w, conv.b = (at, 9 * (c1 + c2) * oc), (at + 9 * (c1 + c2) * oc, oc)
+    weights = noise(at + 9 * (c1 + c2) * oc + oc, 9, 0.4)
+    plan = encode((0, h, w, c1), 3, [2], [first, conv], weights)
+    x = noise(h * w * c1, 1, 1.0)
+    got, _ = gpu_run(cuda_mod, plan, x)
+    check(got[0], oracle_run(oracle_mod, plan, x)[0])
+
+
+@pytest.mark.parametrize("k,s,c,fused", [(3, 1, 8, "swish"), (3, 2, 12, "none"), (5, 1, 16, "relu"),
+                                         (7, 1, 8, "none"), (5, 2, 5, "hardswish"), (5, 1, 96, "hardswish")])
+def test_depthwise(cuda_mod, oracle_mod, k, s, c, fused):
+    h, w = 21, 17
+    x = noise(h * w * c, 11, 1.0)
+    wt = noise(k * k * c, 13, 0.5)
+    b = noise(c, 17, 0.5)
+    p = k // 2
+    op = window(Op("dwconv", x=0, y=1, ic=c, oc=c, fused=fused, w=(0, wt.size), b=(wt.size, c)), (k, k), s, p, p)
+    plan = single(op, (h, w, c), np.concatenate([wt, b]))
+    got, _ = gpu_run(cuda_mod, plan, x)
+    check(got[0], oracle_run(oracle_mod, plan, x)[0])
+
+
+def elementwise_plan(kind, h, w, c, **kw):
+    """pointwise producer of a second tensor (buffer 1), then `kind` from the
+    image (buffer 0) and it into buffer 2."""
+    prod_oc = kw.pop("prod_oc", c)
+    prod = window(Op("conv", x=0, y=1, ic=c, oc=prod_oc, w=(0, c * prod_oc), b=(c * prod_oc, prod_oc)), (1, 1), 1, 0, 0)
+    at = c * prod_oc + prod_oc
+    extra = kw.pop("weights", 0)
+    op = Op(kind, x=0, y=2, ic=c, oc=kw.pop("oc", c), x2=1, **kw)
+    if extra:
+        op.w = (at, extra)
+    weights = noise(at + extra, 23, 0.5)
+    return encode((0, h, w, c), 3, [2], [prod, op], weights)
+
+
+@pytest.mark.parametrize("fused", ["none", "relu", "swish"])
+def test_add(cuda_mod, oracle_mod, fused):
+    plan = elementwise_plan("add", 13, 7, 12, fused=fused)
+    x = noise(13 * 7 * 12, 2, 2.0)
+    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+
+
+def test_concat_and_upsample(cuda_mod, oracle_mod):
+    h, w, c = 6, 5, 8
+    x = noise(h * w * c, 4, 1.0)
+    for cin, plan in ((c, elementwise_plan("concatc", h, w, c, prod_oc=12, oc=20, n2=12)),
+                      (3, elementwise_plan("concatc", h, w, 3, prod_oc=5, oc=8, n2=5))):
+        xx = noise(h * w * cin, 4, 1.0)
+        check(gpu_run(cuda_mod, plan, xx)[0][0], oracle_run(oracle_mod, plan, xx)[0])
+    up = Op("upsample", x=0, y=1, ic=c, oc=c, sh=2, sw=3)
+    plan = single(up, (h, w, c), np.zeros(0, np.float32))
+    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+    # upsampleadd: y = x2 + up(x); x2 made at the upsampled size by a stride-1 conv of an upsample
+    upx = Op("upsample", x=0, y=1, ic=c, oc=c, sh=2, sw=2)
+    conv = window(Op("conv", x=1, y=2, ic=c, oc=c, w=(0, c * c), b=(c * c, c)), (1, 1), 1, 0, 0)
+    add = Op("upsampleadd", x=0, y=3, ic=c, oc=c, x2=2, sh=2, sw=2)
+    plan = encode((0, h, w, c), 4, [3], [upx, conv, add], noise(c * c + c, 6, 0.5))
+    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+
+
+def test_pools_mean_gates(cuda_mod, oracle_mod):
+    h, w, c = 14, 10, 12
+    x = noise(h * w * c, 8, 1.5)
+    mp = Op("maxpool", x=0, y=1, ic=c, oc=c, kh=2, kw=2, sh=1, sw=1, pb=1, pr=1)
+    plan = single(mp, (h, w, c), np.zeros(0, np.float32))
+    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+    ap = Op("avgpool", x=0, y=1, ic=c, oc=c, kh=7, kw=2, sh=7, sw=2)
+    plan = single(ap, (h, w, c), np.zeros(0, np.float32))
+    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+    mean = Op("mean", x=0, y=1, ic=c, oc=c)
+    plan = single(mean, (h, w, c), np.zeros(0, np.float32))
+    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+    # a squeeze-and-excite gate: mean -> 1x1 -> channelmul
+    m = Op("mean", x=0, y=1, ic=c, oc=c)
+    g = window(Op("conv", x=1, y=2, ic=c, oc=c, fused="hardsigmoid", w=(0, c * c), b=(c * c, c)), (1, 1), 1, 0, 0)
+    cm = Op("channelmul", x=0, y=3, ic=c, oc=c, x2=2)
+    plan = encode((0, h, w, c), 4, [3], [m, g, cm], noise(c * c + c, 5, 0.5))
+    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+
+
+def test_mean_on_a_page(cuda_mod, oracle_mod):
+    # layers.rs:1208-1233: a large offset plus small noise over 300k pixels
+    pixels, c = 300_000, 3
+    x = noise(pixels * c, 13, 0.01).reshape(pixels, c)
+    x = (x + np.float32(1000.0) + np.arange(c, dtype=np.float32)).astype(np.float32).reshape(-1)
+    plan = single(Op("mean", x=0, y=1, ic=c, oc=c), (600, 500, c), np.zeros(0, np.float32))
+    got = gpu_run(cuda_mod, plan, x)[0][0]
+    want = oracle_run(oracle_mod, plan, x)[0]
+    assert max_gap(got, want) <= 1e-4
+
+
+def test_layernorm_attention(cuda_mod, oracle_mod):
+    t, c, heads = 37, 120, 8
+    x = noise(t * 3 * c, 21, 1.5)
+    att = Op("attention", x=0, y=1, ic=3 * c, oc=c, n2=heads, w=(0, 1))
+    plan = single(att, (1, t, 3 * c), np.float32([15 ** -0.5]))
+    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+    gamma, beta = noise(c, 3, 1.0) + 1, noise(c, 4, 0.5)
+    ln = Op("layernorm", x=0, y=1, ic=c, oc=c, w=(0, 2 * c + 1))
+    xs = noise(t * c, 9, 3.0)
+    plan = single(ln, (1, t, c), np.concatenate([gamma, beta, np.float32([1e-6])]))
+    check(gpu_run(cuda_mod, plan, xs)[0][0], oracle_run(oracle_mod, plan, xs)[0])
+
+
+def ctc_plan(kind, t, ci, vocab, seed=7):
+    cols = -(-vocab // 16) * 16
+    logical = noise(ci * vocab, seed, 0.8).reshape(ci, vocab)
+    full = np.zeros((ci, cols), np.float32)
+    full[:, :vocab] = logical
+    w = full.reshape(ci, cols // 16, 16).transpose(1, 0, 2).copy()
+    b = np.full(cols, -1e30, np.float32)
+    b[:vocab] = noise(vocab, 11, 0.5)
+    if kind == "ctchead":
+        op = Op("ctchead", x=0, y=1, ic=ci, oc=vocab, w=(0, w.size), b=(w.size, cols))
+    else:
+        op = Op("ctcargmax", x=0, y=1, ic=ci, oc=2, n2=vocab, w=(0, w.size), b=(w.size, cols))
+    return single(op, (1, t, ci), np.concatenate([w.reshape(-1), b]))
+
+
+@pytest.mark.parametrize("t,ci,vocab", [(1, 19, 37), (13, 19, 64), (40, 120, 18710), (97, 120, 1000)])
+def test_ctc_head(cuda_mod, oracle_mod, t, ci, vocab):
+    x = noise(t * ci, t + 3, 2.0)
+    plan = ctc_plan("ctcargmax", t, ci, vocab)
+    got = gpu_run(cuda_mod, plan, x)[0][0].reshape(t, 2)
+    want = oracle_run(oracle_mod, plan, x)[0].reshape(t, 2)
+    assert np.array_equal(got[:, 0], want[:, 0])
+    assert max_gap(got[:, 1], want[:, 1]) <= 1e-6
+    if vocab <= 1000:
+        plan = ctc_plan("ctchead", t, ci, vocab)
+        got = gpu_run(cuda_mod, plan, x)[0][0]
+        assert max_gap(got, oracle_run(oracle_mod, plan, x)[0]) <= 1e-6
+
+
+@pytest.mark.parametrize("ic,oc,k,fused", [(5, 3, 2, "none"), (24, 24, 2, "relu"), (24, 1, 2, "sigmoid"),
+                                           (16, 4, 3, "swish")])
+def test_convtranspose(cuda_mod, oracle_mod, ic, oc, k, fused):
+    h, w = 9, 7
+    x = noise(h * w * ic, 5, 1.0)
+    wt = noise(ic * k * k * oc, 7, 0.6)
+    b = noise(k * k * oc, 9, 0.5)
+    op = Op("convtranspose", x=0, y=1, ic=ic, oc=oc, kh=k, kw=k, sh=k, sw=k, fused=fused,
+            w=(0, wt.size), b=(wt.size, b.size))
+    plan = single(op, (h, w, ic), np.concatenate([wt, b]))
+    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+
+
+# ---------------------------------------------------------- fused layers, nets
+
+def test_fused_layer_config1(cuda_mod, oracle_mod):
+    """Benchmark config 1 at full size: dw 5x5 + hardswish -> pw 96->192 +
+    hardswish, fused into one kernel."""
+    plan = synth.fused_layer_plan(seed=0)
+    x = np.random.default_rng(1).uniform(-1, 1, 240 * 240 * 96).astype(np.float32)
+    got, steps = gpu_run(cuda_mod, plan, x)
+    assert steps == ["dw+pw"]
+    check(got[0], oracle_run(oracle_mod, plan, x)[0])
+
+
+@pytest.mark.parametrize("h,w", [(64, 48), (40, 8), (16, 16), (8, 36), (4, 4)])
+def test_page_model(cuda_mod, oracle_mod, h, w):
+    plan = synth.page_model_plan(16, 16)
+    x = synth.ramp_input(h * w * 3)
+    got, _ = gpu_run(cuda_mod, plan, x, hw=(h, w))
+    check(got[0], oracle_run(oracle_mod, plan, x, hw=(h, w))[0])
+
+
+@pytest.mark.parametrize("width", [3, 17, 40, 64, 1001])
+def test_line_model(cuda_mod, oracle_mod, width):
+    plan = synth.line_model_plan(40)
+    x = synth.ramp_input(2 * width * 3)
+    got = gpu_run(cuda_mod, plan, x, hw=(2, width))[0][0].reshape(-1, 2)
+    want = oracle_run(oracle_mod, plan, x, hw=(2, width))[0].reshape(-1, 2)
+    assert np.array_equal(got[:, 0], want[:, 0])
+    assert max_gap(got[:, 1], want[:, 1]) <= 1e-6
+
+
+@pytest.mark.parametrize("std", [None, 0.02], ids=["busy", "baseline-init"])
+def test_detector_960x736(cuda_mod, oracle_mod, std):
+    """Benchmark config 2: probabilities within 1e-4 (and bit-identical)."""
+    plan = synth.det_plan(seed=3, std=std)
+    x = np.random.default_rng(4).normal(0, 1, 960 * 736 * 3).astype(np.float32)
+    got, steps = gpu_run(cuda_mod, plan, x)
+    assert "dw+pw" in steps and "gate_add" in steps and any("sources" in s for s in steps)
+    want = oracle_run(oracle_mod, plan, x)[0]
+    check(got[0], want)
+
+
+def test_detector_unfused_matches_fused(cuda_mod):
+    plan = synth.det_plan(seed=5, std=None, size=(320, 256))
+    x = synth.stripes(320, 256)
+    fused, _ = gpu_run(cuda_mod, plan, x)
+    plain, steps = gpu_run(cuda_mod, plan, x, options=cuda_mod.OPT_NO_FUSION | cuda_mod.OPT_NO_GRAPH)
+    assert "dw+pw" not in steps
+    assert np.array_equal(fused[0], plain[0])
+
+
+def test_recogniser_16_lanes(cuda_mod, oracle_mod):
+    """Benchmark config 3: 16 lines of 48 x 320 in one batch; classes
+    identical and probabilities within 1e-4 of the oracle, lane by lane."""
+    plan = synth.rec_plan(seed=2, std=None)
+    rng = np.random.default_rng(6)
+    xs = [rng.normal(0, 1, 48 * 320 * 3).astype(np.float32) for _ in range(16)]
+    with cuda_mod.Model(plan) as m:
+        m.set_sizes([(48, 320)] * 16)
+        for i, x in enumerate(xs):
+            m.lane_input_mut(i)[:] = x
+        m.run(60_000)
+        outs = [m.lane_output(i).copy().reshape(-1, 2) for i in range(16)]
+    o = oracle_mod.Oracle(plan)
+    classes = set()
+    for x, got in zip(xs, outs):
+        want = o.run(x)[0].reshape(-1, 2)
+        assert np.array_equal(got[:, 0], want[:, 0])
+        assert max_gap(got[:, 1], want[:, 1]) <= TOL
+        classes |= set(want[:, 0].tolist())
+    assert len(classes) > 5  # the busy weights make varied classes
+
+
+def test_lanes_of_different_sizes(cuda_mod, oracle_mod):
+    """gpu.rs:57-84: lanes of several widths in one run each match the CPU,
+    and a lane alone gives the bits it gives alongside others."""
+    plan = synth.rec_plan(seed=1, std=None, vocab=500)
+    widths = [640, 96, 1280, 96, 320]
+    xs = [synth.stripes(48, wd, phase=i * 31) for i, wd in enumerate(widths)]
+    with cuda_mod.Model(plan) as m:
+        m.set_sizes([(48, wd) for wd in widths])
+        for i, x in enumerate(xs):
+            m.lane_input_mut(i)[:] = x
+        m.run(60_000)
+        together = [m.lane_output(i).copy() for i in range(len(widths))]
+        m.set_sizes([(48, widths[1])])
+        m.input_mut()[:] = xs[1]
+        m.run(60_000)
+        alone = m.output().copy()
+    assert np.array_equal(alone, together[1])
+    o = oracle_mod.Oracle(plan)
+    for wd, x, got in zip(widths, xs, together):
+        o.set_size(48, wd)
+        want = o.run(x)[0].reshape(-1, 2)
+        got = got.reshape(-1, 2)
+        assert np.array_equal(got[:, 0], want[:, 0])
+        assert max_gap(got[:, 1], want[:, 1]) <= TOL
+
+
+def test_bad_size_keeps_model(cuda_mod):
+    plan = synth.page_model_plan(16, 16)
+    x = synth.ramp_input(16 * 16 * 3)
+    with cuda_mod.Model(plan) as m:
+        m.input_mut()[:] = x
+        m.run(60_000)
+        before = m.output().copy()
+        for h, w in [(10, 16), (16, 22), (0, 16), (1 << 20, 1 << 20)]:
+            with pytest.raises(cuda_mod.PpocrError) as e:
+                m.set_input_size(h, w)
+            assert e.value.code == cuda_mod.E_SIZE
+        assert m.input_mut().size == 16 * 16 * 3
+        m.input_mut()[:] = x
+        m.run(60_000)
+        assert np.array_equal(m.output(), before)
+
+
+def test_share_weights_and_graph_replay(cuda_mod):
+    plan = synth.det_plan(seed=8, std=None, size=(256, 192))
+    x = synth.stripes(256, 192)
+    with cuda_mod.Model(plan) as m:
+        m.input_mut()[:] = x
+        m.run(60_000)
+        first = m.output().copy()
+        m.run(60_000)  # graph replay
+        assert np.array_equal(m.output(), first)
+        with m.share_weights() as m2:
+            m2.input_mut()[:] = x
+            m2.run(60_000)
+            assert np.array_equal(m2.output(), first)
+        m.set_options(cuda_mod.OPT_NO_GRAPH)
+        m.input_mut()[:] = x
+        m.run(60_000)
+        assert np.array_equal(m.output(), first)
+
+
+def test_wait_times_out_and_recovers(cuda_mod):
+    """A wait shorter than the run returns PPOCR_E_TIMEOUT; the run itself
+    completes and a later wait returns it (no kernel is harmed)."""
+    plan = synth.det_plan(seed=0, size=(1984, 1536))
+    with cuda_mod.Model(plan) as m:
+        m.set_sizes([(1984, 1536)] * 4)
+        m.enqueue()
+        try:
+            m.wait(1)
+            timed_out = False
+        except cuda_mod.PpocrError as e:
+            assert e.code == cuda_mod.E_TIMEOUT
+            timed_out = True
+        m.wait(0)
+        assert timed_out, "four 1984x1536 pages finished within 1 ms"
+        assert np.isfinite(m.lane_output(3)).all()
+
+
+def _cudart():
+    pats = glob.glob(os.path.join(os.path.dirname(np.__file__), "..", "nvidia", "cuda_runtime", "lib",
+                                  "libcudart.so*"))
+    for p in pats + ["libcudart.so.12", "/usr/local/cuda/lib64/libcudart.so"]:
+        try:
+            return ctypes.CDLL(p)
+        except OSError:
+            continue
+    pytest.fail("no libcudart to copy device memory with")
+
+
+def test_device_resident_path(cuda_mod, oracle_mod):
+    """Inputs written straight to device memory, a run that copies nothing,
+    the output read from device memory."""
+    rt = _cudart()
+    rt.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+    plan = synth.page_model_plan(32, 24)
+    x = synth.ramp_input(32 * 24 * 3)
+    with cuda_mod.Model(plan) as m:
+        dptr, n = m.lane_device_input(0)
+        assert n == x.size
+        assert rt.cudaMemcpy(dptr, x.ctypes.data, x.nbytes, 1) == 0
+        m.enqueue_device()
+        m.wait(60_000)
+        optr, on = m.lane_device_output(0, 0)
+        out = np.empty(on, np.float32)
+        assert rt.cudaMemcpy(out.ctypes.data, optr, out.nbytes, 2) == 0
+    check(out, oracle_run(oracle_mod, plan, x)[0])

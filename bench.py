@@ -19,6 +19,7 @@ Rust and cannot be built here), all host threads, bounded samples.
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import importlib.util
 import json
 import os
@@ -202,7 +203,8 @@ class PagePipeline:
         return h2d, d2h
 
     def close(self):
-        for m in self.models():
+        # the recogniser models run on the detector's stream: they go first
+        for m in reversed(self.models()):
             m.close()
 
 
@@ -435,6 +437,7 @@ def run_reference(args, d: Dist) -> dict | None:
 
 
 def main():
+    faulthandler.enable()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)

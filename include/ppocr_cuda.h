@@ -101,7 +101,9 @@ int ppocr_model_enqueue_device(ppocr_model *model);
 /* The cudaStream_t every kernel of this model runs on. */
 void *ppocr_model_stream(ppocr_model *model);
 /* Run this model on the caller's cudaStream_t (NULL: its own again), e.g.
- * to queue several models behind one another without host waits. */
+ * to queue several models behind one another without host waits. The
+ * caller keeps that stream alive while the model may still use it; freeing
+ * the model waits only for the model's own work, not for the stream. */
 int ppocr_model_set_stream(ppocr_model *model, void *stream);
 
 /* PPOCR_OPT_* bits; takes effect at the next run. */

@@ -7,6 +7,6 @@ with ctypes (the library is opened on first use), `plan` writes plan files,
 `synth` builds the synthetic networks.
 """
 
-from . import cuda, plan, synth  # noqa: F401
+from . import cuda, plan, synth, workload  # noqa: F401
 
-__all__ = ["cuda", "plan", "synth"]
+__all__ = ["cuda", "plan", "synth", "workload"]

@@ -361,11 +361,19 @@ struct ppocr_model {
 
     ~ppocr_model() {
         if (device >= 0) cudaSetDevice(device);
-        if (stream) cudaStreamSynchronize(stream);
+        // Wait for this model's own work through its event: the stream may
+        // belong to the caller (ppocr_model_set_stream) and be gone already.
+        settle();
+        if (own_stream) cudaStreamSynchronize(own_stream);
         drop_graphs();
         groups.clear();
         if (done) cudaEventDestroy(done);
         if (own_stream) cudaStreamDestroy(own_stream);
+    }
+
+    void settle() {
+        if (pending && done) cudaEventSynchronize(done);
+        pending = false;
     }
 
     void drop_graphs() {
@@ -785,10 +793,7 @@ int ppocr_model_set_sizes(ppocr_model *m, const uint32_t *hw, size_t lanes) {
         return fail(PPOCR_E_SIZE, std::to_string(lanes) + " lanes, more than the " +
                                       std::to_string(ppocr_model_max_lanes(m)) + " a run takes");
     if (!cuda_ok(cudaSetDevice(m->device), "selecting the device")) return PPOCR_E_DEVICE;
-    if (m->pending) {
-        cudaStreamSynchronize(m->stream);
-        m->pending = false;
-    }
+    m->settle();
     // Validate every size first, so that a refusal leaves the model as it was.
     std::map<std::pair<size_t, size_t>, size_t> group_of;
     std::vector<std::pair<size_t, size_t>> sizes, where;
@@ -925,10 +930,7 @@ int ppocr_model_set_stream(ppocr_model *m, void *stream) {
     if (!m) return fail(PPOCR_E_ARG, "null model");
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->own_stream;
     if (s == m->stream) return PPOCR_OK;
-    if (m->pending) {
-        cudaStreamSynchronize(m->stream);
-        m->pending = false;
-    }
+    m->settle();
     m->stream = s;
     m->drop_graphs();
     return PPOCR_OK;

@@ -219,7 +219,11 @@ def test_ctc_head(cuda_mod, oracle_mod, t, ci, vocab):
     got = gpu_run(cuda_mod, plan, x)[0][0].reshape(t, 2)
     want = oracle_run(oracle_mod, plan, x)[0].reshape(t, 2)
     assert np.array_equal(got[:, 0], want[:, 0])
-    assert max_gap(got[:, 1], want[:, 1]) <= 1e-6
+    # The logits are bit-identical; 1/sum is summed over the columns in
+    # another order (per column block, then merged) than the reference's one
+    # online pass, so it carries its rounding: within the 1e-5 the
+    # reference's own CTC test allows (layers.rs:1313).
+    assert max_gap(got[:, 1], want[:, 1]) <= 1e-5
     if vocab <= 1000:
         plan = ctc_plan("ctchead", t, ci, vocab)
         got = gpu_run(cuda_mod, plan, x)[0][0]
@@ -419,3 +423,30 @@ def test_device_resident_path(cuda_mod, oracle_mod):
         out = np.empty(on, np.float32)
         assert rt.cudaMemcpy(out.ctypes.data, optr, out.nbytes, 2) == 0
     check(out, oracle_run(oracle_mod, plan, x)[0])
+
+
+def test_models_sharing_a_stream(cuda_mod):
+    """Two models queued on one stream give what they give apart, and can be
+    freed in either order (the borrowed stream is never touched on free)."""
+    det = synth.det_plan(seed=9, std=None, size=(128, 96))
+    rec = synth.rec_plan(seed=9, std=None, vocab=300)
+    xd, xr = synth.stripes(128, 96), synth.stripes(48, 200)
+    apart = []
+    for plan, x, hw in ((det, xd, None), (rec, xr, (48, 200))):
+        apart.append(gpu_run(cuda_mod, plan, x, hw=hw)[0][0])
+    for first_closed in (0, 1):
+        a = cuda_mod.Model(det)
+        b = cuda_mod.Model(rec)
+        b.set_stream(a.stream)
+        b.set_input_size(48, 200)
+        a.input_mut()[:] = xd
+        b.input_mut()[:] = xr
+        a.enqueue()
+        b.enqueue()
+        b.wait(60_000)
+        a.wait(60_000)
+        assert np.array_equal(a.output(), apart[0])
+        assert np.array_equal(b.output(), apart[1])
+        models = [a, b]
+        models[first_closed].close()
+        models[1 - first_closed].close()

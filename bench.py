@@ -152,7 +152,7 @@ def cpu_threads() -> int:
 class PagePipeline:
     """The detector and the recogniser runs of one page, queued on one stream."""
 
-    def __init__(self, cuda, synth, page, device: int):
+    def __init__(self, cuda, synth, page, device: int, workload: str = "page"):
         self.det = cuda.Model(synth.det_plan(seed=0), device=device)
         h, w = page.det.shape[:2]
         self.det.set_input_size(h, w)
@@ -163,8 +163,16 @@ class PagePipeline:
             m.set_stream(self.stream)
             m.set_sizes([(48, page.widths[i]) for i in run])
         self.page = page
+        self.workload = workload
 
     def models(self):
+        if self.workload == "det":
+            return [self.det]
+        if self.workload == "rec":
+            return list(self.recs)
+        return [self.det, *self.recs]
+
+    def all_models(self):
         return [self.det, *self.recs]
 
     def fill_host(self):
@@ -204,24 +212,48 @@ class PagePipeline:
 
     def close(self):
         # the recogniser models run on the detector's stream: they go first
-        for m in reversed(self.models()):
+        for m in reversed(self.all_models()):
             m.close()
 
 
-def probe_kernel(cuda, torch, device: int, reps: int = 20) -> dict:
-    """Time the detector's dominant kernel alone with CUDA events: the 3x3
-    96 -> 24 convolution of the RSE neck at a quarter of a 1984 x 1536 page
-    (496 x 384 pixels), the layer class with the most FLOPs of the page
-    (18 of its 35 detector GFLOP with the DB head's)."""
+DOMINANT = (496, 384, 96, 24)  # h, w, ic, oc of the probed 3x3 convolution
+
+
+def dominant_plan() -> bytes:
+    """The detector's dominant layer alone: the 3x3 96 -> 24 convolution of
+    the RSE neck at a quarter of a 1984 x 1536 page (496 x 384 pixels), the
+    layer class with the most FLOPs of the page (18 of its 35 detector GFLOP
+    with the DB head's)."""
     from ppocr_native_b200.plan import Op, encode, window
 
-    h, w, ic, oc = 496, 384, 96, 24
+    h, w, ic, oc = DOMINANT
     rng = np.random.default_rng(0)
     wt = rng.normal(0, 0.02, 9 * ic * oc).astype(np.float32)
     b = rng.normal(0, 0.02, oc).astype(np.float32)
     op = window(Op("conv", x=0, y=1, ic=ic, oc=oc, w=(0, wt.size), b=(wt.size, oc)), (3, 3), 1, 1, 1)
-    plan = encode((0, h, w, ic), 2, [1], [op], np.concatenate([wt, b]))
-    m = cuda.Model(plan, device=device)
+    return encode((0, h, w, ic), 2, [1], [op], np.concatenate([wt, b]))
+
+
+def run_layer(args, d, cuda, torch, device):
+    """--workload layer: the dominant layer alone, warm-up then timed steps
+    (the command ncu captures)."""
+    m = cuda.Model(dominant_plan(), device=device)
+    h, w, ic, _ = DOMINANT
+    m.input_mut()[:] = np.random.default_rng(0).standard_normal(h * w * ic).astype(np.float32)
+    m.run(60_000)
+    for _ in range(args.warmup + args.steps):
+        m.enqueue_device()
+    m.wait(60_000)
+    m.close()
+    return {"profile": "layer", "launches_per_step": 1} if d.rank == 0 else None
+
+
+def probe_kernel(cuda, torch, device: int, reps: int = 20) -> dict:
+    """Time the detector's dominant kernel alone with CUDA events (see
+    `dominant_plan`)."""
+    h, w, ic, oc = DOMINANT
+    rng = np.random.default_rng(0)
+    m = cuda.Model(dominant_plan(), device=device)
     x = rng.standard_normal(h * w * ic).astype(np.float32)
     m.input_mut()[:] = x
     m.run(60_000)
@@ -310,8 +342,10 @@ def run_ours(args, d: Dist) -> dict | None:
     device = d.local
     torch.cuda.set_device(device)
     d.init("nccl")
+    if args.workload == "layer":
+        return run_layer(args, d, cuda, torch, device)
     page = workload.Page(seed=1000 + d.rank)
-    pipe = PagePipeline(cuda, synth, page, device)
+    pipe = PagePipeline(cuda, synth, page, device, args.workload)
     stream = torch.cuda.ExternalStream(pipe.stream)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
 
@@ -342,6 +376,13 @@ def run_ours(args, d: Dist) -> dict | None:
     local_s = sum(a.elapsed_time(b) for a, b in events) / 1e3
     total_s = d.max(local_s)
     value = d.world * args.steps / total_s
+    if args.profile:
+        launches = pipe.launches()
+        pipe.close()
+        if d.rank == 0:
+            return {"profile": args.workload, "ms_per_step": total_s / args.steps * 1e3,
+                    "launches_per_step": launches}
+        return None
 
     # e2e: the public call sequence with host buffers.
     d.barrier()
@@ -444,6 +485,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["page", "det", "rec", "layer"], default="page",
+                    help="page (the benchmark step); det or rec alone, for profiling")
+    ap.add_argument("--profile", action="store_true",
+                    help="only warm-up and timed steps (no e2e, probe, peak or CPU legs): for ncu launch lists")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     d = Dist()
@@ -451,7 +496,7 @@ def main():
         result = run_reference(args, d)
     else:
         result = run_ours(args, d)
-        if result is not None:
+        if result is not None and not args.profile:
             if args.no_cpu_baseline:
                 result["cpu_baseline"] = None
             else:

@@ -1,6 +1,6 @@
 // Dense convolution as an implicit GEMM on the FP32 pipes (sm_100a).
 //
-// GEMM view: M = N*oh*ow output pixels, Nc = oc output channels,
+// GEMM view: M = output pixels of all lanes, Nc = oc output channels,
 // K = kh*kw*C with k = (ky*kw + kx)*C + c, the order of the weights
 // `[kh][kw][C][oc]` and of the reference's sums (`kernels/dense.rs:20-36`).
 // A block owns a BM x BN output tile; its threads hold TM x TN accumulators
@@ -25,10 +25,6 @@ namespace {
 constexpr int BK = 8;
 constexpr int APAD = 4;
 
-struct Tile {
-    int tap, c0;
-};
-
 template <int TM, int TN, int TX, int TY>
 struct Cfg {
     static constexpr int BM = TM * TY, BN = TN * TX, THREADS = TX * TY;
@@ -38,9 +34,10 @@ struct Cfg {
     static constexpr int BLOADS = (BELEMS + THREADS - 1) / THREADS;
 };
 
-// Pixel coordinates of one A-load slot, fixed for the whole K loop.
+// Pixel coordinates of one A-load slot, fixed for the whole K loop: its
+// lane, the lane's input size, and the top-left input tap.
 struct Pixel {
-    int n, iy0, ix0;
+    int n, iy0, ix0, ih, iw;
     bool ok;
 };
 
@@ -50,7 +47,8 @@ __device__ __forceinline__ void load_a_group(const ConvArgs &a, const Pixel &px,
     if (!px.ok) return;
     int ky = tap / a.kw, kx = tap - ky * a.kw;
     int iy = px.iy0 + ky, ix = px.ix0 + kx;
-    if (iy < 0 || iy >= a.ih || ix < 0 || ix >= a.iw) return;
+    if (iy < 0 || iy >= px.ih || ix < 0 || ix >= px.iw) return;
+    const LaneInfo &L = a.lanes[px.n];
     if (vec4) {
         // All four channels lie in one source (every source has c % 4 == 0).
         if (c >= a.C) return;
@@ -58,8 +56,8 @@ __device__ __forceinline__ void load_a_group(const ConvArgs &a, const Pixel &px,
         while (s + 1 < a.nsrc && c >= start + a.src[s].c) { start += a.src[s].c; s++; }
         const ConvSource &src = a.src[s];
         int sh = src.shift;
-        int hs = a.ih >> sh, ws = a.iw >> sh;
-        long off = (((long)px.n * hs + (iy >> sh)) * ws + (ix >> sh)) * src.c + (c - start);
+        int ws = px.iw >> sh;
+        long off = (__ldg(&L.spix0[s]) + (long)(iy >> sh) * ws + (ix >> sh)) * src.c + (c - start);
         float4 q = __ldg(reinterpret_cast<const float4 *>(src.p + off));
         v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
         if (a.gate) {
@@ -77,8 +75,8 @@ __device__ __forceinline__ void load_a_group(const ConvArgs &a, const Pixel &px,
         while (s + 1 < a.nsrc && ce >= start + a.src[s].c) { start += a.src[s].c; s++; }
         const ConvSource &src = a.src[s];
         int sh = src.shift;
-        int hs = a.ih >> sh, ws = a.iw >> sh;
-        long off = (((long)px.n * hs + (iy >> sh)) * ws + (ix >> sh)) * src.c + (ce - start);
+        int ws = px.iw >> sh;
+        long off = (__ldg(&L.spix0[s]) + (long)(iy >> sh) * ws + (ix >> sh)) * src.c + (ce - start);
         float x = __ldg(src.p + off);
         if (a.gate) x = fmul(x, a.gate[(long)px.n * a.C + ce]);
         v[e] = x;
@@ -95,7 +93,7 @@ __global__ void __launch_bounds__(TX *TY) conv_gemm(const ConvArgs a, int ctiles
 
     const int tid = threadIdx.x;
     const int tx = tid % TX, ty = tid / TX;
-    const long M = (long)a.N * a.oh * a.ow;
+    const long M = a.M;
     const long m0 = (long)blockIdx.x * BM;
     const int n0 = blockIdx.y * BN;
 
@@ -110,14 +108,18 @@ __global__ void __launch_bounds__(TX *TY) conv_gemm(const ConvArgs a, int ctiles
         long m = m0 + am[l];
         px[l].ok = g < C::AGROUPS && m < M;
         if (px[l].ok) {
-            int hw = a.oh * a.ow;
-            int n = int(m / hw), r = int(m - (long)n * hw);
-            int oy = r / a.ow, ox = r - oy * a.ow;
+            int n = find_lane(a.lanes, a.nl, m);
+            const LaneInfo &L = a.lanes[n];
+            int ow = __ldg(&L.ow);
+            int r = int(m - __ldg(&L.pix0));
+            int oy = r / ow, ox = r - oy * ow;
             px[l].n = n;
+            px[l].ih = __ldg(&L.ih);
+            px[l].iw = __ldg(&L.iw);
             px[l].iy0 = oy * a.sh - a.pt;
             px[l].ix0 = ox * a.sw - a.pl;
         } else {
-            px[l].n = px[l].iy0 = px[l].ix0 = 0;
+            px[l].n = px[l].iy0 = px[l].ix0 = px[l].ih = px[l].iw = 0;
         }
     }
 
@@ -194,8 +196,10 @@ __global__ void __launch_bounds__(TX *TY) conv_gemm(const ConvArgs a, int ctiles
         long m = m0 + ty * TM + i;
         bool f = a.bias_mode == BIAS_FIRST;
         if (a.bias_mode == BIAS_FIRST_BUT_ROW_TAIL && m < M) {
-            int ox = int(m % a.ow);
-            f = ox < a.ow - a.ow % 4;
+            const LaneInfo &L = a.lanes[find_lane(a.lanes, a.nl, m)];
+            int ow = __ldg(&L.ow);
+            int ox = int((m - __ldg(&L.pix0)) % ow);
+            f = ox < ow - ow % 4;
         }
         first[i] = f;
 #pragma unroll
@@ -248,7 +252,7 @@ __global__ void __launch_bounds__(TX *TY) conv_gemm(const ConvArgs a, int ctiles
 template <int TM, int TN, int TX, int TY>
 int run(const ConvArgs &a, cudaStream_t s, bool vec4) {
     using C = Cfg<TM, TN, TX, TY>;
-    long M = (long)a.N * a.oh * a.ow;
+    long M = a.M;
     int ctiles = (a.C + BK - 1) / BK;
     int taps = a.kh * a.kw;
     dim3 grid((unsigned)((M + C::BM - 1) / C::BM), (unsigned)((a.oc + C::BN - 1) / C::BN));

@@ -15,19 +15,39 @@ namespace ppocr {
 
 namespace {
 
+// Where output pixel m of a depthwise layer reads: its lane's input, the
+// lane's input size and the output coordinates.
+struct DwPixel {
+    const float *xn;
+    int ih, iw, oy, ox;
+};
+
+__device__ __forceinline__ DwPixel dw_locate(const DwArgs &a, long m) {
+    const LaneInfo &L = a.lanes[find_lane(a.lanes, a.nl, m)];
+    DwPixel p;
+    int ow = __ldg(&L.ow);
+    int r = int(m - __ldg(&L.pix0));
+    p.oy = r / ow;
+    p.ox = r - p.oy * ow;
+    p.ih = __ldg(&L.ih);
+    p.iw = __ldg(&L.iw);
+    p.xn = a.x + __ldg(&L.ipix0) * a.c;
+    return p;
+}
+
 // Depthwise outputs of `count` channels (1 or 4) of one pixel, into v.
 template <int VEC>
-__device__ __forceinline__ void dw_pixel(const DwArgs &a, int n, int oy, int ox, int c, float v[VEC]) {
+__device__ __forceinline__ void dw_pixel(const DwArgs &a, const DwPixel &px, int c, float v[VEC]) {
 #pragma unroll
     for (int e = 0; e < VEC; e++) v[e] = a.b ? __ldg(a.b + c + e) : 0.0f;
-    const float *xn = a.x + (long)n * a.ih * a.iw * a.c;
+    const float *xn = px.xn;
     for (int ky = 0; ky < a.kh; ky++) {
-        int iy = oy * a.sh - a.pt + ky;
-        if (iy < 0 || iy >= a.ih) continue;
+        int iy = px.oy * a.sh - a.pt + ky;
+        if (iy < 0 || iy >= px.ih) continue;
         for (int kx = 0; kx < a.kw; kx++) {
-            int ix = ox * a.sw - a.pl + kx;
-            if (ix < 0 || ix >= a.iw) continue;
-            const float *src = xn + ((long)iy * a.iw + ix) * a.c + c;
+            int ix = px.ox * a.sw - a.pl + kx;
+            if (ix < 0 || ix >= px.iw) continue;
+            const float *src = xn + ((long)iy * px.iw + ix) * a.c + c;
             const float *w = a.w + (ky * a.kw + kx) * a.c + c;
             if (VEC == 4) {
                 float4 q = __ldg(reinterpret_cast<const float4 *>(src));
@@ -47,16 +67,13 @@ __device__ __forceinline__ void dw_pixel(const DwArgs &a, int n, int oy, int ox,
 
 template <int VEC>
 __global__ void __launch_bounds__(256) dw_kernel(const DwArgs a) {
-    long groups = (long)a.N * a.oh * a.ow * (a.c / VEC);
+    long groups = a.M * (a.c / VEC);
     for (long g = (long)blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += (long)gridDim.x * blockDim.x) {
         int cg = a.c / VEC;
         long m = g / cg;
         int c = int(g - m * cg) * VEC;
-        int hw = a.oh * a.ow;
-        int n = int(m / hw), r = int(m - (long)n * hw);
-        int oy = r / a.ow, ox = r - oy * a.ow;
         float v[VEC];
-        dw_pixel<VEC>(a, n, oy, ox, c, v);
+        dw_pixel<VEC>(a, dw_locate(a, m), c, v);
         float *dst = a.y + m * a.c + c;
         if (VEC == 4)
             *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
@@ -83,9 +100,8 @@ __global__ void __launch_bounds__(TX *TY) dw_pw_kernel(const DwPwArgs a) {
 
     const int tid = threadIdx.x;
     const int tx = tid % TX, ty = tid / TX;
-    const long M = (long)d.N * d.oh * d.ow;
+    const long M = d.M;
     const long m0 = (long)blockIdx.x * BM;
-    const int hw = d.oh * d.ow;
 
     // Phase 1: the depthwise tile, [channel][pixel].
     const bool vec = (C % 4) == 0;
@@ -94,16 +110,15 @@ __global__ void __launch_bounds__(TX *TY) dw_pw_kernel(const DwPwArgs a) {
         int p = g / cg, c = (g - p * cg) * (vec ? 4 : 1);
         long m = m0 + p;
         if (m < M) {
-            int n = int(m / hw), r = int(m - (long)n * hw);
-            int oy = r / d.ow, ox = r - oy * d.ow;
+            DwPixel px = dw_locate(d, m);
             if (vec) {
                 float v[4];
-                dw_pixel<4>(d, n, oy, ox, c, v);
+                dw_pixel<4>(d, px, c, v);
 #pragma unroll
                 for (int e = 0; e < 4; e++) Ds[(c + e) * (BM + DPAD) + p] = v[e];
             } else {
                 float v[1];
-                dw_pixel<1>(d, n, oy, ox, c, v);
+                dw_pixel<1>(d, px, c, v);
                 Ds[c * (BM + DPAD) + p] = v[0];
             }
         } else {
@@ -139,8 +154,9 @@ __global__ void __launch_bounds__(TX *TY) dw_pw_kernel(const DwPwArgs a) {
             long m = m0 + ty * TM + i;
             bool f = a.bias_mode2 == BIAS_FIRST;
             if (a.bias_mode2 == BIAS_FIRST_BUT_ROW_TAIL && m < M) {
-                int ox = int(m % d.ow);
-                f = ox < d.ow - d.ow % 4;
+                DwPixel px = dw_locate(d, m);
+                int ow = __ldg(&d.lanes[find_lane(d.lanes, d.nl, m)].ow);
+                f = px.ox < ow - ow % 4;
             }
             first[i] = f;
 #pragma unroll
@@ -202,7 +218,7 @@ template <int TM, int TN, int TX, int TY>
 int run_dw_pw(const DwPwArgs &a, cudaStream_t s) {
     constexpr int BM = TM * TY;
     size_t smem = dw_pw_smem<TM, TN, TX, TY>(a.dw.c);
-    long M = (long)a.dw.N * a.dw.oh * a.dw.ow;
+    long M = a.dw.M;
     dw_pw_kernel<TM, TN, TX, TY><<<(unsigned)((M + BM - 1) / BM), TX * TY, smem, s>>>(a);
     return 1;
 }
@@ -210,7 +226,7 @@ int run_dw_pw(const DwPwArgs &a, cudaStream_t s) {
 }  // namespace
 
 int launch_dw(const DwArgs &a, cudaStream_t s) {
-    long work = (long)a.N * a.oh * a.ow * (a.c % 4 == 0 ? a.c / 4 : a.c);
+    long work = a.M * (a.c % 4 == 0 ? a.c / 4 : a.c);
     long blocks = (work + 255) / 256;
     if (blocks > 148L * 64) blocks = 148L * 64;
     if (blocks < 1) blocks = 1;

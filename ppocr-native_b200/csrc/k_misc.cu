@@ -23,8 +23,7 @@ unsigned grid_for(long work, int threads = 256) {
 template <int VEC>
 __global__ void __launch_bounds__(256) elt_kernel(const EltArgs a) {
     const int cout = a.mode == ELT_CONCAT ? a.c + a.c2 : a.c;
-    const long total = (long)a.N * a.oh * a.ow * cout / VEC;
-    const int hw = a.oh * a.ow;
+    const long total = a.M * cout / VEC;
     for (long g = (long)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (long)gridDim.x * blockDim.x) {
         long e = g * VEC;
         long m = e / cout;
@@ -37,7 +36,7 @@ __global__ void __launch_bounds__(256) elt_kernel(const EltArgs a) {
             break;
         case ELT_CHANNELMUL:
         case ELT_GATE_ADD: {
-            int n = int(m / hw);
+            int n = find_lane(a.lanes, a.nl, m);
             const float *g = a.x2 + (long)n * a.c + c;
 #pragma unroll
             for (int k = 0; k < VEC; k++) {
@@ -49,9 +48,12 @@ __global__ void __launch_bounds__(256) elt_kernel(const EltArgs a) {
         }
         case ELT_UPSAMPLE:
         case ELT_UPSAMPLE_ADD: {
-            int n = int(m / hw), r = int(m - (long)n * hw);
-            int oy = r / a.ow, ox = r - oy * a.ow;
-            const float *src = a.x + (((long)n * a.ih + oy / a.sh) * a.iw + ox / a.sw) * a.c + c;
+            const LaneInfo &L = a.lanes[find_lane(a.lanes, a.nl, m)];
+            int ow = __ldg(&L.ow);
+            int r = int(m - __ldg(&L.pix0));
+            int oy = r / ow, ox = r - oy * ow;
+            long ip = __ldg(&L.ipix0) + (long)(oy / a.sh) * __ldg(&L.iw) + ox / a.sw;
+            const float *src = a.x + ip * a.c + c;
 #pragma unroll
             for (int k = 0; k < VEC; k++) v[k] = a.mode == ELT_UPSAMPLE ? src[k] : fadd(a.x2[e + k], src[k]);
             break;
@@ -78,23 +80,24 @@ __global__ void __launch_bounds__(256) elt_kernel(const EltArgs a) {
 // pool: whole windows, taps summed in row-major order then divided
 // (layers.rs:443-463).
 __global__ void __launch_bounds__(256) pool_kernel(const PoolArgs a) {
-    const long total = (long)a.N * a.oh * a.ow * a.c;
+    const long total = a.M * a.c;
     for (long g = (long)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (long)gridDim.x * blockDim.x) {
         long m = g / a.c;
         int c = int(g - m * a.c);
-        int hw = a.oh * a.ow;
-        int n = int(m / hw), r = int(m - (long)n * hw);
-        int oy = r / a.ow, ox = r - oy * a.ow;
-        const float *xn = a.x + (long)n * a.ih * a.iw * a.c + c;
+        const LaneInfo &L = a.lanes[find_lane(a.lanes, a.nl, m)];
+        int ow = __ldg(&L.ow), ih = __ldg(&L.ih), iw = __ldg(&L.iw);
+        int r = int(m - __ldg(&L.pix0));
+        int oy = r / ow, ox = r - oy * ow;
+        const float *xn = a.x + __ldg(&L.ipix0) * a.c + c;
         float v = 0.0f;
         bool seeded = false;
         for (int ky = 0; ky < a.kh; ky++) {
             int iy = oy * a.sh + ky;
-            if (iy >= a.ih) continue;
+            if (iy >= ih) continue;
             for (int kx = 0; kx < a.kw; kx++) {
                 int ix = ox * a.sw + kx;
-                if (ix >= a.iw) continue;
-                float x = xn[((long)iy * a.iw + ix) * a.c];
+                if (ix >= iw) continue;
+                float x = xn[((long)iy * iw + ix) * a.c];
                 if (a.average) {
                     v = fadd(v, x);
                 } else if (!seeded || x > v) {
@@ -118,9 +121,13 @@ __global__ void __launch_bounds__(256) mean_partial_kernel(const MeanArgs a) {
     const int n = blockIdx.y, chunk = blockIdx.x;
     const int rows = blockDim.x / a.c;  // pixels summed side by side
     const int t = threadIdx.x;
-    const int per = (a.hw + a.chunks - 1) / a.chunks;
-    const int p0 = chunk * per, p1 = min(a.hw, p0 + per);
-    const float *x = a.x + (long)n * a.hw * a.c;
+    const LaneInfo &L = a.lanes[n];
+    const int hw = __ldg(&L.ih) * __ldg(&L.iw);
+    const int chunks = mean_chunks(hw);  // a.chunks is the most of any lane
+    if (chunk >= chunks) return;
+    const int per = (hw + chunks - 1) / chunks;
+    const int p0 = chunk * per, p1 = min(hw, p0 + per);
+    const float *x = a.x + __ldg(&L.ipix0) * a.c;
     if (rows >= 1) {
         int row = t / a.c, c = t - row * a.c;
         double s = 0.0;
@@ -144,11 +151,13 @@ __global__ void __launch_bounds__(256) mean_partial_kernel(const MeanArgs a) {
 
 __global__ void mean_final_kernel(const MeanArgs a) {
     int g = blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= a.N * a.c) return;
+    if (g >= a.nl * a.c) return;
     int n = g / a.c, c = g - n * a.c;
+    int hw = a.lanes[n].ih * a.lanes[n].iw;
+    int chunks = mean_chunks(hw);
     double s = 0.0;
-    for (int k = 0; k < a.chunks; k++) s += a.partial[((long)n * a.chunks + k) * a.c + c];
-    a.y[g] = (float)(s / (double)a.hw);
+    for (int k = 0; k < chunks; k++) s += a.partial[((long)n * a.chunks + k) * a.c + c];
+    a.y[g] = (float)(s / (double)hw);
 }
 
 // --------------------------------------------------------------- layernorm
@@ -192,9 +201,10 @@ __global__ void __launch_bounds__(128) layernorm_kernel(const LayerNormArgs a) {
 __global__ void attention_kernel(const AttentionArgs a) {
     extern __shared__ float kv[];  // K [t][hd], V [t][hd]
     const int n = blockIdx.x / a.heads, h = blockIdx.x % a.heads;
-    const int hd = a.c / a.heads, t = a.t, c = a.c;
+    const LaneInfo &L = a.lanes[n];
+    const int hd = a.c / a.heads, t = L.iw, c = a.c;
     float *K = kv, *V = kv + t * hd;
-    const float *x = a.x + (long)n * t * 3 * c;
+    const float *x = a.x + L.ipix0 * 3 * c;
     for (int i = threadIdx.x; i < t * hd; i += blockDim.x) {
         int j = i / hd, d = i - j * hd;
         K[i] = x[(long)j * 3 * c + c + h * hd + d];
@@ -231,7 +241,7 @@ __global__ void attention_kernel(const AttentionArgs a) {
             float p = fmul(exp_neg(fsub(score(j), mx)), r);
             for (int d = 0; d < hd; d++) out[d] = ffma(V[j * hd + d], p, out[d]);
         }
-        float *y = a.y + ((long)n * t + s) * c + h * hd;
+        float *y = a.y + (L.pix0 + s) * c + h * hd;
         for (int d = 0; d < hd; d++) y[d] = out[d];
     }
 }
@@ -366,8 +376,7 @@ __global__ void ctc_merge_kernel(const CtcArgs a) {
 __global__ void __launch_bounds__(256) convt_kernel(const ConvTArgs a) {
     const int cols = a.kh * a.kw * a.oc;
     const int cg = (cols + 3) / 4;
-    const long total = (long)a.N * a.ih * a.iw * cg;
-    const int ow = a.iw * a.kw;
+    const long total = a.Min * cg;
     for (long g = (long)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (long)gridDim.x * blockDim.x) {
         long pix = g / cg;
         int c0 = int(g - pix * cg) * 4;
@@ -381,9 +390,11 @@ __global__ void __launch_bounds__(256) convt_kernel(const ConvTArgs a) {
             for (int j = 0; j < 4; j++)
                 if (c0 + j < cols) acc[j] = ffma(a.w[(long)i * cols + c0 + j], xv, acc[j]);
         }
-        int hw = a.ih * a.iw;
-        int n = int(pix / hw), r = int(pix - (long)n * hw);
-        int iy = r / a.iw, ix = r - iy * a.iw;
+        const LaneInfo &L = a.lanes[find_lane(a.lanes, a.nl, pix, true)];
+        int iw = __ldg(&L.iw), ow = iw * a.kw;
+        int r = int(pix - __ldg(&L.ipix0));
+        int iy = r / iw, ix = r - iy * iw;
+        long obase = __ldg(&L.pix0);
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             int col = c0 + j;
@@ -394,7 +405,7 @@ __global__ void __launch_bounds__(256) convt_kernel(const ConvTArgs a) {
             int tap = col / a.oc, o = col - tap * a.oc;
             int ky = tap / a.kw, kx = tap - ky * a.kw;
             long oy = (long)iy * a.kh + ky, ox = (long)ix * a.kw + kx;
-            a.y[(((long)n * a.ih * a.kh + oy) * ow + ox) * a.oc + o] = v;
+            a.y[(obase + oy * ow + ox) * a.oc + o] = v;
         }
     }
 }
@@ -404,7 +415,7 @@ __global__ void __launch_bounds__(256) convt_kernel(const ConvTArgs a) {
 int launch_elt(const EltArgs &a, cudaStream_t s) {
     int cout = a.mode == ELT_CONCAT ? a.c + a.c2 : a.c;
     bool vec = cout % 4 == 0 && a.c % 4 == 0 && (a.mode != ELT_CONCAT || a.c2 % 4 == 0);
-    long total = (long)a.N * a.oh * a.ow * cout;
+    long total = a.M * cout;
     if (vec)
         elt_kernel<4><<<grid_for(total / 4), 256, 0, s>>>(a);
     else
@@ -413,23 +424,17 @@ int launch_elt(const EltArgs &a, cudaStream_t s) {
 }
 
 int launch_pool(const PoolArgs &a, cudaStream_t s) {
-    pool_kernel<<<grid_for((long)a.N * a.oh * a.ow * a.c), 256, 0, s>>>(a);
+    pool_kernel<<<grid_for(a.M * a.c), 256, 0, s>>>(a);
     return 1;
 }
 
-int mean_chunks(int N, int hw, int c) {
-    (void)N;
-    (void)c;
-    int chunks = (hw + 511) / 512;
-    return chunks < 1 ? 1 : (chunks > 1024 ? 1024 : chunks);
-}
 
 int launch_mean(const MeanArgs &a, cudaStream_t s) {
     int threads = 256;
     int rows = a.c <= threads ? threads / a.c : 0;
     size_t smem = rows ? sizeof(double) * rows * a.c : 0;
-    mean_partial_kernel<<<dim3(a.chunks, a.N), threads, smem, s>>>(a);
-    mean_final_kernel<<<(a.N * a.c + 255) / 256, 256, 0, s>>>(a);
+    mean_partial_kernel<<<dim3(a.chunks, a.nl), threads, smem, s>>>(a);
+    mean_final_kernel<<<(a.nl * a.c + 255) / 256, 256, 0, s>>>(a);
     return 2;
 }
 
@@ -445,9 +450,9 @@ bool attention_supported(int t, int c, int heads) {
 
 int launch_attention(const AttentionArgs &a, cudaStream_t s) {
     int hd = a.c / a.heads;
-    size_t smem = sizeof(float) * 2 * a.t * hd;
-    int threads = a.t < 32 ? 32 : (a.t > 256 ? 256 : (a.t + 31) / 32 * 32);
-    attention_kernel<<<a.N * a.heads, threads, smem, s>>>(a);
+    size_t smem = sizeof(float) * 2 * a.tmax * hd;
+    int threads = a.tmax < 32 ? 32 : (a.tmax > 256 ? 256 : (a.tmax + 31) / 32 * 32);
+    attention_kernel<<<a.nl * a.heads, threads, smem, s>>>(a);
     return 1;
 }
 
@@ -462,7 +467,7 @@ int launch_ctc(const CtcArgs &a, cudaStream_t s) {
 
 int launch_convt(const ConvTArgs &a, cudaStream_t s) {
     int cols = a.kh * a.kw * a.oc;
-    long total = (long)a.N * a.ih * a.iw * ((cols + 3) / 4);
+    long total = a.Min * ((cols + 3) / 4);
     convt_kernel<<<grid_for(total), 256, 0, s>>>(a);
     return 1;
 }

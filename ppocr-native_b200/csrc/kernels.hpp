@@ -1,6 +1,11 @@
 // Launch arguments and entry points of every CUDA kernel of the backend.
-// Shared by the host runtime (model.cpp) and the kernels (*.cu). Tensors are
-// NHWC f32, lanes of one batch stored back to back ([N][H][W][C]).
+// Shared by the host runtime (model.cpp) and the kernels (*.cu).
+//
+// Tensors are NHWC f32. The lanes of one run (images of any sizes) are packed
+// back to back pixel by pixel, so a pixelwise operation sees one array of
+// M = sum of the lanes' pixels; an operation that needs a pixel's lane and
+// coordinates finds them in its lane table (LaneInfo), one entry per lane
+// with the prefix sums of the lanes' pixel counts.
 #pragma once
 
 #include <cstddef>
@@ -27,31 +32,62 @@ struct ConvSource {
 
 constexpr int MAX_SOURCES = 4;
 
+// One lane of one operation: where its pixels start in the packed output,
+// input and (per source, or the second input) tensors, and its sizes.
+struct LaneInfo {
+    long pix0;                // first output pixel
+    long ipix0;               // first input pixel
+    long spix0[MAX_SOURCES];  // first pixel in each conv source / the second input
+    int ih, iw, oh, ow;
+};
+
+#ifdef __CUDACC__
+// The lane holding packed pixel m: the last whose `pix0` (or `ipix0` when
+// `input`) is at most m.
+__device__ __forceinline__ int find_lane(const LaneInfo *L, int nl, long m, bool input = false) {
+    int lo = 0, hi = nl - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        long start = input ? __ldg(&L[mid].ipix0) : __ldg(&L[mid].pix0);
+        if (start <= m)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
+}
+#endif
+
 struct ConvArgs {
     ConvSource src[MAX_SOURCES];
     int nsrc = 1;
     int C = 0;                 // channels of all sources together
     const float *w = nullptr;  // [kh][kw][C][oc]
     const float *b = nullptr;  // [oc] or null
-    float *y = nullptr;        // [N][oh][ow][oc]
-    int N = 1, ih = 0, iw = 0, oh = 0, ow = 0, oc = 0;
+    float *y = nullptr;        // [M][oc]
+    const LaneInfo *lanes = nullptr;
+    int nl = 1;                // lanes
+    long M = 0;                // output pixels of all lanes
+    int oc = 0;
     int kh = 1, kw = 1, sh = 1, sw = 1, pt = 0, pl = 0;
     int act = 0;
     int bias_mode = BIAS_FIRST;
-    const float *gate = nullptr;  // [N][C]: input channel c of lane n is x * gate[n][c]
-    const float *res = nullptr;   // [N][oh][ow][oc]: y = act2(act(conv) + res)
+    const float *gate = nullptr;  // [lanes][C]: input channel c of lane n is x * gate[n][c]
+    const float *res = nullptr;   // [M][oc]: y = act2(act(conv) + res)
     int act2 = 0;
 };
 
 struct DwArgs {
-    const float *x = nullptr;  // [N][ih][iw][c]
+    const float *x = nullptr;  // packed input, c channels
     const float *w = nullptr;  // [kh][kw][c]
     const float *b = nullptr;  // [c] or null
-    float *y = nullptr;        // [N][oh][ow][c]
-    int N = 1, ih = 0, iw = 0, c = 0, oh = 0, ow = 0;
+    float *y = nullptr;        // [M][c]
+    const LaneInfo *lanes = nullptr;
+    int nl = 1;
+    long M = 0;
+    int c = 0;
     int kh = 3, kw = 3, sh = 1, sw = 1, pt = 0, pl = 0;
     int act = 0;
-    double *mean_partial = nullptr;  // optional: per-block f64 channel sums of y
 };
 
 // Depthwise convolution whose output feeds a pointwise one straight from
@@ -60,7 +96,7 @@ struct DwPwArgs {
     DwArgs dw;                  // dw.y unused
     const float *w2 = nullptr;  // [c][oc]
     const float *b2 = nullptr;  // [oc] or null
-    float *y = nullptr;         // [N][oh][ow][oc]
+    float *y = nullptr;         // [M][oc]
     int oc = 0;
     int act2 = 0;
     int bias_mode2 = BIAS_FIRST;
@@ -81,7 +117,10 @@ struct EltArgs {
     int mode = ELT_ADD;
     const float *x = nullptr, *x2 = nullptr;
     float *y = nullptr;
-    int N = 1, ih = 0, iw = 0, oh = 0, ow = 0, c = 0, c2 = 0;
+    const LaneInfo *lanes = nullptr;  // gates and upsampling
+    int nl = 1;
+    long M = 0;  // output pixels
+    int c = 0, c2 = 0;
     int sh = 1, sw = 1;
     int act = 0;
 };
@@ -89,15 +128,19 @@ struct EltArgs {
 struct PoolArgs {
     const float *x = nullptr;
     float *y = nullptr;
-    int N = 1, ih = 0, iw = 0, c = 0, oh = 0, ow = 0, kh = 1, kw = 1, sh = 1, sw = 1;
+    const LaneInfo *lanes = nullptr;
+    int nl = 1;
+    long M = 0;
+    int c = 0, kh = 1, kw = 1, sh = 1, sw = 1;
     bool average = false;
 };
 
 struct MeanArgs {
-    const float *x = nullptr;  // [N][hw][c]
-    float *y = nullptr;        // [N][c]
-    double *partial = nullptr; // [N][chunks][c] scratch
-    int N = 1, hw = 0, c = 0, chunks = 1;
+    const float *x = nullptr;  // packed input, c channels
+    float *y = nullptr;        // [lanes][c]
+    double *partial = nullptr; // [lanes][chunks][c] scratch
+    const LaneInfo *lanes = nullptr;
+    int nl = 1, c = 0, chunks = 1;
 };
 
 struct LayerNormArgs {
@@ -107,10 +150,11 @@ struct LayerNormArgs {
 };
 
 struct AttentionArgs {
-    const float *x = nullptr;  // [N][t][3c]
-    float *y = nullptr;        // [N][t][c]
+    const float *x = nullptr;  // packed [t][3c] per lane
+    float *y = nullptr;        // packed [t][c] per lane
     const float *scale = nullptr;
-    int N = 1, t = 0, c = 0, heads = 1;
+    const LaneInfo *lanes = nullptr;  // t of lane n = lanes[n].iw
+    int nl = 1, tmax = 0, c = 0, heads = 1;
 };
 
 // CTC head over `cols` = 16 * ceil(vocab / 16) panel columns: each block
@@ -127,11 +171,14 @@ struct CtcArgs {
 };
 
 struct ConvTArgs {
-    const float *x = nullptr;  // [N][ih][iw][ic]
+    const float *x = nullptr;  // packed input, ic channels
     const float *w = nullptr;  // [ic][kh][kw][oc]
     const float *b = nullptr;  // [kh*kw*oc] or null
-    float *y = nullptr;        // [N][ih*kh][iw*kw][oc]
-    int N = 1, ih = 0, iw = 0, ic = 0, oc = 0, kh = 2, kw = 2;
+    float *y = nullptr;        // packed output, oc channels
+    const LaneInfo *lanes = nullptr;
+    int nl = 1;
+    long Min = 0;              // input pixels of all lanes
+    int ic = 0, oc = 0, kh = 2, kw = 2;
     int act = 0;
     bool bias_first = true;
     // A second transposed convolution fed from the first one's output
@@ -157,7 +204,12 @@ int launch_convt(const ConvTArgs &a, cudaStream_t s);
 void configure_dw_kernels();
 
 // Scratch sizes (elements) the launches above need.
-int mean_chunks(int N, int hw, int c);
+// Pixel runs a lane's channel mean is split into; a lane's result depends
+// only on its own size, never on the other lanes of the run.
+__host__ __device__ inline int mean_chunks(long hw) {
+    long chunks = (hw + 511) / 512;
+    return int(chunks < 1 ? 1 : (chunks > 1024 ? 1024 : chunks));
+}
 int ctc_col_blocks(int cols);
 // Largest shared-memory need of launch_dw_pw for `c` input channels; 0 when
 // that kernel cannot take them.

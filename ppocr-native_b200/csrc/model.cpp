@@ -327,16 +327,26 @@ std::vector<Step> fuse(const Plan &p, bool enabled) {
 
 // ------------------------------------------------------------------- model
 
+// The lanes of one run, packed: every plan buffer holds the lanes' tensors
+// back to back, pixel by pixel, sized for the largest total any operation
+// writes there.
 struct Group {
-    size_t h = 0, w = 0;
-    std::vector<size_t> lanes;  // model lane indices, in batch order
-    Plan plan;
+    std::vector<Plan> plans;            // one per distinct lane size
+    std::vector<size_t> lane_plan;      // per lane: index into plans
+    std::vector<size_t> in_off;         // per lane: first float of its input
+    std::vector<std::vector<size_t>> out_off;  // per output, per lane: first float
+    size_t in_floats = 0;
+    std::vector<size_t> out_floats;     // per output: all lanes
     std::vector<std::unique_ptr<DeviceBuffer>> slots;
-    DeviceBuffer mean_scratch, ctc_scratch;
-    HostBuffer in_host;                  // [N][h][w][c]
-    std::vector<std::unique_ptr<HostBuffer>> out_host;  // per output: [N][n]
+    DeviceBuffer mean_scratch, ctc_scratch, lane_tables;
+    HostBuffer in_host;
+    std::vector<std::unique_ptr<HostBuffer>> out_host;
     std::vector<std::function<int(cudaStream_t)>> launches;
+    size_t input_slot = 0;
+    std::vector<size_t> output_slots;
     float *slot_ptr(size_t s) const { return static_cast<float *>(slots[s]->p); }
+    const Plan &lane(size_t n) const { return plans[lane_plan[n]]; }
+    size_t count() const { return lane_plan.size(); }
 };
 
 struct ppocr_model {
@@ -353,8 +363,7 @@ struct ppocr_model {
     std::vector<Step> steps;
     bool steps_fused = false;
     std::vector<std::pair<size_t, size_t>> sizes;  // per lane (h, w)
-    std::vector<std::pair<size_t, size_t>> where;  // per lane (group, index in group)
-    std::vector<std::unique_ptr<Group>> groups;
+    std::unique_ptr<Group> group;
     cudaGraphExec_t graph_host = nullptr, graph_device = nullptr;
     size_t launches = 0;
     bool pending = false;
@@ -366,7 +375,7 @@ struct ppocr_model {
         settle();
         if (own_stream) cudaStreamSynchronize(own_stream);
         drop_graphs();
-        groups.clear();
+        group.reset();
         if (done) cudaEventDestroy(done);
         if (own_stream) cudaStreamDestroy(own_stream);
     }
@@ -400,15 +409,74 @@ int ppocr_model::bias_mode(const Op &op) const {
     return BIAS_FIRST_BUT_ROW_TAIL;
 }
 
+namespace {
+
+// The lane table of operation `i` over the group's lanes, with the source
+// shifts of a dense convolution's inputs (pixel prefix sums per source).
+std::vector<LaneInfo> lane_table(const Group &g, size_t i, const std::vector<int> &shifts) {
+    std::vector<LaneInfo> t(g.count());
+    long pix = 0, ipix = 0, spix[MAX_SOURCES] = {0, 0, 0, 0};
+    for (size_t n = 0; n < g.count(); n++) {
+        const Op &op = g.lane(n).ops[i];
+        LaneInfo &L = t[n];
+        L.pix0 = pix;
+        L.ipix0 = ipix;
+        for (int s = 0; s < MAX_SOURCES; s++) L.spix0[s] = spix[s];
+        L.ih = int(op.ih); L.iw = int(op.iw); L.oh = int(op.oh); L.ow = int(op.ow);
+        pix += long(op.oh * op.ow);
+        ipix += long(op.ih * op.iw);
+        for (size_t s = 0; s < shifts.size() && s < size_t(MAX_SOURCES); s++)
+            spix[s] += long(op.ih >> shifts[s]) * long(op.iw >> shifts[s]);
+    }
+    return t;
+}
+
+long total_out(const Group &g, size_t i) {
+    long m = 0;
+    for (size_t n = 0; n < g.count(); n++) m += long(g.lane(n).ops[i].oh * g.lane(n).ops[i].ow);
+    return m;
+}
+
+long total_in(const Group &g, size_t i) {
+    long m = 0;
+    for (size_t n = 0; n < g.count(); n++) m += long(g.lane(n).ops[i].ih * g.lane(n).ops[i].iw);
+    return m;
+}
+
+}  // namespace
+
 int ppocr_model::build_group(Group &g, std::string &err) {
-    Plan &p = g.plan;
-    const size_t N = g.lanes.size();
+    const Plan &p0 = g.plans[0];
+    const size_t N = g.count();
     int code = PPOCR_OK;
+    g.input_slot = p0.slot;
+    g.output_slots = p0.outputs;
+    // Packed sizes: each buffer holds the most floats any writer puts there.
+    std::vector<size_t> slot_floats(p0.pool.size(), 0);
+    g.in_off.assign(N, 0);
+    g.in_floats = 0;
+    for (size_t n = 0; n < N; n++) {
+        g.in_off[n] = g.in_floats;
+        g.in_floats += g.lane(n).h * g.lane(n).w * g.lane(n).c;
+    }
+    slot_floats[p0.slot] = g.in_floats;
+    for (size_t i = 0; i < p0.ops.size(); i++) {
+        size_t total = 0;
+        for (size_t n = 0; n < N; n++) total += g.lane(n).ops[i].out_len();
+        slot_floats[p0.ops[i].y] = std::max(slot_floats[p0.ops[i].y], total);
+    }
+    g.out_off.assign(p0.outputs.size(), std::vector<size_t>(N, 0));
+    g.out_floats.assign(p0.outputs.size(), 0);
+    for (size_t k = 0; k < p0.outputs.size(); k++)
+        for (size_t n = 0; n < N; n++) {
+            g.out_off[k][n] = g.out_floats[k];
+            g.out_floats[k] += g.lane(n).out_n[k];
+        }
     // Tensors.
     g.slots.clear();
-    for (size_t s = 0; s < p.pool.size(); s++) {
+    for (size_t s = 0; s < slot_floats.size(); s++) {
         auto b = std::make_unique<DeviceBuffer>();
-        b->bytes = std::max<size_t>(p.pool[s], 1) * N * sizeof(float);
+        b->bytes = std::max<size_t>(slot_floats[s], 1) * sizeof(float);
         if (!cuda_ok(cudaMalloc(&b->p, b->bytes), "allocating a tensor", &code)) {
             err = g_error;
             return code;
@@ -417,13 +485,17 @@ int ppocr_model::build_group(Group &g, std::string &err) {
     }
     // Scratch.
     size_t mean_doubles = 1, ctc_floats = 1;
-    for (const Op &op : p.ops) {
-        if (op.kind == K_MEAN)
-            mean_doubles = std::max(mean_doubles, N * mean_chunks(int(N), int(op.ih * op.iw), int(op.ic)) * op.ic);
+    for (size_t i = 0; i < p0.ops.size(); i++) {
+        const Op &op = p0.ops[i];
+        if (op.kind == K_MEAN) {
+            long hw = 0;
+            for (size_t n = 0; n < N; n++) hw = std::max<long>(hw, long(g.lane(n).ops[i].ih * g.lane(n).ops[i].iw));
+            mean_doubles = std::max(mean_doubles, N * size_t(mean_chunks(hw)) * op.ic);
+        }
         if (op.kind == K_CTCHEAD || op.kind == K_CTCARGMAX) {
             size_t vocab = op.kind == K_CTCHEAD ? op.oc : op.n2;
             size_t cols = (vocab + 15) / 16 * 16;
-            ctc_floats = std::max(ctc_floats, N * op.iw * ctc_col_blocks(int(cols)) * 3);
+            ctc_floats = std::max(ctc_floats, size_t(total_in(g, i)) * ctc_col_blocks(int(cols)) * 3);
         }
     }
     g.mean_scratch.bytes = mean_doubles * sizeof(double);
@@ -434,16 +506,16 @@ int ppocr_model::build_group(Group &g, std::string &err) {
         return code;
     }
     // Page-locked host staging.
-    g.in_host.bytes = N * p.h * p.w * p.c * sizeof(float);
+    g.in_host.bytes = std::max<size_t>(g.in_floats, 1) * sizeof(float);
     if (!cuda_ok(cudaHostAlloc(&g.in_host.p, g.in_host.bytes, cudaHostAllocDefault), "allocating host input", &code)) {
         err = g_error;
         return code;
     }
     std::memset(g.in_host.p, 0, g.in_host.bytes);
     g.out_host.clear();
-    for (size_t k = 0; k < p.outputs.size(); k++) {
+    for (size_t k = 0; k < p0.outputs.size(); k++) {
         auto hb = std::make_unique<HostBuffer>();
-        hb->bytes = std::max<size_t>(p.out_n[k], 1) * N * sizeof(float);
+        hb->bytes = std::max<size_t>(g.out_floats[k], 1) * sizeof(float);
         if (!cuda_ok(cudaHostAlloc(&hb->p, hb->bytes, cudaHostAllocDefault), "allocating host output", &code)) {
             err = g_error;
             return code;
@@ -452,26 +524,52 @@ int ppocr_model::build_group(Group &g, std::string &err) {
         g.out_host.push_back(std::move(hb));
     }
 
+    // Lane tables of every step, in one device array.
+    std::vector<LaneInfo> tables;
+    std::vector<size_t> table_at(steps.size(), 0);
+    for (size_t k = 0; k < steps.size(); k++) {
+        const Step &st = steps[k];
+        if (st.kind == S_SKIP) continue;
+        size_t i = st.kind == S_CONV ? st.b : st.a;
+        std::vector<int> shifts;
+        if (st.kind == S_CONV)
+            for (const Step::Src &src : st.srcs) shifts.push_back(src.shift);
+        else if (p0.ops[i].kind == K_CONV && p0.ops[i].n2)
+            shifts = {0, 0};
+        table_at[k] = tables.size();
+        auto t = lane_table(g, i, shifts);
+        tables.insert(tables.end(), t.begin(), t.end());
+    }
+    g.lane_tables.bytes = std::max<size_t>(tables.size(), 1) * sizeof(LaneInfo);
+    if (!cuda_ok(cudaMalloc(&g.lane_tables.p, g.lane_tables.bytes), "allocating lane tables", &code) ||
+        !cuda_ok(cudaMemcpy(g.lane_tables.p, tables.data(), tables.size() * sizeof(LaneInfo),
+                            cudaMemcpyHostToDevice), "uploading lane tables", &code)) {
+        err = g_error;
+        return code;
+    }
+    const LaneInfo *lt = static_cast<const LaneInfo *>(g.lane_tables.p);
+
     // Launches.
     g.launches.clear();
     const Weights &W = *weights;
-    const int n = int(N);
+    const int nl = int(N);
     auto buf = [&g](size_t s) { return g.slot_ptr(s); };
-    for (const Step &st : steps) {
+    for (size_t k = 0; k < steps.size(); k++) {
+        const Step &st = steps[k];
         if (st.kind == S_SKIP) continue;
+        const LaneInfo *L = lt + table_at[k];
         if (st.kind == S_DW_PW) {
-            const Op &dw = p.ops[st.a], &pw = p.ops[st.b];
+            const Op &dw = p0.ops[st.a], &pw = p0.ops[st.b];
             DwPwArgs a;
             a.dw.x = buf(dw.x); a.dw.w = W.w(st.a); a.dw.b = W.b(st.a);
-            a.dw.N = n; a.dw.ih = int(dw.ih); a.dw.iw = int(dw.iw); a.dw.c = int(dw.ic);
-            a.dw.oh = int(dw.oh); a.dw.ow = int(dw.ow); a.dw.kh = int(dw.kh); a.dw.kw = int(dw.kw);
-            a.dw.sh = int(dw.sh); a.dw.sw = int(dw.sw); a.dw.pt = int(dw.pt); a.dw.pl = int(dw.pl);
-            a.dw.act = dw.fused;
+            a.dw.lanes = L; a.dw.nl = nl; a.dw.M = total_out(g, st.a); a.dw.c = int(dw.ic);
+            a.dw.kh = int(dw.kh); a.dw.kw = int(dw.kw); a.dw.sh = int(dw.sh); a.dw.sw = int(dw.sw);
+            a.dw.pt = int(dw.pt); a.dw.pl = int(dw.pl); a.dw.act = dw.fused;
             a.w2 = W.w(st.b); a.b2 = W.b(st.b); a.oc = int(pw.oc); a.act2 = pw.fused;
             a.bias_mode2 = bias_mode(pw);
             a.y = buf(pw.y);
             if (st.has_add) {
-                const Op &add = p.ops[st.c];
+                const Op &add = p0.ops[st.c];
                 a.res = buf(add.x == pw.y ? add.x2 : add.x);
                 a.act3 = add.fused;
                 a.y = buf(add.y);
@@ -480,26 +578,26 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             continue;
         }
         if (st.kind == S_CONV) {
-            const Op &op = p.ops[st.b];
+            const Op &op = p0.ops[st.b];
             ConvArgs a;
             a.nsrc = int(st.srcs.size());
             a.C = 0;
-            for (size_t k = 0; k < st.srcs.size(); k++) {
-                a.src[k].p = buf(st.srcs[k].slot);
-                a.src[k].c = int(st.srcs[k].c);
-                a.src[k].shift = st.srcs[k].shift;
-                a.C += int(st.srcs[k].c);
+            for (size_t q = 0; q < st.srcs.size(); q++) {
+                a.src[q].p = buf(st.srcs[q].slot);
+                a.src[q].c = int(st.srcs[q].c);
+                a.src[q].shift = st.srcs[q].shift;
+                a.C += int(st.srcs[q].c);
             }
-            if (st.gated) a.gate = buf(p.ops[st.a].x2);
+            if (st.gated) a.gate = buf(p0.ops[st.a].x2);
             a.w = W.w(st.b); a.b = W.b(st.b);
-            a.N = n; a.ih = int(op.ih); a.iw = int(op.iw); a.oh = int(op.oh); a.ow = int(op.ow); a.oc = int(op.oc);
+            a.lanes = L; a.nl = nl; a.M = total_out(g, st.b); a.oc = int(op.oc);
             a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
             a.pt = int(op.pt); a.pl = int(op.pl);
             a.act = op.fused;
             a.bias_mode = bias_mode(op);
             a.y = buf(op.y);
             if (st.has_add) {
-                const Op &add = p.ops[st.c];
+                const Op &add = p0.ops[st.c];
                 a.res = buf(add.x == op.y ? add.x2 : add.x);
                 a.act2 = add.fused;
                 a.y = buf(add.y);
@@ -508,17 +606,17 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             continue;
         }
         if (st.kind == S_GATE_ADD) {
-            const Op &cm = p.ops[st.a], &add = p.ops[st.b];
+            const Op &cm = p0.ops[st.a], &add = p0.ops[st.b];
             EltArgs a;
             a.mode = ELT_GATE_ADD;
             a.x = buf(cm.x); a.x2 = buf(cm.x2); a.y = buf(add.y);
-            a.N = n; a.oh = int(cm.oh); a.ow = int(cm.ow); a.c = int(cm.oc); a.act = add.fused;
+            a.lanes = L; a.nl = nl; a.M = total_out(g, st.a); a.c = int(cm.oc); a.act = add.fused;
             g.launches.push_back([a](cudaStream_t s) { return launch_elt(a, s); });
             continue;
         }
         // One operation alone.
         const size_t i = st.a;
-        const Op &op = p.ops[i];
+        const Op &op = p0.ops[i];
         switch (op.kind) {
         case K_CONV: {
             ConvArgs a;
@@ -527,7 +625,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             if (op.n2) { a.src[1] = {buf(op.x2), int(op.n2), 0}; a.nsrc = 2; }
             a.C = int(op.ic + op.n2);
             a.w = W.w(i); a.b = W.b(i);
-            a.N = n; a.ih = int(op.ih); a.iw = int(op.iw); a.oh = int(op.oh); a.ow = int(op.ow); a.oc = int(op.oc);
+            a.lanes = L; a.nl = nl; a.M = total_out(g, i); a.oc = int(op.oc);
             a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
             a.pt = int(op.pt); a.pl = int(op.pl); a.act = op.fused; a.bias_mode = bias_mode(op);
             a.y = buf(op.y);
@@ -537,7 +635,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
         case K_DWCONV: {
             DwArgs a;
             a.x = buf(op.x); a.w = W.w(i); a.b = W.b(i); a.y = buf(op.y);
-            a.N = n; a.ih = int(op.ih); a.iw = int(op.iw); a.c = int(op.ic); a.oh = int(op.oh); a.ow = int(op.ow);
+            a.lanes = L; a.nl = nl; a.M = total_out(g, i); a.c = int(op.ic);
             a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
             a.pt = int(op.pt); a.pl = int(op.pl); a.act = op.fused;
             g.launches.push_back([a](cudaStream_t s) { return launch_dw(a, s); });
@@ -548,7 +646,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             a.mode = op.kind == K_ADD ? ELT_ADD : op.kind == K_CHANNELMUL ? ELT_CHANNELMUL
                      : op.kind == K_CONCATC ? ELT_CONCAT : op.kind == K_UPSAMPLE ? ELT_UPSAMPLE : ELT_UPSAMPLE_ADD;
             a.x = buf(op.x); a.x2 = op.has_second() ? buf(op.x2) : nullptr; a.y = buf(op.y);
-            a.N = n; a.ih = int(op.ih); a.iw = int(op.iw); a.oh = int(op.oh); a.ow = int(op.ow);
+            a.lanes = L; a.nl = nl; a.M = total_out(g, i);
             a.c = int(op.kind == K_CONCATC ? op.ic : op.oc); a.c2 = int(op.n2);
             a.sh = int(std::max<size_t>(op.sh, 1)); a.sw = int(std::max<size_t>(op.sw, 1)); a.act = op.fused;
             g.launches.push_back([a](cudaStream_t s) { return launch_elt(a, s); });
@@ -557,7 +655,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
         case K_MAXPOOL: case K_AVGPOOL: {
             PoolArgs a;
             a.x = buf(op.x); a.y = buf(op.y);
-            a.N = n; a.ih = int(op.ih); a.iw = int(op.iw); a.c = int(op.ic); a.oh = int(op.oh); a.ow = int(op.ow);
+            a.lanes = L; a.nl = nl; a.M = total_out(g, i); a.c = int(op.ic);
             a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
             a.average = op.kind == K_AVGPOOL;
             g.launches.push_back([a](cudaStream_t s) { return launch_pool(a, s); });
@@ -566,26 +664,31 @@ int ppocr_model::build_group(Group &g, std::string &err) {
         case K_MEAN: {
             MeanArgs a;
             a.x = buf(op.x); a.y = buf(op.y); a.partial = static_cast<double *>(g.mean_scratch.p);
-            a.N = n; a.hw = int(op.ih * op.iw); a.c = int(op.ic); a.chunks = mean_chunks(n, a.hw, a.c);
+            a.lanes = L; a.nl = nl; a.c = int(op.ic);
+            long hw = 0;
+            for (size_t n = 0; n < N; n++) hw = std::max<long>(hw, long(g.lane(n).ops[i].ih * g.lane(n).ops[i].iw));
+            a.chunks = mean_chunks(hw);
             g.launches.push_back([a](cudaStream_t s) { return launch_mean(a, s); });
             break;
         }
         case K_LAYERNORM: {
             LayerNormArgs a;
             a.x = buf(op.x); a.w = W.w(i); a.y = buf(op.y);
-            a.pixels = int(N * op.oh * op.ow); a.c = int(op.oc);
+            a.pixels = int(total_out(g, i)); a.c = int(op.oc);
             g.launches.push_back([a](cudaStream_t s) { return launch_layernorm(a, s); });
             break;
         }
         case K_ATTENTION: {
-            if (!attention_supported(int(op.iw), int(op.oc), int(op.n2))) {
-                err = "attention over " + std::to_string(op.iw) + " steps with head size " +
+            int tmax = 0;
+            for (size_t n = 0; n < N; n++) tmax = std::max(tmax, int(g.lane(n).ops[i].iw));
+            if (!attention_supported(tmax, int(op.oc), int(op.n2))) {
+                err = "attention over " + std::to_string(tmax) + " steps with head size " +
                       std::to_string(op.oc / op.n2) + " exceeds this backend";
                 return PPOCR_E_UNSUPPORTED;
             }
             AttentionArgs a;
             a.x = buf(op.x); a.y = buf(op.y); a.scale = W.w(i);
-            a.N = n; a.t = int(op.iw); a.c = int(op.oc); a.heads = int(op.n2);
+            a.lanes = L; a.nl = nl; a.tmax = tmax; a.c = int(op.oc); a.heads = int(op.n2);
             g.launches.push_back([a](cudaStream_t s) { return launch_attention(a, s); });
             break;
         }
@@ -593,7 +696,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             CtcArgs a;
             a.x = buf(op.x); a.w = W.w(i); a.b = W.b(i); a.y = buf(op.y);
             a.partial = static_cast<float *>(g.ctc_scratch.p);
-            a.pixels = int(N * op.iw); a.ci = int(op.ic);
+            a.pixels = int(total_in(g, i)); a.ci = int(op.ic);
             a.probs = op.kind == K_CTCHEAD;
             a.vocab = int(a.probs ? op.oc : op.n2);
             a.cols = (a.vocab + 15) / 16 * 16;
@@ -604,7 +707,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
         case K_CONVTRANSPOSE: {
             ConvTArgs a;
             a.x = buf(op.x); a.w = W.w(i); a.b = W.b(i); a.y = buf(op.y);
-            a.N = n; a.ih = int(op.ih); a.iw = int(op.iw); a.ic = int(op.ic); a.oc = int(op.oc);
+            a.lanes = L; a.nl = nl; a.Min = total_in(g, i); a.ic = int(op.ic); a.oc = int(op.oc);
             a.kh = int(op.kh); a.kw = int(op.kw); a.act = op.fused;
             a.bias_first = (op.kh * op.kw * op.oc) % 16 == 0;
             g.launches.push_back([a](cudaStream_t s) { return launch_convt(a, s); });
@@ -621,22 +724,20 @@ int ppocr_model::build_group(Group &g, std::string &err) {
 // Record one run on the stream: the input copies (when `copies`), every
 // step's kernels, the output copies.
 int ppocr_model::record(bool copies) {
+    Group &g = *group;
+    if (copies) {
+        if (!cuda_ok(cudaMemcpyAsync(g.slot_ptr(g.input_slot), g.in_host.p, g.in_floats * sizeof(float),
+                                     cudaMemcpyHostToDevice, stream), "copying the input"))
+            return PPOCR_E_DEVICE;
+    }
     size_t count = 0;
-    for (auto &gp : groups) {
-        Group &g = *gp;
-        if (copies) {
-            if (!cuda_ok(cudaMemcpyAsync(g.slot_ptr(g.plan.slot), g.in_host.p, g.in_host.bytes,
-                                         cudaMemcpyHostToDevice, stream), "copying the input"))
+    for (auto &l : g.launches) count += size_t(l(stream));
+    if (copies) {
+        for (size_t k = 0; k < g.output_slots.size(); k++) {
+            if (!cuda_ok(cudaMemcpyAsync(g.out_host[k]->p, g.slot_ptr(g.output_slots[k]),
+                                         g.out_floats[k] * sizeof(float), cudaMemcpyDeviceToHost, stream),
+                         "copying an output"))
                 return PPOCR_E_DEVICE;
-        }
-        for (auto &l : g.launches) count += size_t(l(stream));
-        if (copies) {
-            for (size_t k = 0; k < g.plan.outputs.size(); k++) {
-                size_t bytes = g.lanes.size() * g.plan.out_n[k] * sizeof(float);
-                if (!cuda_ok(cudaMemcpyAsync(g.out_host[k]->p, g.slot_ptr(g.plan.outputs[k]), bytes,
-                                             cudaMemcpyDeviceToHost, stream), "copying an output"))
-                    return PPOCR_E_DEVICE;
-            }
         }
     }
     launches = count;
@@ -646,7 +747,7 @@ int ppocr_model::record(bool copies) {
 
 int ppocr_model::enqueue(bool copies) {
     if (!cuda_ok(cudaSetDevice(device), "selecting the device")) return PPOCR_E_DEVICE;
-    if (groups.empty()) return fail(PPOCR_E_SIZE, "the model has no lanes");
+    if (!group) return fail(PPOCR_E_SIZE, "the model has no lanes");
     int rc;
     if (options & PPOCR_OPT_NO_GRAPH) {
         rc = record(copies);
@@ -794,26 +895,21 @@ int ppocr_model_set_sizes(ppocr_model *m, const uint32_t *hw, size_t lanes) {
                                       std::to_string(ppocr_model_max_lanes(m)) + " a run takes");
     if (!cuda_ok(cudaSetDevice(m->device), "selecting the device")) return PPOCR_E_DEVICE;
     m->settle();
-    // Validate every size first, so that a refusal leaves the model as it was.
-    std::map<std::pair<size_t, size_t>, size_t> group_of;
-    std::vector<std::pair<size_t, size_t>> sizes, where;
-    std::vector<std::unique_ptr<Group>> groups;
+    // Every size is checked first, so that a refusal leaves the model as it was.
+    std::map<std::pair<size_t, size_t>, size_t> plan_of;
+    std::vector<std::pair<size_t, size_t>> sizes;
+    auto g = std::make_unique<Group>();
     for (size_t l = 0; l < lanes; l++) {
         std::pair<size_t, size_t> s{hw[2 * l], hw[2 * l + 1]};
-        auto it = group_of.find(s);
-        if (it == group_of.end()) {
-            auto g = std::make_unique<Group>();
-            g->h = s.first;
-            g->w = s.second;
-            g->plan = m->plan;
+        auto it = plan_of.find(s);
+        if (it == plan_of.end()) {
+            Plan p = m->plan;
             std::string err;
-            if (!g->plan.set_size(s.first, s.second, m->weight_floats, err)) return fail(PPOCR_E_SIZE, err);
-            it = group_of.emplace(s, groups.size()).first;
-            groups.push_back(std::move(g));
+            if (!p.set_size(s.first, s.second, m->weight_floats, err)) return fail(PPOCR_E_SIZE, err);
+            it = plan_of.emplace(s, g->plans.size()).first;
+            g->plans.push_back(std::move(p));
         }
-        Group &g = *groups[it->second];
-        where.push_back({it->second, g.lanes.size()});
-        g.lanes.push_back(l);
+        g->lane_plan.push_back(it->second);
         sizes.push_back(s);
     }
     bool fused = !(m->options & PPOCR_OPT_NO_FUSION);
@@ -822,59 +918,54 @@ int ppocr_model_set_sizes(ppocr_model *m, const uint32_t *hw, size_t lanes) {
         m->steps_fused = fused;
     }
     m->drop_graphs();
-    for (auto &g : groups) {
-        std::string err;
-        int rc = m->build_group(*g, err);
-        if (rc) return fail(rc, err);
-    }
-    m->groups = std::move(groups);
+    std::string err;
+    int rc = m->build_group(*g, err);
+    if (rc) return fail(rc, err);
+    m->group = std::move(g);
     m->sizes = std::move(sizes);
-    m->where = std::move(where);
     return PPOCR_OK;
 }
 
 float *ppocr_model_lane_input(ppocr_model *m, size_t lane, size_t *len) {
-    if (!m || lane >= m->where.size()) {
+    if (!m || !m->group || lane >= m->group->count()) {
         fail(PPOCR_E_ARG, "no such lane");
         return nullptr;
     }
-    Group &g = *m->groups[m->where[lane].first];
-    size_t n = g.plan.h * g.plan.w * g.plan.c;
-    if (len) *len = n;
-    return static_cast<float *>(g.in_host.p) + m->where[lane].second * n;
+    const Group &g = *m->group;
+    const Plan &p = g.lane(lane);
+    if (len) *len = p.h * p.w * p.c;
+    return static_cast<float *>(g.in_host.p) + g.in_off[lane];
 }
 
 const float *ppocr_model_lane_output(const ppocr_model *m, size_t lane, size_t index, size_t *len) {
-    if (!m || lane >= m->where.size() || index >= m->plan.outputs.size()) {
+    if (!m || !m->group || lane >= m->group->count() || index >= m->plan.outputs.size()) {
         fail(PPOCR_E_ARG, "no such lane or output");
         return nullptr;
     }
-    const Group &g = *m->groups[m->where[lane].first];
-    size_t n = g.plan.out_n[index];
-    if (len) *len = n;
-    return static_cast<const float *>(g.out_host[index]->p) + m->where[lane].second * n;
+    const Group &g = *m->group;
+    if (len) *len = g.lane(lane).out_n[index];
+    return static_cast<const float *>(g.out_host[index]->p) + g.out_off[index][lane];
 }
 
 float *ppocr_model_lane_device_input(ppocr_model *m, size_t lane, size_t *len) {
-    if (!m || lane >= m->where.size()) {
+    if (!m || !m->group || lane >= m->group->count()) {
         fail(PPOCR_E_ARG, "no such lane");
         return nullptr;
     }
-    Group &g = *m->groups[m->where[lane].first];
-    size_t n = g.plan.h * g.plan.w * g.plan.c;
-    if (len) *len = n;
-    return g.slot_ptr(g.plan.slot) + m->where[lane].second * n;
+    const Group &g = *m->group;
+    const Plan &p = g.lane(lane);
+    if (len) *len = p.h * p.w * p.c;
+    return g.slot_ptr(g.input_slot) + g.in_off[lane];
 }
 
 const float *ppocr_model_lane_device_output(const ppocr_model *m, size_t lane, size_t index, size_t *len) {
-    if (!m || lane >= m->where.size() || index >= m->plan.outputs.size()) {
+    if (!m || !m->group || lane >= m->group->count() || index >= m->plan.outputs.size()) {
         fail(PPOCR_E_ARG, "no such lane or output");
         return nullptr;
     }
-    const Group &g = *m->groups[m->where[lane].first];
-    size_t n = g.plan.out_n[index];
-    if (len) *len = n;
-    return g.slot_ptr(g.plan.outputs[index]) + m->where[lane].second * n;
+    const Group &g = *m->group;
+    if (len) *len = g.lane(lane).out_n[index];
+    return g.slot_ptr(g.output_slots[index]) + g.out_off[index][lane];
 }
 
 int ppocr_model_enqueue(ppocr_model *m) {

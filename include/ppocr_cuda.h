@@ -113,6 +113,23 @@ size_t ppocr_model_launches(const ppocr_model *model);
 /* A text line describing step `i` of the fused schedule (NULL past the end). */
 const char *ppocr_model_step_name(const ppocr_model *model, size_t i);
 
+/* The CTC argmax head (plan kind ctcargmax, the recogniser's last layer)
+ * over device buffers the caller owns, for callers that may not allocate
+ * device memory: hosts that manage a fixed device-memory budget themselves,
+ * or loops that must not stall on cudaMalloc / cudaFree, which can
+ * synchronize the device. No counterpart in the reference (its engine always
+ * allocates per model). x: [pixels][ci] time steps; w: ceil(vocab/16) panels
+ * of [ci][16]; b: 16 * ceil(vocab/16) biases (-1e30 past vocab); y:
+ * [pixels][2] = (best class as float, 1 / sum of exp). Enqueued on `stream`
+ * (a cudaStream_t; NULL is the default stream) on the current device.
+ * Allocates nothing: its scratch is a fixed 4 MiB array in the library's
+ * device memory (3 floats per time step per 256 classes, 1 Mi floats in
+ * all); larger calls return PPOCR_E_SIZE. The first call on a device looks
+ * the array up, so make it before any stream capture. All calls on a device
+ * share the array: calls that overlap on the GPU race. */
+int ppocr_ctc_argmax_noalloc(const float *x, const float *w, const float *b, float *y, size_t pixels,
+                             size_t ci, size_t vocab, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

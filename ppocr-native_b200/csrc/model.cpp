@@ -325,6 +325,11 @@ std::vector<Step> fuse(const Plan &p, bool enabled) {
 
 }  // namespace
 
+namespace ppocr {
+// The thread's last-error text, for entry points defined in other files.
+void set_last_error(const std::string &msg) { g_error = msg; }
+}  // namespace ppocr
+
 // ------------------------------------------------------------------- model
 
 // The lanes of one run, packed: every plan buffer holds the lanes' tensors

@@ -54,6 +54,9 @@ _SIG = {
     "ppocr_model_set_options": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32]),
     "ppocr_model_launches": (ctypes.c_size_t, [ctypes.c_void_p]),
     "ppocr_model_step_name": (ctypes.c_char_p, [ctypes.c_void_p, ctypes.c_size_t]),
+    "ppocr_ctc_argmax_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
+                                                ctypes.c_size_t, ctypes.c_void_p]),
 }
 
 _lib = None
@@ -215,3 +218,12 @@ class Model:
             if s is None:
                 return out
             out.append(s.decode())
+
+
+def ctc_argmax_noalloc(x: int, w: int, b: int, y: int, pixels: int, ci: int, vocab: int,
+                       stream: int | None = None) -> None:
+    """The CTC argmax head over caller-owned device buffers (device
+    pointers as ints), for callers that may not allocate device memory; see
+    `ppocr_ctc_argmax_noalloc` in include/ppocr_cuda.h for the scratch limit
+    and the sharing rules."""
+    _check(lib().ppocr_ctc_argmax_noalloc(x, w, b, y, pixels, ci, vocab, stream or None))

@@ -123,7 +123,7 @@ const char *ppocr_model_step_name(const ppocr_model *model, size_t i);
  * [pixels][2] = (best class as float, 1 / sum of exp). Enqueued on `stream`
  * (a cudaStream_t; NULL is the default stream) on the current device.
  * Allocates nothing: its scratch is a fixed 4 MiB array in the library's
- * device memory (3 floats per time step per 256 classes, 1 Mi floats in
+ * device memory (3 floats per time step per 128 classes, 1 Mi floats in
  * all); larger calls return PPOCR_E_SIZE. The first call on a device looks
  * the array up, so make it before any stream capture. All calls on a device
  * share the array: calls that overlap on the GPU race. */

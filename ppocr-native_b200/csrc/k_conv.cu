@@ -4,17 +4,20 @@
 // K = kh*kw*C with k = (ky*kw + kx)*C + c, the order of the weights
 // `[kh][kw][C][oc]` and of the reference's sums (`kernels/dense.rs:20-36`).
 // A block owns a BM x BN output tile; its threads hold TM x TN accumulators
-// each. K advances one (tap, BK-channel slice) tile at a time, staged through
-// double-buffered shared memory with the next tile prefetched into registers.
-// Every accumulator adds its k terms in increasing k with one fused
-// multiply-add each, starting from the bias or from zero as the reference's
-// tiles do, so each output carries the reference's bits.
+// each. K advances one (tap, BK-channel slice) tile at a time through
+// double-buffered shared memory, the next tile prefetched into registers
+// while the current one is multiplied. Every accumulator adds its k terms in
+// increasing k with one fused multiply-add each, starting from the bias or
+// from zero as the reference's tiles do, so each output carries the
+// reference's bits.
 //
 // The A tile is gathered on the fly: a padded tap reads zero, and each of up
 // to four sources is read nearest-upsampled by 2^shift in place, so the
-// neck's upsample + concat never reach memory. An SE gate (per lane and input
-// channel) multiplies A as it is loaded; a residual add and a second
-// activation run in the epilogue.
+// neck's upsample + concat never reach memory. A pointwise layer (1x1, unit
+// stride, no padding, one source) reads A straight from its input, whose
+// pixels are the output's. An SE gate (per lane and input channel)
+// multiplies A as it is loaded; a residual add and a second activation run in
+// the epilogue.
 #include "devmath.cuh"
 #include "kernels.hpp"
 
@@ -22,30 +25,67 @@ namespace ppocr {
 
 namespace {
 
-constexpr int BK = 8;
 constexpr int APAD = 4;
 
-template <int TM, int TN, int TX, int TY>
+template <int TM, int TN, int TX, int TY, int BK>
 struct Cfg {
     static constexpr int BM = TM * TY, BN = TN * TX, THREADS = TX * TY;
     static constexpr int AGROUPS = BM * BK / 4;  // float4 groups of the A tile
     static constexpr int ALOADS = (AGROUPS + THREADS - 1) / THREADS;
-    static constexpr int BELEMS = BK * BN;
-    static constexpr int BLOADS = (BELEMS + THREADS - 1) / THREADS;
+    static constexpr int BGROUPS = BK * BN / 4;  // float4 groups of the B tile (BN % 4 == 0)
+    static constexpr int BLOADS = (BGROUPS + THREADS - 1) / THREADS;
+    static constexpr size_t SMEM = sizeof(float) * (2 * BK * (BM + APAD) + 2 * BK * BN);
 };
 
-// Pixel coordinates of one A-load slot, fixed for the whole K loop: its
-// lane, the lane's input size, and the top-left input tap.
+// One A-load slot, fixed for the whole K loop: its lane, the lane's input
+// size and the top-left input tap (windowed), or its pixel (pointwise). The
+// block keeps one per tile pixel in shared memory (`meta`) rather than each
+// thread in registers.
 struct Pixel {
+    long m;
     int n, iy0, ix0, ih, iw;
     bool ok;
 };
 
-__device__ __forceinline__ void load_a_group(const ConvArgs &a, const Pixel &px, int tap, int c, bool vec4,
+// Shared form of a Pixel: {lane, iy0, ix0, ih << 16 | iw}; ih 0 marks a
+// pixel past the end.
+__device__ __forceinline__ Pixel unpack(int4 md, long m) {
+    Pixel p;
+    p.m = m;
+    p.n = md.x;
+    p.iy0 = md.y;
+    p.ix0 = md.z;
+    p.ih = md.w >> 16;
+    p.iw = md.w & 0xffff;
+    p.ok = p.ih != 0;
+    return p;
+}
+
+// Four channels c..c+3 of A for one slot at tap (ky, kx).
+template <bool PW>
+__device__ __forceinline__ void load_a_group(const ConvArgs &a, const Pixel &px, int ky, int kx, int c, bool vec4,
                                              float v[4]) {
     v[0] = v[1] = v[2] = v[3] = 0.0f;
     if (!px.ok) return;
-    int ky = tap / a.kw, kx = tap - ky * a.kw;
+    if (PW) {
+        // pointwise: the input pixel is the output pixel, one source
+        if (vec4) {
+            if (c >= a.C) return;
+            float4 q = __ldg(reinterpret_cast<const float4 *>(a.src[0].p + px.m * a.C + c));
+            v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                if (c + e < a.C) v[e] = __ldg(a.src[0].p + px.m * a.C + c + e);
+        }
+        if (a.gate) {
+            const float *g = a.gate + (long)px.n * a.C + c;
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                if (c + e < a.C) v[e] = fmul(v[e], __ldg(g + e));
+        }
+        return;
+    }
     int iy = px.iy0 + ky, ix = px.ix0 + kx;
     if (iy < 0 || iy >= px.ih || ix < 0 || ix >= px.iw) return;
     const LaneInfo &L = a.lanes[px.n];
@@ -83,13 +123,17 @@ __device__ __forceinline__ void load_a_group(const ConvArgs &a, const Pixel &px,
     }
 }
 
-template <int TM, int TN, int TX, int TY>
-__global__ void __launch_bounds__(TX *TY) conv_gemm(const ConvArgs a, int ctiles, int ntiles_k, bool vec4,
+// At most 128 registers a thread, so that two 256-thread (or four
+// 128-thread) blocks share an SM.
+template <int TM, int TN, int TX, int TY, int BK, bool PW>
+__global__ void __launch_bounds__(TX *TY, 65536 / (TX * TY * 128)) conv_gemm(const ConvArgs a, int ctiles, int ntiles_k, bool vec4,
                                                     bool bvec4) {
-    using C = Cfg<TM, TN, TX, TY>;
+    using C = Cfg<TM, TN, TX, TY, BK>;
     constexpr int BM = C::BM, BN = C::BN;
-    __shared__ __align__(16) float As[2][BK][BM + APAD];
-    __shared__ __align__(16) float Bs[2][BK][BN];
+    extern __shared__ __align__(16) float smem[];
+    float *As = smem;                          // [2][BK][BM + APAD]
+    float *Bs = smem + 2 * BK * (BM + APAD);   // [2][BK][BN]
+    __shared__ int4 meta[BM];
 
     const int tid = threadIdx.x;
     const int tx = tid % TX, ty = tid / TX;
@@ -97,94 +141,83 @@ __global__ void __launch_bounds__(TX *TY) conv_gemm(const ConvArgs a, int ctiles
     const long m0 = (long)blockIdx.x * BM;
     const int n0 = blockIdx.y * BN;
 
-    // A-load slots of this thread.
-    Pixel px[C::ALOADS];
-    int am[C::ALOADS], aq[C::ALOADS];
-#pragma unroll
-    for (int l = 0; l < C::ALOADS; l++) {
-        int g = tid + l * C::THREADS;
-        am[l] = g / (BK / 4);
-        aq[l] = g % (BK / 4);
-        long m = m0 + am[l];
-        px[l].ok = g < C::AGROUPS && m < M;
-        if (px[l].ok) {
-            int n = find_lane(a.lanes, a.nl, m);
-            const LaneInfo &L = a.lanes[n];
-            int ow = __ldg(&L.ow);
-            int r = int(m - __ldg(&L.pix0));
-            int oy = r / ow, ox = r - oy * ow;
-            px[l].n = n;
-            px[l].ih = __ldg(&L.ih);
-            px[l].iw = __ldg(&L.iw);
-            px[l].iy0 = oy * a.sh - a.pt;
-            px[l].ix0 = ox * a.sw - a.pl;
-        } else {
-            px[l].n = px[l].iy0 = px[l].ix0 = px[l].ih = px[l].iw = 0;
-        }
-    }
-
-    float ra[C::ALOADS][4];
-    float rb[C::BLOADS];
-
-    auto fetch = [&](int t) {
-        int tap = t / ctiles;
-        int c0 = (t - tap * ctiles) * BK;
-#pragma unroll
-        for (int l = 0; l < C::ALOADS; l++) load_a_group(a, px[l], tap, c0 + aq[l] * 4, vec4, ra[l]);
-        if (bvec4) {
-#pragma unroll
-            for (int l = 0; l < C::BLOADS; l += 4) {
-                int e = (tid + (l / 4) * C::THREADS) * 4;
-                if (l < C::BLOADS) {
-                    int kk = e / BN, nn = e - kk * BN;
-                    int c = c0 + kk, n = n0 + nn;
-                    float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (e < C::BELEMS && c < a.C && n < a.oc)
-                        q = __ldg(reinterpret_cast<const float4 *>(a.w + ((long)tap * a.C + c) * a.oc + n));
-                    rb[l] = q.x;
-                    if (l + 1 < C::BLOADS) rb[l + 1] = q.y;
-                    if (l + 2 < C::BLOADS) rb[l + 2] = q.z;
-                    if (l + 3 < C::BLOADS) rb[l + 3] = q.w;
+    // Where each pixel of the tile reads, once per block.
+    for (int p = tid; p < BM; p += C::THREADS) {
+        long m = m0 + p;
+        int4 md = make_int4(0, 0, 0, 0);
+        if (m < M) {
+            md.w = 1 << 16;  // in range (pointwise reads need no more)
+            if (!PW || a.gate) {
+                int n = find_lane(a.lanes, a.nl, m);
+                md.x = n;
+                if (!PW) {
+                    const LaneInfo &L = a.lanes[n];
+                    int ow = __ldg(&L.ow);
+                    int r = int(m - __ldg(&L.pix0));
+                    int oy = r / ow, ox = r - oy * ow;
+                    md.y = oy * a.sh - a.pt;
+                    md.z = ox * a.sw - a.pl;
+                    md.w = (__ldg(&L.ih) << 16) | __ldg(&L.iw);
                 }
             }
-        } else {
-#pragma unroll
-            for (int l = 0; l < C::BLOADS; l++) {
-                int e = tid + l * C::THREADS;
-                int kk = e / BN, nn = e - kk * BN;
-                int c = c0 + kk, n = n0 + nn;
-                rb[l] = (e < C::BELEMS && c < a.C && n < a.oc) ? __ldg(a.w + ((long)tap * a.C + c) * a.oc + n) : 0.0f;
-            }
         }
-    };
-    auto stash = [&](int buf) {
+        meta[p] = md;
+    }
+    __syncthreads();
+
+    float ra[C::ALOADS][4];
+    float4 rb[C::BLOADS];
+
+    auto fetch = [&](int t) {
+        int tap = PW ? 0 : t / ctiles;
+        int c0 = (t - tap * ctiles) * BK;
+        int ky = PW ? 0 : tap / a.kw;
+        int kx = PW ? 0 : tap - ky * a.kw;
 #pragma unroll
         for (int l = 0; l < C::ALOADS; l++) {
             int g = tid + l * C::THREADS;
+            int am = g / (BK / 4), aq = g % (BK / 4);
             if (g < C::AGROUPS) {
-#pragma unroll
-                for (int e = 0; e < 4; e++) As[buf][aq[l] * 4 + e][am[l]] = ra[l][e];
+                Pixel px = unpack(meta[am], m0 + am);
+                load_a_group<PW>(a, px, ky, kx, c0 + aq * 4, vec4, ra[l]);
             }
         }
-        if (bvec4) {
 #pragma unroll
-            for (int l = 0; l < C::BLOADS; l += 4) {
-                int e = (tid + (l / 4) * C::THREADS) * 4;
-                if (l < C::BLOADS && e < C::BELEMS) {
-                    int kk = e / BN, nn = e - kk * BN;
-                    float *d = &Bs[buf][kk][nn];
-                    d[0] = rb[l];
-                    if (l + 1 < C::BLOADS) d[1] = rb[l + 1];
-                    if (l + 2 < C::BLOADS) d[2] = rb[l + 2];
-                    if (l + 3 < C::BLOADS) d[3] = rb[l + 3];
+        for (int l = 0; l < C::BLOADS; l++) {
+            int g = tid + l * C::THREADS;
+            int kk = (g * 4) / BN, nn = (g * 4) - kk * BN;
+            int c = c0 + kk, n = n0 + nn;
+            float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (g < C::BGROUPS && c < a.C) {
+                const float *src = a.w + ((long)tap * a.C + c) * a.oc + n;
+                if (bvec4 && n + 3 < a.oc) {
+                    q = __ldg(reinterpret_cast<const float4 *>(src));
+                } else {
+                    if (n < a.oc) q.x = __ldg(src);
+                    if (n + 1 < a.oc) q.y = __ldg(src + 1);
+                    if (n + 2 < a.oc) q.z = __ldg(src + 2);
+                    if (n + 3 < a.oc) q.w = __ldg(src + 3);
                 }
             }
-        } else {
+            rb[l] = q;
+        }
+    };
+    auto stash = [&](int buf) {
+        float *Ab = As + buf * BK * (BM + APAD);
+        float *Bb = Bs + buf * BK * BN;
 #pragma unroll
-            for (int l = 0; l < C::BLOADS; l++) {
-                int e = tid + l * C::THREADS;
-                if (e < C::BELEMS) Bs[buf][e / BN][e % BN] = rb[l];
+        for (int l = 0; l < C::ALOADS; l++) {
+            int g = tid + l * C::THREADS;
+            int am = g / (BK / 4), aq = g % (BK / 4);
+            if (g < C::AGROUPS) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) Ab[(aq * 4 + e) * (BM + APAD) + am] = ra[l][e];
             }
+        }
+#pragma unroll
+        for (int l = 0; l < C::BLOADS; l++) {
+            int g = tid + l * C::THREADS;
+            if (g < C::BGROUPS) *reinterpret_cast<float4 *>(Bb + g * 4) = rb[l];
         }
     };
 
@@ -213,15 +246,31 @@ __global__ void __launch_bounds__(TX *TY) conv_gemm(const ConvArgs a, int ctiles
     stash(0);
     __syncthreads();
     for (int t = 0; t < ntiles_k; t++) {
-        int buf = t & 1;
+        const int buf = t & 1;
         if (t + 1 < ntiles_k) fetch(t + 1);
+        const float *Ab = As + buf * BK * (BM + APAD) + ty * TM;
+        const float *Bb = Bs + buf * BK * BN + tx * TN;
 #pragma unroll
         for (int kk = 0; kk < BK; kk++) {
             float fa[TM], fb[TN];
 #pragma unroll
-            for (int i = 0; i < TM; i++) fa[i] = As[buf][kk][ty * TM + i];
+            for (int i = 0; i < TM; i += 4) {
+                float4 q = *reinterpret_cast<const float4 *>(Ab + kk * (BM + APAD) + i);
+                fa[i] = q.x; fa[i + 1] = q.y; fa[i + 2] = q.z; fa[i + 3] = q.w;
+            }
+            if (TN % 4 == 0) {
 #pragma unroll
-            for (int j = 0; j < TN; j++) fb[j] = Bs[buf][kk][tx * TN + j];
+                for (int j = 0; j < TN; j += 4) {
+                    float4 q = *reinterpret_cast<const float4 *>(Bb + kk * BN + j);
+                    fb[j] = q.x; fb[j + 1] = q.y; fb[j + 2] = q.z; fb[j + 3] = q.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < TN; j += 2) {
+                    float2 q = *reinterpret_cast<const float2 *>(Bb + kk * BN + j);
+                    fb[j] = q.x; fb[j + 1] = q.y;
+                }
+            }
 #pragma unroll
             for (int i = 0; i < TM; i++)
 #pragma unroll
@@ -249,34 +298,71 @@ __global__ void __launch_bounds__(TX *TY) conv_gemm(const ConvArgs a, int ctiles
     }
 }
 
-template <int TM, int TN, int TX, int TY>
-int run(const ConvArgs &a, cudaStream_t s, bool vec4) {
-    using C = Cfg<TM, TN, TX, TY>;
-    long M = a.M;
+template <int TM, int TN, int TX, int TY, int BK>
+int run(const ConvArgs &a, cudaStream_t s, bool vec4, bool pw) {
+    using C = Cfg<TM, TN, TX, TY, BK>;
+    static_assert(TM % 4 == 0 && TN % 2 == 0 && C::BN % 4 == 0 && BK % 4 == 0, "tile shape");
     int ctiles = (a.C + BK - 1) / BK;
     int taps = a.kh * a.kw;
-    dim3 grid((unsigned)((M + C::BM - 1) / C::BM), (unsigned)((a.oc + C::BN - 1) / C::BN));
-    bool bvec4 = (a.oc % 4 == 0) && (C::BN % 4 == 0) && (C::BLOADS % 4 == 0) &&
-                 (C::BELEMS % (4 * C::THREADS) == 0);
-    conv_gemm<TM, TN, TX, TY><<<grid, C::THREADS, 0, s>>>(a, ctiles, taps * ctiles, vec4, bvec4);
+    dim3 grid((unsigned)((a.M + C::BM - 1) / C::BM), (unsigned)((a.oc + C::BN - 1) / C::BN));
+    bool bvec4 = a.oc % 4 == 0;
+    if (pw)
+        conv_gemm<TM, TN, TX, TY, BK, true><<<grid, C::THREADS, C::SMEM, s>>>(a, ctiles, ctiles, vec4, bvec4);
+    else
+        conv_gemm<TM, TN, TX, TY, BK, false><<<grid, C::THREADS, C::SMEM, s>>>(a, ctiles, taps * ctiles, vec4, bvec4);
     return 1;
 }
 
+template <int TM, int TN, int TX, int TY, int BK>
+void allow() {
+    using C = Cfg<TM, TN, TX, TY, BK>;
+    cudaFuncSetAttribute(conv_gemm<TM, TN, TX, TY, BK, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         int(C::SMEM));
+    cudaFuncSetAttribute(conv_gemm<TM, TN, TX, TY, BK, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         int(C::SMEM));
+}
+
+// Output pixels under which a layer is short of blocks for 148 SMs: it then
+// takes the tile with fewer pixels per block.
+constexpr long SMALL_M = 148L * 2 * 128;
+
 }  // namespace
 
+void configure_conv_kernels() {
+    allow<8, 8, 16, 16, 8>();
+    allow<4, 8, 16, 16, 16>();
+    allow<8, 6, 16, 16, 8>();
+    allow<4, 6, 16, 16, 16>();
+    allow<8, 4, 16, 16, 8>();
+    allow<8, 6, 8, 32, 8>();
+    allow<4, 6, 8, 32, 16>();
+    allow<8, 6, 4, 32, 8>();
+    allow<4, 6, 4, 32, 16>();
+    allow<4, 4, 4, 64, 16>();
+    allow<4, 2, 4, 64, 16>();
+    allow<4, 4, 8, 32, 16>();
+}
+
+// Tile per output width: the widest per-thread tiles (8 pixels) on layers
+// with enough pixels to fill the SMs, 4 pixels per thread on smaller ones;
+// K slices of 8 channels for the wide tiles, 16 for the narrow ones, which
+// keeps every variant near or under 128 registers.
 int launch_conv(const ConvArgs &a, cudaStream_t s) {
     bool vec4 = true;
     for (int i = 0; i < a.nsrc; i++) vec4 = vec4 && (a.src[i].c % 4 == 0);
+    bool pw = a.kh == 1 && a.kw == 1 && a.sh == 1 && a.sw == 1 && a.pt == 0 && a.pl == 0 && a.nsrc == 1 &&
+              a.src[0].shift == 0;
+    bool small = a.M < SMALL_M;
     int oc = a.oc;
-    if (oc % 128 == 0) return run<8, 8, 16, 16>(a, s, vec4);
-    if (oc % 96 == 0) return run<8, 6, 16, 16>(a, s, vec4);
-    if (oc % 64 == 0) return run<8, 4, 16, 16>(a, s, vec4);
-    if (oc % 48 == 0) return run<4, 6, 8, 32>(a, s, vec4);
-    if (oc % 24 == 0) return run<4, 6, 4, 64>(a, s, vec4);
-    if (oc <= 8) return run<4, 2, 4, 64>(a, s, vec4);
-    if (oc <= 16) return run<4, 4, 4, 64>(a, s, vec4);
-    if (oc <= 32) return run<4, 4, 8, 32>(a, s, vec4);
-    return run<8, 4, 16, 16>(a, s, vec4);
+    if (oc % 128 == 0) return small ? run<4, 8, 16, 16, 16>(a, s, vec4, pw) : run<8, 8, 16, 16, 8>(a, s, vec4, pw);
+    if (oc % 96 == 0) return small ? run<4, 6, 16, 16, 16>(a, s, vec4, pw) : run<8, 6, 16, 16, 8>(a, s, vec4, pw);
+    if (oc % 64 == 0) return run<8, 4, 16, 16, 8>(a, s, vec4, pw);
+    if (oc % 48 == 0) return small ? run<4, 6, 8, 32, 16>(a, s, vec4, pw) : run<8, 6, 8, 32, 8>(a, s, vec4, pw);
+    if (oc % 24 == 0) return small ? run<4, 6, 4, 32, 16>(a, s, vec4, pw) : run<8, 6, 4, 32, 8>(a, s, vec4, pw);
+    if (oc <= 8) return run<4, 2, 4, 64, 16>(a, s, vec4, pw);
+    if (oc <= 16) return run<4, 4, 4, 64, 16>(a, s, vec4, pw);
+    if (oc <= 32) return run<4, 4, 8, 32, 16>(a, s, vec4, pw);
+    return run<8, 4, 16, 16, 8>(a, s, vec4, pw);
 }
 
 }  // namespace ppocr

@@ -149,15 +149,23 @@ __global__ void __launch_bounds__(256) mean_partial_kernel(const MeanArgs a) {
     }
 }
 
-__global__ void mean_final_kernel(const MeanArgs a) {
-    int g = blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= a.nl * a.c) return;
-    int n = g / a.c, c = g - n * a.c;
-    int hw = a.lanes[n].ih * a.lanes[n].iw;
-    int chunks = mean_chunks(hw);
+// Stage 2: one block per (lane, 32 channels); 8 rows of threads sum the
+// lane's chunks strided, then their 8 partials are added in row order.
+__global__ void __launch_bounds__(256) mean_final_kernel(const MeanArgs a) {
+    __shared__ double part[8][32];
+    const int n = blockIdx.y, c = blockIdx.x * 32 + threadIdx.x % 32, row = threadIdx.x / 32;
+    const int hw = a.lanes[n].ih * a.lanes[n].iw;
+    const int chunks = mean_chunks(hw);
     double s = 0.0;
-    for (int k = 0; k < chunks; k++) s += a.partial[((long)n * a.chunks + k) * a.c + c];
-    a.y[g] = (float)(s / (double)hw);
+    if (c < a.c)
+        for (int k = row; k < chunks; k += 8) s += a.partial[((long)n * a.chunks + k) * a.c + c];
+    part[row][threadIdx.x % 32] = s;
+    __syncthreads();
+    if (row == 0 && c < a.c) {
+        double total = 0.0;
+        for (int r = 0; r < 8; r++) total += part[r][threadIdx.x];
+        a.y[(long)n * a.c + c] = (float)(total / (double)hw);
+    }
 }
 
 // --------------------------------------------------------------- layernorm
@@ -198,11 +206,12 @@ __global__ void __launch_bounds__(128) layernorm_kernel(const LayerNormArgs a) {
 // probability e * (1 / sum); the output sum of v * p over the keys in order.
 // Scores and exponentials are recomputed per pass instead of stored: the
 // same operations give the same bits.
+template <int HD>
 __global__ void attention_kernel(const AttentionArgs a) {
     extern __shared__ float kv[];  // K [t][hd], V [t][hd]
     const int n = blockIdx.x / a.heads, h = blockIdx.x % a.heads;
     const LaneInfo &L = a.lanes[n];
-    const int hd = a.c / a.heads, t = L.iw, c = a.c;
+    const int hd = HD > 0 ? HD : a.c / a.heads, t = L.iw, c = a.c;
     float *K = kv, *V = kv + t * hd;
     const float *x = a.x + L.ipix0 * 3 * c;
     for (int i = threadIdx.x; i < t * hd; i += blockDim.x) {
@@ -212,13 +221,18 @@ __global__ void attention_kernel(const AttentionArgs a) {
     }
     __syncthreads();
     const float scale = a.scale[0];
-    constexpr int MAXHD = 64;
+    constexpr int MAXHD = HD > 0 ? HD : 64;
     for (int s = threadIdx.x; s < t; s += blockDim.x) {
         float q[MAXHD];
-        for (int d = 0; d < hd; d++) q[d] = fmul(x[(long)s * 3 * c + h * hd + d], scale);
+#pragma unroll
+        for (int d = 0; d < MAXHD; d++)
+            if (d < hd) q[d] = fmul(x[(long)s * 3 * c + h * hd + d], scale);
         auto score = [&](int j) {
             float acc = 0.0f;
-            for (int d = 0; d < hd; d++) acc = ffma(K[j * hd + d], q[d], acc);
+            const float *k = K + j * hd;
+#pragma unroll
+            for (int d = 0; d < MAXHD; d++)
+                if (d < hd) acc = ffma(k[d], q[d], acc);
             return acc;
         };
         float mx = -FLT_MAX;
@@ -230,81 +244,101 @@ __global__ void attention_kernel(const AttentionArgs a) {
         }
         const int body = t / 8 * 8;
         float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int j = 0; j < body; j++) lanes[j % 8] = fadd(lanes[j % 8], exp_neg(fsub(score(j), mx)));
+        for (int j0 = 0; j0 < body; j0 += 8)
+#pragma unroll
+            for (int l = 0; l < 8; l++) lanes[l] = fadd(lanes[l], exp_neg(fsub(score(j0 + l), mx)));
         float sum = 0.0f;
+#pragma unroll
         for (int l = 0; l < 8; l++) sum = fadd(sum, lanes[l]);
         for (int j = body; j < t; j++) sum = fadd(sum, exp_neg(fsub(score(j), mx)));
         float r = fdiv(1.0f, sum);
         float out[MAXHD];
-        for (int d = 0; d < hd; d++) out[d] = 0.0f;
+#pragma unroll
+        for (int d = 0; d < MAXHD; d++) out[d] = 0.0f;
         for (int j = 0; j < t; j++) {
             float p = fmul(exp_neg(fsub(score(j), mx)), r);
-            for (int d = 0; d < hd; d++) out[d] = ffma(V[j * hd + d], p, out[d]);
+            const float *v = V + j * hd;
+#pragma unroll
+            for (int d = 0; d < MAXHD; d++)
+                if (d < hd) out[d] = ffma(v[d], p, out[d]);
         }
         float *y = a.y + (L.pix0 + s) * c + h * hd;
-        for (int d = 0; d < hd; d++) y[d] = out[d];
+#pragma unroll
+        for (int d = 0; d < MAXHD; d++)
+            if (d < hd) y[d] = out[d];
     }
 }
 
 // --------------------------------------------------------------------- ctc
 
-constexpr int CTC_PX = 32;    // pixels per block
-constexpr int CTC_COLS = 256; // columns (16 panels) per block
+constexpr int CTC_PX = 64;     // pixels (time steps) per block
+constexpr int CTC_COLS = 128;  // columns (8 panels) per block
 constexpr int CTC_THREADS = 256;
+constexpr int CTC_TP = 4;      // pixels per thread
+constexpr int CTC_TC = 8;      // columns per thread (two runs of 4)
 
-// Logits of CTC_PX pixels x CTC_COLS columns: each starts from its bias and
-// adds the inputs in order (layers.rs:771-777), so they carry the
-// reference's bits. Each thread holds 4 pixels x 8 columns; the block then
-// reduces its columns per pixel to (max, sum exp(logit - max), first column
-// reaching max). The reference runs one online softmax per pixel over all
-// panels in order; merging per-block states instead changes only the
-// rounding of the sum (argmax and maximum are exact).
+// Logits of CTC_PX pixels x CTC_COLS columns as a GEMM tile: the block's
+// inputs [ci][CTC_PX] and weight panels [ci][CTC_COLS] sit in shared memory,
+// each thread holds 4 pixels x 8 columns. Every logit starts from its bias
+// and adds the inputs in order (layers.rs:771-777), so it carries the
+// reference's bits. The block then reduces its columns per pixel to (max,
+// sum exp(logit - max), first column reaching max) with warp shuffles. The
+// reference runs one online softmax per pixel over all panels in order;
+// merging per-block states instead changes only the rounding of the sum
+// (argmax and maximum are exact).
 __global__ void __launch_bounds__(CTC_THREADS) ctc_logits_kernel(const CtcArgs a) {
-    extern __shared__ float sm[];
-    float *xs = sm;                         // [ci][CTC_PX]
-    __shared__ float red_m[CTC_PX][32], red_s[CTC_PX][32];
-    __shared__ int red_b[CTC_PX][32];
+    extern __shared__ __align__(16) float sm[];
+    float *xs = sm;                       // [ci][CTC_PX]
+    float *ws = sm + a.ci * CTC_PX;       // [ci][CTC_COLS]
     const int p0 = blockIdx.x * CTC_PX, cb = blockIdx.y;
     const int col0 = cb * CTC_COLS;
     for (int i = threadIdx.x; i < a.ci * CTC_PX; i += CTC_THREADS) {
-        int k = i / CTC_PX, p = i - k * CTC_PX;
-        xs[i] = p0 + p < a.pixels ? a.x[(long)(p0 + p) * a.ci + k] : 0.0f;
+        int p = i / a.ci, k = i - p * a.ci;  // coalesced over k
+        xs[k * CTC_PX + p] = p0 + p < a.pixels ? __ldg(a.x + (long)(p0 + p) * a.ci + k) : 0.0f;
+    }
+    // Panels j = col / 16 hold [ci][16] contiguous floats each.
+    for (int i = threadIdx.x; i < a.ci * CTC_COLS / 4; i += CTC_THREADS) {
+        int e = i * 4;
+        int panel = e / (a.ci * 16), r = e - panel * a.ci * 16;
+        int k = r / 16, c16 = r - k * 16;
+        int col = col0 + panel * 16 + c16;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (col < a.cols)
+            v = __ldg(reinterpret_cast<const float4 *>(a.w + ((long)(col >> 4) * a.ci + k) * 16 + c16));
+        *reinterpret_cast<float4 *>(ws + k * CTC_COLS + panel * 16 + c16) = v;
     }
     __syncthreads();
-    const int tc = threadIdx.x % 32, tp = threadIdx.x / 32;  // 32 column groups x 8 pixel groups
-    float acc[4][8];
-    int cols[8];
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;  // 16 column groups x 16 pixel groups
+    // Columns of this thread: 4 at tx*4 and 4 at 64 + tx*4, so a half-warp
+    // reads 256 contiguous bytes of each weight row.
+    int cols[CTC_TC];
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        // column group tc holds columns tc*4 .. +4 of the first and of the
-        // second 128-column half, so a warp reads 512 contiguous bytes.
-        int col = col0 + (j < 4 ? tc * 4 + j : 128 + tc * 4 + (j - 4));
-        cols[j] = col;
-        float b = col < a.cols ? a.b[col] : -FLT_MAX;
+    for (int j = 0; j < CTC_TC; j++) cols[j] = col0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+    float acc[CTC_TP][CTC_TC];
 #pragma unroll
-        for (int i = 0; i < 4; i++) acc[i][j] = b;
+    for (int j = 0; j < CTC_TC; j++) {
+        float b = cols[j] < a.cols ? __ldg(a.b + cols[j]) : -FLT_MAX;
+#pragma unroll
+        for (int i = 0; i < CTC_TP; i++) acc[i][j] = b;
     }
     for (int k = 0; k < a.ci; k++) {
-        float w[8];
+        float4 xv = *reinterpret_cast<const float4 *>(xs + k * CTC_PX + ty * CTC_TP);
+        float4 w0 = *reinterpret_cast<const float4 *>(ws + k * CTC_COLS + tx * 4);
+        float4 w1 = *reinterpret_cast<const float4 *>(ws + k * CTC_COLS + 64 + tx * 4);
+        float x4[4] = {xv.x, xv.y, xv.z, xv.w};
+        float w8[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            int col = cols[j];
-            w[j] = col < a.cols ? __ldg(a.w + ((long)(col >> 4) * a.ci + k) * 16 + (col & 15)) : 0.0f;
-        }
+        for (int i = 0; i < CTC_TP; i++)
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float xv = xs[k * CTC_PX + tp * 4 + i];
-#pragma unroll
-            for (int j = 0; j < 8; j++) acc[i][j] = ffma(w[j], xv, acc[i][j]);
-        }
+            for (int j = 0; j < CTC_TC; j++) acc[i][j] = ffma(w8[j], x4[i], acc[i][j]);
     }
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        int p = p0 + tp * 4 + i;
+    for (int i = 0; i < CTC_TP; i++) {
+        const int p = p0 + ty * CTC_TP + i;
         float m = -FLT_MAX;
         int best = 0x7fffffff;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
+        for (int j = 0; j < CTC_TC; j++) {
             bool live = cols[j] < a.vocab;
             float v = acc[i][j];
             if (live && (v > m || (v == m && cols[j] < best))) { m = v; best = cols[j]; }
@@ -312,25 +346,23 @@ __global__ void __launch_bounds__(CTC_THREADS) ctc_logits_kernel(const CtcArgs a
         }
         float s = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 8; j++)
+        for (int j = 0; j < CTC_TC; j++)
             if (cols[j] < a.vocab) s = fadd(s, exp_neg(fsub(acc[i][j], m)));
-        red_m[tp * 4 + i][tc] = m;
-        red_s[tp * 4 + i][tc] = s;
-        red_b[tp * 4 + i][tc] = best;
-    }
-    __syncthreads();
-    if (threadIdx.x < CTC_PX) {
-        int pl = threadIdx.x, p = p0 + pl;
-        float m = -FLT_MAX;
-        int best = 0x7fffffff;
-        for (int g = 0; g < 32; g++) {
-            float v = red_m[pl][g];
-            if (v > m || (v == m && red_b[pl][g] < best)) { m = v; best = red_b[pl][g]; }
+        // Combine the 16 column groups of this pixel (lanes of a half-warp).
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) {
+            float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+            float s2 = __shfl_xor_sync(0xffffffffu, s, off);
+            int b2 = __shfl_xor_sync(0xffffffffu, best, off);
+            float mm = m2 > m ? m2 : m;
+            float sa = m > -FLT_MAX ? fmul(s, exp_neg(fsub(m, mm))) : 0.0f;
+            float sb = m2 > -FLT_MAX ? fmul(s2, exp_neg(fsub(m2, mm))) : 0.0f;
+            // a fixed order for the pair, whichever lane computes it
+            s = (tx & off) ? fadd(sb, sa) : fadd(sa, sb);
+            best = (m2 > m || (m2 == m && b2 < best)) ? b2 : best;
+            m = mm;
         }
-        float s = 0.0f;
-        for (int g = 0; g < 32; g++)
-            if (red_m[pl][g] > -FLT_MAX) s = fadd(s, fmul(red_s[pl][g], exp_neg(fsub(red_m[pl][g], m))));
-        if (p < a.pixels) {
+        if (tx == 0 && p < a.pixels) {
             float *st = a.partial + ((long)p * a.col_blocks + cb) * 3;
             st[0] = m;
             st[1] = s;
@@ -434,7 +466,7 @@ int launch_mean(const MeanArgs &a, cudaStream_t s) {
     int rows = a.c <= threads ? threads / a.c : 0;
     size_t smem = rows ? sizeof(double) * rows * a.c : 0;
     mean_partial_kernel<<<dim3(a.chunks, a.nl), threads, smem, s>>>(a);
-    mean_final_kernel<<<(a.nl * a.c + 255) / 256, 256, 0, s>>>(a);
+    mean_final_kernel<<<dim3((a.c + 31) / 32, a.nl), 256, 0, s>>>(a);
     return 2;
 }
 
@@ -452,15 +484,25 @@ int launch_attention(const AttentionArgs &a, cudaStream_t s) {
     int hd = a.c / a.heads;
     size_t smem = sizeof(float) * 2 * a.tmax * hd;
     int threads = a.tmax < 32 ? 32 : (a.tmax > 256 ? 256 : (a.tmax + 31) / 32 * 32);
-    attention_kernel<<<a.nl * a.heads, threads, smem, s>>>(a);
+    if (hd == 15)  // PP-OCRv6's 8 heads of 15 (tools/export_ocr.py:654)
+        attention_kernel<15><<<a.nl * a.heads, threads, smem, s>>>(a);
+    else
+        attention_kernel<0><<<a.nl * a.heads, threads, smem, s>>>(a);
     return 1;
 }
 
 int ctc_col_blocks(int cols) { return (cols + CTC_COLS - 1) / CTC_COLS; }
 
+bool ctc_supported(int ci) { return (size_t)ci * (CTC_PX + CTC_COLS) * sizeof(float) <= 200 * 1024; }
+
+void configure_misc_kernels() {
+    cudaFuncSetAttribute(ctc_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+}
+
 int launch_ctc(const CtcArgs &a, cudaStream_t s) {
     dim3 grid((a.pixels + CTC_PX - 1) / CTC_PX, a.col_blocks);
-    ctc_logits_kernel<<<grid, CTC_THREADS, sizeof(float) * a.ci * CTC_PX, s>>>(a);
+    size_t smem = sizeof(float) * (size_t)a.ci * (CTC_PX + CTC_COLS);
+    ctc_logits_kernel<<<grid, CTC_THREADS, smem, s>>>(a);
     ctc_merge_kernel<<<(a.pixels + 127) / 128, 128, 0, s>>>(a);
     return 2;
 }

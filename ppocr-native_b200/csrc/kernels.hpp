@@ -38,6 +38,7 @@ struct LaneInfo {
     long pix0;                // first output pixel
     long ipix0;               // first input pixel
     long spix0[MAX_SOURCES];  // first pixel in each conv source / the second input
+    long tile0;               // first block of the lane (tiled kernels)
     int ih, iw, oh, ow;
 };
 
@@ -202,6 +203,18 @@ int launch_convt(const ConvTArgs &a, cudaStream_t s);
 
 // Per-device set-up (shared-memory ceilings); call with the device current.
 void configure_dw_kernels();
+void configure_conv_kernels();
+void configure_direct_kernels();
+void configure_misc_kernels();
+bool ctc_supported(int ci);
+
+// Windowed dense convolutions from a shared-memory halo (k_direct.cu): whether
+// the layer fits, its output tile (rows x cols per block), the launch over
+// `tiles` blocks (the lane table's tile0 holds each lane's first block).
+bool conv_direct_supported(const ConvArgs &a);
+int conv_direct_rows(const ConvArgs &a);
+int conv_direct_cols();
+int launch_conv_direct(const ConvArgs &a, long tiles, cudaStream_t s);
 
 // Scratch sizes (elements) the launches above need.
 // Pixel runs a lane's channel mean is split into; a lane's result depends

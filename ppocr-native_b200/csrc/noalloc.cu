@@ -42,8 +42,8 @@ using namespace ppocr;
 
 namespace {
 
-// 1 Mi floats: three floats per (time step, 256-column block), enough for
-// 4723 time steps of the 18 710-class head (a page's 44 lines) in one call.
+// 1 Mi floats: three floats per (time step, 128-column block), enough for
+// 2377 time steps of the 18 710-class head (about 23 lines of 48 x 820) per call.
 constexpr size_t NOALLOC_SCRATCH_FLOATS = size_t(1) << 20;
 
 static __device__ __align__(256) float g_ctc_scratch[NOALLOC_SCRATCH_FLOATS];
@@ -87,6 +87,10 @@ extern "C" int ppocr_ctc_argmax_noalloc(const float *x, const float *w, const fl
     }
     size_t cols = (vocab + 15) / 16 * 16;
     size_t blocks = size_t(ctc_col_blocks(int(cols)));
+    if (!ctc_supported(int(ci > (size_t(1) << 20) ? (size_t(1) << 20) : ci))) {
+        set_last_error("ppocr_ctc_argmax_noalloc: " + std::to_string(ci) + " input channels exceed this backend");
+        return PPOCR_E_SIZE;
+    }
     if (pixels > size_t(1) << 30 || ci > (size_t(1) << 20) || vocab > (size_t(1) << 24) ||
         pixels * blocks * 3 > NOALLOC_SCRATCH_FLOATS) {
         set_last_error("ppocr_ctc_argmax_noalloc: " + std::to_string(pixels) + " time steps x " +

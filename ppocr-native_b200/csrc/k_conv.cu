@@ -341,6 +341,8 @@ void configure_conv_kernels() {
     allow<4, 4, 4, 64, 16>();
     allow<4, 2, 4, 64, 16>();
     allow<4, 4, 8, 32, 16>();
+    allow<8, 6, 4, 32, 4>();
+    allow<8, 6, 8, 32, 4>();
 }
 
 // Tile per output width: the widest per-thread tiles (8 pixels) on layers
@@ -354,6 +356,9 @@ int launch_conv(const ConvArgs &a, cudaStream_t s) {
               a.src[0].shift == 0;
     bool small = a.M < SMALL_M;
     int oc = a.oc;
+    // RGB stems: three channels per tap, K slices of 4
+    if (a.C <= 4 && oc == 24) return run<8, 6, 4, 32, 4>(a, s, vec4, pw);
+    if (a.C <= 4 && oc == 48) return run<8, 6, 8, 32, 4>(a, s, vec4, pw);
     if (oc % 128 == 0) return small ? run<4, 8, 16, 16, 16>(a, s, vec4, pw) : run<8, 8, 16, 16, 8>(a, s, vec4, pw);
     if (oc % 96 == 0) return small ? run<4, 6, 16, 16, 16>(a, s, vec4, pw) : run<8, 6, 16, 16, 8>(a, s, vec4, pw);
     if (oc % 64 == 0) return run<8, 4, 16, 16, 8>(a, s, vec4, pw);

@@ -38,7 +38,6 @@ struct LaneInfo {
     long pix0;                // first output pixel
     long ipix0;               // first input pixel
     long spix0[MAX_SOURCES];  // first pixel in each conv source / the second input
-    long tile0;               // first block of the lane (tiled kernels)
     int ih, iw, oh, ow;
 };
 
@@ -204,17 +203,14 @@ int launch_convt(const ConvTArgs &a, cudaStream_t s);
 // Per-device set-up (shared-memory ceilings); call with the device current.
 void configure_dw_kernels();
 void configure_conv_kernels();
-void configure_direct_kernels();
 void configure_misc_kernels();
 bool ctc_supported(int ci);
 
-// Windowed dense convolutions from a shared-memory halo (k_direct.cu): whether
-// the layer fits, its output tile (rows x cols per block), the launch over
-// `tiles` blocks (the lane table's tile0 holds each lane's first block).
-bool conv_direct_supported(const ConvArgs &a);
-int conv_direct_rows(const ConvArgs &a);
-int conv_direct_cols();
-int launch_conv_direct(const ConvArgs &a, long tiles, cudaStream_t s);
+// Output pixels under which a depthwise layer and the pointwise one it feeds
+// run as two kernels (depthwise, then a small-tile pointwise GEMM over the
+// map, which stays in L2) rather than fused: small maps give the fused
+// kernel's 128-pixel tiles too few blocks for 148 SMs.
+constexpr long DW_PW_MIN_PIXELS = 148L * 2 * 128;
 
 // Scratch sizes (elements) the launches above need.
 // Pixel runs a lane's channel mean is split into; a lane's result depends

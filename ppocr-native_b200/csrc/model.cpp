@@ -66,7 +66,6 @@ void configure_device(int device) {
     if (done.count(device)) return;
     configure_dw_kernels();
     configure_conv_kernels();
-    configure_direct_kernels();
     configure_misc_kernels();
     done.insert(device);
 }
@@ -421,40 +420,22 @@ namespace {
 
 // The lane table of operation `i` over the group's lanes, with the source
 // shifts of a dense convolution's inputs (pixel prefix sums per source).
-std::vector<LaneInfo> lane_table(const Group &g, size_t i, const std::vector<int> &shifts, int tile_rows = 0,
-                                 int tile_cols = 0, long *tiles = nullptr) {
+std::vector<LaneInfo> lane_table(const Group &g, size_t i, const std::vector<int> &shifts) {
     std::vector<LaneInfo> t(g.count());
-    long pix = 0, ipix = 0, spix[MAX_SOURCES] = {0, 0, 0, 0}, tile = 0;
+    long pix = 0, ipix = 0, spix[MAX_SOURCES] = {0, 0, 0, 0};
     for (size_t n = 0; n < g.count(); n++) {
         const Op &op = g.lane(n).ops[i];
         LaneInfo &L = t[n];
         L.pix0 = pix;
         L.ipix0 = ipix;
-        L.tile0 = tile;
         for (int s = 0; s < MAX_SOURCES; s++) L.spix0[s] = spix[s];
         L.ih = int(op.ih); L.iw = int(op.iw); L.oh = int(op.oh); L.ow = int(op.ow);
-        if (tile_rows)
-            tile += long((op.oh + tile_rows - 1) / tile_rows) * long((op.ow + tile_cols - 1) / tile_cols);
         pix += long(op.oh * op.ow);
         ipix += long(op.ih * op.iw);
         for (size_t s = 0; s < shifts.size() && s < size_t(MAX_SOURCES); s++)
             spix[s] += long(op.ih >> shifts[s]) * long(op.iw >> shifts[s]);
     }
-    if (tiles) *tiles = tile;
     return t;
-}
-
-// The direct (halo-tile) kernel's view of a dense windowed conv step, or
-// false when that kernel does not take it.
-bool direct_probe(const Op &op, const std::vector<Step::Src> &srcs, bool gated, ConvArgs &a) {
-    if (op.kind != K_CONV || op.pointwise()) return false;
-    a = ConvArgs();
-    a.C = 0;
-    for (const Step::Src &src : srcs) a.C += int(src.c);
-    a.oc = int(op.oc);
-    a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
-    a.gate = gated ? reinterpret_cast<const float *>(1) : nullptr;
-    return conv_direct_supported(a);
 }
 
 long total_out(const Group &g, size_t i) {
@@ -553,31 +534,17 @@ int ppocr_model::build_group(Group &g, std::string &err) {
     // Lane tables of every step, in one device array.
     std::vector<LaneInfo> tables;
     std::vector<size_t> table_at(steps.size(), 0);
-    std::vector<long> direct_tiles(steps.size(), 0);  // blocks of the direct conv kernel, 0: not used
     for (size_t k = 0; k < steps.size(); k++) {
         const Step &st = steps[k];
         if (st.kind == S_SKIP) continue;
         size_t i = st.kind == S_CONV ? st.b : st.a;
         std::vector<int> shifts;
-        std::vector<Step::Src> srcs = st.srcs;
         if (st.kind == S_CONV)
             for (const Step::Src &src : st.srcs) shifts.push_back(src.shift);
-        else if (p0.ops[i].kind == K_CONV) {
-            srcs = {{p0.ops[i].x, p0.ops[i].ic, 0}};
-            if (p0.ops[i].n2) {
-                srcs.push_back({p0.ops[i].x2, p0.ops[i].n2, 0});
-                shifts = {0, 0};
-            }
-        }
+        else if (p0.ops[i].kind == K_CONV && p0.ops[i].n2)
+            shifts = {0, 0};
         table_at[k] = tables.size();
-        ConvArgs probe;
-        int rows = 0, cols = 0;
-        if ((st.kind == S_CONV || (st.kind == S_OP && p0.ops[i].kind == K_CONV)) &&
-            direct_probe(p0.ops[i], srcs, st.gated, probe)) {
-            rows = conv_direct_rows(probe);
-            cols = conv_direct_cols();
-        }
-        auto t = lane_table(g, i, shifts, rows, cols, &direct_tiles[k]);
+        auto t = lane_table(g, i, shifts);
         tables.insert(tables.end(), t.begin(), t.end());
     }
     g.lane_tables.bytes = std::max<size_t>(tables.size(), 1) * sizeof(LaneInfo);
@@ -614,7 +581,24 @@ int ppocr_model::build_group(Group &g, std::string &err) {
                 a.act3 = add.fused;
                 a.y = buf(add.y);
             }
-            g.launches.push_back([a](cudaStream_t s) { return launch_dw_pw(a, s); });
+            if (a.dw.M >= DW_PW_MIN_PIXELS) {
+                g.launches.push_back([a](cudaStream_t s) { return launch_dw_pw(a, s); });
+                continue;
+            }
+            // A small map: the depthwise layer, then the pointwise GEMM
+            // reading its output back from L2.
+            DwArgs d = a.dw;
+            d.y = buf(dw.y);
+            ConvArgs c;
+            c.src[0] = {buf(dw.y), int(dw.oc), 0};
+            c.nsrc = 1;
+            c.C = int(dw.oc);
+            c.w = a.w2; c.b = a.b2;
+            c.lanes = L; c.nl = nl; c.M = a.dw.M; c.oc = a.oc;
+            c.act = a.act2; c.bias_mode = a.bias_mode2;
+            c.res = a.res; c.act2 = a.act3;
+            c.y = a.y;
+            g.launches.push_back([d, c](cudaStream_t s) { return launch_dw(d, s) + launch_conv(c, s); });
             continue;
         }
         if (st.kind == S_CONV) {
@@ -642,11 +626,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
                 a.act2 = add.fused;
                 a.y = buf(add.y);
             }
-            long tiles = direct_tiles[k];
-            if (tiles)
-                g.launches.push_back([a, tiles](cudaStream_t s) { return launch_conv_direct(a, tiles, s); });
-            else
-                g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
+            g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
             continue;
         }
         if (st.kind == S_GATE_ADD) {
@@ -673,11 +653,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
             a.pt = int(op.pt); a.pl = int(op.pl); a.act = op.fused; a.bias_mode = bias_mode(op);
             a.y = buf(op.y);
-            long tiles = direct_tiles[k];
-            if (tiles)
-                g.launches.push_back([a, tiles](cudaStream_t s) { return launch_conv_direct(a, tiles, s); });
-            else
-                g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
+            g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
             break;
         }
         case K_DWCONV: {

@@ -44,7 +44,8 @@ enum {
 /* Bits of ppocr_model_set_options. */
 enum {
     PPOCR_OPT_NO_FUSION = 1, /* run every plan operation as its own kernel */
-    PPOCR_OPT_NO_GRAPH = 2   /* launch kernels directly instead of replaying a CUDA graph */
+    PPOCR_OPT_NO_GRAPH = 2,  /* launch kernels directly instead of replaying a CUDA graph */
+    PPOCR_OPT_NO_TENSOR_CORES = 4 /* every contraction on the FP32 cores: the reference CPU engine's bits */
 };
 
 /* Number of CUDA devices this process can use (0 when none). */

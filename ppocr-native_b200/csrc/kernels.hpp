@@ -188,6 +188,27 @@ struct ConvTArgs {
     bool bias_first2 = true;
 };
 
+// Pointwise convolution on the tensor cores (k_tc.cu), 3xTF32: weights
+// pre-split and transposed to [n][kpad] (K-major, zero-padded to 32
+// channels and to whole BN tiles of output channels).
+struct PwTcArgs {
+    const float *x = nullptr;     // [M][K]
+    const float *w_hi = nullptr;  // [ntiles * bn][kpad]
+    const float *w_lo = nullptr;
+    const float *b = nullptr;     // [N] or null
+    const float *res = nullptr;   // [M][N] or null
+    float *y = nullptr;           // [M][N]
+    long M = 0;
+    int K = 0, N = 0, kpad = 0, bn = 0, tmem_cols = 32;
+    int act = 0, act2 = 0;
+    bool kvec4 = false;
+    int *err = nullptr;           // set to nonzero when a bounded wait gave up
+};
+int launch_pw_tc(const PwTcArgs &a, cudaStream_t s);
+bool pw_tc_supported(int K, int N);
+int pw_tc_bn(int N);
+void configure_tc_kernels();
+
 // Each returns the number of kernels it launched.
 int launch_conv(const ConvArgs &a, cudaStream_t s);
 int launch_dw(const DwArgs &a, cudaStream_t s);

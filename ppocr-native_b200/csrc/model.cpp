@@ -67,6 +67,7 @@ void configure_device(int device) {
     configure_dw_kernels();
     configure_conv_kernels();
     configure_misc_kernels();
+    configure_tc_kernels();
     done.insert(device);
 }
 
@@ -97,6 +98,17 @@ struct Weights {
     int device = 0;
     DeviceBuffer arena;
     std::vector<size_t> w_at, b_at;  // per op: float offset of its blocks in the arena (or SIZE_MAX)
+    // Pointwise layers' weights for the tensor-core kernel: transposed to
+    // [n][kpad], split into tf32 halves (SIZE_MAX: none).
+    DeviceBuffer tc_arena;
+    std::vector<size_t> tc_hi_at, tc_lo_at;
+    std::vector<int> tc_kpad;
+    const float *tc_hi(size_t op) const {
+        return tc_hi_at[op] == SIZE_MAX ? nullptr : static_cast<const float *>(tc_arena.p) + tc_hi_at[op];
+    }
+    const float *tc_lo(size_t op) const {
+        return tc_lo_at[op] == SIZE_MAX ? nullptr : static_cast<const float *>(tc_arena.p) + tc_lo_at[op];
+    }
     const float *w(size_t op) const {
         return w_at[op] == SIZE_MAX ? nullptr : static_cast<const float *>(arena.p) + w_at[op];
     }
@@ -374,6 +386,9 @@ struct ppocr_model {
     cudaGraphExec_t graph_host = nullptr, graph_device = nullptr;
     size_t launches = 0;
     bool pending = false;
+    // Kernels record a nonzero code here when a bounded wait gives up
+    // (page-locked and mapped, so reading it after a run costs no copy).
+    int *err_host = nullptr, *err_dev = nullptr;
 
     ~ppocr_model() {
         if (device >= 0) cudaSetDevice(device);
@@ -385,6 +400,7 @@ struct ppocr_model {
         group.reset();
         if (done) cudaEventDestroy(done);
         if (own_stream) cudaStreamDestroy(own_stream);
+        if (err_host) cudaFreeHost(err_host);
     }
 
     void settle() {
@@ -451,6 +467,11 @@ long total_in(const Group &g, size_t i) {
 }
 
 }  // namespace
+
+// Pointwise layers with at least this many pixels go to the tensor cores
+// (when allowed); smaller ones, such as the squeeze-and-excite gates, stay
+// on the FP32 kernel.
+constexpr long TC_MIN_PIXELS = 1024;
 
 int ppocr_model::build_group(Group &g, std::string &err) {
     const Plan &p0 = g.plans[0];
@@ -561,6 +582,20 @@ int ppocr_model::build_group(Group &g, std::string &err) {
     const Weights &W = *weights;
     const int nl = int(N);
     auto buf = [&g](size_t s) { return g.slot_ptr(s); };
+    const bool tc_allowed = !(options & PPOCR_OPT_NO_TENSOR_CORES);
+    int *errp = err_dev;
+    // A pointwise conv as the tensor-core kernel's arguments, when it goes there.
+    auto tc_route = [&](size_t i, const ConvArgs &c, PwTcArgs &t) {
+        if (!tc_allowed || !W.tc_hi(i) || c.gate || c.nsrc != 1 || c.src[0].shift || c.M < TC_MIN_PIXELS ||
+            c.kh != 1 || c.kw != 1 || c.sh != 1 || c.sw != 1 || c.pt || c.pl)
+            return false;
+        t.x = c.src[0].p; t.w_hi = W.tc_hi(i); t.w_lo = W.tc_lo(i); t.b = c.b; t.res = c.res; t.y = c.y;
+        t.M = c.M; t.K = c.C; t.N = c.oc; t.kpad = W.tc_kpad[i]; t.bn = pw_tc_bn(c.oc);
+        t.tmem_cols = 32;
+        while (t.tmem_cols < t.bn) t.tmem_cols *= 2;
+        t.act = c.act; t.act2 = c.act2; t.kvec4 = c.C % 4 == 0; t.err = errp;
+        return true;
+    };
     for (size_t k = 0; k < steps.size(); k++) {
         const Step &st = steps[k];
         if (st.kind == S_SKIP) continue;
@@ -598,7 +633,11 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             c.act = a.act2; c.bias_mode = a.bias_mode2;
             c.res = a.res; c.act2 = a.act3;
             c.y = a.y;
-            g.launches.push_back([d, c](cudaStream_t s) { return launch_dw(d, s) + launch_conv(c, s); });
+            PwTcArgs t;
+            if (tc_route(st.b, c, t))
+                g.launches.push_back([d, t](cudaStream_t s) { return launch_dw(d, s) + launch_pw_tc(t, s); });
+            else
+                g.launches.push_back([d, c](cudaStream_t s) { return launch_dw(d, s) + launch_conv(c, s); });
             continue;
         }
         if (st.kind == S_CONV) {
@@ -626,7 +665,11 @@ int ppocr_model::build_group(Group &g, std::string &err) {
                 a.act2 = add.fused;
                 a.y = buf(add.y);
             }
-            g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
+            PwTcArgs t;
+            if (tc_route(st.b, a, t))
+                g.launches.push_back([t](cudaStream_t s) { return launch_pw_tc(t, s); });
+            else
+                g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
             continue;
         }
         if (st.kind == S_GATE_ADD) {
@@ -653,7 +696,11 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
             a.pt = int(op.pt); a.pl = int(op.pl); a.act = op.fused; a.bias_mode = bias_mode(op);
             a.y = buf(op.y);
-            g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
+            PwTcArgs t;
+            if (tc_route(i, a, t))
+                g.launches.push_back([t](cudaStream_t s) { return launch_pw_tc(t, s); });
+            else
+                g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
             break;
         }
         case K_DWCONV: {
@@ -776,6 +823,8 @@ int ppocr_model::record(bool copies) {
 int ppocr_model::enqueue(bool copies) {
     if (!cuda_ok(cudaSetDevice(device), "selecting the device")) return PPOCR_E_DEVICE;
     if (!group) return fail(PPOCR_E_SIZE, "the model has no lanes");
+    if (pending) settle();  // the error word belongs to one run at a time
+    if (err_host) *reinterpret_cast<volatile int *>(err_host) = 0;
     int rc;
     if (options & PPOCR_OPT_NO_GRAPH) {
         rc = record(copies);
@@ -822,8 +871,13 @@ int make_model(Plan &&plan, std::shared_ptr<Weights> weights, size_t weight_floa
     m->integrated = prop.integrated != 0;
     configure_device(device);
     if (!cuda_ok(cudaStreamCreateWithFlags(&m->own_stream, cudaStreamNonBlocking), "creating a stream") ||
-        !cuda_ok(cudaEventCreateWithFlags(&m->done, cudaEventDisableTiming), "creating an event"))
+        !cuda_ok(cudaEventCreateWithFlags(&m->done, cudaEventDisableTiming), "creating an event") ||
+        !cuda_ok(cudaHostAlloc(reinterpret_cast<void **>(&m->err_host), sizeof(int), cudaHostAllocMapped),
+                 "allocating the error word") ||
+        !cuda_ok(cudaHostGetDevicePointer(reinterpret_cast<void **>(&m->err_dev), m->err_host, 0),
+                 "mapping the error word"))
         return PPOCR_E_DEVICE;
+    *m->err_host = 0;
     m->stream = m->own_stream;
     uint32_t hw[2] = {uint32_t(m->plan.h), uint32_t(m->plan.w)};
     int rc = ppocr_model_set_sizes(m.get(), hw, 1);
@@ -876,10 +930,47 @@ int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_mode
         w->b_at.push_back(place(op.b0, op.b1));
     }
     arena.resize(std::max<size_t>(arena.size(), 1) + 64, 0.0f);
+    // Tensor-core copies of the pointwise layers' weights: W [k][n] to
+    // [n][kpad], the high tf32 half (low 13 mantissa bits cleared) and the
+    // exact remainder.
+    std::vector<float> tc;
+    for (const Op &op : plan.ops) {
+        size_t hi = SIZE_MAX, lo = SIZE_MAX;
+        int kpad = 0;
+        if (op.pointwise() && op.w1 && pw_tc_supported(int(op.ic), int(op.oc))) {
+            int K = int(op.ic), N = int(op.oc), bn = pw_tc_bn(N);
+            int rows = (N + bn - 1) / bn * bn;
+            kpad = (K + 31) / 32 * 32;
+            while (tc.size() % 64) tc.push_back(0.0f);
+            hi = tc.size();
+            lo = hi + size_t(rows) * kpad;
+            tc.resize(lo + size_t(rows) * kpad, 0.0f);
+            for (int n = 0; n < N; n++)
+                for (int k = 0; k < K; k++) {
+                    float v = values[op.w0 + size_t(k) * N + n];
+                    uint32_t u;
+                    std::memcpy(&u, &v, 4);
+                    u &= 0xFFFFE000u;
+                    float h;
+                    std::memcpy(&h, &u, 4);
+                    tc[hi + size_t(n) * kpad + k] = h;
+                    tc[lo + size_t(n) * kpad + k] = v - h;
+                }
+        }
+        w->tc_hi_at.push_back(hi);
+        w->tc_lo_at.push_back(lo);
+        w->tc_kpad.push_back(kpad);
+    }
+    tc.resize(std::max<size_t>(tc.size(), 1) + 64, 0.0f);
     int code = PPOCR_E_DEVICE;
     w->arena.bytes = arena.size() * sizeof(float);
     if (!cuda_ok(cudaMalloc(&w->arena.p, w->arena.bytes), "allocating weights", &code)) return code;
     if (!cuda_ok(cudaMemcpy(w->arena.p, arena.data(), w->arena.bytes, cudaMemcpyHostToDevice), "uploading weights"))
+        return PPOCR_E_DEVICE;
+    w->tc_arena.bytes = tc.size() * sizeof(float);
+    if (!cuda_ok(cudaMalloc(&w->tc_arena.p, w->tc_arena.bytes), "allocating weights", &code)) return code;
+    if (!cuda_ok(cudaMemcpy(w->tc_arena.p, tc.data(), w->tc_arena.bytes, cudaMemcpyHostToDevice),
+                 "uploading weights"))
         return PPOCR_E_DEVICE;
     return make_model(std::move(plan), w, values.size(), device, out);
 }
@@ -1033,6 +1124,8 @@ int ppocr_model_wait(ppocr_model *m, uint32_t timeout_ms) {
             std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
     m->pending = false;
+    if (m->err_host && *reinterpret_cast<volatile int *>(m->err_host))
+        return fail(PPOCR_E_DEVICE, "a tensor-core kernel gave up waiting for its MMAs (bounded wait expired)");
     return PPOCR_OK;
 }
 
@@ -1059,7 +1152,7 @@ int ppocr_model_set_options(ppocr_model *m, uint32_t options) {
     g_error.clear();
     if (!m) return fail(PPOCR_E_ARG, "null model");
     if (options == m->options) return PPOCR_OK;
-    bool refuse = (options ^ m->options) & PPOCR_OPT_NO_FUSION;
+    bool refuse = (options ^ m->options) & (PPOCR_OPT_NO_FUSION | PPOCR_OPT_NO_TENSOR_CORES);
     m->options = options;
     m->drop_graphs();
     if (refuse && !m->sizes.empty()) {

@@ -275,31 +275,39 @@ def test_line_model(cuda_mod, oracle_mod, width):
 
 @pytest.mark.parametrize("std", [None, 0.02], ids=["busy", "baseline-init"])
 def test_detector_960x736(cuda_mod, oracle_mod, std):
-    """Benchmark config 2: probabilities within 1e-4 (and bit-identical)."""
+    """Benchmark config 2: probabilities within 1e-4 with the pointwise
+    layers on the tensor cores (3xTF32), bit-identical with every
+    contraction on the FP32 cores."""
     plan = synth.det_plan(seed=3, std=std)
     x = np.random.default_rng(4).normal(0, 1, 960 * 736 * 3).astype(np.float32)
+    want = oracle_run(oracle_mod, plan, x)[0]
     got, steps = gpu_run(cuda_mod, plan, x)
     assert "dw+pw" in steps and "gate_add" in steps and any("sources" in s for s in steps)
-    want = oracle_run(oracle_mod, plan, x)[0]
+    check(got[0], want, exact=False)
+    got, _ = gpu_run(cuda_mod, plan, x, options=cuda_mod.OPT_NO_TENSOR_CORES)
     check(got[0], want)
 
 
 def test_detector_unfused_matches_fused(cuda_mod):
     plan = synth.det_plan(seed=5, std=None, size=(320, 256))
     x = synth.stripes(320, 256)
-    fused, _ = gpu_run(cuda_mod, plan, x)
-    plain, steps = gpu_run(cuda_mod, plan, x, options=cuda_mod.OPT_NO_FUSION | cuda_mod.OPT_NO_GRAPH)
+    fp32 = cuda_mod.OPT_NO_TENSOR_CORES
+    fused, _ = gpu_run(cuda_mod, plan, x, options=fp32)
+    plain, steps = gpu_run(cuda_mod, plan, x, options=fp32 | cuda_mod.OPT_NO_FUSION | cuda_mod.OPT_NO_GRAPH)
     assert "dw+pw" not in steps
     assert np.array_equal(fused[0], plain[0])
 
 
-def test_recogniser_16_lanes(cuda_mod, oracle_mod):
+@pytest.mark.parametrize("fp32", [False, True], ids=["tensor-cores", "fp32-cores"])
+def test_recogniser_16_lanes(cuda_mod, oracle_mod, fp32):
     """Benchmark config 3: 16 lines of 48 x 320 in one batch; classes
     identical and probabilities within 1e-4 of the oracle, lane by lane."""
     plan = synth.rec_plan(seed=2, std=None)
     rng = np.random.default_rng(6)
     xs = [rng.normal(0, 1, 48 * 320 * 3).astype(np.float32) for _ in range(16)]
     with cuda_mod.Model(plan) as m:
+        if fp32:
+            m.set_options(cuda_mod.OPT_NO_TENSOR_CORES)
         m.set_sizes([(48, 320)] * 16)
         for i, x in enumerate(xs):
             m.lane_input_mut(i)[:] = x
@@ -450,3 +458,24 @@ def test_models_sharing_a_stream(cuda_mod):
         models = [a, b]
         models[first_closed].close()
         models[1 - first_closed].close()
+
+
+@pytest.mark.parametrize("k,n", [(24, 24), (48, 96), (96, 192), (192, 192), (384, 384), (120, 360), (36, 20),
+                                 (240, 120), (13, 40)])
+def test_pointwise_tensor_cores(cuda_mod, oracle_mod, k, n):
+    """A pointwise layer large enough for the tensor cores (3xTF32): within
+    a few units of the FP32 result, relative to the output's scale, and the
+    same kernel bit for bit from run to run."""
+    h, w = 37, 91  # 3367 pixels: 27 tiles of 128, the last one partial
+    x = noise(h * w * k, 3, 1.0)
+    wt = noise(k * n, 5, float(k) ** -0.5)
+    b = noise(n, 7, 0.5)
+    op = window(Op("conv", x=0, y=1, ic=k, oc=n, fused="relu", w=(0, wt.size), b=(wt.size, n)), (1, 1), 1, 0, 0)
+    plan = single(op, (h, w, k), np.concatenate([wt, b]))
+    got, _ = gpu_run(cuda_mod, plan, x)
+    again, _ = gpu_run(cuda_mod, plan, x)
+    assert np.array_equal(got[0], again[0])
+    want = oracle_run(oracle_mod, plan, x)[0]
+    assert max_gap(got[0], want) <= 2e-5 * max(1.0, float(np.abs(want).max()))
+    exact, _ = gpu_run(cuda_mod, plan, x, options=cuda_mod.OPT_NO_TENSOR_CORES)
+    check(exact[0], want)

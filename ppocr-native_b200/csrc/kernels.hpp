@@ -192,21 +192,30 @@ struct ConvTArgs {
 // pre-split and transposed to [n][kpad] (K-major, zero-padded to 32
 // channels and to whole BN tiles of output channels).
 struct PwTcArgs {
-    const float *x = nullptr;     // [M][K]
-    const float *w_hi = nullptr;  // [ntiles * bn][kpad]
-    const float *w_lo = nullptr;
+    const float *x = nullptr;     // [M][K], 16-byte aligned, K % 4 == 0
+    const float *w_hi = nullptr;  // [N][kpad]: high tf32 halves, K-major
+    const float *w_lo = nullptr;  // w_hi + N * kpad: the low halves
     const float *b = nullptr;     // [N] or null
     const float *res = nullptr;   // [M][N] or null
     float *y = nullptr;           // [M][N]
     long M = 0;
-    int K = 0, N = 0, kpad = 0, bn = 0, tmem_cols = 32;
+    int K = 0, N = 0, kpad = 0;
     int act = 0, act2 = 0;
-    bool kvec4 = false;
     int *err = nullptr;           // set to nonzero when a bounded wait gave up
+    // filled by pw_tc_prepare: output-channel slice width and count, K
+    // blocks, ring stages, TMEM columns, grid, dynamic shared memory, and
+    // the pixel and weight tensor maps (CUtensorMap, 128 bytes each)
+    int bn = 0, slices = 0, nkb = 0, ns = 0, tmem_cols = 0, grid = 0, smem = 0;
+    unsigned long long tmx[16] = {}, tmw[16] = {};
 };
 int launch_pw_tc(const PwTcArgs &a, cudaStream_t s);
+// Whether a K -> N pointwise layer fits the tensor-core kernel at all.
 bool pw_tc_supported(int K, int N);
-int pw_tc_bn(int N);
+// The padded K of the prepared weights (a multiple of 32).
+int pw_tc_kpad(int K);
+// Fills the launch shape and tensor maps; false when the layer cannot run
+// there (alignment, sizes, no driver entry point).
+bool pw_tc_prepare(PwTcArgs &a);
 void configure_tc_kernels();
 
 // Each returns the number of kernels it launched.

@@ -468,11 +468,6 @@ long total_in(const Group &g, size_t i) {
 
 }  // namespace
 
-// Pointwise layers with at least this many pixels go to the tensor cores
-// (when allowed); smaller ones, such as the squeeze-and-excite gates, stay
-// on the FP32 kernel.
-constexpr long TC_MIN_PIXELS = 1024;
-
 int ppocr_model::build_group(Group &g, std::string &err) {
     const Plan &p0 = g.plans[0];
     const size_t N = g.count();
@@ -584,17 +579,30 @@ int ppocr_model::build_group(Group &g, std::string &err) {
     auto buf = [&g](size_t s) { return g.slot_ptr(s); };
     const bool tc_allowed = !(options & PPOCR_OPT_NO_TENSOR_CORES);
     int *errp = err_dev;
-    // A pointwise conv as the tensor-core kernel's arguments, when it goes there.
+    // A pointwise conv as the tensor-core kernel's arguments, when it goes
+    // there. The choice depends on the layer alone, never on how many
+    // pixels the run holds, so a lane gives the same bits alone as
+    // alongside others.
+    // A layer that reads a channel mean (one pixel per lane, a squeeze-and-
+    // excite gate) stays on the FP32 cores: a tensor-core launch there is
+    // all set-up.
+    std::vector<char> reads_mean(p0.ops.size(), 0);
+    {
+        std::vector<int> writer(p0.pool.size(), -1);
+        for (size_t i = 0; i < p0.ops.size(); i++) {
+            const Op &op = p0.ops[i];
+            reads_mean[i] = writer[op.x] >= 0 && p0.ops[size_t(writer[op.x])].kind == K_MEAN;
+            writer[op.y] = int(i);
+        }
+    }
     auto tc_route = [&](size_t i, const ConvArgs &c, PwTcArgs &t) {
-        if (!tc_allowed || !W.tc_hi(i) || c.gate || c.nsrc != 1 || c.src[0].shift || c.M < TC_MIN_PIXELS ||
-            c.kh != 1 || c.kw != 1 || c.sh != 1 || c.sw != 1 || c.pt || c.pl)
+        if (!tc_allowed || !W.tc_hi(i) || reads_mean[i] || c.gate || c.nsrc != 1 || c.src[0].shift || c.kh != 1 ||
+            c.kw != 1 || c.sh != 1 || c.sw != 1 || c.pt || c.pl)
             return false;
         t.x = c.src[0].p; t.w_hi = W.tc_hi(i); t.w_lo = W.tc_lo(i); t.b = c.b; t.res = c.res; t.y = c.y;
-        t.M = c.M; t.K = c.C; t.N = c.oc; t.kpad = W.tc_kpad[i]; t.bn = pw_tc_bn(c.oc);
-        t.tmem_cols = 32;
-        while (t.tmem_cols < t.bn) t.tmem_cols *= 2;
-        t.act = c.act; t.act2 = c.act2; t.kvec4 = c.C % 4 == 0; t.err = errp;
-        return true;
+        t.M = c.M; t.K = c.C; t.N = c.oc; t.kpad = W.tc_kpad[i];
+        t.act = c.act; t.act2 = c.act2; t.err = errp;
+        return pw_tc_prepare(t);
     };
     for (size_t k = 0; k < steps.size(); k++) {
         const Step &st = steps[k];
@@ -616,12 +624,15 @@ int ppocr_model::build_group(Group &g, std::string &err) {
                 a.act3 = add.fused;
                 a.y = buf(add.y);
             }
-            if (a.dw.M >= DW_PW_MIN_PIXELS) {
+            // With the tensor cores the depthwise layer runs alone and the
+            // pointwise one on the tensor cores; without them, large maps take
+            // the fused FP32 kernel and small ones the two FP32 kernels (the
+            // same bits either way).
+            const bool tc_pw = tc_allowed && W.tc_hi(st.b);
+            if (!tc_pw && a.dw.M >= DW_PW_MIN_PIXELS) {
                 g.launches.push_back([a](cudaStream_t s) { return launch_dw_pw(a, s); });
                 continue;
             }
-            // A small map: the depthwise layer, then the pointwise GEMM
-            // reading its output back from L2.
             DwArgs d = a.dw;
             d.y = buf(dw.y);
             ConvArgs c;
@@ -938,13 +949,12 @@ int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_mode
         size_t hi = SIZE_MAX, lo = SIZE_MAX;
         int kpad = 0;
         if (op.pointwise() && op.w1 && pw_tc_supported(int(op.ic), int(op.oc))) {
-            int K = int(op.ic), N = int(op.oc), bn = pw_tc_bn(N);
-            int rows = (N + bn - 1) / bn * bn;
-            kpad = (K + 31) / 32 * 32;
+            int K = int(op.ic), N = int(op.oc);
+            kpad = pw_tc_kpad(K);
             while (tc.size() % 64) tc.push_back(0.0f);
             hi = tc.size();
-            lo = hi + size_t(rows) * kpad;
-            tc.resize(lo + size_t(rows) * kpad, 0.0f);
+            lo = hi + size_t(N) * kpad;
+            tc.resize(lo + size_t(N) * kpad, 0.0f);
             for (int n = 0; n < N; n++)
                 for (int k = 0; k < K; k++) {
                     float v = values[op.w0 + size_t(k) * N + n];

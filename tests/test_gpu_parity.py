@@ -52,6 +52,18 @@ def check(got, want, exact=True, tol=TOL):
         assert np.array_equal(got, want), f"max gap {gap}, {int(np.sum(got != want))} of {got.size} differ"
 
 
+def check_both(cuda, oracle_mod, plan, x, hw=None, tol=TOL, scale=1.0):
+    """The product path (pointwise layers on the tensor cores, 3xTF32)
+    within `tol` (times the output's scale), and the FP32-only path
+    bit-identical to the oracle."""
+    want = oracle_run(oracle_mod, plan, x, hw)[0]
+    got, steps = gpu_run(cuda, plan, x, hw)
+    check(got[0], want, exact=False, tol=tol * max(1.0, scale * float(np.abs(want).max())))
+    exact, _ = gpu_run(cuda, plan, x, hw, options=cuda.OPT_NO_TENSOR_CORES)
+    check(exact[0], want)
+    return steps
+
+
 # ---------------------------------------------------------------- one op each
 
 CONV_CASES = [
@@ -82,8 +94,7 @@ def test_conv(cuda_mod, oracle_mod, k, s, pads, ic, oc, fused):
     op = Op("conv", x=0, y=1, ic=ic, oc=oc, fused=fused, w=(0, wt.size), b=(wt.size, oc), kh=k, kw=k, sh=s, sw=s,
             pt=pads[0], pb=pads[1], pl=pads[2], pr=pads[3])
     plan = single(op, (h, w, ic), np.concatenate([wt, b]))
-    got, _ = gpu_run(cuda_mod, plan, x)
-    check(got[0], oracle_run(oracle_mod, plan, x)[0])
+    check_both(cuda_mod, oracle_mod, plan, x, scale=1.0)
 
 
 def test_conv_two_inputs(cuda_mod, oracle_mod):
@@ -96,8 +107,7 @@ def test_conv_two_inputs(cuda_mod, oracle_mod):
     weights = noise(at + 9 * (c1 + c2) * oc + oc, 9, 0.4)
     plan = encode((0, h, w, c1), 3, [2], [first, conv], weights)
     x = noise(h * w * c1, 1, 1.0)
-    got, _ = gpu_run(cuda_mod, plan, x)
-    check(got[0], oracle_run(oracle_mod, plan, x)[0])
+    check_both(cuda_mod, oracle_mod, plan, x)
 
 
 @pytest.mark.parametrize("k,s,c,fused", [(3, 1, 8, "swish"), (3, 2, 12, "none"), (5, 1, 16, "relu"),
@@ -132,7 +142,7 @@ def elementwise_plan(kind, h, w, c, **kw):
 def test_add(cuda_mod, oracle_mod, fused):
     plan = elementwise_plan("add", 13, 7, 12, fused=fused)
     x = noise(13 * 7 * 12, 2, 2.0)
-    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+    check_both(cuda_mod, oracle_mod, plan, x)
 
 
 def test_concat_and_upsample(cuda_mod, oracle_mod):
@@ -141,7 +151,7 @@ def test_concat_and_upsample(cuda_mod, oracle_mod):
     for cin, plan in ((c, elementwise_plan("concatc", h, w, c, prod_oc=12, oc=20, n2=12)),
                       (3, elementwise_plan("concatc", h, w, 3, prod_oc=5, oc=8, n2=5))):
         xx = noise(h * w * cin, 4, 1.0)
-        check(gpu_run(cuda_mod, plan, xx)[0][0], oracle_run(oracle_mod, plan, xx)[0])
+        check_both(cuda_mod, oracle_mod, plan, xx)
     up = Op("upsample", x=0, y=1, ic=c, oc=c, sh=2, sw=3)
     plan = single(up, (h, w, c), np.zeros(0, np.float32))
     check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
@@ -150,7 +160,7 @@ def test_concat_and_upsample(cuda_mod, oracle_mod):
     conv = window(Op("conv", x=1, y=2, ic=c, oc=c, w=(0, c * c), b=(c * c, c)), (1, 1), 1, 0, 0)
     add = Op("upsampleadd", x=0, y=3, ic=c, oc=c, x2=2, sh=2, sw=2)
     plan = encode((0, h, w, c), 4, [3], [upx, conv, add], noise(c * c + c, 6, 0.5))
-    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+    check_both(cuda_mod, oracle_mod, plan, x)
 
 
 def test_pools_mean_gates(cuda_mod, oracle_mod):
@@ -170,7 +180,7 @@ def test_pools_mean_gates(cuda_mod, oracle_mod):
     g = window(Op("conv", x=1, y=2, ic=c, oc=c, fused="hardsigmoid", w=(0, c * c), b=(c * c, c)), (1, 1), 1, 0, 0)
     cm = Op("channelmul", x=0, y=3, ic=c, oc=c, x2=2)
     plan = encode((0, h, w, c), 4, [3], [m, g, cm], noise(c * c + c, 5, 0.5))
-    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+    check_both(cuda_mod, oracle_mod, plan, x)
 
 
 def test_mean_on_a_page(cuda_mod, oracle_mod):
@@ -250,27 +260,26 @@ def test_fused_layer_config1(cuda_mod, oracle_mod):
     hardswish, fused into one kernel."""
     plan = synth.fused_layer_plan(seed=0)
     x = np.random.default_rng(1).uniform(-1, 1, 240 * 240 * 96).astype(np.float32)
-    got, steps = gpu_run(cuda_mod, plan, x)
+    steps = check_both(cuda_mod, oracle_mod, plan, x)
     assert steps == ["dw+pw"]
-    check(got[0], oracle_run(oracle_mod, plan, x)[0])
 
 
 @pytest.mark.parametrize("h,w", [(64, 48), (40, 8), (16, 16), (8, 36), (4, 4)])
 def test_page_model(cuda_mod, oracle_mod, h, w):
     plan = synth.page_model_plan(16, 16)
     x = synth.ramp_input(h * w * 3)
-    got, _ = gpu_run(cuda_mod, plan, x, hw=(h, w))
-    check(got[0], oracle_run(oracle_mod, plan, x, hw=(h, w))[0])
+    check_both(cuda_mod, oracle_mod, plan, x, hw=(h, w))
 
 
 @pytest.mark.parametrize("width", [3, 17, 40, 64, 1001])
 def test_line_model(cuda_mod, oracle_mod, width):
     plan = synth.line_model_plan(40)
     x = synth.ramp_input(2 * width * 3)
-    got = gpu_run(cuda_mod, plan, x, hw=(2, width))[0][0].reshape(-1, 2)
     want = oracle_run(oracle_mod, plan, x, hw=(2, width))[0].reshape(-1, 2)
-    assert np.array_equal(got[:, 0], want[:, 0])
-    assert max_gap(got[:, 1], want[:, 1]) <= 1e-6
+    for options in (0, cuda_mod.OPT_NO_TENSOR_CORES):
+        got = gpu_run(cuda_mod, plan, x, hw=(2, width), options=options)[0][0].reshape(-1, 2)
+        assert np.array_equal(got[:, 0], want[:, 0])
+        assert max_gap(got[:, 1], want[:, 1]) <= 1e-5
 
 
 @pytest.mark.parametrize("std", [None, 0.02], ids=["busy", "baseline-init"])
@@ -422,6 +431,7 @@ def test_device_resident_path(cuda_mod, oracle_mod):
     plan = synth.page_model_plan(32, 24)
     x = synth.ramp_input(32 * 24 * 3)
     with cuda_mod.Model(plan) as m:
+        m.set_options(cuda_mod.OPT_NO_TENSOR_CORES)
         dptr, n = m.lane_device_input(0)
         assert n == x.size
         assert rt.cudaMemcpy(dptr, x.ctypes.data, x.nbytes, 1) == 0

@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(256) mean_partial_kernel(const MeanArgs a) {
     const int t = threadIdx.x;
     const LaneInfo &L = a.lanes[n];
     const int hw = __ldg(&L.ih) * __ldg(&L.iw);
-    const int chunks = mean_chunks(hw);  // a.chunks is the most of any lane
+    const int chunks = mean_chunks(hw, a.c);  // a.chunks is the most of any lane
     if (chunk >= chunks) return;
     const int per = (hw + chunks - 1) / chunks;
     const int p0 = chunk * per, p1 = min(hw, p0 + per);
@@ -131,9 +131,20 @@ __global__ void __launch_bounds__(256) mean_partial_kernel(const MeanArgs a) {
     if (rows >= 1) {
         int row = t / a.c, c = t - row * a.c;
         double s = 0.0;
-        if (row < rows)
-            for (int p = p0 + row; p < p1; p += rows) s += (double)x[(long)p * a.c + c];
-        if (row < rows) sums[row * a.c + c] = s;
+        if (row < rows) {
+            int p = p0 + row;
+            // four independent loads in flight, added in pixel order
+            for (; p + 3 * rows < p1; p += 4 * rows) {
+                const float v0 = x[(long)p * a.c + c], v1 = x[(long)(p + rows) * a.c + c];
+                const float v2 = x[(long)(p + 2 * rows) * a.c + c], v3 = x[(long)(p + 3 * rows) * a.c + c];
+                s += (double)v0;
+                s += (double)v1;
+                s += (double)v2;
+                s += (double)v3;
+            }
+            for (; p < p1; p += rows) s += (double)x[(long)p * a.c + c];
+            sums[row * a.c + c] = s;
+        }
         __syncthreads();
         if (t < a.c) {
             double total = 0.0;
@@ -143,27 +154,36 @@ __global__ void __launch_bounds__(256) mean_partial_kernel(const MeanArgs a) {
     } else {
         for (int c = t; c < a.c; c += blockDim.x) {
             double s = 0.0;
-            for (int p = p0; p < p1; p++) s += (double)x[(long)p * a.c + c];
+            int p = p0;
+            for (; p + 3 < p1; p += 4) {
+                const float v0 = x[(long)p * a.c + c], v1 = x[(long)(p + 1) * a.c + c];
+                const float v2 = x[(long)(p + 2) * a.c + c], v3 = x[(long)(p + 3) * a.c + c];
+                s += (double)v0;
+                s += (double)v1;
+                s += (double)v2;
+                s += (double)v3;
+            }
+            for (; p < p1; p++) s += (double)x[(long)p * a.c + c];
             a.partial[((long)n * a.chunks + chunk) * a.c + c] = s;
         }
     }
 }
 
-// Stage 2: one block per (lane, 32 channels); 8 rows of threads sum the
-// lane's chunks strided, then their 8 partials are added in row order.
-__global__ void __launch_bounds__(256) mean_final_kernel(const MeanArgs a) {
-    __shared__ double part[8][32];
+// Stage 2: one block per (lane, 32 channels); 32 rows of threads sum the
+// lane's runs strided, then their 32 partials are added in row order.
+__global__ void __launch_bounds__(1024) mean_final_kernel(const MeanArgs a) {
+    __shared__ double part[32][33];
     const int n = blockIdx.y, c = blockIdx.x * 32 + threadIdx.x % 32, row = threadIdx.x / 32;
     const int hw = a.lanes[n].ih * a.lanes[n].iw;
-    const int chunks = mean_chunks(hw);
+    const int chunks = mean_chunks(hw, a.c);
     double s = 0.0;
     if (c < a.c)
-        for (int k = row; k < chunks; k += 8) s += a.partial[((long)n * a.chunks + k) * a.c + c];
+        for (int k = row; k < chunks; k += 32) s += a.partial[((long)n * a.chunks + k) * a.c + c];
     part[row][threadIdx.x % 32] = s;
     __syncthreads();
     if (row == 0 && c < a.c) {
         double total = 0.0;
-        for (int r = 0; r < 8; r++) total += part[r][threadIdx.x];
+        for (int r = 0; r < 32; r++) total += part[r][threadIdx.x];
         a.y[(long)n * a.c + c] = (float)(total / (double)hw);
     }
 }
@@ -466,7 +486,7 @@ int launch_mean(const MeanArgs &a, cudaStream_t s) {
     int rows = a.c <= threads ? threads / a.c : 0;
     size_t smem = rows ? sizeof(double) * rows * a.c : 0;
     mean_partial_kernel<<<dim3(a.chunks, a.nl), threads, smem, s>>>(a);
-    mean_final_kernel<<<dim3((a.c + 31) / 32, a.nl), 256, 0, s>>>(a);
+    mean_final_kernel<<<dim3((a.c + 31) / 32, a.nl), 1024, 0, s>>>(a);
     return 2;
 }
 

@@ -1,5 +1,7 @@
-// Pointwise (1x1) convolution on the 5th-generation tensor cores (sm_100a,
-// tcgen05) in 3xTF32: y = act2(act(x W + b) + res) over packed pixels.
+// Convolutions on the 5th-generation tensor cores (sm_100a, tcgen05) in
+// 3xTF32: y = act2(act(conv(x) + b) + res) over packed pixels, as an
+// implicit GEMM with M = output pixels, N = output channels and
+// K = kh*kw*C (k = (ky*kw + kx)*C + c, the weights' [kh][kw][C][oc] order).
 //
 // Each product is split into tf32 halves, x = xh + xl and w = wh + wl, and
 // three MMAs accumulate xh wh + xh wl + xl wh in FP32 in tensor memory, which
@@ -7,34 +9,39 @@
 // term is 2^-22 of the product). The weights arrive already split, [n][kpad]
 // (K-major), high halves then low halves; the pixels are split on chip.
 //
-// The kernel is persistent and warp-specialised. Output channels are cut
+// Both kernels are persistent and warp-specialised. Output channels are cut
 // into S slices of BN (a multiple of 32, at most 256); CTA b owns slice
-// b % S, keeps that slice's weights (all of K, both halves) resident in
-// shared memory, and walks the 128-pixel tiles q, q + Q, q + 2Q, ... with
-// q = b / S, so the S CTAs working on one tile do so at about the same time
-// and all but the first read it from L2. Per CTA:
-//   warp 0      TMA producer: the weight slice once, then each tile's K
-//               blocks (128 pixels x 32 channels, 16 KB, 128-byte swizzle)
-//               into a ring of `ns` stages;
-//   warp 1      allocates tensor memory (two accumulators of BN columns) and
-//               one thread issues the MMAs, committing each stage back to the
-//               producer and each finished tile to the epilogue;
-//   warps 2-5   split each staged block in place into its high half and a
-//               low-half twin, then release it to the MMA thread;
-//   warps 6-13  epilogue: warp w drains TMEM lanes 32(w%4)..+31 of a finished
-//               accumulator, 16 columns at a time (the two warps of a lane
-//               quadrant take alternate chunks), adds the bias, applies the
-//               activation (one instantiation per code, no branch per
-//               element), transposes through shared memory and stores rows
-//               (coalesced), adding the residual if any.
-// The epilogue of one tile overlaps the MMAs of the next (two accumulators)
-// and the producer runs up to `ns` K blocks ahead.
+// b % S and walks the 128-pixel tiles q, q + Q, q + 2Q, ... with q = b / S,
+// so the S CTAs working on one tile do so at about the same time and all but
+// the first read it from L2. K advances 32 channels (one 128-byte swizzle
+// row of f32) per stage through a ring of `ns` stages:
+//   producer    fills a stage's A block (128 pixels x 32 k, 16 KB):
+//               pw_tc_kernel (1x1 layers) with one TMA copy from the packed
+//               input, whose pixels are the output's; conv_tc_kernel gathers
+//               it with cp.async, 16 bytes (or 4 when C % 4 != 0) at a time,
+//               zero-filling padded taps and the K tail and reading each of
+//               up to four sources nearest-upsampled by 2^shift in place;
+//   converter   splits the block in place into its high half and a low-half
+//               twin (multiplying by the lane's SE gate first, if any);
+//   MMA         one thread issues the MMAs into one of two TMEM accumulators
+//               and commits each stage back to the producer and each finished
+//               tile to the epilogue;
+//   epilogue    8 warps: warp w drains TMEM lanes 32(w%4)..+31, 16 columns at
+//               a time (the two warps of a lane quadrant take alternate
+//               chunks), adds the bias, applies the activation (one
+//               instantiation per code, no branch per element), transposes
+//               through shared memory and stores rows (coalesced), adding the
+//               residual if any.
+// pw_tc_kernel keeps its slice's weights (all of K, both halves) resident in
+// shared memory; conv_tc_kernel, whose K runs to kh*kw*C, streams them with
+// the A blocks (one TMA copy per stage, from L2).
 //
-// Every wait on an mbarrier is bounded (globaltimer). A wait that runs out
-// records a code in `err` (page-locked host memory the runtime reads after
-// the run) and raises an abort flag in shared memory that ends every role's
-// loop; the producer then waits, bounded, for the copies it issued, the MMA
-// thread for its last commit, and the tensor memory is freed before return.
+// Every wait on an mbarrier is bounded (globaltimer) and sleeps in the
+// barrier rather than spinning. A wait that runs out records a code in `err`
+// (page-locked host memory the runtime reads after the run) and raises an
+// abort flag in shared memory that ends every role's loop; the producers then
+// wait, bounded, for the copies they issued, the MMA thread for its last
+// commit, and the tensor memory is freed before return.
 #include <cuda.h>
 
 #include <algorithm>
@@ -50,15 +57,15 @@ namespace ppocr {
 namespace {
 
 constexpr int TM = 128;                   // pixels per tile (MMA M, one TMEM lane each)
-constexpr int TK = 32;                    // channels per K block: one 128-byte swizzle row of f32
-constexpr int THREADS = 448;              // 14 warps
-constexpr int W_MMA = 1, W_CONV = 2, W_EPI = 6, EPI_WARPS = 8;
-constexpr int SLOT_BYTES = 2 * TM * 128;  // high half (TMA lands here) + low half
+constexpr int TK = 32;                    // k per block: one 128-byte swizzle row of f32
+constexpr int A_BYTES = TM * 128;         // one half of an A block
+constexpr int SLOT_BYTES = 2 * A_BYTES;   // high half (the copy lands here) + low half
+constexpr int EPI_WARPS = 8;
 constexpr int STAGE_FLOATS = 32 * 17;     // one epilogue warp's 32 x 16 transpose tile, padded
 constexpr int EPI_BYTES = EPI_WARPS * STAGE_FLOATS * 4 + 256 * 4;  // + the bias slice
 constexpr int MAX_NS = 6;
 // Dynamic shared memory per CTA: the block's limit (227 KB) less room for the
-// kernel's static shared memory.
+// kernels' static shared memory.
 constexpr int DYN_CEILING = 226 * 1024;
 // How long one wait on an mbarrier may take before the kernel gives up: a
 // K block's copy or MMAs take microseconds.
@@ -66,6 +73,17 @@ constexpr unsigned long long WAIT_LIMIT_NS = 200ull * 1000 * 1000;
 // A waiting thread sleeps in the mbarrier until the phase completes or this
 // many nanoseconds pass, instead of spinning on it.
 constexpr uint32_t SUSPEND_HINT_NS = 100000;
+
+// Warp roles. pw_tc_kernel: producer 0, MMA 1, converters 2-5, epilogue
+// 6-13. conv_tc_kernel: producers 0-3, MMA 4, converters 5-8, epilogue 9-16.
+struct PwRoles {
+    static constexpr int PROD_WARPS = 1, W_MMA = 1, W_CONV = 2, W_EPI = 6;
+    static constexpr int THREADS = (W_EPI + EPI_WARPS) * 32;
+};
+struct ConvRoles {
+    static constexpr int PROD_WARPS = 4, W_MMA = 4, W_CONV = 5, W_EPI = 9;
+    static constexpr int THREADS = (W_EPI + EPI_WARPS) * 32;
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -84,6 +102,11 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
     d |= uint64_t(2) << 61;
     return d;
 }
+
+// Byte offset of 16-byte chunk `c` (0..7) of row `r` in a 128B-swizzled,
+// K-major block whose rows are 128 bytes and whose base is 1024-aligned (the
+// layout TMA's 128-byte swizzle writes and the descriptor above reads).
+__device__ __forceinline__ uint32_t swz(int r, int c) { return uint32_t(r * 128 + ((c ^ (r & 7)) << 4)); }
 
 // Instruction descriptor of kind::tf32: D f32, A and B tf32, both K-major,
 // M = 128, N = n.
@@ -176,19 +199,18 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float v[32]) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+// Non-bulk asynchronous copies; `bytes` 0 writes zeros and reads nothing.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+
+// Arrives on `bar` once this thread's earlier cp.async copies have landed.
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
@@ -227,200 +249,401 @@ __device__ __forceinline__ void bias_act_stage(int act, const float v[16], const
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
-__global__ void __launch_bounds__(THREADS, 1)
-    pw_tc_kernel(const PwTcArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw) {
-    extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // 1024-byte alignment for the swizzled tiles
-    unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-    __shared__ __align__(8) uint64_t full[MAX_NS], conv[MAX_NS], empty[MAX_NS], accf[2], acce[2], bfull;
-    __shared__ uint32_t tmem_base_s;
-    __shared__ int abort_s;
+// What every role of one CTA shares.
+struct Ctx {
+    uint32_t ring;         // shared address of stage 0
+    uint32_t stage_bytes;  // one stage: the A block's two halves (+ the B block's when streamed)
+    uint32_t b_base;       // resident weights (pw_tc_kernel)
+    uint32_t b_bytes;      // one K block of one half of the weight slice: BN x 128 bytes
+    uint64_t *full, *conv, *empty, *accf, *acce;
+    volatile int *abort_flag;
+    int ns, nkb, BN, n0, Q;
+    long first, tiles;
+    uint32_t tmem;
+};
 
-    const int BN = a.bn, ns = a.ns, nkb = a.nkb, S = a.slices;
-    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-    const int Q = gridDim.x / S;
-    const long first = blockIdx.x / S;
-    const int n0 = int(blockIdx.x % S) * BN;
-    const long tiles = (a.M + TM - 1) / TM;
-    volatile int *abort_flag = &abort_s;
+// The MMA thread. The weights of K block kb sit at b_base (resident) or in
+// the stage beside the A block (streamed).
+template <bool RESIDENT>
+__device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
+    const uint32_t idesc = tf32_idesc(x.BN);
+    long it = 0, job = 0;
+    uint32_t last_bar = 0, last_parity = 0;
+    bool ok = !RESIDENT || wait_phase(smem_u32(bfull), 0, x.abort_flag, a.err);
+    for (long t = x.first; t < x.tiles && ok; t += x.Q, job++) {
+        const int buf = int(job & 1);
+        const long use = job >> 1;
+        if (use > 0 && !wait_phase(smem_u32(&x.acce[buf]), uint32_t(use - 1) & 1u, x.abort_flag, a.err)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d = x.tmem + uint32_t(buf * x.BN);
+        for (int kb = 0; kb < x.nkb; kb++, it++) {
+            const int s = int(it % x.ns);
+            const long round = it / x.ns;
+            if (!wait_phase(smem_u32(&x.conv[s]), uint32_t(round) & 1u, x.abort_flag, a.err)) {
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t ah = x.ring + uint32_t(s) * x.stage_bytes, al = ah + A_BYTES;
+            uint32_t bh, bl;
+            if (RESIDENT) {
+                bh = x.b_base + uint32_t(kb) * x.b_bytes;
+                bl = x.b_base + uint32_t(x.nkb + kb) * x.b_bytes;
+            } else {
+                bh = ah + SLOT_BYTES;
+                bl = bh + x.b_bytes;
+            }
+            // K steps of 8 tf32 (32 bytes along the swizzled rows); steps
+            // wholly past K hold zeros and are skipped
+            const int left = a.K - kb * TK;
+            const int steps = left >= TK ? TK / 8 : (left + 7) / 8;
+            for (int kk = 0; kk < steps; kk++) {
+                const uint32_t acc = (kb == 0 && kk == 0) ? 0u : 1u;
+                const uint64_t dah = sw128_desc(ah + kk * 32), dal = sw128_desc(al + kk * 32);
+                const uint64_t dbh = sw128_desc(bh + kk * 32), dbl = sw128_desc(bl + kk * 32);
+                mma_tf32(d, dah, dbh, idesc, acc);
+                mma_tf32(d, dah, dbl, idesc, 1u);
+                mma_tf32(d, dal, dbh, idesc, 1u);
+            }
+            commit(smem_u32(&x.empty[s]));
+            last_bar = smem_u32(&x.empty[s]);
+            last_parity = uint32_t(round) & 1u;
+        }
+        if (!ok) break;
+        commit(smem_u32(&x.accf[buf]));
+        last_bar = smem_u32(&x.accf[buf]);
+        last_parity = uint32_t(use) & 1u;
+    }
+    // the tensor core is done with shared memory and TMEM before the CTA
+    // frees them
+    if (last_bar) drain(last_bar, last_parity);
+}
 
-    const uint32_t ring = smem_u32(smem);
-    const uint32_t b_base = ring + uint32_t(ns) * SLOT_BYTES;
-    const uint32_t b_bytes = uint32_t(BN) * 128;  // one K block of one half
-    float *staging = reinterpret_cast<float *>(smem + size_t(ns) * SLOT_BYTES + size_t(2) * nkb * b_bytes);
-    float *bias_s = staging + EPI_WARPS * STAGE_FLOATS;  // this slice's BN biases, zero past N
+// The converters (128 threads, ct = 0..127): split each landed A block in
+// place into its high half and a low-half twin (the same swizzled layout, so
+// element for element), after the SE gate when there is one. Thread ct
+// always holds the 16-byte chunk ct & 7 of rows (ct >> 3) + 16 j, whose
+// logical chunk is the same for all j.
+__device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
+    const int lc = (ct & 7) ^ ((ct >> 3) & 7);  // logical 16-byte chunk (4 k) of every row this thread holds
+    long it = 0;
+    bool ok = true;
+    for (long t = x.first; t < x.tiles && ok; t += x.Q) {
+        int gl[8];  // the lane of each row, for the gate
+        if (a.gate)
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const long m = t * TM + (ct >> 3) + 16 * j;
+                gl[j] = m < a.M ? find_lane(a.lanes, a.nl, m) : -1;
+            }
+        for (int kb = 0; kb < x.nkb; kb++, it++) {
+            const int s = int(it % x.ns);
+            const long round = it / x.ns;
+            if (!wait_phase(smem_u32(&x.full[s]), uint32_t(round) & 1u, x.abort_flag, a.err)) {
+                ok = false;
+                break;
+            }
+            unsigned char *slot = reinterpret_cast<unsigned char *>(__cvta_shared_to_generic(x.ring)) +
+                                  size_t(s) * x.stage_bytes;
+            float4 *hi = reinterpret_cast<float4 *>(slot);
+            float4 *lo = hi + A_BYTES / 16;
+            const int k = kb * TK + lc * 4;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int i = ct + 128 * j;
+                float4 v = hi[i];
+                if (a.gate) {
+                    float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (gl[j] >= 0 && k < a.K)
+                        g = __ldg(reinterpret_cast<const float4 *>(a.gate + (long)gl[j] * a.K + k));
+                    v = make_float4(fmul(v.x, g.x), fmul(v.y, g.y), fmul(v.z, g.z), fmul(v.w, g.w));
+                }
+                const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+                hi[i] = h;
+                lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+            }
+            // make the generic-proxy stores visible to the tensor core
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            arrive(smem_u32(&x.conv[s]));
+        }
+    }
+}
 
+// The epilogue warps (e = 0..7 among them).
+__device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, int lane, float *staging,
+                              const float *bias_s) {
+    const int qd = warp & 3;  // the TMEM lane quadrant this warp may read
+    const int half = e / 4;   // which alternate 16-column chunks it takes
+    float *stg = staging + e * STAGE_FLOATS;
+    const int col = lane & 15, sub = lane >> 4;
+    long job = 0;
+    for (long t = x.first; t < x.tiles; t += x.Q, job++) {
+        const int buf = int(job & 1);
+        const bool ok = wait_phase(smem_u32(&x.accf[buf]), uint32_t(job >> 1) & 1u, x.abort_flag, a.err);
+        __syncwarp();
+        if (!__all_sync(0xffffffffu, ok)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const long mrow = t * TM + qd * 32;
+        for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
+            float v[16];
+            tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);
+            bias_act_stage(a.act, v, bias_s + c0, stg + lane * 17);
+            __syncwarp();
+            // two rows of 16 channels per pass
+            const int n = x.n0 + c0 + col;
+            if (n < a.N) {
+#pragma unroll 4
+                for (int i = sub; i < 32; i += 2) {
+                    const long m = mrow + i;
+                    if (m >= a.M) break;
+                    float y = stg[i * 17 + col];
+                    if (a.res) y = activate(a.act2, fadd(y, __ldg(a.res + m * a.N + n)));
+                    a.y[m * a.N + n] = y;
+                }
+            }
+            __syncwarp();
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        arrive(smem_u32(&x.acce[buf]));
+    }
+}
+
+// One gathered row of a tile: its lane, top-left input tap and input size
+// (ihw = ih << 16 | iw; 0 past the last pixel).
+struct RowMeta {
+    int n, iy0, ix0, ihw;
+};
+
+__device__ __forceinline__ RowMeta row_meta(const TcArgs &a, long m) {
+    RowMeta r{0, 0, 0, 0};
+    if (m >= a.M) return r;
+    r.n = find_lane(a.lanes, a.nl, m);
+    const LaneInfo &L = a.lanes[r.n];
+    const int ow = __ldg(&L.ow);
+    const int q = int(m - __ldg(&L.pix0));
+    const int oy = q / ow, ox = q - oy * ow;
+    r.iy0 = oy * a.sh - a.pt;
+    r.ix0 = ox * a.sw - a.pl;
+    r.ihw = (__ldg(&L.ih) << 16) | __ldg(&L.iw);
+    return r;
+}
+
+// Where k of a gathered row reads (null for a zero: padding, the K tail, a
+// pixel past the end). With `vec`, k..k+3 lie in one tap and one source.
+__device__ __forceinline__ const float *locate(const TcArgs &a, const RowMeta &r, int k) {
+    if (r.ihw == 0 || k >= a.K) return nullptr;
+    const int tap = k / a.C, c = k - tap * a.C;
+    const int ky = tap / a.kw, kx = tap - ky * a.kw;
+    const int iy = r.iy0 + ky, ix = r.ix0 + kx;
+    const int ih = r.ihw >> 16, iw = r.ihw & 0xffff;
+    if (iy < 0 || iy >= ih || ix < 0 || ix >= iw) return nullptr;
+    int start = 0, s = 0;
+    while (s + 1 < a.nsrc && c >= start + a.src[s].c) {
+        start += a.src[s].c;
+        s++;
+    }
+    const ConvSource &src = a.src[s];
+    const int sh = src.shift;
+    const long pix = __ldg(&a.lanes[r.n].spix0[s]) + (long)(iy >> sh) * (iw >> sh) + (ix >> sh);
+    return src.p + pix * src.c + (c - start);
+}
+
+// Shared set-up of both kernels: barriers, bias slice, TMEM.
+template <class R>
+__device__ __forceinline__ void setup(const TcArgs &a, Ctx &x, int full_count, uint64_t *bfull, float *bias_s,
+                                      uint32_t *tmem_base_s, int *abort_s) {
+    const int tid = threadIdx.x, warp = tid / 32;
     if (tid == 0) {
-        for (int s = 0; s < ns; s++) {
-            bar_init(smem_u32(&full[s]), 1);
-            bar_init(smem_u32(&conv[s]), 128);
-            bar_init(smem_u32(&empty[s]), 1);
+        for (int s = 0; s < x.ns; s++) {
+            bar_init(smem_u32(&x.full[s]), full_count);
+            bar_init(smem_u32(&x.conv[s]), 128);
+            bar_init(smem_u32(&x.empty[s]), 1);
         }
         for (int b = 0; b < 2; b++) {
-            bar_init(smem_u32(&accf[b]), 1);
-            bar_init(smem_u32(&acce[b]), EPI_WARPS * 32);
+            bar_init(smem_u32(&x.accf[b]), 1);
+            bar_init(smem_u32(&x.acce[b]), EPI_WARPS * 32);
         }
-        bar_init(smem_u32(&bfull), 1);
-        abort_s = 0;
+        bar_init(smem_u32(bfull), 1);
+        *abort_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    for (int j = tid; j < BN; j += THREADS) bias_s[j] = (a.b && n0 + j < a.N) ? a.b[n0 + j] : 0.0f;
-    if (warp == W_MMA) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+    for (int j = tid; j < x.BN; j += R::THREADS) bias_s[j] = (a.b && x.n0 + j < a.N) ? a.b[x.n0 + j] : 0.0f;
+    if (warp == R::W_MMA) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_base_s)),
                      "r"(a.tmem_cols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const uint32_t tmem = tmem_base_s;
+    x.tmem = *tmem_base_s;
+}
 
+template <class R>
+__device__ __forceinline__ void teardown(const TcArgs &a, const Ctx &x) {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x / 32 == R::W_MMA) {
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(x.tmem), "r"(a.tmem_cols));
+    }
+}
+
+__global__ void __launch_bounds__(PwRoles::THREADS, 1)
+    pw_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw) {
+    using R = PwRoles;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    __shared__ __align__(8) uint64_t full[MAX_NS], conv[MAX_NS], empty[MAX_NS], accf[2], acce[2], bfull;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s;
+
+    Ctx x;
+    x.ns = a.ns; x.nkb = a.nkb; x.BN = a.bn;
+    x.Q = gridDim.x / a.slices;
+    x.first = blockIdx.x / a.slices;
+    x.n0 = int(blockIdx.x % a.slices) * a.bn;
+    x.tiles = (a.M + TM - 1) / TM;
+    x.ring = smem_u32(smem);
+    x.stage_bytes = SLOT_BYTES;
+    x.b_base = x.ring + uint32_t(x.ns) * SLOT_BYTES;
+    x.b_bytes = uint32_t(a.bn) * 128;
+    x.full = full; x.conv = conv; x.empty = empty; x.accf = accf; x.acce = acce;
+    x.abort_flag = &abort_s;
+    float *staging = reinterpret_cast<float *>(smem + size_t(x.ns) * SLOT_BYTES + size_t(2) * x.nkb * x.b_bytes);
+    float *bias_s = staging + EPI_WARPS * STAGE_FLOATS;  // this slice's BN biases, zero past N
+    setup<R>(a, x, 1, &bfull, bias_s, &tmem_base_s, &abort_s);
+
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     if (warp == 0) {
         if (lane == 0) {
             // the weight slice: nkb blocks of BN rows, high halves then low
             const uint32_t bb = smem_u32(&bfull);
-            arrive_expect(bb, uint32_t(2 * nkb) * b_bytes);
-            for (int kb = 0; kb < nkb; kb++) {
-                tma_load_3d(b_base + uint32_t(kb) * b_bytes, &tmw, kb * TK, n0, 0, bb);
-                tma_load_3d(b_base + uint32_t(nkb + kb) * b_bytes, &tmw, kb * TK, n0, 1, bb);
+            arrive_expect(bb, uint32_t(2 * x.nkb) * x.b_bytes);
+            for (int kb = 0; kb < x.nkb; kb++) {
+                tma_load_3d(x.b_base + uint32_t(kb) * x.b_bytes, &tmw, kb * TK, x.n0, 0, bb);
+                tma_load_3d(x.b_base + uint32_t(x.nkb + kb) * x.b_bytes, &tmw, kb * TK, x.n0, 1, bb);
             }
             long it = 0;  // K blocks issued
             bool ok = true;
-            for (long t = first; t < tiles && ok; t += Q)
-                for (int kb = 0; kb < nkb; kb++, it++) {
-                    const int s = int(it % ns);
-                    const long round = it / ns;
-                    if (round > 0 && !wait_phase(smem_u32(&empty[s]), uint32_t(round - 1) & 1u, abort_flag, a.err)) {
+            for (long t = x.first; t < x.tiles && ok; t += x.Q)
+                for (int kb = 0; kb < x.nkb; kb++, it++) {
+                    const int s = int(it % x.ns);
+                    const long round = it / x.ns;
+                    if (round > 0 && !wait_phase(smem_u32(&empty[s]), uint32_t(round - 1) & 1u, x.abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
-                    arrive_expect(smem_u32(&full[s]), TM * 128);
-                    tma_load_2d(ring + uint32_t(s) * SLOT_BYTES, &tmx, kb * TK, int(t * TM), smem_u32(&full[s]));
+                    arrive_expect(smem_u32(&full[s]), A_BYTES);
+                    tma_load_2d(x.ring + uint32_t(s) * SLOT_BYTES, &tmx, kb * TK, int(t * TM), smem_u32(&full[s]));
                 }
-            if (*abort_flag) {
+            if (*x.abort_flag) {
                 // the copies still in flight land before the CTA leaves
                 drain(bb, 0);
-                for (int s = 0; s < ns && s < it; s++) drain(smem_u32(&full[s]), uint32_t((it - 1 - s) / ns) & 1u);
+                for (int s = 0; s < x.ns && s < it; s++)
+                    drain(smem_u32(&full[s]), uint32_t((it - 1 - s) / x.ns) & 1u);
             }
         }
-    } else if (warp == W_MMA) {
-        if (lane == 0) {
-            const uint32_t idesc = tf32_idesc(BN);
-            long it = 0, job = 0;
-            uint32_t last_bar = 0, last_parity = 0;
-            bool ok = wait_phase(smem_u32(&bfull), 0, abort_flag, a.err);
-            for (long t = first; t < tiles && ok; t += Q, job++) {
-                const int buf = int(job & 1);
-                const long use = job >> 1;
-                if (use > 0 && !wait_phase(smem_u32(&acce[buf]), uint32_t(use - 1) & 1u, abort_flag, a.err)) break;
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t d = tmem + uint32_t(buf * BN);
-                for (int kb = 0; kb < nkb; kb++, it++) {
-                    const int s = int(it % ns);
-                    const long round = it / ns;
-                    if (!wait_phase(smem_u32(&conv[s]), uint32_t(round) & 1u, abort_flag, a.err)) {
-                        ok = false;
-                        break;
-                    }
-                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t ah = ring + uint32_t(s) * SLOT_BYTES, al = ah + TM * 128;
-                    const uint32_t bh = b_base + uint32_t(kb) * b_bytes, bl = b_base + uint32_t(nkb + kb) * b_bytes;
-                    // K steps of 8 tf32 (32 bytes along the swizzled rows);
-                    // steps wholly past K hold zeros and are skipped
-                    const int left = a.K - kb * TK;
-                    const int steps = left >= TK ? TK / 8 : (left + 7) / 8;
-                    for (int kk = 0; kk < steps; kk++) {
-                        const uint32_t acc = (kb == 0 && kk == 0) ? 0u : 1u;
-                        const uint64_t dah = sw128_desc(ah + kk * 32), dal = sw128_desc(al + kk * 32);
-                        const uint64_t dbh = sw128_desc(bh + kk * 32), dbl = sw128_desc(bl + kk * 32);
-                        mma_tf32(d, dah, dbh, idesc, acc);
-                        mma_tf32(d, dah, dbl, idesc, 1u);
-                        mma_tf32(d, dal, dbh, idesc, 1u);
-                    }
-                    commit(smem_u32(&empty[s]));
-                    last_bar = smem_u32(&empty[s]);
-                    last_parity = uint32_t(round) & 1u;
-                }
-                if (!ok) break;
-                commit(smem_u32(&accf[buf]));
-                last_bar = smem_u32(&accf[buf]);
-                last_parity = uint32_t(use) & 1u;
-            }
-            // the tensor core is done with shared memory and TMEM before the
-            // CTA frees them
-            if (last_bar) drain(last_bar, last_parity);
-        }
-    } else if (warp < W_EPI) {
-        // split in place: the staged block becomes the high half, its twin
-        // the low half (same swizzled layout, so element for element)
-        const int ct = tid - W_CONV * 32;
+    } else if (warp == R::W_MMA) {
+        if (lane == 0) role_mma<true>(a, x, &bfull);
+    } else if (warp < R::W_EPI) {
+        role_convert(a, x, tid - R::W_CONV * 32);
+    } else {
+        role_epilogue(a, x, warp - R::W_EPI, warp, lane, staging, bias_s);
+    }
+    teardown<R>(a, x);
+}
+
+__global__ void __launch_bounds__(ConvRoles::THREADS, 1)
+    conv_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw) {
+    using R = ConvRoles;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    __shared__ __align__(8) uint64_t full[MAX_NS], conv[MAX_NS], empty[MAX_NS], accf[2], acce[2], bfull;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s;
+
+    Ctx x;
+    x.ns = a.ns; x.nkb = a.nkb; x.BN = a.bn;
+    x.Q = gridDim.x / a.slices;
+    x.first = blockIdx.x / a.slices;
+    x.n0 = int(blockIdx.x % a.slices) * a.bn;
+    x.tiles = (a.M + TM - 1) / TM;
+    x.ring = smem_u32(smem);
+    x.b_bytes = uint32_t(a.bn) * 128;
+    x.stage_bytes = SLOT_BYTES + 2 * x.b_bytes;
+    x.b_base = 0;
+    x.full = full; x.conv = conv; x.empty = empty; x.accf = accf; x.acce = acce;
+    x.abort_flag = &abort_s;
+    float *staging = reinterpret_cast<float *>(smem + size_t(x.ns) * x.stage_bytes);
+    float *bias_s = staging + EPI_WARPS * STAGE_FLOATS;
+    // a stage is full once the 128 gathering threads' copies and the weight
+    // block's bytes have landed
+    setup<R>(a, x, 128 + 1, &bfull, bias_s, &tmem_base_s, &abort_s);
+
+    const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    if (warp < R::PROD_WARPS) {
+        // Gather: thread g copies the 16-byte chunk g & 7 of rows
+        // (g >> 3) + 16 j, j = 0..7, into its swizzled place.
+        const int g = tid, cc = g & 7, r0 = g >> 3;
+        const bool vec = a.vec4 != 0;
         long it = 0;
         bool ok = true;
-        for (long t = first; t < tiles && ok; t += Q)
-            for (int kb = 0; kb < nkb; kb++, it++) {
-                const int s = int(it % ns);
-                const long round = it / ns;
-                if (!wait_phase(smem_u32(&full[s]), uint32_t(round) & 1u, abort_flag, a.err)) {
+        for (long t = x.first; t < x.tiles && ok; t += x.Q) {
+            RowMeta rm[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) rm[j] = row_meta(a, t * TM + r0 + 16 * j);
+            for (int kb = 0; kb < x.nkb; kb++, it++) {
+                const int s = int(it % x.ns);
+                const long round = it / x.ns;
+                if (round > 0 && !wait_phase(smem_u32(&empty[s]), uint32_t(round - 1) & 1u, x.abort_flag, a.err)) {
                     ok = false;
                     break;
                 }
-                float4 *hi = reinterpret_cast<float4 *>(smem + size_t(s) * SLOT_BYTES);
-                float4 *lo = hi + TM * 128 / 16;
-#pragma unroll
-                for (int i = ct; i < TM * 128 / 16; i += 128) {
-                    const float4 v = hi[i];
-                    const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-                    hi[i] = h;
-                    lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
-                }
-                // make the generic-proxy stores visible to the tensor core
+                // the tensor core's reads of this stage are ordered before
+                // the new writes
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                arrive(smem_u32(&conv[s]));
-            }
-    } else {
-        const int qd = warp & 3;                 // the TMEM lane quadrant this warp may read
-        const int half = (warp - W_EPI) / 4;     // which alternate 16-column chunks it takes
-        float *stg = staging + (warp - W_EPI) * STAGE_FLOATS;
-        const int col = lane & 15, sub = lane >> 4;
-        long job = 0;
-        for (long t = first; t < tiles; t += Q, job++) {
-            const int buf = int(job & 1);
-            const bool ok = wait_phase(smem_u32(&accf[buf]), uint32_t(job >> 1) & 1u, abort_flag, a.err);
-            __syncwarp();
-            if (!__all_sync(0xffffffffu, ok)) break;
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const long mrow = t * TM + qd * 32;
-            for (int c0 = half * 16; c0 < BN; c0 += 32) {
-                float v[16];
-                tmem_ld16(tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * BN + c0), v);
-                bias_act_stage(a.act, v, bias_s + c0, stg + lane * 17);
-                __syncwarp();
-                // two rows of 16 channels per pass
-                const int n = n0 + c0 + col;
-                if (n < a.N) {
-#pragma unroll 4
-                    for (int i = sub; i < 32; i += 2) {
-                        const long m = mrow + i;
-                        if (m >= a.M) break;
-                        float x = stg[i * 17 + col];
-                        if (a.res) x = activate(a.act2, fadd(x, __ldg(a.res + m * a.N + n)));
-                        a.y[m * a.N + n] = x;
+                const uint32_t stage = x.ring + uint32_t(s) * x.stage_bytes;
+                if (g == 0) {
+                    arrive_expect(smem_u32(&full[s]), 2 * x.b_bytes);
+                    tma_load_3d(stage + SLOT_BYTES, &tmw, kb * TK, x.n0, 0, smem_u32(&full[s]));
+                    tma_load_3d(stage + SLOT_BYTES + x.b_bytes, &tmw, kb * TK, x.n0, 1, smem_u32(&full[s]));
+                }
+                const int k = kb * TK + cc * 4;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int r = r0 + 16 * j;
+                    const uint32_t dst = stage + swz(r, cc);
+                    if (vec) {
+                        const float *src = locate(a, rm[j], k);
+                        cp_async16(dst, src ? src : a.y, src ? 16u : 0u);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const float *src = locate(a, rm[j], k + e);
+                            cp_async4(dst + 4 * e, src ? src : a.y, src ? 4u : 0u);
+                        }
                     }
                 }
-                __syncwarp();
+                cp_async_arrive(smem_u32(&full[s]));
             }
-            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            arrive(smem_u32(&acce[buf]));
         }
+        if (*x.abort_flag) {
+            // the copies still in flight land before the CTA leaves
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            if (g == 0)
+                for (int s = 0; s < x.ns && s < it; s++)
+                    drain(smem_u32(&full[s]), uint32_t((it - 1 - s) / x.ns) & 1u);
+        }
+    } else if (warp == R::W_MMA) {
+        if (lane == 0) role_mma<false>(a, x, &bfull);
+    } else if (warp < R::W_EPI) {
+        role_convert(a, x, tid - R::W_CONV * 32);
+    } else {
+        role_epilogue(a, x, warp - R::W_EPI, warp, lane, staging, bias_s);
     }
-
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
-    if (warp == W_MMA) {
-        __syncwarp();
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols));
-    }
+    teardown<R>(a, x);
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -441,43 +664,51 @@ EncodeTiled encode_tiled() {
     return fn;
 }
 
-size_t smem_for(int kpad, int bn, int ns) {
-    return 1024 + size_t(ns) * SLOT_BYTES + size_t(8) * kpad * bn + EPI_BYTES;
-}
+size_t pw_smem(int kpad, int bn, int ns) { return 1024 + size_t(ns) * SLOT_BYTES + size_t(8) * kpad * bn + EPI_BYTES; }
 
-// The weight slice width for K x N: the fewest slices of at most 256
-// channels (a multiple of 32) whose weights, both halves, fit in shared
-// memory beside a three-stage ring (else a two-stage one). 0 when none does.
-int slice_width(int K, int N) {
+size_t conv_smem(int bn, int ns) { return 1024 + size_t(ns) * (SLOT_BYTES + size_t(256) * bn) + EPI_BYTES; }
+
+// The weight slice width for a pointwise K x N: the fewest slices of at
+// most 256 channels (a multiple of 32) whose weights, both halves, fit in
+// shared memory beside a three-stage ring (else a two-stage one). 0 when
+// none does.
+int pw_slice_width(int K, int N) {
     const int kpad = (K + TK - 1) / TK * TK;
     for (int stages = 3; stages >= 2; stages--)
         for (int S = 1; S <= (N + 31) / 32; S++) {
             const int bn = ((N + S - 1) / S + 31) / 32 * 32;
-            if (bn <= 256 && smem_for(kpad, bn, stages) <= size_t(DYN_CEILING)) return bn;
+            if (bn <= 256 && pw_smem(kpad, bn, stages) <= size_t(DYN_CEILING)) return bn;
         }
     return 0;
 }
 
-}  // namespace
+// The gathered kernel streams its weights, so a slice is as wide as a
+// four-stage ring allows (at most 128).
+int conv_slice_width(int N) {
+    for (int S = 1; S <= (N + 31) / 32; S++) {
+        const int bn = ((N + S - 1) / S + 31) / 32 * 32;
+        if (bn <= 128 && conv_smem(bn, 4) <= size_t(DYN_CEILING)) return bn;
+    }
+    return 0;
+}
 
-bool pw_tc_supported(int K, int N) { return K >= 1 && K % 4 == 0 && N >= 1 && slice_width(K, N) > 0; }
+bool encode_weights(TcArgs &a, EncodeTiled enc) {
+    // weights: [half][N][kpad], boxes of 32 k x BN outputs; outputs past N
+    // read as zeros
+    CUtensorMap mw;
+    cuuint64_t dims[3] = {cuuint64_t(a.kpad), cuuint64_t(a.N), 2};
+    cuuint64_t strides[2] = {cuuint64_t(a.kpad) * 4, cuuint64_t(a.N) * a.kpad * 4};
+    cuuint32_t box[3] = {TK, cuuint32_t(a.bn), 1}, estr[3] = {1, 1, 1};
+    if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(a.w_hi), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    static_assert(sizeof(CUtensorMap) == sizeof(a.tmw), "tensor map size");
+    std::memcpy(a.tmw, &mw, sizeof mw);
+    return true;
+}
 
-int pw_tc_kpad(int K) { return (K + TK - 1) / TK * TK; }
-
-bool pw_tc_prepare(PwTcArgs &a) {
-    if (!pw_tc_supported(a.K, a.N) || a.M < 1 || a.kpad != pw_tc_kpad(a.K)) return false;
-    const auto aligned = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-    if (!aligned(a.x) || !aligned(a.w_hi) || a.w_lo != a.w_hi + size_t(a.N) * a.kpad) return false;
-    EncodeTiled enc = encode_tiled();
-    if (!enc) return false;
-    a.bn = slice_width(a.K, a.N);
-    a.slices = (a.N + a.bn - 1) / a.bn;
-    a.nkb = a.kpad / TK;
-    a.ns = 2;
-    while (a.ns < MAX_NS && smem_for(a.kpad, a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
-    a.smem = int(smem_for(a.kpad, a.bn, a.ns));
-    a.tmem_cols = 32;
-    while (a.tmem_cols < 2 * a.bn) a.tmem_cols *= 2;
+bool set_grid(TcArgs &a) {
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
@@ -485,9 +716,34 @@ bool pw_tc_prepare(PwTcArgs &a) {
     const long tiles = (a.M + TM - 1) / TM;
     const long q = std::max(1L, std::min(long(sms / a.slices), tiles));
     a.grid = int(q) * a.slices;
+    a.tmem_cols = 32;
+    while (a.tmem_cols < 2 * a.bn) a.tmem_cols *= 2;
+    return true;
+}
 
-    CUtensorMap mx, mw;
-    {
+}  // namespace
+
+int pw_tc_kpad(int K) { return (K + TK - 1) / TK * TK; }
+
+bool tc_weights_wanted(int K, int N) { return K >= 1 && N >= 1 && N <= 512; }
+
+bool tc_prepare(TcArgs &a) {
+    if (a.M < 1 || a.N < 1 || a.K < 1 || a.kpad != pw_tc_kpad(a.K)) return false;
+    const auto aligned = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (!aligned(a.w_hi) || a.w_lo != a.w_hi + size_t(a.N) * a.kpad) return false;
+    EncodeTiled enc = encode_tiled();
+    if (!enc) return false;
+    a.nkb = a.kpad / TK;
+    if (!a.gather) {
+        // 1x1, one source: one TMA copy per A block
+        if (a.K % 4 || !aligned(a.x) || (a.gate && !aligned(a.gate))) return false;
+        a.bn = pw_slice_width(a.K, a.N);
+        if (!a.bn) return false;
+        a.slices = (a.N + a.bn - 1) / a.bn;
+        a.ns = 2;
+        while (a.ns < MAX_NS && pw_smem(a.kpad, a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
+        a.smem = int(pw_smem(a.kpad, a.bn, a.ns));
+        CUtensorMap mx;
         // pixels: [M][K], boxes of 32 channels x 128 pixels; channels past K
         // and pixels past M read as zeros
         cuuint64_t dims[2] = {cuuint64_t(a.K), cuuint64_t(a.M)};
@@ -497,33 +753,37 @@ bool pw_tc_prepare(PwTcArgs &a) {
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return false;
+        std::memcpy(a.tmx, &mx, sizeof mx);
+    } else {
+        if (a.gate || a.nsrc < 1 || a.C < 1 || a.K != a.kh * a.kw * a.C) return false;
+        a.vec4 = a.C % 4 == 0;
+        for (int s = 0; s < a.nsrc; s++)
+            if (a.src[s].c % 4 || !aligned(a.src[s].p)) a.vec4 = 0;
+        a.bn = conv_slice_width(a.N);
+        if (!a.bn) return false;
+        a.slices = (a.N + a.bn - 1) / a.bn;
+        a.ns = 2;
+        while (a.ns < MAX_NS && conv_smem(a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
+        a.smem = int(conv_smem(a.bn, a.ns));
     }
-    {
-        // weights: [half][N][kpad], boxes of 32 channels x BN outputs; outputs
-        // past N read as zeros
-        cuuint64_t dims[3] = {cuuint64_t(a.kpad), cuuint64_t(a.N), 2};
-        cuuint64_t strides[2] = {cuuint64_t(a.kpad) * 4, cuuint64_t(a.N) * a.kpad * 4};
-        cuuint32_t box[3] = {TK, cuuint32_t(a.bn), 1}, estr[3] = {1, 1, 1};
-        if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(a.w_hi), dims, strides, box, estr,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
-    }
-    static_assert(sizeof(CUtensorMap) == sizeof(a.tmx), "tensor map size");
-    std::memcpy(a.tmx, &mx, sizeof mx);
-    std::memcpy(a.tmw, &mw, sizeof mw);
-    return true;
+    return encode_weights(a, enc) && set_grid(a);
 }
 
 void configure_tc_kernels() {
     cudaFuncSetAttribute(pw_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
+    cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
 }
 
-int launch_pw_tc(const PwTcArgs &a, cudaStream_t s) {
-    CUtensorMap mx, mw;
-    std::memcpy(&mx, a.tmx, sizeof mx);
+int launch_tc(const TcArgs &a, cudaStream_t s) {
+    CUtensorMap mw;
     std::memcpy(&mw, a.tmw, sizeof mw);
-    pw_tc_kernel<<<a.grid, THREADS, a.smem, s>>>(a, mx, mw);
+    if (a.gather) {
+        conv_tc_kernel<<<a.grid, ConvRoles::THREADS, a.smem, s>>>(a, mw);
+    } else {
+        CUtensorMap mx;
+        std::memcpy(&mx, a.tmx, sizeof mx);
+        pw_tc_kernel<<<a.grid, PwRoles::THREADS, a.smem, s>>>(a, mx, mw);
+    }
     return 1;
 }
 

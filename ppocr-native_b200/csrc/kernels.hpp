@@ -191,31 +191,42 @@ struct ConvTArgs {
 // Pointwise convolution on the tensor cores (k_tc.cu), 3xTF32: weights
 // pre-split and transposed to [n][kpad] (K-major, zero-padded to 32
 // channels and to whole BN tiles of output channels).
-struct PwTcArgs {
-    const float *x = nullptr;     // [M][K], 16-byte aligned, K % 4 == 0
+// A convolution on the tensor cores (3xTF32). Pointwise layers (1x1, unit
+// stride, one source) read their input with TMA (`gather` false); the rest
+// gather it like ConvArgs' sources.
+struct TcArgs {
+    bool gather = false;
+    const float *x = nullptr;     // pointwise: [M][K], 16-byte aligned, K % 4 == 0
+    ConvSource src[MAX_SOURCES];  // gathered: up to four sources, nearest-upsampled by 2^shift
+    int nsrc = 0, C = 0;
+    int kh = 1, kw = 1, sh = 1, sw = 1, pt = 0, pl = 0;
+    const LaneInfo *lanes = nullptr;
+    int nl = 1;
+    const float *gate = nullptr;  // pointwise: [lanes][K], x of lane n scaled by gate[n] first
     const float *w_hi = nullptr;  // [N][kpad]: high tf32 halves, K-major
     const float *w_lo = nullptr;  // w_hi + N * kpad: the low halves
     const float *b = nullptr;     // [N] or null
     const float *res = nullptr;   // [M][N] or null
     float *y = nullptr;           // [M][N]
     long M = 0;
-    int K = 0, N = 0, kpad = 0;
+    int K = 0, N = 0, kpad = 0;   // K = kh * kw * C
     int act = 0, act2 = 0;
     int *err = nullptr;           // set to nonzero when a bounded wait gave up
-    // filled by pw_tc_prepare: output-channel slice width and count, K
-    // blocks, ring stages, TMEM columns, grid, dynamic shared memory, and
-    // the pixel and weight tensor maps (CUtensorMap, 128 bytes each)
-    int bn = 0, slices = 0, nkb = 0, ns = 0, tmem_cols = 0, grid = 0, smem = 0;
+    // filled by tc_prepare: output-channel slice width and count, K blocks,
+    // ring stages, TMEM columns, grid, dynamic shared memory, 16-byte
+    // gathers, and the tensor maps (CUtensorMap, 128 bytes each) of the
+    // pointwise input and of the weights
+    int bn = 0, slices = 0, nkb = 0, ns = 0, tmem_cols = 0, grid = 0, smem = 0, vec4 = 0;
     unsigned long long tmx[16] = {}, tmw[16] = {};
 };
-int launch_pw_tc(const PwTcArgs &a, cudaStream_t s);
-// Whether a K -> N pointwise layer fits the tensor-core kernel at all.
-bool pw_tc_supported(int K, int N);
+int launch_tc(const TcArgs &a, cudaStream_t s);
+// Whether a K x N layer gets split tensor-core weights at load.
+bool tc_weights_wanted(int K, int N);
 // The padded K of the prepared weights (a multiple of 32).
 int pw_tc_kpad(int K);
 // Fills the launch shape and tensor maps; false when the layer cannot run
 // there (alignment, sizes, no driver entry point).
-bool pw_tc_prepare(PwTcArgs &a);
+bool tc_prepare(TcArgs &a);
 void configure_tc_kernels();
 
 // Each returns the number of kernels it launched.
@@ -245,9 +256,13 @@ constexpr long DW_PW_MIN_PIXELS = 148L * 2 * 128;
 // Scratch sizes (elements) the launches above need.
 // Pixel runs a lane's channel mean is split into; a lane's result depends
 // only on its own size, never on the other lanes of the run.
-__host__ __device__ inline int mean_chunks(long hw) {
-    long chunks = (hw + 511) / 512;
-    return int(chunks < 1 ? 1 : (chunks > 1024 ? 1024 : chunks));
+// Runs hold about 8192 values (a power of two of pixels, 16..2048), so a
+// block has a few dozen loads per thread whatever the channel count.
+__host__ __device__ inline int mean_chunks(long hw, int c) {
+    int per = 16;
+    while (per < 2048 && per * 2 * c <= 8192) per *= 2;
+    long chunks = (hw + per - 1) / per;
+    return int(chunks < 1 ? 1 : (chunks > 16384 ? 16384 : chunks));
 }
 int ctc_col_blocks(int cols);
 // Largest shared-memory need of launch_dw_pw for `c` input channels; 0 when

@@ -513,7 +513,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
         if (op.kind == K_MEAN) {
             long hw = 0;
             for (size_t n = 0; n < N; n++) hw = std::max<long>(hw, long(g.lane(n).ops[i].ih * g.lane(n).ops[i].iw));
-            mean_doubles = std::max(mean_doubles, N * size_t(mean_chunks(hw)) * op.ic);
+            mean_doubles = std::max(mean_doubles, N * size_t(mean_chunks(hw, int(op.ic))) * op.ic);
         }
         if (op.kind == K_CTCHEAD || op.kind == K_CTCARGMAX) {
             size_t vocab = op.kind == K_CTCHEAD ? op.oc : op.n2;
@@ -595,14 +595,21 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             writer[op.y] = int(i);
         }
     }
-    auto tc_route = [&](size_t i, const ConvArgs &c, PwTcArgs &t) {
-        if (!tc_allowed || !W.tc_hi(i) || reads_mean[i] || c.gate || c.nsrc != 1 || c.src[0].shift || c.kh != 1 ||
-            c.kw != 1 || c.sh != 1 || c.sw != 1 || c.pt || c.pl)
-            return false;
-        t.x = c.src[0].p; t.w_hi = W.tc_hi(i); t.w_lo = W.tc_lo(i); t.b = c.b; t.res = c.res; t.y = c.y;
-        t.M = c.M; t.K = c.C; t.N = c.oc; t.kpad = W.tc_kpad[i];
+    auto tc_route = [&](size_t i, const ConvArgs &c, TcArgs &t) {
+        if (!tc_allowed || !W.tc_hi(i) || reads_mean[i]) return false;
+        const bool pw = c.nsrc == 1 && !c.src[0].shift && c.kh == 1 && c.kw == 1 && c.sh == 1 && c.sw == 1 &&
+                        !c.pt && !c.pl;
+        if (!pw) return false;
+        t.gather = !pw;
+        t.x = c.src[0].p;
+        for (int q = 0; q < c.nsrc; q++) t.src[q] = c.src[q];
+        t.nsrc = c.nsrc; t.C = c.C;
+        t.kh = c.kh; t.kw = c.kw; t.sh = c.sh; t.sw = c.sw; t.pt = c.pt; t.pl = c.pl;
+        t.lanes = c.lanes; t.nl = c.nl; t.gate = c.gate;
+        t.w_hi = W.tc_hi(i); t.w_lo = W.tc_lo(i); t.b = c.b; t.res = c.res; t.y = c.y;
+        t.M = c.M; t.K = c.kh * c.kw * c.C; t.N = c.oc; t.kpad = W.tc_kpad[i];
         t.act = c.act; t.act2 = c.act2; t.err = errp;
-        return pw_tc_prepare(t);
+        return tc_prepare(t);
     };
     for (size_t k = 0; k < steps.size(); k++) {
         const Step &st = steps[k];
@@ -644,9 +651,9 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             c.act = a.act2; c.bias_mode = a.bias_mode2;
             c.res = a.res; c.act2 = a.act3;
             c.y = a.y;
-            PwTcArgs t;
+            TcArgs t;
             if (tc_route(st.b, c, t))
-                g.launches.push_back([d, t](cudaStream_t s) { return launch_dw(d, s) + launch_pw_tc(t, s); });
+                g.launches.push_back([d, t](cudaStream_t s) { return launch_dw(d, s) + launch_tc(t, s); });
             else
                 g.launches.push_back([d, c](cudaStream_t s) { return launch_dw(d, s) + launch_conv(c, s); });
             continue;
@@ -676,9 +683,9 @@ int ppocr_model::build_group(Group &g, std::string &err) {
                 a.act2 = add.fused;
                 a.y = buf(add.y);
             }
-            PwTcArgs t;
+            TcArgs t;
             if (tc_route(st.b, a, t))
-                g.launches.push_back([t](cudaStream_t s) { return launch_pw_tc(t, s); });
+                g.launches.push_back([t](cudaStream_t s) { return launch_tc(t, s); });
             else
                 g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
             continue;
@@ -707,9 +714,9 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
             a.pt = int(op.pt); a.pl = int(op.pl); a.act = op.fused; a.bias_mode = bias_mode(op);
             a.y = buf(op.y);
-            PwTcArgs t;
+            TcArgs t;
             if (tc_route(i, a, t))
-                g.launches.push_back([t](cudaStream_t s) { return launch_pw_tc(t, s); });
+                g.launches.push_back([t](cudaStream_t s) { return launch_tc(t, s); });
             else
                 g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
             break;
@@ -749,7 +756,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             a.lanes = L; a.nl = nl; a.c = int(op.ic);
             long hw = 0;
             for (size_t n = 0; n < N; n++) hw = std::max<long>(hw, long(g.lane(n).ops[i].ih * g.lane(n).ops[i].iw));
-            a.chunks = mean_chunks(hw);
+            a.chunks = mean_chunks(hw, a.c);
             g.launches.push_back([a](cudaStream_t s) { return launch_mean(a, s); });
             break;
         }
@@ -941,15 +948,15 @@ int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_mode
         w->b_at.push_back(place(op.b0, op.b1));
     }
     arena.resize(std::max<size_t>(arena.size(), 1) + 64, 0.0f);
-    // Tensor-core copies of the pointwise layers' weights: W [k][n] to
-    // [n][kpad], the high tf32 half (low 13 mantissa bits cleared) and the
-    // exact remainder.
+    // Tensor-core copies of the dense convolutions' weights: W [k][n] (k
+    // over kh, kw, C) to [n][kpad], the high tf32 half (low 13 mantissa bits
+    // cleared) and the exact remainder.
     std::vector<float> tc;
     for (const Op &op : plan.ops) {
         size_t hi = SIZE_MAX, lo = SIZE_MAX;
         int kpad = 0;
-        if (op.pointwise() && op.w1 && pw_tc_supported(int(op.ic), int(op.oc))) {
-            int K = int(op.ic), N = int(op.oc);
+        const int K = int(op.kh * op.kw * (op.ic + op.n2)), N = int(op.oc);
+        if (op.kind == K_CONV && op.w1 && tc_weights_wanted(K, N)) {
             kpad = pw_tc_kpad(K);
             while (tc.size() % 64) tc.push_back(0.0f);
             hi = tc.size();

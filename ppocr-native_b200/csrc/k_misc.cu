@@ -464,6 +464,39 @@ __global__ void __launch_bounds__(256) convt_kernel(const ConvTArgs a) {
 
 }  // namespace
 
+// ------------------------------------------------------------------ gather
+
+// One thread per (pixel, 4 channels), grid-strided; every source's channel
+// count is a multiple of 4.
+__global__ void __launch_bounds__(256) gather_kernel(const GatherArgs a) {
+    const int groups = a.C / 4;
+    const long total = a.M * groups;
+    for (long g = (long)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (long)gridDim.x * blockDim.x) {
+        const long m = g / groups;
+        const int c = int(g - m * groups) * 4;
+        const int n = find_lane(a.lanes, a.nl, m, true);
+        const LaneInfo &L = a.lanes[n];
+        const int iw = __ldg(&L.iw);
+        const int q = int(m - __ldg(&L.ipix0));
+        const int iy = q / iw, ix = q - iy * iw;
+        int start = 0, s = 0;
+        while (s + 1 < a.nsrc && c >= start + a.src[s].c) {
+            start += a.src[s].c;
+            s++;
+        }
+        const ConvSource &src = a.src[s];
+        const int sh = src.shift;
+        const long pix = __ldg(&L.spix0[s]) + (long)(iy >> sh) * (iw >> sh) + (ix >> sh);
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(src.p + pix * src.c + (c - start)));
+        *reinterpret_cast<float4 *>(a.y + m * a.C + c) = v;
+    }
+}
+
+int launch_gather(const GatherArgs &a, cudaStream_t s) {
+    gather_kernel<<<grid_for(a.M * (a.C / 4)), 256, 0, s>>>(a);
+    return 1;
+}
+
 int launch_elt(const EltArgs &a, cudaStream_t s) {
     int cout = a.mode == ELT_CONCAT ? a.c + a.c2 : a.c;
     bool vec = cout % 4 == 0 && a.c % 4 == 0 && (a.mode != ELT_CONCAT || a.c2 % 4 == 0);

@@ -15,14 +15,18 @@
 // so the S CTAs working on one tile do so at about the same time and all but
 // the first read it from L2. K advances 32 channels (one 128-byte swizzle
 // row of f32) per stage through a ring of `ns` stages:
-//   producer    fills a stage's A block (128 pixels x 32 k, 16 KB):
-//               pw_tc_kernel (1x1 layers) with one TMA copy from the packed
-//               input, whose pixels are the output's; conv_tc_kernel gathers
-//               it with cp.async, 16 bytes (or 4 when C % 4 != 0) at a time,
-//               zero-filling padded taps and the K tail and reading each of
-//               up to four sources nearest-upsampled by 2^shift in place;
+//   producer    one thread fills a stage's A block (128 pixels x 32 k,
+//               16 KB) with one TMA copy: for pw_tc_kernel (1x1 layers) from
+//               the packed input, whose pixels are the output's; for
+//               conv_tc_kernel (stride-1 windowed layers whose output keeps
+//               the input's size, C % 32 == 0) the block of tap (ky, kx) and
+//               channels c0..c0+31 is the 128 packed input pixels starting
+//               (ky - pt) * iw + kx - pl after the tile's first, each lane
+//               tiled on its own;
 //   converter   splits the block in place into its high half and a low-half
-//               twin (multiplying by the lane's SE gate first, if any);
+//               twin (multiplying by the lane's SE gate first, if any; for a
+//               windowed layer, zeroing the rows whose tap falls outside the
+//               image);
 //   MMA         one thread issues the MMAs into one of two TMEM accumulators
 //               and commits each stage back to the producer and each finished
 //               tile to the epilogue;
@@ -74,14 +78,10 @@ constexpr unsigned long long WAIT_LIMIT_NS = 200ull * 1000 * 1000;
 // many nanoseconds pass, instead of spinning on it.
 constexpr uint32_t SUSPEND_HINT_NS = 100000;
 
-// Warp roles. pw_tc_kernel: producer 0, MMA 1, converters 2-5, epilogue
-// 6-13. conv_tc_kernel: producers 0-3, MMA 4, converters 5-8, epilogue 9-16.
-struct PwRoles {
-    static constexpr int PROD_WARPS = 1, W_MMA = 1, W_CONV = 2, W_EPI = 6;
-    static constexpr int THREADS = (W_EPI + EPI_WARPS) * 32;
-};
-struct ConvRoles {
-    static constexpr int PROD_WARPS = 4, W_MMA = 4, W_CONV = 5, W_EPI = 9;
+// Warp roles of both kernels: producer 0, MMA 1, converters 2-5, epilogue
+// 6-13.
+struct Roles {
+    static constexpr int W_MMA = 1, W_CONV = 2, W_EPI = 6;
     static constexpr int THREADS = (W_EPI + EPI_WARPS) * 32;
 };
 
@@ -102,11 +102,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
     d |= uint64_t(2) << 61;
     return d;
 }
-
-// Byte offset of 16-byte chunk `c` (0..7) of row `r` in a 128B-swizzled,
-// K-major block whose rows are 128 bytes and whose base is 1024-aligned (the
-// layout TMA's 128-byte swizzle writes and the descriptor above reads).
-__device__ __forceinline__ uint32_t swz(int r, int c) { return uint32_t(r * 128 + ((c ^ (r & 7)) << 4)); }
 
 // Instruction descriptor of kind::tf32: D f32, A and B tf32, both K-major,
 // M = 128, N = n.
@@ -199,20 +194,6 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
-// Non-bulk asynchronous copies; `bytes` 0 writes zeros and reads nothing.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, uint32_t bytes) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
-}
-
-// Arrives on `bar` once this thread's earlier cp.async copies have landed.
-__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
-
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
     uint32_t r[16];
     asm volatile(
@@ -248,6 +229,38 @@ __device__ __forceinline__ void bias_act_stage(int act, const float v[16], const
 }
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+
+// Where tile t's 128 rows land: output pixels m0..m0+rows-1 of lane n,
+// from the lane's own pixel q0 on.
+struct TileInfo {
+    long m0, q0;
+    int rows, n;
+};
+
+__device__ __forceinline__ TileInfo tile_info(const TcArgs &a, long t) {
+    TileInfo ti;
+    if (!a.windowed) {
+        ti.m0 = ti.q0 = t * TM;
+        ti.rows = int(a.M - ti.m0 < TM ? a.M - ti.m0 : TM);
+        ti.n = 0;
+        return ti;
+    }
+    int lo = 0, hi = a.nl - 1;  // the last lane whose first tile is at most t
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (__ldg(&a.lanes[mid].tile0) <= t)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    const LaneInfo &L = a.lanes[lo];
+    ti.n = lo;
+    ti.q0 = (t - __ldg(&L.tile0)) * TM;
+    ti.m0 = __ldg(&L.pix0) + ti.q0;
+    const long left = long(__ldg(&L.oh)) * __ldg(&L.ow) - ti.q0;
+    ti.rows = int(left < TM ? left : TM);
+    return ti;
+}
 
 // What every role of one CTA shares.
 struct Ctx {
@@ -326,16 +339,33 @@ __device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
 // logical chunk is the same for all j.
 __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
     const int lc = (ct & 7) ^ ((ct >> 3) & 7);  // logical 16-byte chunk (4 k) of every row this thread holds
+    const int cblocks = a.C / TK;                // windowed: K blocks per tap
     long it = 0;
     bool ok = true;
     for (long t = x.first; t < x.tiles && ok; t += x.Q) {
-        int gl[8];  // the lane of each row, for the gate
+        int gl[8];          // the lane of each row, for the gate
+        int oy[8], ox[8];   // windowed: each row's output position (oy far negative past the lane's end)
+        int ih = 0, iw = 0;
         if (a.gate)
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 const long m = t * TM + (ct >> 3) + 16 * j;
                 gl[j] = m < a.M ? find_lane(a.lanes, a.nl, m) : -1;
             }
+        if (a.windowed) {
+            const TileInfo ti = tile_info(a, t);
+            const LaneInfo &L = a.lanes[ti.n];
+            const int ow = __ldg(&L.ow);
+            ih = __ldg(&L.ih);
+            iw = __ldg(&L.iw);
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int r = (ct >> 3) + 16 * j;
+                const int q = int(ti.q0) + r;
+                oy[j] = r < ti.rows ? q / ow : -(1 << 20);
+                ox[j] = r < ti.rows ? q - (q / ow) * ow : 0;
+            }
+        }
         for (int kb = 0; kb < x.nkb; kb++, it++) {
             const int s = int(it % x.ns);
             const long round = it / x.ns;
@@ -348,6 +378,12 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
             float4 *hi = reinterpret_cast<float4 *>(slot);
             float4 *lo = hi + A_BYTES / 16;
             const int k = kb * TK + lc * 4;
+            int dy = 0, dx = 0;
+            if (a.windowed) {
+                const int tap = kb / cblocks, ky = tap / a.kw;
+                dy = ky - a.pt;
+                dx = tap - ky * a.kw - a.pl;
+            }
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 const int i = ct + 128 * j;
@@ -358,6 +394,8 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
                         g = __ldg(reinterpret_cast<const float4 *>(a.gate + (long)gl[j] * a.K + k));
                     v = make_float4(fmul(v.x, g.x), fmul(v.y, g.y), fmul(v.z, g.z), fmul(v.w, g.w));
                 }
+                if (a.windowed && !((unsigned)(oy[j] + dy) < (unsigned)ih && (unsigned)(ox[j] + dx) < (unsigned)iw))
+                    v = make_float4(0.f, 0.f, 0.f, 0.f);
                 const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
                 hi[i] = h;
                 lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
@@ -383,7 +421,9 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
         __syncwarp();
         if (!__all_sync(0xffffffffu, ok)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const long mrow = t * TM + qd * 32;
+        const TileInfo ti = tile_info(a, t);
+        const long mrow = ti.m0 + qd * 32;
+        const int nrows = ti.rows - qd * 32;  // rows of this warp's quadrant that exist
         for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
             float v[16];
             tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);
@@ -394,8 +434,8 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
             if (n < a.N) {
 #pragma unroll 4
                 for (int i = sub; i < 32; i += 2) {
+                    if (i >= nrows) break;
                     const long m = mrow + i;
-                    if (m >= a.M) break;
                     float y = stg[i * 17 + col];
                     if (a.res) y = activate(a.act2, fadd(y, __ldg(a.res + m * a.N + n)));
                     a.y[m * a.N + n] = y;
@@ -406,46 +446,6 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         arrive(smem_u32(&x.acce[buf]));
     }
-}
-
-// One gathered row of a tile: its lane, top-left input tap and input size
-// (ihw = ih << 16 | iw; 0 past the last pixel).
-struct RowMeta {
-    int n, iy0, ix0, ihw;
-};
-
-__device__ __forceinline__ RowMeta row_meta(const TcArgs &a, long m) {
-    RowMeta r{0, 0, 0, 0};
-    if (m >= a.M) return r;
-    r.n = find_lane(a.lanes, a.nl, m);
-    const LaneInfo &L = a.lanes[r.n];
-    const int ow = __ldg(&L.ow);
-    const int q = int(m - __ldg(&L.pix0));
-    const int oy = q / ow, ox = q - oy * ow;
-    r.iy0 = oy * a.sh - a.pt;
-    r.ix0 = ox * a.sw - a.pl;
-    r.ihw = (__ldg(&L.ih) << 16) | __ldg(&L.iw);
-    return r;
-}
-
-// Where k of a gathered row reads (null for a zero: padding, the K tail, a
-// pixel past the end). With `vec`, k..k+3 lie in one tap and one source.
-__device__ __forceinline__ const float *locate(const TcArgs &a, const RowMeta &r, int k) {
-    if (r.ihw == 0 || k >= a.K) return nullptr;
-    const int tap = k / a.C, c = k - tap * a.C;
-    const int ky = tap / a.kw, kx = tap - ky * a.kw;
-    const int iy = r.iy0 + ky, ix = r.ix0 + kx;
-    const int ih = r.ihw >> 16, iw = r.ihw & 0xffff;
-    if (iy < 0 || iy >= ih || ix < 0 || ix >= iw) return nullptr;
-    int start = 0, s = 0;
-    while (s + 1 < a.nsrc && c >= start + a.src[s].c) {
-        start += a.src[s].c;
-        s++;
-    }
-    const ConvSource &src = a.src[s];
-    const int sh = src.shift;
-    const long pix = __ldg(&a.lanes[r.n].spix0[s]) + (long)(iy >> sh) * (iw >> sh) + (ix >> sh);
-    return src.p + pix * src.c + (c - start);
 }
 
 // Shared set-up of both kernels: barriers, bias slice, TMEM.
@@ -490,9 +490,9 @@ __device__ __forceinline__ void teardown(const TcArgs &a, const Ctx &x) {
     }
 }
 
-__global__ void __launch_bounds__(PwRoles::THREADS, 1)
+__global__ void __launch_bounds__(Roles::THREADS, 1)
     pw_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw) {
-    using R = PwRoles;
+    using R = Roles;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     __shared__ __align__(8) uint64_t full[MAX_NS], conv[MAX_NS], empty[MAX_NS], accf[2], acce[2], bfull;
@@ -555,9 +555,9 @@ __global__ void __launch_bounds__(PwRoles::THREADS, 1)
     teardown<R>(a, x);
 }
 
-__global__ void __launch_bounds__(ConvRoles::THREADS, 1)
-    conv_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmw) {
-    using R = ConvRoles;
+__global__ void __launch_bounds__(Roles::THREADS, 1)
+    conv_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw) {
+    using R = Roles;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     __shared__ __align__(8) uint64_t full[MAX_NS], conv[MAX_NS], empty[MAX_NS], accf[2], acce[2], bfull;
@@ -569,7 +569,7 @@ __global__ void __launch_bounds__(ConvRoles::THREADS, 1)
     x.Q = gridDim.x / a.slices;
     x.first = blockIdx.x / a.slices;
     x.n0 = int(blockIdx.x % a.slices) * a.bn;
-    x.tiles = (a.M + TM - 1) / TM;
+    x.tiles = a.tiles;
     x.ring = smem_u32(smem);
     x.b_bytes = uint32_t(a.bn) * 128;
     x.stage_bytes = SLOT_BYTES + 2 * x.b_bytes;
@@ -578,61 +578,41 @@ __global__ void __launch_bounds__(ConvRoles::THREADS, 1)
     x.abort_flag = &abort_s;
     float *staging = reinterpret_cast<float *>(smem + size_t(x.ns) * x.stage_bytes);
     float *bias_s = staging + EPI_WARPS * STAGE_FLOATS;
-    // a stage is full once the 128 gathering threads' copies and the weight
-    // block's bytes have landed
-    setup<R>(a, x, 128 + 1, &bfull, bias_s, &tmem_base_s, &abort_s);
+    setup<R>(a, x, 1, &bfull, bias_s, &tmem_base_s, &abort_s);
 
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-    if (warp < R::PROD_WARPS) {
-        // Gather: thread g copies the 16-byte chunk g & 7 of rows
-        // (g >> 3) + 16 j, j = 0..7, into its swizzled place.
-        const int g = tid, cc = g & 7, r0 = g >> 3;
-        const bool vec = a.vec4 != 0;
-        long it = 0;
-        bool ok = true;
-        for (long t = x.first; t < x.tiles && ok; t += x.Q) {
-            RowMeta rm[8];
-#pragma unroll
-            for (int j = 0; j < 8; j++) rm[j] = row_meta(a, t * TM + r0 + 16 * j);
-            for (int kb = 0; kb < x.nkb; kb++, it++) {
-                const int s = int(it % x.ns);
-                const long round = it / x.ns;
-                if (round > 0 && !wait_phase(smem_u32(&empty[s]), uint32_t(round - 1) & 1u, x.abort_flag, a.err)) {
-                    ok = false;
-                    break;
-                }
-                // the tensor core's reads of this stage are ordered before
-                // the new writes
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                const uint32_t stage = x.ring + uint32_t(s) * x.stage_bytes;
-                if (g == 0) {
-                    arrive_expect(smem_u32(&full[s]), 2 * x.b_bytes);
-                    tma_load_3d(stage + SLOT_BYTES, &tmw, kb * TK, x.n0, 0, smem_u32(&full[s]));
-                    tma_load_3d(stage + SLOT_BYTES + x.b_bytes, &tmw, kb * TK, x.n0, 1, smem_u32(&full[s]));
-                }
-                const int k = kb * TK + cc * 4;
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    const int r = r0 + 16 * j;
-                    const uint32_t dst = stage + swz(r, cc);
-                    if (vec) {
-                        const float *src = locate(a, rm[j], k);
-                        cp_async16(dst, src ? src : a.y, src ? 16u : 0u);
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const float *src = locate(a, rm[j], k + e);
-                            cp_async4(dst + 4 * e, src ? src : a.y, src ? 4u : 0u);
-                        }
+    if (warp == 0) {
+        if (lane == 0) {
+            const int cblocks = a.C / TK;
+            long it = 0;
+            bool ok = true;
+            for (long t = x.first; t < x.tiles && ok; t += x.Q) {
+                const TileInfo ti = tile_info(a, t);
+                const LaneInfo &L = a.lanes[ti.n];
+                const long base = __ldg(&L.ipix0) + ti.q0;
+                const int iw = __ldg(&L.iw);
+                for (int kb = 0; kb < x.nkb; kb++, it++) {
+                    const int s = int(it % x.ns);
+                    const long round = it / x.ns;
+                    if (round > 0 && !wait_phase(smem_u32(&empty[s]), uint32_t(round - 1) & 1u, x.abort_flag, a.err)) {
+                        ok = false;
+                        break;
                     }
+                    const int tap = kb / cblocks, ky = tap / a.kw, kx = tap - ky * a.kw;
+                    const int c0 = (kb - tap * cblocks) * TK;
+                    // rows before the first pixel or past the last read as
+                    // zeros; rows of another lane are zeroed by the converters
+                    const long y = base + long(ky - a.pt) * iw + (kx - a.pl);
+                    const uint32_t stage = x.ring + uint32_t(s) * x.stage_bytes;
+                    const uint32_t bar = smem_u32(&full[s]);
+                    arrive_expect(bar, A_BYTES + 2 * x.b_bytes);
+                    tma_load_2d(stage, &tmx, c0, int(y), bar);
+                    tma_load_3d(stage + SLOT_BYTES, &tmw, kb * TK, x.n0, 0, bar);
+                    tma_load_3d(stage + SLOT_BYTES + x.b_bytes, &tmw, kb * TK, x.n0, 1, bar);
                 }
-                cp_async_arrive(smem_u32(&full[s]));
             }
-        }
-        if (*x.abort_flag) {
-            // the copies still in flight land before the CTA leaves
-            asm volatile("cp.async.wait_all;" ::: "memory");
-            if (g == 0)
+            if (*x.abort_flag)
+                // the copies still in flight land before the CTA leaves
                 for (int s = 0; s < x.ns && s < it; s++)
                     drain(smem_u32(&full[s]), uint32_t((it - 1 - s) / x.ns) & 1u);
         }
@@ -682,7 +662,7 @@ int pw_slice_width(int K, int N) {
     return 0;
 }
 
-// The gathered kernel streams its weights, so a slice is as wide as a
+// The windowed kernel streams its weights, so a slice is as wide as a
 // four-stage ring allows (at most 128).
 int conv_slice_width(int N) {
     for (int S = 1; S <= (N + 31) / 32; S++) {
@@ -713,7 +693,7 @@ bool set_grid(TcArgs &a) {
     if (cudaGetDevice(&dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
         return false;
-    const long tiles = (a.M + TM - 1) / TM;
+    const long tiles = a.windowed ? a.tiles : (a.M + TM - 1) / TM;
     const long q = std::max(1L, std::min(long(sms / a.slices), tiles));
     a.grid = int(q) * a.slices;
     a.tmem_cols = 32;
@@ -734,31 +714,20 @@ bool tc_prepare(TcArgs &a) {
     EncodeTiled enc = encode_tiled();
     if (!enc) return false;
     a.nkb = a.kpad / TK;
-    if (!a.gather) {
-        // 1x1, one source: one TMA copy per A block
-        if (a.K % 4 || !aligned(a.x) || (a.gate && !aligned(a.gate))) return false;
+    if (a.C % 4 || !aligned(a.x) || (a.gate && !aligned(a.gate))) return false;
+    if (!a.windowed) {
+        // 1x1: the packed input is [M][K]
+        if (a.K != a.C) return false;
         a.bn = pw_slice_width(a.K, a.N);
         if (!a.bn) return false;
         a.slices = (a.N + a.bn - 1) / a.bn;
         a.ns = 2;
         while (a.ns < MAX_NS && pw_smem(a.kpad, a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
         a.smem = int(pw_smem(a.kpad, a.bn, a.ns));
-        CUtensorMap mx;
-        // pixels: [M][K], boxes of 32 channels x 128 pixels; channels past K
-        // and pixels past M read as zeros
-        cuuint64_t dims[2] = {cuuint64_t(a.K), cuuint64_t(a.M)};
-        cuuint64_t strides[1] = {cuuint64_t(a.K) * 4};
-        cuuint32_t box[2] = {TK, TM}, estr[2] = {1, 1};
-        if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.x), dims, strides, box, estr,
-                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return false;
-        std::memcpy(a.tmx, &mx, sizeof mx);
     } else {
-        if (a.gate || a.nsrc < 1 || a.C < 1 || a.K != a.kh * a.kw * a.C) return false;
-        a.vec4 = a.C % 4 == 0;
-        for (int s = 0; s < a.nsrc; s++)
-            if (a.src[s].c % 4 || !aligned(a.src[s].p)) a.vec4 = 0;
+        // a tap's K blocks never straddle taps; the output keeps the input's
+        // size, so the packed input has M pixels too
+        if (a.gate || a.C % TK || a.K != a.kh * a.kw * a.C || a.tiles < 1) return false;
         a.bn = conv_slice_width(a.N);
         if (!a.bn) return false;
         a.slices = (a.N + a.bn - 1) / a.bn;
@@ -766,6 +735,17 @@ bool tc_prepare(TcArgs &a) {
         while (a.ns < MAX_NS && conv_smem(a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
         a.smem = int(conv_smem(a.bn, a.ns));
     }
+    // pixels: [M][C], boxes of 32 channels x 128 pixels; channels past C and
+    // pixels outside the buffer read as zeros
+    CUtensorMap mx;
+    cuuint64_t dims[2] = {cuuint64_t(a.C), cuuint64_t(a.M)};
+    cuuint64_t strides[1] = {cuuint64_t(a.C) * 4};
+    cuuint32_t box[2] = {TK, TM}, estr[2] = {1, 1};
+    if (enc(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(a.x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    std::memcpy(a.tmx, &mx, sizeof mx);
     return encode_weights(a, enc) && set_grid(a);
 }
 
@@ -777,13 +757,12 @@ void configure_tc_kernels() {
 int launch_tc(const TcArgs &a, cudaStream_t s) {
     CUtensorMap mw;
     std::memcpy(&mw, a.tmw, sizeof mw);
-    if (a.gather) {
-        conv_tc_kernel<<<a.grid, ConvRoles::THREADS, a.smem, s>>>(a, mw);
-    } else {
-        CUtensorMap mx;
-        std::memcpy(&mx, a.tmx, sizeof mx);
-        pw_tc_kernel<<<a.grid, PwRoles::THREADS, a.smem, s>>>(a, mx, mw);
-    }
+    CUtensorMap mx;
+    std::memcpy(&mx, a.tmx, sizeof mx);
+    if (a.windowed)
+        conv_tc_kernel<<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
+    else
+        pw_tc_kernel<<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
     return 1;
 }
 

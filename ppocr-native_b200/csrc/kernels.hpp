@@ -38,6 +38,7 @@ struct LaneInfo {
     long pix0;                // first output pixel
     long ipix0;               // first input pixel
     long spix0[MAX_SOURCES];  // first pixel in each conv source / the second input
+    long tile0;               // first 128-pixel output tile when every lane is tiled on its own
     int ih, iw, oh, ow;
 };
 
@@ -191,15 +192,18 @@ struct ConvTArgs {
 // Pointwise convolution on the tensor cores (k_tc.cu), 3xTF32: weights
 // pre-split and transposed to [n][kpad] (K-major, zero-padded to 32
 // channels and to whole BN tiles of output channels).
-// A convolution on the tensor cores (3xTF32). Pointwise layers (1x1, unit
-// stride, one source) read their input with TMA (`gather` false); the rest
-// gather it like ConvArgs' sources.
+// A convolution on the tensor cores (3xTF32), its input read with TMA.
+// Pointwise layers (1x1, unit stride) take 128 packed pixels per tile.
+// Windowed ones (`windowed`: unit stride, output the input's size, C % 32
+// == 0) tile each lane on its own, so that a tap's 128 input pixels are 128
+// consecutive packed pixels shifted by (ky - pt) * iw + kx - pl; the rows
+// that fall outside the image read as zeros.
 struct TcArgs {
-    bool gather = false;
-    const float *x = nullptr;     // pointwise: [M][K], 16-byte aligned, K % 4 == 0
-    ConvSource src[MAX_SOURCES];  // gathered: up to four sources, nearest-upsampled by 2^shift
-    int nsrc = 0, C = 0;
-    int kh = 1, kw = 1, sh = 1, sw = 1, pt = 0, pl = 0;
+    bool windowed = false;
+    const float *x = nullptr;     // [pixels][C], 16-byte aligned, C % 4 == 0
+    long tiles = 0;               // windowed: 128-pixel tiles of all lanes, each lane on its own
+    int C = 0;
+    int kh = 1, kw = 1, pt = 0, pl = 0;
     const LaneInfo *lanes = nullptr;
     int nl = 1;
     const float *gate = nullptr;  // pointwise: [lanes][K], x of lane n scaled by gate[n] first
@@ -213,13 +217,26 @@ struct TcArgs {
     int act = 0, act2 = 0;
     int *err = nullptr;           // set to nonzero when a bounded wait gave up
     // filled by tc_prepare: output-channel slice width and count, K blocks,
-    // ring stages, TMEM columns, grid, dynamic shared memory, 16-byte
-    // gathers, and the tensor maps (CUtensorMap, 128 bytes each) of the
-    // pointwise input and of the weights
-    int bn = 0, slices = 0, nkb = 0, ns = 0, tmem_cols = 0, grid = 0, smem = 0, vec4 = 0;
+    // ring stages, TMEM columns, grid, dynamic shared memory, and the tensor
+    // maps (CUtensorMap, 128 bytes each) of the input and of the weights
+    int bn = 0, slices = 0, nkb = 0, ns = 0, tmem_cols = 0, grid = 0, smem = 0;
     unsigned long long tmx[16] = {}, tmw[16] = {};
 };
 int launch_tc(const TcArgs &a, cudaStream_t s);
+
+// The input a multi-source convolution reads, written out: per pixel of the
+// conv's input size, the sources' channels side by side, each source read
+// nearest-upsampled by 2^shift (a copy, so any layer reading it sees the
+// same values the fused reads would).
+struct GatherArgs {
+    ConvSource src[MAX_SOURCES];
+    int nsrc = 1, C = 0;
+    const LaneInfo *lanes = nullptr;  // the conv's: ipix0, spix0, ih, iw
+    int nl = 1;
+    long M = 0;                       // input pixels of all lanes
+    float *y = nullptr;               // [M][C]
+};
+int launch_gather(const GatherArgs &a, cudaStream_t s);
 // Whether a K x N layer gets split tensor-core weights at load.
 bool tc_weights_wanted(int K, int N);
 // The padded K of the prepared weights (a multiple of 32).

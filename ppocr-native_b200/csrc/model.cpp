@@ -358,6 +358,7 @@ struct Group {
     std::vector<size_t> out_floats;     // per output: all lanes
     std::vector<std::unique_ptr<DeviceBuffer>> slots;
     DeviceBuffer mean_scratch, ctc_scratch, lane_tables;
+    DeviceBuffer concat_scratch;  // a multi-source conv's input, written out for the tensor cores
     HostBuffer in_host;
     std::vector<std::unique_ptr<HostBuffer>> out_host;
     std::vector<std::function<int(cudaStream_t)>> launches;
@@ -438,12 +439,14 @@ namespace {
 // shifts of a dense convolution's inputs (pixel prefix sums per source).
 std::vector<LaneInfo> lane_table(const Group &g, size_t i, const std::vector<int> &shifts) {
     std::vector<LaneInfo> t(g.count());
-    long pix = 0, ipix = 0, spix[MAX_SOURCES] = {0, 0, 0, 0};
+    long pix = 0, ipix = 0, spix[MAX_SOURCES] = {0, 0, 0, 0}, tile = 0;
     for (size_t n = 0; n < g.count(); n++) {
         const Op &op = g.lane(n).ops[i];
         LaneInfo &L = t[n];
         L.pix0 = pix;
         L.ipix0 = ipix;
+        L.tile0 = tile;
+        tile += (long(op.oh * op.ow) + 127) / 128;
         for (int s = 0; s < MAX_SOURCES; s++) L.spix0[s] = spix[s];
         L.ih = int(op.ih); L.iw = int(op.iw); L.oh = int(op.oh); L.ow = int(op.ow);
         pix += long(op.oh * op.ow);
@@ -452,6 +455,13 @@ std::vector<LaneInfo> lane_table(const Group &g, size_t i, const std::vector<int
             spix[s] += long(op.ih >> shifts[s]) * long(op.iw >> shifts[s]);
     }
     return t;
+}
+
+// A stride-1 conv whose output keeps its input's size (padding kh - 1 and
+// kw - 1 in all): within a lane, each tap reads the input shifted by a
+// constant number of packed pixels.
+bool tc_windowed(const Op &op) {
+    return op.kind == K_CONV && op.sh == 1 && op.sw == 1 && op.pt + op.pb == op.kh - 1 && op.pl + op.pr == op.kw - 1;
 }
 
 long total_out(const Group &g, size_t i) {
@@ -521,6 +531,27 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             ctc_floats = std::max(ctc_floats, size_t(total_in(g, i)) * ctc_col_blocks(int(cols)) * 3);
         }
     }
+    // A windowed conv of several sources (or upsampled ones) on the tensor
+    // cores reads them written out side by side.
+    const bool tc_allowed = !(options & PPOCR_OPT_NO_TENSOR_CORES);
+    size_t concat_floats = 0;
+    if (tc_allowed)
+        for (const Step &st : steps) {
+            if (st.kind == S_SKIP) continue;
+            const size_t i = st.kind == S_CONV ? st.b : st.a;
+            const Op &op = p0.ops[i];
+            bool multi = op.kind == K_CONV && op.n2 > 0;
+            if (st.kind == S_CONV) multi = st.srcs.size() > 1 || (!st.srcs.empty() && st.srcs[0].shift);
+            if (multi && tc_windowed(op) && weights->tc_hi(i))
+                concat_floats = std::max(concat_floats, size_t(total_in(g, i)) * (op.ic + op.n2));
+        }
+    if (concat_floats) {
+        g.concat_scratch.bytes = concat_floats * sizeof(float);
+        if (!cuda_ok(cudaMalloc(&g.concat_scratch.p, g.concat_scratch.bytes), "allocating scratch", &code)) {
+            err = g_error;
+            return code;
+        }
+    }
     g.mean_scratch.bytes = mean_doubles * sizeof(double);
     g.ctc_scratch.bytes = ctc_floats * sizeof(float);
     if (!cuda_ok(cudaMalloc(&g.mean_scratch.p, g.mean_scratch.bytes), "allocating scratch", &code) ||
@@ -577,7 +608,6 @@ int ppocr_model::build_group(Group &g, std::string &err) {
     const Weights &W = *weights;
     const int nl = int(N);
     auto buf = [&g](size_t s) { return g.slot_ptr(s); };
-    const bool tc_allowed = !(options & PPOCR_OPT_NO_TENSOR_CORES);
     int *errp = err_dev;
     // A pointwise conv as the tensor-core kernel's arguments, when it goes
     // there. The choice depends on the layer alone, never on how many
@@ -595,26 +625,59 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             writer[op.y] = int(i);
         }
     }
-    auto tc_route = [&](size_t i, const ConvArgs &c, TcArgs &t) {
-        if (!tc_allowed || !W.tc_hi(i) || reads_mean[i]) return false;
-        const bool pw = c.nsrc == 1 && !c.src[0].shift && c.kh == 1 && c.kw == 1 && c.sh == 1 && c.sw == 1 &&
-                        !c.pt && !c.pl;
-        if (!pw) return false;
-        t.gather = !pw;
+    // 0: not on the tensor cores; 1: there; 2: there, after the sources are
+    // written out side by side (`gather`).
+    auto tc_route = [&](size_t i, const ConvArgs &c, const LaneInfo *Lh, TcArgs &t, GatherArgs &gather) {
+        if (!tc_allowed || !W.tc_hi(i) || reads_mean[i]) return 0;
+        const Op &op = p0.ops[i];
+        const bool one = c.nsrc == 1 && !c.src[0].shift;
+        const bool pw = one && c.kh == 1 && c.kw == 1 && c.sh == 1 && c.sw == 1 && !c.pt && !c.pl;
+        if (!pw && (c.gate || !tc_windowed(op) || c.C % 32)) return 0;
+        t.windowed = !pw;
         t.x = c.src[0].p;
-        for (int q = 0; q < c.nsrc; q++) t.src[q] = c.src[q];
-        t.nsrc = c.nsrc; t.C = c.C;
-        t.kh = c.kh; t.kw = c.kw; t.sh = c.sh; t.sw = c.sw; t.pt = c.pt; t.pl = c.pl;
+        if (!pw && !one) {
+            gather = GatherArgs();
+            for (int q = 0; q < c.nsrc; q++) {
+                gather.src[q] = c.src[q];
+                if (c.src[q].c % 4) return 0;
+            }
+            gather.nsrc = c.nsrc; gather.C = c.C; gather.lanes = c.lanes; gather.nl = c.nl;
+            gather.M = c.M;  // the output keeps the input's size
+            gather.y = static_cast<float *>(g.concat_scratch.p);
+            if (!gather.y || size_t(c.M) * c.C * sizeof(float) > g.concat_scratch.bytes) return 0;
+            t.x = gather.y;
+        }
+        t.C = c.C;
+        t.kh = c.kh; t.kw = c.kw; t.pt = c.pt; t.pl = c.pl;
         t.lanes = c.lanes; t.nl = c.nl; t.gate = c.gate;
+        t.tiles = Lh[c.nl - 1].tile0 + (long(Lh[c.nl - 1].oh) * Lh[c.nl - 1].ow + 127) / 128;
         t.w_hi = W.tc_hi(i); t.w_lo = W.tc_lo(i); t.b = c.b; t.res = c.res; t.y = c.y;
         t.M = c.M; t.K = c.kh * c.kw * c.C; t.N = c.oc; t.kpad = W.tc_kpad[i];
         t.act = c.act; t.act2 = c.act2; t.err = errp;
-        return tc_prepare(t);
+        if (!tc_prepare(t)) return 0;
+        return (!pw && !one) ? 2 : 1;
+    };
+    // Pushes a dense conv's launch: the tensor cores where the layer goes
+    // there, else the FP32 implicit GEMM; `pre` runs first (a depthwise
+    // layer whose output it reads, or nothing).
+    auto push_conv = [&](size_t i, const ConvArgs &c, const LaneInfo *Lh, std::function<int(cudaStream_t)> pre) {
+        TcArgs t;
+        GatherArgs ga;
+        const int route = tc_route(i, c, Lh, t, ga);
+        if (route == 2)
+            g.launches.push_back([pre, ga, t](cudaStream_t s) {
+                return (pre ? pre(s) : 0) + launch_gather(ga, s) + launch_tc(t, s);
+            });
+        else if (route == 1)
+            g.launches.push_back([pre, t](cudaStream_t s) { return (pre ? pre(s) : 0) + launch_tc(t, s); });
+        else
+            g.launches.push_back([pre, c](cudaStream_t s) { return (pre ? pre(s) : 0) + launch_conv(c, s); });
     };
     for (size_t k = 0; k < steps.size(); k++) {
         const Step &st = steps[k];
         if (st.kind == S_SKIP) continue;
         const LaneInfo *L = lt + table_at[k];
+        const LaneInfo *Lh = tables.data() + table_at[k];  // the same table on the host
         if (st.kind == S_DW_PW) {
             const Op &dw = p0.ops[st.a], &pw = p0.ops[st.b];
             DwPwArgs a;
@@ -651,11 +714,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             c.act = a.act2; c.bias_mode = a.bias_mode2;
             c.res = a.res; c.act2 = a.act3;
             c.y = a.y;
-            TcArgs t;
-            if (tc_route(st.b, c, t))
-                g.launches.push_back([d, t](cudaStream_t s) { return launch_dw(d, s) + launch_tc(t, s); });
-            else
-                g.launches.push_back([d, c](cudaStream_t s) { return launch_dw(d, s) + launch_conv(c, s); });
+            push_conv(st.b, c, Lh, [d](cudaStream_t s) { return launch_dw(d, s); });
             continue;
         }
         if (st.kind == S_CONV) {
@@ -683,11 +742,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
                 a.act2 = add.fused;
                 a.y = buf(add.y);
             }
-            TcArgs t;
-            if (tc_route(st.b, a, t))
-                g.launches.push_back([t](cudaStream_t s) { return launch_tc(t, s); });
-            else
-                g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
+            push_conv(st.b, a, Lh, nullptr);
             continue;
         }
         if (st.kind == S_GATE_ADD) {
@@ -714,11 +769,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
             a.pt = int(op.pt); a.pl = int(op.pl); a.act = op.fused; a.bias_mode = bias_mode(op);
             a.y = buf(op.y);
-            TcArgs t;
-            if (tc_route(i, a, t))
-                g.launches.push_back([t](cudaStream_t s) { return launch_tc(t, s); });
-            else
-                g.launches.push_back([a](cudaStream_t s) { return launch_conv(a, s); });
+            push_conv(i, a, Lh, nullptr);
             break;
         }
         case K_DWCONV: {

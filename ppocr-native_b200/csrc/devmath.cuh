@@ -39,14 +39,24 @@ __device__ __forceinline__ float exp_neg(float z) {
     return z < __uint_as_float(0xc2aeac4fu) ? 0.0f : e;
 }
 
+// A quotient: IEEE-rounded, or (QUICK) __fdividef's reciprocal and product,
+// within 2 ulp, for callers whose sums already differ from the reference's
+// by a few units and whose denominators lie in [1, 2^20].
+template <bool QUICK>
+__device__ __forceinline__ float quot(float a, float b) {
+    return QUICK ? __fdividef(a, b) : fdiv(a, b);
+}
+
 // activation.rs:151-159: e / (e + 1) for negative x, 1 minus it otherwise.
+template <bool QUICK = false>
 __device__ __forceinline__ float sigmoid_one(float x) {
     float e = exp_neg(__uint_as_float(__float_as_uint(x) | 0x80000000u));
-    float f = fdiv(e, fadd(e, 1.0f));
+    float f = quot<QUICK>(e, fadd(e, 1.0f));
     return (__float_as_uint(x) >> 31) ? f : fsub(1.0f, f);
 }
 
 // layers.rs:49-67: x * Phi(x) with the reference's rational fit.
+template <bool QUICK = false>
 __device__ __forceinline__ float gelu_one(float x) {
     float c = clampf_(x, -5.5f, 5.5f);
     float s = fmul(c, c);
@@ -62,18 +72,19 @@ __device__ __forceinline__ float gelu_one(float x) {
     q = ffma(q, s, __uint_as_float(0x3ceaaaeeu));
     q = ffma(q, s, __uint_as_float(0x3e80c788u));
     q = ffma(q, s, 1.0f);
-    return fmul(x, clampf_(ffma(c, fdiv(p, q), 0.5f), 0.0f, 1.0f));
+    return fmul(x, clampf_(ffma(c, quot<QUICK>(p, q), 0.5f), 0.0f, 1.0f));
 }
 
 // The folded activation of `code` (reference conv.rs:36-72; code 7 is this
 // library's hardswish, x * hardsigmoid(x)).
+template <bool QUICK = false>
 __device__ __forceinline__ float activate(int code, float v) {
     const float alpha = __uint_as_float(0x3e2aaaadu);  // layers.rs:42
     switch (code) {
     case 1: return clampf_(v, 0.0f, __int_as_float(0x7f800000));
-    case 2: return sigmoid_one(v);
-    case 3: return gelu_one(v);
-    case 4: return fmul(v, sigmoid_one(v));
+    case 2: return sigmoid_one<QUICK>(v);
+    case 3: return gelu_one<QUICK>(v);
+    case 4: return fmul(v, sigmoid_one<QUICK>(v));
     case 5: return clampf_(fadd(fmul(v, alpha), 0.5f), 0.0f, 1.0f);
     case 6: return clampf_(fadd(fmul(v, 0.2f), 0.5f), 0.0f, 1.0f);
     case 7: return fmul(v, clampf_(fadd(fmul(v, alpha), 0.5f), 0.0f, 1.0f));
@@ -82,9 +93,9 @@ __device__ __forceinline__ float activate(int code, float v) {
 }
 
 // The same with the code known at compile time, for hot epilogues.
-template <int CODE>
+template <int CODE, bool QUICK = false>
 __device__ __forceinline__ float activate_t(float v) {
-    return activate(CODE, v);
+    return activate<QUICK>(CODE, v);
 }
 
 }  // namespace ppocr

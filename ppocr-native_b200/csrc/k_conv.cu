@@ -298,6 +298,50 @@ __global__ void __launch_bounds__(TX *TY, 65536 / (TX * TY * 128)) conv_gemm(con
     }
 }
 
+// A pointwise layer over per-lane vectors (a squeeze-and-excite branch: one
+// pixel per lane). Block b takes output channels 32b..32b+31 of every pixel:
+// its threads first copy that weight slice and the (gated) input vectors to
+// shared memory together, many loads in flight, then each output is one
+// thread's chain of k terms added in increasing k with one fused
+// multiply-add each, from the bias or from zero, as conv_gemm's accumulators
+// do, so the two give the same bits.
+constexpr int VEC_COLS = 32;
+
+__global__ void __launch_bounds__(256) conv_vector_kernel(const ConvArgs a) {
+    extern __shared__ float vsm[];
+    float *ws = vsm;                   // [C][32]
+    float *xs = vsm + a.C * VEC_COLS;  // [M][C]
+    const int n0 = blockIdx.x * VEC_COLS;
+    const int cols = min(VEC_COLS, a.oc - n0);
+    for (int e = threadIdx.x; e < a.C * VEC_COLS; e += blockDim.x) {
+        const int k = e / VEC_COLS, j = e - k * VEC_COLS;
+        ws[e] = j < cols ? __ldg(a.w + (long)k * a.oc + n0 + j) : 0.0f;
+    }
+    const float *x = a.src[0].p;
+    for (long e = threadIdx.x; e < a.M * a.C; e += blockDim.x) {
+        const long m = e / a.C;
+        const int k = int(e - m * a.C);
+        float v = __ldg(x + e);
+        if (a.gate) v = fmul(v, __ldg(a.gate + (long)find_lane(a.lanes, a.nl, m) * a.C + k));
+        xs[e] = v;
+    }
+    __syncthreads();
+    for (long e = threadIdx.x; e < a.M * VEC_COLS; e += blockDim.x) {
+        const long m = e / VEC_COLS;
+        const int j = int(e - m * VEC_COLS);
+        if (j >= cols) continue;
+        const int n = n0 + j;
+        const bool first = a.bias_mode == BIAS_FIRST;
+        float acc = (first && a.b) ? __ldg(a.b + n) : 0.0f;
+        const float *xm = xs + m * a.C;
+        for (int k = 0; k < a.C; k++) acc = ffma(ws[k * VEC_COLS + j], xm[k], acc);
+        if (!first && a.b) acc = fadd(acc, __ldg(a.b + n));
+        acc = activate(a.act, acc);
+        if (a.res) acc = activate(a.act2, fadd(acc, __ldg(a.res + m * a.oc + n)));
+        a.y[m * a.oc + n] = acc;
+    }
+}
+
 template <int TM, int TN, int TX, int TY, int BK>
 int run(const ConvArgs &a, cudaStream_t s, bool vec4, bool pw) {
     using C = Cfg<TM, TN, TX, TY, BK>;
@@ -329,6 +373,7 @@ constexpr long SMALL_M = 148L * 2 * 128;
 }  // namespace
 
 void configure_conv_kernels() {
+    cudaFuncSetAttribute(conv_vector_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     allow<8, 8, 16, 16, 8>();
     allow<4, 8, 16, 16, 16>();
     allow<8, 6, 16, 16, 8>();
@@ -368,6 +413,15 @@ int launch_conv(const ConvArgs &a, cudaStream_t s) {
     if (oc <= 16) return run<4, 4, 4, 64, 16>(a, s, vec4, pw);
     if (oc <= 32) return run<4, 4, 8, 32, 16>(a, s, vec4, pw);
     return run<8, 4, 16, 16, 8>(a, s, vec4, pw);
+}
+
+size_t conv_vector_smem(const ConvArgs &a) { return sizeof(float) * size_t(a.C) * (VEC_COLS + size_t(a.M)); }
+
+bool conv_vector_supported(const ConvArgs &a) { return conv_vector_smem(a) <= 200 * 1024; }
+
+int launch_conv_vector(const ConvArgs &a, cudaStream_t s) {
+    conv_vector_kernel<<<unsigned((a.oc + VEC_COLS - 1) / VEC_COLS), 256, conv_vector_smem(a), s>>>(a);
+    return 1;
 }
 
 }  // namespace ppocr

@@ -65,7 +65,7 @@ constexpr int TK = 32;                    // k per block: one 128-byte swizzle r
 constexpr int A_BYTES = TM * 128;         // one half of an A block
 constexpr int SLOT_BYTES = 2 * A_BYTES;   // high half (the copy lands here) + low half
 constexpr int EPI_WARPS = 8;
-constexpr int STAGE_FLOATS = 32 * 17;     // one epilogue warp's 32 x 16 transpose tile, padded
+constexpr int STAGE_FLOATS = 32 * 16;     // one epilogue warp's 32 x 16 transpose tile (swizzled)
 constexpr int EPI_BYTES = EPI_WARPS * STAGE_FLOATS * 4 + 256 * 4;  // + the bias slice
 constexpr int MAX_NS = 6;
 // Dynamic shared memory per CTA: the block's limit (227 KB) less room for the
@@ -206,26 +206,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// Bias and activation over one thread's 16 accumulators, staged for the
-// transpose; the activation code is a template argument so the loop holds
-// no branch.
-template <int ACT>
-__device__ __forceinline__ void bias_act_stage(const float v[16], const float *bias, float *row) {
-#pragma unroll
-    for (int j = 0; j < 16; j++) row[j] = activate_t<ACT>(fadd(v[j], bias[j]));
+__device__ __forceinline__ float4 lds4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
 }
 
-__device__ __forceinline__ void bias_act_stage(int act, const float v[16], const float *bias, float *row) {
-    switch (act) {
-    case 1: bias_act_stage<1>(v, bias, row); break;
-    case 2: bias_act_stage<2>(v, bias, row); break;
-    case 3: bias_act_stage<3>(v, bias, row); break;
-    case 4: bias_act_stage<4>(v, bias, row); break;
-    case 5: bias_act_stage<5>(v, bias, row); break;
-    case 6: bias_act_stage<6>(v, bias, row); break;
-    case 7: bias_act_stage<7>(v, bias, row); break;
-    default: bias_act_stage<0>(v, bias, row); break;
-    }
+__device__ __forceinline__ void sts4(uint32_t addr, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
 }
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
@@ -373,10 +362,7 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
                 ok = false;
                 break;
             }
-            unsigned char *slot = reinterpret_cast<unsigned char *>(__cvta_shared_to_generic(x.ring)) +
-                                  size_t(s) * x.stage_bytes;
-            float4 *hi = reinterpret_cast<float4 *>(slot);
-            float4 *lo = hi + A_BYTES / 16;
+            const uint32_t hi = x.ring + uint32_t(s) * x.stage_bytes, lo = hi + A_BYTES;
             const int k = kb * TK + lc * 4;
             int dy = 0, dx = 0;
             if (a.windowed) {
@@ -386,8 +372,8 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
             }
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-                const int i = ct + 128 * j;
-                float4 v = hi[i];
+                const uint32_t off = uint32_t(ct + 128 * j) * 16;
+                float4 v = lds4(hi + off);
                 if (a.gate) {
                     float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (gl[j] >= 0 && k < a.K)
@@ -397,8 +383,8 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
                 if (a.windowed && !((unsigned)(oy[j] + dy) < (unsigned)ih && (unsigned)(ox[j] + dx) < (unsigned)iw))
                     v = make_float4(0.f, 0.f, 0.f, 0.f);
                 const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-                hi[i] = h;
-                lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+                sts4(hi + off, h);
+                sts4(lo + off, make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w));
             }
             // make the generic-proxy stores visible to the tensor core
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -407,13 +393,20 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
     }
 }
 
-// The epilogue warps (e = 0..7 among them).
-__device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, int lane, float *staging,
+// The epilogue warps (e = 0..7 among them). The sums already differ from the
+// FP32 ones by a few units, so the activations take the quick quotient.
+// Each thread holds one TMEM lane
+// (one pixel) of 16 columns; it stages them as four 16-byte chunks of its row
+// (chunk q at q ^ ((row >> 1) & 3), so that eight lanes cover all 32 banks),
+// and the warp then writes 8 rows x 64 bytes per store.
+template <int ACT>
+__device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, int lane, uint32_t staging,
                               const float *bias_s) {
     const int qd = warp & 3;  // the TMEM lane quadrant this warp may read
     const int half = e / 4;   // which alternate 16-column chunks it takes
-    float *stg = staging + e * STAGE_FLOATS;
-    const int col = lane & 15, sub = lane >> 4;
+    const uint32_t stg = staging + uint32_t(e * STAGE_FLOATS * 4);
+    const int q = lane & 3;   // read-back chunk of this lane
+    const bool vec = (a.N & 3) == 0;
     long job = 0;
     for (long t = x.first; t < x.tiles; t += x.Q, job++) {
         const int buf = int(job & 1);
@@ -427,18 +420,40 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
         for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
             float v[16];
             tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);
-            bias_act_stage(a.act, v, bias_s + c0, stg + lane * 17);
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const float *bb = bias_s + c0 + 4 * c;
+                const float4 o = make_float4(activate_t<ACT, true>(fadd(v[4 * c], bb[0])),
+                                             activate_t<ACT, true>(fadd(v[4 * c + 1], bb[1])),
+                                             activate_t<ACT, true>(fadd(v[4 * c + 2], bb[2])),
+                                             activate_t<ACT, true>(fadd(v[4 * c + 3], bb[3])));
+                sts4(stg + uint32_t(lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)), o);
+            }
             __syncwarp();
-            // two rows of 16 channels per pass
-            const int n = x.n0 + c0 + col;
-            if (n < a.N) {
-#pragma unroll 4
-                for (int i = sub; i < 32; i += 2) {
-                    if (i >= nrows) break;
-                    const long m = mrow + i;
-                    float y = stg[i * 17 + col];
-                    if (a.res) y = activate(a.act2, fadd(y, __ldg(a.res + m * a.N + n)));
-                    a.y[m * a.N + n] = y;
+            const int n = x.n0 + c0 + 4 * q;
+#pragma unroll
+            for (int p = 0; p < 4; p++) {
+                const int r = 8 * p + (lane >> 2);
+                float4 o = lds4(stg + uint32_t(r * 64 + ((q ^ ((r >> 1) & 3)) << 4)));
+                if (r >= nrows || n >= a.N) continue;
+                const long m = mrow + r;
+                float *dst = a.y + m * a.N + n;
+                if (vec) {
+                    if (a.res) {
+                        const float4 rr = __ldg(reinterpret_cast<const float4 *>(a.res + m * a.N + n));
+                        o = make_float4(activate(a.act2, fadd(o.x, rr.x)), activate(a.act2, fadd(o.y, rr.y)),
+                                        activate(a.act2, fadd(o.z, rr.z)), activate(a.act2, fadd(o.w, rr.w)));
+                    }
+                    *reinterpret_cast<float4 *>(dst) = o;
+                } else {
+                    const float ov[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        if (n + c >= a.N) break;
+                        float y = ov[c];
+                        if (a.res) y = activate(a.act2, fadd(y, __ldg(a.res + m * a.N + n + c)));
+                        dst[c] = y;
+                    }
                 }
             }
             __syncwarp();
@@ -490,6 +505,7 @@ __device__ __forceinline__ void teardown(const TcArgs &a, const Ctx &x) {
     }
 }
 
+template <int ACT>
 __global__ void __launch_bounds__(Roles::THREADS, 1)
     pw_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw) {
     using R = Roles;
@@ -550,11 +566,12 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
     } else if (warp < R::W_EPI) {
         role_convert(a, x, tid - R::W_CONV * 32);
     } else {
-        role_epilogue(a, x, warp - R::W_EPI, warp, lane, staging, bias_s);
+        role_epilogue<ACT>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
     }
     teardown<R>(a, x);
 }
 
+template <int ACT>
 __global__ void __launch_bounds__(Roles::THREADS, 1)
     conv_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw) {
     using R = Roles;
@@ -621,7 +638,7 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
     } else if (warp < R::W_EPI) {
         role_convert(a, x, tid - R::W_CONV * 32);
     } else {
-        role_epilogue(a, x, warp - R::W_EPI, warp, lane, staging, bias_s);
+        role_epilogue<ACT>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
     }
     teardown<R>(a, x);
 }
@@ -749,20 +766,39 @@ bool tc_prepare(TcArgs &a) {
     return encode_weights(a, enc) && set_grid(a);
 }
 
+template <int ACT>
+void configure_act() {
+    cudaFuncSetAttribute(pw_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
+    cudaFuncSetAttribute(conv_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
+}
+
 void configure_tc_kernels() {
-    cudaFuncSetAttribute(pw_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
-    cudaFuncSetAttribute(conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
+    configure_act<0>(); configure_act<1>(); configure_act<2>(); configure_act<3>();
+    configure_act<4>(); configure_act<5>(); configure_act<6>(); configure_act<7>();
+}
+
+template <int ACT>
+void launch_act(const TcArgs &a, const CUtensorMap &mx, const CUtensorMap &mw, cudaStream_t s) {
+    if (a.windowed)
+        conv_tc_kernel<ACT><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
+    else
+        pw_tc_kernel<ACT><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
 }
 
 int launch_tc(const TcArgs &a, cudaStream_t s) {
-    CUtensorMap mw;
-    std::memcpy(&mw, a.tmw, sizeof mw);
-    CUtensorMap mx;
+    CUtensorMap mx, mw;
     std::memcpy(&mx, a.tmx, sizeof mx);
-    if (a.windowed)
-        conv_tc_kernel<<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
-    else
-        pw_tc_kernel<<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
+    std::memcpy(&mw, a.tmw, sizeof mw);
+    switch (a.act) {
+    case 1: launch_act<1>(a, mx, mw, s); break;
+    case 2: launch_act<2>(a, mx, mw, s); break;
+    case 3: launch_act<3>(a, mx, mw, s); break;
+    case 4: launch_act<4>(a, mx, mw, s); break;
+    case 5: launch_act<5>(a, mx, mw, s); break;
+    case 6: launch_act<6>(a, mx, mw, s); break;
+    case 7: launch_act<7>(a, mx, mw, s); break;
+    default: launch_act<0>(a, mx, mw, s); break;
+    }
     return 1;
 }
 

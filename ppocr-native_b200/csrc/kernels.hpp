@@ -248,6 +248,11 @@ void configure_tc_kernels();
 
 // Each returns the number of kernels it launched.
 int launch_conv(const ConvArgs &a, cudaStream_t s);
+// A pointwise layer over per-lane vectors (one pixel per lane, one source),
+// bit-identical to launch_conv; supported while its weights' 32-column slice
+// and the vectors fit in shared memory.
+int launch_conv_vector(const ConvArgs &a, cudaStream_t s);
+bool conv_vector_supported(const ConvArgs &a);
 int launch_dw(const DwArgs &a, cudaStream_t s);
 int launch_dw_pw(const DwPwArgs &a, cudaStream_t s);
 int launch_elt(const EltArgs &a, cudaStream_t s);

@@ -613,22 +613,26 @@ int ppocr_model::build_group(Group &g, std::string &err) {
     // there. The choice depends on the layer alone, never on how many
     // pixels the run holds, so a lane gives the same bits alone as
     // alongside others.
-    // A layer that reads a channel mean (one pixel per lane, a squeeze-and-
-    // excite gate) stays on the FP32 cores: a tensor-core launch there is
-    // all set-up.
-    std::vector<char> reads_mean(p0.ops.size(), 0);
+    // Layers over per-lane vectors: a channel mean's output and the
+    // pointwise convs that follow it (a squeeze-and-excite branch, one pixel
+    // per lane at every size). They take the one-thread-per-output kernel;
+    // a tensor-core launch there would be all set-up.
+    std::vector<char> reads_vector(p0.ops.size(), 0);
     {
         std::vector<int> writer(p0.pool.size(), -1);
+        std::vector<char> vector_out(p0.ops.size(), 0);
         for (size_t i = 0; i < p0.ops.size(); i++) {
             const Op &op = p0.ops[i];
-            reads_mean[i] = writer[op.x] >= 0 && p0.ops[size_t(writer[op.x])].kind == K_MEAN;
+            const int w = writer[op.x];
+            reads_vector[i] = w >= 0 && vector_out[size_t(w)];
+            vector_out[i] = op.kind == K_MEAN || (op.pointwise() && reads_vector[i]);
             writer[op.y] = int(i);
         }
     }
     // 0: not on the tensor cores; 1: there; 2: there, after the sources are
     // written out side by side (`gather`).
     auto tc_route = [&](size_t i, const ConvArgs &c, const LaneInfo *Lh, TcArgs &t, GatherArgs &gather) {
-        if (!tc_allowed || !W.tc_hi(i) || reads_mean[i]) return 0;
+        if (!tc_allowed || !W.tc_hi(i)) return 0;
         const Op &op = p0.ops[i];
         const bool one = c.nsrc == 1 && !c.src[0].shift;
         const bool pw = one && c.kh == 1 && c.kw == 1 && c.sh == 1 && c.sw == 1 && !c.pt && !c.pl;
@@ -661,6 +665,15 @@ int ppocr_model::build_group(Group &g, std::string &err) {
     // there, else the FP32 implicit GEMM; `pre` runs first (a depthwise
     // layer whose output it reads, or nothing).
     auto push_conv = [&](size_t i, const ConvArgs &c, const LaneInfo *Lh, std::function<int(cudaStream_t)> pre) {
+        const Op &op = p0.ops[i];
+        if (reads_vector[i] && op.pointwise() && c.nsrc == 1 && !c.src[0].shift) {
+            // the same bits either way
+            if (conv_vector_supported(c))
+                g.launches.push_back([pre, c](cudaStream_t s) { return (pre ? pre(s) : 0) + launch_conv_vector(c, s); });
+            else
+                g.launches.push_back([pre, c](cudaStream_t s) { return (pre ? pre(s) : 0) + launch_conv(c, s); });
+            return;
+        }
         TcArgs t;
         GatherArgs ga;
         const int route = tc_route(i, c, Lh, t, ga);

@@ -18,6 +18,8 @@
 // pixels are the output's. An SE gate (per lane and input channel)
 // multiplies A as it is loaded; a residual add and a second activation run in
 // the epilogue.
+#include <algorithm>
+
 #include "devmath.cuh"
 #include "kernels.hpp"
 
@@ -299,46 +301,98 @@ __global__ void __launch_bounds__(TX *TY, 65536 / (TX * TY * 128)) conv_gemm(con
 }
 
 // A pointwise layer over per-lane vectors (a squeeze-and-excite branch: one
-// pixel per lane). Block b takes output channels 32b..32b+31 of every pixel:
-// its threads first copy that weight slice and the (gated) input vectors to
-// shared memory together, many loads in flight, then each output is one
-// thread's chain of k terms added in increasing k with one fused
-// multiply-add each, from the bias or from zero, as conv_gemm's accumulators
-// do, so the two give the same bits.
-constexpr int VEC_COLS = 32;
+// pixel per lane). Block (b, r) takes output channels 32b..32b+31 of pixels
+// 8r..8r+7, one thread each: its threads first copy that weight slice and
+// those (gated) input vectors to shared memory together, many loads in
+// flight; then each output is one thread's chain of k terms added in
+// increasing k with one fused multiply-add each, from the bias or from zero,
+// as conv_gemm's accumulators do, so the two give the same bits.
+constexpr int VEC_COLS = 32, VEC_ROWS = 8;
 
-__global__ void __launch_bounds__(256) conv_vector_kernel(const ConvArgs a) {
+__global__ void __launch_bounds__(VEC_COLS *VEC_ROWS) conv_vector_kernel(const ConvArgs a) {
     extern __shared__ float vsm[];
     float *ws = vsm;                   // [C][32]
-    float *xs = vsm + a.C * VEC_COLS;  // [M][C]
+    float *xs = vsm + a.C * VEC_COLS;  // [8][C]
     const int n0 = blockIdx.x * VEC_COLS;
+    const long m0 = (long)blockIdx.y * VEC_ROWS;
     const int cols = min(VEC_COLS, a.oc - n0);
+    const int rows = int(min((long)VEC_ROWS, a.M - m0));
     for (int e = threadIdx.x; e < a.C * VEC_COLS; e += blockDim.x) {
         const int k = e / VEC_COLS, j = e - k * VEC_COLS;
         ws[e] = j < cols ? __ldg(a.w + (long)k * a.oc + n0 + j) : 0.0f;
     }
-    const float *x = a.src[0].p;
-    for (long e = threadIdx.x; e < a.M * a.C; e += blockDim.x) {
-        const long m = e / a.C;
-        const int k = int(e - m * a.C);
-        float v = __ldg(x + e);
-        if (a.gate) v = fmul(v, __ldg(a.gate + (long)find_lane(a.lanes, a.nl, m) * a.C + k));
+    for (int e = threadIdx.x; e < rows * a.C; e += blockDim.x) {
+        const int r = e / a.C, k = e - r * a.C;
+        float v = __ldg(a.src[0].p + (m0 + r) * a.C + k);
+        if (a.gate) v = fmul(v, __ldg(a.gate + (long)find_lane(a.lanes, a.nl, m0 + r) * a.C + k));
         xs[e] = v;
     }
     __syncthreads();
-    for (long e = threadIdx.x; e < a.M * VEC_COLS; e += blockDim.x) {
-        const long m = e / VEC_COLS;
-        const int j = int(e - m * VEC_COLS);
-        if (j >= cols) continue;
-        const int n = n0 + j;
-        const bool first = a.bias_mode == BIAS_FIRST;
-        float acc = (first && a.b) ? __ldg(a.b + n) : 0.0f;
-        const float *xm = xs + m * a.C;
-        for (int k = 0; k < a.C; k++) acc = ffma(ws[k * VEC_COLS + j], xm[k], acc);
-        if (!first && a.b) acc = fadd(acc, __ldg(a.b + n));
-        acc = activate(a.act, acc);
-        if (a.res) acc = activate(a.act2, fadd(acc, __ldg(a.res + m * a.oc + n)));
-        a.y[m * a.oc + n] = acc;
+    const int r = threadIdx.x / VEC_COLS, j = threadIdx.x % VEC_COLS;
+    if (r >= rows || j >= cols) return;
+    const long m = m0 + r;
+    const int n = n0 + j;
+    const bool first = a.bias_mode == BIAS_FIRST;
+    float acc = (first && a.b) ? __ldg(a.b + n) : 0.0f;
+    const float *xm = xs + r * a.C;
+#pragma unroll 8
+    for (int k = 0; k < a.C; k++) acc = ffma(ws[k * VEC_COLS + j], xm[k], acc);
+    if (!first && a.b) acc = fadd(acc, __ldg(a.b + n));
+    acc = activate(a.act, acc);
+    if (a.res) acc = activate(a.act2, fadd(acc, __ldg(a.res + m * a.oc + n)));
+    a.y[m * a.oc + n] = acc;
+}
+
+// An RGB stem (three input channels, bias first, kh * kw <= 9): one thread
+// per output pixel holds its kh*kw*3 input values and all NB outputs; the
+// weights sit in shared memory, read by every thread at once (broadcast).
+// Each output adds its k terms in increasing k = (ky*kw + kx)*3 + c with one
+// fused multiply-add each, padded taps as zeros, from the bias, as
+// conv_gemm's accumulators do, so the two give the same bits.
+template <int NB>
+__global__ void __launch_bounds__(128) stem_kernel(const ConvArgs a) {
+    __shared__ float ws[27 * NB];
+    __shared__ float bs[NB];
+    const int K = a.kh * a.kw * 3;
+    for (int e = threadIdx.x; e < K * NB; e += blockDim.x) ws[e] = __ldg(a.w + e);
+    for (int e = threadIdx.x; e < NB; e += blockDim.x) bs[e] = a.b ? __ldg(a.b + e) : 0.0f;
+    __syncthreads();
+    const float *x = a.src[0].p;
+    for (long m = (long)blockIdx.x * blockDim.x + threadIdx.x; m < a.M; m += (long)gridDim.x * blockDim.x) {
+        const int n = find_lane(a.lanes, a.nl, m);
+        const LaneInfo &L = a.lanes[n];
+        const int ow = __ldg(&L.ow), ih = __ldg(&L.ih), iw = __ldg(&L.iw);
+        const int q = int(m - __ldg(&L.pix0));
+        const int oy = q / ow, ox = q - oy * ow;
+        const int iy0 = oy * a.sh - a.pt, ix0 = ox * a.sw - a.pl;
+        const float *xl = x + __ldg(&L.ipix0) * 3;
+        float in[27];  // taps past kh x kw stay zero and are never used
+#pragma unroll
+        for (int t = 0; t < 9; t++) {
+            const bool tap = t < a.kh * a.kw;
+            const int ty = tap ? t / a.kw : 0;
+            const int iy = iy0 + ty, ix = ix0 + (tap ? t - ty * a.kw : 0);
+            const bool ok = tap && iy >= 0 && iy < ih && ix >= 0 && ix < iw;
+            const float *p = xl + ((long)iy * iw + ix) * 3;
+            in[3 * t] = ok ? __ldg(p) : 0.0f;
+            in[3 * t + 1] = ok ? __ldg(p + 1) : 0.0f;
+            in[3 * t + 2] = ok ? __ldg(p + 2) : 0.0f;
+        }
+        float acc[NB];
+#pragma unroll
+        for (int j = 0; j < NB; j++) acc[j] = bs[j];
+#pragma unroll
+        for (int k = 0; k < 27; k++) {
+            if (k >= K) break;
+#pragma unroll
+            for (int j = 0; j < NB; j++) acc[j] = ffma(ws[k * NB + j], in[k], acc[j]);
+        }
+        float *y = a.y + m * NB;
+#pragma unroll
+        for (int j = 0; j < NB; j += 4)
+            *reinterpret_cast<float4 *>(y + j) =
+                make_float4(activate(a.act, acc[j]), activate(a.act, acc[j + 1]), activate(a.act, acc[j + 2]),
+                            activate(a.act, acc[j + 3]));
     }
 }
 
@@ -401,7 +455,17 @@ int launch_conv(const ConvArgs &a, cudaStream_t s) {
               a.src[0].shift == 0;
     bool small = a.M < SMALL_M;
     int oc = a.oc;
-    // RGB stems: three channels per tap, K slices of 4
+    // RGB stems (bias first): the direct kernel
+    if (a.C == 3 && a.nsrc == 1 && !a.src[0].shift && a.bias_mode == BIAS_FIRST && !a.gate && !a.res &&
+        a.kh * a.kw <= 9 && (oc == 24 || oc == 48)) {
+        const long blocks = std::min<long>((a.M + 127) / 128, 148L * 16);
+        if (oc == 24)
+            stem_kernel<24><<<unsigned(blocks), 128, 0, s>>>(a);
+        else
+            stem_kernel<48><<<unsigned(blocks), 128, 0, s>>>(a);
+        return 1;
+    }
+    // other three- or four-channel inputs: K slices of 4
     if (a.C <= 4 && oc == 24) return run<8, 6, 4, 32, 4>(a, s, vec4, pw);
     if (a.C <= 4 && oc == 48) return run<8, 6, 8, 32, 4>(a, s, vec4, pw);
     if (oc % 128 == 0) return small ? run<4, 8, 16, 16, 16>(a, s, vec4, pw) : run<8, 8, 16, 16, 8>(a, s, vec4, pw);
@@ -415,12 +479,13 @@ int launch_conv(const ConvArgs &a, cudaStream_t s) {
     return run<8, 4, 16, 16, 8>(a, s, vec4, pw);
 }
 
-size_t conv_vector_smem(const ConvArgs &a) { return sizeof(float) * size_t(a.C) * (VEC_COLS + size_t(a.M)); }
+size_t conv_vector_smem(const ConvArgs &a) { return sizeof(float) * size_t(a.C) * (VEC_COLS + VEC_ROWS); }
 
 bool conv_vector_supported(const ConvArgs &a) { return conv_vector_smem(a) <= 200 * 1024; }
 
 int launch_conv_vector(const ConvArgs &a, cudaStream_t s) {
-    conv_vector_kernel<<<unsigned((a.oc + VEC_COLS - 1) / VEC_COLS), 256, conv_vector_smem(a), s>>>(a);
+    dim3 grid(unsigned((a.oc + VEC_COLS - 1) / VEC_COLS), unsigned((a.M + VEC_ROWS - 1) / VEC_ROWS));
+    conv_vector_kernel<<<grid, VEC_COLS * VEC_ROWS, conv_vector_smem(a), s>>>(a);
     return 1;
 }
 

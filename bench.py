@@ -37,6 +37,11 @@ PKG_DIR = ROOT / "ppocr-native_b200"
 sys.path.insert(0, str(ROOT))
 
 L2_FLUSH_BYTES = 256 << 20  # larger than the 126 MB L2
+# DRAM bytes (read + written) of one launch of the probed kernel, from one ncu
+# capture of `bench.py --workload layer` (profiles/pw_tc_kernel_1x1_24to24_992x768.md);
+# writes still dirty in L2 when the kernel ends are not counted there.
+TRAFFIC_PER_LAUNCH = 99.59e6
+TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch (profiles/pw_tc_kernel_1x1_24to24_992x768.md)"
 
 
 def package():
@@ -216,21 +221,21 @@ class PagePipeline:
             m.close()
 
 
-DOMINANT = (496, 384, 96, 24)  # h, w, ic, oc of the probed 3x3 convolution
+DOMINANT = (992, 768, 24, 24)  # h, w, ic, oc of the probed pointwise layer
 
 
 def dominant_plan() -> bytes:
-    """The detector's dominant layer alone: the 3x3 96 -> 24 convolution of
-    the RSE neck at a quarter of a 1984 x 1536 page (496 x 384 pixels), the
-    layer class with the most FLOPs of the page (18 of its 35 detector GFLOP
-    with the DB head's)."""
+    """The page's dominant kernel class alone: pointwise layers on the
+    tensor cores (pw_tc_kernel, the largest share of a page's launch time),
+    here its largest launch, the detector's first 1x1 24 -> 24 + swish at
+    half of a 1984 x 1536 page (992 x 768 pixels)."""
     from ppocr_native_b200.plan import Op, encode, window
 
     h, w, ic, oc = DOMINANT
     rng = np.random.default_rng(0)
-    wt = rng.normal(0, 0.02, 9 * ic * oc).astype(np.float32)
+    wt = rng.normal(0, 0.02, ic * oc).astype(np.float32)
     b = rng.normal(0, 0.02, oc).astype(np.float32)
-    op = window(Op("conv", x=0, y=1, ic=ic, oc=oc, w=(0, wt.size), b=(wt.size, oc)), (3, 3), 1, 1, 1)
+    op = window(Op("conv", x=0, y=1, ic=ic, oc=oc, fused="swish", w=(0, wt.size), b=(wt.size, oc)), (1, 1), 1, 0, 0)
     return encode((0, h, w, ic), 2, [1], [op], np.concatenate([wt, b]))
 
 
@@ -249,11 +254,14 @@ def run_layer(args, d, cuda, torch, device):
 
 
 def probe_kernel(cuda, torch, device: int, reps: int = 20) -> dict:
-    """Time the detector's dominant kernel alone with CUDA events (see
-    `dominant_plan`)."""
+    """Time the dominant kernel alone with CUDA events on the model's stream,
+    L2 flushed before each launch (see `dominant_plan`). Algorithmic bytes:
+    the input and output maps once, the split weights (two tf32 halves,
+    K padded to 32) and the bias."""
     h, w, ic, oc = DOMINANT
     rng = np.random.default_rng(0)
     m = cuda.Model(dominant_plan(), device=device)
+    assert m.steps() == ["conv"]
     x = rng.standard_normal(h * w * ic).astype(np.float32)
     m.input_mut()[:] = x
     m.run(60_000)
@@ -274,31 +282,10 @@ def probe_kernel(cuda, torch, device: int, reps: int = 20) -> dict:
             times.append(e0.elapsed_time(e1) / 1e3)
     m.close()
     t = statistics.median(times)
-    flops = 2 * h * w * 9 * ic * oc
-    algo_bytes = 4 * (h * w * ic + h * w * oc + 9 * ic * oc + oc)
-    return {"kernel": "conv_gemm 3x3 96->24 @ 496x384 (RSE neck / DB head class)", "seconds": t,
-            "flops": flops, "bytes": algo_bytes}
-
-
-def fp32_peak(torch, device: int) -> float:
-    """Measured FP32 CUDA-core peak: cuBLAS SGEMM 8192^3 with TF32 off."""
-    torch.backends.cuda.matmul.allow_tf32 = False
-    n = 8192
-    a = torch.randn(n, n, device=f"cuda:{device}")
-    b = torch.randn(n, n, device=f"cuda:{device}")
-    for _ in range(2):
-        a @ b
-    torch.cuda.synchronize()
-    best = float("inf")
-    for _ in range(5):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        a @ b
-        e1.record()
-        e1.synchronize()
-        best = min(best, e0.elapsed_time(e1) / 1e3)
-    del a, b
-    return 2 * n ** 3 / best / 1e12
+    kpad = -(-ic // 32) * 32
+    algo_bytes = 4 * (h * w * ic + h * w * oc + 2 * oc * kpad + oc)
+    return {"kernel": "pw_tc_kernel: 1x1 24->24 + swish @ 992x768 (3xTF32 tcgen05, the detector's first pointwise)",
+            "seconds": t, "bytes": algo_bytes, "flops": 2 * h * w * ic * oc}
 
 
 def cpu_baseline(widths_seed: int = 0, budget_s: float = 20.0) -> dict:
@@ -418,10 +405,12 @@ def run_ours(args, d: Dist) -> dict | None:
     result = None
     if d.rank == 0:
         probe = probe_kernel(cuda, torch, device)
-        peak = fp32_peak(torch, device)
-        achieved = probe["flops"] / probe["seconds"] / 1e12
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-        hbm = peaks.get("hbm_gbs", 6650.0)
+        hbm = peaks.get("hbm_gbs")
+        peak_source = "measured: MEASURED_PEAKS.json hbm_gbs (copy, burst)"
+        if hbm is None:
+            hbm, peak_source = 6650.0, "fallback: 6.65 TB/s"
+        achieved = probe["bytes"] / probe["seconds"] / 1e9
         result = {
             "metric": "synthetic-page pages/s (det 1984x1536 + rec 44 lines) per B200 job",
             "value": value,
@@ -442,12 +431,10 @@ def run_ours(args, d: Dist) -> dict | None:
                        "parallelism": f"replicas x{d.world} (pages sharded by rank, no collective)"},
             "e2e": {"value": e2e, "unit": "pages/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches * args.steps,
-            "roofline": {"bound": "fp32", "kernel": probe["kernel"], "achieved": achieved,
-                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                         "peak_source": "measured in this run: cuBLAS SGEMM 8192^3, TF32 off (FP32 CUDA cores)",
-                         "traffic": None,
-                         "hbm_achieved_gbs": probe["bytes"] / probe["seconds"] / 1e9,
-                         "hbm_peak_gbs": hbm, "seconds_per_launch": probe["seconds"]},
+            "roofline": {"bound": "hbm", "kernel": probe["kernel"], "achieved": achieved,
+                         "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_source": peak_source,
+                         "traffic": TRAFFIC_PER_LAUNCH, "traffic_source": TRAFFIC_SOURCE,
+                         "algorithmic_bytes": probe["bytes"], "seconds_per_launch": probe["seconds"]},
             "clocks": clocks.summary(),
         }
     return result

@@ -49,6 +49,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cfloat>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -399,7 +400,7 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
 // (one pixel) of 16 columns; it stages them as four 16-byte chunks of its row
 // (chunk q at q ^ ((row >> 1) & 3), so that eight lanes cover all 32 banks),
 // and the warp then writes 8 rows x 64 bytes per store.
-template <int ACT>
+template <int ACT, bool CTC>
 __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, int lane, uint32_t staging,
                               const float *bias_s) {
     const int qd = warp & 3;  // the TMEM lane quadrant this warp may read
@@ -417,6 +418,38 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
         const TileInfo ti = tile_info(a, t);
         const long mrow = ti.m0 + qd * 32;
         const int nrows = ti.rows - qd * 32;  // rows of this warp's quadrant that exist
+        if (CTC) {
+            // this thread's row over the columns of its block, in increasing
+            // column order: an online softmax keeping the first maximum
+            float m = -FLT_MAX, sum = 0.0f;
+            int best = 0x7fffffff;
+            for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
+                float v[16];
+                tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const int col = x.n0 + c0 + j;
+                    if (col >= a.vocab) continue;
+                    const float l = fadd(v[j], bias_s[c0 + j]);
+                    if (l > m) {
+                        sum = m > -FLT_MAX ? ffma(sum, exp_neg(fsub(m, l)), 1.0f) : 1.0f;
+                        m = l;
+                        best = col;
+                    } else {
+                        sum = fadd(sum, exp_neg(fsub(l, m)));
+                    }
+                }
+            }
+            if (lane < nrows) {
+                float *st = a.partial + ((mrow + lane) * a.blocks + 2 * (x.n0 / x.BN) + half) * 3;
+                st[0] = m;
+                st[1] = sum;
+                st[2] = __int_as_float(best);
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            arrive(smem_u32(&x.acce[buf]));
+            continue;
+        }
         for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
             float v[16];
             tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);
@@ -505,7 +538,7 @@ __device__ __forceinline__ void teardown(const TcArgs &a, const Ctx &x) {
     }
 }
 
-template <int ACT>
+template <int ACT, bool CTC = false>
 __global__ void __launch_bounds__(Roles::THREADS, 1)
     pw_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw) {
     using R = Roles;
@@ -566,12 +599,12 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
     } else if (warp < R::W_EPI) {
         role_convert(a, x, tid - R::W_CONV * 32);
     } else {
-        role_epilogue<ACT>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
+        role_epilogue<ACT, CTC>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
     }
     teardown<R>(a, x);
 }
 
-template <int ACT>
+template <int ACT, bool CTC = false>
 __global__ void __launch_bounds__(Roles::THREADS, 1)
     conv_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw) {
     using R = Roles;
@@ -586,7 +619,7 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
     x.Q = gridDim.x / a.slices;
     x.first = blockIdx.x / a.slices;
     x.n0 = int(blockIdx.x % a.slices) * a.bn;
-    x.tiles = a.tiles;
+    x.tiles = a.windowed ? a.tiles : (a.M + TM - 1) / TM;
     x.ring = smem_u32(smem);
     x.b_bytes = uint32_t(a.bn) * 128;
     x.stage_bytes = SLOT_BYTES + 2 * x.b_bytes;
@@ -600,14 +633,18 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
     const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
     if (warp == 0) {
         if (lane == 0) {
-            const int cblocks = a.C / TK;
+            const int cblocks = a.windowed ? a.C / TK : x.nkb;  // K blocks per tap
             long it = 0;
             bool ok = true;
             for (long t = x.first; t < x.tiles && ok; t += x.Q) {
                 const TileInfo ti = tile_info(a, t);
-                const LaneInfo &L = a.lanes[ti.n];
-                const long base = __ldg(&L.ipix0) + ti.q0;
-                const int iw = __ldg(&L.iw);
+                long base = ti.m0;  // a 1x1 layer's packed input is its output's
+                int iw = 0;
+                if (a.windowed) {
+                    const LaneInfo &L = a.lanes[ti.n];
+                    base = __ldg(&L.ipix0) + ti.q0;
+                    iw = __ldg(&L.iw);
+                }
                 for (int kb = 0; kb < x.nkb; kb++, it++) {
                     const int s = int(it % x.ns);
                     const long round = it / x.ns;
@@ -638,9 +675,77 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
     } else if (warp < R::W_EPI) {
         role_convert(a, x, tid - R::W_CONV * 32);
     } else {
-        role_epilogue<ACT>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
+        role_epilogue<ACT, CTC>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
     }
     teardown<R>(a, x);
+}
+
+// One warp per row: the blocks' (max, sum, first column) merge in a fixed
+// order; then every block within the margin of the row's maximum has its 16
+// x (bn / 32) columns recomputed exactly, lanes two columns each.
+__global__ void __launch_bounds__(256) ctc_tc_merge_kernel(const CtcMergeArgs a) {
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const long t = (long)blockIdx.x * 8 + warp;
+    if (t >= a.pixels) return;
+    const float *st = a.partial + t * a.blocks * 3;
+    float m = -FLT_MAX;
+    for (int b = lane; b < a.blocks; b += 32) m = fmaxf(m, st[b * 3]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    float sum = 0.0f;
+    for (int b = lane; b < a.blocks; b += 32)
+        if (st[b * 3] > -FLT_MAX) sum = fadd(sum, fmul(st[b * 3 + 1], exp_neg(fsub(st[b * 3], m))));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float o = __shfl_xor_sync(0xffffffffu, sum, off);
+        sum = (lane & off) ? fadd(o, sum) : fadd(sum, o);  // the same order in both lanes
+    }
+    // The margin: twice a bound on |tensor-core logit - FP32 logit|. Each
+    // sum of k products, |w_k x_k| <= wmax |x_k|, carries at most 3k + 8
+    // roundings of 2^-23 relative in either form (three products per k on
+    // the tensor core, the dropped low-low term, the bias), so
+    // 2 * 2 * (3k + 8) * 2^-23 * (wmax * sum|x| + bmax) covers both errors.
+    const float *x = a.x + t * a.ci;
+    float ax = 0.0f;
+    for (int k = lane; k < a.ci; k += 32) ax += fabsf(x[k]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ax += __shfl_xor_sync(0xffffffffu, ax, off);
+    const float margin = 4.0f * float(3 * a.ci + 8) * 1.1920929e-7f * (ax * a.wmax + a.bmax) * 1.01f;
+    float best_v = -FLT_MAX;
+    int best = 0x7fffffff;
+    for (int b0 = 0; b0 < a.blocks; b0 += 32) {
+        const int b = b0 + lane;
+        unsigned cand = __ballot_sync(0xffffffffu, b < a.blocks && st[b * 3] >= m - margin);
+        while (cand) {
+            const int bb = b0 + __ffs(cand) - 1;
+            cand &= cand - 1;
+            const int slice = bb / 2, half = bb % 2;
+            for (int q = lane; q < a.bn / 2; q += 32) {
+                const int col = slice * a.bn + half * 16 + (q / 16) * 32 + (q % 16);
+                if (col >= a.vocab) continue;
+                float acc = __ldg(a.b + col);
+                const float *wc = a.w + (long)(col >> 4) * a.ci * 16 + (col & 15);
+                for (int k = 0; k < a.ci; k++) acc = ffma(__ldg(wc + k * 16), x[k], acc);
+                if (acc > best_v || (acc == best_v && col < best)) {
+                    best_v = acc;
+                    best = col;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, best_v, off);
+        const int c2 = __shfl_xor_sync(0xffffffffu, best, off);
+        if (v2 > best_v || (v2 == best_v && c2 < best)) {
+            best_v = v2;
+            best = c2;
+        }
+    }
+    if (lane == 0) {
+        a.y[2 * t] = float(best);
+        a.y[2 * t + 1] = fdiv(1.0f, sum);
+    }
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -679,12 +784,12 @@ int pw_slice_width(int K, int N) {
     return 0;
 }
 
-// The windowed kernel streams its weights, so a slice is as wide as a
-// four-stage ring allows (at most 128).
+// The streaming kernel's slice: as wide as a three-stage ring allows (at
+// most 128).
 int conv_slice_width(int N) {
     for (int S = 1; S <= (N + 31) / 32; S++) {
         const int bn = ((N + S - 1) / S + 31) / 32 * 32;
-        if (bn <= 128 && conv_smem(bn, 4) <= size_t(DYN_CEILING)) return bn;
+        if (bn <= 128 && conv_smem(bn, 3) <= size_t(DYN_CEILING)) return bn;
     }
     return 0;
 }
@@ -732,7 +837,8 @@ bool tc_prepare(TcArgs &a) {
     if (!enc) return false;
     a.nkb = a.kpad / TK;
     if (a.C % 4 || !aligned(a.x) || (a.gate && !aligned(a.gate))) return false;
-    if (!a.windowed) {
+    if (a.vocab > 0 && (a.windowed || !a.stream_b || a.act || a.res || a.gate || !a.partial)) return false;
+    if (!a.windowed && !a.stream_b) {
         // 1x1: the packed input is [M][K]
         if (a.K != a.C) return false;
         a.bn = pw_slice_width(a.K, a.N);
@@ -744,7 +850,8 @@ bool tc_prepare(TcArgs &a) {
     } else {
         // a tap's K blocks never straddle taps; the output keeps the input's
         // size, so the packed input has M pixels too
-        if (a.gate || a.C % TK || a.K != a.kh * a.kw * a.C || a.tiles < 1) return false;
+        if (a.gate || a.K != a.kh * a.kw * a.C) return false;
+        if (a.windowed ? (a.C % TK || a.tiles < 1) : (a.kh * a.kw != 1)) return false;
         a.bn = conv_slice_width(a.N);
         if (!a.bn) return false;
         a.slices = (a.N + a.bn - 1) / a.bn;
@@ -763,7 +870,18 @@ bool tc_prepare(TcArgs &a) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
     std::memcpy(a.tmx, &mx, sizeof mx);
+    a.blocks = 2 * a.slices;
     return encode_weights(a, enc) && set_grid(a);
+}
+
+int launch_ctc_tc_merge(const CtcMergeArgs &a, cudaStream_t s) {
+    ctc_tc_merge_kernel<<<unsigned((a.pixels + 7) / 8), 256, 0, s>>>(a);
+    return 1;
+}
+
+int tc_stream_slices(int N) {
+    const int bn = conv_slice_width(N);
+    return bn ? (N + bn - 1) / bn : 0;
 }
 
 template <int ACT>
@@ -773,13 +891,16 @@ void configure_act() {
 }
 
 void configure_tc_kernels() {
+    cudaFuncSetAttribute(conv_tc_kernel<0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
     configure_act<0>(); configure_act<1>(); configure_act<2>(); configure_act<3>();
     configure_act<4>(); configure_act<5>(); configure_act<6>(); configure_act<7>();
 }
 
 template <int ACT>
 void launch_act(const TcArgs &a, const CUtensorMap &mx, const CUtensorMap &mw, cudaStream_t s) {
-    if (a.windowed)
+    if (a.vocab > 0)
+        conv_tc_kernel<0, true><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
+    else if (a.windowed || a.stream_b)
         conv_tc_kernel<ACT><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
     else
         pw_tc_kernel<ACT><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);

@@ -200,6 +200,7 @@ struct ConvTArgs {
 // that fall outside the image read as zeros.
 struct TcArgs {
     bool windowed = false;
+    bool stream_b = false;        // weights streamed with the A blocks even for a 1x1 layer
     const float *x = nullptr;     // [pixels][C], 16-byte aligned, C % 4 == 0
     long tiles = 0;               // windowed: 128-pixel tiles of all lanes, each lane on its own
     int C = 0;
@@ -216,6 +217,13 @@ struct TcArgs {
     int K = 0, N = 0, kpad = 0;   // K = kh * kw * C
     int act = 0, act2 = 0;
     int *err = nullptr;           // set to nonzero when a bounded wait gave up
+    // A CTC argmax head (vocab > 0, streamed, 1x1): no y; per row and column
+    // block, (max, sum of exp(logit - max), first column of the max) over
+    // the block's columns below vocab, into partial [M][blocks][3]. Block
+    // 2s + h holds columns s*bn + h*16 + 32j + e (e < 16) of slice s.
+    int vocab = 0;
+    float *partial = nullptr;
+    int blocks = 0;               // filled: 2 * slices
     // filled by tc_prepare: output-channel slice width and count, K blocks,
     // ring stages, TMEM columns, grid, dynamic shared memory, and the tensor
     // maps (CUtensorMap, 128 bytes each) of the input and of the weights
@@ -223,6 +231,26 @@ struct TcArgs {
     unsigned long long tmx[16] = {}, tmw[16] = {};
 };
 int launch_tc(const TcArgs &a, cudaStream_t s);
+// Slices of the output channels a streamed-weight launch of N channels uses.
+int tc_stream_slices(int N);
+
+// The CTC argmax head's merge after its tensor-core logits: per row, the
+// blocks' maxima and sums combine into 1 / sum exp(logit - max); every
+// block whose maximum lies within `margin` of the row's (a bound on the
+// tensor-core logits' error, twice over) has its logits recomputed in FP32
+// in the reference's order (bias, then k increasing, one FMA each), so the
+// class is the reference's first column of the maximum, bit for bit.
+struct CtcMergeArgs {
+    const float *partial = nullptr;  // [pixels][blocks][3]
+    int blocks = 0, bn = 0;
+    const float *x = nullptr;        // [pixels][ci]
+    const float *w = nullptr;        // [cols/16][ci][16]
+    const float *b = nullptr;        // [cols]
+    float *y = nullptr;              // [pixels][2]
+    int pixels = 0, ci = 0, vocab = 0;
+    float wmax = 0.f, bmax = 0.f;    // largest |w| and |b| over the columns below vocab
+};
+int launch_ctc_tc_merge(const CtcMergeArgs &a, cudaStream_t s);
 
 // The input a multi-source convolution reads, written out: per pixel of the
 // conv's input size, the sources' channels side by side, each source read

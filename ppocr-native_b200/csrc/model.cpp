@@ -23,6 +23,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <chrono>
 #include <cstdio>
 #include <cstring>
@@ -103,6 +104,7 @@ struct Weights {
     DeviceBuffer tc_arena;
     std::vector<size_t> tc_hi_at, tc_lo_at;
     std::vector<int> tc_kpad;
+    std::vector<float> tc_wmax, tc_bmax;  // CTC heads: largest |w|, |b| over the live columns
     const float *tc_hi(size_t op) const {
         return tc_hi_at[op] == SIZE_MAX ? nullptr : static_cast<const float *>(tc_arena.p) + tc_hi_at[op];
     }
@@ -517,6 +519,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
         g.slots.push_back(std::move(b));
     }
     // Scratch.
+    const bool tc_allowed = !(options & PPOCR_OPT_NO_TENSOR_CORES);
     size_t mean_doubles = 1, ctc_floats = 1;
     for (size_t i = 0; i < p0.ops.size(); i++) {
         const Op &op = p0.ops[i];
@@ -529,11 +532,12 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             size_t vocab = op.kind == K_CTCHEAD ? op.oc : op.n2;
             size_t cols = (vocab + 15) / 16 * 16;
             ctc_floats = std::max(ctc_floats, size_t(total_in(g, i)) * ctc_col_blocks(int(cols)) * 3);
+            if (op.kind == K_CTCARGMAX && tc_allowed)
+                ctc_floats = std::max(ctc_floats, size_t(total_in(g, i)) * 2 * tc_stream_slices(int(cols)) * 3);
         }
     }
     // A windowed conv of several sources (or upsampled ones) on the tensor
     // cores reads them written out side by side.
-    const bool tc_allowed = !(options & PPOCR_OPT_NO_TENSOR_CORES);
     size_t concat_floats = 0;
     if (tc_allowed)
         for (const Step &st : steps) {
@@ -858,6 +862,26 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             a.vocab = int(a.probs ? op.oc : op.n2);
             a.cols = (a.vocab + 15) / 16 * 16;
             a.col_blocks = ctc_col_blocks(a.cols);
+            if (!a.probs && tc_allowed && W.tc_hi(i)) {
+                // the logits on the tensor cores, the classes checked exactly
+                TcArgs t;
+                t.stream_b = true;
+                t.x = a.x; t.C = t.K = a.ci; t.N = a.cols; t.kpad = W.tc_kpad[i];
+                t.w_hi = W.tc_hi(i); t.w_lo = W.tc_lo(i); t.b = a.b; t.y = a.y;
+                t.M = a.pixels; t.lanes = L; t.nl = nl; t.err = errp;
+                t.vocab = a.vocab; t.partial = a.partial;
+                CtcMergeArgs mg;
+                mg.partial = a.partial; mg.x = a.x; mg.w = a.w; mg.b = a.b; mg.y = a.y;
+                mg.pixels = a.pixels; mg.ci = a.ci; mg.vocab = a.vocab;
+                mg.wmax = W.tc_wmax[i]; mg.bmax = W.tc_bmax[i];
+                if (tc_prepare(t) &&
+                    size_t(a.pixels) * t.blocks * 3 * sizeof(float) <= g.ctc_scratch.bytes) {
+                    mg.blocks = t.blocks; mg.bn = t.bn;
+                    g.launches.push_back(
+                        [t, mg](cudaStream_t s) { return launch_tc(t, s) + launch_ctc_tc_merge(mg, s); });
+                    break;
+                }
+            }
             g.launches.push_back([a](cudaStream_t s) { return launch_ctc(a, s); });
             break;
         }
@@ -1012,15 +1036,19 @@ int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_mode
         w->b_at.push_back(place(op.b0, op.b1));
     }
     arena.resize(std::max<size_t>(arena.size(), 1) + 64, 0.0f);
-    // Tensor-core copies of the dense convolutions' weights: W [k][n] (k
-    // over kh, kw, C) to [n][kpad], the high tf32 half (low 13 mantissa bits
-    // cleared) and the exact remainder.
+    // Tensor-core copies of the dense convolutions' weights, W [k][n] (k over
+    // kh, kw, C), and of the CTC argmax heads', W [n/16][k][16]: to
+    // [n][kpad], the high tf32 half (low 13 mantissa bits cleared) and the
+    // exact remainder.
     std::vector<float> tc;
     for (const Op &op : plan.ops) {
         size_t hi = SIZE_MAX, lo = SIZE_MAX;
         int kpad = 0;
-        const int K = int(op.kh * op.kw * (op.ic + op.n2)), N = int(op.oc);
-        if (op.kind == K_CONV && op.w1 && tc_weights_wanted(K, N)) {
+        float wmax = 0.0f, bmax = 0.0f;
+        const bool ctc = op.kind == K_CTCARGMAX && op.w1;
+        const int K = ctc ? int(op.ic) : int(op.kh * op.kw * (op.ic + op.n2));
+        const int N = ctc ? int((op.n2 + 15) / 16 * 16) : int(op.oc);
+        if ((op.kind == K_CONV && op.w1 && tc_weights_wanted(K, N)) || ctc) {
             kpad = pw_tc_kpad(K);
             while (tc.size() % 64) tc.push_back(0.0f);
             hi = tc.size();
@@ -1028,7 +1056,8 @@ int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_mode
             tc.resize(lo + size_t(N) * kpad, 0.0f);
             for (int n = 0; n < N; n++)
                 for (int k = 0; k < K; k++) {
-                    float v = values[op.w0 + size_t(k) * N + n];
+                    const size_t at = ctc ? (size_t(n / 16) * K + k) * 16 + n % 16 : size_t(k) * N + n;
+                    float v = values[op.w0 + at];
                     uint32_t u;
                     std::memcpy(&u, &v, 4);
                     u &= 0xFFFFE000u;
@@ -1036,11 +1065,16 @@ int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_mode
                     std::memcpy(&h, &u, 4);
                     tc[hi + size_t(n) * kpad + k] = h;
                     tc[lo + size_t(n) * kpad + k] = v - h;
+                    if (ctc && n < int(op.n2)) wmax = std::max(wmax, std::fabs(v));
                 }
+            if (ctc)
+                for (int n = 0; n < int(op.n2); n++) bmax = std::max(bmax, std::fabs(values[op.b0 + size_t(n)]));
         }
         w->tc_hi_at.push_back(hi);
         w->tc_lo_at.push_back(lo);
         w->tc_kpad.push_back(kpad);
+        w->tc_wmax.push_back(wmax);
+        w->tc_bmax.push_back(bmax);
     }
     tc.resize(std::max<size_t>(tc.size(), 1) + 64, 0.0f);
     int code = PPOCR_E_DEVICE;

@@ -240,6 +240,37 @@ def test_ctc_head(cuda_mod, oracle_mod, t, ci, vocab):
         assert max_gap(got, oracle_run(oracle_mod, plan, x)[0]) <= 1e-6
 
 
+@pytest.mark.parametrize("bump,winner", [(0.0, 5.0), (1.2e-5, 300.0)], ids=["tie", "near-tie"])
+@pytest.mark.parametrize("options", [0, 4], ids=["tensor-cores", "fp32-cores"])
+def test_ctc_head_ties(cuda_mod, oracle_mod, options, bump, winner):
+    """Ties the tensor-core logits cannot order: columns 5, 300 and 700 share
+    weights and dominate every row; 700 copies 5 (an exact tie: the first
+    wins) and 300's bias is 5's plus `bump`, a few ulps of the logits, so
+    each row's class comes from the exact FP32 recompute."""
+    t, ci, vocab = 64, 120, 1000
+    cols = -(-vocab // 16) * 16
+    logical = noise(ci * vocab, 31, 0.05).reshape(ci, vocab)
+    bias = noise(vocab, 37, 0.5)
+    strong = np.abs(noise(ci, 41, 1.0)) + np.float32(0.5)
+    for c in (5, 300, 700):
+        logical[:, c] = strong
+        bias[c] = bias[5]
+    bias[300] = bias[5] + np.float32(bump)
+    full = np.zeros((ci, cols), np.float32)
+    full[:, :vocab] = logical
+    w = full.reshape(ci, cols // 16, 16).transpose(1, 0, 2).copy()
+    b = np.full(cols, -1e30, np.float32)
+    b[:vocab] = bias
+    op = Op("ctcargmax", x=0, y=1, ic=ci, oc=2, n2=vocab, w=(0, w.size), b=(w.size, cols))
+    plan = single(op, (1, t, ci), np.concatenate([w.reshape(-1), b]))
+    x = np.abs(noise(t * ci, 43, 1.0))
+    got = gpu_run(cuda_mod, plan, x, options=options)[0][0].reshape(t, 2)
+    want = oracle_run(oracle_mod, plan, x)[0].reshape(t, 2)
+    assert set(want[:, 0].tolist()) == {winner}
+    assert np.array_equal(got[:, 0], want[:, 0])
+    assert max_gap(got[:, 1], want[:, 1]) <= 1e-5
+
+
 @pytest.mark.parametrize("ic,oc,k,fused", [(5, 3, 2, "none"), (24, 24, 2, "relu"), (24, 1, 2, "sigmoid"),
                                            (16, 4, 3, "swish")])
 def test_convtranspose(cuda_mod, oracle_mod, ic, oc, k, fused):

@@ -684,9 +684,13 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
 // order; then every block within the margin of the row's maximum has its 16
 // x (bn / 32) columns recomputed exactly, lanes two columns each.
 __global__ void __launch_bounds__(256) ctc_tc_merge_kernel(const CtcMergeArgs a) {
+    extern __shared__ float xrow[];  // [8 warps][ci]: each warp's input row
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const long t = (long)blockIdx.x * 8 + warp;
     if (t >= a.pixels) return;
+    float *xs = xrow + warp * a.ci;
+    for (int k = lane; k < a.ci; k += 32) xs[k] = __ldg(a.x + t * a.ci + k);
+    __syncwarp();
     const float *st = a.partial + t * a.blocks * 3;
     float m = -FLT_MAX;
     for (int b = lane; b < a.blocks; b += 32) m = fmaxf(m, st[b * 3]);
@@ -705,9 +709,8 @@ __global__ void __launch_bounds__(256) ctc_tc_merge_kernel(const CtcMergeArgs a)
     // roundings of 2^-23 relative in either form (three products per k on
     // the tensor core, the dropped low-low term, the bias), so
     // 2 * 2 * (3k + 8) * 2^-23 * (wmax * sum|x| + bmax) covers both errors.
-    const float *x = a.x + t * a.ci;
     float ax = 0.0f;
-    for (int k = lane; k < a.ci; k += 32) ax += fabsf(x[k]);
+    for (int k = lane; k < a.ci; k += 32) ax += fabsf(xs[k]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ax += __shfl_xor_sync(0xffffffffu, ax, off);
     const float margin = 4.0f * float(3 * a.ci + 8) * 1.1920929e-7f * (ax * a.wmax + a.bmax) * 1.01f;
@@ -725,7 +728,15 @@ __global__ void __launch_bounds__(256) ctc_tc_merge_kernel(const CtcMergeArgs a)
                 if (col >= a.vocab) continue;
                 float acc = __ldg(a.b + col);
                 const float *wc = a.w + (long)(col >> 4) * a.ci * 16 + (col & 15);
-                for (int k = 0; k < a.ci; k++) acc = ffma(__ldg(wc + k * 16), x[k], acc);
+                // eight weights in flight, then their terms in k order
+                for (int k0 = 0; k0 < a.ci; k0 += 8) {
+                    float wv[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) wv[j] = k0 + j < a.ci ? __ldg(wc + (k0 + j) * 16) : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        if (k0 + j < a.ci) acc = ffma(wv[j], xs[k0 + j], acc);
+                }
                 if (acc > best_v || (acc == best_v && col < best)) {
                     best_v = acc;
                     best = col;
@@ -838,20 +849,28 @@ bool tc_prepare(TcArgs &a) {
     a.nkb = a.kpad / TK;
     if (a.C % 4 || !aligned(a.x) || (a.gate && !aligned(a.gate))) return false;
     if (a.vocab > 0 && (a.windowed || !a.stream_b || a.act || a.res || a.gate || !a.partial)) return false;
+    if (a.windowed) {
+        // a tap's K blocks never straddle taps; the output keeps the input's
+        // size, so the packed input has M pixels too
+        if (a.gate || a.C % TK || a.tiles < 1 || a.K != a.kh * a.kw * a.C) return false;
+    } else {
+        // 1x1: the packed input is [M][K]; its weights stay resident unless
+        // streaming them takes fewer slices
+        if (a.K != a.C || a.kh * a.kw != 1) return false;
+        if (!a.stream_b) {
+            const int bn = pw_slice_width(a.K, a.N);
+            const int streamed = tc_stream_slices(a.N);
+            if (streamed > 0 && (!bn || streamed < (a.N + bn - 1) / bn)) a.stream_b = true;
+            if (!bn && !a.stream_b) return false;
+        }
+    }
     if (!a.windowed && !a.stream_b) {
-        // 1x1: the packed input is [M][K]
-        if (a.K != a.C) return false;
         a.bn = pw_slice_width(a.K, a.N);
-        if (!a.bn) return false;
         a.slices = (a.N + a.bn - 1) / a.bn;
         a.ns = 2;
         while (a.ns < MAX_NS && pw_smem(a.kpad, a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
         a.smem = int(pw_smem(a.kpad, a.bn, a.ns));
     } else {
-        // a tap's K blocks never straddle taps; the output keeps the input's
-        // size, so the packed input has M pixels too
-        if (a.gate || a.K != a.kh * a.kw * a.C) return false;
-        if (a.windowed ? (a.C % TK || a.tiles < 1) : (a.kh * a.kw != 1)) return false;
         a.bn = conv_slice_width(a.N);
         if (!a.bn) return false;
         a.slices = (a.N + a.bn - 1) / a.bn;
@@ -875,7 +894,7 @@ bool tc_prepare(TcArgs &a) {
 }
 
 int launch_ctc_tc_merge(const CtcMergeArgs &a, cudaStream_t s) {
-    ctc_tc_merge_kernel<<<unsigned((a.pixels + 7) / 8), 256, 0, s>>>(a);
+    ctc_tc_merge_kernel<<<unsigned((a.pixels + 7) / 8), 256, sizeof(float) * 8 * a.ci, s>>>(a);
     return 1;
 }
 

@@ -483,7 +483,7 @@ def main():
         result = run_reference(args, d)
     else:
         result = run_ours(args, d)
-        if result is not None and not args.profile:
+        if result is not None and not args.profile and args.workload == "page":
             if args.no_cpu_baseline:
                 result["cpu_baseline"] = None
             else:

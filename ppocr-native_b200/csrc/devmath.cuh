@@ -41,17 +41,21 @@ __device__ __forceinline__ float exp_neg(float z) {
 
 // A quotient: IEEE-rounded, or (QUICK) __fdividef's reciprocal and product,
 // within 2 ulp, for callers whose sums already differ from the reference's
-// by a few units and whose denominators lie in [1, 2^20].
+// by a few units and whose denominators lie in [1, 2^20]. QUICK forms serve
+// the tensor-core epilogues only.
 template <bool QUICK>
 __device__ __forceinline__ float quot(float a, float b) {
     return QUICK ? __fdividef(a, b) : fdiv(a, b);
 }
 
 // activation.rs:151-159: e / (e + 1) for negative x, 1 minus it otherwise.
+// QUICK: 1 / (1 + e^-x) with CUDA's __expf and __fdividef (a few ulp; 0 and
+// 1 at the far ends as e^-x overflows or vanishes).
 template <bool QUICK = false>
 __device__ __forceinline__ float sigmoid_one(float x) {
+    if (QUICK) return __fdividef(1.0f, 1.0f + __expf(-x));
     float e = exp_neg(__uint_as_float(__float_as_uint(x) | 0x80000000u));
-    float f = quot<QUICK>(e, fadd(e, 1.0f));
+    float f = fdiv(e, fadd(e, 1.0f));
     return (__float_as_uint(x) >> 31) ? f : fsub(1.0f, f);
 }
 

@@ -873,6 +873,10 @@ bool tc_prepare(TcArgs &a) {
     } else {
         a.bn = conv_slice_width(a.N);
         if (!a.bn) return false;
+        // few tiles: narrower slices, so that more SMs share the layer (each
+        // output's sum is the same whatever the slice)
+        const long tiles = a.windowed ? a.tiles : (a.M + TM - 1) / TM;
+        while (a.bn > 32 && tiles * ((a.N + a.bn - 1) / a.bn) < 74) a.bn -= 32;
         a.slices = (a.N + a.bn - 1) / a.bn;
         a.ns = 2;
         while (a.ns < MAX_NS && conv_smem(a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;

@@ -218,20 +218,26 @@ __global__ void __launch_bounds__(128) layernorm_kernel(const LayerNormArgs a) {
 
 // --------------------------------------------------------------- attention
 
-// One block per (lane, head), one thread per query. Per query, as the
-// reference (layers.rs:488-522 with softmax_row :254-294): scores
-// (q * scale) . k summed over the head dimension in order; the maximum; the
-// exponentials summed in 8 lanes (element j in lane j % 8) over whole groups
-// of eight, the lanes folded in order, the rest added one at a time; each
-// probability e * (1 / sum); the output sum of v * p over the keys in order.
-// Scores and exponentials are recomputed per pass instead of stored: the
-// same operations give the same bits.
+// One block per (lane, head, run of ATT_Q queries), one thread per query. Per
+// query, as the reference (layers.rs:488-522 with softmax_row :254-294):
+// scores (q * scale) . k summed over the head dimension in order; the
+// maximum; the exponentials summed in 8 lanes (element j in lane j % 8) over
+// whole groups of eight, the lanes folded in order, the rest added one at a
+// time; each probability e * (1 / sum); the output sum of v * p over the
+// keys in order. Scores and exponentials are recomputed per pass instead of
+// stored (the same operations give the same bits), four keys at a time so
+// that their independent chains overlap; every running sum still takes its
+// terms in key order.
+constexpr int ATT_Q = 128;
+
 template <int HD>
-__global__ void attention_kernel(const AttentionArgs a) {
+__global__ void __launch_bounds__(ATT_Q) attention_kernel(const AttentionArgs a) {
     extern __shared__ float kv[];  // K [t][hd], V [t][hd]
     const int n = blockIdx.x / a.heads, h = blockIdx.x % a.heads;
     const LaneInfo &L = a.lanes[n];
     const int hd = HD > 0 ? HD : a.c / a.heads, t = L.iw, c = a.c;
+    const int s = blockIdx.y * ATT_Q + threadIdx.x;
+    if (blockIdx.y * ATT_Q >= t) return;
     float *K = kv, *V = kv + t * hd;
     const float *x = a.x + L.ipix0 * 3 * c;
     for (int i = threadIdx.x; i < t * hd; i += blockDim.x) {
@@ -240,53 +246,76 @@ __global__ void attention_kernel(const AttentionArgs a) {
         V[i] = x[(long)j * 3 * c + 2 * c + h * hd + d];
     }
     __syncthreads();
+    if (s >= t) return;
     const float scale = a.scale[0];
     constexpr int MAXHD = HD > 0 ? HD : 64;
-    for (int s = threadIdx.x; s < t; s += blockDim.x) {
-        float q[MAXHD];
+    float q[MAXHD];
+#pragma unroll
+    for (int d = 0; d < MAXHD; d++)
+        if (d < hd) q[d] = fmul(x[(long)s * 3 * c + h * hd + d], scale);
+    auto score = [&](int j) {
+        float acc = 0.0f;
+        const float *k = K + j * hd;
 #pragma unroll
         for (int d = 0; d < MAXHD; d++)
-            if (d < hd) q[d] = fmul(x[(long)s * 3 * c + h * hd + d], scale);
-        auto score = [&](int j) {
-            float acc = 0.0f;
-            const float *k = K + j * hd;
+            if (d < hd) acc = ffma(k[d], q[d], acc);
+        return acc;
+    };
+    float mx = -FLT_MAX;
+    bool any = false;
+    int j = 0;
+    for (; j + 4 <= t; j += 4) {
+        float v[4];
 #pragma unroll
-            for (int d = 0; d < MAXHD; d++)
-                if (d < hd) acc = ffma(k[d], q[d], acc);
-            return acc;
-        };
-        float mx = -FLT_MAX;
-        bool any = false;
-        for (int j = 0; j < t; j++) {
-            float v = score(j);
-            if (!any || v > mx) mx = v;
+        for (int u = 0; u < 4; u++) v[u] = score(j + u);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            if (!any || v[u] > mx) mx = v[u];
             any = true;
         }
-        const int body = t / 8 * 8;
-        float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int j0 = 0; j0 < body; j0 += 8)
+    }
+    for (; j < t; j++) {
+        float v = score(j);
+        if (!any || v > mx) mx = v;
+        any = true;
+    }
+    const int body = t / 8 * 8;
+    float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j0 = 0; j0 < body; j0 += 8)
 #pragma unroll
-            for (int l = 0; l < 8; l++) lanes[l] = fadd(lanes[l], exp_neg(fsub(score(j0 + l), mx)));
-        float sum = 0.0f;
+        for (int l = 0; l < 8; l++) lanes[l] = fadd(lanes[l], exp_neg(fsub(score(j0 + l), mx)));
+    float sum = 0.0f;
 #pragma unroll
-        for (int l = 0; l < 8; l++) sum = fadd(sum, lanes[l]);
-        for (int j = body; j < t; j++) sum = fadd(sum, exp_neg(fsub(score(j), mx)));
-        float r = fdiv(1.0f, sum);
-        float out[MAXHD];
+    for (int l = 0; l < 8; l++) sum = fadd(sum, lanes[l]);
+    for (int jj = body; jj < t; jj++) sum = fadd(sum, exp_neg(fsub(score(jj), mx)));
+    float r = fdiv(1.0f, sum);
+    float out[MAXHD];
 #pragma unroll
-        for (int d = 0; d < MAXHD; d++) out[d] = 0.0f;
-        for (int j = 0; j < t; j++) {
-            float p = fmul(exp_neg(fsub(score(j), mx)), r);
-            const float *v = V + j * hd;
+    for (int d = 0; d < MAXHD; d++) out[d] = 0.0f;
+    j = 0;
+    for (; j + 4 <= t; j += 4) {
+        float p[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) p[u] = fmul(exp_neg(fsub(score(j + u), mx)), r);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const float *v = V + (j + u) * hd;
 #pragma unroll
             for (int d = 0; d < MAXHD; d++)
-                if (d < hd) out[d] = ffma(v[d], p, out[d]);
+                if (d < hd) out[d] = ffma(v[d], p[u], out[d]);
         }
-        float *y = a.y + (L.pix0 + s) * c + h * hd;
+    }
+    for (; j < t; j++) {
+        float p = fmul(exp_neg(fsub(score(j), mx)), r);
+        const float *v = V + j * hd;
 #pragma unroll
         for (int d = 0; d < MAXHD; d++)
-            if (d < hd) y[d] = out[d];
+            if (d < hd) out[d] = ffma(v[d], p, out[d]);
     }
+    float *y = a.y + (L.pix0 + s) * c + h * hd;
+#pragma unroll
+    for (int d = 0; d < MAXHD; d++)
+        if (d < hd) y[d] = out[d];
 }
 
 // --------------------------------------------------------------------- ctc
@@ -536,11 +565,11 @@ bool attention_supported(int t, int c, int heads) {
 int launch_attention(const AttentionArgs &a, cudaStream_t s) {
     int hd = a.c / a.heads;
     size_t smem = sizeof(float) * 2 * a.tmax * hd;
-    int threads = a.tmax < 32 ? 32 : (a.tmax > 256 ? 256 : (a.tmax + 31) / 32 * 32);
+    dim3 grid(unsigned(a.nl * a.heads), unsigned((a.tmax + ATT_Q - 1) / ATT_Q));
     if (hd == 15)  // PP-OCRv6's 8 heads of 15 (tools/export_ocr.py:654)
-        attention_kernel<15><<<a.nl * a.heads, threads, smem, s>>>(a);
+        attention_kernel<15><<<grid, ATT_Q, smem, s>>>(a);
     else
-        attention_kernel<0><<<a.nl * a.heads, threads, smem, s>>>(a);
+        attention_kernel<0><<<grid, ATT_Q, smem, s>>>(a);
     return 1;
 }
 

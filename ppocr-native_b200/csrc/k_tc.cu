@@ -400,14 +400,18 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
 // (one pixel) of 16 columns; it stages them as four 16-byte chunks of its row
 // (chunk q at q ^ ((row >> 1) & 3), so that eight lanes cover all 32 banks),
 // and the warp then writes 8 rows x 64 bytes per store.
-template <int ACT, bool CTC>
+// Epilogue modes: the plain store, the CTC argmax partials, a transposed
+// conv's scattered store.
+enum EpiMode : int { EPI_PLAIN = 0, EPI_CTC = 1, EPI_CONVT = 2 };
+
+template <int ACT, int MODE>
 __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, int lane, uint32_t staging,
                               const float *bias_s) {
     const int qd = warp & 3;  // the TMEM lane quadrant this warp may read
     const int half = e / 4;   // which alternate 16-column chunks it takes
     const uint32_t stg = staging + uint32_t(e * STAGE_FLOATS * 4);
     const int q = lane & 3;   // read-back chunk of this lane
-    const bool vec = (a.N & 3) == 0;
+    const bool vec = (a.N & 3) == 0 && (MODE != EPI_CONVT || (a.toc & 3) == 0);
     long job = 0;
     for (long t = x.first; t < x.tiles; t += x.Q, job++) {
         const int buf = int(job & 1);
@@ -418,7 +422,20 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
         const TileInfo ti = tile_info(a, t);
         const long mrow = ti.m0 + qd * 32;
         const int nrows = ti.rows - qd * 32;  // rows of this warp's quadrant that exist
-        if (CTC) {
+        // a transposed conv: this lane's row (an input pixel) and where its
+        // kh x kw output block starts
+        long tbase = 0;
+        int tow = 0;
+        if (MODE == EPI_CONVT && lane < nrows) {
+            const long m = mrow + lane;
+            const LaneInfo &L = a.lanes[find_lane(a.lanes, a.nl, m, true)];
+            const int iw = __ldg(&L.iw);
+            const int qq = int(m - __ldg(&L.ipix0));
+            const int iy = qq / iw, ix = qq - iy * iw;
+            tow = __ldg(&L.ow);
+            tbase = __ldg(&L.pix0) + (long)iy * a.tkh * tow + (long)ix * a.tkw;
+        }
+        if (MODE == EPI_CTC) {
             // this thread's row over the columns of its block, in increasing
             // column order: an online softmax keeping the first maximum
             float m = -FLT_MAX, sum = 0.0f;
@@ -464,13 +481,28 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
             }
             __syncwarp();
             const int n = x.n0 + c0 + 4 * q;
+            // a transposed conv's column n is tap (ky, kx), channel o
+            int tap_off = 0, o_ch = 0;
+            if (MODE == EPI_CONVT) {
+                const int tap = n / a.toc, ky = tap / a.tkw;
+                o_ch = n - tap * a.toc;
+                tap_off = ky * 0x10000 + (tap - ky * a.tkw);
+            }
 #pragma unroll
             for (int p = 0; p < 4; p++) {
                 const int r = 8 * p + (lane >> 2);
                 float4 o = lds4(stg + uint32_t(r * 64 + ((q ^ ((r >> 1) & 3)) << 4)));
+                long ob = 0;
+                int ow2 = 0;
+                if (MODE == EPI_CONVT) {
+                    ob = __shfl_sync(0xffffffffu, tbase, r);
+                    ow2 = __shfl_sync(0xffffffffu, tow, r);
+                }
                 if (r >= nrows || n >= a.N) continue;
                 const long m = mrow + r;
-                float *dst = a.y + m * a.N + n;
+                float *dst = MODE == EPI_CONVT
+                                 ? a.y + (ob + (long)(tap_off >> 16) * ow2 + (tap_off & 0xffff)) * a.toc + o_ch
+                                 : a.y + m * a.N + n;
                 if (vec) {
                     if (a.res) {
                         const float4 rr = __ldg(reinterpret_cast<const float4 *>(a.res + m * a.N + n));
@@ -485,7 +517,13 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
                         if (n + c >= a.N) break;
                         float y = ov[c];
                         if (a.res) y = activate(a.act2, fadd(y, __ldg(a.res + m * a.N + n + c)));
-                        dst[c] = y;
+                        if (MODE == EPI_CONVT) {
+                            // column n + c: its own tap when the channels end
+                            const int tap = (n + c) / a.toc, ky = tap / a.tkw;
+                            a.y[(ob + (long)ky * ow2 + (tap - ky * a.tkw)) * a.toc + (n + c - tap * a.toc)] = y;
+                        } else {
+                            dst[c] = y;
+                        }
                     }
                 }
             }
@@ -538,7 +576,7 @@ __device__ __forceinline__ void teardown(const TcArgs &a, const Ctx &x) {
     }
 }
 
-template <int ACT, bool CTC = false>
+template <int ACT, int MODE = EPI_PLAIN>
 __global__ void __launch_bounds__(Roles::THREADS, 1)
     pw_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw) {
     using R = Roles;
@@ -599,12 +637,12 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
     } else if (warp < R::W_EPI) {
         role_convert(a, x, tid - R::W_CONV * 32);
     } else {
-        role_epilogue<ACT, CTC>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
+        role_epilogue<ACT, MODE>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
     }
     teardown<R>(a, x);
 }
 
-template <int ACT, bool CTC = false>
+template <int ACT, int MODE = EPI_PLAIN>
 __global__ void __launch_bounds__(Roles::THREADS, 1)
     conv_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw) {
     using R = Roles;
@@ -675,7 +713,7 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
     } else if (warp < R::W_EPI) {
         role_convert(a, x, tid - R::W_CONV * 32);
     } else {
-        role_epilogue<ACT, CTC>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
+        role_epilogue<ACT, MODE>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
     }
     teardown<R>(a, x);
 }
@@ -849,6 +887,12 @@ bool tc_prepare(TcArgs &a) {
     a.nkb = a.kpad / TK;
     if (a.C % 4 || !aligned(a.x) || (a.gate && !aligned(a.gate))) return false;
     if (a.vocab > 0 && (a.windowed || !a.stream_b || a.act || a.res || a.gate || !a.partial)) return false;
+    if (a.tkh) {
+        // the scattering epilogue lives in the streaming kernel; its stores
+        // are 16-byte runs of one tap's channels
+        if (a.windowed || a.res || a.gate || a.vocab || a.N != a.tkh * a.tkw * a.toc || a.toc % 4) return false;
+        a.stream_b = true;
+    }
     if (a.windowed) {
         // a tap's K blocks never straddle taps; the output keeps the input's
         // size, so the packed input has M pixels too
@@ -911,10 +955,11 @@ template <int ACT>
 void configure_act() {
     cudaFuncSetAttribute(pw_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
     cudaFuncSetAttribute(conv_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
+    cudaFuncSetAttribute(conv_tc_kernel<ACT, EPI_CONVT>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
 }
 
 void configure_tc_kernels() {
-    cudaFuncSetAttribute(conv_tc_kernel<0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
+    cudaFuncSetAttribute(conv_tc_kernel<0, EPI_CTC>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
     configure_act<0>(); configure_act<1>(); configure_act<2>(); configure_act<3>();
     configure_act<4>(); configure_act<5>(); configure_act<6>(); configure_act<7>();
 }
@@ -922,7 +967,9 @@ void configure_tc_kernels() {
 template <int ACT>
 void launch_act(const TcArgs &a, const CUtensorMap &mx, const CUtensorMap &mw, cudaStream_t s) {
     if (a.vocab > 0)
-        conv_tc_kernel<0, true><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
+        conv_tc_kernel<0, EPI_CTC><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
+    else if (a.tkh)
+        conv_tc_kernel<ACT, EPI_CONVT><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
     else if (a.windowed || a.stream_b)
         conv_tc_kernel<ACT><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
     else

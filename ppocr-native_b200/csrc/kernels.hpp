@@ -224,6 +224,10 @@ struct TcArgs {
     int vocab = 0;
     float *partial = nullptr;
     int blocks = 0;               // filled: 2 * slices
+    // A non-overlapping transposed conv (tkh > 0): rows are input pixels
+    // (lanes by ipix0), column n = (ky * tkw + kx) * toc + o goes to output
+    // pixel (iy * tkh + ky, ix * tkw + kx) of the lane (pix0, ow), channel o.
+    int tkh = 0, tkw = 0, toc = 0;
     // filled by tc_prepare: output-channel slice width and count, K blocks,
     // ring stages, TMEM columns, grid, dynamic shared memory, and the tensor
     // maps (CUtensorMap, 128 bytes each) of the input and of the weights

@@ -891,6 +891,19 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             a.lanes = L; a.nl = nl; a.Min = total_in(g, i); a.ic = int(op.ic); a.oc = int(op.oc);
             a.kh = int(op.kh); a.kw = int(op.kw); a.act = op.fused;
             a.bias_first = (op.kh * op.kw * op.oc) % 16 == 0;
+            if (tc_allowed && W.tc_hi(i)) {
+                // a pointwise GEMM ic -> kh*kw*oc whose epilogue places each
+                // column in its output pixel
+                TcArgs t;
+                t.x = a.x; t.C = t.K = a.ic; t.N = a.kh * a.kw * a.oc; t.kpad = W.tc_kpad[i];
+                t.w_hi = W.tc_hi(i); t.w_lo = W.tc_lo(i); t.b = a.b; t.y = a.y;
+                t.M = a.Min; t.lanes = L; t.nl = nl; t.act = a.act; t.err = errp;
+                t.tkh = a.kh; t.tkw = a.kw; t.toc = a.oc;
+                if (tc_prepare(t)) {
+                    g.launches.push_back([t](cudaStream_t s) { return launch_tc(t, s); });
+                    break;
+                }
+            }
             g.launches.push_back([a](cudaStream_t s) { return launch_convt(a, s); });
             break;
         }
@@ -1046,9 +1059,10 @@ int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_mode
         int kpad = 0;
         float wmax = 0.0f, bmax = 0.0f;
         const bool ctc = op.kind == K_CTCARGMAX && op.w1;
-        const int K = ctc ? int(op.ic) : int(op.kh * op.kw * (op.ic + op.n2));
-        const int N = ctc ? int((op.n2 + 15) / 16 * 16) : int(op.oc);
-        if ((op.kind == K_CONV && op.w1 && tc_weights_wanted(K, N)) || ctc) {
+        const bool convt = op.kind == K_CONVTRANSPOSE && op.w1;  // [ic][kh][kw][oc]: K = ic
+        const int K = ctc || convt ? int(op.ic) : int(op.kh * op.kw * (op.ic + op.n2));
+        const int N = ctc ? int((op.n2 + 15) / 16 * 16) : convt ? int(op.kh * op.kw * op.oc) : int(op.oc);
+        if (((op.kind == K_CONV || convt) && op.w1 && tc_weights_wanted(K, N)) || ctc) {
             kpad = pw_tc_kpad(K);
             while (tc.size() % 64) tc.push_back(0.0f);
             hi = tc.size();

@@ -281,7 +281,7 @@ def test_convtranspose(cuda_mod, oracle_mod, ic, oc, k, fused):
     op = Op("convtranspose", x=0, y=1, ic=ic, oc=oc, kh=k, kw=k, sh=k, sw=k, fused=fused,
             w=(0, wt.size), b=(wt.size, b.size))
     plan = single(op, (h, w, ic), np.concatenate([wt, b]))
-    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+    check_both(cuda_mod, oracle_mod, plan, x)
 
 
 # ---------------------------------------------------------- fused layers, nets
@@ -326,6 +326,31 @@ def test_detector_960x736(cuda_mod, oracle_mod, std):
     check(got[0], want, exact=False)
     got, _ = gpu_run(cuda_mod, plan, x, options=cuda_mod.OPT_NO_TENSOR_CORES)
     check(got[0], want)
+
+
+def test_detector_lanes(cuda_mod, oracle_mod):
+    """Three pages of different sizes in one detector run (lane-packed
+    windowed convs, transposed convs and gates on the tensor cores): each
+    within the tolerance of the oracle, and bit-identical to the oracle with
+    every contraction on the FP32 cores."""
+    plan = synth.det_plan(seed=11, std=None, size=(96, 64))
+    sizes = [(96, 64), (64, 128), (32, 96)]
+    xs = [synth.stripes(h, w, phase=7 * i) for i, (h, w) in enumerate(sizes)]
+    o = oracle_mod.Oracle(plan)
+    wants = []
+    for (h, w), x in zip(sizes, xs):
+        o.set_size(h, w)
+        wants.append(o.run(x)[0])
+    for options in (0, cuda_mod.OPT_NO_TENSOR_CORES):
+        with cuda_mod.Model(plan) as m:
+            if options:
+                m.set_options(options)
+            m.set_sizes(sizes)
+            for i, x in enumerate(xs):
+                m.lane_input_mut(i)[:] = x
+            m.run(60_000)
+            for i, want in enumerate(wants):
+                check(m.lane_output(i).copy(), want, exact=bool(options))
 
 
 def test_detector_unfused_matches_fused(cuda_mod):

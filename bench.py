@@ -37,11 +37,15 @@ PKG_DIR = ROOT / "ppocr-native_b200"
 sys.path.insert(0, str(ROOT))
 
 L2_FLUSH_BYTES = 256 << 20  # larger than the 126 MB L2
-# DRAM bytes (read + written) of one launch of the probed kernel, from one ncu
-# capture of `bench.py --workload layer` (profiles/pw_tc_kernel_1x1_24to24_992x768.md);
-# writes still dirty in L2 when the kernel ends are not counted there.
-TRAFFIC_PER_LAUNCH = 99.59e6
+# DRAM bytes (read + written) of one launch of the pointwise probe, from one
+# ncu capture of `bench.py --workload layer`
+# (profiles/pw_tc_kernel_1x1_24to24_992x768.md); writes still dirty in L2 when
+# the kernel ends are not counted there.
+TRAFFIC_PER_LAUNCH = 100.64e6
 TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch (profiles/pw_tc_kernel_1x1_24to24_992x768.md)"
+# The same for the dominant kernel's probe (`bench.py --workload conv3x3`).
+CONV_TRAFFIC_PER_LAUNCH = None
+CONV_TRAFFIC_SOURCE = "not captured yet"
 
 
 def package():
@@ -221,49 +225,57 @@ class PagePipeline:
             m.close()
 
 
-DOMINANT = (992, 768, 24, 24)  # h, w, ic, oc of the probed pointwise layer
+# The probed layers: the page's dominant kernel (conv_tc_kernel, the
+# tensor-core implicit GEMM for stride-1 windowed convolutions, the largest
+# share of a page's launch time) at its most common launch, the detector's
+# 3x3 96 -> 24 RSE convolution at a quarter of a 1984 x 1536 page; and the
+# pointwise kernel (pw_tc_kernel) at its largest launch, the detector's first
+# 1x1 24 -> 24 + swish at half the page.
+LAYERS = {
+    "conv3x3": dict(h=496, w=384, ic=96, oc=24, k=3, fused="none",
+                    kernel="conv_tc_kernel: 3x3 96->24 @ 496x384 (3xTF32 tcgen05, the RSE neck's convolution)"),
+    "layer": dict(h=992, w=768, ic=24, oc=24, k=1, fused="swish",
+                  kernel="pw_tc_kernel: 1x1 24->24 + swish @ 992x768 (3xTF32 tcgen05, the detector's first pointwise)"),
+}
 
 
-def dominant_plan() -> bytes:
-    """The page's dominant kernel class alone: pointwise layers on the
-    tensor cores (pw_tc_kernel, the largest share of a page's launch time),
-    here its largest launch, the detector's first 1x1 24 -> 24 + swish at
-    half of a 1984 x 1536 page (992 x 768 pixels)."""
+def layer_plan(name: str) -> bytes:
     from ppocr_native_b200.plan import Op, encode, window
 
-    h, w, ic, oc = DOMINANT
+    L = LAYERS[name]
     rng = np.random.default_rng(0)
-    wt = rng.normal(0, 0.02, ic * oc).astype(np.float32)
-    b = rng.normal(0, 0.02, oc).astype(np.float32)
-    op = window(Op("conv", x=0, y=1, ic=ic, oc=oc, fused="swish", w=(0, wt.size), b=(wt.size, oc)), (1, 1), 1, 0, 0)
-    return encode((0, h, w, ic), 2, [1], [op], np.concatenate([wt, b]))
+    wt = rng.normal(0, 0.02, L["k"] * L["k"] * L["ic"] * L["oc"]).astype(np.float32)
+    b = rng.normal(0, 0.02, L["oc"]).astype(np.float32)
+    op = window(Op("conv", x=0, y=1, ic=L["ic"], oc=L["oc"], fused=L["fused"], w=(0, wt.size), b=(wt.size, L["oc"])),
+                (L["k"], L["k"]), 1, L["k"] // 2, L["k"] // 2)
+    return encode((0, L["h"], L["w"], L["ic"]), 2, [1], [op], np.concatenate([wt, b]))
 
 
 def run_layer(args, d, cuda, torch, device):
-    """--workload layer: the dominant layer alone, warm-up then timed steps
-    (the command ncu captures)."""
-    m = cuda.Model(dominant_plan(), device=device)
-    h, w, ic, _ = DOMINANT
-    m.input_mut()[:] = np.random.default_rng(0).standard_normal(h * w * ic).astype(np.float32)
+    """--workload layer | conv3x3: the probed layer alone, warm-up then timed
+    steps (the command ncu captures)."""
+    L = LAYERS[args.workload]
+    m = cuda.Model(layer_plan(args.workload), device=device)
+    m.input_mut()[:] = np.random.default_rng(0).standard_normal(L["h"] * L["w"] * L["ic"]).astype(np.float32)
     m.run(60_000)
     for _ in range(args.warmup + args.steps):
         m.enqueue_device()
     m.wait(60_000)
     m.close()
-    return {"profile": "layer", "launches_per_step": 1} if d.rank == 0 else None
+    return {"profile": args.workload, "launches_per_step": 1} if d.rank == 0 else None
 
 
-def probe_kernel(cuda, torch, device: int, reps: int = 20) -> dict:
-    """Time the dominant kernel alone with CUDA events on the model's stream,
-    L2 flushed before each launch (see `dominant_plan`). Algorithmic bytes:
-    the input and output maps once, the split weights (two tf32 halves,
-    K padded to 32) and the bias."""
-    h, w, ic, oc = DOMINANT
+def probe_kernel(cuda, torch, device: int, name: str, reps: int = 20) -> dict:
+    """Time one probed layer alone with CUDA events on the model's stream, L2
+    flushed before each launch. Algorithmic bytes: the input and output maps
+    once, the split weights (two tf32 halves, K padded to 32) and the bias;
+    FLOPs: 2 per multiply-add of the convolution (FP32 arithmetic)."""
+    L = LAYERS[name]
+    h, w, ic, oc, k = L["h"], L["w"], L["ic"], L["oc"], L["k"]
     rng = np.random.default_rng(0)
-    m = cuda.Model(dominant_plan(), device=device)
+    m = cuda.Model(layer_plan(name), device=device)
     assert m.steps() == ["conv"]
-    x = rng.standard_normal(h * w * ic).astype(np.float32)
-    m.input_mut()[:] = x
+    m.input_mut()[:] = rng.standard_normal(h * w * ic).astype(np.float32)
     m.run(60_000)
     stream = torch.cuda.ExternalStream(m.stream)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
@@ -282,10 +294,10 @@ def probe_kernel(cuda, torch, device: int, reps: int = 20) -> dict:
             times.append(e0.elapsed_time(e1) / 1e3)
     m.close()
     t = statistics.median(times)
-    kpad = -(-ic // 32) * 32
-    algo_bytes = 4 * (h * w * ic + h * w * oc + 2 * oc * kpad + oc)
-    return {"kernel": "pw_tc_kernel: 1x1 24->24 + swish @ 992x768 (3xTF32 tcgen05, the detector's first pointwise)",
-            "seconds": t, "bytes": algo_bytes, "flops": 2 * h * w * ic * oc}
+    kk = k * k * ic
+    kpad = -(-kk // 32) * 32
+    return {"kernel": L["kernel"], "seconds": t, "flops": 2 * h * w * kk * oc,
+            "bytes": 4 * (h * w * ic + h * w * oc + 2 * oc * kpad + oc)}
 
 
 def cpu_baseline(widths_seed: int = 0, budget_s: float = 20.0) -> dict:
@@ -329,7 +341,7 @@ def run_ours(args, d: Dist) -> dict | None:
     device = d.local
     torch.cuda.set_device(device)
     d.init("nccl")
-    if args.workload == "layer":
+    if args.workload in LAYERS:
         return run_layer(args, d, cuda, torch, device)
     page = workload.Page(seed=1000 + d.rank)
     pipe = PagePipeline(cuda, synth, page, device, args.workload)
@@ -404,13 +416,18 @@ def run_ours(args, d: Dist) -> dict | None:
 
     result = None
     if d.rank == 0:
-        probe = probe_kernel(cuda, torch, device)
+        probe = probe_kernel(cuda, torch, device, "conv3x3")
+        pw = probe_kernel(cuda, torch, device, "layer")
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-        hbm = peaks.get("hbm_gbs")
-        peak_source = "measured: MEASURED_PEAKS.json hbm_gbs (copy, burst)"
+        hbm, bf16 = peaks.get("hbm_gbs"), peaks.get("bf16_tflops")
+        hbm_source = "measured: MEASURED_PEAKS.json hbm_gbs (copy, burst)"
+        bf16_source = "measured: MEASURED_PEAKS.json bf16_tflops (cuBLAS, burst)"
         if hbm is None:
-            hbm, peak_source = 6650.0, "fallback: 6.65 TB/s"
-        achieved = probe["bytes"] / probe["seconds"] / 1e9
+            hbm, hbm_source = 6650.0, "fallback: 6.65 TB/s"
+        if bf16 is None:
+            bf16, bf16_source = 1590.0, "fallback: 1.59 PFLOP/s"
+        # 3xTF32: the tf32 rate is half the bf16 one, three MMAs per product
+        tc_peak = bf16 / 2 / 3
         result = {
             "metric": "synthetic-page pages/s (det 1984x1536 + rec 44 lines) per B200 job",
             "value": value,
@@ -431,10 +448,19 @@ def run_ours(args, d: Dist) -> dict | None:
                        "parallelism": f"replicas x{d.world} (pages sharded by rank, no collective)"},
             "e2e": {"value": e2e, "unit": "pages/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches * args.steps,
-            "roofline": {"bound": "hbm", "kernel": probe["kernel"], "achieved": achieved,
-                         "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_source": peak_source,
-                         "traffic": TRAFFIC_PER_LAUNCH, "traffic_source": TRAFFIC_SOURCE,
-                         "algorithmic_bytes": probe["bytes"], "seconds_per_launch": probe["seconds"]},
+            "roofline": {"bound": "tensor", "kernel": probe["kernel"],
+                         "achieved": probe["flops"] / probe["seconds"] / 1e12, "peak": tc_peak, "unit": "TFLOP/s",
+                         "frac": probe["flops"] / probe["seconds"] / 1e12 / tc_peak,
+                         "peak_source": bf16_source + " / 2 (tf32) / 3 (3xTF32 products): FP32-equivalent",
+                         "traffic": CONV_TRAFFIC_PER_LAUNCH, "traffic_source": CONV_TRAFFIC_SOURCE,
+                         "algorithmic_flops": probe["flops"], "algorithmic_bytes": probe["bytes"],
+                         "hbm_frac": probe["bytes"] / probe["seconds"] / 1e9 / hbm,
+                         "seconds_per_launch": probe["seconds"]},
+            "roofline_pointwise": {"bound": "hbm", "kernel": pw["kernel"],
+                                   "achieved": pw["bytes"] / pw["seconds"] / 1e9, "peak": hbm, "unit": "GB/s",
+                                   "frac": pw["bytes"] / pw["seconds"] / 1e9 / hbm, "peak_source": hbm_source,
+                                   "traffic": TRAFFIC_PER_LAUNCH, "traffic_source": TRAFFIC_SOURCE,
+                                   "algorithmic_bytes": pw["bytes"], "seconds_per_launch": pw["seconds"]},
             "clocks": clocks.summary(),
         }
     return result
@@ -472,7 +498,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["page", "det", "rec", "layer"], default="page",
+    ap.add_argument("--workload", choices=["page", "det", "rec", "layer", "conv3x3"], default="page",
                     help="page (the benchmark step); det or rec alone, for profiling")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up and timed steps (no e2e, probe, peak or CPU legs): for ncu launch lists")

@@ -79,10 +79,11 @@ constexpr unsigned long long WAIT_LIMIT_NS = 200ull * 1000 * 1000;
 // many nanoseconds pass, instead of spinning on it.
 constexpr uint32_t SUSPEND_HINT_NS = 100000;
 
-// Warp roles of both kernels: producer 0, MMA 1, converters 2-5, epilogue
-// 6-13.
+// Warp roles of both kernels: producer 0, MMA 1, converters 2-9, epilogue
+// 10-17.
+constexpr int CONV_THREADS = 256;
 struct Roles {
-    static constexpr int W_MMA = 1, W_CONV = 2, W_EPI = 6;
+    static constexpr int W_MMA = 1, W_CONV = 2, W_EPI = W_CONV + CONV_THREADS / 32;
     static constexpr int THREADS = (W_EPI + EPI_WARPS) * 32;
 };
 
@@ -156,11 +157,15 @@ __device__ __forceinline__ unsigned long long global_ns() {
 
 // Waits for the phase of `bar` with this parity to complete. Gives up when
 // another role raised the abort flag, or after the time limit (then raises
-// it and records the error).
+// it and records the error). BACKOFF: a wait expected to be long (a tile's
+// accumulator) sleeps between polls, leaving the issue slots to the roles on
+// the critical path.
+template <bool BACKOFF = false>
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int *abort_flag, int *err) {
     if (try_wait(bar, parity)) return true;
     const unsigned long long t0 = global_ns();
     for (;;) {
+        if (BACKOFF) __nanosleep(200);
         if (try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
         if (global_ns() - t0 > WAIT_LIMIT_NS) {
@@ -194,6 +199,13 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
         : "memory");
 }
+
+// A named barrier among `count` threads (a multiple of 32): the threads
+// that wait there issue nothing.
+__device__ __forceinline__ void named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+constexpr int BAR_CONV = 1, BAR_EPI = 2;
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float v[16]) {
     uint32_t r[16];
@@ -260,6 +272,10 @@ struct Ctx {
     uint32_t b_bytes;      // one K block of one half of the weight slice: BN x 128 bytes
     uint64_t *full, *conv, *empty, *accf, *acce;
     volatile int *abort_flag;
+    // the converters' and the epilogue's polling thread's verdicts, two
+    // slots each (alternate rounds), read by the others after the named
+    // barrier: 1 go on, 0 stop
+    volatile int *go_conv, *go_epi;
     int ns, nkb, BN, n0, Q;
     long first, tiles;
     uint32_t tmem;
@@ -270,7 +286,9 @@ struct Ctx {
 template <bool RESIDENT>
 __device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
     const uint32_t idesc = tf32_idesc(x.BN);
-    long it = 0, job = 0;
+    long job = 0;
+    int s = 0;        // ring stage
+    uint32_t ph = 0;  // parity of this stage's current round
     uint32_t last_bar = 0, last_parity = 0;
     bool ok = !RESIDENT || wait_phase(smem_u32(bfull), 0, x.abort_flag, a.err);
     for (long t = x.first; t < x.tiles && ok; t += x.Q, job++) {
@@ -279,10 +297,8 @@ __device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
         if (use > 0 && !wait_phase(smem_u32(&x.acce[buf]), uint32_t(use - 1) & 1u, x.abort_flag, a.err)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t d = x.tmem + uint32_t(buf * x.BN);
-        for (int kb = 0; kb < x.nkb; kb++, it++) {
-            const int s = int(it % x.ns);
-            const long round = it / x.ns;
-            if (!wait_phase(smem_u32(&x.conv[s]), uint32_t(round) & 1u, x.abort_flag, a.err)) {
+        for (int kb = 0; kb < x.nkb; kb++) {
+            if (!wait_phase(smem_u32(&x.conv[s]), ph, x.abort_flag, a.err)) {
                 ok = false;
                 break;
             }
@@ -310,7 +326,11 @@ __device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
             }
             commit(smem_u32(&x.empty[s]));
             last_bar = smem_u32(&x.empty[s]);
-            last_parity = uint32_t(round) & 1u;
+            last_parity = ph;
+            if (++s == x.ns) {
+                s = 0;
+                ph ^= 1u;
+            }
         }
         if (!ok) break;
         commit(smem_u32(&x.accf[buf]));
@@ -322,58 +342,69 @@ __device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
     if (last_bar) drain(last_bar, last_parity);
 }
 
-// The converters (128 threads, ct = 0..127): split each landed A block in
-// place into its high half and a low-half twin (the same swizzled layout, so
-// element for element), after the SE gate when there is one. Thread ct
-// always holds the 16-byte chunk ct & 7 of rows (ct >> 3) + 16 j, whose
-// logical chunk is the same for all j.
+// The converters (CONV_THREADS threads, ct = 0..255): split each landed A
+// block in place into its high half and a low-half twin (the same swizzled
+// layout, so element for element), after the SE gate when there is one.
+// Thread ct always holds the 16-byte chunk ct & 7 of rows (ct >> 3) + 32 j,
+// whose logical chunk is the same for all j. For a windowed layer each row's
+// taps that fall inside the image are found once per tile (a bit per tap)
+// and the others zeroed.
+constexpr int CONV_ROWS = TM * 8 / CONV_THREADS;  // rows per converter thread
+
 __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
     const int lc = (ct & 7) ^ ((ct >> 3) & 7);  // logical 16-byte chunk (4 k) of every row this thread holds
     const int cblocks = a.C / TK;                // windowed: K blocks per tap
-    long it = 0;
+    const int taps = a.kh * a.kw;
+    int s = 0;         // ring stage
+    uint32_t ph = 0;   // parity of this stage's current round
+    int gi = 0;        // verdict slot
     bool ok = true;
     for (long t = x.first; t < x.tiles && ok; t += x.Q) {
-        int gl[8];          // the lane of each row, for the gate
-        int oy[8], ox[8];   // windowed: each row's output position (oy far negative past the lane's end)
-        int ih = 0, iw = 0;
+        int gl[CONV_ROWS];         // the lane of each row, for the gate
+        uint32_t inside[CONV_ROWS];  // windowed: bit k set when tap k of the row reads the image
         if (a.gate)
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const long m = t * TM + (ct >> 3) + 16 * j;
+            for (int j = 0; j < CONV_ROWS; j++) {
+                const long m = t * TM + (ct >> 3) + 32 * j;
                 gl[j] = m < a.M ? find_lane(a.lanes, a.nl, m) : -1;
             }
         if (a.windowed) {
             const TileInfo ti = tile_info(a, t);
             const LaneInfo &L = a.lanes[ti.n];
-            const int ow = __ldg(&L.ow);
-            ih = __ldg(&L.ih);
-            iw = __ldg(&L.iw);
+            const int ow = __ldg(&L.ow), ih = __ldg(&L.ih), iw = __ldg(&L.iw);
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const int r = (ct >> 3) + 16 * j;
-                const int q = int(ti.q0) + r;
-                oy[j] = r < ti.rows ? q / ow : -(1 << 20);
-                ox[j] = r < ti.rows ? q - (q / ow) * ow : 0;
+            for (int j = 0; j < CONV_ROWS; j++) {
+                const int r = (ct >> 3) + 32 * j;
+                uint32_t bits = 0;
+                if (r < ti.rows) {
+                    const int q = int(ti.q0) + r;
+                    const int oy = q / ow, ox = q - oy * ow;
+                    for (int k = 0; k < taps && k < 32; k++) {
+                        const int ky = k / a.kw, kx = k - ky * a.kw;
+                        if ((unsigned)(oy + ky - a.pt) < (unsigned)ih && (unsigned)(ox + kx - a.pl) < (unsigned)iw)
+                            bits |= 1u << k;
+                    }
+                }
+                inside[j] = bits;
             }
         }
-        for (int kb = 0; kb < x.nkb; kb++, it++) {
-            const int s = int(it % x.ns);
-            const long round = it / x.ns;
-            if (!wait_phase(smem_u32(&x.full[s]), uint32_t(round) & 1u, x.abort_flag, a.err)) {
+        int tap = 0, cb = 0;  // windowed: the K block's tap and channel block
+        for (int kb = 0; kb < x.nkb; kb++) {
+            // one thread polls the stage, the others wait in the named
+            // barrier (ordered after its acquire of the landed bytes)
+            if (ct == 0) x.go_conv[gi] = wait_phase(smem_u32(&x.full[s]), ph, x.abort_flag, a.err);
+            named_sync(BAR_CONV, CONV_THREADS);
+            if (!x.go_conv[gi]) {
                 ok = false;
                 break;
             }
+            gi ^= 1;
             const uint32_t hi = x.ring + uint32_t(s) * x.stage_bytes, lo = hi + A_BYTES;
             const int k = kb * TK + lc * 4;
-            int dy = 0, dx = 0;
-            if (a.windowed) {
-                const int tap = kb / cblocks, ky = tap / a.kw;
-                dy = ky - a.pt;
-                dx = tap - ky * a.kw - a.pl;
-            }
+            const uint32_t tapbit = a.windowed ? 1u << tap : 0u;
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const uint32_t off = uint32_t(ct + 128 * j) * 16;
+            for (int j = 0; j < CONV_ROWS; j++) {
+                const uint32_t off = uint32_t(ct + CONV_THREADS * j) * 16;
                 float4 v = lds4(hi + off);
                 if (a.gate) {
                     float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -381,8 +412,7 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
                         g = __ldg(reinterpret_cast<const float4 *>(a.gate + (long)gl[j] * a.K + k));
                     v = make_float4(fmul(v.x, g.x), fmul(v.y, g.y), fmul(v.z, g.z), fmul(v.w, g.w));
                 }
-                if (a.windowed && !((unsigned)(oy[j] + dy) < (unsigned)ih && (unsigned)(ox[j] + dx) < (unsigned)iw))
-                    v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (a.windowed && !(inside[j] & tapbit)) v = make_float4(0.f, 0.f, 0.f, 0.f);
                 const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
                 sts4(hi + off, h);
                 sts4(lo + off, make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w));
@@ -390,16 +420,18 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
             // make the generic-proxy stores visible to the tensor core
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             arrive(smem_u32(&x.conv[s]));
+            if (++s == x.ns) {
+                s = 0;
+                ph ^= 1u;
+            }
+            if (++cb == cblocks) {
+                cb = 0;
+                tap++;
+            }
         }
     }
 }
 
-// The epilogue warps (e = 0..7 among them). The sums already differ from the
-// FP32 ones by a few units, so the activations take the quick quotient.
-// Each thread holds one TMEM lane
-// (one pixel) of 16 columns; it stages them as four 16-byte chunks of its row
-// (chunk q at q ^ ((row >> 1) & 3), so that eight lanes cover all 32 banks),
-// and the warp then writes 8 rows x 64 bytes per store.
 // Epilogue modes: the plain store, the CTC argmax partials, a transposed
 // conv's scattered store.
 enum EpiMode : int { EPI_PLAIN = 0, EPI_CTC = 1, EPI_CONVT = 2 };
@@ -415,9 +447,12 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
     long job = 0;
     for (long t = x.first; t < x.tiles; t += x.Q, job++) {
         const int buf = int(job & 1);
-        const bool ok = wait_phase(smem_u32(&x.accf[buf]), uint32_t(job >> 1) & 1u, x.abort_flag, a.err);
-        __syncwarp();
-        if (!__all_sync(0xffffffffu, ok)) break;
+        // one thread polls the accumulator (sleeping between polls), the
+        // other epilogue threads wait in the named barrier
+        if (e == 0 && lane == 0)
+            x.go_epi[job & 1] = wait_phase<true>(smem_u32(&x.accf[buf]), uint32_t(job >> 1) & 1u, x.abort_flag, a.err);
+        named_sync(BAR_EPI, EPI_WARPS * 32);
+        if (!x.go_epi[job & 1]) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const TileInfo ti = tile_info(a, t);
         const long mrow = ti.m0 + qd * 32;
@@ -542,7 +577,7 @@ __device__ __forceinline__ void setup(const TcArgs &a, Ctx &x, int full_count, u
     if (tid == 0) {
         for (int s = 0; s < x.ns; s++) {
             bar_init(smem_u32(&x.full[s]), full_count);
-            bar_init(smem_u32(&x.conv[s]), 128);
+            bar_init(smem_u32(&x.conv[s]), CONV_THREADS);
             bar_init(smem_u32(&x.empty[s]), 1);
         }
         for (int b = 0; b < 2; b++) {
@@ -584,9 +619,11 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
     unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     __shared__ __align__(8) uint64_t full[MAX_NS], conv[MAX_NS], empty[MAX_NS], accf[2], acce[2], bfull;
     __shared__ uint32_t tmem_base_s;
-    __shared__ int abort_s;
+    __shared__ int abort_s, go_conv_s[2], go_epi_s[2];
 
     Ctx x;
+    x.go_conv = go_conv_s;
+    x.go_epi = go_epi_s;
     x.ns = a.ns; x.nkb = a.nkb; x.BN = a.bn;
     x.Q = gridDim.x / a.slices;
     x.first = blockIdx.x / a.slices;
@@ -613,23 +650,28 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
                 tma_load_3d(x.b_base + uint32_t(x.nkb + kb) * x.b_bytes, &tmw, kb * TK, x.n0, 1, bb);
             }
             long it = 0;  // K blocks issued
+            int s = 0;
+            uint32_t ph = 0;
             bool ok = true;
             for (long t = x.first; t < x.tiles && ok; t += x.Q)
                 for (int kb = 0; kb < x.nkb; kb++, it++) {
-                    const int s = int(it % x.ns);
-                    const long round = it / x.ns;
-                    if (round > 0 && !wait_phase(smem_u32(&empty[s]), uint32_t(round - 1) & 1u, x.abort_flag, a.err)) {
+                    // the stage's previous round was read by the MMAs
+                    if (it >= x.ns && !wait_phase(smem_u32(&empty[s]), ph ^ 1u, x.abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
                     arrive_expect(smem_u32(&full[s]), A_BYTES);
                     tma_load_2d(x.ring + uint32_t(s) * SLOT_BYTES, &tmx, kb * TK, int(t * TM), smem_u32(&full[s]));
+                    if (++s == x.ns) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
                 }
             if (*x.abort_flag) {
                 // the copies still in flight land before the CTA leaves
                 drain(bb, 0);
-                for (int s = 0; s < x.ns && s < it; s++)
-                    drain(smem_u32(&full[s]), uint32_t((it - 1 - s) / x.ns) & 1u);
+                for (int q = 0; q < x.ns && q < it; q++)
+                    drain(smem_u32(&full[q]), uint32_t((it - 1 - q) / x.ns) & 1u);
             }
         }
     } else if (warp == R::W_MMA) {
@@ -650,9 +692,11 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
     unsigned char *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     __shared__ __align__(8) uint64_t full[MAX_NS], conv[MAX_NS], empty[MAX_NS], accf[2], acce[2], bfull;
     __shared__ uint32_t tmem_base_s;
-    __shared__ int abort_s;
+    __shared__ int abort_s, go_conv_s[2], go_epi_s[2];
 
     Ctx x;
+    x.go_conv = go_conv_s;
+    x.go_epi = go_epi_s;
     x.ns = a.ns; x.nkb = a.nkb; x.BN = a.bn;
     x.Q = gridDim.x / a.slices;
     x.first = blockIdx.x / a.slices;
@@ -673,6 +717,8 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
         if (lane == 0) {
             const int cblocks = a.windowed ? a.C / TK : x.nkb;  // K blocks per tap
             long it = 0;
+            int s = 0;
+            uint32_t ph = 0;
             bool ok = true;
             for (long t = x.first; t < x.tiles && ok; t += x.Q) {
                 const TileInfo ti = tile_info(a, t);
@@ -683,15 +729,13 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
                     base = __ldg(&L.ipix0) + ti.q0;
                     iw = __ldg(&L.iw);
                 }
+                int cb = 0, ky = 0, kx = 0;  // the K block's channel block and tap
                 for (int kb = 0; kb < x.nkb; kb++, it++) {
-                    const int s = int(it % x.ns);
-                    const long round = it / x.ns;
-                    if (round > 0 && !wait_phase(smem_u32(&empty[s]), uint32_t(round - 1) & 1u, x.abort_flag, a.err)) {
+                    if (it >= x.ns && !wait_phase(smem_u32(&empty[s]), ph ^ 1u, x.abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
-                    const int tap = kb / cblocks, ky = tap / a.kw, kx = tap - ky * a.kw;
-                    const int c0 = (kb - tap * cblocks) * TK;
+                    const int c0 = cb * TK;
                     // rows before the first pixel or past the last read as
                     // zeros; rows of another lane are zeroed by the converters
                     const long y = base + long(ky - a.pt) * iw + (kx - a.pl);
@@ -701,12 +745,23 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
                     tma_load_2d(stage, &tmx, c0, int(y), bar);
                     tma_load_3d(stage + SLOT_BYTES, &tmw, kb * TK, x.n0, 0, bar);
                     tma_load_3d(stage + SLOT_BYTES + x.b_bytes, &tmw, kb * TK, x.n0, 1, bar);
+                    if (++s == x.ns) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                    if (++cb == cblocks) {
+                        cb = 0;
+                        if (++kx == a.kw) {
+                            kx = 0;
+                            ky++;
+                        }
+                    }
                 }
             }
             if (*x.abort_flag)
                 // the copies still in flight land before the CTA leaves
-                for (int s = 0; s < x.ns && s < it; s++)
-                    drain(smem_u32(&full[s]), uint32_t((it - 1 - s) / x.ns) & 1u);
+                for (int q = 0; q < x.ns && q < it; q++)
+                    drain(smem_u32(&full[q]), uint32_t((it - 1 - q) / x.ns) & 1u);
         }
     } else if (warp == R::W_MMA) {
         if (lane == 0) role_mma<false>(a, x, &bfull);
@@ -896,7 +951,7 @@ bool tc_prepare(TcArgs &a) {
     if (a.windowed) {
         // a tap's K blocks never straddle taps; the output keeps the input's
         // size, so the packed input has M pixels too
-        if (a.gate || a.C % TK || a.tiles < 1 || a.K != a.kh * a.kw * a.C) return false;
+        if (a.gate || a.C % TK || a.tiles < 1 || a.K != a.kh * a.kw * a.C || a.kh * a.kw > 32) return false;
     } else {
         // 1x1: the packed input is [M][K]; its weights stay resident unless
         // streaming them takes fewer slices

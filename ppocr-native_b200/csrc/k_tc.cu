@@ -75,9 +75,6 @@ constexpr int DYN_CEILING = 226 * 1024;
 // How long one wait on an mbarrier may take before the kernel gives up: a
 // K block's copy or MMAs take microseconds.
 constexpr unsigned long long WAIT_LIMIT_NS = 200ull * 1000 * 1000;
-// A waiting thread sleeps in the mbarrier until the phase completes or this
-// many nanoseconds pass, instead of spinning on it.
-constexpr uint32_t SUSPEND_HINT_NS = 100000;
 
 // Warp roles of both kernels: producer 0, MMA 1, converters 2-9, epilogue
 // 10-17.
@@ -141,10 +138,10 @@ __device__ __forceinline__ bool try_wait(uint32_t bar, uint32_t parity) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.b32 %0, 1, 0, p;\n\t}\n"
         : "=r"(done)
-        : "r"(bar), "r"(parity), "r"(SUSPEND_HINT_NS)
+        : "r"(bar), "r"(parity)
         : "memory");
     return done != 0;
 }

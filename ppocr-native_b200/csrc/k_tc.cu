@@ -64,11 +64,20 @@ namespace {
 constexpr int TM = 128;                   // pixels per tile (MMA M, one TMEM lane each)
 constexpr int TK = 32;                    // k per block: one 128-byte swizzle row of f32
 constexpr int A_BYTES = TM * 128;         // one half of an A block
-constexpr int SLOT_BYTES = 2 * A_BYTES;   // high half (the copy lands here) + low half
+constexpr int SLOT_BYTES = A_BYTES;       // the staged A block (its split halves go to TMEM)
 constexpr int EPI_WARPS = 8;
 constexpr int STAGE_FLOATS = 32 * 16;     // one epilogue warp's 32 x 16 transpose tile (swizzled)
 constexpr int EPI_BYTES = EPI_WARPS * STAGE_FLOATS * 4 + 256 * 4;  // + the bias slice
-constexpr int MAX_NS = 6;
+constexpr int MAX_NS = 8;
+// Tensor memory: all 512 columns; the two accumulators (BN columns each)
+// first, then one 64-column stage per ring slot for the split A block (high
+// half in its first 32 columns, low half in the next 32), one lane per pixel.
+constexpr int TMEM_COLS = 512;
+// With nacc = 3 each accumulator is three (hi*hi, hi*lo, lo*hi: independent
+// MMA chains, summed by the epilogue), for slices narrow enough that the MMAs
+// alone would not cover the tensor core's latency.
+__host__ __device__ constexpr int a_col0(int bn, int nacc = 1) { return (2 * nacc * bn + 63) / 64 * 64; }
+__host__ __device__ constexpr int tmem_stages(int bn, int nacc = 1) { return (TMEM_COLS - a_col0(bn, nacc)) / 64; }
 // Dynamic shared memory per CTA: the block's limit (227 KB) less room for the
 // kernels' static shared memory.
 constexpr int DYN_CEILING = 226 * 1024;
@@ -115,6 +124,17 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n"
         :
         : "r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// The same with A in tensor memory (lanes = rows, one tf32 per column).
+__device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n"
+        :
+        : "r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
 }
 
 __device__ __forceinline__ void commit(uint32_t bar) {
@@ -227,6 +247,16 @@ __device__ __forceinline__ void sts4(uint32_t addr, float4 v) {
                  : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float v[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+        : "memory");
+}
+
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
 // Where tile t's 128 rows land: output pixels m0..m0+rows-1 of lane n,
@@ -293,33 +323,41 @@ __device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
         const long use = job >> 1;
         if (use > 0 && !wait_phase(smem_u32(&x.acce[buf]), uint32_t(use - 1) & 1u, x.abort_flag, a.err)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t d = x.tmem + uint32_t(buf * x.BN);
+        const int nacc = a.nacc;
+        const uint32_t d = x.tmem + uint32_t(buf * nacc * x.BN);
+        const uint32_t d1 = nacc == 3 ? d + uint32_t(x.BN) : d, d2 = nacc == 3 ? d + uint32_t(2 * x.BN) : d;
         for (int kb = 0; kb < x.nkb; kb++) {
             if (!wait_phase(smem_u32(&x.conv[s]), ph, x.abort_flag, a.err)) {
                 ok = false;
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t ah = x.ring + uint32_t(s) * x.stage_bytes, al = ah + A_BYTES;
+            // A: the converters' split halves in this slot's TMEM stage
+            const uint32_t ah = x.tmem + uint32_t(a_col0(x.BN, nacc) + s * 64), al = ah + 32;
             uint32_t bh, bl;
             if (RESIDENT) {
                 bh = x.b_base + uint32_t(kb) * x.b_bytes;
                 bl = x.b_base + uint32_t(x.nkb + kb) * x.b_bytes;
             } else {
-                bh = ah + SLOT_BYTES;
+                bh = x.ring + uint32_t(s) * x.stage_bytes + SLOT_BYTES;
                 bl = bh + x.b_bytes;
             }
-            // K steps of 8 tf32 (32 bytes along the swizzled rows); steps
-            // wholly past K hold zeros and are skipped
+            // K steps of 8 tf32: 8 TMEM columns of A, 32 bytes along B's
+            // swizzled rows (+2 in the descriptor's address field, which stays
+            // below 2^14 for any shared address); steps wholly past K hold
+            // zeros and are skipped
             const int left = a.K - kb * TK;
             const int steps = left >= TK ? TK / 8 : (left + 7) / 8;
-            for (int kk = 0; kk < steps; kk++) {
-                const uint32_t acc = (kb == 0 && kk == 0) ? 0u : 1u;
-                const uint64_t dah = sw128_desc(ah + kk * 32), dal = sw128_desc(al + kk * 32);
-                const uint64_t dbh = sw128_desc(bh + kk * 32), dbl = sw128_desc(bl + kk * 32);
-                mma_tf32(d, dah, dbh, idesc, acc);
-                mma_tf32(d, dah, dbl, idesc, 1u);
-                mma_tf32(d, dal, dbh, idesc, 1u);
+            const uint64_t dbh = sw128_desc(bh), dbl = sw128_desc(bl);
+#pragma unroll
+            for (int kk = 0; kk < TK / 8; kk++) {
+                if (kk >= steps) break;
+                const uint64_t step = uint64_t(2 * kk);
+                const uint32_t col = uint32_t(8 * kk);
+                const uint32_t first = (kb | kk) ? 1u : 0u;
+                mma_tf32_ta(d, ah + col, dbh + step, idesc, first);
+                mma_tf32_ta(d1, ah + col, dbl + step, idesc, nacc == 3 ? first : 1u);
+                mma_tf32_ta(d2, al + col, dbh + step, idesc, nacc == 3 ? first : 1u);
             }
             commit(smem_u32(&x.empty[s]));
             last_bar = smem_u32(&x.empty[s]);
@@ -339,50 +377,43 @@ __device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
     if (last_bar) drain(last_bar, last_parity);
 }
 
-// The converters (CONV_THREADS threads, ct = 0..255): split each landed A
-// block in place into its high half and a low-half twin (the same swizzled
-// layout, so element for element), after the SE gate when there is one.
-// Thread ct always holds the 16-byte chunk ct & 7 of rows (ct >> 3) + 32 j,
-// whose logical chunk is the same for all j. For a windowed layer each row's
-// taps that fall inside the image are found once per tile (a bit per tap)
-// and the others zeroed.
-constexpr int CONV_ROWS = TM * 8 / CONV_THREADS;  // rows per converter thread
-
-__device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
-    const int lc = (ct & 7) ^ ((ct >> 3) & 7);  // logical 16-byte chunk (4 k) of every row this thread holds
-    const int cblocks = a.C / TK;                // windowed: K blocks per tap
+// The converters (8 warps, ct = 0..255): split each landed A block into its
+// high tf32 half and the remainder, after the SE gate when there is one, and
+// store both into the slot's TMEM stage. Warp w owns TMEM lane quadrant w % 4
+// (32 pixels, one per thread) and K columns 16 h .. 16 h + 15 of the block,
+// h = (w - first converter warp) / 4: the thread reads those 16 values of its
+// pixel's 128-byte swizzled row. For a windowed layer each row's taps that
+// fall inside the image are found once per tile (a bit per tap) and the
+// others zeroed.
+__device__ void role_convert(const TcArgs &a, const Ctx &x, int ct, int warp, int lane) {
+    const int qd = warp & 3, h = ct / 128;
+    const int r = qd * 32 + lane;  // this thread's row (pixel) of every tile
+    const int cblocks = a.C / TK;  // windowed: K blocks per tap
     const int taps = a.kh * a.kw;
+    const uint32_t tlane = uint32_t(qd * 32) << 16;
     int s = 0;         // ring stage
     uint32_t ph = 0;   // parity of this stage's current round
     int gi = 0;        // verdict slot
     bool ok = true;
     for (long t = x.first; t < x.tiles && ok; t += x.Q) {
-        int gl[CONV_ROWS];         // the lane of each row, for the gate
-        uint32_t inside[CONV_ROWS];  // windowed: bit k set when tap k of the row reads the image
-        if (a.gate)
-#pragma unroll
-            for (int j = 0; j < CONV_ROWS; j++) {
-                const long m = t * TM + (ct >> 3) + 32 * j;
-                gl[j] = m < a.M ? find_lane(a.lanes, a.nl, m) : -1;
-            }
+        int gl = -1;           // the row's lane, for the gate
+        uint32_t inside = 0;   // windowed: bit k set when tap k of the row reads the image
+        if (a.gate) {
+            const long m = t * TM + r;
+            gl = m < a.M ? find_lane(a.lanes, a.nl, m) : -1;
+        }
         if (a.windowed) {
             const TileInfo ti = tile_info(a, t);
             const LaneInfo &L = a.lanes[ti.n];
             const int ow = __ldg(&L.ow), ih = __ldg(&L.ih), iw = __ldg(&L.iw);
-#pragma unroll
-            for (int j = 0; j < CONV_ROWS; j++) {
-                const int r = (ct >> 3) + 32 * j;
-                uint32_t bits = 0;
-                if (r < ti.rows) {
-                    const int q = int(ti.q0) + r;
-                    const int oy = q / ow, ox = q - oy * ow;
-                    for (int k = 0; k < taps && k < 32; k++) {
-                        const int ky = k / a.kw, kx = k - ky * a.kw;
-                        if ((unsigned)(oy + ky - a.pt) < (unsigned)ih && (unsigned)(ox + kx - a.pl) < (unsigned)iw)
-                            bits |= 1u << k;
-                    }
+            if (r < ti.rows) {
+                const int q = int(ti.q0) + r;
+                const int oy = q / ow, ox = q - oy * ow;
+                for (int k = 0; k < taps && k < 32; k++) {
+                    const int ky = k / a.kw, kx = k - ky * a.kw;
+                    if ((unsigned)(oy + ky - a.pt) < (unsigned)ih && (unsigned)(ox + kx - a.pl) < (unsigned)iw)
+                        inside |= 1u << k;
                 }
-                inside[j] = bits;
             }
         }
         int tap = 0, cb = 0;  // windowed: the K block's tap and channel block
@@ -396,26 +427,32 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
                 break;
             }
             gi ^= 1;
-            const uint32_t hi = x.ring + uint32_t(s) * x.stage_bytes, lo = hi + A_BYTES;
-            const int k = kb * TK + lc * 4;
-            const uint32_t tapbit = a.windowed ? 1u << tap : 0u;
+            const uint32_t row = x.ring + uint32_t(s) * x.stage_bytes + uint32_t(r) * 128;
+            const bool zero = a.windowed && !(inside & (1u << tap));
+            float hv[16], lv[16];
 #pragma unroll
-            for (int j = 0; j < CONV_ROWS; j++) {
-                const uint32_t off = uint32_t(ct + CONV_THREADS * j) * 16;
-                float4 v = lds4(hi + off);
+            for (int q = 0; q < 4; q++) {
+                const int lc = 4 * h + q;  // logical 16-byte chunk: k = kb*32 + 4 lc .. + 3
+                float4 v = lds4(row + uint32_t(((lc ^ (r & 7)) << 4)));
                 if (a.gate) {
+                    const int k = kb * TK + 4 * lc;
                     float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (gl[j] >= 0 && k < a.K)
-                        g = __ldg(reinterpret_cast<const float4 *>(a.gate + (long)gl[j] * a.K + k));
+                    if (gl >= 0 && k < a.K) g = __ldg(reinterpret_cast<const float4 *>(a.gate + (long)gl * a.K + k));
                     v = make_float4(fmul(v.x, g.x), fmul(v.y, g.y), fmul(v.z, g.z), fmul(v.w, g.w));
                 }
-                if (a.windowed && !(inside[j] & tapbit)) v = make_float4(0.f, 0.f, 0.f, 0.f);
-                const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-                sts4(hi + off, h);
-                sts4(lo + off, make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w));
+                if (zero) v = make_float4(0.f, 0.f, 0.f, 0.f);
+                const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    hv[4 * q + u] = tf32_hi(e[u]);
+                    lv[4 * q + u] = e[u] - hv[4 * q + u];
+                }
             }
-            // make the generic-proxy stores visible to the tensor core
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            const uint32_t col = uint32_t(a_col0(x.BN, a.nacc) + s * 64 + 16 * h);
+            tmem_st16(x.tmem + tlane + col, hv);
+            tmem_st16(x.tmem + tlane + col + 32, lv);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             arrive(smem_u32(&x.conv[s]));
             if (++s == x.ns) {
                 s = 0;
@@ -426,6 +463,20 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct) {
                 tap++;
             }
         }
+    }
+}
+
+// Sixteen accumulator columns of this warp's lane quadrant: the sum of the
+// three product chains when there are three (the small corrections first).
+__device__ __forceinline__ void load_acc16(const TcArgs &a, const Ctx &x, int qd, int buf, int c0, float v[16]) {
+    const uint32_t base = x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * a.nacc * x.BN + c0);
+    tmem_ld16(base, v);
+    if (a.nacc == 3) {
+        float v1[16], v2[16];
+        tmem_ld16(base + uint32_t(x.BN), v1);
+        tmem_ld16(base + uint32_t(2 * x.BN), v2);
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[j] = fadd(v[j], fadd(v1[j], v2[j]));
     }
 }
 
@@ -474,7 +525,7 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
             int best = 0x7fffffff;
             for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
                 float v[16];
-                tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);
+                load_acc16(a, x, qd, buf, c0, v);
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
                     const int col = x.n0 + c0 + j;
@@ -501,7 +552,7 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
         }
         for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
             float v[16];
-            tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);
+            load_acc16(a, x, qd, buf, c0, v);
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 const float *bb = bias_s + c0 + 4 * c;
@@ -674,7 +725,7 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
     } else if (warp == R::W_MMA) {
         if (lane == 0) role_mma<true>(a, x, &bfull);
     } else if (warp < R::W_EPI) {
-        role_convert(a, x, tid - R::W_CONV * 32);
+        role_convert(a, x, tid - R::W_CONV * 32, warp, lane);
     } else {
         role_epilogue<ACT, MODE>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
     }
@@ -763,7 +814,7 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
     } else if (warp == R::W_MMA) {
         if (lane == 0) role_mma<false>(a, x, &bfull);
     } else if (warp < R::W_EPI) {
-        role_convert(a, x, tid - R::W_CONV * 32);
+        role_convert(a, x, tid - R::W_CONV * 32, warp, lane);
     } else {
         role_epilogue<ACT, MODE>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
     }
@@ -871,6 +922,12 @@ size_t pw_smem(int kpad, int bn, int ns) { return 1024 + size_t(ns) * SLOT_BYTES
 
 size_t conv_smem(int bn, int ns) { return 1024 + size_t(ns) * (SLOT_BYTES + size_t(256) * bn) + EPI_BYTES; }
 
+// Ring stages: as many as shared memory and the TMEM A stages allow.
+int max_stages(int bn, int nacc) { return tmem_stages(bn, nacc) < MAX_NS ? tmem_stages(bn, nacc) : MAX_NS; }
+
+// Three accumulator chains where they still leave four TMEM A stages.
+int chains(int bn) { return tmem_stages(bn, 3) >= 4 ? 3 : 1; }
+
 // The weight slice width for a pointwise K x N: the fewest slices of at
 // most 256 channels (a multiple of 32) whose weights, both halves, fit in
 // shared memory beside a three-stage ring (else a two-stage one). 0 when
@@ -880,7 +937,7 @@ int pw_slice_width(int K, int N) {
     for (int stages = 3; stages >= 2; stages--)
         for (int S = 1; S <= (N + 31) / 32; S++) {
             const int bn = ((N + S - 1) / S + 31) / 32 * 32;
-            if (bn <= 256 && pw_smem(kpad, bn, stages) <= size_t(DYN_CEILING)) return bn;
+            if (bn <= 128 && pw_smem(kpad, bn, stages) <= size_t(DYN_CEILING)) return bn;
         }
     return 0;
 }
@@ -919,8 +976,7 @@ bool set_grid(TcArgs &a) {
     const long tiles = a.windowed ? a.tiles : (a.M + TM - 1) / TM;
     const long q = std::max(1L, std::min(long(sms / a.slices), tiles));
     a.grid = int(q) * a.slices;
-    a.tmem_cols = 32;
-    while (a.tmem_cols < 2 * a.bn) a.tmem_cols *= 2;
+    a.tmem_cols = TMEM_COLS;
     return true;
 }
 
@@ -964,18 +1020,21 @@ bool tc_prepare(TcArgs &a) {
         a.bn = pw_slice_width(a.K, a.N);
         a.slices = (a.N + a.bn - 1) / a.bn;
         a.ns = 2;
-        while (a.ns < MAX_NS && pw_smem(a.kpad, a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
+        a.nacc = chains(a.bn);
+        while (a.ns < max_stages(a.bn, a.nacc) && pw_smem(a.kpad, a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
         a.smem = int(pw_smem(a.kpad, a.bn, a.ns));
     } else {
         a.bn = conv_slice_width(a.N);
         if (!a.bn) return false;
+        // the chains follow the layer's own slice width, never the run's size
+        a.nacc = chains(a.bn);
         // few tiles: narrower slices, so that more SMs share the layer (each
         // output's sum is the same whatever the slice)
         const long tiles = a.windowed ? a.tiles : (a.M + TM - 1) / TM;
         while (a.bn > 32 && tiles * ((a.N + a.bn - 1) / a.bn) < 74) a.bn -= 32;
         a.slices = (a.N + a.bn - 1) / a.bn;
         a.ns = 2;
-        while (a.ns < MAX_NS && conv_smem(a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
+        while (a.ns < max_stages(a.bn, a.nacc) && conv_smem(a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
         a.smem = int(conv_smem(a.bn, a.ns));
     }
     // pixels: [M][C], boxes of 32 channels x 128 pixels; channels past C and

@@ -388,11 +388,16 @@ __global__ void __launch_bounds__(128) stem_kernel(const ConvArgs a) {
             for (int j = 0; j < NB; j++) acc[j] = ffma(ws[k * NB + j], in[k], acc[j]);
         }
         float *y = a.y + m * NB;
+        if (a.quick) {
+#pragma unroll
+            for (int j = 0; j < NB; j++) acc[j] = activate<true>(a.act, acc[j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < NB; j++) acc[j] = activate(a.act, acc[j]);
+        }
 #pragma unroll
         for (int j = 0; j < NB; j += 4)
-            *reinterpret_cast<float4 *>(y + j) =
-                make_float4(activate(a.act, acc[j]), activate(a.act, acc[j + 1]), activate(a.act, acc[j + 2]),
-                            activate(a.act, acc[j + 3]));
+            *reinterpret_cast<float4 *>(y + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
     }
 }
 

@@ -61,8 +61,13 @@ __device__ __forceinline__ void dw_pixel(const DwArgs &a, const DwPixel &px, int
             }
         }
     }
+    if (a.quick) {
 #pragma unroll
-    for (int e = 0; e < VEC; e++) v[e] = activate(a.act, v[e]);
+        for (int e = 0; e < VEC; e++) v[e] = activate<true>(a.act, v[e]);
+    } else {
+#pragma unroll
+        for (int e = 0; e < VEC; e++) v[e] = activate(a.act, v[e]);
+    }
 }
 
 template <int VEC>

@@ -76,6 +76,7 @@ struct ConvArgs {
     const float *gate = nullptr;  // [lanes][C]: input channel c of lane n is x * gate[n][c]
     const float *res = nullptr;   // [M][oc]: y = act2(act(conv) + res)
     int act2 = 0;
+    bool quick = false;           // stems: the activation's quick quotient (tensor-core mode)
 };
 
 struct DwArgs {
@@ -89,6 +90,7 @@ struct DwArgs {
     int c = 0;
     int kh = 3, kw = 3, sh = 1, sw = 1, pt = 0, pl = 0;
     int act = 0;
+    bool quick = false;        // the activation's quick quotient (tensor-core mode)
 };
 
 // Depthwise convolution whose output feeds a pointwise one straight from

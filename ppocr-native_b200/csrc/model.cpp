@@ -722,6 +722,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             }
             DwArgs d = a.dw;
             d.y = buf(dw.y);
+            d.quick = tc_allowed;
             ConvArgs c;
             c.src[0] = {buf(dw.y), int(dw.oc), 0};
             c.nsrc = 1;
@@ -785,6 +786,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             a.lanes = L; a.nl = nl; a.M = total_out(g, i); a.oc = int(op.oc);
             a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
             a.pt = int(op.pt); a.pl = int(op.pl); a.act = op.fused; a.bias_mode = bias_mode(op);
+            a.quick = tc_allowed;
             a.y = buf(op.y);
             push_conv(i, a, Lh, nullptr);
             break;
@@ -795,6 +797,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             a.lanes = L; a.nl = nl; a.M = total_out(g, i); a.c = int(op.ic);
             a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
             a.pt = int(op.pt); a.pl = int(op.pl); a.act = op.fused;
+            a.quick = tc_allowed;
             g.launches.push_back([a](cudaStream_t s) { return launch_dw(a, s); });
             break;
         }

@@ -355,36 +355,47 @@ def run_ours(args, d: Dist) -> dict | None:
         return run_layer(args, d, cuda, torch, device)
     page = workload.Page(seed=1000 + d.rank)
     pipe = PagePipeline(cuda, synth, page, device, args.workload)
-    stream = torch.cuda.ExternalStream(pipe.stream)
+    # Pages in flight: one pipeline each (own models, streams and buffers,
+    # shared weights); launch lists (--profile) take one.
+    k = 1 if args.profile else max(1, args.inflight)
+    pipes = [pipe] + [PagePipeline(cuda, synth, page, device, args.workload, like=pipe) for _ in range(k - 1)]
+    streams = [torch.cuda.ExternalStream(p.stream) for p in pipes]
+    main = torch.cuda.Stream(device=device)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
 
     # Inputs into HBM once through the public path (copies included).
-    pipe.fill_host()
-    pipe.run_host()
-    for _ in range(args.warmup):
-        pipe.enqueue_device()
+    for p in pipes:
+        p.fill_host()
+        p.run_host()
+        for _ in range(args.warmup):
+            p.enqueue_device()
     torch.cuda.synchronize()
 
-    # value: device-resident inputs, K steps, L2 flushed before each.
+    # value: device-resident inputs; a step is k pages enqueued at once, each
+    # on its own stream, L2 flushed before each step outside its events.
     events = []
     d.barrier()
     torch.cuda.synchronize()
     with Clocks(device) as clocks:
         for _ in range(args.steps):
-            with torch.cuda.stream(stream):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(main):
                 flush.zero_()
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-            pipe.enqueue_device()
-            with torch.cuda.stream(stream):
-                e1.record(stream)
+                e0.record(main)
+            for p, st in zip(pipes, streams):
+                st.wait_event(e0)
+                p.enqueue_device()
+                done = torch.cuda.Event()
+                done.record(st)
+                main.wait_event(done)
+            e1.record(main)
             events.append((e0, e1))
         torch.cuda.synchronize()
     d.barrier()
     local_s = sum(a.elapsed_time(b) for a, b in events) / 1e3
     total_s = d.max(local_s)
-    value = d.world * args.steps / total_s
+    value = d.world * args.steps * k / total_s
     if args.profile:
         launches = pipe.launches()
         pipe.close()
@@ -396,35 +407,30 @@ def run_ours(args, d: Dist) -> dict | None:
     # e2e: the public call sequence with host buffers. The page sits in the
     # models' page-locked lane inputs (where a caller's preprocessing writes
     # it); every step copies its inputs in, runs, copies its outputs out and
-    # the host reads the result. Two pipelines (own models, streams and
-    # buffers, shared weights) alternate, so one page's copies overlap the
-    # other's kernels, as enqueue/wait allow any caller.
-    pipe2 = PagePipeline(cuda, synth, page, device, args.workload, like=pipe)
-    pipes = [pipe, pipe2]
-    for p in pipes:
-        p.fill_host()
-        p.run_host()
+    # the host reads the result. The k pipelines take the pages in turn, so
+    # one page's copies and latency-bound kernels overlap the others', as
+    # enqueue/wait allow any caller.
     d.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for step in range(args.steps):
-        p = pipes[step % 2]
-        if step >= 2:
+        p = pipes[step % k]
+        if step >= k:
             outs = p.wait_host()
             _ = float(outs[0][0])
         p.enqueue_host()
-    for step in range(max(0, args.steps - 2), args.steps):
-        outs = pipes[step % 2].wait_host()
+    for step in range(max(0, args.steps - k), args.steps):
+        outs = pipes[step % k].wait_host()
         _ = float(outs[0][0])
     torch.cuda.synchronize()
     e2e_local = time.perf_counter() - t0
-    pipe2.close()
     e2e_s = d.max(e2e_local)
     e2e = d.world * args.steps / e2e_s
     h2d, d2h = pipe.io_bytes()
     launches = pipe.launches()
 
     # det alone (ms), for the metric's "det fwd ms"
+    stream = streams[0]
     det_times = []
     for _ in range(5):
         with torch.cuda.stream(stream):
@@ -437,7 +443,8 @@ def run_ours(args, d: Dist) -> dict | None:
             e1.record(stream)
         e1.synchronize()
         det_times.append(e0.elapsed_time(e1))
-    pipe.close()
+    for p in reversed(pipes):
+        p.close()
     d.barrier()
 
     result = None
@@ -470,12 +477,14 @@ def run_ours(args, d: Dist) -> dict | None:
                     "random-init weights N(0,0.02) of the synthetic PP-OCRv6-shaped det/rec plans",
             "config": {"workload": "page: det 1984x1536 + rec 44 lines (48 x 320..1600, runs of 16)",
                        "det_fwd_ms": statistics.median(det_times),
+                       "pages_per_step": k,
                        "l2": "flushed (256 MB write) before every timed step, outside the step's events",
                        "parallelism": f"replicas x{d.world} (pages sharded by rank, no collective)"},
             "e2e": {"value": e2e, "unit": "pages/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "method": "C ABI enqueue/wait, inputs in the models' page-locked buffers, per step: H2D, "
-                              "kernels, D2H, host read; two pages in flight on two streams"},
-            "gpu_launches": launches * args.steps,
+                              f"kernels, D2H, host read; one page per step, {k} pages in flight on their own "
+                              "streams"},
+            "gpu_launches": launches * args.steps * k,
             "roofline": {"bound": "tensor", "kernel": probe["kernel"],
                          "achieved": probe["flops"] / probe["seconds"] / 1e12, "peak": tc_peak, "unit": "TFLOP/s",
                          "frac": probe["flops"] / probe["seconds"] / 1e12 / tc_peak,
@@ -525,6 +534,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--inflight", type=int, default=4,
+                    help="pages in flight (own models and streams, shared weights): a step's pages")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["page", "det", "rec", "layer", "conv3x3"], default="page",
                     help="page (the benchmark step); det or rec alone, for profiling")

@@ -120,8 +120,7 @@ def test_depthwise(cuda_mod, oracle_mod, k, s, c, fused):
     p = k // 2
     op = window(Op("dwconv", x=0, y=1, ic=c, oc=c, fused=fused, w=(0, wt.size), b=(wt.size, c)), (k, k), s, p, p)
     plan = single(op, (h, w, c), np.concatenate([wt, b]))
-    got, _ = gpu_run(cuda_mod, plan, x)
-    check(got[0], oracle_run(oracle_mod, plan, x)[0])
+    check_both(cuda_mod, oracle_mod, plan, x)
 
 
 def elementwise_plan(kind, h, w, c, **kw):

@@ -343,6 +343,16 @@ __global__ void __launch_bounds__(VEC_COLS *VEC_ROWS) conv_vector_kernel(const C
     a.y[m * a.oc + n] = acc;
 }
 
+// A stem pixel's NB outputs, activated and stored four at a time.
+template <int NB, bool QUICK>
+__device__ __forceinline__ void stem_store(int act, const float acc[NB], float *y) {
+#pragma unroll
+    for (int j = 0; j < NB; j += 4)
+        *reinterpret_cast<float4 *>(y + j) =
+            make_float4(activate<QUICK>(act, acc[j]), activate<QUICK>(act, acc[j + 1]),
+                        activate<QUICK>(act, acc[j + 2]), activate<QUICK>(act, acc[j + 3]));
+}
+
 // An RGB stem (three input channels, bias first, kh * kw <= 9): one thread
 // per output pixel holds its kh*kw*3 input values and all NB outputs; the
 // weights sit in shared memory, read by every thread at once (broadcast).
@@ -351,7 +361,7 @@ __global__ void __launch_bounds__(VEC_COLS *VEC_ROWS) conv_vector_kernel(const C
 // conv_gemm's accumulators do, so the two give the same bits.
 template <int NB>
 __global__ void __launch_bounds__(128) stem_kernel(const ConvArgs a) {
-    __shared__ float ws[27 * NB];
+    __shared__ __align__(16) float ws[27 * NB];
     __shared__ float bs[NB];
     const int K = a.kh * a.kw * 3;
     for (int e = threadIdx.x; e < K * NB; e += blockDim.x) ws[e] = __ldg(a.w + e);
@@ -385,19 +395,19 @@ __global__ void __launch_bounds__(128) stem_kernel(const ConvArgs a) {
         for (int k = 0; k < 27; k++) {
             if (k >= K) break;
 #pragma unroll
-            for (int j = 0; j < NB; j++) acc[j] = ffma(ws[k * NB + j], in[k], acc[j]);
+            for (int j = 0; j < NB; j += 4) {
+                const float4 w4 = *reinterpret_cast<const float4 *>(ws + k * NB + j);  // broadcast
+                acc[j] = ffma(w4.x, in[k], acc[j]);
+                acc[j + 1] = ffma(w4.y, in[k], acc[j + 1]);
+                acc[j + 2] = ffma(w4.z, in[k], acc[j + 2]);
+                acc[j + 3] = ffma(w4.w, in[k], acc[j + 3]);
+            }
         }
         float *y = a.y + m * NB;
-        if (a.quick) {
-#pragma unroll
-            for (int j = 0; j < NB; j++) acc[j] = activate<true>(a.act, acc[j]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < NB; j++) acc[j] = activate(a.act, acc[j]);
-        }
-#pragma unroll
-        for (int j = 0; j < NB; j += 4)
-            *reinterpret_cast<float4 *>(y + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        if (a.quick)
+            stem_store<NB, true>(a.act, acc, y);
+        else
+            stem_store<NB, false>(a.act, acc, y);
     }
 }
 

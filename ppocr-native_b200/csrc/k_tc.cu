@@ -73,11 +73,8 @@ constexpr int MAX_NS = 8;
 // first, then one 64-column stage per ring slot for the split A block (high
 // half in its first 32 columns, low half in the next 32), one lane per pixel.
 constexpr int TMEM_COLS = 512;
-// With nacc = 3 each accumulator is three (hi*hi, hi*lo, lo*hi: independent
-// MMA chains, summed by the epilogue), for slices narrow enough that the MMAs
-// alone would not cover the tensor core's latency.
-__host__ __device__ constexpr int a_col0(int bn, int nacc = 1) { return (2 * nacc * bn + 63) / 64 * 64; }
-__host__ __device__ constexpr int tmem_stages(int bn, int nacc = 1) { return (TMEM_COLS - a_col0(bn, nacc)) / 64; }
+__host__ __device__ constexpr int a_col0(int bn) { return (2 * bn + 63) / 64 * 64; }
+__host__ __device__ constexpr int tmem_stages(int bn) { return (TMEM_COLS - a_col0(bn)) / 64; }
 // Dynamic shared memory per CTA: the block's limit (227 KB) less room for the
 // kernels' static shared memory.
 constexpr int DYN_CEILING = 226 * 1024;
@@ -323,9 +320,7 @@ __device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
         const long use = job >> 1;
         if (use > 0 && !wait_phase(smem_u32(&x.acce[buf]), uint32_t(use - 1) & 1u, x.abort_flag, a.err)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int nacc = a.nacc;
-        const uint32_t d = x.tmem + uint32_t(buf * nacc * x.BN);
-        const uint32_t d1 = nacc == 3 ? d + uint32_t(x.BN) : d, d2 = nacc == 3 ? d + uint32_t(2 * x.BN) : d;
+        const uint32_t d = x.tmem + uint32_t(buf * x.BN);
         for (int kb = 0; kb < x.nkb; kb++) {
             if (!wait_phase(smem_u32(&x.conv[s]), ph, x.abort_flag, a.err)) {
                 ok = false;
@@ -333,7 +328,7 @@ __device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             // A: the converters' split halves in this slot's TMEM stage
-            const uint32_t ah = x.tmem + uint32_t(a_col0(x.BN, nacc) + s * 64), al = ah + 32;
+            const uint32_t ah = x.tmem + uint32_t(a_col0(x.BN) + s * 64), al = ah + 32;
             uint32_t bh, bl;
             if (RESIDENT) {
                 bh = x.b_base + uint32_t(kb) * x.b_bytes;
@@ -354,10 +349,9 @@ __device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
                 if (kk >= steps) break;
                 const uint64_t step = uint64_t(2 * kk);
                 const uint32_t col = uint32_t(8 * kk);
-                const uint32_t first = (kb | kk) ? 1u : 0u;
-                mma_tf32_ta(d, ah + col, dbh + step, idesc, first);
-                mma_tf32_ta(d1, ah + col, dbl + step, idesc, nacc == 3 ? first : 1u);
-                mma_tf32_ta(d2, al + col, dbh + step, idesc, nacc == 3 ? first : 1u);
+                mma_tf32_ta(d, ah + col, dbh + step, idesc, (kb | kk) ? 1u : 0u);
+                mma_tf32_ta(d, ah + col, dbl + step, idesc, 1u);
+                mma_tf32_ta(d, al + col, dbh + step, idesc, 1u);
             }
             commit(smem_u32(&x.empty[s]));
             last_bar = smem_u32(&x.empty[s]);
@@ -448,7 +442,7 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct, int warp, in
                     lv[4 * q + u] = e[u] - hv[4 * q + u];
                 }
             }
-            const uint32_t col = uint32_t(a_col0(x.BN, a.nacc) + s * 64 + 16 * h);
+            const uint32_t col = uint32_t(a_col0(x.BN) + s * 64 + 16 * h);
             tmem_st16(x.tmem + tlane + col, hv);
             tmem_st16(x.tmem + tlane + col + 32, lv);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -463,20 +457,6 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct, int warp, in
                 tap++;
             }
         }
-    }
-}
-
-// Sixteen accumulator columns of this warp's lane quadrant: the sum of the
-// three product chains when there are three (the small corrections first).
-__device__ __forceinline__ void load_acc16(const TcArgs &a, const Ctx &x, int qd, int buf, int c0, float v[16]) {
-    const uint32_t base = x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * a.nacc * x.BN + c0);
-    tmem_ld16(base, v);
-    if (a.nacc == 3) {
-        float v1[16], v2[16];
-        tmem_ld16(base + uint32_t(x.BN), v1);
-        tmem_ld16(base + uint32_t(2 * x.BN), v2);
-#pragma unroll
-        for (int j = 0; j < 16; j++) v[j] = fadd(v[j], fadd(v1[j], v2[j]));
     }
 }
 
@@ -525,7 +505,7 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
             int best = 0x7fffffff;
             for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
                 float v[16];
-                load_acc16(a, x, qd, buf, c0, v);
+                tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
                     const int col = x.n0 + c0 + j;
@@ -552,7 +532,7 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
         }
         for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
             float v[16];
-            load_acc16(a, x, qd, buf, c0, v);
+            tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 const float *bb = bias_s + c0 + 4 * c;
@@ -923,10 +903,7 @@ size_t pw_smem(int kpad, int bn, int ns) { return 1024 + size_t(ns) * SLOT_BYTES
 size_t conv_smem(int bn, int ns) { return 1024 + size_t(ns) * (SLOT_BYTES + size_t(256) * bn) + EPI_BYTES; }
 
 // Ring stages: as many as shared memory and the TMEM A stages allow.
-int max_stages(int bn, int nacc) { return tmem_stages(bn, nacc) < MAX_NS ? tmem_stages(bn, nacc) : MAX_NS; }
-
-// Three accumulator chains where they still leave four TMEM A stages.
-int chains(int bn) { return tmem_stages(bn, 3) >= 4 ? 3 : 1; }
+int max_stages(int bn) { return tmem_stages(bn) < MAX_NS ? tmem_stages(bn) : MAX_NS; }
 
 // The weight slice width for a pointwise K x N: the fewest slices of at
 // most 256 channels (a multiple of 32) whose weights, both halves, fit in
@@ -1020,21 +997,18 @@ bool tc_prepare(TcArgs &a) {
         a.bn = pw_slice_width(a.K, a.N);
         a.slices = (a.N + a.bn - 1) / a.bn;
         a.ns = 2;
-        a.nacc = chains(a.bn);
-        while (a.ns < max_stages(a.bn, a.nacc) && pw_smem(a.kpad, a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
+        while (a.ns < max_stages(a.bn) && pw_smem(a.kpad, a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
         a.smem = int(pw_smem(a.kpad, a.bn, a.ns));
     } else {
         a.bn = conv_slice_width(a.N);
         if (!a.bn) return false;
-        // the chains follow the layer's own slice width, never the run's size
-        a.nacc = chains(a.bn);
         // few tiles: narrower slices, so that more SMs share the layer (each
         // output's sum is the same whatever the slice)
         const long tiles = a.windowed ? a.tiles : (a.M + TM - 1) / TM;
         while (a.bn > 32 && tiles * ((a.N + a.bn - 1) / a.bn) < 74) a.bn -= 32;
         a.slices = (a.N + a.bn - 1) / a.bn;
         a.ns = 2;
-        while (a.ns < max_stages(a.bn, a.nacc) && conv_smem(a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
+        while (a.ns < max_stages(a.bn) && conv_smem(a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
         a.smem = int(conv_smem(a.bn, a.ns));
     }
     // pixels: [M][C], boxes of 32 channels x 128 pixels; channels past C and

@@ -234,7 +234,6 @@ struct TcArgs {
     // ring stages, TMEM columns, grid, dynamic shared memory, and the tensor
     // maps (CUtensorMap, 128 bytes each) of the input and of the weights
     int bn = 0, slices = 0, nkb = 0, ns = 0, tmem_cols = 0, grid = 0, smem = 0;
-    int nacc = 1;                 // accumulator chains per tile (1, or 3 for narrow slices)
     unsigned long long tmx[16] = {}, tmw[16] = {};
 };
 int launch_tc(const TcArgs &a, cudaStream_t s);

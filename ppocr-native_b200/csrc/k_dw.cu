@@ -87,6 +87,97 @@ __global__ void __launch_bounds__(256) dw_kernel(const DwArgs a) {
     }
 }
 
+// Depthwise outputs of DW_RUN consecutive pixels of one output row for four
+// channels per thread: the input columns under the run are loaded once per
+// kernel row (a window of (DW_RUN - 1) * S + K float4s) and shared by the
+// run's outputs, and the thread's channels stay fixed across the grid-stride
+// loop, so its weights and bias are loaded once (kept in registers for
+// K = 3). Each output keeps the reference order: bias, then the taps inside
+// the image in kernel row-major order. A block holds `per_block` runs of all
+// c / 4 channel groups, the groups of one run on consecutive threads so that
+// a warp's loads cover whole pixels.
+template <int K, int S, bool QUICK>
+__global__ void __launch_bounds__(256) dw_row_kernel(const DwArgs a, int per_block) {
+    constexpr int WC = (DW_RUN - 1) * S + K;  // window columns
+    constexpr bool HOLD = K == 3;              // weights in registers
+    const int cg = a.c >> 2;
+    const int slot = threadIdx.x / cg;
+    if (slot >= per_block) return;
+    const int c = (threadIdx.x - slot * cg) * 4;
+    const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float4 bias = a.b ? __ldg(reinterpret_cast<const float4 *>(a.b + c)) : zero;
+    float4 wr[HOLD ? K * K : 1];
+    if (HOLD) {
+#pragma unroll
+        for (int t = 0; t < K * K; t++) wr[t] = __ldg(reinterpret_cast<const float4 *>(a.w + t * a.c + c));
+    }
+    for (long run = (long)blockIdx.x * per_block + slot; run < a.runs; run += (long)gridDim.x * per_block) {
+        const LaneInfo &L = a.lanes[find_run_lane(a.lanes, a.nl, run)];
+        const int ow = __ldg(&L.ow), ih = __ldg(&L.ih), iw = __ldg(&L.iw);
+        const int rpr = (ow + DW_RUN - 1) / DW_RUN;
+        const int r = int(run - __ldg(&L.run0));
+        const int oy = r / rpr;
+        const int ox0 = (r - oy * rpr) * DW_RUN;
+        const int ix0 = ox0 * S - a.pl;
+        unsigned cols = 0;  // window columns inside the image
+#pragma unroll
+        for (int i = 0; i < WC; i++)
+            if (ix0 + i >= 0 && ix0 + i < iw) cols |= 1u << i;
+        const float *xn = a.x + __ldg(&L.ipix0) * a.c + c;
+        float4 v[DW_RUN];
+#pragma unroll
+        for (int j = 0; j < DW_RUN; j++) v[j] = bias;
+#pragma unroll
+        for (int ky = 0; ky < K; ky++) {
+            const int iy = oy * S - a.pt + ky;
+            if (iy < 0 || iy >= ih) continue;
+            const float *row = xn + ((long)iy * iw + ix0) * a.c;
+            float4 win[WC];
+#pragma unroll
+            for (int i = 0; i < WC; i++)
+                win[i] = (cols >> i & 1u) ? __ldg(reinterpret_cast<const float4 *>(row + (long)i * a.c)) : zero;
+#pragma unroll
+            for (int kx = 0; kx < K; kx++) {
+                const float4 g = HOLD ? wr[HOLD ? ky * K + kx : 0]
+                                      : __ldg(reinterpret_cast<const float4 *>(a.w + (ky * K + kx) * a.c + c));
+#pragma unroll
+                for (int j = 0; j < DW_RUN; j++) {
+                    if (!(cols >> (j * S + kx) & 1u)) continue;
+                    const float4 q = win[j * S + kx];
+                    v[j].x = ffma(g.x, q.x, v[j].x);
+                    v[j].y = ffma(g.y, q.y, v[j].y);
+                    v[j].z = ffma(g.z, q.z, v[j].z);
+                    v[j].w = ffma(g.w, q.w, v[j].w);
+                }
+            }
+        }
+        float *dst = a.y + (__ldg(&L.pix0) + (long)oy * ow + ox0) * a.c + c;
+#pragma unroll
+        for (int j = 0; j < DW_RUN; j++) {
+            if (ox0 + j >= ow) break;
+            float4 o;
+            o.x = activate<QUICK>(a.act, v[j].x);
+            o.y = activate<QUICK>(a.act, v[j].y);
+            o.z = activate<QUICK>(a.act, v[j].z);
+            o.w = activate<QUICK>(a.act, v[j].w);
+            *reinterpret_cast<float4 *>(dst + (long)j * a.c) = o;
+        }
+    }
+}
+
+template <int K, int S>
+void run_dw_rows(const DwArgs &a, cudaStream_t s) {
+    const int cg = a.c / 4;
+    const int per_block = 256 / cg;
+    long blocks = (a.runs + per_block - 1) / per_block;
+    if (blocks > 148L * 16) blocks = 148L * 16;
+    if (blocks < 1) blocks = 1;
+    if (a.quick)
+        dw_row_kernel<K, S, true><<<(unsigned)blocks, cg * per_block, 0, s>>>(a, per_block);
+    else
+        dw_row_kernel<K, S, false><<<(unsigned)blocks, cg * per_block, 0, s>>>(a, per_block);
+}
+
 constexpr int BK = 8;
 constexpr int DPAD = 4;
 
@@ -231,6 +322,15 @@ int run_dw_pw(const DwPwArgs &a, cudaStream_t s) {
 }  // namespace
 
 int launch_dw(const DwArgs &a, cudaStream_t s) {
+    // square 3x3 and 5x5 kernels of stride 1 or 2 over whole float4s: row runs
+    if (a.c % 4 == 0 && a.c <= 1024 && a.runs > 0 && a.kh == a.kw && a.sh == a.sw && (a.kh == 3 || a.kh == 5) &&
+        (a.sh == 1 || a.sh == 2)) {
+        if (a.kh == 3)
+            a.sh == 1 ? run_dw_rows<3, 1>(a, s) : run_dw_rows<3, 2>(a, s);
+        else
+            a.sh == 1 ? run_dw_rows<5, 1>(a, s) : run_dw_rows<5, 2>(a, s);
+        return 1;
+    }
     long work = a.M * (a.c % 4 == 0 ? a.c / 4 : a.c);
     long blocks = (work + 255) / 256;
     if (blocks > 148L * 64) blocks = 148L * 64;

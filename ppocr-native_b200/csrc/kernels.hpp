@@ -39,6 +39,7 @@ struct LaneInfo {
     long ipix0;               // first input pixel
     long spix0[MAX_SOURCES];  // first pixel in each conv source / the second input
     long tile0;               // first 128-pixel output tile when every lane is tiled on its own
+    long run0;                // first DW_RUN-pixel run along an output row (depthwise threads)
     int ih, iw, oh, ow;
 };
 
@@ -51,6 +52,19 @@ __device__ __forceinline__ int find_lane(const LaneInfo *L, int nl, long m, bool
         int mid = (lo + hi + 1) >> 1;
         long start = input ? __ldg(&L[mid].ipix0) : __ldg(&L[mid].pix0);
         if (start <= m)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
+}
+
+// The lane holding row run `r` (LaneInfo::run0).
+__device__ __forceinline__ int find_run_lane(const LaneInfo *L, int nl, long r) {
+    int lo = 0, hi = nl - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (__ldg(&L[mid].run0) <= r)
             lo = mid;
         else
             hi = mid - 1;
@@ -79,6 +93,9 @@ struct ConvArgs {
     bool quick = false;           // stems: the activation's quick quotient (tensor-core mode)
 };
 
+// Output pixels along one row that a depthwise thread computes together.
+constexpr int DW_RUN = 4;
+
 struct DwArgs {
     const float *x = nullptr;  // packed input, c channels
     const float *w = nullptr;  // [kh][kw][c]
@@ -91,6 +108,7 @@ struct DwArgs {
     int kh = 3, kw = 3, sh = 1, sw = 1, pt = 0, pl = 0;
     int act = 0;
     bool quick = false;        // the activation's quick quotient (tensor-core mode)
+    long runs = 0;             // DW_RUN-pixel row runs over all lanes (LaneInfo::run0)
 };
 
 // Depthwise convolution whose output feeds a pointwise one straight from

@@ -441,7 +441,7 @@ namespace {
 // shifts of a dense convolution's inputs (pixel prefix sums per source).
 std::vector<LaneInfo> lane_table(const Group &g, size_t i, const std::vector<int> &shifts) {
     std::vector<LaneInfo> t(g.count());
-    long pix = 0, ipix = 0, spix[MAX_SOURCES] = {0, 0, 0, 0}, tile = 0;
+    long pix = 0, ipix = 0, spix[MAX_SOURCES] = {0, 0, 0, 0}, tile = 0, run = 0;
     for (size_t n = 0; n < g.count(); n++) {
         const Op &op = g.lane(n).ops[i];
         LaneInfo &L = t[n];
@@ -449,6 +449,8 @@ std::vector<LaneInfo> lane_table(const Group &g, size_t i, const std::vector<int
         L.ipix0 = ipix;
         L.tile0 = tile;
         tile += (long(op.oh * op.ow) + 127) / 128;
+        L.run0 = run;
+        run += long(op.oh) * ((long(op.ow) + DW_RUN - 1) / DW_RUN);
         for (int s = 0; s < MAX_SOURCES; s++) L.spix0[s] = spix[s];
         L.ih = int(op.ih); L.iw = int(op.iw); L.oh = int(op.oh); L.ow = int(op.ow);
         pix += long(op.oh * op.ow);
@@ -457,6 +459,12 @@ std::vector<LaneInfo> lane_table(const Group &g, size_t i, const std::vector<int
             spix[s] += long(op.ih >> shifts[s]) * long(op.iw >> shifts[s]);
     }
     return t;
+}
+
+// Row runs of DW_RUN output pixels over all lanes of a lane table.
+long row_runs(const LaneInfo *t, int nl) {
+    const LaneInfo &L = t[nl - 1];
+    return L.run0 + long(L.oh) * ((long(L.ow) + DW_RUN - 1) / DW_RUN);
 }
 
 // A stride-1 conv whose output keeps its input's size (padding kh - 1 and
@@ -722,6 +730,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             }
             DwArgs d = a.dw;
             d.y = buf(dw.y);
+            d.runs = row_runs(Lh, nl);
             d.quick = tc_allowed;
             ConvArgs c;
             c.src[0] = {buf(dw.y), int(dw.oc), 0};
@@ -798,6 +807,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             a.kh = int(op.kh); a.kw = int(op.kw); a.sh = int(op.sh); a.sw = int(op.sw);
             a.pt = int(op.pt); a.pl = int(op.pl); a.act = op.fused;
             a.quick = tc_allowed;
+            a.runs = row_runs(Lh, nl);
             g.launches.push_back([a](cudaStream_t s) { return launch_dw(a, s); });
             break;
         }

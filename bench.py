@@ -240,12 +240,17 @@ class PagePipeline:
 # share of a page's launch time) at its most common launch, the detector's
 # 3x3 96 -> 24 RSE convolution at a quarter of a 1984 x 1536 page; and the
 # pointwise kernel (pw_tc_kernel) at its largest launch, the detector's first
-# 1x1 24 -> 24 + swish at half the page.
+# 1x1 24 -> 24 + swish at half the page; and the depthwise kernel
+# (dw_row_kernel) at its largest launch, the detector's first 3x3 depthwise
+# layer over 24 channels + swish at half the page.
 LAYERS = {
     "conv3x3": dict(h=496, w=384, ic=96, oc=24, k=3, fused="none",
                     kernel="conv_tc_kernel: 3x3 96->24 @ 496x384 (3xTF32 tcgen05, the RSE neck's convolution)"),
     "layer": dict(h=992, w=768, ic=24, oc=24, k=1, fused="swish",
                   kernel="pw_tc_kernel: 1x1 24->24 + swish @ 992x768 (3xTF32 tcgen05, the detector's first pointwise)"),
+    "dw3x3": dict(h=992, w=768, ic=24, oc=24, k=3, fused="swish", kind="dwconv",
+                  kernel="dw_row_kernel: depthwise 3x3 24 channels + swish @ 992x768 (FP32 FMA, the detector's first "
+                         "depthwise)"),
 }
 
 
@@ -253,16 +258,17 @@ def layer_plan(name: str) -> bytes:
     from ppocr_native_b200.plan import Op, encode, window
 
     L = LAYERS[name]
+    kind = L.get("kind", "conv")
     rng = np.random.default_rng(0)
-    wt = rng.normal(0, 0.02, L["k"] * L["k"] * L["ic"] * L["oc"]).astype(np.float32)
+    wt = rng.normal(0, 0.02, L["k"] * L["k"] * (1 if kind == "dwconv" else L["ic"]) * L["oc"]).astype(np.float32)
     b = rng.normal(0, 0.02, L["oc"]).astype(np.float32)
-    op = window(Op("conv", x=0, y=1, ic=L["ic"], oc=L["oc"], fused=L["fused"], w=(0, wt.size), b=(wt.size, L["oc"])),
+    op = window(Op(kind, x=0, y=1, ic=L["ic"], oc=L["oc"], fused=L["fused"], w=(0, wt.size), b=(wt.size, L["oc"])),
                 (L["k"], L["k"]), 1, L["k"] // 2, L["k"] // 2)
     return encode((0, L["h"], L["w"], L["ic"]), 2, [1], [op], np.concatenate([wt, b]))
 
 
 def run_layer(args, d, cuda, torch, device):
-    """--workload layer | conv3x3: the probed layer alone, warm-up then timed
+    """--workload layer | conv3x3 | dw3x3: the probed layer alone, warm-up then timed
     steps (the command ncu captures)."""
     L = LAYERS[args.workload]
     m = cuda.Model(layer_plan(args.workload), device=device)
@@ -278,13 +284,14 @@ def run_layer(args, d, cuda, torch, device):
 def probe_kernel(cuda, torch, device: int, name: str, reps: int = 20) -> dict:
     """Time one probed layer alone with CUDA events on the model's stream, L2
     flushed before each launch. Algorithmic bytes: the input and output maps
-    once, the split weights (two tf32 halves, K padded to 32) and the bias;
-    FLOPs: 2 per multiply-add of the convolution (FP32 arithmetic)."""
+    once, the weights (for the tensor cores: two tf32 halves, K padded to 32)
+    and the bias; FLOPs: 2 per multiply-add of the convolution."""
     L = LAYERS[name]
     h, w, ic, oc, k = L["h"], L["w"], L["ic"], L["oc"], L["k"]
+    dw = L.get("kind") == "dwconv"
     rng = np.random.default_rng(0)
     m = cuda.Model(layer_plan(name), device=device)
-    assert m.steps() == ["conv"]
+    assert m.steps() == ["dwconv" if dw else "conv"], m.steps()
     m.input_mut()[:] = rng.standard_normal(h * w * ic).astype(np.float32)
     m.run(60_000)
     stream = torch.cuda.ExternalStream(m.stream)
@@ -304,6 +311,9 @@ def probe_kernel(cuda, torch, device: int, name: str, reps: int = 20) -> dict:
             times.append(e0.elapsed_time(e1) / 1e3)
     m.close()
     t = statistics.median(times)
+    if dw:
+        return {"kernel": L["kernel"], "seconds": t, "flops": 2 * h * w * k * k * ic,
+                "bytes": 4 * (h * w * ic + h * w * oc + k * k * ic + ic)}
     kk = k * k * ic
     kpad = -(-kk // 32) * 32
     return {"kernel": L["kernel"], "seconds": t, "flops": 2 * h * w * kk * oc,
@@ -451,6 +461,7 @@ def run_ours(args, d: Dist) -> dict | None:
     if d.rank == 0:
         probe = probe_kernel(cuda, torch, device, "conv3x3")
         pw = probe_kernel(cuda, torch, device, "layer")
+        dwp = probe_kernel(cuda, torch, device, "dw3x3")
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
         hbm, bf16 = peaks.get("hbm_gbs"), peaks.get("bf16_tflops")
         hbm_source = "measured: MEASURED_PEAKS.json hbm_gbs (copy, burst)"
@@ -498,6 +509,11 @@ def run_ours(args, d: Dist) -> dict | None:
                                    "frac": pw["bytes"] / pw["seconds"] / 1e9 / hbm, "peak_source": hbm_source,
                                    "traffic": TRAFFIC_PER_LAUNCH, "traffic_source": TRAFFIC_SOURCE,
                                    "algorithmic_bytes": pw["bytes"], "seconds_per_launch": pw["seconds"]},
+            "roofline_depthwise": {"bound": "hbm", "kernel": dwp["kernel"],
+                                   "achieved": dwp["bytes"] / dwp["seconds"] / 1e9, "peak": hbm, "unit": "GB/s",
+                                   "frac": dwp["bytes"] / dwp["seconds"] / 1e9 / hbm, "peak_source": hbm_source,
+                                   "traffic": None, "algorithmic_bytes": dwp["bytes"],
+                                   "seconds_per_launch": dwp["seconds"]},
             "clocks": clocks.summary(),
         }
     return result
@@ -537,7 +553,7 @@ def main():
     ap.add_argument("--inflight", type=int, default=4,
                     help="pages in flight (own models and streams, shared weights): a step's pages")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["page", "det", "rec", "layer", "conv3x3"], default="page",
+    ap.add_argument("--workload", choices=["page", "det", "rec", *LAYERS], default="page",
                     help="page (the benchmark step); det or rec alone, for profiling")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up and timed steps (no e2e, probe, peak or CPU legs): for ncu launch lists")

@@ -165,12 +165,28 @@ __global__ void __launch_bounds__(256) dw_row_kernel(const DwArgs a, int per_blo
     }
 }
 
+// Resident 256-thread blocks per SM of each row-run instance (register
+// bound), found once per process by configure_dw_kernels.
+int g_row_resident[2][2][2];  // [K == 5][S == 2][QUICK]
+int g_sms = 148;
+
+template <int K, int S, bool QUICK>
+void note_residency() {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, dw_row_kernel<K, S, QUICK>, 256, 0) != cudaSuccess || n < 1)
+        n = 1;
+    g_row_resident[K == 5][S == 2][QUICK] = n;
+}
+
+// One wave: at most as many blocks as can be resident at once, each looping
+// over its share of the runs (keeping its weights).
 template <int K, int S>
 void run_dw_rows(const DwArgs &a, cudaStream_t s) {
     const int cg = a.c / 4;
     const int per_block = 256 / cg;
     long blocks = (a.runs + per_block - 1) / per_block;
-    if (blocks > 148L * 16) blocks = 148L * 16;
+    const long wave = long(g_sms) * g_row_resident[K == 5][S == 2][a.quick ? 1 : 0];
+    if (blocks > wave) blocks = wave;
     if (blocks < 1) blocks = 1;
     if (a.quick)
         dw_row_kernel<K, S, true><<<(unsigned)blocks, cg * per_block, 0, s>>>(a, per_block);
@@ -350,6 +366,18 @@ void allow_smem() {
 // Raise the dynamic shared-memory ceiling of every fused instance; once per
 // device, with that device current.
 void configure_dw_kernels() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+        sms > 0)
+        g_sms = sms;
+    note_residency<3, 1, false>();
+    note_residency<3, 1, true>();
+    note_residency<3, 2, false>();
+    note_residency<3, 2, true>();
+    note_residency<5, 1, false>();
+    note_residency<5, 1, true>();
+    note_residency<5, 2, false>();
+    note_residency<5, 2, true>();
     allow_smem<8, 6, 16, 16>();
     allow_smem<8, 4, 16, 16>();
     allow_smem<8, 3, 16, 16>();

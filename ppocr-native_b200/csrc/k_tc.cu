@@ -274,17 +274,18 @@ __device__ __forceinline__ TileInfo tile_info(const TcArgs &a, long t) {
     int lo = 0, hi = a.nl - 1;  // the last lane whose first tile is at most t
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (__ldg(&a.lanes[mid].tile0) <= t)
+        if ((a.fold ? __ldg(&a.lanes[mid].ftile0) : __ldg(&a.lanes[mid].tile0)) <= t)
             lo = mid;
         else
             hi = mid - 1;
     }
     const LaneInfo &L = a.lanes[lo];
+    const int per = a.fold ? FOLD_OUT : TM;
     ti.n = lo;
-    ti.q0 = (t - __ldg(&L.tile0)) * TM;
+    ti.q0 = (t - (a.fold ? __ldg(&L.ftile0) : __ldg(&L.tile0))) * per;
     ti.m0 = __ldg(&L.pix0) + ti.q0;
     const long left = long(__ldg(&L.oh)) * __ldg(&L.ow) - ti.q0;
-    ti.rows = int(left < TM ? left : TM);
+    ti.rows = int(left < per ? left : per);
     return ti;
 }
 
@@ -381,9 +382,13 @@ __device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
 // others zeroed.
 __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct, int warp, int lane) {
     const int qd = warp & 3, h = ct / 128;
-    const int r = qd * 32 + lane;  // this thread's row (pixel) of every tile
+    // this thread's row (pixel) of every tile, and the staged row it reads:
+    // with folded taps, quadrant qd holds tile pixels 30 qd - 1 .. 30 qd + 30
+    // (staged from pixel -1 on)
+    const int r = a.fold ? qd * (32 - 2) + lane - 1 : qd * 32 + lane;
+    const int srow = a.fold ? r + 1 : r;
     const int cblocks = a.C / TK;  // windowed: K blocks per tap
-    const int taps = a.kh * a.kw;
+    const int taps = a.fold ? a.kh : a.kh * a.kw;
     const uint32_t tlane = uint32_t(qd * 32) << 16;
     int s = 0;         // ring stage
     uint32_t ph = 0;   // parity of this stage's current round
@@ -400,9 +405,14 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct, int warp, in
             const TileInfo ti = tile_info(a, t);
             const LaneInfo &L = a.lanes[ti.n];
             const int ow = __ldg(&L.ow), ih = __ldg(&L.ih), iw = __ldg(&L.iw);
-            if (r < ti.rows) {
-                const int q = int(ti.q0) + r;
-                const int oy = q / ow, ox = q - oy * ow;
+            const long q = ti.q0 + r;
+            if (a.fold && q >= 0 && q < long(__ldg(&L.oh)) * ow) {
+                // rows whose vertical tap falls inside the image
+                const int oy = int(q / ow);
+                for (int k = 0; k < taps && k < 32; k++)
+                    if ((unsigned)(oy + k - a.pt) < (unsigned)ih) inside |= 1u << k;
+            } else if (!a.fold && r < ti.rows) {
+                const int oy = int(q / ow), ox = int(q - long(oy) * ow);
                 for (int k = 0; k < taps && k < 32; k++) {
                     const int ky = k / a.kw, kx = k - ky * a.kw;
                     if ((unsigned)(oy + ky - a.pt) < (unsigned)ih && (unsigned)(ox + kx - a.pl) < (unsigned)iw)
@@ -421,13 +431,13 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct, int warp, in
                 break;
             }
             gi ^= 1;
-            const uint32_t row = x.ring + uint32_t(s) * x.stage_bytes + uint32_t(r) * 128;
+            const uint32_t row = x.ring + uint32_t(s) * x.stage_bytes + uint32_t(srow) * 128;
             const bool zero = a.windowed && !(inside & (1u << tap));
             float hv[16], lv[16];
 #pragma unroll
             for (int q = 0; q < 4; q++) {
                 const int lc = 4 * h + q;  // logical 16-byte chunk: k = kb*32 + 4 lc .. + 3
-                float4 v = lds4(row + uint32_t(((lc ^ (r & 7)) << 4)));
+                float4 v = lds4(row + uint32_t(((lc ^ (srow & 7)) << 4)));
                 if (a.gate) {
                     const int k = kb * TK + 4 * lc;
                     float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -461,8 +471,8 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct, int warp, in
 }
 
 // Epilogue modes: the plain store, the CTC argmax partials, a transposed
-// conv's scattered store.
-enum EpiMode : int { EPI_PLAIN = 0, EPI_CTC = 1, EPI_CONVT = 2 };
+// conv's scattered store, a folded conv's sum of its three horizontal taps.
+enum EpiMode : int { EPI_PLAIN = 0, EPI_CTC = 1, EPI_CONVT = 2, EPI_FOLD = 3 };
 
 template <int ACT, int MODE>
 __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, int lane, uint32_t staging,
@@ -597,6 +607,94 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
     }
 }
 
+// The epilogue of a conv with folded horizontal taps: lane i of quadrant qd
+// holds tile pixel p = 30 qd + i - 1 and, per output channel, its products
+// with the taps kx = 0, 1, 2 (columns 48 j + 16 kx + e). Output p sums its
+// own kx = 1 column, its left neighbour's kx = 0 and its right neighbour's
+// kx = 2 (adjacent lanes, by shuffles), skipping a neighbour outside the
+// image row, then adds the bias and applies the activation; lanes 1..30 of
+// each quadrant are the tile's outputs. Stores go through the same swizzled
+// transpose as the plain epilogue.
+template <int ACT>
+__device__ void role_epilogue_fold(const TcArgs &a, const Ctx &x, int e, int warp, int lane, uint32_t staging,
+                                   const float *bias_s) {
+    const int qd = warp & 3;
+    const int half = e / 4;
+    const uint32_t stg = staging + uint32_t(e * STAGE_FLOATS * 4);
+    const int q4 = lane & 3;
+    const bool vec = (a.toc & 3) == 0;
+    const int chunks = x.BN / 48;
+    long job = 0;
+    for (long t = x.first; t < x.tiles; t += x.Q, job++) {
+        const int buf = int(job & 1);
+        if (e == 0 && lane == 0)
+            x.go_epi[job & 1] = wait_phase<true>(smem_u32(&x.accf[buf]), uint32_t(job >> 1) & 1u, x.abort_flag, a.err);
+        named_sync(BAR_EPI, EPI_WARPS * 32);
+        if (!x.go_epi[job & 1]) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const TileInfo ti = tile_info(a, t);
+        const int ow = __ldg(&a.lanes[ti.n].ow);
+        const int p = qd * 30 + lane - 1;  // this lane's tile pixel
+        const long q = ti.q0 + p;
+        const int ox = q >= 0 ? int(q % ow) : 0;
+        const bool has_l = ox > 0, has_r = ox < ow - 1;
+        const long mq = ti.m0 + qd * 30 - 1;  // packed pixel of lane 0
+        const int last = ti.rows - qd * 30;  // lanes 1..last are outputs (at most 30)
+        for (int ch = half; ch < chunks; ch += 2) {
+            float z0[16], z1[16], z2[16];
+            const uint32_t col = x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + ch * 48);
+            tmem_ld16(col, z0);
+            tmem_ld16(col + 16, z1);
+            tmem_ld16(col + 32, z2);
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float o[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int j = 4 * c + u;
+                    const float l = __shfl_up_sync(0xffffffffu, z0[j], 1);
+                    const float r = __shfl_down_sync(0xffffffffu, z2[j], 1);
+                    float v = z1[j];
+                    if (has_l) v = fadd(l, v);
+                    if (has_r) v = fadd(v, r);
+                    o[u] = activate_t<ACT, true>(fadd(v, bias_s[ch * 16 + j]));
+                }
+                sts4(stg + uint32_t(lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)), make_float4(o[0], o[1], o[2], o[3]));
+            }
+            __syncwarp();
+            const int n = x.n0 / 3 + ch * 16 + 4 * q4;  // output channel
+#pragma unroll
+            for (int pp = 0; pp < 4; pp++) {
+                const int rr = 8 * pp + (lane >> 2);
+                float4 o = lds4(stg + uint32_t(rr * 64 + ((q4 ^ ((rr >> 1) & 3)) << 4)));
+                if (rr < 1 || rr > 30 || rr > last || n >= a.toc) continue;
+                const long m = mq + rr;
+                float *dst = a.y + m * a.toc + n;
+                if (vec) {
+                    if (a.res) {
+                        const float4 rv = __ldg(reinterpret_cast<const float4 *>(a.res + m * a.toc + n));
+                        o = make_float4(activate(a.act2, fadd(o.x, rv.x)), activate(a.act2, fadd(o.y, rv.y)),
+                                        activate(a.act2, fadd(o.z, rv.z)), activate(a.act2, fadd(o.w, rv.w)));
+                    }
+                    *reinterpret_cast<float4 *>(dst) = o;
+                } else {
+                    const float ov[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        if (n + c >= a.toc) break;
+                        float y = ov[c];
+                        if (a.res) y = activate(a.act2, fadd(y, __ldg(a.res + m * a.toc + n + c)));
+                        dst[c] = y;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        arrive(smem_u32(&x.acce[buf]));
+    }
+}
+
 // Shared set-up of both kernels: barriers, bias slice, TMEM.
 template <class R>
 __device__ __forceinline__ void setup(const TcArgs &a, Ctx &x, int full_count, uint64_t *bfull, float *bias_s,
@@ -616,7 +714,13 @@ __device__ __forceinline__ void setup(const TcArgs &a, Ctx &x, int full_count, u
         *abort_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    for (int j = tid; j < x.BN; j += R::THREADS) bias_s[j] = (a.b && x.n0 + j < a.N) ? a.b[x.n0 + j] : 0.0f;
+    if (a.fold) {
+        // a folded slice's BN / 3 output channels start at channel n0 / 3
+        for (int j = tid; j < x.BN / 3; j += R::THREADS)
+            bias_s[j] = (a.b && x.n0 / 3 + j < a.toc) ? a.b[x.n0 / 3 + j] : 0.0f;
+    } else {
+        for (int j = tid; j < x.BN; j += R::THREADS) bias_s[j] = (a.b && x.n0 + j < a.N) ? a.b[x.n0 + j] : 0.0f;
+    }
     if (warp == R::W_MMA) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_base_s)),
                      "r"(a.tmem_cols));
@@ -779,7 +883,9 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
                     }
                     if (++cb == cblocks) {
                         cb = 0;
-                        if (++kx == a.kw) {
+                        // folded taps: the K blocks walk the vertical taps
+                        // only, each staged from the tile's pixel -1 on
+                        if (a.fold || ++kx == a.kw) {
                             kx = 0;
                             ky++;
                         }
@@ -795,6 +901,8 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
         if (lane == 0) role_mma<false>(a, x, &bfull);
     } else if (warp < R::W_EPI) {
         role_convert(a, x, tid - R::W_CONV * 32, warp, lane);
+    } else if constexpr (MODE == EPI_FOLD) {
+        role_epilogue_fold<ACT>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
     } else {
         role_epilogue<ACT, MODE>(a, x, warp - R::W_EPI, warp, lane, smem_u32(staging), bias_s);
     }
@@ -978,10 +1086,17 @@ bool tc_prepare(TcArgs &a) {
         if (a.windowed || a.res || a.gate || a.vocab || a.N != a.tkh * a.tkw * a.toc || a.toc % 4) return false;
         a.stream_b = true;
     }
+    if (a.fold) {
+        // three horizontal taps (pl = 1) in 48-column groups of 16 outputs
+        if (!a.windowed || a.kw != 3 || a.pl != 1 || a.K != a.kh * a.C || a.N % 48 || a.toc < 1 ||
+            a.toc > a.N / 3)
+            return false;
+    }
     if (a.windowed) {
         // a tap's K blocks never straddle taps; the output keeps the input's
         // size, so the packed input has M pixels too
-        if (a.gate || a.C % TK || a.tiles < 1 || a.K != a.kh * a.kw * a.C || a.kh * a.kw > 32) return false;
+        if (a.gate || a.C % TK || a.tiles < 1 || (!a.fold && a.K != a.kh * a.kw * a.C) || a.kh * a.kw > 32)
+            return false;
     } else {
         // 1x1: the packed input is [M][K]; its weights stay resident unless
         // streaming them takes fewer slices
@@ -999,6 +1114,13 @@ bool tc_prepare(TcArgs &a) {
         a.ns = 2;
         while (a.ns < max_stages(a.bn) && pw_smem(a.kpad, a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
         a.smem = int(pw_smem(a.kpad, a.bn, a.ns));
+    } else if (a.fold) {
+        // two 16-channel groups per slice, one when few tiles
+        a.bn = a.N >= 96 && a.tiles * ((a.N + 95) / 96) >= 74 ? 96 : 48;
+        a.slices = a.N / a.bn + (a.N % a.bn ? 1 : 0);
+        a.ns = 2;
+        while (a.ns < max_stages(a.bn) && conv_smem(a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
+        a.smem = int(conv_smem(a.bn, a.ns));
     } else {
         a.bn = conv_slice_width(a.N);
         if (!a.bn) return false;
@@ -1041,6 +1163,7 @@ void configure_act() {
     cudaFuncSetAttribute(pw_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
     cudaFuncSetAttribute(conv_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
     cudaFuncSetAttribute(conv_tc_kernel<ACT, EPI_CONVT>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
+    cudaFuncSetAttribute(conv_tc_kernel<ACT, EPI_FOLD>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
 }
 
 void configure_tc_kernels() {
@@ -1055,6 +1178,8 @@ void launch_act(const TcArgs &a, const CUtensorMap &mx, const CUtensorMap &mw, c
         conv_tc_kernel<0, EPI_CTC><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
     else if (a.tkh)
         conv_tc_kernel<ACT, EPI_CONVT><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
+    else if (a.fold)
+        conv_tc_kernel<ACT, EPI_FOLD><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
     else if (a.windowed || a.stream_b)
         conv_tc_kernel<ACT><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
     else

@@ -40,6 +40,7 @@ struct LaneInfo {
     long spix0[MAX_SOURCES];  // first pixel in each conv source / the second input
     long tile0;               // first 128-pixel output tile when every lane is tiled on its own
     long run0;                // first DW_RUN-pixel run along an output row (depthwise threads)
+    long ftile0;              // first FOLD_OUT-pixel tile of a tensor-core conv with folded taps
     int ih, iw, oh, ow;
 };
 
@@ -218,8 +219,18 @@ struct ConvTArgs {
 // == 0) tile each lane on its own, so that a tap's 128 input pixels are 128
 // consecutive packed pixels shifted by (ky - pt) * iw + kx - pl; the rows
 // that fall outside the image read as zeros.
+// Output pixels per tile of a tensor-core 3-wide conv with its horizontal
+// taps folded into N: four 32-lane quadrants of 30 outputs, each quadrant's
+// first and last lane holding the neighbours' sums.
+constexpr int FOLD_OUT = 120;
+
 struct TcArgs {
     bool windowed = false;
+    // A windowed conv of kw = 3, pl = 1 with its three horizontal taps folded
+    // into the columns: K = kh * C (k = ky * C + c), N = 48 per 16 output
+    // channels (column 48 j + 16 kx + e is channel 16 j + e of tap kx), toc
+    // the output channels; tiles of FOLD_OUT outputs (LaneInfo::ftile0).
+    bool fold = false;
     bool stream_b = false;        // weights streamed with the A blocks even for a 1x1 layer
     const float *x = nullptr;     // [pixels][C], 16-byte aligned, C % 4 == 0
     long tiles = 0;               // windowed: 128-pixel tiles of all lanes, each lane on its own
@@ -247,6 +258,7 @@ struct TcArgs {
     // A non-overlapping transposed conv (tkh > 0): rows are input pixels
     // (lanes by ipix0), column n = (ky * tkw + kx) * toc + o goes to output
     // pixel (iy * tkh + ky, ix * tkw + kx) of the lane (pix0, ow), channel o.
+    // toc is also a folded conv's output channel count.
     int tkh = 0, tkw = 0, toc = 0;
     // filled by tc_prepare: output-channel slice width and count, K blocks,
     // ring stages, TMEM columns, grid, dynamic shared memory, and the tensor

@@ -105,6 +105,7 @@ struct Weights {
     std::vector<size_t> tc_hi_at, tc_lo_at;
     std::vector<int> tc_kpad;
     std::vector<float> tc_wmax, tc_bmax;  // CTC heads: largest |w|, |b| over the live columns
+    std::vector<char> tc_fold;            // the copy has its horizontal taps folded into N (TcArgs::fold)
     const float *tc_hi(size_t op) const {
         return tc_hi_at[op] == SIZE_MAX ? nullptr : static_cast<const float *>(tc_arena.p) + tc_hi_at[op];
     }
@@ -441,7 +442,7 @@ namespace {
 // shifts of a dense convolution's inputs (pixel prefix sums per source).
 std::vector<LaneInfo> lane_table(const Group &g, size_t i, const std::vector<int> &shifts) {
     std::vector<LaneInfo> t(g.count());
-    long pix = 0, ipix = 0, spix[MAX_SOURCES] = {0, 0, 0, 0}, tile = 0, run = 0;
+    long pix = 0, ipix = 0, spix[MAX_SOURCES] = {0, 0, 0, 0}, tile = 0, run = 0, ftile = 0;
     for (size_t n = 0; n < g.count(); n++) {
         const Op &op = g.lane(n).ops[i];
         LaneInfo &L = t[n];
@@ -451,6 +452,8 @@ std::vector<LaneInfo> lane_table(const Group &g, size_t i, const std::vector<int
         tile += (long(op.oh * op.ow) + 127) / 128;
         L.run0 = run;
         run += long(op.oh) * ((long(op.ow) + DW_RUN - 1) / DW_RUN);
+        L.ftile0 = ftile;
+        ftile += (long(op.oh * op.ow) + FOLD_OUT - 1) / FOLD_OUT;
         for (int s = 0; s < MAX_SOURCES; s++) L.spix0[s] = spix[s];
         L.ih = int(op.ih); L.iw = int(op.iw); L.oh = int(op.oh); L.ow = int(op.ow);
         pix += long(op.oh * op.ow);
@@ -472,6 +475,12 @@ long row_runs(const LaneInfo *t, int nl) {
 // constant number of packed pixels.
 bool tc_windowed(const Op &op) {
     return op.kind == K_CONV && op.sh == 1 && op.sw == 1 && op.pt + op.pb == op.kh - 1 && op.pl + op.pr == op.kw - 1;
+}
+
+// A windowed 3-wide conv whose horizontal taps go into the tensor cores'
+// columns (TcArgs::fold): whole 32-channel K blocks per vertical tap.
+bool tc_foldable(const Op &op) {
+    return tc_windowed(op) && op.kw == 3 && op.pl == 1 && (op.ic + op.n2) % 32 == 0 && op.oc <= 160;
 }
 
 long total_out(const Group &g, size_t i) {
@@ -666,9 +675,18 @@ int ppocr_model::build_group(Group &g, std::string &err) {
         t.C = c.C;
         t.kh = c.kh; t.kw = c.kw; t.pt = c.pt; t.pl = c.pl;
         t.lanes = c.lanes; t.nl = c.nl; t.gate = c.gate;
-        t.tiles = Lh[c.nl - 1].tile0 + (long(Lh[c.nl - 1].oh) * Lh[c.nl - 1].ow + 127) / 128;
+        const LaneInfo &last = Lh[c.nl - 1];
+        t.tiles = last.tile0 + (long(last.oh) * last.ow + 127) / 128;
         t.w_hi = W.tc_hi(i); t.w_lo = W.tc_lo(i); t.b = c.b; t.res = c.res; t.y = c.y;
         t.M = c.M; t.K = c.kh * c.kw * c.C; t.N = c.oc; t.kpad = W.tc_kpad[i];
+        if (W.tc_fold[i]) {
+            if (pw) return 0;
+            t.fold = true;
+            t.tiles = last.ftile0 + (long(last.oh) * last.ow + FOLD_OUT - 1) / FOLD_OUT;
+            t.K = c.kh * c.C;
+            t.N = (c.oc + 15) / 16 * 48;
+            t.toc = c.oc;
+        }
         t.act = c.act; t.act2 = c.act2; t.err = errp;
         if (!tc_prepare(t)) return 0;
         return (!pw && !one) ? 2 : 1;
@@ -1073,8 +1091,14 @@ int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_mode
         float wmax = 0.0f, bmax = 0.0f;
         const bool ctc = op.kind == K_CTCARGMAX && op.w1;
         const bool convt = op.kind == K_CONVTRANSPOSE && op.w1;  // [ic][kh][kw][oc]: K = ic
-        const int K = ctc || convt ? int(op.ic) : int(op.kh * op.kw * (op.ic + op.n2));
-        const int N = ctc ? int((op.n2 + 15) / 16 * 16) : convt ? int(op.kh * op.kw * op.oc) : int(op.oc);
+        const bool fold = op.w1 && tc_foldable(op);
+        const int C = int(op.ic + op.n2);
+        int K = ctc || convt ? int(op.ic) : int(op.kh * op.kw * C);
+        int N = ctc ? int((op.n2 + 15) / 16 * 16) : convt ? int(op.kh * op.kw * op.oc) : int(op.oc);
+        if (fold) {
+            K = int(op.kh) * C;
+            N = int((op.oc + 15) / 16) * 48;
+        }
         if (((op.kind == K_CONV || convt) && op.w1 && tc_weights_wanted(K, N)) || ctc) {
             kpad = pw_tc_kpad(K);
             while (tc.size() % 64) tc.push_back(0.0f);
@@ -1083,7 +1107,13 @@ int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_mode
             tc.resize(lo + size_t(N) * kpad, 0.0f);
             for (int n = 0; n < N; n++)
                 for (int k = 0; k < K; k++) {
-                    const size_t at = ctc ? (size_t(n / 16) * K + k) * 16 + n % 16 : size_t(k) * N + n;
+                    size_t at = ctc ? (size_t(n / 16) * K + k) * 16 + n % 16 : size_t(k) * N + n;
+                    if (fold) {
+                        // column 48 j + 16 kx + e: channel 16 j + e of tap (ky, kx), k = ky * C + c
+                        const int o = n / 48 * 16 + n % 16, kx = n % 48 / 16, ky = k / C, c = k % C;
+                        if (o >= int(op.oc)) continue;
+                        at = (size_t(ky * 3 + kx) * C + c) * op.oc + o;
+                    }
                     float v = values[op.w0 + at];
                     uint32_t u;
                     std::memcpy(&u, &v, 4);
@@ -1102,6 +1132,7 @@ int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_mode
         w->tc_kpad.push_back(kpad);
         w->tc_wmax.push_back(wmax);
         w->tc_bmax.push_back(bmax);
+        w->tc_fold.push_back(fold && hi != SIZE_MAX);
     }
     tc.resize(std::max<size_t>(tc.size(), 1) + 64, 0.0f);
     int code = PPOCR_E_DEVICE;

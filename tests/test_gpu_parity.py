@@ -82,6 +82,11 @@ CONV_CASES = [
     (5, 2, (2, 2, 2, 2), 6, 10, "sigmoid"),
     (3, 1, (1, 1, 1, 1), 16, 64, "hardsigmoidfifth"),
     (3, 1, (1, 1, 1, 1), 7, 13, "none"),
+    # 3-wide, 32-channel blocks: the tensor cores with the horizontal taps folded
+    (3, 1, (1, 1, 1, 1), 64, 40, "relu"),    # a slice's second 16-channel group half empty
+    (3, 1, (1, 1, 1, 1), 32, 4, "swish"),    # one 16-channel group, 4 live
+    (3, 1, (1, 1, 1, 1), 32, 128, "none"),   # four slices
+    (5, 1, (2, 2, 2, 2), 32, 24, "none"),    # 5x5: the unfolded windowed path
 ]
 
 
@@ -350,6 +355,36 @@ def test_detector_lanes(cuda_mod, oracle_mod):
             m.run(60_000)
             for i, want in enumerate(wants):
                 check(m.lane_output(i).copy(), want, exact=bool(options))
+
+
+def test_folded_conv_lanes(cuda_mod, oracle_mod):
+    """A 3x3 96 -> 24 conv (horizontal taps folded into the tensor cores'
+    columns, 120-pixel tiles of 30-pixel lane quadrants) over lanes whose
+    widths and sizes fall on every tile and quadrant edge: 1, 2, 29..31,
+    120, 121 pixels wide, one pixel high, and more tiles than SMs."""
+    ic, oc = 96, 24
+    wt = noise(9 * ic * oc, 5, 0.1)
+    b = noise(oc, 7, 0.5)
+    op = window(Op("conv", x=0, y=1, ic=ic, oc=oc, fused="swish", w=(0, wt.size), b=(wt.size, oc)), (3, 3), 1, 1, 1)
+    plan = single(op, (8, 8, ic), np.concatenate([wt, b]))
+    sizes = [(5, 1), (3, 2), (7, 29), (1, 30), (4, 31), (2, 120), (3, 121), (1, 1), (181, 97)]
+    xs = [noise(h * w * ic, 11 + i, 1.0) for i, (h, w) in enumerate(sizes)]
+    o = oracle_mod.Oracle(plan)
+    wants = []
+    for (h, w), x in zip(sizes, xs):
+        o.set_size(h, w)
+        wants.append(o.run(x)[0])
+    for options in (0, cuda_mod.OPT_NO_TENSOR_CORES):
+        with cuda_mod.Model(plan) as m:
+            if options:
+                m.set_options(options)
+            m.set_sizes(sizes)
+            for i, x in enumerate(xs):
+                m.lane_input_mut(i)[:] = x
+            m.run(60_000)
+            for i, want in enumerate(wants):
+                check(m.lane_output(i).copy(), want, exact=bool(options),
+                      tol=TOL * max(1.0, float(np.abs(want).max())))
 
 
 def test_detector_unfused_matches_fused(cuda_mod):

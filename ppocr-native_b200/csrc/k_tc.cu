@@ -54,6 +54,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "async.cuh"
 #include "devmath.cuh"
 #include "kernels.hpp"
 
@@ -90,9 +91,6 @@ struct Roles {
     static constexpr int THREADS = (W_EPI + EPI_WARPS) * 32;
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SM100 layout: start >> 4 in [0,14), leading offset
@@ -139,35 +137,6 @@ __device__ __forceinline__ void commit(uint32_t bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void bar_init(uint32_t bar, int count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-
-__device__ __forceinline__ void arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void arrive_expect(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return done != 0;
-}
-
-__device__ __forceinline__ unsigned long long global_ns() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
 
 // Waits for the phase of `bar` with this parity to complete. Gives up when
 // another role raised the abort flag, or after the time limit (then raises
@@ -190,29 +159,6 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volati
     }
 }
 
-// The same wait for the clean-up after an abort: bounded, flag ignored.
-__device__ __forceinline__ void drain(uint32_t bar, uint32_t parity) {
-    const unsigned long long t0 = global_ns();
-    while (!try_wait(bar, parity))
-        if (global_ns() - t0 > WAIT_LIMIT_NS) return;
-}
-
-// Tiled TMA loads (no multicast) completing on an mbarrier.
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-        "[%4];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, int x, int y, int z, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-        "[%5];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
-        : "memory");
-}
 
 // A named barrier among `count` threads (a multiple of 32): the threads
 // that wait there issue nothing.
@@ -369,7 +315,7 @@ __device__ void role_mma(const TcArgs &a, const Ctx &x, uint64_t *bfull) {
     }
     // the tensor core is done with shared memory and TMEM before the CTA
     // frees them
-    if (last_bar) drain(last_bar, last_parity);
+    if (last_bar) drain(last_bar, last_parity, WAIT_LIMIT_NS);
 }
 
 // The converters (8 warps, ct = 0..255): split each landed A block into its
@@ -801,9 +747,9 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
                 }
             if (*x.abort_flag) {
                 // the copies still in flight land before the CTA leaves
-                drain(bb, 0);
+                drain(bb, 0, WAIT_LIMIT_NS);
                 for (int q = 0; q < x.ns && q < it; q++)
-                    drain(smem_u32(&full[q]), uint32_t((it - 1 - q) / x.ns) & 1u);
+                    drain(smem_u32(&full[q]), uint32_t((it - 1 - q) / x.ns) & 1u, WAIT_LIMIT_NS);
             }
         }
     } else if (warp == R::W_MMA) {
@@ -895,7 +841,7 @@ __global__ void __launch_bounds__(Roles::THREADS, 1)
             if (*x.abort_flag)
                 // the copies still in flight land before the CTA leaves
                 for (int q = 0; q < x.ns && q < it; q++)
-                    drain(smem_u32(&full[q]), uint32_t((it - 1 - q) / x.ns) & 1u);
+                    drain(smem_u32(&full[q]), uint32_t((it - 1 - q) / x.ns) & 1u, WAIT_LIMIT_NS);
         }
     } else if (warp == R::W_MMA) {
         if (lane == 0) role_mma<false>(a, x, &bfull);

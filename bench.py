@@ -44,7 +44,7 @@ L2_FLUSH_BYTES = 256 << 20  # larger than the 126 MB L2
 TRAFFIC_PER_LAUNCH = 100.64e6
 TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch (profiles/pw_tc_kernel_1x1_24to24_992x768.md)"
 # The same for the dominant kernel's probe (`bench.py --workload conv3x3`).
-CONV_TRAFFIC_PER_LAUNCH = 78.71e6
+CONV_TRAFFIC_PER_LAUNCH = 78.19e6
 CONV_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
                        "(profiles/conv_tc_kernel_3x3_96to24_496x384.md)")
 

@@ -411,6 +411,90 @@ __global__ void __launch_bounds__(128) stem_kernel(const ConvArgs a) {
     }
 }
 
+// A 3x3 stride-2 RGB stem by row segments: a block computes STEM_SEG
+// consecutive outputs of one output row (grid y: the row over all lanes,
+// grid x: the segment). The three input rows under the segment are staged
+// in shared memory with coalesced loads (zeros outside the image), each
+// thread computes NB / 2 outputs of one pixel (bias first, then the 27 terms
+// in increasing k = (ky * 3 + kx) * 3 + c, padded taps as zeros: the same
+// bits as stem_kernel), and the segment's outputs, contiguous in the packed
+// output, leave through shared memory as coalesced 16-byte stores.
+constexpr int STEM_SEG = 128;
+
+template <int NB, bool QUICK>
+__global__ void __launch_bounds__(256) stem_rows_kernel(const ConvArgs a) {
+    constexpr int SPAN = 2 * STEM_SEG + 1;  // staged input columns
+    constexpr int OS = NB + 4;              // padded smem output row (conflict-free 16-byte stores)
+    constexpr int HALF = NB / 2;
+    __shared__ __align__(16) float ws[27 * NB];
+    __shared__ float bs[NB];
+    __shared__ float xin[3 * SPAN * 3];
+    __shared__ __align__(16) float yout[STEM_SEG * OS];
+    const int tid = threadIdx.x;
+    const LaneInfo &L = a.lanes[find_row_lane(a.lanes, a.nl, blockIdx.y)];
+    const int ow = __ldg(&L.ow), ih = __ldg(&L.ih), iw = __ldg(&L.iw);
+    const int oy = int(blockIdx.y - __ldg(&L.row0));
+    const int ox0 = int(blockIdx.x) * STEM_SEG;
+    if (ox0 >= ow) return;  // a narrower lane's row
+    const int cnt = ow - ox0 < STEM_SEG ? ow - ox0 : STEM_SEG;
+    for (int e = tid; e < 27 * NB; e += 256) ws[e] = __ldg(a.w + e);
+    for (int e = tid; e < NB; e += 256) bs[e] = a.b ? __ldg(a.b + e) : 0.0f;
+    const float *xl = a.src[0].p + __ldg(&L.ipix0) * 3;
+    const int iy0 = oy * 2 - a.pt, ix0 = ox0 * 2 - a.pl;
+    for (int e = tid; e < 3 * SPAN * 3; e += 256) {
+        const int r = e / (SPAN * 3), rem = e - r * (SPAN * 3);
+        const int iy = iy0 + r, ix = ix0 + rem / 3;
+        xin[e] = ((unsigned)iy < (unsigned)ih && (unsigned)ix < (unsigned)iw)
+                     ? __ldg(xl + ((long)iy * iw + ix0) * 3 + rem)
+                     : 0.0f;
+    }
+    __syncthreads();
+    const int p = tid % STEM_SEG, h = tid / STEM_SEG;
+    if (p < cnt) {
+        float in[27];
+#pragma unroll
+        for (int ky = 0; ky < 3; ky++)
+#pragma unroll
+            for (int kx = 0; kx < 3; kx++)
+#pragma unroll
+                for (int c = 0; c < 3; c++) in[(ky * 3 + kx) * 3 + c] = xin[(ky * SPAN + 2 * p + kx) * 3 + c];
+        float acc[HALF];
+#pragma unroll
+        for (int j = 0; j < HALF; j++) acc[j] = bs[h * HALF + j];
+#pragma unroll
+        for (int k = 0; k < 27; k++) {
+#pragma unroll
+            for (int j = 0; j < HALF; j += 4) {
+                const float4 w4 = *reinterpret_cast<const float4 *>(ws + k * NB + h * HALF + j);  // broadcast
+                acc[j] = ffma(w4.x, in[k], acc[j]);
+                acc[j + 1] = ffma(w4.y, in[k], acc[j + 1]);
+                acc[j + 2] = ffma(w4.z, in[k], acc[j + 2]);
+                acc[j + 3] = ffma(w4.w, in[k], acc[j + 3]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < HALF; j += 4)
+            *reinterpret_cast<float4 *>(yout + p * OS + h * HALF + j) =
+                make_float4(activate<QUICK>(a.act, acc[j]), activate<QUICK>(a.act, acc[j + 1]),
+                            activate<QUICK>(a.act, acc[j + 2]), activate<QUICK>(a.act, acc[j + 3]));
+    }
+    __syncthreads();
+    float *dst = a.y + (__ldg(&L.pix0) + (long)oy * ow + ox0) * NB;
+    for (int e = tid; e < cnt * (NB / 4); e += 256) {
+        const int px = e / (NB / 4), c4 = e - px * (NB / 4);
+        reinterpret_cast<float4 *>(dst)[e] = *reinterpret_cast<const float4 *>(yout + px * OS + 4 * c4);
+    }
+}
+
+template <int NB>
+void run_stem_rows(const ConvArgs &a, cudaStream_t s) {
+    const dim3 grid(unsigned((a.max_ow + STEM_SEG - 1) / STEM_SEG), unsigned(a.out_rows));
+    if (a.quick)
+        stem_rows_kernel<NB, true><<<grid, 256, 0, s>>>(a);
+    else
+        stem_rows_kernel<NB, false><<<grid, 256, 0, s>>>(a);
+}
+
 template <int TM, int TN, int TX, int TY, int BK>
 int run(const ConvArgs &a, cudaStream_t s, bool vec4, bool pw) {
     using C = Cfg<TM, TN, TX, TY, BK>;
@@ -473,6 +557,10 @@ int launch_conv(const ConvArgs &a, cudaStream_t s) {
     // RGB stems (bias first): the direct kernel
     if (a.C == 3 && a.nsrc == 1 && !a.src[0].shift && a.bias_mode == BIAS_FIRST && !a.gate && !a.res &&
         a.kh * a.kw <= 9 && (oc == 24 || oc == 48)) {
+        if (a.kh == 3 && a.kw == 3 && a.sh == 2 && a.sw == 2 && a.out_rows > 0 && a.out_rows < 65536 && a.max_ow > 0) {
+            oc == 24 ? run_stem_rows<24>(a, s) : run_stem_rows<48>(a, s);
+            return 1;
+        }
         const long blocks = std::min<long>((a.M + 127) / 128, 148L * 16);
         if (oc == 24)
             stem_kernel<24><<<unsigned(blocks), 128, 0, s>>>(a);

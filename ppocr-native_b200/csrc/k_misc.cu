@@ -133,14 +133,13 @@ __global__ void __launch_bounds__(256) mean_partial_kernel(const MeanArgs a) {
         double s = 0.0;
         if (row < rows) {
             int p = p0 + row;
-            // four independent loads in flight, added in pixel order
-            for (; p + 3 * rows < p1; p += 4 * rows) {
-                const float v0 = x[(long)p * a.c + c], v1 = x[(long)(p + rows) * a.c + c];
-                const float v2 = x[(long)(p + 2 * rows) * a.c + c], v3 = x[(long)(p + 3 * rows) * a.c + c];
-                s += (double)v0;
-                s += (double)v1;
-                s += (double)v2;
-                s += (double)v3;
+            // eight independent loads in flight, added in pixel order
+            for (; p + 7 * rows < p1; p += 8 * rows) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) v[u] = __ldg(x + (long)(p + u * rows) * a.c + c);
+#pragma unroll
+                for (int u = 0; u < 8; u++) s += (double)v[u];
             }
             for (; p < p1; p += rows) s += (double)x[(long)p * a.c + c];
             sums[row * a.c + c] = s;
@@ -177,8 +176,19 @@ __global__ void __launch_bounds__(1024) mean_final_kernel(const MeanArgs a) {
     const int hw = a.lanes[n].ih * a.lanes[n].iw;
     const int chunks = mean_chunks(hw, a.c);
     double s = 0.0;
-    if (c < a.c)
-        for (int k = row; k < chunks; k += 32) s += a.partial[((long)n * a.chunks + k) * a.c + c];
+    if (c < a.c) {
+        // eight loads in flight, added in run order
+        const double *pp = a.partial + (long)n * a.chunks * a.c + c;
+        int k = row;
+        for (; k + 7 * 32 < chunks; k += 8 * 32) {
+            double v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = pp[(long)(k + 32 * u) * a.c];
+#pragma unroll
+            for (int u = 0; u < 8; u++) s += v[u];
+        }
+        for (; k < chunks; k += 32) s += pp[(long)k * a.c];
+    }
     part[row][threadIdx.x % 32] = s;
     __syncthreads();
     if (row == 0 && c < a.c) {
@@ -316,6 +326,72 @@ __global__ void __launch_bounds__(ATT_Q) attention_kernel(const AttentionArgs a)
 #pragma unroll
     for (int d = 0; d < MAXHD; d++)
         if (d < hd) y[d] = out[d];
+}
+
+// Beside the tensor cores (tolerance mode): eight threads per query, thread
+// l taking the keys j = l mod 8. Two passes: the maximum of the scores
+// (reduced over the eight threads by shuffles), then the exponentials
+// (__expf) summed and the value rows accumulated with them; the eight
+// partial sums and rows are reduced by shuffles and the row divided by the
+// sum. Same K / V staging as attention_kernel.
+constexpr int ATT_FAST_Q = 32;  // queries per block (x 8 threads)
+
+template <int HD>
+__global__ void __launch_bounds__(ATT_FAST_Q * 8) attention_fast_kernel(const AttentionArgs a) {
+    extern __shared__ float kv[];  // K [t][HD], V [t][HD]
+    const int n = blockIdx.x / a.heads, h = blockIdx.x % a.heads;
+    const LaneInfo &L = a.lanes[n];
+    const int t = L.iw, c = a.c;
+    if (blockIdx.y * ATT_FAST_Q >= t) return;
+    float *K = kv, *V = kv + t * HD;
+    const float *x = a.x + L.ipix0 * 3 * c;
+    for (int i = threadIdx.x; i < t * HD; i += blockDim.x) {
+        const int j = i / HD, d = i - j * HD;
+        K[i] = x[(long)j * 3 * c + c + h * HD + d];
+        V[i] = x[(long)j * 3 * c + 2 * c + h * HD + d];
+    }
+    __syncthreads();
+    const int l = threadIdx.x % 8;
+    const int s = blockIdx.y * ATT_FAST_Q + threadIdx.x / 8;
+    const bool live = s < t;
+    const float scale = a.scale[0];
+    float q[HD];
+#pragma unroll
+    for (int d = 0; d < HD; d++) q[d] = live ? x[(long)s * 3 * c + h * HD + d] * scale : 0.0f;
+    auto score = [&](int j) {
+        const float *k = K + j * HD;
+        float acc = 0.0f;
+#pragma unroll
+        for (int d = 0; d < HD; d++) acc = fmaf(k[d], q[d], acc);
+        return acc;
+    };
+    float mx = -FLT_MAX;
+    for (int j = l; j < t; j += 8) mx = fmaxf(mx, score(j));
+#pragma unroll
+    for (int off = 4; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float sum = 0.0f, o[HD];
+#pragma unroll
+    for (int d = 0; d < HD; d++) o[d] = 0.0f;
+    for (int j = l; j < t; j += 8) {
+        const float p = __expf(score(j) - mx);
+        sum += p;
+        const float *v = V + j * HD;
+#pragma unroll
+        for (int d = 0; d < HD; d++) o[d] = fmaf(v[d], p, o[d]);
+    }
+#pragma unroll
+    for (int off = 4; off > 0; off >>= 1) {
+        sum += __shfl_xor_sync(0xffffffffu, sum, off);
+#pragma unroll
+        for (int d = 0; d < HD; d++) o[d] += __shfl_xor_sync(0xffffffffu, o[d], off);
+    }
+    if (!live) return;
+    const float r = 1.0f / sum;
+    float *y = a.y + (L.pix0 + s) * c + h * HD;
+    // the eight threads write two outputs each
+#pragma unroll
+    for (int d = 0; d < HD; d++)
+        if (d % 8 == l) y[d] = o[d] * r;
 }
 
 // --------------------------------------------------------------------- ctc
@@ -566,7 +642,10 @@ int launch_attention(const AttentionArgs &a, cudaStream_t s) {
     int hd = a.c / a.heads;
     size_t smem = sizeof(float) * 2 * a.tmax * hd;
     dim3 grid(unsigned(a.nl * a.heads), unsigned((a.tmax + ATT_Q - 1) / ATT_Q));
-    if (hd == 15)  // PP-OCRv6's 8 heads of 15 (tools/export_ocr.py:654)
+    if (hd == 15 && a.fast) {
+        dim3 fgrid(unsigned(a.nl * a.heads), unsigned((a.tmax + ATT_FAST_Q - 1) / ATT_FAST_Q));
+        attention_fast_kernel<15><<<fgrid, ATT_FAST_Q * 8, smem, s>>>(a);
+    } else if (hd == 15)  // PP-OCRv6's 8 heads of 15 (tools/export_ocr.py:654)
         attention_kernel<15><<<grid, ATT_Q, smem, s>>>(a);
     else
         attention_kernel<0><<<grid, ATT_Q, smem, s>>>(a);
@@ -579,6 +658,10 @@ bool ctc_supported(int ci) { return (size_t)ci * (CTC_PX + CTC_COLS) * sizeof(fl
 
 void configure_misc_kernels() {
     cudaFuncSetAttribute(ctc_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    // K and V of one lane and head (attention_supported: at most 160 KB)
+    cudaFuncSetAttribute(attention_kernel<15>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cudaFuncSetAttribute(attention_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    cudaFuncSetAttribute(attention_fast_kernel<15>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
 }
 
 int launch_ctc(const CtcArgs &a, cudaStream_t s) {

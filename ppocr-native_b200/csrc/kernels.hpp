@@ -41,6 +41,7 @@ struct LaneInfo {
     long tile0;               // first 128-pixel output tile when every lane is tiled on its own
     long run0;                // first DW_RUN-pixel run along an output row (depthwise threads)
     long ftile0;              // first FOLD_OUT-pixel tile of a tensor-core conv with folded taps
+    long row0;                // first output row (rows of all lanes back to back)
     int ih, iw, oh, ow;
 };
 
@@ -53,6 +54,19 @@ __device__ __forceinline__ int find_lane(const LaneInfo *L, int nl, long m, bool
         int mid = (lo + hi + 1) >> 1;
         long start = input ? __ldg(&L[mid].ipix0) : __ldg(&L[mid].pix0);
         if (start <= m)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
+}
+
+// The lane holding output row `r` (LaneInfo::row0).
+__device__ __forceinline__ int find_row_lane(const LaneInfo *L, int nl, long r) {
+    int lo = 0, hi = nl - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (__ldg(&L[mid].row0) <= r)
             lo = mid;
         else
             hi = mid - 1;
@@ -92,6 +106,8 @@ struct ConvArgs {
     const float *res = nullptr;   // [M][oc]: y = act2(act(conv) + res)
     int act2 = 0;
     bool quick = false;           // stems: the activation's quick quotient (tensor-core mode)
+    long out_rows = 0;            // output rows of all lanes (LaneInfo::row0)
+    int max_ow = 0;               // the widest lane's output width
 };
 
 // Output pixels along one row that a depthwise thread computes together.
@@ -177,6 +193,7 @@ struct AttentionArgs {
     const float *scale = nullptr;
     const LaneInfo *lanes = nullptr;  // t of lane n = lanes[n].iw
     int nl = 1, tmax = 0, c = 0, heads = 1;
+    bool fast = false;  // tensor-core mode: eight threads per query, __expf, any order
 };
 
 // CTC head over `cols` = 16 * ceil(vocab / 16) panel columns: each block

@@ -442,7 +442,7 @@ namespace {
 // shifts of a dense convolution's inputs (pixel prefix sums per source).
 std::vector<LaneInfo> lane_table(const Group &g, size_t i, const std::vector<int> &shifts) {
     std::vector<LaneInfo> t(g.count());
-    long pix = 0, ipix = 0, spix[MAX_SOURCES] = {0, 0, 0, 0}, tile = 0, run = 0, ftile = 0;
+    long pix = 0, ipix = 0, spix[MAX_SOURCES] = {0, 0, 0, 0}, tile = 0, run = 0, ftile = 0, row = 0;
     for (size_t n = 0; n < g.count(); n++) {
         const Op &op = g.lane(n).ops[i];
         LaneInfo &L = t[n];
@@ -454,6 +454,8 @@ std::vector<LaneInfo> lane_table(const Group &g, size_t i, const std::vector<int
         run += long(op.oh) * ((long(op.ow) + DW_RUN - 1) / DW_RUN);
         L.ftile0 = ftile;
         ftile += (long(op.oh * op.ow) + FOLD_OUT - 1) / FOLD_OUT;
+        L.row0 = row;
+        row += long(op.oh);
         for (int s = 0; s < MAX_SOURCES; s++) L.spix0[s] = spix[s];
         L.ih = int(op.ih); L.iw = int(op.iw); L.oh = int(op.oh); L.ow = int(op.ow);
         pix += long(op.oh * op.ow);
@@ -694,8 +696,11 @@ int ppocr_model::build_group(Group &g, std::string &err) {
     // Pushes a dense conv's launch: the tensor cores where the layer goes
     // there, else the FP32 implicit GEMM; `pre` runs first (a depthwise
     // layer whose output it reads, or nothing).
-    auto push_conv = [&](size_t i, const ConvArgs &c, const LaneInfo *Lh, std::function<int(cudaStream_t)> pre) {
+    auto push_conv = [&](size_t i, const ConvArgs &c0, const LaneInfo *Lh, std::function<int(cudaStream_t)> pre) {
         const Op &op = p0.ops[i];
+        ConvArgs c = c0;
+        c.out_rows = Lh[c.nl - 1].row0 + Lh[c.nl - 1].oh;
+        for (int n = 0; n < c.nl; n++) c.max_ow = std::max(c.max_ow, Lh[n].ow);
         if (reads_vector[i] && op.pointwise() && c.nsrc == 1 && !c.src[0].shift) {
             // the same bits either way
             if (conv_vector_supported(c))
@@ -780,6 +785,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             a.pt = int(op.pt); a.pl = int(op.pl);
             a.act = op.fused;
             a.bias_mode = bias_mode(op);
+            a.quick = tc_allowed;  // stems: the quick quotient beside the tensor cores
             a.y = buf(op.y);
             if (st.has_add) {
                 const Op &add = p0.ops[st.c];
@@ -877,6 +883,7 @@ int ppocr_model::build_group(Group &g, std::string &err) {
             AttentionArgs a;
             a.x = buf(op.x); a.y = buf(op.y); a.scale = W.w(i);
             a.lanes = L; a.nl = nl; a.tmax = tmax; a.c = int(op.oc); a.heads = int(op.n2);
+            a.fast = tc_allowed;
             g.launches.push_back([a](cudaStream_t s) { return launch_attention(a, s); });
             break;
         }

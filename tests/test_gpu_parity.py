@@ -198,12 +198,19 @@ def test_mean_on_a_page(cuda_mod, oracle_mod):
     assert max_gap(got, want) <= 1e-4
 
 
-def test_layernorm_attention(cuda_mod, oracle_mod):
-    t, c, heads = 37, 120, 8
+@pytest.mark.parametrize("t", [1, 7, 37, 203])
+def test_attention(cuda_mod, oracle_mod, t):
+    """Exact on the FP32 path; beside the tensor cores (eight threads per
+    query, __expf) within the tolerance."""
+    c, heads = 120, 8
     x = noise(t * 3 * c, 21, 1.5)
     att = Op("attention", x=0, y=1, ic=3 * c, oc=c, n2=heads, w=(0, 1))
     plan = single(att, (1, t, 3 * c), np.float32([15 ** -0.5]))
-    check(gpu_run(cuda_mod, plan, x)[0][0], oracle_run(oracle_mod, plan, x)[0])
+    check_both(cuda_mod, oracle_mod, plan, x)
+
+
+def test_layernorm_attention(cuda_mod, oracle_mod):
+    t, c = 37, 120
     gamma, beta = noise(c, 3, 1.0) + 1, noise(c, 4, 0.5)
     ln = Op("layernorm", x=0, y=1, ic=c, oc=c, w=(0, 2 * c + 1))
     xs = noise(t * c, 9, 3.0)

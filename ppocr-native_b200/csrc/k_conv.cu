@@ -317,15 +317,35 @@ __global__ void __launch_bounds__(VEC_COLS *VEC_ROWS) conv_vector_kernel(const C
     const long m0 = (long)blockIdx.y * VEC_ROWS;
     const int cols = min(VEC_COLS, a.oc - n0);
     const int rows = int(min((long)VEC_ROWS, a.M - m0));
-    for (int e = threadIdx.x; e < a.C * VEC_COLS; e += blockDim.x) {
-        const int k = e / VEC_COLS, j = e - k * VEC_COLS;
-        ws[e] = j < cols ? __ldg(a.w + (long)k * a.oc + n0 + j) : 0.0f;
+    // staged eight loads at a time, so that their latencies overlap
+    constexpr int BATCH = 8;
+    const int wn = a.C * VEC_COLS;
+    for (int e0 = threadIdx.x; e0 < wn; e0 += BATCH * blockDim.x) {
+        float v[BATCH];
+#pragma unroll
+        for (int u = 0; u < BATCH; u++) {
+            const int e = e0 + u * blockDim.x, k = e / VEC_COLS, j = e - k * VEC_COLS;
+            v[u] = (e < wn && j < cols) ? __ldg(a.w + (long)k * a.oc + n0 + j) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < BATCH; u++)
+            if (e0 + u * blockDim.x < wn) ws[e0 + u * blockDim.x] = v[u];
     }
-    for (int e = threadIdx.x; e < rows * a.C; e += blockDim.x) {
-        const int r = e / a.C, k = e - r * a.C;
-        float v = __ldg(a.src[0].p + (m0 + r) * a.C + k);
-        if (a.gate) v = fmul(v, __ldg(a.gate + (long)find_lane(a.lanes, a.nl, m0 + r) * a.C + k));
-        xs[e] = v;
+    const int xn = rows * a.C;
+    for (int e0 = threadIdx.x; e0 < xn; e0 += BATCH * blockDim.x) {
+        float v[BATCH];
+#pragma unroll
+        for (int u = 0; u < BATCH; u++) {
+            const int e = e0 + u * blockDim.x, r = e / a.C, k = e - r * a.C;
+            v[u] = 0.0f;
+            if (e < xn) {
+                v[u] = __ldg(a.src[0].p + (m0 + r) * a.C + k);
+                if (a.gate) v[u] = fmul(v[u], __ldg(a.gate + (long)find_lane(a.lanes, a.nl, m0 + r) * a.C + k));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < BATCH; u++)
+            if (e0 + u * blockDim.x < xn) xs[e0 + u * blockDim.x] = v[u];
     }
     __syncthreads();
     const int r = threadIdx.x / VEC_COLS, j = threadIdx.x % VEC_COLS;
@@ -441,12 +461,21 @@ __global__ void __launch_bounds__(256) stem_rows_kernel(const ConvArgs a) {
     for (int e = tid; e < NB; e += 256) bs[e] = a.b ? __ldg(a.b + e) : 0.0f;
     const float *xl = a.src[0].p + __ldg(&L.ipix0) * 3;
     const int iy0 = oy * 2 - a.pt, ix0 = ox0 * 2 - a.pl;
-    for (int e = tid; e < 3 * SPAN * 3; e += 256) {
-        const int r = e / (SPAN * 3), rem = e - r * (SPAN * 3);
-        const int iy = iy0 + r, ix = ix0 + rem / 3;
-        xin[e] = ((unsigned)iy < (unsigned)ih && (unsigned)ix < (unsigned)iw)
-                     ? __ldg(xl + ((long)iy * iw + ix0) * 3 + rem)
-                     : 0.0f;
+    // eight loads in flight per thread
+    constexpr int NX = 3 * SPAN * 3;
+    for (int e0 = tid; e0 < NX; e0 += 8 * 256) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int e = e0 + u * 256, r = e / (SPAN * 3), rem = e - r * (SPAN * 3);
+            const int iy = iy0 + r, ix = ix0 + rem / 3;
+            v[u] = (e < NX && (unsigned)iy < (unsigned)ih && (unsigned)ix < (unsigned)iw)
+                       ? __ldg(xl + ((long)iy * iw + ix0) * 3 + rem)
+                       : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+            if (e0 + u * 256 < NX) xin[e0 + u * 256] = v[u];
     }
     __syncthreads();
     const int p = tid % STEM_SEG, h = tid / STEM_SEG;

@@ -20,50 +20,74 @@ unsigned grid_for(long work, int threads = 256) {
 
 // ----------------------------------------------------------------- eltwise
 
+// Four values (VEC) or one at a time; index arithmetic in 32 bits when the
+// tensor allows (SMALL), 64 otherwise.
 template <int VEC>
+__device__ __forceinline__ void load_vec(const float *p, float v[VEC]) {
+    if (VEC == 4) {
+        const float4 q = __ldg(reinterpret_cast<const float4 *>(p));
+        v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+    } else {
+        v[0] = __ldg(p);
+    }
+}
+
+template <int VEC, bool SMALL>
 __global__ void __launch_bounds__(256) elt_kernel(const EltArgs a) {
     const int cout = a.mode == ELT_CONCAT ? a.c + a.c2 : a.c;
     const long total = a.M * cout / VEC;
     for (long g = (long)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (long)gridDim.x * blockDim.x) {
-        long e = g * VEC;
-        long m = e / cout;
-        int c = int(e - m * cout);
+        const long e = g * VEC;
+        const long m = SMALL ? long(unsigned(e) / unsigned(cout)) : e / cout;
+        const int c = int(e - m * cout);
         float v[VEC];
         switch (a.mode) {
-        case ELT_ADD:
+        case ELT_ADD: {
+            float p[VEC], q[VEC];
+            load_vec<VEC>(a.x + e, p);
+            load_vec<VEC>(a.x2 + e, q);
 #pragma unroll
-            for (int k = 0; k < VEC; k++) v[k] = activate(a.act, fadd(a.x[e + k], a.x2[e + k]));
+            for (int k = 0; k < VEC; k++) v[k] = activate(a.act, fadd(p[k], q[k]));
             break;
+        }
         case ELT_CHANNELMUL:
         case ELT_GATE_ADD: {
-            int n = find_lane(a.lanes, a.nl, m);
-            const float *g = a.x2 + (long)n * a.c + c;
+            const int n = a.nl > 1 ? find_lane(a.lanes, a.nl, m) : 0;
+            float x[VEC], g[VEC];
+            load_vec<VEC>(a.x + e, x);
+            load_vec<VEC>(a.x2 + (long)n * a.c + c, g);
 #pragma unroll
             for (int k = 0; k < VEC; k++) {
-                float x = a.x[e + k];
-                float p = fmul(x, g[k]);
-                v[k] = a.mode == ELT_CHANNELMUL ? p : activate(a.act, fadd(p, x));
+                const float p = fmul(x[k], g[k]);
+                v[k] = a.mode == ELT_CHANNELMUL ? p : activate(a.act, fadd(p, x[k]));
             }
             break;
         }
         case ELT_UPSAMPLE:
         case ELT_UPSAMPLE_ADD: {
-            const LaneInfo &L = a.lanes[find_lane(a.lanes, a.nl, m)];
-            int ow = __ldg(&L.ow);
-            int r = int(m - __ldg(&L.pix0));
-            int oy = r / ow, ox = r - oy * ow;
-            long ip = __ldg(&L.ipix0) + (long)(oy / a.sh) * __ldg(&L.iw) + ox / a.sw;
-            const float *src = a.x + ip * a.c + c;
+            const LaneInfo &L = a.lanes[a.nl > 1 ? find_lane(a.lanes, a.nl, m) : 0];
+            const int ow = __ldg(&L.ow);
+            const int r = int(m - __ldg(&L.pix0));
+            const int oy = r / ow, ox = r - oy * ow;
+            const long ip = __ldg(&L.ipix0) + (long)(oy / a.sh) * __ldg(&L.iw) + ox / a.sw;
+            float u[VEC];
+            load_vec<VEC>(a.x + ip * a.c + c, u);
+            if (a.mode == ELT_UPSAMPLE) {
 #pragma unroll
-            for (int k = 0; k < VEC; k++) v[k] = a.mode == ELT_UPSAMPLE ? src[k] : fadd(a.x2[e + k], src[k]);
+                for (int k = 0; k < VEC; k++) v[k] = u[k];
+            } else {
+                float q[VEC];
+                load_vec<VEC>(a.x2 + e, q);
+#pragma unroll
+                for (int k = 0; k < VEC; k++) v[k] = fadd(q[k], u[k]);
+            }
             break;
         }
-        default: {  // ELT_CONCAT
-#pragma unroll
-            for (int k = 0; k < VEC; k++) {
-                int ck = c + k;
-                v[k] = ck < a.c ? a.x[m * a.c + ck] : a.x2[m * a.c2 + (ck - a.c)];
-            }
+        default: {  // ELT_CONCAT: c, a.c and a.c2 are multiples of VEC
+            if (c < a.c)
+                load_vec<VEC>(a.x + m * a.c + c, v);
+            else
+                load_vec<VEC>(a.x2 + m * a.c2 + (c - a.c), v);
         }
         }
         if (VEC == 4)
@@ -345,10 +369,20 @@ __global__ void __launch_bounds__(ATT_FAST_Q * 8) attention_fast_kernel(const At
     if (blockIdx.y * ATT_FAST_Q >= t) return;
     float *K = kv, *V = kv + t * HD;
     const float *x = a.x + L.ipix0 * 3 * c;
-    for (int i = threadIdx.x; i < t * HD; i += blockDim.x) {
-        const int j = i / HD, d = i - j * HD;
-        K[i] = x[(long)j * 3 * c + c + h * HD + d];
-        V[i] = x[(long)j * 3 * c + 2 * c + h * HD + d];
+    for (int i0 = threadIdx.x; i0 < t * HD; i0 += 4 * blockDim.x) {
+        float kk[4], vv[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int i = i0 + u * blockDim.x, j = i / HD, d = i - j * HD;
+            kk[u] = i < t * HD ? __ldg(x + (long)j * 3 * c + c + h * HD + d) : 0.0f;
+            vv[u] = i < t * HD ? __ldg(x + (long)j * 3 * c + 2 * c + h * HD + d) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+            if (i0 + u * blockDim.x < t * HD) {
+                K[i0 + u * blockDim.x] = kk[u];
+                V[i0 + u * blockDim.x] = vv[u];
+            }
     }
     __syncthreads();
     const int l = threadIdx.x % 8;
@@ -603,13 +637,18 @@ int launch_gather(const GatherArgs &a, cudaStream_t s) {
 }
 
 int launch_elt(const EltArgs &a, cudaStream_t s) {
-    int cout = a.mode == ELT_CONCAT ? a.c + a.c2 : a.c;
-    bool vec = cout % 4 == 0 && a.c % 4 == 0 && (a.mode != ELT_CONCAT || a.c2 % 4 == 0);
-    long total = a.M * cout;
+    const int cout = a.mode == ELT_CONCAT ? a.c + a.c2 : a.c;
+    const auto aligned = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const bool vec = cout % 4 == 0 && a.c % 4 == 0 && (a.mode != ELT_CONCAT || a.c2 % 4 == 0) && aligned(a.x) &&
+                     aligned(a.y) && (!a.x2 || aligned(a.x2));
+    const long total = a.M * cout;
+    const bool small = total < (1L << 31);
     if (vec)
-        elt_kernel<4><<<grid_for(total / 4), 256, 0, s>>>(a);
+        small ? elt_kernel<4, true><<<grid_for(total / 4), 256, 0, s>>>(a)
+              : elt_kernel<4, false><<<grid_for(total / 4), 256, 0, s>>>(a);
     else
-        elt_kernel<1><<<grid_for(total), 256, 0, s>>>(a);
+        small ? elt_kernel<1, true><<<grid_for(total), 256, 0, s>>>(a)
+              : elt_kernel<1, false><<<grid_for(total), 256, 0, s>>>(a);
     return 1;
 }
 

@@ -455,25 +455,37 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
             tbase = __ldg(&L.pix0) + (long)iy * a.tkh * tow + (long)ix * a.tkw;
         }
         if (MODE == EPI_CTC) {
-            // this thread's row over the columns of its block, in increasing
-            // column order: an online softmax keeping the first maximum
+            // this thread's row over the columns of its block, 16 at a
+            // time in increasing column order: the chunk's maximum (its
+            // first column on ties) raises the running one, then the
+            // chunk's exponentials (__expf, columns past vocab as zeros)
+            // join the running sum
             float m = -FLT_MAX, sum = 0.0f;
             int best = 0x7fffffff;
             for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
                 float v[16];
                 tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);
+                float cm = -FLT_MAX;
+                int ci = 0x7fffffff;
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
                     const int col = x.n0 + c0 + j;
-                    if (col >= a.vocab) continue;
-                    const float l = fadd(v[j], bias_s[c0 + j]);
-                    if (l > m) {
-                        sum = m > -FLT_MAX ? ffma(sum, exp_neg(fsub(m, l)), 1.0f) : 1.0f;
-                        m = l;
-                        best = col;
-                    } else {
-                        sum = fadd(sum, exp_neg(fsub(l, m)));
+                    v[j] = col < a.vocab ? v[j] + bias_s[c0 + j] : -FLT_MAX;
+                    if (v[j] > cm) {
+                        cm = v[j];
+                        ci = col;
                     }
+                }
+                if (cm > m) {
+                    sum = m > -FLT_MAX ? sum * __expf(m - cm) : 0.0f;
+                    m = cm;
+                    best = ci;
+                }
+                if (m > -FLT_MAX) {
+                    float cs = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) cs += __expf(v[j] - m);
+                    sum += cs;
                 }
             }
             if (lane < nrows) {
@@ -873,7 +885,7 @@ __global__ void __launch_bounds__(256) ctc_tc_merge_kernel(const CtcMergeArgs a)
     for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
     float sum = 0.0f;
     for (int b = lane; b < a.blocks; b += 32)
-        if (st[b * 3] > -FLT_MAX) sum = fadd(sum, fmul(st[b * 3 + 1], exp_neg(fsub(st[b * 3], m))));
+        if (st[b * 3] > -FLT_MAX) sum = fadd(sum, fmul(st[b * 3 + 1], __expf(fsub(st[b * 3], m))));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
         const float o = __shfl_xor_sync(0xffffffffu, sum, off);

@@ -403,7 +403,8 @@ __device__ void role_convert(const TcArgs &a, const Ctx &x, int ct, int warp, in
             tmem_st16(x.tmem + tlane + col + 32, lv);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            arrive(smem_u32(&x.conv[s]));
+            __syncwarp();
+            if (lane == 0) arrive(smem_u32(&x.conv[s]));  // one arrival per warp
             if (++s == x.ns) {
                 s = 0;
                 ph ^= 1u;
@@ -495,7 +496,8 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
                 st[2] = __int_as_float(best);
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            arrive(smem_u32(&x.acce[buf]));
+            __syncwarp();
+            if (lane == 0) arrive(smem_u32(&x.acce[buf]));  // one arrival per warp
             continue;
         }
         for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
@@ -561,7 +563,8 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
             __syncwarp();
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        arrive(smem_u32(&x.acce[buf]));
+        __syncwarp();
+        if (lane == 0) arrive(smem_u32(&x.acce[buf]));  // one arrival per warp
     }
 }
 
@@ -649,7 +652,8 @@ __device__ void role_epilogue_fold(const TcArgs &a, const Ctx &x, int e, int war
             __syncwarp();
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        arrive(smem_u32(&x.acce[buf]));
+        __syncwarp();
+        if (lane == 0) arrive(smem_u32(&x.acce[buf]));  // one arrival per warp
     }
 }
 
@@ -661,12 +665,12 @@ __device__ __forceinline__ void setup(const TcArgs &a, Ctx &x, int full_count, u
     if (tid == 0) {
         for (int s = 0; s < x.ns; s++) {
             bar_init(smem_u32(&x.full[s]), full_count);
-            bar_init(smem_u32(&x.conv[s]), CONV_THREADS);
+            bar_init(smem_u32(&x.conv[s]), CONV_THREADS / 32);
             bar_init(smem_u32(&x.empty[s]), 1);
         }
         for (int b = 0; b < 2; b++) {
             bar_init(smem_u32(&x.accf[b]), 1);
-            bar_init(smem_u32(&x.acce[b]), EPI_WARPS * 32);
+            bar_init(smem_u32(&x.acce[b]), EPI_WARPS);
         }
         bar_init(smem_u32(bfull), 1);
         *abort_s = 0;

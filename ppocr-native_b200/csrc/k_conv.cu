@@ -441,6 +441,15 @@ __global__ void __launch_bounds__(128) stem_kernel(const ConvArgs a) {
 // output, leave through shared memory as coalesced 16-byte stores.
 constexpr int STEM_SEG = 128;
 
+template <int N, int ACT, bool QUICK>
+__device__ __forceinline__ void stem_activate(const float acc[N], float *out) {
+#pragma unroll
+    for (int j = 0; j < N; j += 4)
+        *reinterpret_cast<float4 *>(out + j) =
+            make_float4(activate_t<ACT, QUICK>(acc[j]), activate_t<ACT, QUICK>(acc[j + 1]),
+                        activate_t<ACT, QUICK>(acc[j + 2]), activate_t<ACT, QUICK>(acc[j + 3]));
+}
+
 template <int NB, bool QUICK>
 __global__ void __launch_bounds__(256) stem_rows_kernel(const ConvArgs a) {
     constexpr int SPAN = 2 * STEM_SEG + 1;  // staged input columns
@@ -461,22 +470,28 @@ __global__ void __launch_bounds__(256) stem_rows_kernel(const ConvArgs a) {
     for (int e = tid; e < NB; e += 256) bs[e] = a.b ? __ldg(a.b + e) : 0.0f;
     const float *xl = a.src[0].p + __ldg(&L.ipix0) * 3;
     const int iy0 = oy * 2 - a.pt, ix0 = ox0 * 2 - a.pl;
-    // eight loads in flight per thread
-    constexpr int NX = 3 * SPAN * 3;
-    for (int e0 = tid; e0 < NX; e0 += 8 * 256) {
-        float v[8];
+    // each staged row is one run of 3 * SPAN floats of the input row (zeros
+    // outside the image): all twelve loads of a thread in flight at once
+    constexpr int RF = 3 * SPAN, PER = (RF + 255) / 256;
+    const int lo = (ix0 < 0 ? -ix0 : 0) * 3, hi = (iw - ix0 < SPAN ? iw - ix0 : SPAN) * 3;
+    float v[3][PER];
 #pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int e = e0 + u * 256, r = e / (SPAN * 3), rem = e - r * (SPAN * 3);
-            const int iy = iy0 + r, ix = ix0 + rem / 3;
-            v[u] = (e < NX && (unsigned)iy < (unsigned)ih && (unsigned)ix < (unsigned)iw)
-                       ? __ldg(xl + ((long)iy * iw + ix0) * 3 + rem)
-                       : 0.0f;
+    for (int r = 0; r < 3; r++) {
+        const bool row_ok = (unsigned)(iy0 + r) < (unsigned)ih;
+        const float *src = xl + ((long)(iy0 + r) * iw + ix0) * 3;
+#pragma unroll
+        for (int u = 0; u < PER; u++) {
+            const int j = tid + u * 256;
+            v[r][u] = (row_ok && j >= lo && j < hi) ? __ldg(src + j) : 0.0f;
         }
-#pragma unroll
-        for (int u = 0; u < 8; u++)
-            if (e0 + u * 256 < NX) xin[e0 + u * 256] = v[u];
     }
+#pragma unroll
+    for (int r = 0; r < 3; r++)
+#pragma unroll
+        for (int u = 0; u < PER; u++) {
+            const int j = tid + u * 256;
+            if (j < RF) xin[r * RF + j] = v[r][u];
+        }
     __syncthreads();
     const int p = tid % STEM_SEG, h = tid / STEM_SEG;
     if (p < cnt) {
@@ -501,11 +516,18 @@ __global__ void __launch_bounds__(256) stem_rows_kernel(const ConvArgs a) {
                 acc[j + 3] = ffma(w4.w, in[k], acc[j + 3]);
             }
         }
-#pragma unroll
-        for (int j = 0; j < HALF; j += 4)
-            *reinterpret_cast<float4 *>(yout + p * OS + h * HALF + j) =
-                make_float4(activate<QUICK>(a.act, acc[j]), activate<QUICK>(a.act, acc[j + 1]),
-                            activate<QUICK>(a.act, acc[j + 2]), activate<QUICK>(a.act, acc[j + 3]));
+        float *out = yout + p * OS + h * HALF;
+        // one branch on the activation per thread, not per value
+        switch (a.act) {
+        case 1: stem_activate<HALF, 1, QUICK>(acc, out); break;
+        case 2: stem_activate<HALF, 2, QUICK>(acc, out); break;
+        case 3: stem_activate<HALF, 3, QUICK>(acc, out); break;
+        case 4: stem_activate<HALF, 4, QUICK>(acc, out); break;
+        case 5: stem_activate<HALF, 5, QUICK>(acc, out); break;
+        case 6: stem_activate<HALF, 6, QUICK>(acc, out); break;
+        case 7: stem_activate<HALF, 7, QUICK>(acc, out); break;
+        default: stem_activate<HALF, 0, QUICK>(acc, out); break;
+        }
     }
     __syncthreads();
     float *dst = a.y + (__ldg(&L.pix0) + (long)oy * ow + ox0) * NB;

@@ -87,6 +87,18 @@ __global__ void __launch_bounds__(256) dw_kernel(const DwArgs a) {
     }
 }
 
+// The first n outputs of a run, activated, four channels each.
+template <int ACT, bool QUICK>
+__device__ __forceinline__ void dw_store(const float4 (&v)[DW_RUN], float *dst, int c, int n) {
+#pragma unroll
+    for (int j = 0; j < DW_RUN; j++) {
+        if (j >= n) break;
+        const float4 o = make_float4(activate_t<ACT, QUICK>(v[j].x), activate_t<ACT, QUICK>(v[j].y),
+                                     activate_t<ACT, QUICK>(v[j].z), activate_t<ACT, QUICK>(v[j].w));
+        *reinterpret_cast<float4 *>(dst + (long)j * c) = o;
+    }
+}
+
 // Depthwise outputs of DW_RUN consecutive pixels of one output row for four
 // channels per thread: the input columns under the run are loaded once per
 // kernel row (a window of (DW_RUN - 1) * S + K float4s) and shared by the
@@ -152,15 +164,29 @@ __global__ void __launch_bounds__(256) dw_row_kernel(const DwArgs a, int per_blo
             }
         }
         float *dst = a.y + (__ldg(&L.pix0) + (long)oy * ow + ox0) * a.c + c;
+        const int n = ow - ox0 < DW_RUN ? ow - ox0 : DW_RUN;
+        if constexpr (K == 5) {
+            // (the 5x5 kernels keep the per-value branch: the per-run one
+            // costs them registers)
 #pragma unroll
-        for (int j = 0; j < DW_RUN; j++) {
-            if (ox0 + j >= ow) break;
-            float4 o;
-            o.x = activate<QUICK>(a.act, v[j].x);
-            o.y = activate<QUICK>(a.act, v[j].y);
-            o.z = activate<QUICK>(a.act, v[j].z);
-            o.w = activate<QUICK>(a.act, v[j].w);
-            *reinterpret_cast<float4 *>(dst + (long)j * a.c) = o;
+            for (int j = 0; j < DW_RUN; j++) {
+                if (j >= n) break;
+                const float4 o = make_float4(activate<QUICK>(a.act, v[j].x), activate<QUICK>(a.act, v[j].y),
+                                             activate<QUICK>(a.act, v[j].z), activate<QUICK>(a.act, v[j].w));
+                *reinterpret_cast<float4 *>(dst + (long)j * a.c) = o;
+            }
+            continue;
+        }
+        // one branch on the activation per run, not per value
+        switch (a.act) {
+        case 1: dw_store<1, QUICK>(v, dst, a.c, n); break;
+        case 2: dw_store<2, QUICK>(v, dst, a.c, n); break;
+        case 3: dw_store<3, QUICK>(v, dst, a.c, n); break;
+        case 4: dw_store<4, QUICK>(v, dst, a.c, n); break;
+        case 5: dw_store<5, QUICK>(v, dst, a.c, n); break;
+        case 6: dw_store<6, QUICK>(v, dst, a.c, n); break;
+        case 7: dw_store<7, QUICK>(v, dst, a.c, n); break;
+        default: dw_store<0, QUICK>(v, dst, a.c, n); break;
         }
     }
 }

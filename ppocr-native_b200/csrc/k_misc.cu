@@ -711,7 +711,58 @@ int launch_ctc(const CtcArgs &a, cudaStream_t s) {
     return 2;
 }
 
+// A 2x2 transposed conv to one channel (the DB head's last layer): one
+// thread per input pixel, its channels read as float4s, the 4 x ic weights
+// in shared memory, the same sums in the same order as convt_kernel; the
+// 2x2 output block leaves as two float2 stores.
+__global__ void __launch_bounds__(256) convt_2x2x1_kernel(const ConvTArgs a) {
+    __shared__ __align__(16) float ws[256 * 4];
+    for (int e = threadIdx.x; e < a.ic * 4; e += blockDim.x) ws[e] = __ldg(a.w + e);
+    __syncthreads();
+    float bias[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) bias[j] = a.b ? __ldg(a.b + j) : 0.0f;
+    for (long pix = (long)blockIdx.x * blockDim.x + threadIdx.x; pix < a.Min; pix += (long)gridDim.x * blockDim.x) {
+        const float4 *x = reinterpret_cast<const float4 *>(a.x + pix * a.ic);
+        float acc[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[j] = a.bias_first ? bias[j] : 0.0f;
+        for (int i4 = 0; i4 < a.ic / 4; i4++) {
+            const float4 xv = __ldg(x + i4);
+            const float xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float4 w = *reinterpret_cast<const float4 *>(ws + (4 * i4 + u) * 4);
+                acc[0] = ffma(w.x, xs[u], acc[0]);
+                acc[1] = ffma(w.y, xs[u], acc[1]);
+                acc[2] = ffma(w.z, xs[u], acc[2]);
+                acc[3] = ffma(w.w, xs[u], acc[3]);
+            }
+        }
+        const LaneInfo &L = a.lanes[a.nl > 1 ? find_lane(a.lanes, a.nl, pix, true) : 0];
+        const int iw = __ldg(&L.iw), ow = iw * 2;
+        const int r = int(pix - __ldg(&L.ipix0));
+        const int iy = r / iw, ix = r - iy * iw;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            v[j] = acc[j];
+            if (a.b && !a.bias_first) v[j] = fadd(v[j], bias[j]);
+            v[j] = activate(a.act, v[j]);
+        }
+        float *y = a.y + __ldg(&L.pix0) + (long)(2 * iy) * ow + 2 * ix;
+        *reinterpret_cast<float2 *>(y) = make_float2(v[0], v[1]);       // ky = 0: kx = 0, 1
+        *reinterpret_cast<float2 *>(y + ow) = make_float2(v[2], v[3]);  // ky = 1
+    }
+}
+
 int launch_convt(const ConvTArgs &a, cudaStream_t s) {
+    const auto aligned = [](const void *p, int n) { return (reinterpret_cast<uintptr_t>(p) & (n - 1)) == 0; };
+    if (a.kh == 2 && a.kw == 2 && a.oc == 1 && a.ic % 4 == 0 && a.ic <= 256 && aligned(a.x, 16) &&
+        aligned(a.y, 8)) {
+        convt_2x2x1_kernel<<<grid_for(a.Min), 256, 0, s>>>(a);
+        return 1;
+    }
     int cols = a.kh * a.kw * a.oc;
     long total = a.Min * ((cols + 3) / 4);
     convt_kernel<<<grid_for(total), 256, 0, s>>>(a);

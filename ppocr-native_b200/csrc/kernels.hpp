@@ -220,11 +220,6 @@ struct ConvTArgs {
     int ic = 0, oc = 0, kh = 2, kw = 2;
     int act = 0;
     bool bias_first = true;
-    // A second transposed convolution fed from the first one's output
-    // block on chip (the DB head's pair); w2 null when absent.
-    const float *w2 = nullptr, *b2 = nullptr;
-    int oc2 = 0, kh2 = 2, kw2 = 2, act2 = 0;
-    bool bias_first2 = true;
 };
 
 // Pointwise convolution on the tensor cores (k_tc.cu), 3xTF32: weights

@@ -41,10 +41,14 @@ L2_FLUSH_BYTES = 256 << 20  # larger than the 126 MB L2
 # ncu capture of `bench.py --workload layer`
 # (profiles/pw_tc_kernel_1x1_24to24_992x768.md); writes still dirty in L2 when
 # the kernel ends are not counted there.
-TRAFFIC_PER_LAUNCH = 100.64e6
+TRAFFIC_PER_LAUNCH = 99.67e6
 TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch (profiles/pw_tc_kernel_1x1_24to24_992x768.md)"
 # The same for the dominant kernel's probe (`bench.py --workload conv3x3`).
 CONV_TRAFFIC_PER_LAUNCH = 78.19e6
+# The same for the depthwise probe (`bench.py --workload dw3x3`).
+DW_TRAFFIC_PER_LAUNCH = 109.81e6
+DW_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                     "(profiles/dw_row_kernel_3x3_c24_992x768.md)")
 CONV_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
                        "(profiles/conv_tc_kernel_3x3_96to24_496x384.md)")
 
@@ -512,7 +516,8 @@ def run_ours(args, d: Dist) -> dict | None:
             "roofline_depthwise": {"bound": "hbm", "kernel": dwp["kernel"],
                                    "achieved": dwp["bytes"] / dwp["seconds"] / 1e9, "peak": hbm, "unit": "GB/s",
                                    "frac": dwp["bytes"] / dwp["seconds"] / 1e9 / hbm, "peak_source": hbm_source,
-                                   "traffic": None, "algorithmic_bytes": dwp["bytes"],
+                                   "traffic": DW_TRAFFIC_PER_LAUNCH, "traffic_source": DW_TRAFFIC_SOURCE,
+                                   "algorithmic_bytes": dwp["bytes"],
                                    "seconds_per_launch": dwp["seconds"]},
             "clocks": clocks.summary(),
         }

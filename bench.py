@@ -73,6 +73,7 @@ class Dist:
         self.world = int(os.environ.get("WORLD_SIZE", 1))
         self.local = int(os.environ.get("LOCAL_RANK", 0))
         self.pg = None
+        self.device = "cuda"
 
     def init(self, backend: str):
         if self.world > 1:
@@ -82,6 +83,7 @@ class Dist:
 
             dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
             self.pg = dist
+            self.device = "cuda" if backend == "nccl" else "cpu"
 
     def barrier(self):
         if self.pg:
@@ -92,13 +94,20 @@ class Dist:
             return v
         import torch
 
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        t = torch.tensor([v], dtype=torch.float64, device=self.device)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
     def close(self):
         if self.pg:
             self.pg.destroy_process_group()
+
+    def whole_job(self, units_per_rank: float, local_seconds: float) -> tuple[float, float]:
+        """Units of all ranks per second over the slowest rank's time (every
+        rank processes the same number of its own pages: weak scaling), and
+        that time."""
+        t = self.max(local_seconds)
+        return self.world * units_per_rank / t, t
 
 
 class Clocks:
@@ -408,8 +417,7 @@ def run_ours(args, d: Dist) -> dict | None:
         torch.cuda.synchronize()
     d.barrier()
     local_s = sum(a.elapsed_time(b) for a, b in events) / 1e3
-    total_s = d.max(local_s)
-    value = d.world * args.steps * k / total_s
+    value, total_s = d.whole_job(args.steps * k, local_s)
     if args.profile:
         launches = pipe.launches()
         pipe.close()
@@ -438,8 +446,7 @@ def run_ours(args, d: Dist) -> dict | None:
         _ = float(outs[0][0])
     torch.cuda.synchronize()
     e2e_local = time.perf_counter() - t0
-    e2e_s = d.max(e2e_local)
-    e2e = d.world * args.steps / e2e_s
+    e2e, _ = d.whole_job(args.steps, e2e_local)
     h2d, d2h = pipe.io_bytes()
     launches = pipe.launches()
 

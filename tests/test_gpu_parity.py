@@ -394,6 +394,48 @@ def test_folded_conv_lanes(cuda_mod, oracle_mod):
                       tol=TOL * max(1.0, float(np.abs(want).max())))
 
 
+@pytest.mark.parametrize("k,s,c,oc", [(3, 1, 24, 24), (3, 2, 48, 96), (5, 1, 96, 192), (5, 2, 40, 24)])
+def test_depthwise_pointwise_step_on_tensor_cores(cuda_mod, oracle_mod, k, s, c, oc):
+    """A depthwise layer feeding a 1x1 layer, as one step beside the tensor
+    cores (the row-run depthwise kernel, then the pointwise tensor-core
+    kernel): the same bits as the two layers run as separate steps, and
+    within the tolerance of the oracle; strides 1 and 2, 3x3 and 5x5, channel
+    counts that leave part of a K block, several lanes of different sizes."""
+    rng = np.random.default_rng(k * 100 + s * 10 + c)
+    dw_w = rng.normal(0, 0.3, k * k * c).astype(np.float32)
+    dw_b = rng.normal(0, 0.2, c).astype(np.float32)
+    pw_w = rng.normal(0, 0.2, c * oc).astype(np.float32)
+    pw_b = rng.normal(0, 0.2, oc).astype(np.float32)
+    dw = window(Op("dwconv", x=0, y=1, ic=c, oc=c, fused="hardswish", w=(0, dw_w.size), b=(dw_w.size, c)),
+                (k, k), s, k // 2, k // 2)
+    at = dw_w.size + c
+    pw = window(Op("conv", x=1, y=2, ic=c, oc=oc, fused="swish", w=(at, pw_w.size), b=(at + pw_w.size, oc)),
+                (1, 1), 1, 0, 0)
+    plan = encode((0, 16, 16, c), 3, [2], [dw, pw], np.concatenate([dw_w, dw_b, pw_w, pw_b]))
+    sizes = [(37, 41), (8, 130), (3, 5)]
+    xs = [rng.uniform(-1, 1, h * w * c).astype(np.float32) for h, w in sizes]
+    o = oracle_mod.Oracle(plan)
+    wants = []
+    for (h, w), x in zip(sizes, xs):
+        o.set_size(h, w)
+        wants.append(o.run(x)[0])
+    outs = []
+    for options in (0, cuda_mod.OPT_NO_FUSION):
+        with cuda_mod.Model(plan) as m:
+            if options:
+                m.set_options(options)
+            m.set_sizes(sizes)
+            for i, x in enumerate(xs):
+                m.lane_input_mut(i)[:] = x
+            m.run(60_000)
+            if not options:
+                assert m.steps() == ["dw+pw"]
+            outs.append([m.lane_output(i).copy() for i in range(len(sizes))])
+    for fused, apart, want in zip(outs[0], outs[1], wants):
+        assert np.array_equal(fused, apart), max_gap(fused, apart)
+        assert max_gap(fused, want) <= TOL * max(1.0, float(np.abs(want).max()))
+
+
 def test_detector_unfused_matches_fused(cuda_mod):
     plan = synth.det_plan(seed=5, std=None, size=(320, 256))
     x = synth.stripes(320, 256)

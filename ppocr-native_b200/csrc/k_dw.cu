@@ -108,10 +108,25 @@ __device__ __forceinline__ void dw_store(const float4 (&v)[DW_RUN], float *dst, 
 // the image in kernel row-major order. A block holds `per_block` runs of all
 // c / 4 channel groups, the groups of one run on consecutive threads so that
 // a warp's loads cover whole pixels.
+// Weights: 3x3 stride 1 reads them from shared memory (fewer registers:
+// three blocks per SM), 3x3 stride 2 holds them in registers, 5x5 reads them
+// through L1 (each measured fastest its way).
+template <int K, int S>
+struct DwWeights {
+    static constexpr bool SMEM = K == 3 && S == 1;
+    static constexpr bool HOLD = K == 3 && S == 2;
+    static constexpr int MIN_BLOCKS = SMEM ? 3 : 2;
+};
+
 template <int K, int S, bool QUICK>
-__global__ void __launch_bounds__(256) dw_row_kernel(const DwArgs a, int per_block) {
+__global__ void __launch_bounds__(256, DwWeights<K, S>::MIN_BLOCKS) dw_row_kernel(const DwArgs a, int per_block) {
     constexpr int WC = (DW_RUN - 1) * S + K;  // window columns
-    constexpr bool HOLD = K == 3;              // weights in registers
+    constexpr bool SMEM = DwWeights<K, S>::SMEM, HOLD = DwWeights<K, S>::HOLD;
+    extern __shared__ __align__(16) float dw_ws[];  // SMEM: [K * K][c], the layer's weights
+    if (SMEM) {
+        for (int e = threadIdx.x; e < K * K * a.c; e += blockDim.x) dw_ws[e] = __ldg(a.w + e);
+        __syncthreads();
+    }
     const int cg = a.c >> 2;
     const int slot = threadIdx.x / cg;
     if (slot >= per_block) return;
@@ -150,8 +165,9 @@ __global__ void __launch_bounds__(256) dw_row_kernel(const DwArgs a, int per_blo
                 win[i] = (cols >> i & 1u) ? __ldg(reinterpret_cast<const float4 *>(row + (long)i * a.c)) : zero;
 #pragma unroll
             for (int kx = 0; kx < K; kx++) {
-                const float4 g = HOLD ? wr[HOLD ? ky * K + kx : 0]
-                                      : __ldg(reinterpret_cast<const float4 *>(a.w + (ky * K + kx) * a.c + c));
+                const float4 g = HOLD   ? wr[HOLD ? ky * K + kx : 0]
+                                 : SMEM ? *reinterpret_cast<const float4 *>(dw_ws + (ky * K + kx) * a.c + c)
+                                        : __ldg(reinterpret_cast<const float4 *>(a.w + (ky * K + kx) * a.c + c));
 #pragma unroll
                 for (int j = 0; j < DW_RUN; j++) {
                     if (!(cols >> (j * S + kx) & 1u)) continue;
@@ -211,13 +227,16 @@ void run_dw_rows(const DwArgs &a, cudaStream_t s) {
     const int cg = a.c / 4;
     const int per_block = 256 / cg;
     long blocks = (a.runs + per_block - 1) / per_block;
-    const long wave = long(g_sms) * g_row_resident[K == 5][S == 2][a.quick ? 1 : 0];
+    const size_t smem = DwWeights<K, S>::SMEM ? sizeof(float) * K * K * a.c : 0;
+    int per_sm = g_row_resident[K == 5][S == 2][a.quick ? 1 : 0];
+    if (long(per_sm) * long(smem + 1024) > 220L * 1024) per_sm = int(220L * 1024 / long(smem + 1024));
+    const long wave = long(g_sms) * (per_sm < 1 ? 1 : per_sm);
     if (blocks > wave) blocks = wave;
     if (blocks < 1) blocks = 1;
     if (a.quick)
-        dw_row_kernel<K, S, true><<<(unsigned)blocks, cg * per_block, 0, s>>>(a, per_block);
+        dw_row_kernel<K, S, true><<<(unsigned)blocks, cg * per_block, smem, s>>>(a, per_block);
     else
-        dw_row_kernel<K, S, false><<<(unsigned)blocks, cg * per_block, 0, s>>>(a, per_block);
+        dw_row_kernel<K, S, false><<<(unsigned)blocks, cg * per_block, smem, s>>>(a, per_block);
 }
 
 constexpr int BK = 8;
@@ -365,7 +384,7 @@ int run_dw_pw(const DwPwArgs &a, cudaStream_t s) {
 
 int launch_dw(const DwArgs &a, cudaStream_t s) {
     // square 3x3 and 5x5 kernels of stride 1 or 2 over whole float4s: row runs
-    if (a.c % 4 == 0 && a.c <= 1024 && a.runs > 0 && a.kh == a.kw && a.sh == a.sw && (a.kh == 3 || a.kh == 5) &&
+    if (a.c % 4 == 0 && a.c <= 1024 && size_t(a.kh) * a.kw * a.c * 4 <= 48 * 1024 && a.runs > 0 && a.kh == a.kw && a.sh == a.sw && (a.kh == 3 || a.kh == 5) &&
         (a.sh == 1 || a.sh == 2)) {
         if (a.kh == 3)
             a.sh == 1 ? run_dw_rows<3, 1>(a, s) : run_dw_rows<3, 2>(a, s);

@@ -46,7 +46,7 @@ TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch (
 # The same for the dominant kernel's probe (`bench.py --workload conv3x3`).
 CONV_TRAFFIC_PER_LAUNCH = 78.19e6
 # The same for the depthwise probe (`bench.py --workload dw3x3`).
-DW_TRAFFIC_PER_LAUNCH = 109.81e6
+DW_TRAFFIC_PER_LAUNCH = 107.59e6
 DW_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
                      "(profiles/dw_row_kernel_3x3_c24_992x768.md)")
 CONV_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "

@@ -112,16 +112,8 @@ __host__ __device__ constexpr uint32_t tf32_idesc(int n) {
     return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(TM >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n"
-        :
-        : "r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-
-// The same with A in tensor memory (lanes = rows, one tf32 per column).
+// One MMA with A in tensor memory (lanes = rows, one tf32 per column) and B
+// in shared memory; acc 0 overwrites D.
 __device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
                                             uint32_t acc) {
     asm volatile(

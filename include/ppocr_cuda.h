@@ -131,6 +131,19 @@ const char *ppocr_model_step_name(const ppocr_model *model, size_t i);
 int ppocr_ctc_argmax_noalloc(const float *x, const float *w, const float *b, float *y, size_t pixels,
                              size_t ci, size_t vocab, void *stream);
 
+/* The detector's input on the GPU (replaces the CPU preparation of the page
+ * before the detector runs: det_input_hwc, reference src/det.rs:230-292,
+ * with resize_linear_rows, src/image.rs:91-142): `image` (device memory,
+ * width x height RGB bytes, rows of width * 3) resized to out_width x
+ * out_height by OpenCV's INTER_LINEAR in the reference's integer staging,
+ * scaled to [0, 1] and normalized per channel ((x - mean[c]) / std[c] in
+ * f64, rounded once to f32), written to `out` (device memory, out_height x
+ * out_width x 3 floats: the detector's input layout) on `stream` (NULL: the
+ * default stream). The same bytes and bits as the reference's CPU path.
+ * Sizes from 1 to 2^20; allocates nothing. */
+int ppocr_det_input_hwc(const uint8_t *image, size_t width, size_t height, size_t out_width, size_t out_height,
+                        const double *mean, const double *std, float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

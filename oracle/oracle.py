@@ -52,6 +52,9 @@ def lib() -> ctypes.CDLL:
         L.orc_exp_neg.argtypes = [ctypes.c_float]
         L.orc_activation.restype = ctypes.c_float
         L.orc_activation.argtypes = [ctypes.c_int, ctypes.c_float]
+        L.orc_det_input_hwc.restype = ctypes.c_int
+        L.orc_det_input_hwc.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                                        ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         _lib = L
     return _lib
 
@@ -104,6 +107,19 @@ def exp_neg(z: float) -> float:
 
 def activation(code: int, x: float) -> float:
     return lib().orc_activation(code, x)
+
+
+def det_input_hwc(image: np.ndarray, ow: int, oh: int, mean, std) -> np.ndarray:
+    """The detector input of an (ih, iw, 3) uint8 image at ow x oh,
+    (oh, ow, 3) float32 (orc_det_input_hwc)."""
+    image = np.ascontiguousarray(image, dtype=np.uint8)
+    ih, iw, _ = image.shape
+    out = np.empty((oh, ow, 3), np.float32)
+    m = np.asarray(mean, np.float64)
+    s = np.asarray(std, np.float64)
+    if lib().orc_det_input_hwc(image.ctypes.data, iw, ih, ow, oh, m.ctypes.data, s.ctypes.data, out.ctypes.data):
+        raise OracleError("empty size")
+    return out
 
 
 def threads_available() -> int:

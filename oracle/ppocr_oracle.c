@@ -791,3 +791,55 @@ done:
     free(buf);
     return rc;
 }
+
+/* ------------------------------------------------------------ det input */
+
+/* One output coordinate of the bilinear resize (image.rs:34-63): output d
+ * sits at source (d + 0.5) * src / dst - 0.5, computed in f64 and rounded to
+ * f32; its two source indices are clamped to the edge, and each weight is
+ * rounded to 1/2048 on its own (ties to even). */
+typedef struct {
+    size_t near, far;
+    int near_w, far_w;
+} orc_tap;
+
+static orc_tap orc_resize_tap(size_t src, size_t dst, size_t d) {
+    const double scale = 1.0 / ((double)dst / (double)src);
+    const float f = (float)(((double)d + 0.5) * scale - 0.5);
+    const float fl = floorf(f);
+    const float a = f - fl;
+    const long s = (long)fl, last = (long)src - 1;
+    orc_tap t;
+    t.near = (size_t)(s < 0 ? 0 : s > last ? last : s);
+    t.far = (size_t)(s + 1 < 0 ? 0 : s + 1 > last ? last : s + 1);
+    t.near_w = (int)rintf((1.0f - a) * 2048.0f);
+    t.far_w = (int)rintf(a * 2048.0f);
+    return t;
+}
+
+/* reference det.rs:230-292, image.rs:91-142: the horizontal pass keeps the
+ * 1/2048 products, the vertical pass drops four bits of each row before
+ * weighting and sixteen after, then rounds the sum of the two; the byte then
+ * goes through ((f64)(byte * (f32)(1/255)) - mean) / std, rounded to f32. */
+int orc_det_input_hwc(const unsigned char *image, size_t iw, size_t ih, size_t ow, size_t oh, const double *mean,
+                      const double *std, float *out) {
+    if (!iw || !ih || !ow || !oh) return 1;
+    const float scale = (float)(1.0 / 255.0);
+    for (size_t oy = 0; oy < oh; oy++) {
+        const orc_tap ty = orc_resize_tap(ih, oh, oy);
+        for (size_t ox = 0; ox < ow; ox++) {
+            const orc_tap tx = orc_resize_tap(iw, ow, ox);
+            for (int c = 0; c < 3; c++) {
+                const unsigned char *r0 = image + ty.near * iw * 3, *r1 = image + ty.far * iw * 3;
+                const int a = (int)r0[tx.near * 3 + c] * tx.near_w + (int)r0[tx.far * 3 + c] * tx.far_w;
+                const int b = (int)r1[tx.near * 3 + c] * tx.near_w + (int)r1[tx.far * 3 + c] * tx.far_w;
+                const int v = (((a >> 4) * ty.near_w) >> 16) + (((b >> 4) * ty.far_w) >> 16);
+                int byte = (v + 2) >> 2;
+                byte = byte < 0 ? 0 : byte > 255 ? 255 : byte;
+                const float x = (float)byte * scale;
+                out[(oy * ow + ox) * 3 + c] = (float)(((double)x - mean[c]) / std[c]);
+            }
+        }
+    }
+    return 0;
+}

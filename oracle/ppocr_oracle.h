@@ -43,6 +43,14 @@ int orc_run(orc_plan *p, const float *input, float *const *outputs, int threads)
 /* Scalar definitions, exposed for the f64 checks. */
 float orc_exp_neg(float z);
 float orc_activation(int code, float x);
+/* The detector's input from an 8-bit RGB image (iw x ih, pixels by rows,
+ * channels together): resized to ow x oh by OpenCV's INTER_LINEAR in the
+ * reference's integer staging, scaled to [0, 1] in f32 and normalized per
+ * channel in f64, rounded once to f32, written channels together
+ * (reference det.rs:230-292 det_input_hwc, image.rs:46-142). Returns 0, or
+ * 1 for an empty size. */
+int orc_det_input_hwc(const unsigned char *image, size_t iw, size_t ih, size_t ow, size_t oh, const double *mean,
+                      const double *std, float *out);
 
 #ifdef __cplusplus
 }

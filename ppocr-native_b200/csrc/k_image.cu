@@ -1,0 +1,107 @@
+// The detector's input on the GPU: an 8-bit RGB page image resized to the
+// detector's size and normalized, written channels together as the model
+// reads its input (reference det.rs:230-292 det_input_hwc, the resize of
+// image.rs:46-142, which reproduces OpenCV's INTER_LINEAR).
+//
+// One thread per output pixel. Its two taps along each axis are computed
+// the reference's way with correctly rounded IEEE operations (the source
+// coordinate (d + 0.5) * src / dst - 0.5 in f64, rounded to f32, each weight
+// rounded to 1/2048 on its own, ties to even), the four source pixels are
+// blended with the reference's integer staging (the horizontal products
+// kept at 1/2048, four bits of each row dropped before the vertical weight
+// and sixteen after, the sum of the two rounded), and each byte becomes
+// ((f64)(byte * (f32)(1/255)) - mean) / std rounded once to f32: the same
+// bytes and bits as the CPU path.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "../../include/ppocr_cuda.h"
+#include "kernels.hpp"
+
+namespace ppocr {
+void set_last_error(const std::string &msg);
+}
+
+namespace {
+
+struct ImageArgs {
+    const uint8_t *image;
+    float *out;
+    int iw, ih, ow, oh;
+    double mean[3], std[3];
+};
+
+struct Tap {
+    int near, far, near_w, far_w;
+};
+
+__device__ __forceinline__ Tap resize_tap(int src, int dst, int d) {
+    const double scale = __ddiv_rn(1.0, __ddiv_rn(double(dst), double(src)));
+    const float f = __double2float_rn(__dadd_rn(__dmul_rn(__dadd_rn(double(d), 0.5), scale), -0.5));
+    const float fl = floorf(f);
+    const float a = __fsub_rn(f, fl);
+    const int s = int(fl), last = src - 1;
+    Tap t;
+    t.near = s < 0 ? 0 : s > last ? last : s;
+    t.far = s + 1 < 0 ? 0 : s + 1 > last ? last : s + 1;
+    t.near_w = __float2int_rn(__fmul_rn(__fsub_rn(1.0f, a), 2048.0f));
+    t.far_w = __float2int_rn(__fmul_rn(a, 2048.0f));
+    return t;
+}
+
+__global__ void __launch_bounds__(256) det_input_kernel(const ImageArgs a) {
+    const long total = long(a.ow) * a.oh;
+    const float scale = __double2float_rn(__ddiv_rn(1.0, 255.0));
+    for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += long(gridDim.x) * blockDim.x) {
+        const int oy = int(i / a.ow), ox = int(i - long(oy) * a.ow);
+        const Tap ty = resize_tap(a.ih, a.oh, oy), tx = resize_tap(a.iw, a.ow, ox);
+        const uint8_t *r0 = a.image + long(ty.near) * a.iw * 3, *r1 = a.image + long(ty.far) * a.iw * 3;
+        float *o = a.out + i * 3;
+#pragma unroll
+        for (int c = 0; c < 3; c++) {
+            const int p = int(r0[tx.near * 3 + c]) * tx.near_w + int(r0[tx.far * 3 + c]) * tx.far_w;
+            const int q = int(r1[tx.near * 3 + c]) * tx.near_w + int(r1[tx.far * 3 + c]) * tx.far_w;
+            const int v = (((p >> 4) * ty.near_w) >> 16) + (((q >> 4) * ty.far_w) >> 16);
+            int byte = (v + 2) >> 2;
+            byte = byte < 0 ? 0 : byte > 255 ? 255 : byte;
+            const float x = __fmul_rn(float(byte), scale);
+            o[c] = __double2float_rn(__ddiv_rn(__dsub_rn(double(x), a.mean[c]), a.std[c]));
+        }
+    }
+}
+
+}  // namespace
+
+extern "C" int ppocr_det_input_hwc(const uint8_t *image, size_t width, size_t height, size_t out_width,
+                                   size_t out_height, const double *mean, const double *std, float *out,
+                                   void *stream) {
+    if (!image || !out || !mean || !std) {
+        ppocr::set_last_error("ppocr_det_input_hwc: null pointer");
+        return PPOCR_E_ARG;
+    }
+    if (!width || !height || !out_width || !out_height || width > (1u << 20) || height > (1u << 20) ||
+        out_width > (1u << 20) || out_height > (1u << 20)) {
+        ppocr::set_last_error("ppocr_det_input_hwc: sizes must be between 1 and 2^20");
+        return PPOCR_E_SIZE;
+    }
+    ImageArgs a;
+    a.image = image;
+    a.out = out;
+    a.iw = int(width); a.ih = int(height); a.ow = int(out_width); a.oh = int(out_height);
+    for (int c = 0; c < 3; c++) {
+        a.mean[c] = mean[c];
+        a.std[c] = std[c];
+    }
+    const long total = long(out_width) * long(out_height);
+    long blocks = (total + 255) / 256;
+    if (blocks > 148L * 16) blocks = 148L * 16;
+    det_input_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        ppocr::set_last_error(std::string("ppocr_det_input_hwc: ") + cudaGetErrorString(e));
+        return PPOCR_E_DEVICE;
+    }
+    return PPOCR_OK;
+}

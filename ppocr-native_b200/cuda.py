@@ -57,6 +57,9 @@ _SIG = {
     "ppocr_ctc_argmax_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                                 ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
                                                 ctypes.c_size_t, ctypes.c_void_p]),
+    "ppocr_det_input_hwc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                                           ctypes.c_size_t, ctypes.POINTER(ctypes.c_double),
+                                           ctypes.POINTER(ctypes.c_double), ctypes.c_void_p, ctypes.c_void_p]),
 }
 
 _lib = None
@@ -227,3 +230,13 @@ def ctc_argmax_noalloc(x: int, w: int, b: int, y: int, pixels: int, ci: int, voc
     `ppocr_ctc_argmax_noalloc` in include/ppocr_cuda.h for the scratch limit
     and the sharing rules."""
     _check(lib().ppocr_ctc_argmax_noalloc(x, w, b, y, pixels, ci, vocab, stream or None))
+
+
+def det_input_hwc(image: int, width: int, height: int, out_width: int, out_height: int, mean, std, out: int,
+                  stream: int | None = None) -> None:
+    """The detector's input from an RGB byte image, on the GPU (device
+    pointers as ints): resized to out_width x out_height and normalized,
+    channels together; see `ppocr_det_input_hwc` in include/ppocr_cuda.h."""
+    m = (ctypes.c_double * 3)(*[float(v) for v in mean])
+    s = (ctypes.c_double * 3)(*[float(v) for v in std])
+    _check(lib().ppocr_det_input_hwc(image, width, height, out_width, out_height, m, s, out, stream or None))

@@ -144,6 +144,19 @@ int ppocr_ctc_argmax_noalloc(const float *x, const float *w, const float *b, flo
 int ppocr_det_input_hwc(const uint8_t *image, size_t width, size_t height, size_t out_width, size_t out_height,
                         const double *mean, const double *std, float *out, void *stream);
 
+/* The recogniser's input for one line crop on the GPU (replaces rec_input,
+ * reference src/rec.rs:19-43, turned HWC as ocr.rs:534-549 rec_hwc does):
+ * `crop` (device memory, width x height RGB bytes) resized to height 48 at
+ * its aspect ratio (width rounded up, cut to the tensor), scaled to [-1, 1]
+ * in f32 and zero-padded on the right to the tensor width
+ * max(320, trunc(48 * width / height)), written to `out` (device memory,
+ * 48 x tensor_width x 3 floats, `capacity` floats available) on `stream`.
+ * *tensor_width receives the width; with out NULL only the width is
+ * computed. The same bytes and bits as the reference's CPU path. Crop sizes
+ * from 1 to 2^20; allocates nothing. */
+int ppocr_rec_input_hwc(const uint8_t *crop, size_t width, size_t height, float *out, size_t capacity,
+                        size_t *tensor_width, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -52,6 +52,8 @@ def lib() -> ctypes.CDLL:
         L.orc_exp_neg.argtypes = [ctypes.c_float]
         L.orc_activation.restype = ctypes.c_float
         L.orc_activation.argtypes = [ctypes.c_int, ctypes.c_float]
+        L.orc_rec_input_hwc.restype = ctypes.c_size_t
+        L.orc_rec_input_hwc.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p]
         L.orc_det_input_hwc.restype = ctypes.c_int
         L.orc_det_input_hwc.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
                                         ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
@@ -119,6 +121,19 @@ def det_input_hwc(image: np.ndarray, ow: int, oh: int, mean, std) -> np.ndarray:
     s = np.asarray(std, np.float64)
     if lib().orc_det_input_hwc(image.ctypes.data, iw, ih, ow, oh, m.ctypes.data, s.ctypes.data, out.ctypes.data):
         raise OracleError("empty size")
+    return out
+
+
+def rec_input_hwc(crop: np.ndarray) -> np.ndarray:
+    """The recogniser's input of an (h, w, 3) uint8 crop, (48, width, 3)
+    float32 (orc_rec_input_hwc)."""
+    crop = np.ascontiguousarray(crop, dtype=np.uint8)
+    ch, cw, _ = crop.shape
+    width = lib().orc_rec_input_hwc(crop.ctypes.data, cw, ch, None)
+    if not width:
+        raise OracleError("empty crop")
+    out = np.empty((48, width, 3), np.float32)
+    lib().orc_rec_input_hwc(crop.ctypes.data, cw, ch, out.ctypes.data)
     return out
 
 

@@ -843,3 +843,36 @@ int orc_det_input_hwc(const unsigned char *image, size_t iw, size_t ih, size_t o
     }
     return 0;
 }
+
+/* reference rec.rs:19-43: width = trunc(48 * max(320 / 48, w / h)); the
+ * resized width ceil(48 * w / h), cut to the width; (v / 255 - 0.5) / 0.5 in
+ * f32; zeros on the right. */
+size_t orc_rec_input_hwc(const unsigned char *crop, size_t cw, size_t ch, float *out) {
+    if (!cw || !ch) return 0;
+    const double h = (double)ch, w = (double)cw, height = 48.0;
+    const double ratio = 320.0 / height > w / h ? 320.0 / height : w / h;
+    const size_t width = (size_t)(height * ratio);
+    const double fitted = ceil(height * (w / h));
+    const size_t rw = fitted > (double)width ? width : (size_t)fitted;
+    if (!out) return width;
+    for (size_t oy = 0; oy < 48; oy++) {
+        const orc_tap ty = orc_resize_tap(ch, 48, oy);
+        for (size_t ox = 0; ox < width; ox++) {
+            for (int c = 0; c < 3; c++) {
+                float val = 0.0f;
+                if (ox < rw) {
+                    const orc_tap tx = orc_resize_tap(cw, rw, ox);
+                    const unsigned char *r0 = crop + ty.near * cw * 3, *r1 = crop + ty.far * cw * 3;
+                    const int a = (int)r0[tx.near * 3 + c] * tx.near_w + (int)r0[tx.far * 3 + c] * tx.far_w;
+                    const int b = (int)r1[tx.near * 3 + c] * tx.near_w + (int)r1[tx.far * 3 + c] * tx.far_w;
+                    const int v = (((a >> 4) * ty.near_w) >> 16) + (((b >> 4) * ty.far_w) >> 16);
+                    int byte = (v + 2) >> 2;
+                    byte = byte < 0 ? 0 : byte > 255 ? 255 : byte;
+                    val = ((float)byte / 255.0f - 0.5f) / 0.5f;
+                }
+                out[(oy * width + ox) * 3 + c] = val;
+            }
+        }
+    }
+    return width;
+}

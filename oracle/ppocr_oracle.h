@@ -51,6 +51,13 @@ float orc_activation(int code, float x);
  * 1 for an empty size. */
 int orc_det_input_hwc(const unsigned char *image, size_t iw, size_t ih, size_t ow, size_t oh, const double *mean,
                       const double *std, float *out);
+/* The recogniser's input for one crop (cw x ch RGB bytes): its tensor width
+ * (at least 320, the crop's aspect at height 48), and, when out is not null,
+ * the crop resized to height 48 (width rounded up, cut to the tensor),
+ * scaled to [-1, 1] in f32 and zero-padded on the right, channels together
+ * (reference rec.rs:19-43 rec_input, ocr.rs:534-549 rec_hwc). Returns the
+ * width, 0 for an empty crop. */
+size_t orc_rec_input_hwc(const unsigned char *crop, size_t cw, size_t ch, float *out);
 
 #ifdef __cplusplus
 }

@@ -57,6 +57,8 @@ _SIG = {
     "ppocr_ctc_argmax_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                                 ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
                                                 ctypes.c_size_t, ctypes.c_void_p]),
+    "ppocr_rec_input_hwc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
+                                           ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t), ctypes.c_void_p]),
     "ppocr_det_input_hwc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
                                            ctypes.c_size_t, ctypes.POINTER(ctypes.c_double),
                                            ctypes.POINTER(ctypes.c_double), ctypes.c_void_p, ctypes.c_void_p]),
@@ -240,3 +242,20 @@ def det_input_hwc(image: int, width: int, height: int, out_width: int, out_heigh
     m = (ctypes.c_double * 3)(*[float(v) for v in mean])
     s = (ctypes.c_double * 3)(*[float(v) for v in std])
     _check(lib().ppocr_det_input_hwc(image, width, height, out_width, out_height, m, s, out, stream or None))
+
+
+def rec_input_width(width: int, height: int) -> int:
+    """The recogniser tensor width of a width x height crop."""
+    w = ctypes.c_size_t()
+    _check(lib().ppocr_rec_input_hwc(None, width, height, None, 0, ctypes.byref(w), None))
+    return w.value
+
+
+def rec_input_hwc(crop: int, width: int, height: int, out: int, capacity: int, stream: int | None = None) -> int:
+    """The recogniser's input of one RGB byte crop, on the GPU (device
+    pointers as ints): 48 x tensor width x 3 floats into out (capacity
+    floats); returns the tensor width. See `ppocr_rec_input_hwc` in
+    include/ppocr_cuda.h."""
+    w = ctypes.c_size_t()
+    _check(lib().ppocr_rec_input_hwc(crop, width, height, out, capacity, ctypes.byref(w), stream or None))
+    return w.value

@@ -1,8 +1,9 @@
-"""The detector's input preparation (reference src/det.rs:230-292
-det_input_hwc with the INTER_LINEAR resize of src/image.rs:46-142): the
-oracle against an independent numpy restatement and the reference test's
-property (identity and constant images), on the CPU; the GPU entry point
-`ppocr_det_input_hwc` against the oracle, bit for bit."""
+"""The detector's and the recogniser's input preparation (reference
+src/det.rs:230-292 det_input_hwc and src/rec.rs:19-43 rec_input, both over
+the INTER_LINEAR resize of src/image.rs:46-142): the oracle against an
+independent numpy restatement and identity / constant images, on the CPU;
+the GPU entry points `ppocr_det_input_hwc` and `ppocr_rec_input_hwc` against
+the oracle, bit for bit."""
 
 from __future__ import annotations
 
@@ -94,6 +95,64 @@ def test_gpu_det_input_matches_oracle(cuda_mod, oracle_mod, src, dst):
     try:
         assert rt.cudaMemcpy(din, image.ctypes.data, image.nbytes, 1) == 0
         cuda_mod.det_input_hwc(din.value, src[1], src[0], dst[1], dst[0], MEAN, STD, dout.value)
+        got = np.empty_like(want)
+        assert rt.cudaMemcpy(got.ctypes.data, dout, got.nbytes, 2) == 0
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), float(np.abs(got - want).max())
+    finally:
+        rt.cudaFree(din)
+        rt.cudaFree(dout)
+
+
+# ------------------------------------------------------- recogniser input
+
+def rec_input_numpy(crop: np.ndarray) -> np.ndarray:
+    """reference rec.rs:19-43 (HWC as ocr.rs:534-549 turns it)."""
+    ch, cw, _ = crop.shape
+    h, w, rows = float(ch), float(cw), 48.0
+    width = int(rows * max(320.0 / rows, w / h))
+    fitted = np.ceil(rows * (w / h))
+    rw = width if fitted > width else int(fitted)
+    xn, xf, xnw, xfw = taps(cw, rw)
+    yn, yf, ynw, yfw = taps(ch, 48)
+    img = crop.astype(np.int32)
+    horiz = img[:, xn, :] * xnw[None, :, None] + img[:, xf, :] * xfw[None, :, None]
+    a, b = horiz[yn], horiz[yf]
+    v = (((a >> 4) * ynw[:, None, None]) >> 16) + (((b >> 4) * yfw[:, None, None]) >> 16)
+    byte = np.clip((v + 2) >> 2, 0, 255).astype(np.float32)
+    out = np.zeros((48, width, 3), np.float32)
+    out[:, :rw] = (byte / np.float32(255.0) - np.float32(0.5)) / np.float32(0.5)
+    return out
+
+
+CROPS = [(30, 200), (48, 48), (17, 1500), (60, 33), (1, 1), (9, 61), (100, 2000)]
+
+
+@pytest.mark.parametrize("crop", CROPS)
+def test_oracle_rec_input_matches_numpy_restatement(oracle_mod, crop):
+    rng = np.random.default_rng(crop[0] * 13 + crop[1])
+    image = rng.integers(0, 256, (*crop, 3), dtype=np.uint8)
+    got = oracle_mod.rec_input_hwc(image)
+    want = rec_input_numpy(image)
+    assert got.shape == want.shape
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("crop", CROPS)
+def test_gpu_rec_input_matches_oracle(cuda_mod, oracle_mod, crop):
+    rng = np.random.default_rng(crop[1] * 5 + crop[0])
+    image = rng.integers(0, 256, (*crop, 3), dtype=np.uint8)
+    want = oracle_mod.rec_input_hwc(image)
+    width = cuda_mod.rec_input_width(crop[1], crop[0])
+    assert width == want.shape[1]
+    rt = _cudart()
+    din, dout = ctypes.c_void_p(), ctypes.c_void_p()
+    assert rt.cudaMalloc(ctypes.byref(din), image.nbytes) == 0
+    assert rt.cudaMalloc(ctypes.byref(dout), want.nbytes) == 0
+    try:
+        assert rt.cudaMemcpy(din, image.ctypes.data, image.nbytes, 1) == 0
+        got_w = cuda_mod.rec_input_hwc(din.value, crop[1], crop[0], dout.value, want.size)
+        assert got_w == width
         got = np.empty_like(want)
         assert rt.cudaMemcpy(got.ctypes.data, dout, got.nbytes, 2) == 0
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), float(np.abs(got - want).max())

@@ -157,6 +157,12 @@ int ppocr_det_input_hwc(const uint8_t *image, size_t width, size_t height, size_
 int ppocr_rec_input_hwc(const uint8_t *crop, size_t width, size_t height, float *out, size_t capacity,
                         size_t *tensor_width, void *stream);
 
+/* The DB postprocess's text mask on the GPU (the first line of
+ * boxes_from_prob, reference src/det.rs:438): mask[i] = prob[i] > thresh,
+ * compared in f32, for `pixels` values of the detector's probability map
+ * (device memory in and out) on `stream`. Allocates nothing. */
+int ppocr_db_mask(const float *prob, size_t pixels, float thresh, uint8_t *mask, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

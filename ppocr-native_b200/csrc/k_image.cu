@@ -106,7 +106,31 @@ __global__ void __launch_bounds__(256) rec_input_kernel(const RecArgs a) {
     }
 }
 
+// The DB threshold: mask = prob > thresh, compared in f32 (reference
+// det.rs:438), a grid-stride loop over the pixels.
+__global__ void __launch_bounds__(256) db_mask_kernel(const float *prob, long n, float thresh, uint8_t *mask) {
+    for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += long(gridDim.x) * blockDim.x)
+        mask[i] = prob[i] > thresh ? 1 : 0;
+}
+
 }  // namespace
+
+extern "C" int ppocr_db_mask(const float *prob, size_t pixels, float thresh, uint8_t *mask, void *stream) {
+    if (!prob || !mask) {
+        ppocr::set_last_error("ppocr_db_mask: null pointer");
+        return PPOCR_E_ARG;
+    }
+    if (!pixels) return PPOCR_OK;
+    long blocks = long((pixels + 255) / 256);
+    if (blocks > 148L * 16) blocks = 148L * 16;
+    db_mask_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(prob, long(pixels), thresh, mask);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        ppocr::set_last_error(std::string("ppocr_db_mask: ") + cudaGetErrorString(e));
+        return PPOCR_E_DEVICE;
+    }
+    return PPOCR_OK;
+}
 
 extern "C" int ppocr_rec_input_hwc(const uint8_t *crop, size_t width, size_t height, float *out, size_t capacity,
                                    size_t *tensor_width, void *stream) {

@@ -59,6 +59,8 @@ _SIG = {
                                                 ctypes.c_size_t, ctypes.c_void_p]),
     "ppocr_rec_input_hwc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
                                            ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t), ctypes.c_void_p]),
+    "ppocr_db_mask": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_float, ctypes.c_void_p,
+                                     ctypes.c_void_p]),
     "ppocr_det_input_hwc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
                                            ctypes.c_size_t, ctypes.POINTER(ctypes.c_double),
                                            ctypes.POINTER(ctypes.c_double), ctypes.c_void_p, ctypes.c_void_p]),
@@ -259,3 +261,9 @@ def rec_input_hwc(crop: int, width: int, height: int, out: int, capacity: int, s
     w = ctypes.c_size_t()
     _check(lib().ppocr_rec_input_hwc(crop, width, height, out, capacity, ctypes.byref(w), stream or None))
     return w.value
+
+
+def db_mask(prob: int, pixels: int, thresh: float, mask: int, stream: int | None = None) -> None:
+    """The DB text mask prob > thresh (device pointers as ints); see
+    `ppocr_db_mask` in include/ppocr_cuda.h."""
+    _check(lib().ppocr_db_mask(prob, pixels, thresh, mask, stream or None))

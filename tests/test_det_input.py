@@ -159,3 +159,29 @@ def test_gpu_rec_input_matches_oracle(cuda_mod, oracle_mod, crop):
     finally:
         rt.cudaFree(din)
         rt.cudaFree(dout)
+
+
+# ------------------------------------------------------------- DB mask
+
+@pytest.mark.gpu
+def test_gpu_db_mask_matches_f32_comparison(cuda_mod):
+    """mask = prob > thresh in f32 (det.rs:438), values at and around the
+    threshold included."""
+    rng = np.random.default_rng(11)
+    thresh = np.float32(0.3)
+    prob = rng.random(1984 * 1536 + 7).astype(np.float32)
+    prob[:5] = [thresh, np.nextafter(thresh, np.float32(1)), np.nextafter(thresh, np.float32(0)), 0.0, 1.0]
+    want = (prob > thresh).astype(np.uint8)
+    rt = _cudart()
+    dp, dm = ctypes.c_void_p(), ctypes.c_void_p()
+    assert rt.cudaMalloc(ctypes.byref(dp), prob.nbytes) == 0
+    assert rt.cudaMalloc(ctypes.byref(dm), want.nbytes) == 0
+    try:
+        assert rt.cudaMemcpy(dp, prob.ctypes.data, prob.nbytes, 1) == 0
+        cuda_mod.db_mask(dp.value, prob.size, float(thresh), dm.value)
+        got = np.empty_like(want)
+        assert rt.cudaMemcpy(got.ctypes.data, dm, got.nbytes, 2) == 0
+        assert np.array_equal(got, want)
+    finally:
+        rt.cudaFree(dp)
+        rt.cudaFree(dm)

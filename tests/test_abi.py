@@ -68,3 +68,28 @@ def test_det_and_rec_plans_parse(tmp_path):
             cuda.Model(p, device=99)
         assert e.value.code == cuda.E_DEVICE
     assert np.isfinite(describe(synth.det_plan())["weights"]).all()
+
+
+def test_input_preparation_arguments_checked_before_any_device():
+    """The GPU input-preparation entry points refuse null pointers and empty
+    or oversized images with their codes before touching a device, and the
+    recogniser's tensor width follows rec.rs:20-31 (no device needed)."""
+    with pytest.raises(cuda.PpocrError) as e:
+        cuda.det_input_hwc(0, 10, 10, 8, 8, [0, 0, 0], [1, 1, 1], 0)
+    assert e.value.code == cuda.E_ARG
+    with pytest.raises(cuda.PpocrError) as e:
+        cuda.det_input_hwc(16, 0, 10, 8, 8, [0, 0, 0], [1, 1, 1], 16)
+    assert e.value.code == cuda.E_SIZE
+    with pytest.raises(cuda.PpocrError) as e:
+        cuda.db_mask(0, 10, 0.3, 16)
+    assert e.value.code == cuda.E_ARG
+    with pytest.raises(cuda.PpocrError) as e:
+        cuda.rec_input_width(0, 48)
+    assert e.value.code == cuda.E_SIZE
+    # the tensor width: at least 320, else trunc(48 * w / h)
+    assert cuda.rec_input_width(100, 48) == 320
+    assert cuda.rec_input_width(1500, 17) == int(48 * (1500 / 17))
+    assert cuda.rec_input_width(2000, 100) == 960
+    with pytest.raises(cuda.PpocrError) as e:  # out too small for 48 x 320 x 3
+        cuda.rec_input_hwc(16, 100, 48, 16, 10)
+    assert e.value.code == cuda.E_SIZE

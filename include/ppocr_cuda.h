@@ -121,12 +121,16 @@ const char *ppocr_model_step_name(const ppocr_model *model, size_t i);
  * synchronize the device. No counterpart in the reference (its engine always
  * allocates per model). x: [pixels][ci] time steps; w: ceil(vocab/16) panels
  * of [ci][16]; b: 16 * ceil(vocab/16) biases (-1e30 past vocab); y:
- * [pixels][2] = (best class as float, 1 / sum of exp). Enqueued on `stream`
- * (a cudaStream_t; NULL is the default stream) on the current device.
+ * [pixels][2] = (best class as float, 1 / sum of exp). w must be 16-byte
+ * aligned (its panels are read as 16-byte vectors), x, b and y 4-byte
+ * aligned; a misaligned pointer returns PPOCR_E_ARG before any launch.
+ * Enqueued on `stream` (a cudaStream_t; NULL is the default stream) on the
+ * current device.
  * Allocates nothing: its scratch is a fixed 4 MiB array in the library's
  * device memory (3 floats per time step per 128 classes, 1 Mi floats in
  * all); larger calls return PPOCR_E_SIZE. The first call on a device looks
- * the array up, so make it before any stream capture. All calls on a device
+ * the array up and raises the kernels' shared-memory limits on that device
+ * (no model needs to exist), so make it before any stream capture. All calls on a device
  * share the array: calls that overlap on the GPU race. */
 int ppocr_ctc_argmax_noalloc(const float *x, const float *w, const float *b, float *y, size_t pixels,
                              size_t ci, size_t vocab, void *stream);
@@ -138,11 +142,12 @@ int ppocr_ctc_argmax_noalloc(const float *x, const float *w, const float *b, flo
  * out_height by OpenCV's INTER_LINEAR in the reference's integer staging,
  * scaled to [0, 1] and normalized per channel ((x - mean[c]) / std[c] in
  * f64, rounded once to f32), written to `out` (device memory, out_height x
- * out_width x 3 floats: the detector's input layout) on `stream` (NULL: the
- * default stream). The same bytes and bits as the reference's CPU path.
- * Sizes from 1 to 2^20; allocates nothing. */
+ * out_width x 3 floats: the detector's input layout; `capacity` floats
+ * available, PPOCR_E_SIZE when fewer) on `stream` (NULL: the default
+ * stream). The same bytes and bits as the reference's CPU path. Sizes from
+ * 1 to 2^20; allocates nothing. */
 int ppocr_det_input_hwc(const uint8_t *image, size_t width, size_t height, size_t out_width, size_t out_height,
-                        const double *mean, const double *std, float *out, void *stream);
+                        const double *mean, const double *std, float *out, size_t capacity, void *stream);
 
 /* The recogniser's input for one line crop on the GPU (replaces rec_input,
  * reference src/rec.rs:19-43, turned HWC as ocr.rs:534-549 rec_hwc does):

@@ -21,7 +21,7 @@ LIB = HERE / "libppocr_oracle.so"
 
 def build(force: bool = False) -> Path:
     """Compile the oracle (gcc, -O3 -mavx2 -mfma -fopenmp -ffp-contract=off)."""
-    src = [HERE / "ppocr_oracle.c", HERE / "ppocr_oracle.h", HERE / "Makefile"]
+    src = [HERE / "ppocr_oracle.c", HERE / "page_oracle.c", HERE / "ppocr_oracle.h", HERE / "Makefile"]
     if force or not LIB.exists() or any(s.stat().st_mtime > LIB.stat().st_mtime for s in src):
         subprocess.run(["make", "-s", "-C", str(HERE), "libppocr_oracle.so"], check=True)
     return LIB
@@ -139,3 +139,203 @@ def rec_input_hwc(crop: np.ndarray) -> np.ndarray:
 
 def threads_available() -> int:
     return len(os.sched_getaffinity(0))
+
+
+# ------------------------------------------------------------ page steps
+
+def _page_lib() -> ctypes.CDLL:
+    L = lib()
+    if getattr(L, "_page_ready", False):
+        return L
+    c_sz, c_vp = ctypes.c_size_t, ctypes.c_void_p
+    L.orc_resize_linear.restype = ctypes.c_int
+    L.orc_resize_linear.argtypes = [c_vp, c_sz, c_sz, c_sz, c_sz, c_vp]
+    L.orc_rotate_ccw.argtypes = [c_vp, c_sz, c_sz, c_vp]
+    L.orc_det_size.restype = ctypes.c_int
+    L.orc_det_size.argtypes = [c_sz, c_sz, c_sz, ctypes.POINTER(c_sz), ctypes.POINTER(c_sz)]
+    L.orc_prepare_page.restype = ctypes.c_int
+    L.orc_prepare_page.argtypes = [c_sz, c_sz, c_sz, c_sz, ctypes.c_double, c_sz, ctypes.POINTER(c_sz),
+                                   ctypes.POINTER(c_sz), ctypes.POINTER(ctypes.c_double),
+                                   ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_sz)]
+    L.orc_find_contours.restype = c_vp
+    L.orc_find_contours.argtypes = [c_vp, c_sz, c_sz]
+    L.orc_contours_count.restype = c_sz
+    L.orc_contours_count.argtypes = [c_vp]
+    L.orc_contour.restype = ctypes.POINTER(ctypes.c_int32)
+    L.orc_contour.argtypes = [c_vp, c_sz, ctypes.POINTER(c_sz)]
+    L.orc_contours_free.argtypes = [c_vp]
+    L.orc_contour_mean.restype = ctypes.c_double
+    L.orc_contour_mean.argtypes = [c_vp, c_sz, c_sz, c_vp, c_sz]
+    L.orc_min_area_rect.argtypes = [c_vp, c_sz, c_vp]
+    L.orc_box_points.argtypes = [c_vp, c_vp]
+    L.orc_mini_box.restype = ctypes.c_float
+    L.orc_mini_box.argtypes = [c_vp, c_sz, c_vp]
+    L.orc_unclip.restype = ctypes.c_long
+    L.orc_unclip.argtypes = [c_vp, ctypes.c_double, c_vp, c_sz]
+    L.orc_boxes_from_prob.restype = c_sz
+    L.orc_boxes_from_prob.argtypes = [c_vp, c_sz, c_sz, c_sz, c_sz, ctypes.c_float, ctypes.c_double,
+                                      ctypes.c_double, c_sz, c_vp, c_sz]
+    L.orc_crop_size.argtypes = [c_vp, ctypes.POINTER(c_sz), ctypes.POINTER(c_sz), ctypes.POINTER(ctypes.c_int)]
+    L.orc_crop_text.restype = ctypes.c_int
+    L.orc_crop_text.argtypes = [c_vp, c_sz, c_sz, c_vp, c_vp]
+    L.orc_ctc_decode.restype = ctypes.c_double
+    L.orc_ctc_decode.argtypes = [c_vp, c_vp, c_sz, c_vp, ctypes.POINTER(c_sz)]
+    L.orc_to_page.argtypes = [c_vp, ctypes.c_double, ctypes.c_double, c_sz, c_sz, c_sz, c_vp]
+    L._page_ready = True
+    return L
+
+
+def _u8(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.uint8)
+
+
+def resize_linear(image: np.ndarray, ow: int, oh: int) -> np.ndarray:
+    """cv2.resize INTER_LINEAR of an (h, w, 3) uint8 image (image.rs:91-142)."""
+    image = _u8(image)
+    out = np.empty((oh, ow, 3), np.uint8)
+    if _page_lib().orc_resize_linear(image.ctypes.data, image.shape[1], image.shape[0], ow, oh, out.ctypes.data):
+        raise OracleError("empty size")
+    return out
+
+
+def det_size(w: int, h: int, limit_min: int = 0):
+    """det_size (det.rs:166-193): (width, height) or None."""
+    ow, oh = ctypes.c_size_t(), ctypes.c_size_t()
+    if not _page_lib().orc_det_size(w, h, limit_min, ctypes.byref(ow), ctypes.byref(oh)):
+        return None
+    return ow.value, oh.value
+
+
+def prepare_page(w: int, h: int, min_side: int = 30, max_side: int = 4096, whr: float = 8.0,
+                 min_height: int = 30):
+    """prepare_page's sizes (det.rs:44-131): (fw, fh, ratio_h, ratio_w, pad_top) or None."""
+    fw, fh, pad = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
+    rh, rw = ctypes.c_double(), ctypes.c_double()
+    if not _page_lib().orc_prepare_page(w, h, min_side, max_side, whr, min_height, ctypes.byref(fw),
+                                        ctypes.byref(fh), ctypes.byref(rh), ctypes.byref(rw), ctypes.byref(pad)):
+        return None
+    return fw.value, fh.value, rh.value, rw.value, pad.value
+
+
+def find_contours(mask: np.ndarray) -> list[list[list[int]]]:
+    """cv2.findContours LIST/SIMPLE of an (h, w) mask (contour.rs:44-130)."""
+    mask = _u8(mask)
+    L = _page_lib()
+    c = L.orc_find_contours(mask.ctypes.data, mask.shape[1], mask.shape[0])
+    if not c:
+        raise OracleError("out of memory")
+    try:
+        out = []
+        for i in range(L.orc_contours_count(c)):
+            n = ctypes.c_size_t()
+            p = L.orc_contour(c, i, ctypes.byref(n))
+            pts = np.ctypeslib.as_array(p, shape=(n.value, 2)).tolist() if n.value else []
+            out.append(pts)
+        return out
+    finally:
+        L.orc_contours_free(c)
+
+
+def _pts(points) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(points, np.int32).reshape(-1, 2))
+
+
+def contour_mean(prob: np.ndarray, points) -> float:
+    prob = np.ascontiguousarray(prob, np.float32)
+    p = _pts(points)
+    return _page_lib().orc_contour_mean(prob.ctypes.data, prob.shape[1], prob.shape[0], p.ctypes.data, len(p))
+
+
+def min_area_rect_points(points) -> np.ndarray:
+    """cv2.boxPoints(cv2.minAreaRect(points)) (geometry.rs:228-240, 406-457), (4, 2) f32."""
+    p = _pts(points)
+    rect = np.empty(5, np.float32)
+    quad = np.empty((4, 2), np.float32)
+    L = _page_lib()
+    L.orc_min_area_rect(p.ctypes.data, len(p), rect.ctypes.data)
+    L.orc_box_points(rect.ctypes.data, quad.ctypes.data)
+    return quad
+
+
+def mini_box(points):
+    p = _pts(points)
+    quad = np.empty((4, 2), np.float32)
+    side = _page_lib().orc_mini_box(p.ctypes.data, len(p), quad.ctypes.data)
+    return quad, side
+
+
+def unclip(quad, ratio: float = 1.5) -> list[list[int]]:
+    q = np.ascontiguousarray(np.asarray(quad, np.float32).reshape(8))
+    out = np.empty((4096, 2), np.int32)
+    n = _page_lib().orc_unclip(q.ctypes.data, ratio, out.ctypes.data, 4096)
+    if n < 0:
+        raise OracleError("ring too long")
+    return out[:n].tolist()
+
+
+def boxes_from_prob(prob: np.ndarray, dest_w: int, dest_h: int, thresh: float = 0.3, box_thresh: float = 0.5,
+                    unclip_ratio: float = 1.5, max_candidates: int = 1000) -> np.ndarray:
+    """The DB postprocess (det.rs:430-452): (n, 4, 2) f32 quads in reading order."""
+    prob = np.ascontiguousarray(prob, np.float32)
+    mh, mw = prob.shape
+    cap = 4096
+    out = np.empty((cap, 4, 2), np.float32)
+    n = _page_lib().orc_boxes_from_prob(prob.ctypes.data, mw, mh, dest_w, dest_h, thresh, box_thresh,
+                                        unclip_ratio, max_candidates, out.ctypes.data, cap)
+    if n > cap:
+        raise OracleError(f"{n} boxes exceed {cap}")
+    return out[:n].copy()
+
+
+def crop_text(image: np.ndarray, quad) -> np.ndarray:
+    """crop_text (crop.rs:84-127): the (h, w, 3) uint8 crop, turned when tall."""
+    image = _u8(image)
+    q = np.ascontiguousarray(np.asarray(quad, np.float32).reshape(8))
+    w, h, turns = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_int()
+    L = _page_lib()
+    L.orc_crop_size(q.ctypes.data, ctypes.byref(w), ctypes.byref(h), ctypes.byref(turns))
+    shape = (w.value, h.value, 3) if turns.value else (h.value, w.value, 3)
+    out = np.zeros(shape, np.uint8)
+    if L.orc_crop_text(image.ctypes.data, image.shape[1], image.shape[0], q.ctypes.data, out.ctypes.data):
+        raise OracleError("empty page")
+    return out
+
+
+def dictionary(text: str) -> list[str]:
+    """Dictionary::from_metadata (rec.rs:54-79): blank, the lines as Python's
+    str.splitlines splits them (the reference restates exactly that), space."""
+    return ["blank", *text.splitlines(), " "]
+
+
+def ctc_decode(best, prob, classes: list[str]) -> tuple[str, float]:
+    """ctc_decode (rec.rs:144-161): the text and the score."""
+    b = np.ascontiguousarray(np.asarray(best, np.uint32))
+    p = np.ascontiguousarray(np.asarray(prob, np.float32))
+    kept = np.empty(max(len(b), 1), np.uint32)
+    n = ctypes.c_size_t()
+    score = _page_lib().orc_ctc_decode(b.ctypes.data, p.ctypes.data, len(b), kept.ctypes.data, ctypes.byref(n))
+    return "".join(classes[int(c)] for c in kept[:n.value]), score
+
+
+def to_page(quad, ratio_w: float, ratio_h: float, pad_top: int, width: int, height: int) -> np.ndarray:
+    q = np.ascontiguousarray(np.asarray(quad, np.float32).reshape(8))
+    out = np.empty((4, 2), np.float32)
+    _page_lib().orc_to_page(q.ctypes.data, ratio_w, ratio_h, pad_top, width, height, out.ctypes.data)
+    return out
+
+
+def is_blank(text: str) -> bool:
+    """rec.rs:168-172: nothing but whitespace and the separators 0x1c-0x1f."""
+    return all(c.isspace() or "\x1c" <= c <= "\x1f" for c in text)
+
+
+def page_lines(boxes, reads, ratio_w: float, ratio_h: float, pad_top: int, width: int, height: int,
+               text_score: float = 0.3):
+    """page_lines (lib.rs:96-117): (quad, text, score) of the kept lines; a
+    NaN score is never under text_score."""
+    out = []
+    for quad, (text, score) in zip(boxes, reads):
+        if is_blank(text) or score < text_score:
+            continue
+        out.append((to_page(quad, ratio_w, ratio_h, pad_top, width, height), text, score))
+    return out

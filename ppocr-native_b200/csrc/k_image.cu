@@ -173,7 +173,7 @@ extern "C" int ppocr_rec_input_hwc(const uint8_t *crop, size_t width, size_t hei
 
 extern "C" int ppocr_det_input_hwc(const uint8_t *image, size_t width, size_t height, size_t out_width,
                                    size_t out_height, const double *mean, const double *std, float *out,
-                                   void *stream) {
+                                   size_t capacity, void *stream) {
     if (!image || !out || !mean || !std) {
         ppocr::set_last_error("ppocr_det_input_hwc: null pointer");
         return PPOCR_E_ARG;
@@ -181,6 +181,10 @@ extern "C" int ppocr_det_input_hwc(const uint8_t *image, size_t width, size_t he
     if (!width || !height || !out_width || !out_height || width > (1u << 20) || height > (1u << 20) ||
         out_width > (1u << 20) || out_height > (1u << 20)) {
         ppocr::set_last_error("ppocr_det_input_hwc: sizes must be between 1 and 2^20");
+        return PPOCR_E_SIZE;
+    }
+    if (capacity / 3 / out_width < out_height) {
+        ppocr::set_last_error("ppocr_det_input_hwc: out holds fewer than out_height x out_width x 3 floats");
         return PPOCR_E_SIZE;
     }
     ImageArgs a;

@@ -21,12 +21,21 @@
 //
 // Host code cannot pass the array's name to a kernel (on the host that name
 // is only a stand-in for the device variable); its device address comes from
-// cudaGetSymbolAddress, once per device, with that device current. The first
-// call on each device does that set-up, so that first call should come before
-// any stream capture. No call allocates: no cudaMalloc, cudaFree or
-// allocating library routine is used here.
+// cudaGetSymbolAddress, once per device, with that device current. The same
+// once-per-device set-up raises the logits kernel's dynamic shared-memory
+// limit on that device (the head's ci x (64 + 128) floats of staging exceed
+// the 48 KB default for ci > 64), so a process that never builds a model can
+// call this entry point. The first call on each device does that set-up, so
+// that first call should come before any stream capture. No call allocates:
+// no cudaMalloc, cudaFree or allocating library routine is used here.
+//
+// The logits kernel reads the weight panels as 16-byte vectors, so `w` must
+// be 16-byte aligned; the other buffers are read and written as floats. A
+// misaligned pointer is refused before any launch (PPOCR_E_ARG) rather than
+// faulting on the device.
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <map>
 #include <mutex>
 #include <string>
@@ -48,7 +57,8 @@ constexpr size_t NOALLOC_SCRATCH_FLOATS = size_t(1) << 20;
 
 static __device__ __align__(256) float g_ctc_scratch[NOALLOC_SCRATCH_FLOATS];
 
-// The array's device address on the current device, looked up once.
+// The array's device address on the current device, looked up once, and
+// the kernels' limits raised on that device at the same time.
 int scratch_on_device(float **out) {
     static std::mutex mu;
     static std::map<int, float *> by_device;
@@ -71,6 +81,13 @@ int scratch_on_device(float **out) {
                        cudaGetErrorString(e));
         return PPOCR_E_DEVICE;
     }
+    configure_misc_kernels();
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_last_error(std::string("ppocr_ctc_argmax_noalloc: raising the kernels' shared-memory limits: ") +
+                       cudaGetErrorString(e));
+        return PPOCR_E_DEVICE;
+    }
     by_device[device] = ptr;
     *out = ptr;
     return PPOCR_OK;
@@ -83,6 +100,11 @@ extern "C" int ppocr_ctc_argmax_noalloc(const float *x, const float *w, const fl
     set_last_error("");
     if (!x || !w || !b || !y || pixels == 0 || ci == 0 || vocab == 0) {
         set_last_error("ppocr_ctc_argmax_noalloc: null buffer or empty size");
+        return PPOCR_E_ARG;
+    }
+    const auto misaligned = [](const void *p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) & (n - 1)) != 0; };
+    if (misaligned(w, 16) || misaligned(x, 4) || misaligned(b, 4) || misaligned(y, 4)) {
+        set_last_error("ppocr_ctc_argmax_noalloc: w must be 16-byte aligned and x, b, y 4-byte aligned");
         return PPOCR_E_ARG;
     }
     size_t cols = (vocab + 15) / 16 * 16;

@@ -63,7 +63,8 @@ _SIG = {
                                      ctypes.c_void_p]),
     "ppocr_det_input_hwc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
                                            ctypes.c_size_t, ctypes.POINTER(ctypes.c_double),
-                                           ctypes.POINTER(ctypes.c_double), ctypes.c_void_p, ctypes.c_void_p]),
+                                           ctypes.POINTER(ctypes.c_double), ctypes.c_void_p, ctypes.c_size_t,
+                                           ctypes.c_void_p]),
 }
 
 _lib = None
@@ -237,13 +238,16 @@ def ctc_argmax_noalloc(x: int, w: int, b: int, y: int, pixels: int, ci: int, voc
 
 
 def det_input_hwc(image: int, width: int, height: int, out_width: int, out_height: int, mean, std, out: int,
-                  stream: int | None = None) -> None:
+                  capacity: int | None = None, stream: int | None = None) -> None:
     """The detector's input from an RGB byte image, on the GPU (device
     pointers as ints): resized to out_width x out_height and normalized,
-    channels together; see `ppocr_det_input_hwc` in include/ppocr_cuda.h."""
+    channels together, into out (capacity floats; default exactly
+    out_width x out_height x 3); see `ppocr_det_input_hwc` in
+    include/ppocr_cuda.h."""
     m = (ctypes.c_double * 3)(*[float(v) for v in mean])
     s = (ctypes.c_double * 3)(*[float(v) for v in std])
-    _check(lib().ppocr_det_input_hwc(image, width, height, out_width, out_height, m, s, out, stream or None))
+    cap = out_width * out_height * 3 if capacity is None else capacity
+    _check(lib().ppocr_det_input_hwc(image, width, height, out_width, out_height, m, s, out, cap, stream or None))
 
 
 def rec_input_width(width: int, height: int) -> int:

@@ -41,3 +41,65 @@ def max_gap(a: np.ndarray, b: np.ndarray) -> float:
 
 
 __all__ = ["noise", "rng_values", "single", "max_gap", "Op", "window", "encode"]
+
+
+# ------------------------------------------------ device buffers for tests
+
+def cudart():
+    """The CUDA runtime through ctypes, for tests that hold device buffers of
+    their own (the C ABI's entry points take device pointers)."""
+    import ctypes
+    import glob
+    import os
+
+    here = os.path.dirname(np.__file__)
+    for p in glob.glob(os.path.join(here, "..", "nvidia", "cuda_runtime", "lib", "libcudart.so*")) + [
+            "libcudart.so.12", "/usr/local/cuda/lib64/libcudart.so"]:
+        try:
+            rt = ctypes.CDLL(p)
+        except OSError:
+            continue
+        rt.cudaMalloc.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_size_t]
+        rt.cudaFree.argtypes = [ctypes.c_void_p]
+        rt.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+        rt.cudaMemset.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t]
+        rt.cudaDeviceSynchronize.argtypes = []
+        return rt
+    raise RuntimeError("no libcudart for the test's device buffers")
+
+
+class Device:
+    """Device buffers a test owns: `put(array)` copies a host array in and
+    returns its pointer, `alloc(nbytes)` reserves one, `get(ptr, like)` copies
+    one back; everything is freed on exit."""
+
+    def __init__(self):
+        self.rt = cudart()
+        self.ptrs = []
+
+    def __enter__(self):
+        return self
+
+    def alloc(self, nbytes: int) -> int:
+        import ctypes
+
+        p = ctypes.c_void_p()
+        assert self.rt.cudaMalloc(ctypes.byref(p), max(int(nbytes), 1)) == 0
+        self.ptrs.append(p.value)
+        return p.value
+
+    def put(self, a: np.ndarray) -> int:
+        a = np.ascontiguousarray(a)
+        p = self.alloc(a.nbytes)
+        assert self.rt.cudaMemcpy(p, a.ctypes.data, a.nbytes, 1) == 0
+        return p
+
+    def get(self, p: int, shape, dtype) -> np.ndarray:
+        out = np.empty(shape, dtype)
+        assert self.rt.cudaMemcpy(out.ctypes.data, p, out.nbytes, 2) == 0
+        return out
+
+    def __exit__(self, *exc):
+        for p in self.ptrs:
+            self.rt.cudaFree(p)
+        self.ptrs = []

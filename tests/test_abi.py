@@ -93,3 +93,17 @@ def test_input_preparation_arguments_checked_before_any_device():
     with pytest.raises(cuda.PpocrError) as e:  # out too small for 48 x 320 x 3
         cuda.rec_input_hwc(16, 100, 48, 16, 10)
     assert e.value.code == cuda.E_SIZE
+    with pytest.raises(cuda.PpocrError) as e:  # out too small for 8 x 8 x 3
+        cuda.det_input_hwc(16, 10, 10, 8, 8, [0, 0, 0], [1, 1, 1], 16, capacity=8 * 8 * 3 - 1)
+    assert e.value.code == cuda.E_SIZE
+
+
+def test_noalloc_refuses_misaligned_buffers_before_any_launch():
+    """The no-allocation CTC head reads its weight panels as 16-byte vectors:
+    a w that is not 16-byte aligned (or a float buffer that is not 4-byte
+    aligned) is an argument error, returned before any device work."""
+    for x, w, b, y in ((256, 260, 512, 768), (257, 256, 512, 768), (256, 256, 514, 768), (256, 256, 512, 770)):
+        with pytest.raises(cuda.PpocrError) as e:
+            cuda.ctc_argmax_noalloc(x, w, b, y, 40, 120, 18710)
+        assert e.value.code == cuda.E_ARG, (x, w, b, y)
+        assert "aligned" in str(e.value)

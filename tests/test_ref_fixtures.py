@@ -121,7 +121,7 @@ def test_page_lines_match_worker(oracle_mod):
 def test_padding_score_filter_and_empty_pages(oracle_mod):
     # apply_vertical_padding with width_height_ratio -1, min_height 30 (parity.rs:296-299)
     for h, w, pad in [(100, 100, 0), (20, 100, 20), (10, 200, 25)]:
-        got = oracle_mod.prepare_page(w, h, whr=-1.0, min_height=30)
+        got = oracle_mod.prepare_page(w, h, min_side=1, whr=-1.0, min_height=30)  # no upscale: the band alone
         assert got is not None and got[4] == pad, (w, h, got)
     quad = [[0, 0], [9, 0], [9, 9], [0, 9]]
     lines = oracle_mod.page_lines([quad, quad], [("ab", math.nan), ("cd", 0.1)], 1.0, 1.0, 0, 10, 10)

@@ -168,6 +168,145 @@ int ppocr_rec_input_hwc(const uint8_t *crop, size_t width, size_t height, float 
  * (device memory in and out) on `stream`. Allocates nothing. */
 int ppocr_db_mask(const float *prob, size_t pixels, float thresh, uint8_t *mask, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Page reading: the steps around the two networks.
+ *
+ * The reference's library exposes its page steps as plain functions the
+ * worker strings together (src/lib.rs:15-48, re-exports at :533-544); its
+ * worker's Reader reads a page with them and the two networks
+ * (src/bin/ppocr-native/ocr.rs:205-263). The host steps below are those
+ * functions, bit for bit (border following, boxes, unclip, page sizes,
+ * CTC decode, the dictionary); a reader runs the whole page on the GPU
+ * where the step is data-parallel (page fit, detector input, text mask, box
+ * scores, crops, recogniser inputs) and on the calling thread where it is
+ * sequential. Quads are 8 floats: top-left, top-right, bottom-right,
+ * bottom-left, (x, y) each. Images are RGB (or BGR: channel order is kept)
+ * bytes, rows of width * 3.
+ * ---------------------------------------------------------------------- */
+
+/* The worker's options (det.rs:142-152 PageOptions, :305-315 DbOptions,
+ * main.rs:112-122, ocr.rs:20-25 MEAN / STD). */
+typedef struct {
+    float thresh;              /* text pixel: prob > thresh (0.3) */
+    double box_thresh;         /* mean probability a box needs (0.5) */
+    double unclip_ratio;       /* growth: area * ratio / perimeter (1.5) */
+    uint32_t max_candidates;   /* contours considered (1000) */
+    double text_score;         /* lines scoring less are dropped (0.3) */
+    uint32_t min_side, max_side;   /* page fit (30, 4096) */
+    double width_height_ratio; /* vertical padding rule (8; -1 turns it off) */
+    uint32_t min_height;       /* (30) */
+    uint32_t limit_min;        /* 0: Limit::Max (960/1500/2000); else Limit::Min(limit_min) */
+    double mean[3], std[3];    /* detector normalization per channel */
+} ppocr_reader_options;
+
+typedef struct ppocr_reader ppocr_reader;
+
+void ppocr_reader_options_default(ppocr_reader_options *options);
+/* A reader over a detector and a recogniser (an argmax recogniser: output
+ * [steps][2] = (class, probability)) whose weights it shares, with the
+ * recogniser's classes from `characters` (the model's metadata, one class
+ * per line, as rec.rs:54-79 Dictionary::from_metadata). The reader makes
+ * its own models and stream (replaces ocr.rs:114-201 Reader::load). */
+int ppocr_reader_create(const ppocr_model *det, const ppocr_model *rec, const char *characters, size_t len,
+                        const ppocr_reader_options *options, ppocr_reader **out);
+void ppocr_reader_free(ppocr_reader *reader);
+/* The cudaStream_t the reader runs on. */
+void *ppocr_reader_stream(ppocr_reader *reader);
+/* Page-locked host memory for a width x height page, valid until the next
+ * call or ppocr_reader_free; a page written there and passed to
+ * ppocr_reader_detect / _read is copied to the GPU at full speed (any other
+ * host pointer works too, through the driver's staging). */
+uint8_t *ppocr_reader_page(ppocr_reader *reader, size_t width, size_t height);
+/* Detection (ocr.rs:205-231 Reader::detect): the page prepared (fit and
+ * padding, det.rs:110-131), the detector at det_size, the DB postprocess
+ * (det.rs:430-452). The boxes (on the prepared page, in reading order)
+ * stay until the next call. A page with no usable size has no boxes. */
+int ppocr_reader_detect(ppocr_reader *reader, const uint8_t *page, size_t width, size_t height,
+                        uint32_t timeout_ms);
+size_t ppocr_reader_box_count(const ppocr_reader *reader);
+const float *ppocr_reader_boxes(const ppocr_reader *reader);
+/* The prepared page of the last detection: its size, the ratios back to
+ * the page as given and the padding band (det.rs:28-38 PreparedPage). */
+int ppocr_reader_prepared(const ppocr_reader *reader, size_t *width, size_t *height, double *ratio_w,
+                          double *ratio_h, size_t *pad_top);
+/* Recognition of n quads on the prepared page of the last detection
+ * (ocr.rs:436-530 recognise_on_gpu / read_on_gpu): crops (crop.rs:84-127),
+ * recogniser inputs (rec.rs:19-43), the recogniser, CTC decode
+ * (rec.rs:144-161). Read i is quad i's text and score. */
+int ppocr_reader_recognise(ppocr_reader *reader, const float *quads, size_t n, uint32_t timeout_ms);
+size_t ppocr_reader_text_count(const ppocr_reader *reader);
+int ppocr_reader_text(const ppocr_reader *reader, size_t i, const char **text, double *score);
+/* A whole page (ocr.rs:234-263 Reader::read, without its vertical re-read
+ * of low-scoring vertical lines): detection, the boxes read, then
+ * page_lines (lib.rs:96-129): blank or low-scoring lines dropped, boxes
+ * mapped back to the page as given. */
+int ppocr_reader_read(ppocr_reader *reader, const uint8_t *page, size_t width, size_t height, uint32_t timeout_ms);
+size_t ppocr_reader_line_count(const ppocr_reader *reader);
+int ppocr_reader_line(const ppocr_reader *reader, size_t i, float quad[8], const char **text, double *score);
+/* PPOCR_OPT_* bits for the reader's models (PPOCR_OPT_NO_TENSOR_CORES:
+ * both networks in the reference CPU engine's exact arithmetic). */
+int ppocr_reader_set_options(ppocr_reader *reader, uint32_t options);
+/* The detector's probability map of the last detection (host memory,
+ * capacity floats; *width x *height values). */
+int ppocr_reader_prob_map(ppocr_reader *reader, float *out, size_t capacity, size_t *width, size_t *height);
+/* Contours the GPU scored, and how many of those the host scored again in
+ * the reference's summation order because their mean lay within the
+ * parallel sum's error bound of box_thresh. */
+int ppocr_reader_stats(const ppocr_reader *reader, size_t *scored, size_t *rescored);
+
+/* cv2.findContours(mask, RETR_LIST, CHAIN_APPROX_SIMPLE) (contour.rs:44-130):
+ * contour i is points[2*starts[i] .. 2*starts[i+1]); *contours and *npoints
+ * receive the counts, PPOCR_E_SIZE when the capacities are short. */
+int ppocr_find_contours(const uint8_t *mask, size_t width, size_t height, int32_t *points, size_t points_cap,
+                        size_t *starts, size_t starts_cap, size_t *contours, size_t *npoints);
+/* The map's f64 mean inside a contour (contour.rs:142-199). */
+int ppocr_contour_mean(const float *map, size_t width, size_t height, const int32_t *points, size_t n,
+                       double *mean);
+/* cv2.minAreaRect as OpenCV 5 computes it (geometry.rs:406-457):
+ * rect = {cx, cy, width, height, angle in degrees}. */
+int ppocr_min_area_rect(const int32_t *points, size_t n, float rect[5]);
+/* cv2.boxPoints (geometry.rs:228-240). */
+int ppocr_box_points(const float rect[5], float quad[8]);
+/* RapidOCR's get_mini_boxes (geometry.rs:462-477): ordered corners and the
+ * shorter side. */
+int ppocr_mini_box(const int32_t *points, size_t n, float quad[8], float *side);
+/* RapidOCR's unclip (geometry.rs:519-606, pyclipper's round offset): ring
+ * points into out (cap points), their count in *n. */
+int ppocr_unclip(const float quad[8], double ratio, int32_t *out, size_t cap, size_t *n);
+/* The DB postprocess on the host (det.rs:430-452): quads in reading order
+ * on a dest_w x dest_h page. */
+int ppocr_boxes_from_prob(const float *prob, size_t map_w, size_t map_h, size_t dest_w, size_t dest_h, float thresh,
+                          double box_thresh, double unclip_ratio, size_t max_candidates, float *quads, size_t cap,
+                          size_t *n);
+/* The detector input size (det.rs:166-193): limit_min 0 is Limit::Max. */
+int ppocr_det_size(size_t width, size_t height, size_t limit_min, size_t *out_width, size_t *out_height);
+/* prepare_page's sizes (det.rs:44-131) under `options` (NULL: defaults). */
+int ppocr_prepare_page(size_t width, size_t height, const ppocr_reader_options *options, size_t *out_width,
+                       size_t *out_height, double *ratio_w, double *ratio_h, size_t *pad_top);
+/* The size of crop_text's result for a quad, turned when tall. */
+int ppocr_crop_size(const float quad[8], size_t *width, size_t *height);
+/* crop_text on the GPU (crop.rs:84-127): the quad straightened out of
+ * `image` (device memory) by its projective map and Keys' bicubic taps,
+ * turned a quarter counter-clockwise when 1.5 times taller than wide, into
+ * `out` (device memory, capacity bytes) on `stream`. Allocates nothing. */
+int ppocr_crop_text(const uint8_t *image, size_t width, size_t height, const float quad[8], uint8_t *out,
+                    size_t capacity, void *stream);
+
+/* The recogniser's classes (rec.rs:54-79): blank, the metadata's lines as
+ * Python's str.splitlines splits them, a space. */
+typedef struct ppocr_dictionary ppocr_dictionary;
+int ppocr_dictionary_load(const char *text, size_t len, ppocr_dictionary **out);
+size_t ppocr_dictionary_size(const ppocr_dictionary *d);
+const char *ppocr_dictionary_class(const ppocr_dictionary *d, size_t i, size_t *len);
+void ppocr_dictionary_free(ppocr_dictionary *d);
+/* RapidOCR's greedy CTC decode of an argmax recogniser's [steps][2] output
+ * (rec.rs:144-161, ocr.rs:551-560): UTF-8 text (NUL-terminated, capacity
+ * bytes) and its score. */
+int ppocr_ctc_decode(const float *output, size_t steps, const ppocr_dictionary *d, char *text, size_t capacity,
+                     size_t *len, double *score);
+/* 1 when the text is only white space (rec.rs:168-172). */
+int ppocr_text_is_blank(const char *text, size_t len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -339,3 +339,65 @@ def page_lines(boxes, reads, ratio_w: float, ratio_h: float, pad_top: int, width
             continue
         out.append((to_page(quad, ratio_w, ratio_h, pad_top, width, height), text, score))
     return out
+
+
+# ------------------------------------------------------ a whole page
+
+MEAN = (0.485, 0.456, 0.406)  # the worker's detector normalization (ocr.rs:20-25)
+STD = (0.229, 0.224, 0.225)
+
+
+def prepared_image(page: np.ndarray, min_side: int = 30, max_side: int = 4096, whr: float = 8.0,
+                   min_height: int = 30):
+    """prepare_page (det.rs:110-131): the fitted, padded page and its
+    (ratio_w, ratio_h, pad_top), or None."""
+    h, w = page.shape[:2]
+    got = prepare_page(w, h, min_side, max_side, whr, min_height)
+    if got is None:
+        return None
+    fw, fh, rh, rw, pad = got
+    fit_h = fh - 2 * pad
+    img = page if (fw, fit_h) == (w, h) else resize_linear(page, fw, fit_h)
+    if pad:
+        band = np.zeros((pad, fw, 3), np.uint8)
+        img = np.concatenate([band, img, band], axis=0)
+    return np.ascontiguousarray(img), (rw, rh, pad)
+
+
+def read_page(page: np.ndarray, det: "Oracle", rec: "Oracle", classes: list[str], quads=None, threads: int = 0,
+              text_score: float = 0.3, limit_min: int = 0, max_side: int = 4096):
+    """The worker's page read on the CPU oracle (ocr.rs:205-263 without the
+    vertical re-read): prepare, detect at det_size, DB boxes, crops,
+    recogniser inputs, recogniser, CTC decode, page_lines. With `quads`,
+    those are recognised instead of the detected boxes (and no page lines
+    are formed). Returns dict(boxes, reads, lines, prob)."""
+    prep = prepared_image(page, max_side=max_side)
+    if prep is None:
+        return {"boxes": np.zeros((0, 4, 2), np.float32), "reads": [], "lines": [], "prob": None}
+    img, (rw, rh, pad) = prep
+    ph, pw = img.shape[:2]
+    size = det_size(pw, ph, limit_min)
+    if size is None or size[0] * size[1] > max_side * max_side:
+        size = det_size(pw, ph, 0)
+    dw, dh = size
+    x = det_input_hwc(img, dw, dh, MEAN, STD)
+    det.set_size(dh, dw)
+    prob = det.run(x.reshape(-1), threads=threads)[0].reshape(dh, dw)
+    boxes = boxes_from_prob(prob, pw, ph)
+    todo = boxes if quads is None else np.asarray(quads, np.float32).reshape(-1, 4, 2)
+    reads = []
+    crops = []
+    for q in todo:
+        crop = crop_text(img, q)
+        crops.append(crop)
+        if crop.shape[0] == 0 or crop.shape[1] == 0:
+            reads.append(("", 0.0))
+            continue
+        xin = rec_input_hwc(crop)
+        rec.set_size(48, xin.shape[1])
+        out = rec.run(xin.reshape(-1), threads=threads)[0].reshape(-1, 2)
+        reads.append(ctc_decode(out[:, 0].astype(np.uint32), out[:, 1], classes))
+    lines = []
+    if quads is None:
+        lines = page_lines(boxes, reads, rw, rh, pad, page.shape[1], page.shape[0], text_score)
+    return {"boxes": boxes, "reads": reads, "lines": lines, "prob": prob, "crops": crops}

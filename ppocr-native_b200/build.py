@@ -27,7 +27,7 @@ INCLUDE = HERE.parent / "include"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # IEEE division and square root, no flush-to-zero: the kernels reproduce the
 # reference's f32 arithmetic; every contraction is written out explicitly.
-COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3",
+COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-ffp-contract=off",
           "-ftz=false", "-prec-div=true", "-prec-sqrt=true", f"-I{INCLUDE}"]
 
 

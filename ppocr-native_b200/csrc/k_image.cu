@@ -20,11 +20,15 @@
 #include <string>
 
 #include "../../include/ppocr_cuda.h"
+#include "image.cuh"
 #include "kernels.hpp"
 
 namespace ppocr {
 void set_last_error(const std::string &msg);
 }
+
+using ppocr::resize_tap;
+using ppocr::Tap;
 
 namespace {
 
@@ -35,23 +39,6 @@ struct ImageArgs {
     double mean[3], std[3];
 };
 
-struct Tap {
-    int near, far, near_w, far_w;
-};
-
-__device__ __forceinline__ Tap resize_tap(int src, int dst, int d) {
-    const double scale = __ddiv_rn(1.0, __ddiv_rn(double(dst), double(src)));
-    const float f = __double2float_rn(__dadd_rn(__dmul_rn(__dadd_rn(double(d), 0.5), scale), -0.5));
-    const float fl = floorf(f);
-    const float a = __fsub_rn(f, fl);
-    const int s = int(fl), last = src - 1;
-    Tap t;
-    t.near = s < 0 ? 0 : s > last ? last : s;
-    t.far = s + 1 < 0 ? 0 : s + 1 > last ? last : s + 1;
-    t.near_w = __float2int_rn(__fmul_rn(__fsub_rn(1.0f, a), 2048.0f));
-    t.far_w = __float2int_rn(__fmul_rn(a, 2048.0f));
-    return t;
-}
 
 __global__ void __launch_bounds__(256) det_input_kernel(const ImageArgs a) {
     const long total = long(a.ow) * a.oh;

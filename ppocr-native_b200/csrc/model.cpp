@@ -94,6 +94,39 @@ struct HostBuffer {
     }
 };
 
+// Buffers of a new set of sizes take over the previous set's allocation
+// when it is large enough and allocate (with a quarter of headroom) only when
+// they grow, as the reference's lanes do (`gpu/mod.rs:297-388`): a run of
+// new sizes then costs no cudaMalloc / cudaFree, which would synchronize the
+// device, and no page-locked allocation.
+bool reserve(DeviceBuffer &b, DeviceBuffer *old, size_t bytes, const char *what, int &code) {
+    b.bytes = bytes;
+    if (old && old->p && old->bytes >= bytes) {
+        b.p = old->p;
+        b.bytes = old->bytes;
+        old->p = nullptr;
+        return true;
+    }
+    const size_t grown = bytes + bytes / 4;
+    if (!cuda_ok(cudaMalloc(&b.p, grown), what, &code)) return false;
+    b.bytes = grown;
+    return true;
+}
+
+bool reserve(HostBuffer &b, HostBuffer *old, size_t bytes, const char *what, int &code) {
+    b.bytes = bytes;
+    if (old && old->p && old->bytes >= bytes) {
+        b.p = old->p;
+        b.bytes = old->bytes;
+        old->p = nullptr;
+        return true;
+    }
+    const size_t grown = bytes + bytes / 4;
+    if (!cuda_ok(cudaHostAlloc(&b.p, grown, cudaHostAllocDefault), what, &code)) return false;
+    b.bytes = grown;
+    return true;
+}
+
 // Weights on one device, shared by the models made with share_weights.
 struct Weights {
     int device = 0;
@@ -419,7 +452,7 @@ struct ppocr_model {
     }
 
     int bias_mode(const Op &op) const;
-    int build_group(Group &g, std::string &err);
+    int build_group(Group &g, std::string &err, Group *old);
     int record(bool copies);
     int enqueue(bool copies);
 };
@@ -499,7 +532,7 @@ long total_in(const Group &g, size_t i) {
 
 }  // namespace
 
-int ppocr_model::build_group(Group &g, std::string &err) {
+int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
     const Plan &p0 = g.plans[0];
     const size_t N = g.count();
     int code = PPOCR_OK;
@@ -530,8 +563,8 @@ int ppocr_model::build_group(Group &g, std::string &err) {
     g.slots.clear();
     for (size_t s = 0; s < slot_floats.size(); s++) {
         auto b = std::make_unique<DeviceBuffer>();
-        b->bytes = std::max<size_t>(slot_floats[s], 1) * sizeof(float);
-        if (!cuda_ok(cudaMalloc(&b->p, b->bytes), "allocating a tensor", &code)) {
+        DeviceBuffer *prev = old && s < old->slots.size() ? old->slots[s].get() : nullptr;
+        if (!reserve(*b, prev, std::max<size_t>(slot_floats[s], 1) * sizeof(float), "allocating a tensor", code)) {
             err = g_error;
             return code;
         }
@@ -569,35 +602,36 @@ int ppocr_model::build_group(Group &g, std::string &err) {
                 concat_floats = std::max(concat_floats, size_t(total_in(g, i)) * (op.ic + op.n2));
         }
     if (concat_floats) {
-        g.concat_scratch.bytes = concat_floats * sizeof(float);
-        if (!cuda_ok(cudaMalloc(&g.concat_scratch.p, g.concat_scratch.bytes), "allocating scratch", &code)) {
+        if (!reserve(g.concat_scratch, old ? &old->concat_scratch : nullptr, concat_floats * sizeof(float),
+                     "allocating scratch", code)) {
             err = g_error;
             return code;
         }
     }
-    g.mean_scratch.bytes = mean_doubles * sizeof(double);
-    g.ctc_scratch.bytes = ctc_floats * sizeof(float);
-    if (!cuda_ok(cudaMalloc(&g.mean_scratch.p, g.mean_scratch.bytes), "allocating scratch", &code) ||
-        !cuda_ok(cudaMalloc(&g.ctc_scratch.p, g.ctc_scratch.bytes), "allocating scratch", &code)) {
+    if (!reserve(g.mean_scratch, old ? &old->mean_scratch : nullptr, mean_doubles * sizeof(double),
+                 "allocating scratch", code) ||
+        !reserve(g.ctc_scratch, old ? &old->ctc_scratch : nullptr, ctc_floats * sizeof(float), "allocating scratch",
+                 code)) {
         err = g_error;
         return code;
     }
     // Page-locked host staging.
-    g.in_host.bytes = std::max<size_t>(g.in_floats, 1) * sizeof(float);
-    if (!cuda_ok(cudaHostAlloc(&g.in_host.p, g.in_host.bytes, cudaHostAllocDefault), "allocating host input", &code)) {
+    if (!reserve(g.in_host, old ? &old->in_host : nullptr, std::max<size_t>(g.in_floats, 1) * sizeof(float),
+                 "allocating host input", code)) {
         err = g_error;
         return code;
     }
-    std::memset(g.in_host.p, 0, g.in_host.bytes);
+    std::memset(g.in_host.p, 0, std::max<size_t>(g.in_floats, 1) * sizeof(float));
     g.out_host.clear();
     for (size_t k = 0; k < p0.outputs.size(); k++) {
         auto hb = std::make_unique<HostBuffer>();
-        hb->bytes = std::max<size_t>(g.out_floats[k], 1) * sizeof(float);
-        if (!cuda_ok(cudaHostAlloc(&hb->p, hb->bytes, cudaHostAllocDefault), "allocating host output", &code)) {
+        HostBuffer *prev = old && k < old->out_host.size() ? old->out_host[k].get() : nullptr;
+        if (!reserve(*hb, prev, std::max<size_t>(g.out_floats[k], 1) * sizeof(float), "allocating host output",
+                     code)) {
             err = g_error;
             return code;
         }
-        std::memset(hb->p, 0, hb->bytes);
+        std::memset(hb->p, 0, std::max<size_t>(g.out_floats[k], 1) * sizeof(float));
         g.out_host.push_back(std::move(hb));
     }
 
@@ -617,8 +651,8 @@ int ppocr_model::build_group(Group &g, std::string &err) {
         auto t = lane_table(g, i, shifts);
         tables.insert(tables.end(), t.begin(), t.end());
     }
-    g.lane_tables.bytes = std::max<size_t>(tables.size(), 1) * sizeof(LaneInfo);
-    if (!cuda_ok(cudaMalloc(&g.lane_tables.p, g.lane_tables.bytes), "allocating lane tables", &code) ||
+    if (!reserve(g.lane_tables, old ? &old->lane_tables : nullptr, std::max<size_t>(tables.size(), 1) * sizeof(LaneInfo),
+                 "allocating lane tables", code) ||
         !cuda_ok(cudaMemcpy(g.lane_tables.p, tables.data(), tables.size() * sizeof(LaneInfo),
                             cudaMemcpyHostToDevice), "uploading lane tables", &code)) {
         err = g_error;
@@ -1218,7 +1252,7 @@ int ppocr_model_set_sizes(ppocr_model *m, const uint32_t *hw, size_t lanes) {
     }
     m->drop_graphs();
     std::string err;
-    int rc = m->build_group(*g, err);
+    int rc = m->build_group(*g, err, m->group.get());
     if (rc) return fail(rc, err);
     m->group = std::move(g);
     m->sizes = std::move(sizes);

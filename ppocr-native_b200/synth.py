@@ -230,3 +230,34 @@ def stripes(h: int, w: int, c: int = 3, phase: int = 0) -> np.ndarray:
     (`tests/gpu.rs:18-22`)."""
     i = np.arange(h * w * c, dtype=np.int64)
     return (np.sin(((i + phase) % 977).astype(np.float32) * np.float32(0.37)) * 2).astype(np.float32)
+
+
+def darkness_det_plan(size: tuple[int, int] = (480, 640), blur: int = 7, gain: float = 3.0) -> bytes:
+    """A detector-shaped plan with set (not random) weights whose map marks
+    dark ink: a depthwise blur of `blur` x `blur` over the normalized page,
+    then a 1x1 conv 3 -> 1 of weight -gain/3 per channel and a sigmoid, so
+    dark glyph rows with small gaps become blobs of probability near 1 on a
+    near-0 background. It gives the page reader real text boxes to find
+    (a random-init detector maps a page to a near-constant 0.5); it is a
+    test input, not a model."""
+    k = blur
+    b = Builder(size[0], size[1], 3, np.random.default_rng(0), 0.0)
+    d = b.new(3)
+    op = Op("dwconv", x=0, y=d, ic=3, oc=3, fused="none", kh=k, kw=k, sh=1, sw=1,
+            pt=k // 2, pb=k // 2, pl=k // 2, pr=k // 2)
+    op.w = b.put(np.full((k, k, 3), 1.0 / (k * k), np.float32))
+    op.b = b.put(np.zeros(3, np.float32))
+    b.ops.append(op)
+    y = b.new(1)
+    pw = Op("conv", x=d, y=y, ic=3, oc=1, fused="sigmoid", kh=1, kw=1, sh=1, sw=1)
+    pw.w = b.put(np.full((1, 1, 3, 1), -gain / 3.0, np.float32))
+    pw.b = b.put(np.zeros(1, np.float32))
+    b.ops.append(pw)
+    return encode(b.input, b.buffers, [y], b.ops, np.concatenate(b.blob))
+
+
+def characters(vocab: int = VOCAB) -> str:
+    """Dictionary metadata for a `vocab`-class recogniser: vocab - 2 lines
+    (blank and space are added by the dictionary), distinct CJK code points
+    from U+4E00 (characters.txt of the real model is 18 707 such lines)."""
+    return "".join(chr(0x4E00 + i) + "\n" for i in range(vocab - 2))

@@ -52,3 +52,47 @@ class Page:
 
     def input_bytes(self) -> int:
         return self.det.nbytes + sum(x.nbytes for x in self.lines)
+
+
+# ------------------------------------------------------- synthetic pages
+
+PAGE_WIDTH, PAGE_HEIGHT = 2550, 3300  # a 300-dpi letter page
+
+
+def synthetic_page(seed: int, lines: int = LINES_PER_PAGE, width: int = PAGE_WIDTH, height: int = PAGE_HEIGHT):
+    """A seeded 300-dpi page as benchmark config 4 describes it: white, `lines`
+    horizontal rows of dark glyph-like rectangles of random widths, 20-40 px
+    tall with 1-3 px gaps, gray noise of sigma 4; 8-bit, channels together.
+
+    Each row's length is chosen so that its crop at height 48 is 80-1600 px
+    wide. Returns the page (height, width, 3) uint8 and the rows' quads
+    (lines, 4, 2) float32 (top-left, top-right, bottom-right, bottom-left:
+    each row's outer edges) on the page.
+    """
+    rng = np.random.default_rng(seed)
+    page = np.full((height, width), 255.0, np.float32)
+    pitch = (height - 200) / max(lines, 1)
+    quads = np.zeros((lines, 4, 2), np.float32)
+    for i in range(lines):
+        h = int(rng.integers(20, 41))
+        y0 = int(100 + i * pitch + rng.integers(0, max(1, int(pitch) - h)))
+        target = int(rng.integers(80, 1601))  # crop width at height 48
+        length = min(max(int(round(target * h / 48)), 8), width - 200)
+        x0 = int(rng.integers(100, width - 100 - length + 1))
+        x, end = x0, x0 + length
+        while x < end:
+            gw = min(int(rng.integers(4, 25)), end - x)
+            page[y0:y0 + h, x:x + gw] = float(rng.integers(0, 90))
+            x += gw + int(rng.integers(1, 4))
+        quads[i] = [[x0, y0], [end, y0], [end, y0 + h], [x0, y0 + h]]
+    page += rng.standard_normal(page.shape, dtype=np.float32) * np.float32(4.0)
+    gray = np.clip(np.rint(page), 0, 255).astype(np.uint8)
+    return np.repeat(gray[:, :, None], 3, axis=2), quads
+
+
+def page_stream(seed: int, pages: int, distinct: int | None = None):
+    """Benchmark config 5's stream: `pages` pages with 20-60 lines each, drawn
+    from `distinct` seeded pages (all distinct when None)."""
+    rng = np.random.default_rng(seed)
+    counts = rng.integers(20, 61, size=pages if distinct is None else distinct)
+    return [(seed * 100003 + k, int(counts[k])) for k in range(len(counts))]

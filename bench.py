@@ -1,26 +1,42 @@
-"""Benchmark: synthetic 300-dpi pages through the PP-OCRv6 detector and
-recogniser on B200, one process per GPU.
+"""Benchmark: synthetic 300-dpi pages read end to end on B200, one process per
+GPU.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload page|det|rec|layer]
+                    [--workload page|stream|neural|det|rec|layer|conv3x3|dw3x3]
 
-A step is one page's neural hot path: the detector at 1984 x 1536 and the
-recogniser over the page's 44 lines (runs of up to 16 lanes, each line at
-its own width). `value` is pages/s over all ranks with every input already
-in HBM; `e2e` the same through the public C ABI from page-locked host
-buffers, copies in and out included. With N > 1 each rank reads its own
-pages (weak scaling); ranks exchange nothing but the timing.
+The headline workload (`page`, benchmark config 4): a seeded 2550 x 3300
+8-bit page (44 rows of glyph-like rectangles) goes through the public page
+reader (include/ppocr_cuda.h `ppocr_reader_*`): the page bytes to the GPU,
+the detector's input (OpenCV resize + normalization) at 1984 x 1536, the
+detector, the text mask, border following and box scores, the DB boxes, the
+crops of the page's 44 line quads, their recogniser inputs, the recogniser
+over all lines of the page as lanes of one run, the CTC decode. The
+detector's weights are random-init (N(0, 0.02)) as the configuration asks,
+so its map is a near-constant 0.5 and the DB postprocess finds one
+page-sized box; the lines recognised are therefore the generator's own 44
+quads, cropped from the page through the same crop path (the DB
+postprocess still runs in full on every page).
+
+A step is one page per reader in flight (`--readers`, each on its own host
+thread and stream, weights shared). `value`: pages/s with the pages already
+in HBM; `e2e`: the same through the C ABI from page-locked host pages, the
+page's bytes copied in and every result (mask, scores, reads) copied out
+inside the timed region. `--workload stream` is config 5: 800 pages of 20-60
+lines sharded by page over the ranks (strong scaling). With N > 1 each rank
+reads its own pages; ranks exchange nothing but the timing.
 
 `--impl reference` times the reference CPU path on this host: the C
-restatement of ppocr-native's CPU engine (oracle/, the reference itself is
-Rust and cannot be built here), all host threads, bounded samples.
+restatement of ppocr-native's CPU engine and host page steps (oracle/; the
+reference itself is Rust and cannot be built here), all host threads.
 """
 
 from __future__ import annotations
 
 import argparse
+import concurrent.futures as cf
 import faulthandler
 import importlib.util
+import itertools
 import json
 import os
 import statistics
@@ -37,20 +53,17 @@ PKG_DIR = ROOT / "ppocr-native_b200"
 sys.path.insert(0, str(ROOT))
 
 L2_FLUSH_BYTES = 256 << 20  # larger than the 126 MB L2
-# DRAM bytes (read + written) of one launch of the pointwise probe, from one
-# ncu capture of `bench.py --workload layer`
-# (profiles/pw_tc_kernel_1x1_24to24_992x768.md); writes still dirty in L2 when
-# the kernel ends are not counted there.
-TRAFFIC_PER_LAUNCH = 99.67e6
-TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch (profiles/pw_tc_kernel_1x1_24to24_992x768.md)"
-# The same for the dominant kernel's probe (`bench.py --workload conv3x3`).
-CONV_TRAFFIC_PER_LAUNCH = 78.19e6
-# The same for the depthwise probe (`bench.py --workload dw3x3`).
-DW_TRAFFIC_PER_LAUNCH = 107.59e6
-DW_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
-                     "(profiles/dw_row_kernel_3x3_c24_992x768.md)")
-CONV_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
-                       "(profiles/conv_tc_kernel_3x3_96to24_496x384.md)")
+# DRAM bytes (read + written) of one launch of each probed kernel, from one
+# ncu capture of its probe command (dram__bytes_read.sum +
+# dram__bytes_write.sum; writes still dirty in L2 at the kernel's end are not
+# counted there): `bench.py --workload layer|conv3x3|dw3x3 --profile
+# --steps 2 --warmup 1` under `ncu -k regex:<kernel> -c 1`.
+TRAFFIC = {
+    "layer": (99.67e6, "pw_tc_kernel, bench.py --workload layer"),
+    "conv3x3": (78.19e6, "conv_tc_kernel, bench.py --workload conv3x3"),
+    "dw3x3": (107.59e6, "dw_row_kernel, bench.py --workload dw3x3"),
+}
+METRIC = "synthetic-page pages/s (2550x3300 page -> det 1984x1536 -> DB boxes -> crops -> rec -> CTC decode) per B200 job"
 
 
 def package():
@@ -98,14 +111,25 @@ class Dist:
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
+    def gather(self, values: list[float]) -> list[list[float]]:
+        """Every rank's `values` (same length on every rank), on every rank."""
+        if not self.pg:
+            return [values]
+        import torch
+
+        t = torch.tensor(values, dtype=torch.float64, device=self.device)
+        out = [torch.empty_like(t) for _ in range(self.world)]
+        self.pg.all_gather(out, t)
+        return [o.tolist() for o in out]
+
     def close(self):
         if self.pg:
             self.pg.destroy_process_group()
 
     def whole_job(self, units_per_rank: float, local_seconds: float) -> tuple[float, float]:
         """Units of all ranks per second over the slowest rank's time (every
-        rank processes the same number of its own pages: weak scaling), and
-        that time."""
+        rank reads the same number of its own pages: weak scaling), and that
+        time."""
         t = self.max(local_seconds)
         return self.world * units_per_rank / t, t
 
@@ -170,92 +194,192 @@ def cpu_threads() -> int:
     return len(os.sched_getaffinity(0))
 
 
-# -------------------------------------------------------------- our path
+def peaks() -> dict:
+    p = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    hbm, bf16 = p.get("hbm_gbs"), p.get("bf16_tflops")
+    out = {"hbm": hbm, "hbm_source": "measured: MEASURED_PEAKS.json hbm_gbs (copy, burst)",
+           "bf16": bf16, "bf16_source": "measured: MEASURED_PEAKS.json bf16_tflops (cuBLAS, burst)"}
+    if hbm is None:
+        out["hbm"], out["hbm_source"] = 6650.0, "fallback: 6.65 TB/s"
+    if bf16 is None:
+        out["bf16"], out["bf16_source"] = 1590.0, "fallback: 1.59 PFLOP/s"
+    return out
 
-class PagePipeline:
-    """The detector and the recogniser runs of one page, queued on one stream."""
 
-    def __init__(self, cuda, synth, page, device: int, workload: str = "page", like=None):
-        """`like`: another pipeline whose weights this one shares (its own
-        models, stream and buffers)."""
+# ------------------------------------------------------------- the pages
+
+def make_pages(seeds_lines, threads: int = 8):
+    """Synthetic pages (config 4 generator) for (seed, lines) pairs, made on
+    host threads: [(page (h, w, 3) uint8, quads (n, 4, 2) float32)]."""
+    workload = package().workload
+    with cf.ThreadPoolExecutor(max_workers=threads) as ex:
+        return list(ex.map(lambda sl: workload.synthetic_page(sl[0], lines=sl[1]), seeds_lines))
+
+
+class PagePool:
+    """Pages in page-locked host memory and, for the device-resident run, in
+    HBM; each with its line quads."""
+
+    def __init__(self, torch, device: int, pages):
+        self.host, self.dev, self.quads = [], [], []
+        for page, quads in pages:
+            h = torch.from_numpy(page).pin_memory()
+            self.host.append(h)
+            self.dev.append(h.to(f"cuda:{device}", non_blocking=False))
+            self.quads.append(np.ascontiguousarray(quads.reshape(-1, 8), dtype=np.float32))
+        self.h, self.w = pages[0][0].shape[:2]
+        torch.cuda.synchronize()
+
+    def __len__(self):
+        return len(self.host)
+
+
+def read_pages(torch, readers, pool: PagePool, total: int, on_device: bool, main):
+    """`total` pages (pool pages in turn) over the readers, one host thread
+    each; every page: detection (the full DB postprocess on the model's
+    map), then the page's line quads recognised and their texts read on the
+    host. Returns device seconds (CUDA events on `main`, every reader stream
+    ordered between them), wall seconds, host CPU seconds, per-page wall
+    latencies and kernel launches per page."""
+    counter = itertools.count()
+    lock = threading.Lock()
+    errors, lat, launches = [], [], []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(main)
+    streams = [torch.cuda.ExternalStream(r.stream) for r in readers]
+    for st in streams:
+        st.wait_event(e0)
+
+    def work(r):
+        try:
+            while True:
+                with lock:
+                    i = next(counter)
+                if i >= total:
+                    return
+                k = i % len(pool)
+                t0 = time.perf_counter()
+                if on_device:
+                    r.detect_ptr(pool.dev[k].data_ptr(), pool.w, pool.h, on_device=True)
+                else:
+                    r.detect_ptr(pool.host[k].data_ptr(), pool.w, pool.h)
+                q = pool.quads[k]
+                r.recognise_ptr(q.ctypes.data, len(q))
+                texts = r.texts()  # the page's result, read on the host
+                if len(texts) != len(q):
+                    raise RuntimeError("a read is missing")
+                lat.append(time.perf_counter() - t0)
+                launches.append(r.launches)
+        except Exception as e:  # reported by the caller
+            errors.append(e)
+
+    cpu0, w0 = time.process_time(), time.perf_counter()
+    threads = [threading.Thread(target=work, args=(r,)) for r in readers]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    wall = time.perf_counter() - w0
+    cpu = time.process_time() - cpu0
+    if errors:
+        raise errors[0]
+    for st in streams:
+        ev = torch.cuda.Event()
+        ev.record(st)
+        main.wait_event(ev)
+    e1.record(main)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / 1e3, wall, cpu, lat, (statistics.median(launches) if launches else 0)
+
+
+# ------------------------------------------------------ secondary measures
+
+class NeuralPipeline:
+    """The detector and the recogniser runs of one page's tensors (seeded
+    N(0, 1) inputs of the page's shapes), queued on one stream: the neural
+    hot path alone, device-resident."""
+
+    def __init__(self, cuda, synth, workload, device: int, like=None):
+        page = workload.Page(seed=7)
         self.det = like.det.share_weights() if like else cuda.Model(synth.det_plan(seed=0), device=device)
         h, w = page.det.shape[:2]
         self.det.set_input_size(h, w)
-        rec = like.recs[0].share_weights() if like else cuda.Model(synth.rec_plan(seed=1), device=device)
-        self.recs = [rec] + [rec.share_weights() for _ in page.runs[1:]]
+        rec = like.rec.share_weights() if like else cuda.Model(synth.rec_plan(seed=1), device=device)
+        self.rec = rec
         self.stream = self.det.stream
-        for m, run in zip(self.recs, page.runs):
-            m.set_stream(self.stream)
-            m.set_sizes([(48, page.widths[i]) for i in run])
-        self.page = page
-        self.workload = workload
+        rec.set_stream(self.stream)
+        rec.set_sizes([(48, wd) for wd in page.widths])  # all lines of the page: one run
+        np.copyto(self.det.input_mut(), page.det.reshape(-1))
+        for lane in range(len(page.widths)):
+            np.copyto(rec.lane_input_mut(lane), page.lines[lane].reshape(-1))
+        self.det.run(60_000)
+        rec.run(60_000)
 
-    def models(self):
-        if self.workload == "det":
-            return [self.det]
-        if self.workload == "rec":
-            return list(self.recs)
-        return [self.det, *self.recs]
-
-    def all_models(self):
-        return [self.det, *self.recs]
-
-    def fill_host(self):
-        """Copy the page into the page-locked lane inputs."""
-        np.copyto(self.det.input_mut(), self.page.det.reshape(-1))
-        for m, run in zip(self.recs, self.page.runs):
-            for lane, i in enumerate(run):
-                np.copyto(m.lane_input_mut(lane), self.page.lines[i].reshape(-1))
-
-    def enqueue_host(self):
-        """The public call sequence, first half: every run queues the copy of
-        its page-locked inputs in, its kernels and the copy of its outputs
-        out."""
-        for m in self.models():
-            m.enqueue()
-
-    def wait_host(self):
-        """Second half: wait for the runs; the host reads each result."""
-        for m in self.models():
-            m.wait(0)
-        outs = [self.det.output()]
-        for m, run in zip(self.recs, self.page.runs):
-            for lane in range(len(run)):
-                outs.append(m.lane_output(lane))
-        return outs
-
-    def run_host(self):
-        self.enqueue_host()
-        return self.wait_host()
-
-    def enqueue_device(self):
-        for m in self.models():
-            m.enqueue_device()
-
-    def launches(self) -> int:
-        return sum(m.launches for m in self.models())
-
-    def io_bytes(self):
-        h2d = self.page.input_bytes()
-        d2h = self.det.output().nbytes
-        for m, run in zip(self.recs, self.page.runs):
-            d2h += sum(m.lane_output(lane).nbytes for lane in range(len(run)))
-        return h2d, d2h
+    def enqueue(self):
+        self.det.enqueue_device()
+        self.rec.enqueue_device()
 
     def close(self):
-        # the recogniser models run on the detector's stream: they go first
-        for m in reversed(self.all_models()):
-            m.close()
+        self.rec.close()
+        self.det.close()
+
+
+def device_time(torch, stream_ptr: int, fn, reps: int, flush) -> float:
+    """Median seconds of fn() on a stream, CUDA events, L2 flushed before each."""
+    stream = torch.cuda.ExternalStream(stream_ptr)
+    times = []
+    for i in range(reps + 3):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        fn()
+        with torch.cuda.stream(stream):
+            e1.record(stream)
+        e1.synchronize()
+        if i >= 3:
+            times.append(e0.elapsed_time(e1) / 1e3)
+    return statistics.median(times)
+
+
+def configs_1_to_3(cuda, synth, torch, device: int, flush) -> dict:
+    """Benchmark configs 1-3 on the device, inputs resident, L2 flushed: the
+    fused depthwise 5x5 + pointwise 96->192 layer at 240 x 240, the detector
+    at 960 x 736, the recogniser over 16 lines of 48 x 320."""
+    rng = np.random.default_rng(0)
+    out = {}
+    with cuda.Model(synth.fused_layer_plan(seed=0)) as m:
+        m.input_mut()[:] = rng.uniform(-1, 1, 240 * 240 * 96).astype(np.float32)
+        m.run(60_000)
+        t = device_time(torch, m.stream, m.enqueue_device, 20, flush)
+        out["config1_fused_layer_us"] = t * 1e6
+        out["config1_tflops"] = 2.400e9 / t / 1e12
+        out["config1_steps"] = m.steps()
+    with cuda.Model(synth.det_plan(seed=0)) as m:
+        m.set_input_size(960, 736)
+        m.input_mut()[:] = rng.standard_normal(960 * 736 * 3).astype(np.float32)
+        m.run(60_000)
+        out["config2_det_960x736_ms"] = device_time(torch, m.stream, m.enqueue_device, 20, flush) * 1e3
+        m.set_input_size(1984, 1536)
+        m.input_mut()[:] = rng.standard_normal(1984 * 1536 * 3).astype(np.float32)
+        m.run(60_000)
+        out["det_1984x1536_ms"] = device_time(torch, m.stream, m.enqueue_device, 10, flush) * 1e3
+    with cuda.Model(synth.rec_plan(seed=1)) as m:
+        m.set_sizes([(48, 320)] * 16)
+        for lane in range(16):
+            m.lane_input_mut(lane)[:] = rng.standard_normal(48 * 320 * 3).astype(np.float32)
+        m.run(60_000)
+        out["config3_rec_16x320_ms"] = device_time(torch, m.stream, m.enqueue_device, 20, flush) * 1e3
+    return out
 
 
 # The probed layers: the page's dominant kernel (conv_tc_kernel, the
-# tensor-core implicit GEMM for stride-1 windowed convolutions, the largest
-# share of a page's launch time) at its most common launch, the detector's
-# 3x3 96 -> 24 RSE convolution at a quarter of a 1984 x 1536 page; and the
-# pointwise kernel (pw_tc_kernel) at its largest launch, the detector's first
-# 1x1 24 -> 24 + swish at half the page; and the depthwise kernel
-# (dw_row_kernel) at its largest launch, the detector's first 3x3 depthwise
-# layer over 24 channels + swish at half the page.
+# tensor-core implicit GEMM for stride-1 windowed convolutions) at its most
+# common launch, the detector's 3x3 96 -> 24 RSE convolution at a quarter of
+# a 1984 x 1536 page; the pointwise kernel (pw_tc_kernel) at its largest
+# launch, the detector's first 1x1 24 -> 24 + swish at half the page; the
+# depthwise kernel (dw_row_kernel) at its largest launch, the detector's
+# first 3x3 depthwise layer over 24 channels + swish at half the page.
 LAYERS = {
     "conv3x3": dict(h=496, w=384, ic=96, oc=24, k=3, fused="none",
                     kernel="conv_tc_kernel: 3x3 96->24 @ 496x384 (3xTF32 tcgen05, the RSE neck's convolution)"),
@@ -280,9 +404,101 @@ def layer_plan(name: str) -> bytes:
     return encode((0, L["h"], L["w"], L["ic"]), 2, [1], [op], np.concatenate([wt, b]))
 
 
-def run_layer(args, d, cuda, torch, device):
-    """--workload layer | conv3x3 | dw3x3: the probed layer alone, warm-up then timed
-    steps (the command ncu captures)."""
+def probe_kernel(cuda, torch, device: int, name: str, flush, reps: int = 20) -> dict:
+    """One probed layer alone, CUDA events on the model's stream, L2 flushed
+    before each launch. Algorithmic bytes: the input and output maps once,
+    the weights (for the tensor cores: two tf32 halves, K padded to 32) and
+    the bias; FLOPs: 2 per multiply-add."""
+    L = LAYERS[name]
+    h, w, ic, oc, k = L["h"], L["w"], L["ic"], L["oc"], L["k"]
+    dw = L.get("kind") == "dwconv"
+    m = cuda.Model(layer_plan(name), device=device)
+    assert m.steps() == ["dwconv" if dw else "conv"], m.steps()
+    m.input_mut()[:] = np.random.default_rng(0).standard_normal(h * w * ic).astype(np.float32)
+    m.run(60_000)
+    t = device_time(torch, m.stream, m.enqueue_device, reps, flush)
+    m.close()
+    if dw:
+        return {"kernel": L["kernel"], "seconds": t, "flops": 2 * h * w * k * k * ic,
+                "bytes": 4 * (h * w * ic + h * w * oc + k * k * ic + ic)}
+    kk = k * k * ic
+    kpad = -(-kk // 32) * 32
+    return {"kernel": L["kernel"], "seconds": t, "flops": 2 * h * w * kk * oc,
+            "bytes": 4 * (h * w * ic + h * w * oc + 2 * oc * kpad + oc)}
+
+
+def roofline_entry(probe: dict, name: str, pk: dict, tensor: bool) -> dict:
+    traffic, source = TRAFFIC[name]
+    if tensor:
+        tc_peak = pk["bf16"] / 2 / 3  # 3xTF32: tf32 at half the bf16 rate, three MMAs per product
+        achieved = probe["flops"] / probe["seconds"] / 1e12
+        return {"bound": "tensor", "kernel": probe["kernel"], "achieved": achieved, "peak": tc_peak,
+                "unit": "TFLOP/s", "frac": achieved / tc_peak,
+                "peak_source": pk["bf16_source"] + " / 2 (tf32) / 3 (3xTF32 products): FP32-equivalent",
+                "traffic": traffic, "traffic_source": "ncu, one launch: " + source,
+                "algorithmic_flops": probe["flops"], "algorithmic_bytes": probe["bytes"],
+                "hbm_frac": probe["bytes"] / probe["seconds"] / 1e9 / pk["hbm"],
+                "seconds_per_launch": probe["seconds"]}
+    achieved = probe["bytes"] / probe["seconds"] / 1e9
+    return {"bound": "hbm", "kernel": probe["kernel"], "achieved": achieved, "peak": pk["hbm"], "unit": "GB/s",
+            "frac": achieved / pk["hbm"], "peak_source": pk["hbm_source"], "traffic": traffic,
+            "traffic_source": "ncu, one launch: " + source, "algorithmic_bytes": probe["bytes"],
+            "seconds_per_launch": probe["seconds"]}
+
+
+# --------------------------------------------------------------- CPU side
+
+def cpu_page_sample(page, quads, budget_s: float = 10.0, threads: int = 0) -> dict:
+    """The reference CPU path (oracle, all host threads) over one page: the
+    detector input, the detector at 1984 x 1536, the DB postprocess, then
+    crops, recogniser inputs, recogniser and CTC decode of the page's lines
+    until the budget is spent; seconds per page, lines scaled to all."""
+    pkg = package()
+    from oracle import oracle as o
+
+    o.build()
+    synth = pkg.synth
+    threads = threads or cpu_threads()
+    det = o.Oracle(synth.det_plan(seed=0))
+    rec = o.Oracle(synth.rec_plan(seed=1))
+    classes = o.dictionary(synth.characters(synth.VOCAB))
+    t0 = time.perf_counter()
+    dw, dh = o.det_size(page.shape[1], page.shape[0])
+    x = o.det_input_hwc(page, dw, dh, o.MEAN, o.STD)
+    det.set_size(dh, dw)
+    prob = det.run(x.reshape(-1), threads=threads)[0].reshape(dh, dw)
+    o.boxes_from_prob(prob, page.shape[1], page.shape[0])
+    t_det = time.perf_counter() - t0
+    t_rec, done, macs = 0.0, 0, 0
+    for q in quads:
+        t0 = time.perf_counter()
+        crop = o.crop_text(page, q)
+        xin = o.rec_input_hwc(crop)
+        rec.set_size(48, xin.shape[1])
+        out = rec.run(xin.reshape(-1), threads=threads)[0].reshape(-1, 2)
+        o.ctc_decode(out[:, 0].astype(np.uint32), out[:, 1], classes)
+        t_rec += time.perf_counter() - t0
+        done += 1
+        if t_det + t_rec > budget_s:
+            break
+    page_s = t_det + t_rec * len(quads) / done
+    return {"seconds": page_s, "t_det": t_det, "t_rec": t_rec, "lines": done, "of": len(quads), "threads": threads}
+
+
+def cpu_baseline(page, quads, budget_s: float = 15.0) -> dict:
+    s = cpu_page_sample(page, quads, budget_s)
+    return {"value": 1.0 / s["seconds"], "unit": "pages/s", "cores": s["threads"], "kind": "port",
+            "sample": f"1 page: detector input + detector 1984x1536 + DB boxes ({s['t_det']:.2f} s), "
+                      f"{s['lines']} of {s['of']} lines cropped, recognised and decoded ({s['t_rec']:.2f} s, "
+                      "scaled to all); C restatement of the reference CPU engine and page steps (tier-3 FMA "
+                      "order), OpenMP over output rows"}
+
+
+# ------------------------------------------------------------------ ours
+
+def run_layer(args, d, cuda, device):
+    """--workload layer | conv3x3 | dw3x3: the probed layer alone, warm-up then
+    timed steps (the command ncu captures)."""
     L = LAYERS[args.workload]
     m = cuda.Model(layer_plan(args.workload), device=device)
     m.input_mut()[:] = np.random.default_rng(0).standard_normal(L["h"] * L["w"] * L["ic"]).astype(np.float32)
@@ -294,76 +510,51 @@ def run_layer(args, d, cuda, torch, device):
     return {"profile": args.workload, "launches_per_step": 1} if d.rank == 0 else None
 
 
-def probe_kernel(cuda, torch, device: int, name: str, reps: int = 20) -> dict:
-    """Time one probed layer alone with CUDA events on the model's stream, L2
-    flushed before each launch. Algorithmic bytes: the input and output maps
-    once, the weights (for the tensor cores: two tf32 halves, K padded to 32)
-    and the bias; FLOPs: 2 per multiply-add of the convolution."""
-    L = LAYERS[name]
-    h, w, ic, oc, k = L["h"], L["w"], L["ic"], L["oc"], L["k"]
-    dw = L.get("kind") == "dwconv"
-    rng = np.random.default_rng(0)
-    m = cuda.Model(layer_plan(name), device=device)
-    assert m.steps() == ["dwconv" if dw else "conv"], m.steps()
-    m.input_mut()[:] = rng.standard_normal(h * w * ic).astype(np.float32)
-    m.run(60_000)
-    stream = torch.cuda.ExternalStream(m.stream)
+def run_neural(args, d, cuda, synth, workload, torch, device):
+    """--workload neural|det|rec: the neural hot path alone, device-resident,
+    k page pipelines in flight (the commands the launch lists come from)."""
+    k = 1 if args.profile else max(1, args.readers)
+    pipes = [NeuralPipeline(cuda, synth, workload, device)]
+    pipes += [NeuralPipeline(cuda, synth, workload, device, like=pipes[0]) for _ in range(k - 1)]
+    main = torch.cuda.Stream(device=device)
+    streams = [torch.cuda.ExternalStream(p.stream) for p in pipes]
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
-    times = []
-    for i in range(reps + 3):
-        with torch.cuda.stream(stream):
+
+    def one(p):
+        if args.workload in ("neural", "det"):
+            p.det.enqueue_device()
+        if args.workload in ("neural", "rec"):
+            p.rec.enqueue_device()
+
+    for _ in range(args.warmup):
+        for p in pipes:
+            one(p)
+    torch.cuda.synchronize()
+    d.barrier()
+    events = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(main):
             flush.zero_()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-        m.enqueue_device()
-        with torch.cuda.stream(stream):
-            e1.record(stream)
-        e1.synchronize()
-        if i >= 3:
-            times.append(e0.elapsed_time(e1) / 1e3)
-    m.close()
-    t = statistics.median(times)
-    if dw:
-        return {"kernel": L["kernel"], "seconds": t, "flops": 2 * h * w * k * k * ic,
-                "bytes": 4 * (h * w * ic + h * w * oc + k * k * ic + ic)}
-    kk = k * k * ic
-    kpad = -(-kk // 32) * 32
-    return {"kernel": L["kernel"], "seconds": t, "flops": 2 * h * w * kk * oc,
-            "bytes": 4 * (h * w * ic + h * w * oc + 2 * oc * kpad + oc)}
-
-
-def cpu_baseline(widths_seed: int = 0, budget_s: float = 20.0) -> dict:
-    """The reference CPU path (C restatement, all host threads) on a bounded
-    sample: one page's detector and as many of its lines as fit the budget,
-    scaled to pages/s."""
-    pkg = package()
-    from oracle.oracle import Oracle, build
-
-    build()
-    synth, workload = pkg.synth, pkg.workload
-    page = workload.Page(widths_seed)
-    threads = cpu_threads()
-    det = Oracle(synth.det_plan(seed=0))
-    det.set_size(*page.det.shape[:2])
-    t0 = time.perf_counter()
-    det.run(page.det.reshape(-1), threads=threads)
-    t_det = time.perf_counter() - t0
-    rec = Oracle(synth.rec_plan(seed=1))
-    t_rec, done = 0.0, 0
-    for i, wd in enumerate(page.widths):
-        rec.set_size(48, wd)
-        t0 = time.perf_counter()
-        rec.run(page.lines[i].reshape(-1), threads=threads)
-        t_rec += time.perf_counter() - t0
-        done += 1
-        if t_det + t_rec > budget_s:
-            break
-    page_s = t_det + t_rec * len(page.widths) / done
-    return {"value": 1.0 / page_s, "unit": "pages/s", "cores": threads, "kind": "port",
-            "sample": f"1 page: detector 1984x1536 ({t_det:.2f} s) + {done} of {len(page.widths)} lines "
-                      f"({t_rec:.2f} s, scaled to all); C restatement of the reference CPU engine "
-                      "(tier-3 FMA order), OpenMP over output rows"}
+            e0.record(main)
+        for p, st in zip(pipes, streams):
+            st.wait_event(e0)
+            one(p)
+            done = torch.cuda.Event()
+            done.record(st)
+            main.wait_event(done)
+        e1.record(main)
+        events.append((e0, e1))
+    torch.cuda.synchronize()
+    local = sum(a.elapsed_time(b) for a, b in events) / 1e3
+    value, total = d.whole_job(args.steps * k, local)
+    launches = pipes[0].det.launches + pipes[0].rec.launches
+    for p in reversed(pipes):
+        p.close()
+    if d.rank == 0:
+        return {"profile": args.workload, "pages_per_s": value, "ms_per_step": total / args.steps * 1e3,
+                "launches_per_page": launches}
+    return None
 
 
 def run_ours(args, d: Dist) -> dict | None:
@@ -375,182 +566,159 @@ def run_ours(args, d: Dist) -> dict | None:
     torch.cuda.set_device(device)
     d.init("nccl")
     if args.workload in LAYERS:
-        return run_layer(args, d, cuda, torch, device)
-    page = workload.Page(seed=1000 + d.rank)
-    pipe = PagePipeline(cuda, synth, page, device, args.workload)
-    # Pages in flight: one pipeline each (own models, streams and buffers,
-    # shared weights); launch lists (--profile) take one.
-    k = 1 if args.profile else max(1, args.inflight)
-    pipes = [pipe] + [PagePipeline(cuda, synth, page, device, args.workload, like=pipe) for _ in range(k - 1)]
-    streams = [torch.cuda.ExternalStream(p.stream) for p in pipes]
-    main = torch.cuda.Stream(device=device)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
+        return run_layer(args, d, cuda, device)
+    if args.workload in ("neural", "det", "rec"):
+        return run_neural(args, d, cuda, synth, workload, torch, device)
 
-    # Inputs into HBM once through the public path (copies included).
-    for p in pipes:
-        p.fill_host()
-        p.run_host()
-        for _ in range(args.warmup):
-            p.enqueue_device()
+    R = max(1, args.readers)
+    # The pages: config 4 (44 lines each) or config 5's stream (20-60 lines),
+    # a pool of distinct seeded pages per rank read in turn.
+    if args.workload == "stream":
+        stream = workload.page_stream(seed=5, pages=args.stream_pages)
+        mine = stream[d.rank::d.world]
+        total = len(mine)
+        distinct = mine[:args.pool]
+    else:
+        total = args.steps * R
+        distinct = [(1000 * d.rank + i, workload.LINES_PER_PAGE) for i in range(args.pool)]
+    pages = make_pages(distinct, threads=min(16, cpu_threads()))
+    pool = PagePool(torch, device, pages)
+    text = synth.characters(synth.VOCAB)
+    det = cuda.Model(synth.det_plan(seed=0), device=device)
+    rec = cuda.Model(synth.rec_plan(seed=1), device=device)
+    readers = [cuda.Reader(det, rec, text) for _ in range(R)]
+    main = torch.cuda.Stream(device=device)
+
+    # Warm-up: every reader reads pages until its buffers have grown.
+    read_pages(torch, readers, pool, max(args.warmup, 1) * R, False, main)
     torch.cuda.synchronize()
 
-    # value: device-resident inputs; a step is k pages enqueued at once, each
-    # on its own stream, L2 flushed before each step outside its events.
-    events = []
+    # value: the pages already in HBM.
     d.barrier()
     torch.cuda.synchronize()
     with Clocks(device) as clocks:
-        for _ in range(args.steps):
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(main):
-                flush.zero_()
-                e0.record(main)
-            for p, st in zip(pipes, streams):
-                st.wait_event(e0)
-                p.enqueue_device()
-                done = torch.cuda.Event()
-                done.record(st)
-                main.wait_event(done)
-            e1.record(main)
-            events.append((e0, e1))
-        torch.cuda.synchronize()
+        dev_s, dev_wall, dev_cpu, dev_lat, launches = read_pages(torch, readers, pool, total, True, main)
     d.barrier()
-    local_s = sum(a.elapsed_time(b) for a, b in events) / 1e3
-    value, total_s = d.whole_job(args.steps * k, local_s)
-    if args.profile:
-        launches = pipe.launches()
-        pipe.close()
-        if d.rank == 0:
-            return {"profile": args.workload, "ms_per_step": total_s / args.steps * 1e3,
-                    "launches_per_step": launches}
+    # e2e: the pages in page-locked host memory, copied in by the reader.
+    torch.cuda.synchronize()
+    e2e_s, e2e_wall, e2e_cpu, e2e_lat, _ = read_pages(torch, readers, pool, total, False, main)
+    d.barrier()
+    boxes_found = readers[0].boxes().shape[0]
+    scored, rescored = readers[0].stats()
+    for r in readers:
+        r.close()
+    value, value_t = d.whole_job(total, dev_s)
+    e2e, e2e_t = d.whole_job(total, e2e_s)
+    page_bytes = pool.h * pool.w * 3
+    # per rank: pages/s, median and max page latency, host CPU use (of all host threads)
+    per_rank = d.gather([total / dev_s, statistics.median(dev_lat), max(dev_lat),
+                         dev_cpu / dev_wall / cpu_threads(), total / e2e_s, statistics.median(e2e_lat), max(e2e_lat),
+                         e2e_cpu / e2e_wall / cpu_threads()])
+    extra = {}
+    if d.rank == 0 and not args.quick:
+        flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
+        # the neural hot path alone (device-resident page tensors, R pages in flight)
+        nargs = argparse.Namespace(**vars(args))
+        nargs.workload, nargs.steps, nargs.warmup, nargs.profile = "neural", 20, 3, False
+        extra["neural"] = run_neural(nargs, Dist(), cuda, synth, workload, torch, device)
+        extra.update(configs_1_to_3(cuda, synth, torch, device, flush))
+        pk = peaks()
+        extra["probes"] = {n: probe_kernel(cuda, torch, device, n, flush) for n in LAYERS}
+        extra["peaks"] = pk
+    det.close()
+    rec.close()
+    if d.rank != 0:
         return None
+    # bytes per page through the C ABI: in, the page and its quads; out, the
+    # mask and the reads (2 floats per time step of every line; the box
+    # scores are a few bytes)
+    def steps_of(q):
+        w = cuda.rec_input_width(int(np.rint(q[2] - q[0])), int(np.rint(q[5] - q[1])))
+        return -(-w // 8)
 
-    # e2e: the public call sequence with host buffers. The page sits in the
-    # models' page-locked lane inputs (where a caller's preprocessing writes
-    # it); every step copies its inputs in, runs, copies its outputs out and
-    # the host reads the result. The k pipelines take the pages in turn, so
-    # one page's copies and latency-bound kernels overlap the others', as
-    # enqueue/wait allow any caller.
-    d.barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for step in range(args.steps):
-        p = pipes[step % k]
-        if step >= k:
-            outs = p.wait_host()
-            _ = float(outs[0][0])
-        p.enqueue_host()
-    for step in range(max(0, args.steps - k), args.steps):
-        outs = pipes[step % k].wait_host()
-        _ = float(outs[0][0])
-    torch.cuda.synchronize()
-    e2e_local = time.perf_counter() - t0
-    e2e, _ = d.whole_job(args.steps, e2e_local)
-    h2d, d2h = pipe.io_bytes()
-    launches = pipe.launches()
-
-    # det alone (ms), for the metric's "det fwd ms"
-    stream = streams[0]
-    det_times = []
-    for _ in range(5):
-        with torch.cuda.stream(stream):
-            flush.zero_()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-        pipe.det.enqueue_device()
-        with torch.cuda.stream(stream):
-            e1.record(stream)
-        e1.synchronize()
-        det_times.append(e0.elapsed_time(e1))
-    for p in reversed(pipes):
-        p.close()
-    d.barrier()
-
-    result = None
-    if d.rank == 0:
-        probe = probe_kernel(cuda, torch, device, "conv3x3")
-        pw = probe_kernel(cuda, torch, device, "layer")
-        dwp = probe_kernel(cuda, torch, device, "dw3x3")
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-        hbm, bf16 = peaks.get("hbm_gbs"), peaks.get("bf16_tflops")
-        hbm_source = "measured: MEASURED_PEAKS.json hbm_gbs (copy, burst)"
-        bf16_source = "measured: MEASURED_PEAKS.json bf16_tflops (cuBLAS, burst)"
-        if hbm is None:
-            hbm, hbm_source = 6650.0, "fallback: 6.65 TB/s"
-        if bf16 is None:
-            bf16, bf16_source = 1590.0, "fallback: 1.59 PFLOP/s"
-        # 3xTF32: the tf32 rate is half the bf16 one, three MMAs per product
-        tc_peak = bf16 / 2 / 3
-        result = {
-            "metric": "synthetic-page pages/s (det 1984x1536 + rec 44 lines) per B200 job",
-            "value": value,
-            "unit": "pages/s",
-            "n_gpus": d.world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": total_s / args.steps * 1e3,
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": "f32",
-            "data": "synthetic: seeded N(0,1) page tensors with the reference's page/line shapes; "
-                    "random-init weights N(0,0.02) of the synthetic PP-OCRv6-shaped det/rec plans",
-            "config": {"workload": "page: det 1984x1536 + rec 44 lines (48 x 320..1600, runs of 16)",
-                       "det_fwd_ms": statistics.median(det_times),
-                       "pages_per_step": k,
-                       "l2": "flushed (256 MB write) before every timed step, outside the step's events",
-                       "parallelism": f"replicas x{d.world} (pages sharded by rank, no collective)"},
-            "e2e": {"value": e2e, "unit": "pages/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "method": "C ABI enqueue/wait, inputs in the models' page-locked buffers, per step: H2D, "
-                              f"kernels, D2H, host read; one page per step, {k} pages in flight on their own "
-                              "streams"},
-            "gpu_launches": launches * args.steps * k,
-            "roofline": {"bound": "tensor", "kernel": probe["kernel"],
-                         "achieved": probe["flops"] / probe["seconds"] / 1e12, "peak": tc_peak, "unit": "TFLOP/s",
-                         "frac": probe["flops"] / probe["seconds"] / 1e12 / tc_peak,
-                         "peak_source": bf16_source + " / 2 (tf32) / 3 (3xTF32 products): FP32-equivalent",
-                         "traffic": CONV_TRAFFIC_PER_LAUNCH, "traffic_source": CONV_TRAFFIC_SOURCE,
-                         "algorithmic_flops": probe["flops"], "algorithmic_bytes": probe["bytes"],
-                         "hbm_frac": probe["bytes"] / probe["seconds"] / 1e9 / hbm,
-                         "seconds_per_launch": probe["seconds"]},
-            "roofline_pointwise": {"bound": "hbm", "kernel": pw["kernel"],
-                                   "achieved": pw["bytes"] / pw["seconds"] / 1e9, "peak": hbm, "unit": "GB/s",
-                                   "frac": pw["bytes"] / pw["seconds"] / 1e9 / hbm, "peak_source": hbm_source,
-                                   "traffic": TRAFFIC_PER_LAUNCH, "traffic_source": TRAFFIC_SOURCE,
-                                   "algorithmic_bytes": pw["bytes"], "seconds_per_launch": pw["seconds"]},
-            "roofline_depthwise": {"bound": "hbm", "kernel": dwp["kernel"],
-                                   "achieved": dwp["bytes"] / dwp["seconds"] / 1e9, "peak": hbm, "unit": "GB/s",
-                                   "frac": dwp["bytes"] / dwp["seconds"] / 1e9 / hbm, "peak_source": hbm_source,
-                                   "traffic": DW_TRAFFIC_PER_LAUNCH, "traffic_source": DW_TRAFFIC_SOURCE,
-                                   "algorithmic_bytes": dwp["bytes"],
-                                   "seconds_per_launch": dwp["seconds"]},
-            "clocks": clocks.summary(),
-        }
+    steps_per_page = float(np.mean([sum(steps_of(q) for q in pool.quads[k]) for k in range(len(pool))]))
+    h2d = page_bytes + 32 * float(np.mean([len(q) for q in pool.quads]))
+    d2h = 1984 * 1536 + 8 * steps_per_page
+    result = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "pages/s",
+        "n_gpus": d.world,
+        "steps": args.steps if args.workload == "page" else total,
+        "warmup": args.warmup,
+        "ms_per_step": value_t / (total / R) * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong" if args.workload == "stream" else "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: seeded 2550x3300 pages (white, rows of dark glyph-like rectangles 20-40 px tall with "
+                "1-3 px gaps, gray noise sigma 4); random-init weights N(0,0.02) of the PP-OCRv6-shaped det/rec plans",
+        "config": {
+            "workload": ("config 5: 800-page stream, 20-60 lines per page, sharded by page" if args.workload == "stream"
+                         else "config 4: 2550x3300 page -> resize+normalize -> det 1984x1536 -> DB postprocess -> "
+                              "crops of the page's 44 line quads -> rec inputs -> rec (all lines, one run) -> "
+                              "CTC decode (18 710 classes)"),
+            "boxes": f"DB postprocess of the random-init detector's map: {boxes_found} box(es) (a near-constant 0.5 "
+                     "map); the generator's line quads are recognised",
+            "pages_per_step": R,
+            "readers": f"{R} readers per GPU, one host thread and one stream each, weights shared",
+            "distinct_pages": len(pool),
+            "l2": "inputs larger than L2: each page is 25 MB and the detector's tensors ~1.5 GB per page",
+            "parallelism": f"replicas x{d.world} (pages sharded by rank, no collective)",
+            "box_scores": {"gpu_scored": scored, "host_rescored": rescored},
+            **extra,
+        },
+        "e2e": {"value": e2e, "unit": "pages/s", "h2d_bytes_per_step": int(h2d * R),
+                "d2h_bytes_per_step": int(d2h * R),
+                "method": "C ABI ppocr_reader_detect + ppocr_reader_recognise + texts read, page bytes in "
+                          "page-locked host memory; per page: page H2D, kernels, mask/scores/reads D2H, host "
+                          f"page steps; {R} readers in flight; CUDA events around all readers' streams"},
+        "gpu_launches": int(launches * total),
+        "per_rank": [{"rank": i, "pages_per_s": v[0], "page_ms_median": v[1] * 1e3, "page_ms_max": v[2] * 1e3,
+                      "host_cpu_busy": v[3], "e2e_pages_per_s": v[4], "e2e_page_ms_median": v[5] * 1e3,
+                      "e2e_page_ms_max": v[6] * 1e3, "e2e_host_cpu_busy": v[7]} for i, v in enumerate(per_rank)],
+        "clocks": clocks.summary(),
+    }
+    if extra.get("probes"):
+        pr, pk = extra.pop("probes"), extra["peaks"]
+        result["config"].pop("probes", None)
+        result["roofline"] = roofline_entry(pr["conv3x3"], "conv3x3", pk, True)
+        result["roofline_pointwise"] = roofline_entry(pr["layer"], "layer", pk, False)
+        result["roofline_depthwise"] = roofline_entry(pr["dw3x3"], "dw3x3", pk, False)
     return result
 
 
+# ------------------------------------------------------------- reference
+
 def run_reference(args, d: Dist) -> dict | None:
+    """The reference CPU path on this host, rank 0 only: each timed step one
+    bounded sample (a page's detector and DB postprocess, and its lines
+    until a budget, scaled); at most three timed samples so the run ends in
+    minutes whatever --steps asks."""
     if d.rank != 0:
         return None
-    samples = []
-    base = None
-    for step in range(args.warmup + args.steps):
-        b = cpu_baseline(widths_seed=step, budget_s=8.0)
-        if step >= args.warmup:
-            samples.append(b["value"])
-            base = b
+    pkg = package()
+    page, quads = pkg.workload.synthetic_page(1000)
+    samples, base = [], None
+    n = min(max(args.steps, 1), 3)
+    for step in range(min(args.warmup, 1) + n):
+        s = cpu_page_sample(page, quads, budget_s=args.ref_budget)
+        if step >= min(args.warmup, 1):
+            samples.append(1.0 / s["seconds"])
+            base = s
     value = statistics.median(samples)
     return {
         "impl": "reference",
-        "metric": "synthetic-page pages/s (det 1984x1536 + rec 44 lines) per B200 job",
-        "value": value, "unit": "pages/s", "n_gpus": d.world, "steps": args.steps, "warmup": args.warmup,
+        "metric": METRIC,
+        "value": value, "unit": "pages/s", "n_gpus": d.world, "steps": n, "warmup": min(args.warmup, 1),
         "ms_per_step": 1e3 / value, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (same pages and weights as the GPU arm)",
-        "config": {"workload": "page: det 1984x1536 + rec 44 lines (48 x 320..1600, runs of 16)"},
-        "cpu_baseline": {"value": value, "unit": "pages/s", "cores": base["cores"], "kind": "port",
-                         "sample": base["sample"]},
+        "dtype": "f32", "data": "synthetic (the same page generator and weights as the GPU arm)",
+        "config": {"workload": "config 4: 2550x3300 page -> det 1984x1536 -> DB boxes -> crops of the 44 line quads "
+                               "-> rec -> CTC decode, on the host cores"},
+        "cpu_baseline": {"value": value, "unit": "pages/s", "cores": base["threads"], "kind": "port",
+                         "sample": f"per step 1 page: detector + DB boxes ({base['t_det']:.2f} s), {base['lines']} of "
+                                   f"{base['of']} lines ({base['t_rec']:.2f} s, scaled); C restatement of the "
+                                   "reference CPU engine and page steps, OpenMP over output rows"},
         "e2e": {"value": value, "unit": "pages/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -559,14 +727,16 @@ def main():
     faulthandler.enable()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50, help="steps of `--readers` pages each")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--inflight", type=int, default=8,
-                    help="pages in flight (own models and streams, shared weights): a step's pages")
+    ap.add_argument("--readers", type=int, default=8, help="readers (pages in flight) per GPU")
+    ap.add_argument("--pool", type=int, default=16, help="distinct pages per rank")
+    ap.add_argument("--stream-pages", type=int, default=800)
+    ap.add_argument("--ref-budget", type=float, default=10.0, help="seconds of CPU work per reference sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["page", "det", "rec", *LAYERS], default="page",
-                    help="page (the benchmark step); det or rec alone, for profiling")
+    ap.add_argument("--quick", action="store_true", help="the page run alone (no neural, config 1-3 or probe legs)")
+    ap.add_argument("--workload", choices=["page", "stream", "neural", "det", "rec", *LAYERS], default="page")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up and timed steps (no e2e, probe, peak or CPU legs): for ncu launch lists")
     args = ap.parse_args()
@@ -576,11 +746,12 @@ def main():
         result = run_reference(args, d)
     else:
         result = run_ours(args, d)
-        if result is not None and not args.profile and args.workload == "page":
-            if args.no_cpu_baseline:
+        if result is not None and not args.profile and args.workload in ("page", "stream"):
+            if args.no_cpu_baseline or args.quick:
                 result["cpu_baseline"] = None
             else:
-                result["cpu_baseline"] = cpu_baseline()
+                page, quads = package().workload.synthetic_page(1000)
+                result["cpu_baseline"] = cpu_baseline(page, quads)
     d.close()
     if result is not None:
         print(json.dumps(result))

@@ -223,6 +223,13 @@ uint8_t *ppocr_reader_page(ppocr_reader *reader, size_t width, size_t height);
  * stay until the next call. A page with no usable size has no boxes. */
 int ppocr_reader_detect(ppocr_reader *reader, const uint8_t *page, size_t width, size_t height,
                         uint32_t timeout_ms);
+/* The same for a page already in device memory (read where it lies: keep
+ * it unchanged until the next detection, or the recognition after it,
+ * returns). */
+int ppocr_reader_detect_device(ppocr_reader *reader, const uint8_t *page, size_t width, size_t height,
+                               uint32_t timeout_ms);
+/* Kernels the last detection and the recognitions after it launched. */
+size_t ppocr_reader_launches(const ppocr_reader *reader);
 size_t ppocr_reader_box_count(const ppocr_reader *reader);
 const float *ppocr_reader_boxes(const ppocr_reader *reader);
 /* The prepared page of the last detection: its size, the ratios back to

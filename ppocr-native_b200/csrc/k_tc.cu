@@ -1079,9 +1079,13 @@ bool tc_prepare(TcArgs &a) {
         a.bn = conv_slice_width(a.N);
         if (!a.bn) return false;
         // few tiles: narrower slices, so that more SMs share the layer (each
-        // output's sum is the same whatever the slice)
+        // output's sum is the same whatever the slice). Not for the CTC
+        // head: its per-block softmax sums group the columns by slice, so the
+        // slice width must depend on the head alone, never on how many time
+        // steps the run holds (a lane then reads the same alone as beside
+        // others).
         const long tiles = a.windowed ? a.tiles : (a.M + TM - 1) / TM;
-        while (a.bn > 32 && tiles * ((a.N + a.bn - 1) / a.bn) < 74) a.bn -= 32;
+        while (a.vocab == 0 && a.bn > 32 && tiles * ((a.N + a.bn - 1) / a.bn) < 74) a.bn -= 32;
         a.slices = (a.N + a.bn - 1) / a.bn;
         a.ns = 2;
         while (a.ns < max_stages(a.bn) && conv_smem(a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;

@@ -705,7 +705,7 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
             gather.nsrc = c.nsrc; gather.C = c.C; gather.lanes = c.lanes; gather.nl = c.nl;
             gather.M = c.M;  // the output keeps the input's size
             gather.y = static_cast<float *>(g.concat_scratch.p);
-            if (!gather.y || size_t(c.M) * c.C * sizeof(float) > g.concat_scratch.bytes) return 0;
+            if (!gather.y || size_t(c.M) * c.C > concat_floats) return 0;
             t.x = gather.y;
         }
         t.C = c.C;
@@ -946,8 +946,9 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
                 mg.partial = a.partial; mg.x = a.x; mg.w = a.w; mg.b = a.b; mg.y = a.y;
                 mg.pixels = a.pixels; mg.ci = a.ci; mg.vocab = a.vocab;
                 mg.wmax = W.tc_wmax[i]; mg.bmax = W.tc_bmax[i];
-                if (tc_prepare(t) &&
-                    size_t(a.pixels) * t.blocks * 3 * sizeof(float) <= g.ctc_scratch.bytes) {
+                // the path depends on the layer's own need, never on how
+                // large a reused scratch buffer happens to be
+                if (tc_prepare(t) && size_t(a.pixels) * t.blocks * 3 <= ctc_floats) {
                     mg.blocks = t.blocks; mg.bn = t.bn;
                     g.launches.push_back(
                         [t, mg](cudaStream_t s) { return launch_tc(t, s) + launch_ctc_tc_merge(mg, s); });

@@ -141,6 +141,7 @@ struct ppocr_reader {
     page::Contours contours;
     page::ContourScratch scratch;
     size_t rescored = 0, scored = 0;
+    size_t launches = 0;  // kernels of the last detection and the recognitions after it
 
     ~ppocr_reader() {
         cudaSetDevice(device);
@@ -168,7 +169,7 @@ struct ppocr_reader {
         }
     }
 
-    int detect(const uint8_t *page, size_t w, size_t h, uint32_t timeout_ms);
+    int detect(const uint8_t *page, size_t w, size_t h, uint32_t timeout_ms, bool on_device = false);
     int recognise(const Quad *quads, size_t n, uint32_t timeout_ms);
     int score_boxes(const std::vector<std::pair<size_t, Quad>> &cand, uint32_t timeout_ms);
 };
@@ -176,7 +177,7 @@ struct ppocr_reader {
 // ocr.rs:205-231 Reader::detect: the page prepared (det.rs:110-131), the
 // detector at det_size (the page limit squared bounds Limit::Min, else
 // Limit::Max), the DB postprocess (det.rs:430-452) on its map.
-int ppocr_reader::detect(const uint8_t *page, size_t w, size_t h, uint32_t timeout_ms) {
+int ppocr_reader::detect(const uint8_t *page, size_t w, size_t h, uint32_t timeout_ms, bool on_device) {
     found.clear();
     reads.clear();
     lines.clear();
@@ -191,16 +192,22 @@ int ppocr_reader::detect(const uint8_t *page, size_t w, size_t h, uint32_t timeo
     if (!sized) sized = page::det_size(p.width, p.height, 0, dw, dh);
     if (!sized) return PPOCR_OK;
     int code = PPOCR_OK;
-    // the page on the device
+    launches = 0;
+    // the page on the device (a device page is read where it lies and must
+    // stay unchanged until the next detection or recognition returns)
     const size_t raw = w * h * 3;
-    if (!page_raw.fit(raw, code)) return code;
-    if (!cuda_ok(cudaMemcpyAsync(page_raw.p, page, raw, cudaMemcpyHostToDevice, stream), "copying the page in"))
-        return PPOCR_E_DEVICE;
-    const uint8_t *src = page_raw.as<uint8_t>();
+    const uint8_t *src = page;
+    if (!on_device) {
+        if (!page_raw.fit(raw, code)) return code;
+        if (!cuda_ok(cudaMemcpyAsync(page_raw.p, page, raw, cudaMemcpyHostToDevice, stream), "copying the page in"))
+            return PPOCR_E_DEVICE;
+        src = page_raw.as<uint8_t>();
+    }
     if (p.fit_width != w || p.fit_height != h || p.pad_top) {
         if (!page_fit.fit(p.width * p.height * 3, code)) return code;
         FitArgs fa{src, int(w), int(h), int(p.fit_width), int(p.fit_height), int(p.pad_top), page_fit.as<uint8_t>()};
         launch_fit_page(fa, stream);
+        launches++;
         src = page_fit.as<uint8_t>();
     }
     // the detector
@@ -216,6 +223,7 @@ int ppocr_reader::detect(const uint8_t *page, size_t w, size_t h, uint32_t timeo
     int rc = ppocr_det_input_hwc(src, p.width, p.height, dw, dh, opt.mean, opt.std, din, in_len, stream);
     if (rc) return rc;
     if ((rc = ppocr_model_enqueue_device(det))) return rc;
+    launches += 2 + ppocr_model_launches(det);  // input, network, and the mask below
     const float *prob = ppocr_model_lane_device_output(det, 0, 0, &out_len);
     if (!prob || out_len != dw * dh) return fail(PPOCR_E_UNSUPPORTED, "the detector's first output is not a map");
     if (!mask.fit(out_len, code) || !mask_host.fit(out_len, code)) return code;
@@ -290,6 +298,7 @@ int ppocr_reader::score_boxes(const std::vector<std::pair<size_t, Quad>> &cand, 
     ScoreArgs a{prob, int(det_w), pts.as<int2>(), boxes.as<ScoreBox>(),
                 reinterpret_cast<const ScoreWork *>(boxes.as<char>() + bytes_boxes), scores.as<ScoreOut>(), words};
     launch_box_scores(a, int(items), stream);
+    launches++;
     if (!cuda_ok(cudaGetLastError(), "launching the box scores")) return PPOCR_E_DEVICE;
     if (!cuda_ok(cudaMemcpyAsync(scores_host.p, scores.p, items * sizeof(ScoreOut), cudaMemcpyDeviceToHost,
                                  stream), "copying box scores out"))
@@ -415,6 +424,7 @@ int ppocr_reader::recognise(const Quad *quads, size_t n, uint32_t timeout_ms) {
         if (!cuda_ok(cudaGetLastError(), "launching the crops")) return PPOCR_E_DEVICE;
         int rc = ppocr_model_enqueue_device(rec);
         if (rc) return rc;
+        launches += 2 + ppocr_model_launches(rec);
         // the lanes' outputs lie back to back: one copy
         size_t first_len = 0, out_floats = 0;
         const float *out0 = ppocr_model_lane_device_output(rec, 0, 0, &first_len);
@@ -513,6 +523,16 @@ int ppocr_reader_detect(ppocr_reader *r, const uint8_t *page, size_t width, size
     if (width > (1u << 20) || height > (1u << 20)) return fail(PPOCR_E_SIZE, "page sides above 2^20");
     return r->detect(page, width, height, timeout_ms);
 }
+
+int ppocr_reader_detect_device(ppocr_reader *r, const uint8_t *page, size_t width, size_t height,
+                               uint32_t timeout_ms) {
+    set_last_error("");
+    if (!r || (!page && width && height)) return fail(PPOCR_E_ARG, "null argument");
+    if (width > (1u << 20) || height > (1u << 20)) return fail(PPOCR_E_SIZE, "page sides above 2^20");
+    return r->detect(page, width, height, timeout_ms, true);
+}
+
+size_t ppocr_reader_launches(const ppocr_reader *r) { return r ? r->launches : 0; }
 
 size_t ppocr_reader_box_count(const ppocr_reader *r) { return r ? r->found.size() : 0; }
 

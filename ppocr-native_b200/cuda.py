@@ -74,6 +74,9 @@ _SIG = {
     "ppocr_reader_page": (ctypes.POINTER(ctypes.c_uint8), [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t]),
     "ppocr_reader_detect": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
                                            ctypes.c_uint32]),
+    "ppocr_reader_detect_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                                  ctypes.c_size_t, ctypes.c_uint32]),
+    "ppocr_reader_launches": (ctypes.c_size_t, [ctypes.c_void_p]),
     "ppocr_reader_box_count": (ctypes.c_size_t, [ctypes.c_void_p]),
     "ppocr_reader_boxes": (ctypes.POINTER(ctypes.c_float), [ctypes.c_void_p]),
     "ppocr_reader_prepared": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_size_t),
@@ -535,6 +538,21 @@ class Reader:
         h, w = page.shape[:2]
         _check(lib().ppocr_reader_detect(self._h, page.ctypes.data, w, h, timeout_ms))
         return self.boxes()
+
+    def detect_ptr(self, page: int, width: int, height: int, on_device: bool = False,
+                   timeout_ms: int = 60_000) -> int:
+        """Detection of a page given by pointer (host memory, or device
+        memory with on_device); returns the number of boxes."""
+        f = lib().ppocr_reader_detect_device if on_device else lib().ppocr_reader_detect
+        _check(f(self._h, page, width, height, timeout_ms))
+        return lib().ppocr_reader_box_count(self._h)
+
+    def recognise_ptr(self, quads: int, n: int, timeout_ms: int = 60_000) -> None:
+        _check(lib().ppocr_reader_recognise(self._h, quads, n, timeout_ms))
+
+    @property
+    def launches(self) -> int:
+        return lib().ppocr_reader_launches(self._h)
 
     def boxes(self) -> np.ndarray:
         n = lib().ppocr_reader_box_count(self._h)

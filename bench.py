@@ -596,8 +596,11 @@ def run_ours(args, d: Dist) -> dict | None:
     # value: the pages already in HBM.
     d.barrier()
     torch.cuda.synchronize()
+    before = [r.host_times() for r in readers]
     with Clocks(device) as clocks:
         dev_s, dev_wall, dev_cpu, dev_lat, launches = read_pages(torch, readers, pool, total, True, main)
+    after = [r.host_times() for r in readers]
+    host_ms = {k: sum(a[k] - b[k] for a, b in zip(after, before)) / total * 1e3 for k in after[0]}
     d.barrier()
     # e2e: the pages in page-locked host memory, copied in by the reader.
     torch.cuda.synchronize()
@@ -611,9 +614,10 @@ def run_ours(args, d: Dist) -> dict | None:
     e2e, e2e_t = d.whole_job(total, e2e_s)
     page_bytes = pool.h * pool.w * 3
     # per rank: pages/s, median and max page latency, host CPU use (of all host threads)
+    host_keys = list(host_ms)
     per_rank = d.gather([total / dev_s, statistics.median(dev_lat), max(dev_lat),
                          dev_cpu / dev_wall / cpu_threads(), total / e2e_s, statistics.median(e2e_lat), max(e2e_lat),
-                         e2e_cpu / e2e_wall / cpu_threads()])
+                         e2e_cpu / e2e_wall / cpu_threads(), dev_cpu / total * 1e3] + [host_ms[k] for k in host_keys])
     extra = {}
     if d.rank == 0 and not args.quick:
         flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{device}")
@@ -676,7 +680,9 @@ def run_ours(args, d: Dist) -> dict | None:
         "gpu_launches": int(launches * total),
         "per_rank": [{"rank": i, "pages_per_s": v[0], "page_ms_median": v[1] * 1e3, "page_ms_max": v[2] * 1e3,
                       "host_cpu_busy": v[3], "e2e_pages_per_s": v[4], "e2e_page_ms_median": v[5] * 1e3,
-                      "e2e_page_ms_max": v[6] * 1e3, "e2e_host_cpu_busy": v[7]} for i, v in enumerate(per_rank)],
+                      "e2e_page_ms_max": v[6] * 1e3, "e2e_host_cpu_busy": v[7], "host_cpu_ms_per_page": v[8],
+                      "reader_host_ms_per_page": dict(zip(host_keys, v[9:])),
+                      "host_cores": cpu_threads()} for i, v in enumerate(per_rank)],
         "clocks": clocks.summary(),
     }
     if extra.get("probes"):

@@ -256,6 +256,11 @@ int ppocr_reader_set_options(ppocr_reader *reader, uint32_t options);
 /* The detector's probability map of the last detection (host memory,
  * capacity floats; *width x *height values). */
 int ppocr_reader_prob_map(ppocr_reader *reader, float *out, size_t capacity, size_t *width, size_t *height);
+/* Host seconds this reader has spent, summed over its calls, in: waits for
+ * the GPU, border following, box geometry (minimum-area boxes, scores'
+ * check, unclip, order), recogniser set-up (crop maps, lane sizes,
+ * descriptors), CTC decoding. */
+int ppocr_reader_host_times(const ppocr_reader *reader, double seconds[5]);
 /* Contours the GPU scored, and how many of those the host scored again in
  * the reference's summation order because their mean lay within the
  * parallel sum's error bound of box_thresh. */

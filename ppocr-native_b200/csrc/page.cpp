@@ -38,21 +38,29 @@ bool total_less(float a, float b) {
     return x < y;
 }
 
-// A foreground byte at or after `from` in row [from, end), word at a time.
-size_t next_foreground(const uint8_t *row, size_t from, size_t end) {
+// Per byte of a word of scan states (0..3): 0x80 where the byte is nonzero
+// (no byte reaches 0x81 when 0x7f is added, so nothing carries).
+inline uint64_t nonzero_bytes(uint64_t w) { return (w + 0x7f7f7f7f7f7f7f7full) & 0x8080808080808080ull; }
+
+// The next pixel at or after `from` in [from, end) of a frame row that can
+// start a border: foreground with background to its west or east (the only
+// starts of an outer or a hole border; background never changes during the
+// scan). Eight pixels at a time; `row` has a background byte before `from`
+// and after `end`.
+size_t next_start(const uint8_t *row, size_t from, size_t end) {
     size_t i = from;
-    while (i < end && (i & 7)) {
-        if (row[i]) return i;
-        i++;
-    }
-    while (i + 8 <= end) {
-        uint64_t w;
+    while (i + 9 <= end + 1) {
+        uint64_t w, wl, wr;
         std::memcpy(&w, row + i, 8);
-        if (w) break;
+        std::memcpy(&wl, row + i - 1, 8);
+        std::memcpy(&wr, row + i + 1, 8);
+        const uint64_t cand = nonzero_bytes(w) & ~(nonzero_bytes(wl) & nonzero_bytes(wr));
+        if (cand) return i + size_t(__builtin_ctzll(cand) >> 3);
         i += 8;
     }
-    while (i < end && !row[i]) i++;
-    return i;
+    for (; i < end; i++)
+        if (row[i] && (!row[i - 1] || !row[i + 1])) return i;
+    return end;
 }
 
 }  // namespace
@@ -66,12 +74,16 @@ void find_contours(const uint8_t *mask, size_t width, size_t height, Contours &o
     out.start.assign(1, 0);
     out.pts.clear();
     const size_t stride = width + 2;
-    s.state.assign(stride * (height + 2), BACKGROUND);
+    if (s.state.size() < stride * (height + 2)) s.state.resize(stride * (height + 2));
     uint8_t *state = s.state.data();
+    // the frame of background, then each row (one pass over the buffer)
+    std::memset(state, BACKGROUND, stride);
+    std::memset(state + (height + 1) * stride, BACKGROUND, stride);
     for (size_t y = 0; y < height; y++) {
-        uint8_t *dst = state + (y + 1) * stride + 1;
+        uint8_t *dst = state + (y + 1) * stride;
         const uint8_t *src = mask + y * width;
-        for (size_t x = 0; x < width; x++) dst[x] = src[x] ? UNSEEN : BACKGROUND;
+        dst[0] = dst[width + 1] = BACKGROUND;
+        for (size_t x = 0; x < width; x++) dst[x + 1] = src[x] ? UNSEEN : BACKGROUND;
     }
     long off[8];
     for (int d = 0; d < 8; d++) off[d] = STEP_DX[d] + STEP_DY[d] * long(stride);
@@ -81,7 +93,7 @@ void find_contours(const uint8_t *mask, size_t width, size_t height, Contours &o
     std::vector<Point> corners;
     for (size_t y = 1; y <= height; y++) {
         const uint8_t *row = state + y * stride;
-        size_t x = next_foreground(row, 1, width + 1);
+        size_t x = next_start(row, 1, width + 1);
         while (x <= width) {
             const size_t start = y * stride + x;
             const uint8_t here = state[start];
@@ -147,7 +159,7 @@ void find_contours(const uint8_t *mask, size_t width, size_t height, Contours &o
                     found.emplace_back(at, corners.size() - at);
                 }
             }
-            x = next_foreground(row, x + 1, width + 1);
+            x = next_start(row, x + 1, width + 1);
         }
     }
     out.pts.reserve(corners.size());

@@ -31,7 +31,7 @@ struct ScoreWork {
 
 // Rows of one contour a CTA scores: large contours are split over CTAs and
 // their partial sums added on the host in order.
-constexpr int SCORE_ROWS = 64;
+constexpr int SCORE_ROWS = 16;
 
 struct ScoreArgs {
     const float *prob;

@@ -151,21 +151,36 @@ struct ppocr_reader {
         if (ev) cudaEventDestroy(ev);
     }
 
-    // Wait for everything queued on the stream, at most timeout_ms (0: no limit).
+    // Host time by step (nanoseconds, summed over calls): waiting for the
+    // GPU, border following, box geometry, recogniser set-up, decoding.
+    enum { T_WAIT, T_CONTOURS, T_BOXES, T_PREP, T_DECODE, T_COUNT };
+    uint64_t t_ns[T_COUNT] = {0, 0, 0, 0, 0};
+    struct Clock {
+        uint64_t &acc;
+        std::chrono::steady_clock::time_point t0 = std::chrono::steady_clock::now();
+        explicit Clock(uint64_t &a) : acc(a) {}
+        ~Clock() {
+            acc += uint64_t(
+                std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t0).count());
+        }
+    };
+
+    // Wait for everything queued on the stream, at most timeout_ms (0: no
+    // limit). A few quick polls catch short waits; then the thread sleeps
+    // between polls, so readers waiting on the GPU leave the host cores to
+    // the readers doing page steps.
     int sync(uint32_t timeout_ms) {
+        Clock c(t_ns[T_WAIT]);
         if (!cuda_ok(cudaEventRecord(ev, stream), "recording a reader event")) return PPOCR_E_DEVICE;
         const auto start = std::chrono::steady_clock::now();
-        for (unsigned spin = 0;; spin++) {
+        for (unsigned poll = 0;; poll++) {
             const cudaError_t e = cudaEventQuery(ev);
             if (e == cudaSuccess) return PPOCR_OK;
             if (e != cudaErrorNotReady) return cuda_ok(e, "reading a page") ? PPOCR_OK : PPOCR_E_DEVICE;
             if (timeout_ms && std::chrono::steady_clock::now() - start > std::chrono::milliseconds(timeout_ms))
                 return fail(PPOCR_E_TIMEOUT, "the GPU did not finish the page within " + std::to_string(timeout_ms) +
                                                  " ms");
-            if (spin < 4000)
-                std::this_thread::yield();
-            else
-                std::this_thread::sleep_for(std::chrono::microseconds(20));
+            if (poll >= 8) std::this_thread::sleep_for(std::chrono::microseconds(poll < 64 ? 20 : 100));
         }
     }
 
@@ -238,11 +253,17 @@ int ppocr_reader::detect(const uint8_t *page, size_t w, size_t h, uint32_t timeo
     page_h = h;
     have_page = true;
     // border following and the first rejections on the host
-    page::find_contours(mask_host.as<uint8_t>(), dw, dh, contours, scratch);
+    {
+        Clock c(t_ns[T_CONTOURS]);
+        page::find_contours(mask_host.as<uint8_t>(), dw, dh, contours, scratch);
+    }
     std::vector<std::pair<size_t, Quad>> cand;
-    for (size_t i = 0; i < contours.size() && i < opt.max_candidates; i++) {
-        Quad q;
-        if (page::mini_box(contours.at(i), contours.len(i), q) >= 3.0f) cand.emplace_back(i, q);
+    {
+        Clock c(t_ns[T_BOXES]);
+        for (size_t i = 0; i < contours.size() && i < opt.max_candidates; i++) {
+            Quad q;
+            if (page::mini_box(contours.at(i), contours.len(i), q) >= 3.0f) cand.emplace_back(i, q);
+        }
     }
     if (!cand.empty() && (rc = score_boxes(cand, timeout_ms))) return rc;
     page::sort_boxes(found);
@@ -307,6 +328,7 @@ int ppocr_reader::score_boxes(const std::vector<std::pair<size_t, Quad>> &cand, 
     if (rc) return rc;
     bool prob_here = false;
     const ScoreOut *so = scores_host.as<ScoreOut>();
+    Clock clk(t_ns[T_BOXES]);
     for (size_t k = 0; k < cand.size(); k++) {
         ScoreOut o{0.0, 0.0, 0, 0};
         for (size_t j = first_item[k]; j < first_item[k + 1]; j++) {  // the slices in row order
@@ -357,6 +379,11 @@ int ppocr_reader::recognise(const Quad *quads, size_t n, uint32_t timeout_ms) {
         size_t cw, ch, width, rw, crop;
     };
     std::vector<Lane> all;
+    auto prep_start = std::chrono::steady_clock::now();
+    const auto prep_stop = [&] {
+        t_ns[T_PREP] += uint64_t(std::chrono::duration_cast<std::chrono::nanoseconds>(
+                                     std::chrono::steady_clock::now() - prep_start).count());
+    };
     for (size_t i = 0; i < n; i++) {
         Lane L;
         L.quad = i;
@@ -370,6 +397,7 @@ int ppocr_reader::recognise(const Quad *quads, size_t n, uint32_t timeout_ms) {
     const size_t per_run = ppocr_model_max_lanes(rec);
     int code = PPOCR_OK;
     for (size_t r0 = 0; r0 < all.size(); r0 += per_run) {
+        if (r0) prep_start = std::chrono::steady_clock::now();
         const size_t r1 = std::min(all.size(), r0 + per_run), k = r1 - r0;
         std::vector<std::pair<size_t, size_t>> sizes;
         std::vector<uint32_t> hw;
@@ -422,6 +450,7 @@ int ppocr_reader::recognise(const Quad *quads, size_t n, uint32_t timeout_ms) {
                         reinterpret_cast<const long *>(dd + off_rf), int(k), rec_px};
         launch_rec_lines(ra, stream);
         if (!cuda_ok(cudaGetLastError(), "launching the crops")) return PPOCR_E_DEVICE;
+        prep_stop();
         int rc = ppocr_model_enqueue_device(rec);
         if (rc) return rc;
         launches += 2 + ppocr_model_launches(rec);
@@ -440,6 +469,7 @@ int ppocr_reader::recognise(const Quad *quads, size_t n, uint32_t timeout_ms) {
         if ((rc = sync(timeout_ms))) return rc;
         if ((rc = ppocr_model_wait(rec, timeout_ms))) return rc;
         const float *ho = rec_host.as<float>();
+        Clock cd(t_ns[T_DECODE]);
         for (size_t j = 0; j < k; j++) {
             auto &out = reads[all[r0 + j].quad];
             out.second = page::ctc_decode(ho, lens[j] / 2, dict, out.first);
@@ -621,6 +651,12 @@ int ppocr_reader_prob_map(ppocr_reader *r, float *out, size_t capacity, size_t *
         !cuda_ok(cudaMemcpyAsync(out, prob, len * sizeof(float), cudaMemcpyDeviceToHost, r->stream), "copying the map") ||
         !cuda_ok(cudaStreamSynchronize(r->stream), "copying the map"))
         return PPOCR_E_DEVICE;
+    return PPOCR_OK;
+}
+
+int ppocr_reader_host_times(const ppocr_reader *r, double seconds[5]) {
+    if (!r || !seconds) return fail(PPOCR_E_ARG, "null argument");
+    for (int i = 0; i < ppocr_reader::T_COUNT; i++) seconds[i] = double(r->t_ns[i]) * 1e-9;
     return PPOCR_OK;
 }
 

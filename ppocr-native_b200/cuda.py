@@ -94,6 +94,7 @@ _SIG = {
     "ppocr_reader_set_options": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32]),
     "ppocr_reader_prob_map": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                              ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
+    "ppocr_reader_host_times": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "ppocr_reader_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_size_t),
                                           ctypes.POINTER(ctypes.c_size_t)]),
     "ppocr_find_contours": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
@@ -608,6 +609,12 @@ class Reader:
         out = np.empty((h.value, w.value), np.float32)
         _check(lib().ppocr_reader_prob_map(self._h, out.ctypes.data, out.size, ctypes.byref(w), ctypes.byref(h)))
         return out
+
+    def host_times(self) -> dict:
+        """Host seconds by step, summed over this reader's calls."""
+        out = np.zeros(5, np.float64)
+        _check(lib().ppocr_reader_host_times(self._h, out.ctypes.data))
+        return dict(zip(("wait", "contours", "boxes", "recogniser_setup", "decode"), out.tolist()))
 
     def stats(self) -> tuple[int, int]:
         a, b = ctypes.c_size_t(), ctypes.c_size_t()

@@ -113,9 +113,11 @@ def det_plan(seed: int = 0, std: float | None = 0.02, size: tuple[int, int] = DE
 
 
 def rec_plan(seed: int = 0, std: float | None = 0.02, width: int = 320, argmax: bool = True,
-             vocab: int = VOCAB) -> bytes:
+             vocab: int = VOCAB, logits: bool = False) -> bytes:
     """Benchmark config 3's recogniser; input HWC 48 x W x 3, output
-    `[T][2]` = (best class as f32, 1 / sum exp) with T = ceil(W / 8)."""
+    `[T][2]` = (best class as f32, 1 / sum exp) with T = ceil(W / 8). With
+    `logits` the network ends in the head's logits instead: a 1x1 conv
+    120 -> vocab, output `[T][vocab]` (the tap the logits parity test reads)."""
     b = Builder(REC_HEIGHT, width, 3, np.random.default_rng(seed), std)
     x = b.conv(0, 48, k=3, s=2, act="swish")  # 24 x W/2
     x = _block(b, x, 96, 3, 1, False)
@@ -135,7 +137,7 @@ def rec_plan(seed: int = 0, std: float | None = 0.02, width: int = 320, argmax: 
         m = b.conv(b.conv(n, 240, act="gelu"), 120)
         x = b.add(x, m)
     x = b.layernorm(x)
-    out = b.ctc(x, vocab, argmax=argmax)
+    out = b.conv(x, vocab) if logits else b.ctc(x, vocab, argmax=argmax)
     return b.build([out])
 
 

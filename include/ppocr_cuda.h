@@ -45,7 +45,9 @@ enum {
 enum {
     PPOCR_OPT_NO_FUSION = 1, /* run every plan operation as its own kernel */
     PPOCR_OPT_NO_GRAPH = 2,  /* launch kernels directly instead of replaying a CUDA graph */
-    PPOCR_OPT_NO_TENSOR_CORES = 4 /* every contraction on the FP32 cores: the reference CPU engine's bits */
+    PPOCR_OPT_NO_TENSOR_CORES = 4, /* every contraction on the FP32 cores: the reference CPU engine's bits */
+    PPOCR_OPT_THROUGHPUT = 8       /* size grids for several runs in flight: small tensor-core layers take few
+                                      SMs (same results, longer latency alone, more pages per second together) */
 };
 
 /* Number of CUDA devices this process can use (0 when none). */
@@ -79,7 +81,9 @@ int ppocr_model_set_input_size(ppocr_model *model, uint32_t height, uint32_t wid
 int ppocr_model_set_sizes(ppocr_model *model, const uint32_t *hw_pairs, size_t lanes);
 
 /* The lane's HWC input in page-locked host memory, to be filled before each
- * run (`GpuModel::lane_input_mut`, :240-246); *len receives its floats. */
+ * run (`GpuModel::lane_input_mut`, :240-246); *len receives its floats. Its
+ * contents after ppocr_model_set_sizes are unspecified (buffers are kept
+ * across sizes, never cleared). */
 float *ppocr_model_lane_input(ppocr_model *model, size_t lane, size_t *len);
 /* Output `index` of the lane's last run (`GpuModel::lane_output`, :255-259). */
 const float *ppocr_model_lane_output(const ppocr_model *model, size_t lane, size_t index, size_t *len);

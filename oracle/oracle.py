@@ -48,6 +48,7 @@ def lib() -> ctypes.CDLL:
         L.orc_output_len.restype = ctypes.c_size_t
         L.orc_output_len.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
         L.orc_run.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        L.orc_set_fast.argtypes = [ctypes.c_int]
         L.orc_exp_neg.restype = ctypes.c_float
         L.orc_exp_neg.argtypes = [ctypes.c_float]
         L.orc_activation.restype = ctypes.c_float
@@ -101,6 +102,11 @@ class Oracle:
         if lib().orc_run(self._p, x.ctypes.data, ptrs, int(threads)) != 0:
             raise OracleError("oracle run failed")
         return outs
+
+
+def set_fast(on: bool) -> None:
+    """The register-tiled timed path (same bits as the plain loops)."""
+    lib().orc_set_fast(1 if on else 0)
 
 
 def exp_neg(z: float) -> float:

@@ -16,6 +16,7 @@
  */
 #include "ppocr_oracle.h"
 
+#include <immintrin.h>
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -52,6 +53,10 @@ struct orc_plan {
     orc_op *ops;
     float *weights;
     size_t nweights;
+    /* buffers kept from run to run (the reference's arena is allocated once
+     * per size, src/engine/schedule.rs:528-620), grown when a size needs more */
+    float **kept;
+    size_t *kept_n;
 };
 
 /* ---------------------------------------------------------------- errors */
@@ -142,6 +147,7 @@ float orc_activation(int code, float v) {
 
 static void tail(float *y, size_t n, int code) {
     if (code == A_NONE) return;
+#pragma omp parallel for schedule(static) if (n > 65536)
     for (size_t i = 0; i < n; i++) y[i] = orc_activation(code, y[i]);
 }
 
@@ -423,6 +429,9 @@ bad:
 
 void orc_free(orc_plan *p) {
     if (!p) return;
+    if (p->kept)
+        for (size_t b = 0; b < p->nbuf; b++) free(p->kept[b]);
+    free(p->kept); free(p->kept_n);
     free(p->outputs); free(p->out_n); free(p->pool); free(p->ops); free(p->weights);
     free(p);
 }
@@ -455,17 +464,112 @@ static int bias_first(const orc_op *op, size_t ox) {
     return ox < op->ow - op->ow % 4;
 }
 
+/* The timed CPU path (bench.py's reference arm): register-tiled AVX2+FMA
+ * loops with the reference tier-3 engine's tile shape (6 pixels x 16 output
+ * columns in 12 ymm accumulators, kernels/pointwise.rs:429 pw_p6o16_avx2) for
+ * the dense convolutions and the CTC head's logits. Every output keeps its
+ * own chain of fused multiply-adds in the same order as the loops below
+ * (bias first or last per bias_first, taps in row-major order, channels in
+ * order), so the results are the same bits; tests/test_oracle.py checks it.
+ * Off by default: the parity tests use the plain loops. */
+static int g_fast = 0;
+void orc_set_fast(int on) { g_fast = on; }
+
+/* Whether the 6 output pixels from ox on all read every horizontal tap
+ * inside the image (their ix run is monotonic in ox). */
+static int row_interior(const orc_op *op, size_t ox) {
+    long first = (long)(ox * op->sw) - op->pl, last = (long)((ox + 5) * op->sw + op->kw - 1) - op->pl;
+    return ox + 6 <= op->ow && first >= 0 && last < (long)op->iw;
+}
+
+/* Six interior pixels of one output row, output columns o0 .. o0 + 8 * NV,
+ * NV = 2 (16 columns) or 1 (8). */
+static inline void conv_tile6(const orc_op *op, const float *w, const float *b, const float *x, const float *x2,
+                              float *y, long oy, size_t ox, size_t o0, int nv) {
+    const size_t co = op->oc, ch = op->ic + op->n2;
+    __m256 acc[6][2];
+    int first[6];
+    for (int r = 0; r < 6; r++) {
+        first[r] = bias_first(op, ox + r);
+        for (int v = 0; v < nv; v++)
+            acc[r][v] = (b && first[r]) ? _mm256_loadu_ps(b + o0 + 8 * v) : _mm256_setzero_ps();
+    }
+    for (size_t ky = 0; ky < op->kh; ky++) {
+        long iy = oy * (long)op->sh + (long)ky - op->pt;
+        if (iy < 0 || iy >= (long)op->ih) continue;
+        for (size_t kx = 0; kx < op->kw; kx++) {
+            const float *tap = w + (ky * op->kw + kx) * ch * co + o0;
+            const float *px[6], *px2[6];
+            for (int r = 0; r < 6; r++) {
+                size_t ix = (ox + r) * op->sw + kx - op->pl;
+                px[r] = x + ((size_t)iy * op->iw + ix) * op->ic;
+                px2[r] = op->n2 ? x2 + ((size_t)iy * op->iw + ix) * op->n2 : NULL;
+            }
+            for (size_t i = 0; i < op->ic; i++) {
+                const float *row = tap + i * co;
+                __m256 w0 = _mm256_loadu_ps(row), w1 = nv > 1 ? _mm256_loadu_ps(row + 8) : w0;
+                for (int r = 0; r < 6; r++) {
+                    __m256 xv = _mm256_broadcast_ss(px[r] + i);
+                    acc[r][0] = _mm256_fmadd_ps(w0, xv, acc[r][0]);
+                    if (nv > 1) acc[r][1] = _mm256_fmadd_ps(w1, xv, acc[r][1]);
+                }
+            }
+            for (size_t i = 0; i < op->n2; i++) {
+                const float *row = tap + (op->ic + i) * co;
+                __m256 w0 = _mm256_loadu_ps(row), w1 = nv > 1 ? _mm256_loadu_ps(row + 8) : w0;
+                for (int r = 0; r < 6; r++) {
+                    __m256 xv = _mm256_broadcast_ss(px2[r] + i);
+                    acc[r][0] = _mm256_fmadd_ps(w0, xv, acc[r][0]);
+                    if (nv > 1) acc[r][1] = _mm256_fmadd_ps(w1, xv, acc[r][1]);
+                }
+            }
+        }
+    }
+    for (int r = 0; r < 6; r++) {
+        float *out = y + ((size_t)oy * op->ow + ox + r) * co + o0;
+        for (int v = 0; v < nv; v++) {
+            __m256 a = acc[r][v];
+            if (b && !first[r]) a = _mm256_add_ps(a, _mm256_loadu_ps(b + o0 + 8 * v));
+            _mm256_storeu_ps(out + 8 * v, a);
+        }
+    }
+}
+
+static void conv_pixel(const orc_plan *p, const orc_op *op, const float *x, const float *x2, float *y, long oy,
+                       size_t ox);
+
+static void conv_fast(const orc_plan *p, const orc_op *op, const float *x, const float *x2, float *y) {
+    const float *w = W(p, op->w0), *b = op->b1 ? W(p, op->b0) : NULL;
+    const size_t co = op->oc;
+    long rows = (long)op->oh;
+#pragma omp parallel for schedule(static)
+    for (long oy = 0; oy < rows; oy++) {
+        size_t ox = 0;
+        while (ox < op->ow) {
+            if (row_interior(op, ox)) {
+                size_t o0 = 0;
+                for (; o0 + 16 <= co; o0 += 16) conv_tile6(op, w, b, x, x2, y, oy, ox, o0, 2);
+                for (; o0 + 8 <= co; o0 += 8) conv_tile6(op, w, b, x, x2, y, oy, ox, o0, 1);
+                for (int r = 0; r < 6; r++) tail(y + ((size_t)oy * op->ow + ox + r) * co, co, op->fused);
+                ox += 6;
+            } else {
+                conv_pixel(p, op, x, x2, y, oy, ox);
+                ox++;
+            }
+        }
+    }
+}
+
 /* Dense convolution of any window over the channel concatenation of x (ic
  * channels) and x2 (n2 channels): kernels/dense.rs:20-141 and the stem path
  * conv.rs:146-236. Weights [kh][kw][ic+n2][oc]; padded taps are skipped (the
  * reference multiplies them by zeros, which leaves every sum unchanged). */
-static void conv(const orc_plan *p, const orc_op *op, const float *x, const float *x2, float *y) {
+static void conv_pixel(const orc_plan *p, const orc_op *op, const float *x, const float *x2, float *y, long oy,
+                       size_t ox) {
     const float *w = W(p, op->w0), *b = op->b1 ? W(p, op->b0) : NULL;
     size_t co = op->oc, ch = op->ic + op->n2;
-    long rows = (long)op->oh;
-#pragma omp parallel for schedule(static)
-    for (long oy = 0; oy < rows; oy++) {
-        for (size_t ox = 0; ox < op->ow; ox++) {
+    {
+        {
             float *acc = y + ((size_t)oy * op->ow + ox) * co;
             int first = bias_first(op, ox);
             for (size_t o = 0; o < co; o++) acc[o] = (b && first) ? b[o] : 0.0f;
@@ -499,12 +603,75 @@ static void conv(const orc_plan *p, const orc_op *op, const float *x, const floa
     }
 }
 
+static void conv(const orc_plan *p, const orc_op *op, const float *x, const float *x2, float *y) {
+    if (g_fast && op->oc % 8 == 0) {
+        conv_fast(p, op, x, x2, y);
+        return;
+    }
+    long rows = (long)op->oh;
+#pragma omp parallel for schedule(static)
+    for (long oy = 0; oy < rows; oy++)
+        for (size_t ox = 0; ox < op->ow; ox++) conv_pixel(p, op, x, x2, y, oy, ox);
+}
+
 /* Depthwise convolution: conv.rs:244-339, kernels/depthwise.rs:12-45 —
  * bias first, taps in row-major order, one fused multiply-add per tap. */
+/* The timed path's depthwise tile: six interior pixels of a row, eight
+ * channels, the accumulators in registers, the same chain per output. */
+static inline void dw_tile6(const orc_op *op, const float *w, const float *b, const float *x, float *y, long oy,
+                            size_t ox, size_t c0) {
+    const size_t c = op->oc;
+    __m256 acc[6];
+    for (int r = 0; r < 6; r++) acc[r] = b ? _mm256_loadu_ps(b + c0) : _mm256_setzero_ps();
+    for (size_t ky = 0; ky < op->kh; ky++) {
+        long iy = oy * (long)op->sh + (long)ky - op->pt;
+        if (iy < 0 || iy >= (long)op->ih) continue;
+        const float *xrow = x + (size_t)iy * op->iw * c + c0;
+        for (size_t kx = 0; kx < op->kw; kx++) {
+            __m256 wv = _mm256_loadu_ps(w + (ky * op->kw + kx) * c + c0);
+            for (int r = 0; r < 6; r++) {
+                size_t ix = (ox + r) * op->sw + kx - op->pl;
+                acc[r] = _mm256_fmadd_ps(wv, _mm256_loadu_ps(xrow + ix * c), acc[r]);
+            }
+        }
+    }
+    for (int r = 0; r < 6; r++) _mm256_storeu_ps(y + ((size_t)oy * op->ow + ox + r) * c + c0, acc[r]);
+}
+
 static void dwconv(const orc_plan *p, const orc_op *op, const float *x, float *y) {
     const float *w = W(p, op->w0), *b = op->b1 ? W(p, op->b0) : NULL;
     size_t c = op->oc;
     long rows = (long)op->oh;
+    if (g_fast && c % 8 == 0) {
+#pragma omp parallel for schedule(static)
+        for (long oy = 0; oy < rows; oy++) {
+            size_t ox = 0;
+            while (ox < op->ow) {
+                if (row_interior(op, ox)) {
+                    for (size_t c0 = 0; c0 < c; c0 += 8) dw_tile6(op, w, b, x, y, oy, ox, c0);
+                    for (int r = 0; r < 6; r++) tail(y + ((size_t)oy * op->ow + ox + r) * c, c, op->fused);
+                    ox += 6;
+                    continue;
+                }
+                float *acc = y + ((size_t)oy * op->ow + ox) * c;
+                for (size_t k = 0; k < c; k++) acc[k] = b ? b[k] : 0.0f;
+                for (size_t ky = 0; ky < op->kh; ky++) {
+                    long iy = oy * (long)op->sh + (long)ky - op->pt;
+                    if (iy < 0 || iy >= (long)op->ih) continue;
+                    for (size_t kx = 0; kx < op->kw; kx++) {
+                        long ix = (long)(ox * op->sw + kx) - op->pl;
+                        if (ix < 0 || ix >= (long)op->iw) continue;
+                        const float *tap = w + (ky * op->kw + kx) * c;
+                        const float *px = x + ((size_t)iy * op->iw + (size_t)ix) * c;
+                        for (size_t k = 0; k < c; k++) acc[k] = fmaf(tap[k], px[k], acc[k]);
+                    }
+                }
+                tail(acc, c, op->fused);
+                ox++;
+            }
+        }
+        return;
+    }
 #pragma omp parallel for schedule(static)
     for (long oy = 0; oy < rows; oy++) {
         for (size_t ox = 0; ox < op->ow; ox++) {
@@ -651,8 +818,69 @@ static void ctc_head(const orc_plan *p, const orc_op *op, const float *x, float 
     size_t npanels = (vocab + 15) / 16;
     const float *w = W(p, op->w0), *b = W(p, op->b0);
     long tl = (long)t;
+    /* the timed path: groups of six time steps, logits of a panel for all
+     * six in registers (the same chain per logit), then each step's update */
+    long groups = g_fast ? tl / 6 : 0;
 #pragma omp parallel for schedule(static)
-    for (long pp = 0; pp < tl; pp++) {
+    for (long gi = 0; gi < groups; gi++) {
+        float m[6][8], sum[6][8], best[6][8], logits[6][16];
+        for (int r = 0; r < 6; r++)
+            for (int l = 0; l < 8; l++) { m[r][l] = -INFINITY; sum[r][l] = 0.0f; best[r][l] = 0.0f; }
+        const float *xv = x + (size_t)(gi * 6) * ci;
+        for (size_t j = 0; j < npanels; j++) {
+            const float *panel = w + j * ci * 16;
+            __m256 acc[6][2];
+            for (int r = 0; r < 6; r++) {
+                acc[r][0] = _mm256_loadu_ps(b + j * 16);
+                acc[r][1] = _mm256_loadu_ps(b + j * 16 + 8);
+            }
+            for (size_t i = 0; i < ci; i++) {
+                __m256 w0 = _mm256_loadu_ps(panel + i * 16), w1 = _mm256_loadu_ps(panel + i * 16 + 8);
+                for (int r = 0; r < 6; r++) {
+                    __m256 xb = _mm256_broadcast_ss(xv + (size_t)r * ci + i);
+                    acc[r][0] = _mm256_fmadd_ps(w0, xb, acc[r][0]);
+                    acc[r][1] = _mm256_fmadd_ps(w1, xb, acc[r][1]);
+                }
+            }
+            for (int r = 0; r < 6; r++) {
+                _mm256_storeu_ps(logits[r], acc[r][0]);
+                _mm256_storeu_ps(logits[r] + 8, acc[r][1]);
+                for (int l = 0; l < 8; l++) {
+                    float a0 = logits[r][l], a1 = logits[r][8 + l], mm = m[r][l];
+                    float top = a0 > a1 ? a0 : a1;
+                    float grown = mm > top ? mm : top;
+                    float s = sum[r][l] * orc_exp_neg(mm - grown);
+                    s += orc_exp_neg(a0 - grown);
+                    s += orc_exp_neg(a1 - grown);
+                    m[r][l] = grown; sum[r][l] = s;
+                    if (top > mm) best[r][l] = (float)(j * 16 + l + (a1 > a0 ? 8 : 0));
+                }
+                if (probs) {
+                    size_t n = vocab - j * 16 < 16 ? vocab - j * 16 : 16;
+                    memcpy(y + (size_t)(gi * 6 + r) * vocab + j * 16, logits[r], n * sizeof(float));
+                }
+            }
+        }
+        for (int r = 0; r < 6; r++) {
+            long pp = gi * 6 + r;
+            float mx = -INFINITY;
+            for (int l = 0; l < 8; l++) mx = fmaxf(mx, m[r][l]);
+            float total = 0.0f;
+            for (int l = 0; l < 8; l++) total += sum[r][l] * orc_exp_neg(m[r][l] - mx);
+            float rr = 1.0f / total;
+            if (probs) {
+                for (size_t k = 0; k < vocab; k++)
+                    y[(size_t)pp * vocab + k] = orc_exp_neg(y[(size_t)pp * vocab + k] - mx) * rr;
+            } else {
+                float bc = INFINITY;
+                for (int l = 0; l < 8; l++) if (m[r][l] == mx && best[r][l] < bc) bc = best[r][l];
+                y[2 * pp] = bc;
+                y[2 * pp + 1] = rr;
+            }
+        }
+    }
+#pragma omp parallel for schedule(static)
+    for (long pp = groups * 6; pp < tl; pp++) {
         float m[8], sum[8], best[8], logits[16];
         for (int l = 0; l < 8; l++) { m[l] = -INFINITY; sum[l] = 0.0f; best[l] = 0.0f; }
         const float *xv = x + (size_t)pp * ci;
@@ -732,11 +960,20 @@ int orc_run(orc_plan *p, const float *input, float *const *outputs, int threads)
 #else
     (void)threads;
 #endif
-    float **buf = calloc(p->nbuf, sizeof(float *));
-    if (!buf) return -1;
+    if (!p->kept) {
+        p->kept = calloc(p->nbuf, sizeof(float *));
+        p->kept_n = calloc(p->nbuf, sizeof(size_t));
+        if (!p->kept || !p->kept_n) return -1;
+    }
+    float **buf = p->kept;
     int rc = 0;
     for (size_t b = 0; b < p->nbuf; b++) {
-        buf[b] = malloc((p->pool[b] ? p->pool[b] : 1) * sizeof(float));
+        const size_t need = p->pool[b] ? p->pool[b] : 1;
+        if (p->kept_n[b] < need) {
+            free(buf[b]);
+            buf[b] = malloc(need * sizeof(float));
+            p->kept_n[b] = buf[b] ? need : 0;
+        }
         if (!buf[b]) { rc = -1; goto done; }
     }
     memcpy(buf[p->slot], input, orc_input_len(p) * sizeof(float));
@@ -749,16 +986,19 @@ int orc_run(orc_plan *p, const float *input, float *const *outputs, int threads)
         case K_CONV: conv(p, op, x, x2, y); break;
         case K_DWCONV: dwconv(p, op, x, y); break;
         case K_ADD: /* conv.rs:74-79 */
+#pragma omp parallel for schedule(static)
             for (size_t k = 0; k < n; k++) y[k] = x[k] + x2[k];
             tail(y, n, op->fused);
             break;
         case K_MAXPOOL: maxpool(op, x, y); break;
         case K_AVGPOOL: avgpool(op, x, y); break;
         case K_CHANNELMUL: /* kernels/elementwise.rs:178-200 */
+#pragma omp parallel for schedule(static)
             for (size_t px = 0; px < op->oh * op->ow; px++)
                 for (size_t k = 0; k < op->oc; k++) y[px * op->oc + k] = x[px * op->oc + k] * x2[k];
             break;
         case K_CONCATC: /* layers.rs:375-381 */
+#pragma omp parallel for schedule(static)
             for (size_t px = 0; px < op->oh * op->ow; px++) {
                 memcpy(y + px * op->oc, x + px * op->ic, op->ic * sizeof(float));
                 memcpy(y + px * op->oc + op->ic, x2 + px * op->n2, op->n2 * sizeof(float));
@@ -770,6 +1010,7 @@ int orc_run(orc_plan *p, const float *input, float *const *outputs, int threads)
         case K_CTCHEAD: ctc_head(p, op, x, y, 1); break;
         case K_CTCARGMAX: ctc_head(p, op, x, y, 0); break;
         case K_UPSAMPLE: case K_UPSAMPLEADD: /* layers.rs:526-565 */
+#pragma omp parallel for schedule(static)
             for (size_t oy = 0; oy < op->oh; oy++)
                 for (size_t ox = 0; ox < op->ow; ox++) {
                     const float *src = x + ((oy / op->sh) * op->iw + ox / op->sw) * op->oc;
@@ -787,8 +1028,6 @@ int orc_run(orc_plan *p, const float *input, float *const *outputs, int threads)
     }
     for (size_t k = 0; k < p->nout; k++) memcpy(outputs[k], buf[p->outputs[k]], p->out_n[k] * sizeof(float));
 done:
-    for (size_t b = 0; b < p->nbuf; b++) free(buf[b]);
-    free(buf);
     return rc;
 }
 

@@ -40,6 +40,10 @@ size_t orc_output_len(const orc_plan *p, size_t k);
  * thread in a fixed order, so any thread count gives the same bits. */
 int orc_run(orc_plan *p, const float *input, float *const *outputs, int threads);
 
+/* The timed CPU path on or off (register-tiled AVX2+FMA loops that give the
+ * same bits as the plain ones); off by default. */
+void orc_set_fast(int on);
+
 /* Scalar definitions, exposed for the f64 checks. */
 float orc_exp_neg(float z);
 float orc_activation(int code, float x);

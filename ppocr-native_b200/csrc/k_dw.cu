@@ -8,6 +8,10 @@
 // depthwise outputs of BM consecutive pixels for every channel into shared
 // memory, then runs the pointwise GEMM over them for every output channel:
 // the depthwise map never reaches HBM.
+#include <algorithm>
+#include <cstdint>
+#include <mutex>
+
 #include "devmath.cuh"
 #include "kernels.hpp"
 
@@ -380,6 +384,160 @@ int run_dw_pw(const DwPwArgs &a, cudaStream_t s) {
     return 1;
 }
 
+
+// ---------------------------------------------------------------- row tiles
+
+constexpr int TILE_THREADS = 256;
+
+// Fused depthwise -> pointwise for narrow layers, by row tiles. A block
+// keeps both layers' weights in shared memory for its whole life and walks
+// tiles of TP consecutive output pixels of one row (TP * N = 256 * OPT):
+//  1. the depthwise outputs of the tile, four channels per thread, taps read
+//     through L1 (neighbouring outputs share them), into shared memory
+//     [pixel][c] (row stride c + 1: the pointwise reads are conflict-free);
+//  2. the pointwise outputs, OPT consecutive channels of one pixel per
+//     thread, each a chain of c fused multiply-adds in channel order from
+//     shared memory, then bias (first or last, as the reference's tiles put
+//     it), activation, residual, and 16-byte stores: a warp writes whole
+//     consecutive pixels.
+// The depthwise map never leaves the chip. Every output is formed in the
+// reference's order (depthwise: bias, then the taps inside the image in
+// kernel row-major order; pointwise: the channel chain), so the results are
+// the exact FP32 kernels' bits; QUICK selects the tensor-core mode's
+// activation quotient.
+template <int K, int S, int OPT, bool QUICK>
+__global__ void __launch_bounds__(TILE_THREADS) dwpw_tile_kernel(const DwPwArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    const DwArgs &d = a.dw;
+    const int C = d.c, N = a.oc, tid = threadIdx.x;
+    const int TP = TILE_THREADS * OPT / N, XS = C + 1, groups = N / OPT;
+    float *wpw = sm;              // [C][N]
+    float *wdw = wpw + C * N;     // [K * K][C]
+    float *bdw = wdw + K * K * C; // [C]
+    float *bpw = bdw + C;         // [N]
+    float *xs = bpw + N;          // [TP][C + 1]
+    for (int i = tid; i < C * N; i += TILE_THREADS) wpw[i] = __ldg(a.w2 + i);
+    for (int i = tid; i < K * K * C; i += TILE_THREADS) wdw[i] = __ldg(d.w + i);
+    for (int i = tid; i < C; i += TILE_THREADS) bdw[i] = d.b ? __ldg(d.b + i) : 0.0f;
+    for (int i = tid; i < N; i += TILE_THREADS) bpw[i] = a.b2 ? __ldg(a.b2 + i) : 0.0f;
+    __syncthreads();
+    const int cg = C / 4;
+    const bool first = a.bias_mode2 == BIAS_FIRST;
+    const long tiles = a.rows * a.segs;
+    for (long t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const long r = t / a.segs;
+        const int seg = int(t - r * a.segs);
+        const LaneInfo &L = d.lanes[d.nl > 1 ? find_row_lane(d.lanes, d.nl, r) : 0];
+        const int ow = __ldg(&L.ow), ox0 = seg * TP;
+        if (ox0 >= ow) continue;  // the whole block: this lane's row is shorter
+        const int oy = int(r - __ldg(&L.row0)), ih = __ldg(&L.ih), iw = __ldg(&L.iw);
+        const int np = min(TP, ow - ox0);
+        const float *xn = d.x + __ldg(&L.ipix0) * C;
+        // 1. depthwise
+        for (int item = tid; item < np * cg; item += TILE_THREADS) {
+            const int p = item / cg, c = (item - p * cg) * 4;
+            const int ox = ox0 + p;
+            float v0 = bdw[c], v1 = bdw[c + 1], v2 = bdw[c + 2], v3 = bdw[c + 3];
+#pragma unroll
+            for (int ky = 0; ky < K; ky++) {
+                const int iy = oy * S - d.pt + ky;
+                if (iy < 0 || iy >= ih) continue;
+                const float *row = xn + long(iy) * iw * C + c;
+#pragma unroll
+                for (int kx = 0; kx < K; kx++) {
+                    const int ix = ox * S - d.pl + kx;
+                    if (ix < 0 || ix >= iw) continue;
+                    const float4 q = __ldg(reinterpret_cast<const float4 *>(row + long(ix) * C));
+                    const float4 w = *reinterpret_cast<const float4 *>(wdw + (ky * K + kx) * C + c);
+                    v0 = ffma(w.x, q.x, v0);
+                    v1 = ffma(w.y, q.y, v1);
+                    v2 = ffma(w.z, q.z, v2);
+                    v3 = ffma(w.w, q.w, v3);
+                }
+            }
+            float *xp = xs + p * XS + c;
+            xp[0] = activate<QUICK>(d.act, v0);
+            xp[1] = activate<QUICK>(d.act, v1);
+            xp[2] = activate<QUICK>(d.act, v2);
+            xp[3] = activate<QUICK>(d.act, v3);
+        }
+        __syncthreads();
+        // 2. pointwise
+        const int p = tid / groups, n0 = (tid - p * groups) * OPT;
+        if (p < np) {
+            float acc[OPT];
+#pragma unroll
+            for (int j = 0; j < OPT; j++) acc[j] = first ? bpw[n0 + j] : 0.0f;
+            const float *xp = xs + p * XS;
+#pragma unroll 4
+            for (int k = 0; k < C; k++) {
+                const float x = xp[k];
+                const float4 *wk = reinterpret_cast<const float4 *>(wpw + k * N + n0);
+#pragma unroll
+                for (int j4 = 0; j4 < OPT / 4; j4++) {
+                    const float4 w = wk[j4];
+                    acc[4 * j4] = ffma(w.x, x, acc[4 * j4]);
+                    acc[4 * j4 + 1] = ffma(w.y, x, acc[4 * j4 + 1]);
+                    acc[4 * j4 + 2] = ffma(w.z, x, acc[4 * j4 + 2]);
+                    acc[4 * j4 + 3] = ffma(w.w, x, acc[4 * j4 + 3]);
+                }
+            }
+            const long m = __ldg(&L.pix0) + long(oy) * ow + ox0 + p;
+#pragma unroll
+            for (int j4 = 0; j4 < OPT / 4; j4++) {
+                float v[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    float u = acc[4 * j4 + e];
+                    if (!first && a.b2) u = fadd(u, bpw[n0 + 4 * j4 + e]);
+                    v[e] = activate<QUICK>(a.act2, u);
+                }
+                if (a.res) {
+                    const float4 q = __ldg(reinterpret_cast<const float4 *>(a.res + m * N + n0 + 4 * j4));
+                    v[0] = activate<QUICK>(a.act3, fadd(v[0], q.x));
+                    v[1] = activate<QUICK>(a.act3, fadd(v[1], q.y));
+                    v[2] = activate<QUICK>(a.act3, fadd(v[2], q.z));
+                    v[3] = activate<QUICK>(a.act3, fadd(v[3], q.w));
+                }
+                *reinterpret_cast<float4 *>(a.y + m * N + n0 + 4 * j4) = make_float4(v[0], v[1], v[2], v[3]);
+            }
+        }
+        __syncthreads();  // the tile's depthwise outputs are read; the next tile may write them
+    }
+}
+
+int tile_opt(int N) { return N == 24 ? 12 : 24; }
+
+size_t dwpw_tile_smem(const DwPwArgs &a) {
+    const int C = a.dw.c, N = a.oc, K = a.dw.kh, TP = TILE_THREADS * tile_opt(N) / N;
+    return sizeof(float) * (size_t(C) * N + size_t(K) * K * C + C + N + size_t(TP) * (C + 1));
+}
+
+template <int K, int S, int OPT, bool QUICK>
+int run_dwpw_tile(const DwPwArgs &a, cudaStream_t s) {
+    static int per_sm[2] = {0, 0};  // blocks per SM at the last smem size, found once per size
+    static size_t at_smem = 0;
+    static std::mutex mu;
+    const size_t smem = dwpw_tile_smem(a);
+    int resident;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (at_smem != smem || !per_sm[0]) {
+            int n = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, dwpw_tile_kernel<K, S, OPT, QUICK>, TILE_THREADS,
+                                                              smem) != cudaSuccess || n < 1)
+                n = 1;
+            per_sm[0] = n;
+            at_smem = smem;
+        }
+        resident = per_sm[0];
+    }
+    const long tiles = a.rows * a.segs;
+    const long blocks = std::max(1L, std::min(tiles, long(g_sms) * resident));
+    dwpw_tile_kernel<K, S, OPT, QUICK><<<unsigned(blocks), TILE_THREADS, smem, s>>>(a);
+    return 1;
+}
+
 }  // namespace
 
 int launch_dw(const DwArgs &a, cudaStream_t s) {
@@ -408,6 +566,14 @@ void allow_smem() {
     cudaFuncSetAttribute(dw_pw_kernel<TM, TN, TX, TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
 }
 
+template <int K, int S>
+void allow_tile() {
+    cudaFuncSetAttribute(dwpw_tile_kernel<K, S, 12, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    cudaFuncSetAttribute(dwpw_tile_kernel<K, S, 12, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    cudaFuncSetAttribute(dwpw_tile_kernel<K, S, 24, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    cudaFuncSetAttribute(dwpw_tile_kernel<K, S, 24, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+}
+
 // Raise the dynamic shared-memory ceiling of every fused instance; once per
 // device, with that device current.
 void configure_dw_kernels() {
@@ -431,12 +597,46 @@ void configure_dw_kernels() {
     allow_smem<8, 4, 32, 8>();
     allow_smem<8, 3, 32, 8>();
     allow_smem<8, 2, 32, 8>();
+    allow_tile<3, 1>();
+    allow_tile<3, 2>();
+    allow_tile<5, 1>();
+    allow_tile<5, 2>();
 }
 
 bool dw_pw_supported(const DwPwArgs &a) {
     // The depthwise tile of 128 (or 64) pixels x C channels must fit.
     size_t smem = a.dw.c <= 192 ? dw_pw_smem<8, 4, 16, 16>(a.dw.c) : dw_pw_smem<8, 4, 32, 8>(a.dw.c);
     return smem <= 200 * 1024;
+}
+
+
+bool dwpw_tile_supported(const DwPwArgs &a) {
+    const DwArgs &d = a.dw;
+    const bool shape = (d.c == 24 || d.c == 48 || d.c == 96) && (a.oc == 24 || a.oc == 48 || a.oc == 96 || a.oc == 192) &&
+                       d.kh == d.kw && (d.kh == 3 || d.kh == 5) && d.sh == d.sw && (d.sh == 1 || d.sh == 2);
+    if (!shape || a.rows < 1 || a.segs < 1) return false;
+    const auto aligned = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    return aligned(d.x) && aligned(d.w) && aligned(a.y) && (!a.res || aligned(a.res)) &&
+           dwpw_tile_smem(a) <= 100 * 1024;
+}
+
+int dwpw_tile_pixels(const DwPwArgs &a) { return TILE_THREADS * tile_opt(a.oc) / a.oc; }
+
+int launch_dwpw_tile(const DwPwArgs &a, bool quick, cudaStream_t s) {
+    const int K = a.dw.kh, S = a.dw.sh, opt = tile_opt(a.oc);
+#define PPOCR_TILE(KK, SS, OO)                                                                       \
+    if (K == KK && S == SS && opt == OO)                                                             \
+        return quick ? run_dwpw_tile<KK, SS, OO, true>(a, s) : run_dwpw_tile<KK, SS, OO, false>(a, s);
+    PPOCR_TILE(3, 1, 12)
+    PPOCR_TILE(3, 1, 24)
+    PPOCR_TILE(3, 2, 12)
+    PPOCR_TILE(3, 2, 24)
+    PPOCR_TILE(5, 1, 12)
+    PPOCR_TILE(5, 1, 24)
+    PPOCR_TILE(5, 2, 12)
+    PPOCR_TILE(5, 2, 24)
+#undef PPOCR_TILE
+    return 0;
 }
 
 int launch_dw_pw(const DwPwArgs &a, cudaStream_t s) {

@@ -1013,7 +1013,8 @@ bool set_grid(TcArgs &a) {
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
         return false;
     const long tiles = a.windowed ? a.tiles : (a.M + TM - 1) / TM;
-    const long q = std::max(1L, std::min(long(sms / a.slices), tiles));
+    const long per = std::max(1, a.min_tiles);
+    const long q = std::max(1L, std::min(long(sms / a.slices), (tiles + per - 1) / per));
     a.grid = int(q) * a.slices;
     a.tmem_cols = TMEM_COLS;
     return true;
@@ -1070,7 +1071,7 @@ bool tc_prepare(TcArgs &a) {
         a.smem = int(pw_smem(a.kpad, a.bn, a.ns));
     } else if (a.fold) {
         // two 16-channel groups per slice, one when few tiles
-        a.bn = a.N >= 96 && a.tiles * ((a.N + 95) / 96) >= 74 ? 96 : 48;
+        a.bn = a.N >= 96 && (a.min_tiles > 1 || a.tiles * ((a.N + 95) / 96) >= 74) ? 96 : 48;
         a.slices = a.N / a.bn + (a.N % a.bn ? 1 : 0);
         a.ns = 2;
         while (a.ns < max_stages(a.bn) && conv_smem(a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;
@@ -1085,7 +1086,7 @@ bool tc_prepare(TcArgs &a) {
         // steps the run holds (a lane then reads the same alone as beside
         // others).
         const long tiles = a.windowed ? a.tiles : (a.M + TM - 1) / TM;
-        while (a.vocab == 0 && a.bn > 32 && tiles * ((a.N + a.bn - 1) / a.bn) < 74) a.bn -= 32;
+        while (a.vocab == 0 && a.min_tiles <= 1 && a.bn > 32 && tiles * ((a.N + a.bn - 1) / a.bn) < 74) a.bn -= 32;
         a.slices = (a.N + a.bn - 1) / a.bn;
         a.ns = 2;
         while (a.ns < max_stages(a.bn) && conv_smem(a.bn, a.ns + 1) <= size_t(DYN_CEILING)) a.ns++;

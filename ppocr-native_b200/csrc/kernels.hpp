@@ -140,6 +140,10 @@ struct DwPwArgs {
     int bias_mode2 = BIAS_FIRST;
     const float *res = nullptr;  // optional residual, y = act3(act2(pw) + res)
     int act3 = 0;
+    // Row tiles of the fused tile kernel (dwpw_tile): output rows of all
+    // lanes (LaneInfo::row0) times segments of each row.
+    long rows = 0;
+    int segs = 0;
 };
 
 enum EltMode : int {
@@ -260,6 +264,11 @@ struct TcArgs {
     int K = 0, N = 0, kpad = 0;   // K = kh * kw * C
     int act = 0, act2 = 0;
     int *err = nullptr;           // set to nonzero when a bounded wait gave up
+    // Tiles each CTA takes at least: above 1 a small layer occupies few SMs
+    // (other runs in flight use the rest) instead of spreading one tile per
+    // SM, and slices are not narrowed for few tiles. Each output's sum is the
+    // same whatever the grid and the slices.
+    int min_tiles = 1;
     // A CTC argmax head (vocab > 0, streamed, 1x1): no y; per row and column
     // block, (max, sum of exp(logit - max), first column of the max) over
     // the block's columns below vocab, into partial [M][blocks][3]. Block
@@ -366,6 +375,13 @@ int ctc_col_blocks(int cols);
 // Largest shared-memory need of launch_dw_pw for `c` input channels; 0 when
 // that kernel cannot take them.
 bool dw_pw_supported(const DwPwArgs &a);
+// The fused depthwise -> pointwise tile kernel for narrow layers (c of 24,
+// 48 or 96 channels into oc of 24, 48, 96 or 192, 3x3 or 5x5, stride 1 or
+// 2): whether it takes the layer, the pixels of one tile (segments of a
+// row), and the launch (quick: the tensor-core mode's activation quotient).
+bool dwpw_tile_supported(const DwPwArgs &a);
+int dwpw_tile_pixels(const DwPwArgs &a);
+int launch_dwpw_tile(const DwPwArgs &a, bool quick, cudaStream_t s);
 bool attention_supported(int t, int c, int heads);
 
 }  // namespace ppocr

@@ -59,6 +59,9 @@ bool cuda_ok(cudaError_t e, const char *what, int *code = nullptr) {
     return false;
 }
 
+// Tiles per CTA at least, in throughput mode (PPOCR_OPT_THROUGHPUT).
+constexpr int THROUGHPUT_TILES = 4;
+
 // Raise per-kernel limits once per device.
 void configure_device(int device) {
     static std::mutex mu;
@@ -572,6 +575,7 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
     }
     // Scratch.
     const bool tc_allowed = !(options & PPOCR_OPT_NO_TENSOR_CORES);
+    const int min_tiles = (options & PPOCR_OPT_THROUGHPUT) ? THROUGHPUT_TILES : 1;
     size_t mean_doubles = 1, ctc_floats = 1;
     for (size_t i = 0; i < p0.ops.size(); i++) {
         const Op &op = p0.ops[i];
@@ -621,7 +625,10 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
         err = g_error;
         return code;
     }
-    std::memset(g.in_host.p, 0, std::max<size_t>(g.in_floats, 1) * sizeof(float));
+    // Not cleared: the caller writes every lane's input before a run (a
+    // reader writing the lanes on the GPU never touches this staging), and a
+    // buffer kept from earlier sizes keeps its old contents, as the
+    // reference's lanes do.
     g.out_host.clear();
     for (size_t k = 0; k < p0.outputs.size(); k++) {
         auto hb = std::make_unique<HostBuffer>();
@@ -631,7 +638,7 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
             err = g_error;
             return code;
         }
-        std::memset(hb->p, 0, std::max<size_t>(g.out_floats[k], 1) * sizeof(float));
+        // outputs are written by every run before they are read
         g.out_host.push_back(std::move(hb));
     }
 
@@ -724,6 +731,7 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
             t.toc = c.oc;
         }
         t.act = c.act; t.act2 = c.act2; t.err = errp;
+        t.min_tiles = min_tiles;
         if (!tc_prepare(t)) return 0;
         return (!pw && !one) ? 2 : 1;
     };
@@ -776,10 +784,34 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
                 a.act3 = add.fused;
                 a.y = buf(add.y);
             }
-            // With the tensor cores the depthwise layer runs alone and the
-            // pointwise one on the tensor cores; without them, large maps take
-            // the fused FP32 kernel and small ones the two FP32 kernels (the
-            // same bits either way).
+            // Without the tensor cores, narrow layers (24 to 96 channels in,
+            // 24 to 96 out: the high-resolution blocks of both networks) take
+            // the fused row-tile kernel: the depthwise map stays in shared
+            // memory, both layers keep the exact FP32 order, and it runs
+            // 1.7-2.2x faster than the tiled fused kernel below. Beside the
+            // tensor cores it is slower than the depthwise row runs followed
+            // by the pointwise tensor-core kernel, which keep those layers.
+            if (!tc_allowed && pw.oc <= 96) {
+                long rows = 0;
+                int max_ow = 0;
+                for (int n = 0; n < nl; n++) {
+                    rows = std::max(rows, Lh[n].row0 + Lh[n].oh);
+                    max_ow = std::max(max_ow, Lh[n].ow);
+                }
+                a.rows = rows;
+                a.segs = 1;
+                if (dwpw_tile_supported(a)) {
+                    const int tp = dwpw_tile_pixels(a);
+                    a.segs = (max_ow + tp - 1) / tp;
+                    const bool quick = tc_allowed;
+                    g.launches.push_back([a, quick](cudaStream_t s) { return launch_dwpw_tile(a, quick, s); });
+                    continue;
+                }
+            }
+            // Otherwise, with the tensor cores the depthwise layer runs alone
+            // and the pointwise one on the tensor cores; without them, large
+            // maps take the fused FP32 kernel and small ones the two FP32
+            // kernels (the same bits either way).
             const bool tc_pw = tc_allowed && W.tc_hi(st.b);
             if (!tc_pw && a.dw.M >= DW_PW_MIN_PIXELS) {
                 g.launches.push_back([a](cudaStream_t s) { return launch_dw_pw(a, s); });
@@ -946,6 +978,7 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
                 mg.partial = a.partial; mg.x = a.x; mg.w = a.w; mg.b = a.b; mg.y = a.y;
                 mg.pixels = a.pixels; mg.ci = a.ci; mg.vocab = a.vocab;
                 mg.wmax = W.tc_wmax[i]; mg.bmax = W.tc_bmax[i];
+                t.min_tiles = min_tiles;
                 // the path depends on the layer's own need, never on how
                 // large a reused scratch buffer happens to be
                 if (tc_prepare(t) && size_t(a.pixels) * t.blocks * 3 <= ctc_floats) {
@@ -972,6 +1005,7 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
                 t.w_hi = W.tc_hi(i); t.w_lo = W.tc_lo(i); t.b = a.b; t.y = a.y;
                 t.M = a.Min; t.lanes = L; t.nl = nl; t.act = a.act; t.err = errp;
                 t.tkh = a.kh; t.tkw = a.kw; t.toc = a.oc;
+                t.min_tiles = min_tiles;
                 if (tc_prepare(t)) {
                     g.launches.push_back([t](cudaStream_t s) { return launch_tc(t, s); });
                     break;
@@ -1367,7 +1401,7 @@ int ppocr_model_set_options(ppocr_model *m, uint32_t options) {
     g_error.clear();
     if (!m) return fail(PPOCR_E_ARG, "null model");
     if (options == m->options) return PPOCR_OK;
-    bool refuse = (options ^ m->options) & (PPOCR_OPT_NO_FUSION | PPOCR_OPT_NO_TENSOR_CORES);
+    bool refuse = (options ^ m->options) & (PPOCR_OPT_NO_FUSION | PPOCR_OPT_NO_TENSOR_CORES | PPOCR_OPT_THROUGHPUT);
     m->options = options;
     m->drop_graphs();
     if (refuse && !m->sizes.empty()) {

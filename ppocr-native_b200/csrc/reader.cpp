@@ -522,8 +522,10 @@ int ppocr_reader_create(const ppocr_model *det, const ppocr_model *rec, const ch
     r->stream = static_cast<cudaStream_t>(ppocr_model_stream(r->det));
     if ((rc = ppocr_model_set_stream(r->rec, r->stream))) return rc;
     // The recogniser's lanes change with every page: direct launches instead
-    // of a graph captured once per set of sizes.
-    if ((rc = ppocr_model_set_options(r->rec, PPOCR_OPT_NO_GRAPH))) return rc;
+    // of a graph captured once per set of sizes. Readers run several pages at
+    // once, so both networks size their grids for throughput.
+    if ((rc = ppocr_model_set_options(r->det, PPOCR_OPT_THROUGHPUT))) return rc;
+    if ((rc = ppocr_model_set_options(r->rec, PPOCR_OPT_NO_GRAPH | PPOCR_OPT_THROUGHPUT))) return rc;
     if (!cuda_ok(cudaGetDevice(&r->device), "reading the device") ||
         !cuda_ok(cudaEventCreateWithFlags(&r->ev, cudaEventDisableTiming), "creating an event"))
         return PPOCR_E_DEVICE;
@@ -630,9 +632,9 @@ int ppocr_reader_line(const ppocr_reader *r, size_t i, float quad[8], const char
 int ppocr_reader_set_options(ppocr_reader *r, uint32_t options) {
     set_last_error("");
     if (!r) return fail(PPOCR_E_ARG, "null reader");
-    int rc = ppocr_model_set_options(r->det, options);
+    int rc = ppocr_model_set_options(r->det, options | PPOCR_OPT_THROUGHPUT);
     if (rc) return rc;
-    if ((rc = ppocr_model_set_options(r->rec, options | PPOCR_OPT_NO_GRAPH))) return rc;
+    if ((rc = ppocr_model_set_options(r->rec, options | PPOCR_OPT_NO_GRAPH | PPOCR_OPT_THROUGHPUT))) return rc;
     r->det_w = r->det_h = 0;  // sizes are set again at the next page
     r->rec_sizes.clear();
     return PPOCR_OK;

@@ -19,7 +19,7 @@ HERE = Path(__file__).resolve().parent
 LIB = HERE / "libppocr_cuda.so"
 
 OK, E_PLAN, E_SIZE, E_NOMEM, E_DEVICE, E_TIMEOUT, E_UNSUPPORTED, E_ARG = range(8)
-OPT_NO_FUSION, OPT_NO_GRAPH, OPT_NO_TENSOR_CORES = 1, 2, 4
+OPT_NO_FUSION, OPT_NO_GRAPH, OPT_NO_TENSOR_CORES, OPT_THROUGHPUT = 1, 2, 4, 8
 
 # The exported C entry points and their signatures; tests check the library
 # exports every one the header declares.

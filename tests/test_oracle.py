@@ -362,3 +362,32 @@ def test_line_width_matches_fresh_load(oracle_mod):
         with pytest.raises(oracle_mod.OracleError):
             o.set_size(2, width)
         assert np.array_equal(ramp_run(o), before)
+
+
+def test_timed_path_gives_the_plain_loops_bits(oracle_mod):
+    """The register-tiled AVX2+FMA loops bench.py times (dense convolutions
+    and depthwise layers in 6-pixel tiles, the CTC head's logits six time
+    steps at a time) keep every output's chain of fused multiply-adds in the
+    plain loops' order: the same bits on the detector, the recogniser (argmax
+    and logits heads) and the fused benchmark layer, at sizes with border and
+    interior tiles and widths that are not multiples of six."""
+    from ppocr_native_b200 import synth
+
+    rng = np.random.default_rng(21)
+    cases = [(synth.det_plan(seed=5, std=None, size=(160, 128)), (160, 128)),
+             (synth.det_plan(seed=5, std=None, size=(160, 128)), (96, 70)),
+             (synth.rec_plan(seed=3, std=None, vocab=700), (48, 328)),
+             (synth.rec_plan(seed=3, std=None, vocab=300, logits=True), (48, 100)),
+             (synth.fused_layer_plan(seed=0, h=23, w=31), (23, 31))]
+    try:
+        for plan, (h, w) in cases:
+            p = oracle_mod.Oracle(plan)
+            p.set_size(h, w)
+            x = rng.standard_normal(p.input_len).astype(np.float32)
+            oracle_mod.set_fast(False)
+            plain = p.run(x)[0]
+            oracle_mod.set_fast(True)
+            fast = p.run(x)[0]
+            assert np.array_equal(plain.view(np.uint32), fast.view(np.uint32))
+    finally:
+        oracle_mod.set_fast(False)

@@ -375,7 +375,7 @@ def test_timed_path_gives_the_plain_loops_bits(oracle_mod):
 
     rng = np.random.default_rng(21)
     cases = [(synth.det_plan(seed=5, std=None, size=(160, 128)), (160, 128)),
-             (synth.det_plan(seed=5, std=None, size=(160, 128)), (96, 70)),
+             (synth.det_plan(seed=5, std=None, size=(160, 128)), (96, 224)),
              (synth.rec_plan(seed=3, std=None, vocab=700), (48, 328)),
              (synth.rec_plan(seed=3, std=None, vocab=300, logits=True), (48, 100)),
              (synth.fused_layer_plan(seed=0, h=23, w=31), (23, 31))]

@@ -660,8 +660,13 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
     }
     if (!reserve(g.lane_tables, old ? &old->lane_tables : nullptr, std::max<size_t>(tables.size(), 1) * sizeof(LaneInfo),
                  "allocating lane tables", code) ||
-        !cuda_ok(cudaMemcpy(g.lane_tables.p, tables.data(), tables.size() * sizeof(LaneInfo),
-                            cudaMemcpyHostToDevice), "uploading lane tables", &code)) {
+        // On the model's own stream, so that its kernels read the new tables:
+        // a plain cudaMemcpy from pageable memory can return before its DMA
+        // lands and is not ordered with a non-blocking stream, and a reused
+        // buffer still holds the previous sizes' tables. The host vector is
+        // staged before the call returns.
+        !cuda_ok(cudaMemcpyAsync(g.lane_tables.p, tables.data(), tables.size() * sizeof(LaneInfo),
+                                 cudaMemcpyHostToDevice, stream), "uploading lane tables", &code)) {
         err = g_error;
         return code;
     }
@@ -1221,6 +1226,9 @@ int ppocr_model_load_bytes(const void *bytes, size_t len, int device, ppocr_mode
     if (!cuda_ok(cudaMemcpy(w->tc_arena.p, tc.data(), w->tc_arena.bytes, cudaMemcpyHostToDevice),
                  "uploading weights"))
         return PPOCR_E_DEVICE;
+    // A copy from pageable memory may return before its DMA lands; the
+    // weights are complete before any stream of any model reads them.
+    if (!cuda_ok(cudaDeviceSynchronize(), "uploading weights")) return PPOCR_E_DEVICE;
     return make_model(std::move(plan), w, values.size(), device, out);
 }
 
@@ -1392,6 +1400,11 @@ int ppocr_model_set_stream(ppocr_model *m, void *stream) {
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->own_stream;
     if (s == m->stream) return PPOCR_OK;
     m->settle();
+    // uploads queued on the old stream (the lane tables) land before the
+    // new stream's kernels read them
+    if (!cuda_ok(cudaSetDevice(m->device), "selecting the device") ||
+        !cuda_ok(cudaStreamSynchronize(m->stream), "switching streams"))
+        return PPOCR_E_DEVICE;
     m->stream = s;
     m->drop_graphs();
     return PPOCR_OK;

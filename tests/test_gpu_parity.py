@@ -711,3 +711,30 @@ def test_fused_dw_pw_row_tiles(cuda_mod, oracle_mod, c, n, k, s):
                     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (sizes[i], opts)
                 else:
                     assert max_gap(got, want) <= 1e-4 * max(1.0, float(np.abs(want).max())), sizes[i]
+
+
+def test_lane_layouts_back_to_back(cuda_mod):
+    """A model whose lanes change run after run (more, fewer, wider,
+    narrower; its buffers are kept and its lane tables rewritten) gives each
+    run the bits a fresh model gives it."""
+    plan = synth.rec_plan(seed=12, std=None, vocab=600)
+    rng = np.random.default_rng(3)
+    layouts = [[320, 800, 96, 1280, 48 * 9], [96], [1600, 320], [48 * 7] * 12, [640]]
+    inputs = [[rng.standard_normal(48 * w * 3).astype(np.float32) for w in ws] for ws in layouts]
+    fresh = []
+    for ws, xs in zip(layouts, inputs):
+        with cuda_mod.Model(plan) as m:
+            m.set_sizes([(48, w) for w in ws])
+            for i, x in enumerate(xs):
+                m.lane_input_mut(i)[:] = x
+            m.run(60_000)
+            fresh.append([m.lane_output(i).copy() for i in range(len(ws))])
+    with cuda_mod.Model(plan) as m:
+        for _ in range(2):
+            for ws, xs, want in zip(layouts, inputs, fresh):
+                m.set_sizes([(48, w) for w in ws])
+                for i, x in enumerate(xs):
+                    m.lane_input_mut(i)[:] = x
+                m.run(60_000)
+                for i in range(len(ws)):
+                    assert np.array_equal(m.lane_output(i), want[i])

@@ -217,3 +217,20 @@ def test_reader_without_a_page(cuda_mod, small):
         assert e.value.code == cuda_mod.E_ARG
         empty = np.zeros((0, 0, 3), np.uint8)
         assert r.read(empty) == [] and len(r.boxes()) == 0
+
+
+def test_reader_pages_of_changing_line_counts(cuda_mod, small):
+    """Pages whose line counts and widths change from page to page (config 5's
+    stream: the recogniser's lanes are laid out anew for every page while
+    its buffers are kept) read each as a fresh reader reads it alone."""
+    pages = [workload.synthetic_page(40 + i, lines=n, width=500, height=900) for i, n in enumerate((9, 2, 12, 1, 6))]
+    alone = []
+    for page, quads in pages:
+        with cuda_mod.Reader(small["det"], small["rec"], small["text"]) as r:
+            r.detect(page)
+            alone.append(r.recognise(quads))
+    with cuda_mod.Reader(small["det"], small["rec"], small["text"]) as r:
+        for _ in range(3):
+            for (page, quads), want in zip(pages, alone):
+                r.detect(page)
+                assert r.recognise(quads) == want

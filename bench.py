@@ -624,7 +624,17 @@ def run_ours(args, d: Dist) -> dict | None:
     readers = [cuda.Reader(det, rec, text) for _ in range(R)]
     main = torch.cuda.Stream(device=device)
 
-    # Warm-up: every reader reads pages until its buffers have grown.
+    # Warm-up: every reader reads every distinct page once (its buffers grow
+    # to the largest page: no allocation, which would synchronize the
+    # device, inside the timed passes), then the warm-up steps.
+    def warm(r):
+        for k in range(len(pool)):
+            r.detect_ptr(pool.host[k].data_ptr(), pool.w, pool.h)
+            q = pool.quads[k]
+            r.recognise_ptr(q.ctypes.data, len(q))
+
+    with cf.ThreadPoolExecutor(max_workers=R) as ex:
+        list(ex.map(warm, readers))
     read_pages(torch, readers, pool, max(args.warmup, 1) * R, False, main)
     torch.cuda.synchronize()
 

@@ -64,8 +64,10 @@ __global__ void __launch_bounds__(256) elt_kernel(const EltArgs a) {
             break;
         }
         case ELT_UPSAMPLE:
-        case ELT_UPSAMPLE_ADD: {
-            const LaneInfo &L = a.lanes[a.nl > 1 ? find_lane(a.lanes, a.nl, m) : 0];
+        case ELT_UPSAMPLE_ADD:
+        case ELT_GATE_UPSAMPLE_ADD: {
+            const int n = a.nl > 1 ? find_lane(a.lanes, a.nl, m) : 0;
+            const LaneInfo &L = a.lanes[n];
             const int ow = __ldg(&L.ow);
             const int r = int(m - __ldg(&L.pix0));
             const int oy = r / ow, ox = r - oy * ow;
@@ -78,6 +80,13 @@ __global__ void __launch_bounds__(256) elt_kernel(const EltArgs a) {
             } else {
                 float q[VEC];
                 load_vec<VEC>(a.x2 + e, q);
+                if (a.mode == ELT_GATE_UPSAMPLE_ADD) {
+                    // the full-size input as the gate-add would have written it
+                    float gg[VEC];
+                    load_vec<VEC>(a.g + (long)n * a.c + c, gg);
+#pragma unroll
+                    for (int k = 0; k < VEC; k++) q[k] = activate(a.act, fadd(fmul(q[k], gg[k]), q[k]));
+                }
 #pragma unroll
                 for (int k = 0; k < VEC; k++) v[k] = fadd(q[k], u[k]);
             }
@@ -103,35 +112,55 @@ __global__ void __launch_bounds__(256) elt_kernel(const EltArgs a) {
 // copied and later ones kept only when greater (conv.rs:404-440). Average
 // pool: whole windows, taps summed in row-major order then divided
 // (layers.rs:443-463).
+// VEC channels per thread (4 when c % 4 == 0: float4 loads and stores, one
+// lane search per four values); each channel keeps its own order.
+template <int VEC>
 __global__ void __launch_bounds__(256) pool_kernel(const PoolArgs a) {
-    const long total = a.M * a.c;
+    const int cg = a.c / VEC;
+    const long total = a.M * cg;
     for (long g = (long)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (long)gridDim.x * blockDim.x) {
-        long m = g / a.c;
-        int c = int(g - m * a.c);
+        const long m = g / cg;
+        const int c = int(g - m * cg) * VEC;
         const LaneInfo &L = a.lanes[find_lane(a.lanes, a.nl, m)];
-        int ow = __ldg(&L.ow), ih = __ldg(&L.ih), iw = __ldg(&L.iw);
-        int r = int(m - __ldg(&L.pix0));
-        int oy = r / ow, ox = r - oy * ow;
+        const int ow = __ldg(&L.ow), ih = __ldg(&L.ih), iw = __ldg(&L.iw);
+        const int r = int(m - __ldg(&L.pix0));
+        const int oy = r / ow, ox = r - oy * ow;
         const float *xn = a.x + __ldg(&L.ipix0) * a.c + c;
-        float v = 0.0f;
+        float v[VEC];
+#pragma unroll
+        for (int e = 0; e < VEC; e++) v[e] = 0.0f;
         bool seeded = false;
         for (int ky = 0; ky < a.kh; ky++) {
-            int iy = oy * a.sh + ky;
+            const int iy = oy * a.sh + ky;
             if (iy >= ih) continue;
             for (int kx = 0; kx < a.kw; kx++) {
-                int ix = ox * a.sw + kx;
+                const int ix = ox * a.sw + kx;
                 if (ix >= iw) continue;
-                float x = xn[((long)iy * iw + ix) * a.c];
-                if (a.average) {
-                    v = fadd(v, x);
-                } else if (!seeded || x > v) {
-                    v = x;
-                    seeded = true;
+                const float *src = xn + ((long)iy * iw + ix) * a.c;
+                float x[VEC];
+                if (VEC == 4) {
+                    const float4 q = __ldg(reinterpret_cast<const float4 *>(src));
+                    x[0] = q.x; x[1] = q.y; x[2 % VEC] = q.z; x[3 % VEC] = q.w;
+                } else {
+                    x[0] = __ldg(src);
                 }
+#pragma unroll
+                for (int e = 0; e < VEC; e++) {
+                    if (a.average)
+                        v[e] = fadd(v[e], x[e]);
+                    else if (!seeded || x[e] > v[e])
+                        v[e] = x[e];
+                }
+                seeded = true;
             }
         }
-        if (a.average) v = fdiv(v, float(a.kh * a.kw));
-        a.y[g] = v;
+        float *dst = a.y + m * a.c + c;
+#pragma unroll
+        for (int e = 0; e < VEC; e++) {
+            if (a.average) v[e] = fdiv(v[e], float(a.kh * a.kw));
+            if (VEC == 1) dst[e] = v[e];
+        }
+        if (VEC == 4) *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1 % VEC], v[2 % VEC], v[3 % VEC]);
     }
 }
 
@@ -352,34 +381,40 @@ __global__ void __launch_bounds__(ATT_Q) attention_kernel(const AttentionArgs a)
         if (d < hd) y[d] = out[d];
 }
 
-// Beside the tensor cores (tolerance mode): eight threads per query, thread
-// l taking the keys j = l mod 8. Two passes: the maximum of the scores
-// (reduced over the eight threads by shuffles), then the exponentials
-// (__expf) summed and the value rows accumulated with them; the eight
-// partial sums and rows are reduced by shuffles and the row divided by the
-// sum. Same K / V staging as attention_kernel.
+// The tensor-core mode's attention (head size 15): a block per (lane, head,
+// 32 queries), eight threads per query taking keys j = l mod 8. K and V of
+// the lane and head are staged in shared memory, each row padded to 20
+// floats (a key's 15 values read as four 16-byte loads; the eight keys of a
+// query's threads fall in distinct banks). One pass over the keys with an
+// online softmax (a running maximum; the sum and the value row rescaled by
+// exp(old - new) when it rises, __expf), then the eight threads' states merge
+// by shuffles and the row is divided by the sum. Within a few ulp of the
+// two-pass exact kernel, in another order.
 constexpr int ATT_FAST_Q = 32;  // queries per block (x 8 threads)
+constexpr int ATT_ROW = 20;     // padded K / V row (floats)
 
 template <int HD>
 __global__ void __launch_bounds__(ATT_FAST_Q * 8) attention_fast_kernel(const AttentionArgs a) {
-    extern __shared__ float kv[];  // K [t][HD], V [t][HD]
+    static_assert(HD <= 16, "one row is four float4s");
+    extern __shared__ __align__(16) float kv[];  // K [t][ATT_ROW], V [t][ATT_ROW]
     const int n = blockIdx.x / a.heads, h = blockIdx.x % a.heads;
     const LaneInfo &L = a.lanes[n];
     const int t = L.iw, c = a.c;
     if (blockIdx.y * ATT_FAST_Q >= t) return;
-    float *K = kv, *V = kv + t * HD;
+    float *K = kv, *V = kv + t * ATT_ROW;
     const float *x = a.x + L.ipix0 * 3 * c;
-    for (int i0 = threadIdx.x; i0 < t * HD; i0 += 4 * blockDim.x) {
+    for (int i0 = threadIdx.x; i0 < t * ATT_ROW; i0 += 4 * blockDim.x) {
         float kk[4], vv[4];
 #pragma unroll
         for (int u = 0; u < 4; u++) {
-            const int i = i0 + u * blockDim.x, j = i / HD, d = i - j * HD;
-            kk[u] = i < t * HD ? __ldg(x + (long)j * 3 * c + c + h * HD + d) : 0.0f;
-            vv[u] = i < t * HD ? __ldg(x + (long)j * 3 * c + 2 * c + h * HD + d) : 0.0f;
+            const int i = i0 + u * blockDim.x, j = i / ATT_ROW, d = i - j * ATT_ROW;
+            const bool in = i < t * ATT_ROW && d < HD;
+            kk[u] = in ? __ldg(x + (long)j * 3 * c + c + h * HD + d) : 0.0f;
+            vv[u] = in ? __ldg(x + (long)j * 3 * c + 2 * c + h * HD + d) : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < 4; u++)
-            if (i0 + u * blockDim.x < t * HD) {
+            if (i0 + u * blockDim.x < t * ATT_ROW) {
                 K[i0 + u * blockDim.x] = kk[u];
                 V[i0 + u * blockDim.x] = vv[u];
             }
@@ -389,30 +424,50 @@ __global__ void __launch_bounds__(ATT_FAST_Q * 8) attention_fast_kernel(const At
     const int s = blockIdx.y * ATT_FAST_Q + threadIdx.x / 8;
     const bool live = s < t;
     const float scale = a.scale[0];
-    float q[HD];
+    float q[16];
 #pragma unroll
-    for (int d = 0; d < HD; d++) q[d] = live ? x[(long)s * 3 * c + h * HD + d] * scale : 0.0f;
-    auto score = [&](int j) {
-        const float *k = K + j * HD;
+    for (int d = 0; d < 16; d++) q[d] = live && d < HD ? x[(long)s * 3 * c + h * HD + d] * scale : 0.0f;
+    float m = -FLT_MAX, sum = 0.0f, o[16];
+#pragma unroll
+    for (int d = 0; d < 16; d++) o[d] = 0.0f;
+    for (int j = l; j < t; j += 8) {
+        const float4 *k4 = reinterpret_cast<const float4 *>(K + j * ATT_ROW);
         float acc = 0.0f;
 #pragma unroll
-        for (int d = 0; d < HD; d++) acc = fmaf(k[d], q[d], acc);
-        return acc;
-    };
-    float mx = -FLT_MAX;
-    for (int j = l; j < t; j += 8) mx = fmaxf(mx, score(j));
+        for (int g = 0; g < 4; g++) {
+            const float4 kq = k4[g];
+            acc = fmaf(kq.x, q[4 * g], acc);
+            acc = fmaf(kq.y, q[4 * g + 1], acc);
+            acc = fmaf(kq.z, q[4 * g + 2], acc);
+            acc = fmaf(kq.w, q[4 * g + 3], acc);
+        }
+        if (acc > m) {
+            const float f = __expf(m - acc);  // 0 on the first key
+            sum *= f;
 #pragma unroll
-    for (int off = 4; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    float sum = 0.0f, o[HD];
-#pragma unroll
-    for (int d = 0; d < HD; d++) o[d] = 0.0f;
-    for (int j = l; j < t; j += 8) {
-        const float p = __expf(score(j) - mx);
+            for (int d = 0; d < 16; d++) o[d] *= f;
+            m = acc;
+        }
+        const float p = __expf(acc - m);
         sum += p;
-        const float *v = V + j * HD;
+        const float4 *v4 = reinterpret_cast<const float4 *>(V + j * ATT_ROW);
 #pragma unroll
-        for (int d = 0; d < HD; d++) o[d] = fmaf(v[d], p, o[d]);
+        for (int g = 0; g < 4; g++) {
+            const float4 vq = v4[g];
+            o[4 * g] = fmaf(vq.x, p, o[4 * g]);
+            o[4 * g + 1] = fmaf(vq.y, p, o[4 * g + 1]);
+            o[4 * g + 2] = fmaf(vq.z, p, o[4 * g + 2]);
+            o[4 * g + 3] = fmaf(vq.w, p, o[4 * g + 3]);
+        }
     }
+    // the eight threads' states: rescaled to the query's maximum, then summed
+    float mq = m;
+#pragma unroll
+    for (int off = 4; off > 0; off >>= 1) mq = fmaxf(mq, __shfl_xor_sync(0xffffffffu, mq, off));
+    const float f = sum > 0.0f ? __expf(m - mq) : 0.0f;  // a thread without keys holds nothing
+    sum *= f;
+#pragma unroll
+    for (int d = 0; d < HD; d++) o[d] *= f;
 #pragma unroll
     for (int off = 4; off > 0; off >>= 1) {
         sum += __shfl_xor_sync(0xffffffffu, sum, off);
@@ -640,7 +695,7 @@ int launch_elt(const EltArgs &a, cudaStream_t s) {
     const int cout = a.mode == ELT_CONCAT ? a.c + a.c2 : a.c;
     const auto aligned = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     const bool vec = cout % 4 == 0 && a.c % 4 == 0 && (a.mode != ELT_CONCAT || a.c2 % 4 == 0) && aligned(a.x) &&
-                     aligned(a.y) && (!a.x2 || aligned(a.x2));
+                     aligned(a.y) && (!a.x2 || aligned(a.x2)) && (!a.g || aligned(a.g));
     const long total = a.M * cout;
     const bool small = total < (1L << 31);
     if (vec)
@@ -653,7 +708,12 @@ int launch_elt(const EltArgs &a, cudaStream_t s) {
 }
 
 int launch_pool(const PoolArgs &a, cudaStream_t s) {
-    pool_kernel<<<grid_for(a.M * a.c), 256, 0, s>>>(a);
+    const bool vec = a.c % 4 == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+    if (vec)
+        pool_kernel<4><<<grid_for(a.M * (a.c / 4)), 256, 0, s>>>(a);
+    else
+        pool_kernel<1><<<grid_for(a.M * a.c), 256, 0, s>>>(a);
     return 1;
 }
 
@@ -681,9 +741,10 @@ int launch_attention(const AttentionArgs &a, cudaStream_t s) {
     int hd = a.c / a.heads;
     size_t smem = sizeof(float) * 2 * a.tmax * hd;
     dim3 grid(unsigned(a.nl * a.heads), unsigned((a.tmax + ATT_Q - 1) / ATT_Q));
-    if (hd == 15 && a.fast) {
+    const size_t fast_smem = sizeof(float) * 2 * a.tmax * ATT_ROW;
+    if (hd == 15 && a.fast && fast_smem <= 160 * 1024) {
         dim3 fgrid(unsigned(a.nl * a.heads), unsigned((a.tmax + ATT_FAST_Q - 1) / ATT_FAST_Q));
-        attention_fast_kernel<15><<<fgrid, ATT_FAST_Q * 8, smem, s>>>(a);
+        attention_fast_kernel<15><<<fgrid, ATT_FAST_Q * 8, fast_smem, s>>>(a);
     } else if (hd == 15)  // PP-OCRv6's 8 heads of 15 (tools/export_ocr.py:654)
         attention_kernel<15><<<grid, ATT_Q, smem, s>>>(a);
     else

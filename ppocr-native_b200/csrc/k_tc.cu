@@ -625,7 +625,7 @@ bool tc_prepare(TcArgs &a) {
     if (!enc) return false;
     a.nkb = a.kpad / TK;
     if (a.C % 4 || !aligned(a.x) || (a.gate && !aligned(a.gate))) return false;
-    if (a.vocab > 0 && (a.windowed || !a.stream_b || a.act || a.res || a.gate || !a.partial)) return false;
+    if (a.vocab > 0 && (a.windowed || a.act || a.res || a.gate || !a.partial)) return false;
     if (a.tkh) {
         // the scattering epilogue lives in the streaming kernel; its stores
         // are 16-byte runs of one tap's channels
@@ -708,6 +708,15 @@ int tc_stream_slices(int N) {
     return bn ? (N + bn - 1) / bn : 0;
 }
 
+int tc_pointwise_slices(int K, int N) {
+    // set_grid's choice for a 1x1 layer: resident weights unless streaming
+    // them takes fewer slices
+    const int bn = pw_slice_width(K, N);
+    const int streamed = tc_stream_slices(N);
+    if (streamed > 0 && (!bn || streamed < (N + bn - 1) / bn)) return streamed;
+    return bn ? (N + bn - 1) / bn : 0;
+}
+
 template <int ACT>
 void configure_act() {
     cudaFuncSetAttribute(pw_tc_kernel<ACT>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
@@ -718,14 +727,17 @@ void configure_act() {
 
 void configure_tc_kernels() {
     cudaFuncSetAttribute(conv_tc_kernel<0, EPI_CTC>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
+    cudaFuncSetAttribute(pw_tc_kernel<0, EPI_CTC>, cudaFuncAttributeMaxDynamicSharedMemorySize, DYN_CEILING);
     configure_act<0>(); configure_act<1>(); configure_act<2>(); configure_act<3>();
     configure_act<4>(); configure_act<5>(); configure_act<6>(); configure_act<7>();
 }
 
 template <int ACT>
 void launch_act(const TcArgs &a, const CUtensorMap &mx, const CUtensorMap &mw, cudaStream_t s) {
-    if (a.vocab > 0)
+    if (a.vocab > 0 && a.stream_b)
         conv_tc_kernel<0, EPI_CTC><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
+    else if (a.vocab > 0)
+        pw_tc_kernel<0, EPI_CTC><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
     else if (a.tkh)
         conv_tc_kernel<ACT, EPI_CONVT><<<a.grid, Roles::THREADS, a.smem, s>>>(a, mx, mw);
     else if (a.fold)

@@ -153,11 +153,13 @@ enum EltMode : int {
     ELT_UPSAMPLE,       // y[r][c] = x[r/sh][c/sw]
     ELT_UPSAMPLE_ADD,   // y = x2 + upsample(x)
     ELT_CONCAT,         // y = [x | x2] per pixel
+    ELT_GATE_UPSAMPLE_ADD,  // y = act(x2 * g[n][c] + x2) + upsample(x)
 };
 
 struct EltArgs {
     int mode = ELT_ADD;
     const float *x = nullptr, *x2 = nullptr;
+    const float *g = nullptr;  // ELT_GATE_UPSAMPLE_ADD: the gate, [lanes][c]
     float *y = nullptr;
     const LaneInfo *lanes = nullptr;  // gates and upsampling
     int nl = 1;
@@ -290,6 +292,9 @@ struct TcArgs {
 int launch_tc(const TcArgs &a, cudaStream_t s);
 // Slices of the output channels a streamed-weight launch of N channels uses.
 int tc_stream_slices(int N);
+// Slices a 1x1 K x N layer takes on the tensor cores (resident or streamed
+// weights, whichever takes fewer); 0 when neither fits.
+int tc_pointwise_slices(int K, int N);
 
 // The CTC argmax head's merge after its tensor-core logits: per row, the
 // blocks' maxima and sums combine into 1 / sum exp(logit - max); every

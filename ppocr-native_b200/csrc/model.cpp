@@ -163,6 +163,8 @@ enum StepKind {
     S_DW_PW,     // depthwise `a` feeding pointwise `b` [+ residual add `c`]
     S_CONV,      // a dense convolution with optional gate, sources, residual
     S_GATE_ADD,  // channelmul `a` and add `b`: y = act(x * g + x)
+    S_GATE_UPADD,  // upsample-add `a` whose full-size input is the gate-add of channelmul `b` and
+                   // add `c` (its only reader), computed on the fly: y = act(x2 * g + x2) + up(x)
     S_SKIP,      // folded into another step
 };
 
@@ -288,7 +290,7 @@ std::vector<Step> fuse(const Plan &p, bool enabled) {
         st.name += "+add";
     };
     for (size_t i = 0; i < p.ops.size(); i++) {
-        if (steps[i].kind == S_SKIP) continue;
+        if (steps[i].kind == S_SKIP || steps[i].kind == S_GATE_UPADD) continue;
         const Op &op = p.ops[i];
         // depthwise -> pointwise
         if (op.kind == K_DWCONV && i + 1 < p.ops.size() && only_reader(u[i], i + 1)) {
@@ -339,6 +341,26 @@ std::vector<Step> fuse(const Plan &p, bool enabled) {
                 st.op = i + 1;
                 st.name = "gate_add";
                 steps[i + 1].kind = S_SKIP;
+                // an RSE output read only as the full-size input of an
+                // upsample-add (the neck's top-down path): the gate-add runs
+                // inside that upsample-add, at its place, from the conv
+                // output and the gate, which must still hold their values
+                const Uses &ua = u[i + 1];
+                if (!ua.out && ua.readers.size() == 1) {
+                    const size_t r = ua.readers[0];
+                    const Op &up = p.ops[r];
+                    if (up.kind == K_UPSAMPLEADD && up.x2 == add.y && up.x != add.y && intact(p, op.x, i + 1, r) &&
+                        intact(p, op.x2, i + 1, r) && disjoint({up.x, op.x, op.x2}, up.y)) {
+                        Step &su = steps[r];
+                        su.kind = S_GATE_UPADD;
+                        su.a = r;
+                        su.b = i;
+                        su.c = i + 1;
+                        su.op = r;
+                        su.name = "gate_add+upsample_add";
+                        st.kind = S_SKIP;
+                    }
+                }
                 continue;
             }
         }
@@ -589,7 +611,8 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
             size_t cols = (vocab + 15) / 16 * 16;
             ctc_floats = std::max(ctc_floats, size_t(total_in(g, i)) * ctc_col_blocks(int(cols)) * 3);
             if (op.kind == K_CTCARGMAX && tc_allowed)
-                ctc_floats = std::max(ctc_floats, size_t(total_in(g, i)) * 2 * tc_stream_slices(int(cols)) * 3);
+                ctc_floats = std::max(ctc_floats,
+                                      size_t(total_in(g, i)) * 2 * tc_pointwise_slices(int(op.ic), int(cols)) * 3);
         }
     }
     // A windowed conv of several sources (or upsampled ones) on the tensor
@@ -867,6 +890,16 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
             push_conv(st.b, a, Lh, nullptr);
             continue;
         }
+        if (st.kind == S_GATE_UPADD) {
+            const Op &up = p0.ops[st.a], &cm = p0.ops[st.b], &add = p0.ops[st.c];
+            EltArgs a;
+            a.mode = ELT_GATE_UPSAMPLE_ADD;
+            a.x = buf(up.x); a.x2 = buf(cm.x); a.g = buf(cm.x2); a.y = buf(up.y);
+            a.lanes = L; a.nl = nl; a.M = total_out(g, st.a); a.c = int(up.oc); a.act = add.fused;
+            a.sh = int(std::max<size_t>(up.sh, 1)); a.sw = int(std::max<size_t>(up.sw, 1));
+            g.launches.push_back([a](cudaStream_t s) { return launch_elt(a, s); });
+            continue;
+        }
         if (st.kind == S_GATE_ADD) {
             const Op &cm = p0.ops[st.a], &add = p0.ops[st.b];
             EltArgs a;
@@ -972,9 +1005,10 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
             a.cols = (a.vocab + 15) / 16 * 16;
             a.col_blocks = ctc_col_blocks(a.cols);
             if (!a.probs && tc_allowed && W.tc_hi(i)) {
-                // the logits on the tensor cores, the classes checked exactly
+                // the logits on the tensor cores, the classes checked exactly;
+                // each CTA keeps its slice of the head's weights resident and
+                // walks the time steps (streamed when that takes fewer slices)
                 TcArgs t;
-                t.stream_b = true;
                 t.x = a.x; t.C = t.K = a.ci; t.N = a.cols; t.kpad = W.tc_kpad[i];
                 t.w_hi = W.tc_hi(i); t.w_lo = W.tc_lo(i); t.b = a.b; t.y = a.y;
                 t.M = a.pixels; t.lanes = L; t.nl = nl; t.err = errp;

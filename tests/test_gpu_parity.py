@@ -328,12 +328,15 @@ def test_line_model(cuda_mod, oracle_mod, width):
 def test_detector_960x736(cuda_mod, oracle_mod, std):
     """Benchmark config 2: probabilities within 1e-4 with the pointwise
     layers on the tensor cores (3xTF32), bit-identical with every
-    contraction on the FP32 cores."""
+    contraction on the FP32 cores. The neck's RSE outputs read only by an
+    upsample-add are never written (their gate-add runs inside it): three
+    such steps."""
     plan = synth.det_plan(seed=3, std=std)
     x = np.random.default_rng(4).normal(0, 1, 960 * 736 * 3).astype(np.float32)
     want = oracle_run(oracle_mod, plan, x)[0]
     got, steps = gpu_run(cuda_mod, plan, x)
     assert "dw+pw" in steps and "gate_add" in steps and any("sources" in s for s in steps)
+    assert steps.count("gate_add+upsample_add") == 3, steps
     check(got[0], want, exact=False)
     got, _ = gpu_run(cuda_mod, plan, x, options=cuda_mod.OPT_NO_TENSOR_CORES)
     check(got[0], want)

@@ -119,7 +119,7 @@ template <int K, int S>
 struct DwWeights {
     static constexpr bool SMEM = K == 3 && S == 1;
     static constexpr bool HOLD = K == 3 && S == 2;
-    static constexpr int MIN_BLOCKS = SMEM ? 3 : 2;
+    static constexpr int MIN_BLOCKS = SMEM || (K == 5 && S == 1) ? 3 : 2;
 };
 
 template <int K, int S, bool QUICK>

@@ -738,3 +738,55 @@ def test_lane_layouts_back_to_back(cuda_mod):
                 for i in range(len(ws)):
                     assert np.array_equal(m.lane_output(i), want[i])
 
+
+
+def test_narrow_pointwise_rows(cuda_mod, oracle_mod):
+    """Narrow pointwise layers in both modes: a layer gated by a
+    squeeze-and-excite vector (the gate folded into its input loads), one
+    with a residual add folded in, lanes whose widths are not multiples of
+    four, a one-pixel lane; bit for bit against the oracle with every
+    contraction on the FP32 cores, within 1e-4 beside the tensor cores."""
+    rng = np.random.default_rng(21)
+    blobs, at = [], 0
+
+    def weights(n):
+        nonlocal at
+        v = rng.normal(0, 0.3, n).astype(np.float32)
+        blobs.append(v)
+        at += n
+        return (at - n, n)
+
+    ops = [Op("mean", x=0, y=1, ic=24, oc=24)]
+    op = window(Op("conv", x=1, y=2, ic=24, oc=24, fused="hardsigmoid"), (1, 1), 1, 0, 0)
+    op.w, op.b = weights(24 * 24), weights(24)
+    ops.append(op)
+    ops.append(Op("channelmul", x=0, y=3, ic=24, oc=24, x2=2))
+    op = window(Op("conv", x=3, y=4, ic=24, oc=48, fused="swish"), (1, 1), 1, 0, 0)
+    op.w, op.b = weights(24 * 48), weights(48)
+    ops.append(op)
+    op = window(Op("conv", x=4, y=5, ic=48, oc=48, fused="none"), (1, 1), 1, 0, 0)
+    op.w, op.b = weights(48 * 48), weights(48)
+    ops.append(op)
+    ops.append(Op("add", x=5, y=6, ic=48, oc=48, x2=4))
+    plan = encode((0, 16, 16, 24), 7, [6], ops, np.concatenate(blobs))
+    sizes = [(7, 13), (1, 1), (33, 129), (12, 66)]
+    xs = [rng.uniform(-1, 1, h * w * 24).astype(np.float32) for h, w in sizes]
+    o = oracle_mod.Oracle(plan)
+    wants = []
+    for (h, w), x in zip(sizes, xs):
+        o.set_size(h, w)
+        wants.append(o.run(x)[0])
+    for opts in (cuda_mod.OPT_NO_TENSOR_CORES, 0):
+        with cuda_mod.Model(plan) as m:
+            m.set_options(opts)
+            m.set_sizes(sizes)
+            for i, x in enumerate(xs):
+                m.lane_input_mut(i)[:] = x
+            m.run(60_000)
+            assert "gate+conv" in m.steps() and "conv+add" in m.steps(), m.steps()
+            for i, want in enumerate(wants):
+                got = m.lane_output(i)
+                if opts:
+                    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), sizes[i]
+                else:
+                    assert max_gap(got, want) <= 1e-4 * max(1.0, float(np.abs(want).max())), sizes[i]

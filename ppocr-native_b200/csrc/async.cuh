@@ -36,6 +36,21 @@ __device__ __forceinline__ bool try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
+// The same test, letting the hardware suspend the thread until the phase
+// completes or about `hint_ns` have passed: a waiting thread issues nothing
+// meanwhile (a plain poll loop takes issue slots from the working warps).
+__device__ __forceinline__ bool try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return done != 0;
+}
+
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -46,7 +61,7 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // clean-up after an abort: the copies or MMAs still in flight land first).
 __device__ __forceinline__ void drain(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
     const unsigned long long t0 = global_ns();
-    while (!try_wait(bar, parity))
+    while (!try_wait_sleep(bar, parity, 100000u))
         if (global_ns() - t0 > limit_ns) return;
 }
 

@@ -271,8 +271,8 @@ struct TcArgs {
     // SM, and slices are not narrowed for few tiles. Each output's sum is the
     // same whatever the grid and the slices.
     int min_tiles = 1;
-    // A CTC argmax head (vocab > 0, streamed, 1x1): no y; per row and column
-    // block, (max, sum of exp(logit - max), first column of the max) over
+    // A CTC argmax head (vocab > 0, 1x1, weights resident or streamed): no
+    // y; per row and column block, (max, sum of exp(logit - max), 0) over
     // the block's columns below vocab, into partial [M][blocks][3]. Block
     // 2s + h holds columns s*bn + h*16 + 32j + e (e < 16) of slice s.
     int vocab = 0;

@@ -40,6 +40,9 @@ constexpr int DYN_CEILING = 226 * 1024;
 // How long one wait on an mbarrier may take before the kernel gives up: a
 // K block's copy or MMAs take microseconds.
 constexpr unsigned long long WAIT_LIMIT_NS = 200ull * 1000 * 1000;
+// How long a waiting thread may stay suspended in an mbarrier before it
+// looks at the abort flag and the time limit again.
+constexpr uint32_t WAIT_SLEEP_NS = 20000;
 // Threads of the converter role (arrivals on a stage's `conv` barrier: one
 // per warp).
 constexpr int CONV_THREADS = 256;
@@ -84,16 +87,17 @@ __device__ __forceinline__ void commit(uint32_t bar) {
 
 // Waits for the phase of `bar` with this parity to complete. Gives up when
 // another role raised the abort flag, or after the time limit (then raises
-// it and records the error). BACKOFF: a wait expected to be long (a tile's
-// accumulator) sleeps between polls, leaving the issue slots to the roles on
-// the critical path.
+// it and records the error). The waiting thread stays suspended in the
+// barrier between looks (longer with BACKOFF: a wait expected to be long, a
+// tile's accumulator).
 template <bool BACKOFF = false>
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int *abort_flag, int *err) {
     if (try_wait(bar, parity)) return true;
     const unsigned long long t0 = global_ns();
     for (;;) {
-        if (BACKOFF) __nanosleep(200);
-        if (try_wait(bar, parity)) return true;
+        // suspended in the barrier (at most WAIT_SLEEP_NS a round) rather
+        // than polling: the roles on the critical path keep the issue slots
+        if (try_wait_sleep(bar, parity, BACKOFF ? WAIT_SLEEP_NS : WAIT_SLEEP_NS / 4)) return true;
         if (*abort_flag) return false;
         if (global_ns() - t0 > WAIT_LIMIT_NS) {
             *abort_flag = 1;
@@ -236,30 +240,33 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
         }
         if (MODE == EPI_CTC) {
             // this thread's row over the columns of its block, 16 at a
-            // time in increasing column order: the chunk's maximum (its
-            // first column on ties) raises the running one, then the
-            // chunk's exponentials (__expf, columns past vocab as zeros)
-            // join the running sum
+            // time in increasing column order: the chunk's maximum raises
+            // the running one (rescaling the sum), then the chunk's
+            // exponentials (__expf; columns past vocab count as -FLT_MAX,
+            // so as zeros) join the running sum. Only the block's maximum
+            // and sum are kept: the merge finds the class by recomputing
+            // every block near the row's maximum exactly.
             float m = -FLT_MAX, sum = 0.0f;
-            int best = 0x7fffffff;
             for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
                 float v[16];
                 tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);
                 float cm = -FLT_MAX;
-                int ci = 0x7fffffff;
+                if (x.n0 + c0 + 16 <= a.vocab) {
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const int col = x.n0 + c0 + j;
-                    v[j] = col < a.vocab ? v[j] + bias_s[c0 + j] : -FLT_MAX;
-                    if (v[j] > cm) {
-                        cm = v[j];
-                        ci = col;
+                    for (int j = 0; j < 16; j++) {
+                        v[j] += bias_s[c0 + j];
+                        cm = fmaxf(cm, v[j]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        v[j] = x.n0 + c0 + j < a.vocab ? v[j] + bias_s[c0 + j] : -FLT_MAX;
+                        cm = fmaxf(cm, v[j]);
                     }
                 }
                 if (cm > m) {
                     sum = m > -FLT_MAX ? sum * __expf(m - cm) : 0.0f;
                     m = cm;
-                    best = ci;
                 }
                 if (m > -FLT_MAX) {
                     float cs = 0.0f;
@@ -272,7 +279,7 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
                 float *st = a.partial + ((mrow + lane) * a.blocks + 2 * (x.n0 / x.BN) + half) * 3;
                 st[0] = m;
                 st[1] = sum;
-                st[2] = __int_as_float(best);
+                st[2] = 0.0f;  // (unused)
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();

@@ -33,9 +33,10 @@
 //   epilogue    8 warps: warp w drains TMEM lanes 32(w%4)..+31, 16 columns at
 //               a time (the two warps of a lane quadrant take alternate
 //               chunks), adds the bias, applies the activation (one
-//               instantiation per code, no branch per element), transposes
-//               through shared memory and stores rows (coalesced), adding the
-//               residual if any.
+//               instantiation per code, no branch per element), adds the
+//               residual if any, and stores: rows of at most 48 channels
+//               straight from each lane's registers (16-byte stores), wider
+//               ones transposed through shared memory into coalesced rows.
 // pw_tc_kernel keeps its slice's weights (all of K, both halves) resident in
 // shared memory; conv_tc_kernel, whose K runs to kh*kw*C, streams them with
 // the A blocks (one TMA copy per stage, from L2).

@@ -286,6 +286,38 @@ __device__ void role_epilogue(const TcArgs &a, const Ctx &x, int e, int warp, in
             if (lane == 0) arrive(smem_u32(&x.acce[buf]));  // one arrival per warp
             continue;
         }
+        if (MODE == EPI_PLAIN && vec && a.N <= 48) {
+            // narrow rows (at most 192 bytes) straight to memory: each lane
+            // stores its own four-channel groups, 16 bytes each (a row's
+            // pieces merge in L2), with no transpose through shared memory
+            // on the epilogue's critical path; wider rows are stored
+            // coalesced below, fewer L2 transactions per byte
+            const long m = mrow + lane;
+            for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
+                float v[16];
+                tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const int n = x.n0 + c0 + 4 * c;
+                    const float *bb = bias_s + c0 + 4 * c;
+                    float4 o = make_float4(activate_t<ACT, true>(fadd(v[4 * c], bb[0])),
+                                           activate_t<ACT, true>(fadd(v[4 * c + 1], bb[1])),
+                                           activate_t<ACT, true>(fadd(v[4 * c + 2], bb[2])),
+                                           activate_t<ACT, true>(fadd(v[4 * c + 3], bb[3])));
+                    if (lane >= nrows || n >= a.N) continue;
+                    if (a.res) {
+                        const float4 rr = __ldg(reinterpret_cast<const float4 *>(a.res + m * a.N + n));
+                        o = make_float4(activate(a.act2, fadd(o.x, rr.x)), activate(a.act2, fadd(o.y, rr.y)),
+                                        activate(a.act2, fadd(o.z, rr.z)), activate(a.act2, fadd(o.w, rr.w)));
+                    }
+                    *reinterpret_cast<float4 *>(a.y + m * a.N + n) = o;
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) arrive(smem_u32(&x.acce[buf]));  // one arrival per warp
+            continue;
+        }
         for (int c0 = half * 16; c0 < x.BN; c0 += 32) {
             float v[16];
             tmem_ld16(x.tmem + (uint32_t(qd * 32) << 16) + uint32_t(buf * x.BN + c0), v);

@@ -790,3 +790,41 @@ def test_narrow_pointwise_rows(cuda_mod, oracle_mod):
                     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), sizes[i]
                 else:
                     assert max_gap(got, want) <= 1e-4 * max(1.0, float(np.abs(want).max())), sizes[i]
+
+
+@pytest.mark.parametrize("k", [3, 5], ids=["folded-3x3", "5x5"])
+def test_conv_sources(cuda_mod, oracle_mod, k):
+    """A windowed conv over four sources, three of them nearest-upsampled
+    by 8, 4 and 2 (an upsample + concat chain, the DB head's shape) and the
+    second input at full size, folded into the conv as sources: on the FP32
+    cores read in place, bit for bit against the oracle; on the tensor cores
+    (their nearest-upsampled copy side by side, then the conv: 3-wide with
+    its horizontal taps folded, 5x5 not) within 1e-4 of the output's scale;
+    lanes of different sizes."""
+    from ppocr_native_b200.plan import Builder
+
+    b = Builder(64, 96, 24, np.random.default_rng(40 + k), None)
+    s8, s4, s2 = b.avgpool(0, (8, 8), (8, 8)), b.avgpool(0, (4, 4), (4, 4)), b.avgpool(0, (2, 2), (2, 2))
+    cat = b.concat(b.concat(b.upsample(s8, 8), b.upsample(s4, 4)), b.upsample(s2, 2))
+    y = b.conv(cat, 24, k=k, act="relu", x2=0)
+    plan = b.build([y])
+    sizes = [(64, 96), (32, 40), (8, 8), (48, 128)]
+    rng = np.random.default_rng(k)
+    xs = [rng.uniform(-1, 1, h * w * 24).astype(np.float32) for h, w in sizes]
+    o = oracle_mod.Oracle(plan)
+    wants = []
+    for (h, w), x in zip(sizes, xs):
+        o.set_size(h, w)
+        wants.append(o.run(x)[0])
+    for options in (0, cuda_mod.OPT_NO_TENSOR_CORES):
+        with cuda_mod.Model(plan) as m:
+            if options:
+                m.set_options(options)
+            m.set_sizes(sizes)
+            for i, x in enumerate(xs):
+                m.lane_input_mut(i)[:] = x
+            m.run(60_000)
+            assert any("sources" in st for st in m.steps()), m.steps()
+            for i, want in enumerate(wants):
+                check(m.lane_output(i).copy(), want, exact=bool(options),
+                      tol=TOL * max(1.0, float(np.abs(want).max())))

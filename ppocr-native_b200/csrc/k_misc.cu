@@ -126,9 +126,7 @@ __global__ void __launch_bounds__(256) pool_kernel(const PoolArgs a) {
         const int r = int(m - __ldg(&L.pix0));
         const int oy = r / ow, ox = r - oy * ow;
         const float *xn = a.x + __ldg(&L.ipix0) * a.c + c;
-        float v[VEC];
-#pragma unroll
-        for (int e = 0; e < VEC; e++) v[e] = 0.0f;
+        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // the first VEC used
         bool seeded = false;
         for (int ky = 0; ky < a.kh; ky++) {
             const int iy = oy * a.sh + ky;
@@ -137,10 +135,10 @@ __global__ void __launch_bounds__(256) pool_kernel(const PoolArgs a) {
                 const int ix = ox * a.sw + kx;
                 if (ix >= iw) continue;
                 const float *src = xn + ((long)iy * iw + ix) * a.c;
-                float x[VEC];
+                float x[4];
                 if (VEC == 4) {
                     const float4 q = __ldg(reinterpret_cast<const float4 *>(src));
-                    x[0] = q.x; x[1] = q.y; x[2 % VEC] = q.z; x[3 % VEC] = q.w;
+                    x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
                 } else {
                     x[0] = __ldg(src);
                 }
@@ -160,7 +158,7 @@ __global__ void __launch_bounds__(256) pool_kernel(const PoolArgs a) {
             if (a.average) v[e] = fdiv(v[e], float(a.kh * a.kw));
             if (VEC == 1) dst[e] = v[e];
         }
-        if (VEC == 4) *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1 % VEC], v[2 % VEC], v[3 % VEC]);
+        if (VEC == 4) *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
     }
 }
 

@@ -14,11 +14,17 @@ struct Tap {
     int near, far, near_w, far_w;
 };
 
-// Output coordinate d of a src -> dst resize: source (d + 0.5) * src / dst -
-// 0.5 in f64 rounded to f32, indices clamped to the edge, each weight
-// rounded to 1/2048 on its own (ties to even).
-__device__ __forceinline__ Tap resize_tap(int src, int dst, int d) {
-    const double scale = __ddiv_rn(1.0, __ddiv_rn(double(dst), double(src)));
+// The f64 scale of a src -> dst resize, 1 / (dst / src), rounded as the
+// reference rounds it (one value per axis: a kernel computes it once).
+__device__ __forceinline__ double resize_scale(int src, int dst) {
+    return __ddiv_rn(1.0, __ddiv_rn(double(dst), double(src)));
+}
+
+// Output coordinate d of a src -> dst resize whose scale is `scale`
+// (resize_scale): source (d + 0.5) * scale - 0.5 in f64 rounded to f32,
+// indices clamped to the edge, each weight rounded to 1/2048 on its own
+// (ties to even).
+__device__ __forceinline__ Tap resize_tap_scaled(int src, double scale, int d) {
     const float f = __double2float_rn(__dadd_rn(__dmul_rn(__dadd_rn(double(d), 0.5), scale), -0.5));
     const float fl = floorf(f);
     const float a = __fsub_rn(f, fl);
@@ -29,6 +35,10 @@ __device__ __forceinline__ Tap resize_tap(int src, int dst, int d) {
     t.near_w = __float2int_rn(__fmul_rn(__fsub_rn(1.0f, a), 2048.0f));
     t.far_w = __float2int_rn(__fmul_rn(a, 2048.0f));
     return t;
+}
+
+__device__ __forceinline__ Tap resize_tap(int src, int dst, int d) {
+    return resize_tap_scaled(src, resize_scale(src, dst), d);
 }
 
 // One channel of one output byte from its two source rows (RGB bytes): the

@@ -27,7 +27,6 @@ namespace ppocr {
 void set_last_error(const std::string &msg);
 }
 
-using ppocr::resize_tap;
 using ppocr::Tap;
 
 namespace {
@@ -41,11 +40,21 @@ struct ImageArgs {
 
 
 __global__ void __launch_bounds__(256) det_input_kernel(const ImageArgs a) {
-    const long total = long(a.ow) * a.oh;
+    // every output value is a function of its byte and channel alone: the
+    // 3 x 256 of them, computed once per block
+    __shared__ float norm[3][256];
     const float scale = __double2float_rn(__ddiv_rn(1.0, 255.0));
+    for (int e = threadIdx.x; e < 3 * 256; e += blockDim.x) {
+        const int c = e / 256, byte = e - c * 256;
+        const float x = __fmul_rn(float(byte), scale);
+        norm[c][byte] = __double2float_rn(__ddiv_rn(__dsub_rn(double(x), a.mean[c]), a.std[c]));
+    }
+    __syncthreads();
+    const double sy = ppocr::resize_scale(a.ih, a.oh), sx = ppocr::resize_scale(a.iw, a.ow);
+    const long total = long(a.ow) * a.oh;
     for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += long(gridDim.x) * blockDim.x) {
         const int oy = int(i / a.ow), ox = int(i - long(oy) * a.ow);
-        const Tap ty = resize_tap(a.ih, a.oh, oy), tx = resize_tap(a.iw, a.ow, ox);
+        const Tap ty = ppocr::resize_tap_scaled(a.ih, sy, oy), tx = ppocr::resize_tap_scaled(a.iw, sx, ox);
         const uint8_t *r0 = a.image + long(ty.near) * a.iw * 3, *r1 = a.image + long(ty.far) * a.iw * 3;
         float *o = a.out + i * 3;
 #pragma unroll
@@ -55,8 +64,7 @@ __global__ void __launch_bounds__(256) det_input_kernel(const ImageArgs a) {
             const int v = (((p >> 4) * ty.near_w) >> 16) + (((q >> 4) * ty.far_w) >> 16);
             int byte = (v + 2) >> 2;
             byte = byte < 0 ? 0 : byte > 255 ? 255 : byte;
-            const float x = __fmul_rn(float(byte), scale);
-            o[c] = __double2float_rn(__ddiv_rn(__dsub_rn(double(x), a.mean[c]), a.std[c]));
+            o[c] = norm[c][byte];
         }
     }
 }
@@ -71,6 +79,7 @@ struct RecArgs {
 };
 
 __global__ void __launch_bounds__(256) rec_input_kernel(const RecArgs a) {
+    const double sy = ppocr::resize_scale(a.ch, 48), sx = ppocr::resize_scale(a.cw, a.rw);
     const long total = long(a.width) * 48;
     for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += long(gridDim.x) * blockDim.x) {
         const int oy = int(i / a.width), ox = int(i - long(oy) * a.width);
@@ -79,7 +88,7 @@ __global__ void __launch_bounds__(256) rec_input_kernel(const RecArgs a) {
             o[0] = o[1] = o[2] = 0.0f;
             continue;
         }
-        const Tap ty = resize_tap(a.ch, 48, oy), tx = resize_tap(a.cw, a.rw, ox);
+        const Tap ty = ppocr::resize_tap_scaled(a.ch, sy, oy), tx = ppocr::resize_tap_scaled(a.cw, sx, ox);
         const uint8_t *r0 = a.crop + long(ty.near) * a.cw * 3, *r1 = a.crop + long(ty.far) * a.cw * 3;
 #pragma unroll
         for (int c = 0; c < 3; c++) {

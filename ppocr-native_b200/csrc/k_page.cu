@@ -228,6 +228,11 @@ __global__ void __launch_bounds__(256) crop_kernel(const CropArgs a) {
 // rw x 48 (INTER_LINEAR in the reference's staging), (v / 255 - 0.5) / 0.5
 // in f32, zeros from rw to the tensor width.
 __global__ void __launch_bounds__(256) rec_lines_kernel(const RecLinesArgs a) {
+    // each value is a function of its byte alone: the 256 of them once per block
+    __shared__ float norm[256];
+    for (int e = threadIdx.x; e < 256; e += blockDim.x)
+        norm[e] = __fdiv_rn(__fsub_rn(__fdiv_rn(float(e), 255.0f), 0.5f), 0.5f);
+    __syncthreads();
     for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < a.total; i += long(gridDim.x) * blockDim.x) {
         const int l = find_line(a.first, a.lines, i);
         const RecLine &L = a.line[l];
@@ -238,18 +243,18 @@ __global__ void __launch_bounds__(256) rec_lines_kernel(const RecLinesArgs a) {
             o[0] = o[1] = o[2] = 0.0f;
             continue;
         }
-        const Tap ty = resize_tap(L.ch, 48, oy), tx = resize_tap(L.cw, L.rw, ox);
+        const Tap ty = resize_tap_scaled(L.ch, L.sy, oy), tx = resize_tap_scaled(L.cw, L.sx, ox);
         const uint8_t *crop = a.crops + L.crop;
         const uint8_t *r0 = crop + long(ty.near) * L.cw * 3, *r1 = crop + long(ty.far) * L.cw * 3;
 #pragma unroll
-        for (int c = 0; c < 3; c++)
-            o[c] = __fdiv_rn(__fsub_rn(__fdiv_rn(float(blend(r0, r1, tx, ty, c)), 255.0f), 0.5f), 0.5f);
+        for (int c = 0; c < 3; c++) o[c] = norm[blend(r0, r1, tx, ty, c)];
     }
 }
 
 // The page fitted to its detector page: resized to fw x fh when the size
 // changes, `pad` rows of zeros above and below (det.rs:81-92).
 __global__ void __launch_bounds__(256) fit_page_kernel(const FitArgs a) {
+    const double sy = resize_scale(a.ih, a.fh), sx = resize_scale(a.iw, a.fw);
     const long total = long(a.fw) * (a.fh + 2 * a.pad);
     for (long i = long(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += long(gridDim.x) * blockDim.x) {
         const int oy = int(i / a.fw), ox = int(i - long(oy) * a.fw);
@@ -264,7 +269,7 @@ __global__ void __launch_bounds__(256) fit_page_kernel(const FitArgs a) {
             o[0] = s[0]; o[1] = s[1]; o[2] = s[2];
             continue;
         }
-        const Tap ty = resize_tap(a.ih, a.fh, y), tx = resize_tap(a.iw, a.fw, ox);
+        const Tap ty = resize_tap_scaled(a.ih, sy, y), tx = resize_tap_scaled(a.iw, sx, ox);
         const uint8_t *r0 = a.image + long(ty.near) * a.iw * 3, *r1 = a.image + long(ty.far) * a.iw * 3;
 #pragma unroll
         for (int c = 0; c < 3; c++) o[c] = uint8_t(blend(r0, r1, tx, ty, c));

@@ -69,6 +69,9 @@ struct RecLine {
     long crop;
     int cw, ch, rw, width;
     float *out;
+    // the resize's f64 scales, 1 / (48 / ch) and 1 / (rw / cw), IEEE-rounded
+    // on the host exactly as a device division rounds them
+    double sy, sx;
 };
 
 struct RecLinesArgs {

@@ -436,7 +436,8 @@ int ppocr_reader::recognise(const Quad *quads, size_t n, uint32_t timeout_ms) {
             size_t len = 0;
             float *in = ppocr_model_lane_device_input(rec, j, &len);
             if (!in || len != 48 * L.width * 3) return fail(PPOCR_E_UNSUPPORTED, "the recogniser's input is not 48 x width x 3");
-            rl[j] = RecLine{long(L.crop), int(L.cw), int(L.ch), int(L.rw), int(L.width), in};
+            rl[j] = RecLine{long(L.crop), int(L.cw), int(L.ch), int(L.rw), int(L.width), in,
+                            1.0 / (48.0 / double(L.ch)), 1.0 / (double(L.rw) / double(L.cw))};
             rf[j] = rec_px;
             rec_px += long(48 * L.width);
         }

@@ -277,6 +277,46 @@ __global__ void __launch_bounds__(128) layernorm_kernel(const LayerNormArgs a) {
         a.y[p * a.c + k] = fadd(fmul(fdiv(fsub(v[k], m), r), a.w[k]), a.w[a.c + k]);
 }
 
+// The tensor-core mode's LayerNorm (tolerance, not bits): one warp per
+// pixel, each lane summing its channels (k = lane, lane + 32, ...), the
+// partial sums folded to lane 0 by shuffles and broadcast from it, so every
+// lane normalizes with the same mean and deviation; the mean first, then the
+// squared deviations from it, as the exact kernel does.
+__global__ void __launch_bounds__(256) layernorm_fast_kernel(const LayerNormArgs a) {
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const long p = (long)blockIdx.x * 8 + warp;
+    if (p >= a.pixels) return;
+    const float *x = a.x + p * a.c;
+    constexpr int PER = 16;  // up to 512 channels
+    float v[PER];
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const int k = lane + 32 * j;
+        v[j] = k < a.c ? __ldg(x + k) : 0.0f;
+        s += v[j];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_down_sync(0xffffffffu, s, off);
+    const float m = __shfl_sync(0xffffffffu, s, 0) / float(a.c);
+    float q = 0.0f;
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const int k = lane + 32 * j;
+        const float d = v[j] - m;
+        if (k < a.c) q = fmaf(d, d, q);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) q += __shfl_down_sync(0xffffffffu, q, off);
+    const float var = __shfl_sync(0xffffffffu, q, 0) / float(a.c);
+    const float r = 1.0f / sqrtf(var + a.w[2 * a.c]);
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const int k = lane + 32 * j;
+        if (k < a.c) a.y[p * a.c + k] = fmaf((v[j] - m) * r, __ldg(a.w + k), __ldg(a.w + a.c + k));
+    }
+}
+
 // --------------------------------------------------------------- attention
 
 // One block per (lane, head, run of ATT_Q queries), one thread per query. Per
@@ -726,7 +766,10 @@ int launch_mean(const MeanArgs &a, cudaStream_t s) {
 }
 
 int launch_layernorm(const LayerNormArgs &a, cudaStream_t s) {
-    layernorm_kernel<<<(a.pixels + 3) / 4, 128, sizeof(float) * 4 * a.c, s>>>(a);
+    if (a.fast && a.c <= 512)
+        layernorm_fast_kernel<<<(a.pixels + 7) / 8, 256, 0, s>>>(a);
+    else
+        layernorm_kernel<<<(a.pixels + 3) / 4, 128, sizeof(float) * 4 * a.c, s>>>(a);
     return 1;
 }
 

@@ -191,6 +191,7 @@ struct LayerNormArgs {
     const float *x = nullptr, *w = nullptr;  // w = [gamma | beta | eps]
     float *y = nullptr;
     int pixels = 0, c = 0;
+    bool fast = false;  // tensor-core mode: the sums by warp-parallel reductions (another order)
 };
 
 struct AttentionArgs {

@@ -973,6 +973,7 @@ int ppocr_model::build_group(Group &g, std::string &err, Group *old) {
             LayerNormArgs a;
             a.x = buf(op.x); a.w = W.w(i); a.y = buf(op.y);
             a.pixels = int(total_out(g, i)); a.c = int(op.oc);
+            a.fast = tc_allowed;
             g.launches.push_back([a](cudaStream_t s) { return launch_layernorm(a, s); });
             break;
         }

@@ -215,7 +215,9 @@ def test_layernorm_attention(cuda_mod, oracle_mod):
     ln = Op("layernorm", x=0, y=1, ic=c, oc=c, w=(0, 2 * c + 1))
     xs = noise(t * c, 9, 3.0)
     plan = single(ln, (1, t, c), np.concatenate([gamma, beta, np.float32([1e-6])]))
-    check(gpu_run(cuda_mod, plan, xs)[0][0], oracle_run(oracle_mod, plan, xs)[0])
+    # beside the tensor cores the sums are warp reductions (within tolerance);
+    # on the FP32 cores the reference's order, bit for bit
+    check_both(cuda_mod, oracle_mod, plan, xs)
 
 
 def ctc_plan(kind, t, ci, vocab, seed=7):

@@ -549,8 +549,10 @@ def cpu_baseline(page, quads, budget_s: float = 15.0) -> dict:
             "sample": f"1 page: detector input + detector 1984x1536 + DB boxes ({s['t_det']:.2f} s), "
                       f"{s['lines']} of {s['of']} lines cropped, recognised and decoded ({s['t_rec']:.2f} s, "
                       "scaled to all); C restatement of the reference CPU engine and page steps (tier-3 FMA "
-                      "order; dense convolutions and the CTC head's logits in register-tiled AVX2+FMA 6 x 16 "
-                      "tiles like the reference's own), OpenMP over output rows; "
+                      "order; dense convolutions in register-tiled AVX2+FMA tiles of 4 pixels x 24 columns, "
+                      "the CTC head panel by panel over all time steps as the reference's, activations, "
+                      "softmax, attention and transposed convolutions vectorised, input resizes through the "
+                      "reference's byte tables), OpenMP over output rows; "
                       f"{s['gmacs_per_core']:.2f} GMAC/s per core over the whole page, against about 58 for the "
                       "reference's pointwise tile alone on one Zen 3 core (its README)",
             "gmacs_per_core": s["gmacs_per_core"]}

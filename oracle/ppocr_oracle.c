@@ -98,6 +98,21 @@ float orc_exp_neg(float z) {
     return fmaf(t * s, p, s);
 }
 
+/* exp_neg over eight lanes: orc_exp_neg's operations, one lane each (the
+ * same fused multiply-adds, shift, subtraction and cut-off). */
+static inline __m256 exp_neg8(__m256 z) {
+    __m256 n = _mm256_fmadd_ps(z, _mm256_set1_ps(LOG2E), _mm256_set1_ps(EXP_MAGIC_BIAS));
+    __m256 sc = _mm256_castsi256_ps(_mm256_slli_epi32(_mm256_castps_si256(n), 23));
+    n = _mm256_sub_ps(n, _mm256_set1_ps(EXP_MAGIC_BIAS));
+    __m256 t = _mm256_fmadd_ps(n, _mm256_set1_ps(MINUS_LN2), z);
+    __m256 q = _mm256_fmadd_ps(_mm256_set1_ps(EXP_C5), t, _mm256_set1_ps(EXP_C4));
+    q = _mm256_fmadd_ps(q, t, _mm256_set1_ps(EXP_C3));
+    q = _mm256_fmadd_ps(q, t, _mm256_set1_ps(EXP_C2));
+    q = _mm256_fmadd_ps(q, t, _mm256_set1_ps(EXP_C1));
+    __m256 r = _mm256_fmadd_ps(_mm256_mul_ps(t, sc), q, sc);
+    return _mm256_andnot_ps(_mm256_cmp_ps(z, _mm256_set1_ps(EXP_CUTOFF), _CMP_LT_OQ), r);
+}
+
 /* Rust's f32::clamp: NaN passes through. */
 static inline float clampf(float v, float lo, float hi) {
     if (v < lo) v = lo;
@@ -145,10 +160,90 @@ float orc_activation(int code, float v) {
     }
 }
 
+/* The activation over a span, one loop per code so that each one vectorises;
+ * every element takes the same operations as orc_activation. */
+/* clampf over eight lanes: below lo gives lo, then above hi gives hi, NaN
+ * passes through. */
+static inline __m256 clamp8(__m256 v, float lo, float hi) {
+    __m256 l = _mm256_set1_ps(lo), h = _mm256_set1_ps(hi);
+    v = _mm256_blendv_ps(v, l, _mm256_cmp_ps(v, l, _CMP_LT_OQ));
+    return _mm256_blendv_ps(v, h, _mm256_cmp_ps(v, h, _CMP_GT_OQ));
+}
+
+/* sigmoid_one over eight lanes; the sign bit of x picks f or 1 - f. */
+static inline __m256 sigmoid8(__m256 x) {
+    __m256 e = exp_neg8(_mm256_or_ps(x, _mm256_set1_ps(-0.0f)));
+    __m256 f = _mm256_div_ps(e, _mm256_add_ps(e, _mm256_set1_ps(1.0f)));
+    return _mm256_blendv_ps(_mm256_sub_ps(_mm256_set1_ps(1.0f), f), f, x);
+}
+
+/* gelu_one over eight lanes. */
+static inline __m256 gelu8(__m256 x) {
+    __m256 c = clamp8(x, -5.5f, 5.5f), sq = _mm256_mul_ps(c, c);
+    __m256 p = _mm256_set1_ps(f_of(PHI_P[5]));
+    for (int k = 4; k >= 0; k--) p = _mm256_fmadd_ps(p, sq, _mm256_set1_ps(f_of(PHI_P[k])));
+    __m256 q = _mm256_set1_ps(f_of(PHI_Q[4]));
+    for (int k = 3; k >= 0; k--) q = _mm256_fmadd_ps(q, sq, _mm256_set1_ps(f_of(PHI_Q[k])));
+    q = _mm256_fmadd_ps(q, sq, _mm256_set1_ps(1.0f));
+    __m256 g = _mm256_fmadd_ps(c, _mm256_div_ps(p, q), _mm256_set1_ps(0.5f));
+    return _mm256_mul_ps(x, clamp8(g, 0.0f, 1.0f));
+}
+
+/* Eight activations at a time with orc_activation's operations per lane. */
+static inline __m256 activation8(int code, __m256 v) {
+    switch (code) {
+    case A_RELU: return clamp8(v, 0.0f, INFINITY);
+    case A_SIGMOID: return sigmoid8(v);
+    case A_GELU: return gelu8(v);
+    case A_SWISH: return _mm256_mul_ps(v, sigmoid8(v));
+    case A_HARDSIGMOID:
+        return clamp8(_mm256_add_ps(_mm256_mul_ps(v, _mm256_set1_ps(HARDSIGMOID_ALPHA)), _mm256_set1_ps(0.5f)),
+                      0.0f, 1.0f);
+    case A_HARDSIGMOIDFIFTH:
+        return clamp8(_mm256_add_ps(_mm256_mul_ps(v, _mm256_set1_ps(0.2f)), _mm256_set1_ps(0.5f)), 0.0f, 1.0f);
+    case A_HARDSWISH:
+        return _mm256_mul_ps(v, clamp8(_mm256_add_ps(_mm256_mul_ps(v, _mm256_set1_ps(HARDSIGMOID_ALPHA)),
+                                                     _mm256_set1_ps(0.5f)),
+                                       0.0f, 1.0f));
+    default: return v;
+    }
+}
+
+/* The activation over a span, eight lanes at a time, the rest one by one;
+ * every element takes the same operations as orc_activation. */
+static void tail_span(float *y, size_t n, int code) {
+    size_t i = 0;
+#define TAIL_CASE(c)                                                                                               \
+    case c:                                                                                                        \
+        for (; i + 8 <= n; i += 8) _mm256_storeu_ps(y + i, activation8(c, _mm256_loadu_ps(y + i)));               \
+        break;
+    switch (code) {
+        TAIL_CASE(A_RELU)
+        TAIL_CASE(A_SIGMOID)
+        TAIL_CASE(A_GELU)
+        TAIL_CASE(A_SWISH)
+        TAIL_CASE(A_HARDSIGMOID)
+        TAIL_CASE(A_HARDSIGMOIDFIFTH)
+        TAIL_CASE(A_HARDSWISH)
+    default: break;
+    }
+#undef TAIL_CASE
+    for (; i < n; i++) y[i] = orc_activation(code, y[i]);
+}
+
+/* The fused activation of a layer's outputs. Spans of up to 64 Ki values
+ * (the per-pixel and per-tile calls, made from inside the layers' own
+ * parallel loops) run on the calling thread: opening a nested parallel
+ * region for each of them cost more than the activation itself. */
 static void tail(float *y, size_t n, int code) {
     if (code == A_NONE) return;
-#pragma omp parallel for schedule(static) if (n > 65536)
-    for (size_t i = 0; i < n; i++) y[i] = orc_activation(code, y[i]);
+    if (n <= 65536) {
+        tail_span(y, n, code);
+        return;
+    }
+    const size_t chunk = 16384, chunks = (n + chunk - 1) / chunk;
+#pragma omp parallel for schedule(static)
+    for (size_t k = 0; k < chunks; k++) tail_span(y + k * chunk, k + 1 < chunks ? chunk : n - k * chunk, code);
 }
 
 /* ------------------------------------------------------------------ parse */
@@ -477,21 +572,29 @@ void orc_set_fast(int on) { g_fast = on; }
 
 /* Whether the 6 output pixels from ox on all read every horizontal tap
  * inside the image (their ix run is monotonic in ox). */
-static int row_interior(const orc_op *op, size_t ox) {
-    long first = (long)(ox * op->sw) - op->pl, last = (long)((ox + 5) * op->sw + op->kw - 1) - op->pl;
-    return ox + 6 <= op->ow && first >= 0 && last < (long)op->iw;
+/* Whether output pixels ox .. ox + n - 1 of a row read only columns inside
+ * the input (no padded taps). */
+static int row_interior(const orc_op *op, size_t ox, size_t n) {
+    long first = (long)(ox * op->sw) - op->pl, last = (long)((ox + n - 1) * op->sw + op->kw - 1) - op->pl;
+    return ox + n <= op->ow && first >= 0 && last < (long)op->iw;
 }
 
-/* Six interior pixels of one output row, output columns o0 .. o0 + 8 * NV,
- * NV = 2 (16 columns) or 1 (8). */
-static inline void conv_tile6(const orc_op *op, const float *w, const float *b, const float *x, const float *x2,
-                              float *y, long oy, size_t ox, size_t o0, int nv) {
+/* The timed path's register tile: P interior pixels of one output row by
+ * output columns o0 .. o0 + 8 * NV, the accumulators in registers. Each
+ * output keeps conv_pixel's chain: the bias first or last per bias_first,
+ * taps in kernel row-major order, each tap's x channels then x2's, one fused
+ * multiply-add each. */
+static inline __attribute__((always_inline)) void conv_tile(const orc_op *op, const float *w, const float *b,
+                                                            const float *x, const float *x2, float *y, long oy,
+                                                            size_t ox, size_t o0, const int P, const int NV) {
     const size_t co = op->oc, ch = op->ic + op->n2;
-    __m256 acc[6][2];
-    int first[6];
-    for (int r = 0; r < 6; r++) {
+    __m256 acc[4][3];
+    int first[4];
+#pragma GCC unroll 6
+    for (int r = 0; r < P; r++) {
         first[r] = bias_first(op, ox + r);
-        for (int v = 0; v < nv; v++)
+#pragma GCC unroll 3
+        for (int v = 0; v < NV; v++)
             acc[r][v] = (b && first[r]) ? _mm256_loadu_ps(b + o0 + 8 * v) : _mm256_setzero_ps();
     }
     for (size_t ky = 0; ky < op->kh; ky++) {
@@ -499,41 +602,60 @@ static inline void conv_tile6(const orc_op *op, const float *w, const float *b, 
         if (iy < 0 || iy >= (long)op->ih) continue;
         for (size_t kx = 0; kx < op->kw; kx++) {
             const float *tap = w + (ky * op->kw + kx) * ch * co + o0;
-            const float *px[6], *px2[6];
-            for (int r = 0; r < 6; r++) {
-                size_t ix = (ox + r) * op->sw + kx - op->pl;
-                px[r] = x + ((size_t)iy * op->iw + ix) * op->ic;
-                px2[r] = op->n2 ? x2 + ((size_t)iy * op->iw + ix) * op->n2 : NULL;
-            }
+            const float *px[4];
+#pragma GCC unroll 6
+            for (int r = 0; r < P; r++)
+                px[r] = x + ((size_t)iy * op->iw + (ox + r) * op->sw + kx - op->pl) * op->ic;
             for (size_t i = 0; i < op->ic; i++) {
                 const float *row = tap + i * co;
-                __m256 w0 = _mm256_loadu_ps(row), w1 = nv > 1 ? _mm256_loadu_ps(row + 8) : w0;
-                for (int r = 0; r < 6; r++) {
+                __m256 wv[3];
+#pragma GCC unroll 3
+                for (int v = 0; v < NV; v++) wv[v] = _mm256_loadu_ps(row + 8 * v);
+#pragma GCC unroll 6
+                for (int r = 0; r < P; r++) {
                     __m256 xv = _mm256_broadcast_ss(px[r] + i);
-                    acc[r][0] = _mm256_fmadd_ps(w0, xv, acc[r][0]);
-                    if (nv > 1) acc[r][1] = _mm256_fmadd_ps(w1, xv, acc[r][1]);
+#pragma GCC unroll 3
+                    for (int v = 0; v < NV; v++) acc[r][v] = _mm256_fmadd_ps(wv[v], xv, acc[r][v]);
                 }
             }
-            for (size_t i = 0; i < op->n2; i++) {
-                const float *row = tap + (op->ic + i) * co;
-                __m256 w0 = _mm256_loadu_ps(row), w1 = nv > 1 ? _mm256_loadu_ps(row + 8) : w0;
-                for (int r = 0; r < 6; r++) {
-                    __m256 xv = _mm256_broadcast_ss(px2[r] + i);
-                    acc[r][0] = _mm256_fmadd_ps(w0, xv, acc[r][0]);
-                    if (nv > 1) acc[r][1] = _mm256_fmadd_ps(w1, xv, acc[r][1]);
+            if (op->n2) {
+#pragma GCC unroll 6
+                for (int r = 0; r < P; r++)
+                    px[r] = x2 + ((size_t)iy * op->iw + (ox + r) * op->sw + kx - op->pl) * op->n2;
+                for (size_t i = 0; i < op->n2; i++) {
+                    const float *row = tap + (op->ic + i) * co;
+                    __m256 wv[3];
+#pragma GCC unroll 3
+                    for (int v = 0; v < NV; v++) wv[v] = _mm256_loadu_ps(row + 8 * v);
+#pragma GCC unroll 6
+                    for (int r = 0; r < P; r++) {
+                        __m256 xv = _mm256_broadcast_ss(px[r] + i);
+#pragma GCC unroll 3
+                        for (int v = 0; v < NV; v++) acc[r][v] = _mm256_fmadd_ps(wv[v], xv, acc[r][v]);
+                    }
                 }
             }
         }
     }
-    for (int r = 0; r < 6; r++) {
+#pragma GCC unroll 6
+    for (int r = 0; r < P; r++) {
         float *out = y + ((size_t)oy * op->ow + ox + r) * co + o0;
-        for (int v = 0; v < nv; v++) {
+#pragma GCC unroll 3
+        for (int v = 0; v < NV; v++) {
             __m256 a = acc[r][v];
             if (b && !first[r]) a = _mm256_add_ps(a, _mm256_loadu_ps(b + o0 + 8 * v));
             _mm256_storeu_ps(out + 8 * v, a);
         }
     }
 }
+
+
+static void conv_tile_p4v3(const orc_op *op, const float *w, const float *b, const float *x, const float *x2,
+                           float *y, long oy, size_t ox, size_t o0) { conv_tile(op, w, b, x, x2, y, oy, ox, o0, 4, 3); }
+static void conv_tile_p4v2(const orc_op *op, const float *w, const float *b, const float *x, const float *x2,
+                           float *y, long oy, size_t ox, size_t o0) { conv_tile(op, w, b, x, x2, y, oy, ox, o0, 4, 2); }
+static void conv_tile_p4v1(const orc_op *op, const float *w, const float *b, const float *x, const float *x2,
+                           float *y, long oy, size_t ox, size_t o0) { conv_tile(op, w, b, x, x2, y, oy, ox, o0, 4, 1); }
 
 static void conv_pixel(const orc_plan *p, const orc_op *op, const float *x, const float *x2, float *y, long oy,
                        size_t ox);
@@ -542,16 +664,18 @@ static void conv_fast(const orc_plan *p, const orc_op *op, const float *x, const
     const float *w = W(p, op->w0), *b = op->b1 ? W(p, op->b0) : NULL;
     const size_t co = op->oc;
     long rows = (long)op->oh;
+    const size_t P = 4;
 #pragma omp parallel for schedule(static)
     for (long oy = 0; oy < rows; oy++) {
         size_t ox = 0;
         while (ox < op->ow) {
-            if (row_interior(op, ox)) {
+            if (row_interior(op, ox, P)) {
                 size_t o0 = 0;
-                for (; o0 + 16 <= co; o0 += 16) conv_tile6(op, w, b, x, x2, y, oy, ox, o0, 2);
-                for (; o0 + 8 <= co; o0 += 8) conv_tile6(op, w, b, x, x2, y, oy, ox, o0, 1);
-                for (int r = 0; r < 6; r++) tail(y + ((size_t)oy * op->ow + ox + r) * co, co, op->fused);
-                ox += 6;
+                for (; o0 + 24 <= co; o0 += 24) conv_tile_p4v3(op, w, b, x, x2, y, oy, ox, o0);
+                for (; o0 + 16 <= co; o0 += 16) conv_tile_p4v2(op, w, b, x, x2, y, oy, ox, o0);
+                for (; o0 + 8 <= co; o0 += 8) conv_tile_p4v1(op, w, b, x, x2, y, oy, ox, o0);
+                tail(y + ((size_t)oy * op->ow + ox) * co, P * co, op->fused);
+                ox += P;
             } else {
                 conv_pixel(p, op, x, x2, y, oy, ox);
                 ox++;
@@ -647,9 +771,9 @@ static void dwconv(const orc_plan *p, const orc_op *op, const float *x, float *y
         for (long oy = 0; oy < rows; oy++) {
             size_t ox = 0;
             while (ox < op->ow) {
-                if (row_interior(op, ox)) {
+                if (row_interior(op, ox, 6)) {
                     for (size_t c0 = 0; c0 < c; c0 += 8) dw_tile6(op, w, b, x, y, oy, ox, c0);
-                    for (int r = 0; r < 6; r++) tail(y + ((size_t)oy * op->ow + ox + r) * c, c, op->fused);
+                    tail(y + ((size_t)oy * op->ow + ox) * c, 6 * c, op->fused);
                     ox += 6;
                     continue;
                 }
@@ -780,12 +904,100 @@ static void softmax_row(float *v, size_t n) {
     for (size_t j = 0; j < n; j++) v[j] *= r;
 }
 
+/* softmax_row's operations, the eight lanes as one vector: the same lane
+ * maxima and lane sums, the same final reductions in lane order. */
+static void softmax_row_fast(float *v, size_t n) {
+    size_t body = n / 8 * 8;
+    __m256 lanes = _mm256_set1_ps(-INFINITY);
+    for (size_t j = 0; j < body; j += 8) {
+        __m256 a = _mm256_loadu_ps(v + j);
+        lanes = _mm256_blendv_ps(a, lanes, _mm256_cmp_ps(lanes, a, _CMP_GT_OQ));
+    }
+    float ln[8];
+    _mm256_storeu_ps(ln, lanes);
+    float mx = -INFINITY;
+    for (int l = 0; l < 8; l++) mx = fmaxf(mx, ln[l]);
+    for (size_t j = body; j < n; j++) mx = fmaxf(mx, v[j]);
+    __m256 sums = _mm256_setzero_ps(), m8 = _mm256_set1_ps(mx);
+    for (size_t j = 0; j < body; j += 8) {
+        __m256 e = exp_neg8(_mm256_sub_ps(_mm256_loadu_ps(v + j), m8));
+        _mm256_storeu_ps(v + j, e);
+        sums = _mm256_add_ps(sums, e);
+    }
+    _mm256_storeu_ps(ln, sums);
+    float sum = 0.0f;
+    for (int l = 0; l < 8; l++) sum += ln[l];
+    for (size_t j = body; j < n; j++) { v[j] = orc_exp_neg(v[j] - mx); sum += v[j]; }
+    float r = 1.0f / sum;
+    for (size_t j = 0; j < n; j++) v[j] *= r;
+}
+
+/* The timed path's attention for a head size of 9 to 16: attention's
+ * products with the accumulators in registers. Scores run eight keys a
+ * vector over a transposed copy of the head's keys, four queries at a time;
+ * S V runs the head's 16 (masked) value columns as two vectors, four query
+ * rows at a time. Every score and output keeps attention's chain (the head
+ * dimension in order, then the keys in order). */
+static void attention_fast(const float *x, float *y, size_t t, size_t c, size_t heads, float scale) {
+    const size_t hd = c / heads, tp = (t + 7) / 8 * 8;
+    const __m256i tailmask = _mm256_cmpgt_epi32(_mm256_set1_epi32((int)hd - 8), _mm256_setr_epi32(0, 1, 2, 3, 4, 5, 6, 7));
+#pragma omp parallel for schedule(static)
+    for (long hh = 0; hh < (long)heads; hh++) {
+        size_t h = (size_t)hh;
+        float *q = malloc(t * hd * sizeof(float)), *kt = calloc(hd * tp, sizeof(float));
+        float *scores = malloc(t * tp * sizeof(float));
+        for (size_t s = 0; s < t; s++)
+            for (size_t d = 0; d < hd; d++) q[s * hd + d] = x[s * 3 * c + h * hd + d] * scale;
+        for (size_t j = 0; j < t; j++)
+            for (size_t d = 0; d < hd; d++) kt[d * tp + j] = x[j * 3 * c + c + h * hd + d];
+        size_t s = 0;
+        for (; s < t; s += 4) {
+            const size_t rows = t - s < 4 ? t - s : 4;
+            for (size_t j = 0; j < tp; j += 8) {
+                __m256 acc[4] = {_mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps(), _mm256_setzero_ps()};
+                for (size_t d = 0; d < hd; d++) {
+                    __m256 kv = _mm256_loadu_ps(kt + d * tp + j);
+                    for (size_t r = 0; r < 4; r++)
+                        if (r < rows) acc[r] = _mm256_fmadd_ps(kv, _mm256_broadcast_ss(q + (s + r) * hd + d), acc[r]);
+                }
+                for (size_t r = 0; r < rows; r++) _mm256_storeu_ps(scores + (s + r) * tp + j, acc[r]);
+            }
+        }
+        for (size_t i = 0; i < t; i++) softmax_row_fast(scores + i * tp, t);
+        const float *v = x + 2 * c + h * hd;
+        for (size_t i = 0; i < t; i += 4) {
+            const size_t rows = t - i < 4 ? t - i : 4;
+            __m256 a0[4], a1[4];
+            for (int r = 0; r < 4; r++) { a0[r] = _mm256_setzero_ps(); a1[r] = _mm256_setzero_ps(); }
+            for (size_t j = 0; j < t; j++) {
+                __m256 v0 = _mm256_loadu_ps(v + j * 3 * c), v1 = _mm256_maskload_ps(v + j * 3 * c + 8, tailmask);
+                for (size_t r = 0; r < 4; r++)
+                    if (r < rows) {
+                        __m256 pr = _mm256_broadcast_ss(scores + (i + r) * tp + j);
+                        a0[r] = _mm256_fmadd_ps(v0, pr, a0[r]);
+                        a1[r] = _mm256_fmadd_ps(v1, pr, a1[r]);
+                    }
+            }
+            for (size_t r = 0; r < rows; r++) {
+                float *out = y + (i + r) * c + h * hd;
+                _mm256_storeu_ps(out, a0[r]);
+                _mm256_maskstore_ps(out + 8, tailmask, a1[r]);
+            }
+        }
+        free(q); free(kt); free(scores);
+    }
+}
+
 /* layers.rs:494-522: per head, scores (Q * scale) K^T with sums over the
  * head dimension in order, a softmax per row, then S V with sums over the
  * keys in order (both products through pointwise_with, no bias). */
 static void attention(const orc_plan *p, const orc_op *op, const float *x, float *y) {
     size_t t = op->iw, c = op->oc, heads = op->n2, hd = c / heads;
     float scale = *W(p, op->w0);
+    if (g_fast && hd > 8 && hd <= 16) {
+        attention_fast(x, y, t, c, heads, scale);
+        return;
+    }
     float *q = malloc(t * hd * sizeof(float)), *scores = malloc(t * t * sizeof(float));
     for (size_t h = 0; h < heads; h++) {
         for (size_t s = 0; s < t; s++)
@@ -809,6 +1021,104 @@ static void attention(const orc_plan *p, const orc_op *op, const float *x, float
     free(q); free(scores);
 }
 
+/* One panel's logits for ROWS time steps (bias first, inputs in order) and
+ * each step's online-softmax update, the eight lanes at once: state holds
+ * per step the lane maxima, sums and best columns (3 x 8 floats). */
+static inline __attribute__((always_inline)) void head_panel(const float *panel, const float *bias, const float *xv,
+                                                             size_t ci, float *state, float *y, size_t j,
+                                                             size_t vocab, int probs, size_t step0, int rows) {
+    __m256 acc[6][2];
+    for (int r = 0; r < rows; r++) {
+        acc[r][0] = _mm256_loadu_ps(bias);
+        acc[r][1] = _mm256_loadu_ps(bias + 8);
+    }
+    for (size_t i = 0; i < ci; i++) {
+        __m256 w0 = _mm256_loadu_ps(panel + i * 16), w1 = _mm256_loadu_ps(panel + i * 16 + 8);
+        for (int r = 0; r < rows; r++) {
+            __m256 xb = _mm256_broadcast_ss(xv + (size_t)r * ci + i);
+            acc[r][0] = _mm256_fmadd_ps(w0, xb, acc[r][0]);
+            acc[r][1] = _mm256_fmadd_ps(w1, xb, acc[r][1]);
+        }
+    }
+    const __m256 col = _mm256_add_ps(_mm256_set1_ps((float)(j * 16)), _mm256_setr_ps(0, 1, 2, 3, 4, 5, 6, 7));
+    for (int r = 0; r < rows; r++) {
+        float *st = state + (size_t)r * 24;
+        __m256 a0 = acc[r][0], a1 = acc[r][1];
+        __m256 mm = _mm256_loadu_ps(st), sum = _mm256_loadu_ps(st + 8), best = _mm256_loadu_ps(st + 16);
+        __m256 second = _mm256_cmp_ps(a1, a0, _CMP_GT_OQ);
+        __m256 top = _mm256_blendv_ps(a1, a0, _mm256_cmp_ps(a0, a1, _CMP_GT_OQ));
+        __m256 grown = _mm256_blendv_ps(top, mm, _mm256_cmp_ps(mm, top, _CMP_GT_OQ));
+        __m256 sn = _mm256_mul_ps(sum, exp_neg8(_mm256_sub_ps(mm, grown)));
+        sn = _mm256_add_ps(sn, exp_neg8(_mm256_sub_ps(a0, grown)));
+        sn = _mm256_add_ps(sn, exp_neg8(_mm256_sub_ps(a1, grown)));
+        __m256 c = _mm256_add_ps(col, _mm256_and_ps(second, _mm256_set1_ps(8.0f)));
+        best = _mm256_blendv_ps(best, c, _mm256_cmp_ps(top, mm, _CMP_GT_OQ));
+        _mm256_storeu_ps(st, grown);
+        _mm256_storeu_ps(st + 8, sn);
+        _mm256_storeu_ps(st + 16, best);
+        if (probs) {
+            float logits[16];
+            _mm256_storeu_ps(logits, a0);
+            _mm256_storeu_ps(logits + 8, a1);
+            size_t n = vocab - j * 16 < 16 ? vocab - j * 16 : 16;
+            memcpy(y + (step0 + (size_t)r) * vocab + j * 16, logits, n * sizeof(float));
+        }
+    }
+}
+
+/* The timed path's CTC head, as the reference's tier-3 head runs it: each
+ * 16-column panel stays in cache while every time step of the thread's
+ * block passes through it (six steps a register tile), so the weights are
+ * read once per block instead of once per step. Every step's logits and
+ * lane updates are the ones ctc_head's per-step loop makes, in the same
+ * order (panels in order), so the results are the same bits. */
+static void head_fast(const float *w, const float *b, const float *x, float *y, size_t t, size_t ci, size_t vocab,
+                      int probs) {
+    size_t npanels = (vocab + 15) / 16;
+    float *state = malloc(t * 24 * sizeof(float));
+    for (size_t pp = 0; pp < t; pp++)
+        for (int l = 0; l < 8; l++) {
+            state[pp * 24 + l] = -INFINITY;
+            state[pp * 24 + 8 + l] = 0.0f;
+            state[pp * 24 + 16 + l] = 0.0f;
+        }
+    long nthreads = omp_get_max_threads();
+    long per = ((long)t + nthreads - 1) / nthreads;
+    per = (per + 5) / 6 * 6;
+    long blocks = per ? ((long)t + per - 1) / per : 0;
+#pragma omp parallel for schedule(static)
+    for (long blk = 0; blk < blocks; blk++) {
+        size_t s0 = (size_t)(blk * per), s1 = s0 + (size_t)per < t ? s0 + (size_t)per : t;
+        for (size_t j = 0; j < npanels; j++) {
+            const float *panel = w + j * ci * 16, *bias = b + j * 16;
+            size_t pp = s0;
+            for (; pp + 6 <= s1; pp += 6)
+                head_panel(panel, bias, x + pp * ci, ci, state + pp * 24, y, j, vocab, probs, pp, 6);
+            for (; pp < s1; pp++)
+                head_panel(panel, bias, x + pp * ci, ci, state + pp * 24, y, j, vocab, probs, pp, 1);
+        }
+    }
+#pragma omp parallel for schedule(static)
+    for (long q = 0; q < (long)t; q++) {
+        size_t pp = (size_t)q;
+        const float *m = state + pp * 24, *sum = m + 8, *best = m + 16;
+        float mx = -INFINITY;
+        for (int l = 0; l < 8; l++) mx = fmaxf(mx, m[l]);
+        float total = 0.0f;
+        for (int l = 0; l < 8; l++) total += sum[l] * orc_exp_neg(m[l] - mx);
+        float rr = 1.0f / total;
+        if (probs) {
+            for (size_t k = 0; k < vocab; k++) y[pp * vocab + k] = orc_exp_neg(y[pp * vocab + k] - mx) * rr;
+        } else {
+            float bc = INFINITY;
+            for (int l = 0; l < 8; l++) if (m[l] == mx && best[l] < bc) bc = best[l];
+            y[2 * pp] = bc;
+            y[2 * pp + 1] = rr;
+        }
+    }
+    free(state);
+}
+
 /* layers.rs:692-832 (head_scalar, tier 3): logits from the bias, inputs
  * added in order; an online softmax in 8 lanes, lane l holding columns
  * 16j+l and 16j+8+l of panel j; the best column the first to reach the
@@ -818,69 +1128,12 @@ static void ctc_head(const orc_plan *p, const orc_op *op, const float *x, float 
     size_t npanels = (vocab + 15) / 16;
     const float *w = W(p, op->w0), *b = W(p, op->b0);
     long tl = (long)t;
-    /* the timed path: groups of six time steps, logits of a panel for all
-     * six in registers (the same chain per logit), then each step's update */
-    long groups = g_fast ? tl / 6 : 0;
-#pragma omp parallel for schedule(static)
-    for (long gi = 0; gi < groups; gi++) {
-        float m[6][8], sum[6][8], best[6][8], logits[6][16];
-        for (int r = 0; r < 6; r++)
-            for (int l = 0; l < 8; l++) { m[r][l] = -INFINITY; sum[r][l] = 0.0f; best[r][l] = 0.0f; }
-        const float *xv = x + (size_t)(gi * 6) * ci;
-        for (size_t j = 0; j < npanels; j++) {
-            const float *panel = w + j * ci * 16;
-            __m256 acc[6][2];
-            for (int r = 0; r < 6; r++) {
-                acc[r][0] = _mm256_loadu_ps(b + j * 16);
-                acc[r][1] = _mm256_loadu_ps(b + j * 16 + 8);
-            }
-            for (size_t i = 0; i < ci; i++) {
-                __m256 w0 = _mm256_loadu_ps(panel + i * 16), w1 = _mm256_loadu_ps(panel + i * 16 + 8);
-                for (int r = 0; r < 6; r++) {
-                    __m256 xb = _mm256_broadcast_ss(xv + (size_t)r * ci + i);
-                    acc[r][0] = _mm256_fmadd_ps(w0, xb, acc[r][0]);
-                    acc[r][1] = _mm256_fmadd_ps(w1, xb, acc[r][1]);
-                }
-            }
-            for (int r = 0; r < 6; r++) {
-                _mm256_storeu_ps(logits[r], acc[r][0]);
-                _mm256_storeu_ps(logits[r] + 8, acc[r][1]);
-                for (int l = 0; l < 8; l++) {
-                    float a0 = logits[r][l], a1 = logits[r][8 + l], mm = m[r][l];
-                    float top = a0 > a1 ? a0 : a1;
-                    float grown = mm > top ? mm : top;
-                    float s = sum[r][l] * orc_exp_neg(mm - grown);
-                    s += orc_exp_neg(a0 - grown);
-                    s += orc_exp_neg(a1 - grown);
-                    m[r][l] = grown; sum[r][l] = s;
-                    if (top > mm) best[r][l] = (float)(j * 16 + l + (a1 > a0 ? 8 : 0));
-                }
-                if (probs) {
-                    size_t n = vocab - j * 16 < 16 ? vocab - j * 16 : 16;
-                    memcpy(y + (size_t)(gi * 6 + r) * vocab + j * 16, logits[r], n * sizeof(float));
-                }
-            }
-        }
-        for (int r = 0; r < 6; r++) {
-            long pp = gi * 6 + r;
-            float mx = -INFINITY;
-            for (int l = 0; l < 8; l++) mx = fmaxf(mx, m[r][l]);
-            float total = 0.0f;
-            for (int l = 0; l < 8; l++) total += sum[r][l] * orc_exp_neg(m[r][l] - mx);
-            float rr = 1.0f / total;
-            if (probs) {
-                for (size_t k = 0; k < vocab; k++)
-                    y[(size_t)pp * vocab + k] = orc_exp_neg(y[(size_t)pp * vocab + k] - mx) * rr;
-            } else {
-                float bc = INFINITY;
-                for (int l = 0; l < 8; l++) if (m[r][l] == mx && best[r][l] < bc) bc = best[r][l];
-                y[2 * pp] = bc;
-                y[2 * pp + 1] = rr;
-            }
-        }
+    if (g_fast) {
+        head_fast(w, b, x, y, t, ci, vocab, probs);
+        return;
     }
 #pragma omp parallel for schedule(static)
-    for (long pp = groups * 6; pp < tl; pp++) {
+    for (long pp = 0; pp < tl; pp++) {
         float m[8], sum[8], best[8], logits[16];
         for (int l = 0; l < 8; l++) { m[l] = -INFINITY; sum[l] = 0.0f; best[l] = 0.0f; }
         const float *xv = x + (size_t)pp * ci;
@@ -925,10 +1178,100 @@ static void ctc_head(const orc_plan *p, const orc_op *op, const float *x, float 
 /* layers.rs:595-680: each input pixel's channels times w [ic][kh][kw][oc]
  * give its kh x kw block of outputs (bias per tap, placed as a pointwise
  * layer of kh*kw*oc columns places it), then the tail. */
+/* Columns c0 .. c0 + 8 * NV of one input pixel's block of a transposed
+ * convolution, in registers, stored where they land in the output rows of
+ * `out` (a column group never crosses a kernel row: kw * oc is a multiple
+ * of eight). */
+static inline __attribute__((always_inline)) void ct_cols(const orc_op *op, const float *px, const float *w,
+                                                          const float *b, int first, float *out, size_t ix,
+                                                          size_t c0, const int NV) {
+    const size_t cols = op->kh * op->kw * op->oc, span = op->kw * op->oc;
+    __m256 acc[8];
+#pragma GCC unroll 8
+    for (int v = 0; v < NV; v++) acc[v] = (b && first) ? _mm256_loadu_ps(b + c0 + 8 * v) : _mm256_setzero_ps();
+    for (size_t i = 0; i < op->ic; i++) {
+        __m256 xv = _mm256_broadcast_ss(px + i);
+        const float *row = w + i * cols + c0;
+#pragma GCC unroll 8
+        for (int v = 0; v < NV; v++) acc[v] = _mm256_fmadd_ps(_mm256_loadu_ps(row + 8 * v), xv, acc[v]);
+    }
+#pragma GCC unroll 8
+    for (int v = 0; v < NV; v++) {
+        size_t c = c0 + 8 * (size_t)v, ky = c / span, k = c % span;
+        __m256 a = acc[v];
+        if (b && !first) a = _mm256_add_ps(a, _mm256_loadu_ps(b + c));
+        _mm256_storeu_ps(out + (ky * op->ow + ix * op->kw) * op->oc + k, a);
+    }
+}
+
+/* The timed path's transposed convolution: each input pixel's block of
+ * kh*kw*oc outputs in registers (eight columns a lane group; four-column
+ * blocks two pixels at a time, one per half), stored in place (the kw*oc
+ * outputs of one kernel row lie side by side), the activation once per
+ * output row pair. Every output keeps convtranspose's chain: the bias first
+ * or last as there, then the input channels in order. */
+static void convtranspose_fast(const orc_op *op, const float *w, const float *b, const float *x, float *y) {
+    const size_t cols = op->kh * op->kw * op->oc, span = op->kw * op->oc, ic = op->ic;
+    const int first = cols % 16 == 0;
+    long rows = (long)op->ih;
+#pragma omp parallel for schedule(static)
+    for (long iy = 0; iy < rows; iy++) {
+        float *out = y + (size_t)iy * op->kh * op->ow * op->oc;
+        if (cols == 4) {
+            const __m256 bias = b ? _mm256_setr_ps(b[0], b[1], b[2], b[3], b[0], b[1], b[2], b[3])
+                                  : _mm256_setzero_ps();
+            size_t ix = 0;
+            for (; ix + 2 <= op->iw; ix += 2) {
+                const float *p0 = x + ((size_t)iy * op->iw + ix) * ic, *p1 = p0 + ic;
+                __m256 acc = (b && first) ? bias : _mm256_setzero_ps();
+                for (size_t i = 0; i < ic; i++) {
+                    __m128 wr = _mm_loadu_ps(w + i * 4);
+                    __m256 wv = _mm256_set_m128(wr, wr);
+                    __m256 xv = _mm256_set_m128(_mm_broadcast_ss(p1 + i), _mm_broadcast_ss(p0 + i));
+                    acc = _mm256_fmadd_ps(wv, xv, acc);
+                }
+                if (b && !first) acc = _mm256_add_ps(acc, bias);
+                float v[8];
+                _mm256_storeu_ps(v, acc);
+                for (size_t ky = 0; ky < op->kh; ky++) {
+                    float *o = out + (ky * op->ow + ix * op->kw) * op->oc;
+                    memcpy(o, v + ky * span, span * sizeof(float));
+                    memcpy(o + span, v + 4 + ky * span, span * sizeof(float));
+                }
+            }
+            for (; ix < op->iw; ix++) {
+                const float *px = x + ((size_t)iy * op->iw + ix) * ic;
+                float v[4];
+                for (size_t o = 0; o < 4; o++) v[o] = (b && first) ? b[o] : 0.0f;
+                for (size_t i = 0; i < ic; i++)
+                    for (size_t o = 0; o < 4; o++) v[o] = fmaf(w[i * 4 + o], px[i], v[o]);
+                if (b && !first)
+                    for (size_t o = 0; o < 4; o++) v[o] += b[o];
+                for (size_t ky = 0; ky < op->kh; ky++)
+                    memcpy(out + (ky * op->ow + ix * op->kw) * op->oc, v + ky * span, span * sizeof(float));
+            }
+        } else {
+            for (size_t ix = 0; ix < op->iw; ix++) {
+                const float *px = x + ((size_t)iy * op->iw + ix) * ic;
+                size_t c0 = 0;
+                for (; c0 + 64 <= cols; c0 += 64) ct_cols(op, px, w, b, first, out, ix, c0, 8);
+                for (; c0 + 32 <= cols; c0 += 32) ct_cols(op, px, w, b, first, out, ix, c0, 4);
+                for (; c0 + 16 <= cols; c0 += 16) ct_cols(op, px, w, b, first, out, ix, c0, 2);
+                for (; c0 + 8 <= cols; c0 += 8) ct_cols(op, px, w, b, first, out, ix, c0, 1);
+            }
+        }
+        tail(out, op->kh * op->ow * op->oc, op->fused);
+    }
+}
+
 static void convtranspose(const orc_plan *p, const orc_op *op, const float *x, float *y) {
     const float *w = W(p, op->w0), *b = op->b1 ? W(p, op->b0) : NULL;
     size_t cols = op->kh * op->kw * op->oc;
     long rows = (long)op->ih;
+    if (g_fast && (cols == 4 || (cols % 8 == 0 && (op->kw * op->oc) % 8 == 0))) {
+        convtranspose_fast(op, w, b, x, y);
+        return;
+    }
 #pragma omp parallel for schedule(static)
     for (long iy = 0; iy < rows; iy++) {
         float *block = malloc(cols * sizeof(float));
@@ -1064,22 +1407,33 @@ int orc_det_input_hwc(const unsigned char *image, size_t iw, size_t ih, size_t o
                       const double *std, float *out) {
     if (!iw || !ih || !ow || !oh) return 1;
     const float scale = (float)(1.0 / 255.0);
-    for (size_t oy = 0; oy < oh; oy++) {
+    /* the reference's per-channel table of the 256 byte values (det.rs:239-241)
+     * and the column taps, computed once; bands of rows over the threads */
+    float table[3][256];
+    for (int c = 0; c < 3; c++)
+        for (int v = 0; v < 256; v++) table[c][v] = (float)(((double)((float)v * scale) - mean[c]) / std[c]);
+    orc_tap *tx = malloc(ow * sizeof(orc_tap));
+    if (!tx) return 1;
+    for (size_t ox = 0; ox < ow; ox++) tx[ox] = orc_resize_tap(iw, ow, ox);
+#pragma omp parallel for schedule(static)
+    for (long y = 0; y < (long)oh; y++) {
+        const size_t oy = (size_t)y;
         const orc_tap ty = orc_resize_tap(ih, oh, oy);
+        const unsigned char *r0 = image + ty.near * iw * 3, *r1 = image + ty.far * iw * 3;
+        float *o = out + oy * ow * 3;
         for (size_t ox = 0; ox < ow; ox++) {
-            const orc_tap tx = orc_resize_tap(iw, ow, ox);
+            const orc_tap t = tx[ox];
             for (int c = 0; c < 3; c++) {
-                const unsigned char *r0 = image + ty.near * iw * 3, *r1 = image + ty.far * iw * 3;
-                const int a = (int)r0[tx.near * 3 + c] * tx.near_w + (int)r0[tx.far * 3 + c] * tx.far_w;
-                const int b = (int)r1[tx.near * 3 + c] * tx.near_w + (int)r1[tx.far * 3 + c] * tx.far_w;
+                const int a = (int)r0[t.near * 3 + c] * t.near_w + (int)r0[t.far * 3 + c] * t.far_w;
+                const int b = (int)r1[t.near * 3 + c] * t.near_w + (int)r1[t.far * 3 + c] * t.far_w;
                 const int v = (((a >> 4) * ty.near_w) >> 16) + (((b >> 4) * ty.far_w) >> 16);
                 int byte = (v + 2) >> 2;
                 byte = byte < 0 ? 0 : byte > 255 ? 255 : byte;
-                const float x = (float)byte * scale;
-                out[(oy * ow + ox) * 3 + c] = (float)(((double)x - mean[c]) / std[c]);
+                o[ox * 3 + c] = table[c][byte];
             }
         }
     }
+    free(tx);
     return 0;
 }
 
@@ -1094,24 +1448,28 @@ size_t orc_rec_input_hwc(const unsigned char *crop, size_t cw, size_t ch, float 
     const double fitted = ceil(height * (w / h));
     const size_t rw = fitted > (double)width ? width : (size_t)fitted;
     if (!out) return width;
+    float table[256];
+    for (int v = 0; v < 256; v++) table[v] = ((float)v / 255.0f - 0.5f) / 0.5f;
+    orc_tap *tx = malloc((rw ? rw : 1) * sizeof(orc_tap));
+    if (!tx) return 0;
+    for (size_t ox = 0; ox < rw; ox++) tx[ox] = orc_resize_tap(cw, rw, ox);
     for (size_t oy = 0; oy < 48; oy++) {
         const orc_tap ty = orc_resize_tap(ch, 48, oy);
-        for (size_t ox = 0; ox < width; ox++) {
+        const unsigned char *r0 = crop + ty.near * cw * 3, *r1 = crop + ty.far * cw * 3;
+        float *o = out + oy * width * 3;
+        for (size_t ox = 0; ox < rw; ox++) {
+            const orc_tap t = tx[ox];
             for (int c = 0; c < 3; c++) {
-                float val = 0.0f;
-                if (ox < rw) {
-                    const orc_tap tx = orc_resize_tap(cw, rw, ox);
-                    const unsigned char *r0 = crop + ty.near * cw * 3, *r1 = crop + ty.far * cw * 3;
-                    const int a = (int)r0[tx.near * 3 + c] * tx.near_w + (int)r0[tx.far * 3 + c] * tx.far_w;
-                    const int b = (int)r1[tx.near * 3 + c] * tx.near_w + (int)r1[tx.far * 3 + c] * tx.far_w;
-                    const int v = (((a >> 4) * ty.near_w) >> 16) + (((b >> 4) * ty.far_w) >> 16);
-                    int byte = (v + 2) >> 2;
-                    byte = byte < 0 ? 0 : byte > 255 ? 255 : byte;
-                    val = ((float)byte / 255.0f - 0.5f) / 0.5f;
-                }
-                out[(oy * width + ox) * 3 + c] = val;
+                const int a = (int)r0[t.near * 3 + c] * t.near_w + (int)r0[t.far * 3 + c] * t.far_w;
+                const int b = (int)r1[t.near * 3 + c] * t.near_w + (int)r1[t.far * 3 + c] * t.far_w;
+                const int v = (((a >> 4) * ty.near_w) >> 16) + (((b >> 4) * ty.far_w) >> 16);
+                int byte = (v + 2) >> 2;
+                byte = byte < 0 ? 0 : byte > 255 ? 255 : byte;
+                o[ox * 3 + c] = table[byte];
             }
         }
+        for (size_t k = rw * 3; k < width * 3; k++) o[k] = 0.0f;
     }
+    free(tx);
     return width;
 }

@@ -32,6 +32,29 @@ def activation_values(oracle_mod, code: str, xs: np.ndarray) -> np.ndarray:
     return np.array([oracle_mod.activation(ACT[code], float(v)) for v in xs], np.float32)
 
 
+@pytest.mark.parametrize("n", [1003, 70001])
+@pytest.mark.parametrize("code", ["relu", "sigmoid", "gelu", "swish", "hardsigmoid", "hardsigmoidfifth",
+                                  "hardswish"])
+def test_layer_activations_match_the_scalar_definition(oracle_mod, code, n):
+    """A layer's fused activation (eight lanes at a time, the rest one by
+    one, spans past 64 Ki values split over threads) gives orc_activation's
+    bits on every value: signed zeros, infinities, NaN, the exp cut-off and
+    the clamp edges among seeded normals of several scales."""
+    special = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 87.3, -87.3, 88.8, -88.8, 104.0, -104.0, 3.0, -3.0,
+                        2.9999998, -2.9999998, 5.5, -5.5, 6.0, -6.0, 2.5, -2.5, 1e-30, -1e-30, 1e-7, -1e-7],
+                       np.float32)
+    rng = np.random.default_rng(n)
+    xs = np.concatenate([special, (rng.standard_normal(n - special.size) *
+                                   rng.choice([0.1, 1.0, 10.0, 100.0], n - special.size)).astype(np.float32)])
+    got = oracle_mod.Oracle(act_plan(code, xs)).run(xs)[0]
+    with np.errstate(invalid="ignore", over="ignore"):
+        zero_conv = xs * np.float32(0.0) + np.float32(0.0)  # the plan's zero-weight conv: NaN at the infinities
+        want = activation_values(oracle_mod, code, xs + zero_conv)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    ok = ~np.isnan(want)
+    assert np.array_equal(got[ok].view(np.uint32), want[ok].view(np.uint32))
+
+
 # activation.rs:241-300 (sigmoid_tiers_match_scalar_and_libm)
 def test_sigmoid_within_1e7_of_float64(oracle_mod):
     xs = np.concatenate([(np.arange(4000, dtype=np.float32) - 2000) * np.float32(0.0517),
@@ -379,6 +402,12 @@ def test_timed_path_gives_the_plain_loops_bits(oracle_mod):
              (synth.rec_plan(seed=3, std=None, vocab=700), (48, 328)),
              (synth.rec_plan(seed=3, std=None, vocab=300, logits=True), (48, 100)),
              (synth.fused_layer_plan(seed=0, h=23, w=31), (23, 31))]
+    for oc, fused in [(1, "sigmoid"), (4, "relu"), (8, "swish")]:  # 4-, 16- and 32-column blocks
+        w = noise(5 * 4 * oc, 3, 0.5)
+        bias = noise(4 * oc, 4, 0.5)
+        op = Op("convtranspose", x=0, y=1, ic=5, oc=oc, kh=2, kw=2, sh=2, sw=2, fused=fused,
+                w=(0, w.size), b=(w.size, bias.size))
+        cases.append((single(op, (3, 7, 5), np.concatenate([w, bias])), (3, 7)))
     try:
         for plan, (h, w) in cases:
             p = oracle_mod.Oracle(plan)

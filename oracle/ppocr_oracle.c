@@ -660,28 +660,55 @@ static void conv_tile_p4v1(const orc_op *op, const float *w, const float *b, con
 static void conv_pixel(const orc_plan *p, const orc_op *op, const float *x, const float *x2, float *y, long oy,
                        size_t ox);
 
-static void conv_fast(const orc_plan *p, const orc_op *op, const float *x, const float *x2, float *y) {
+/* One output row of the timed path's dense convolution: 4-pixel register
+ * tiles where the window lies inside the input, conv_pixel elsewhere. */
+static void conv_fast_row(const orc_plan *p, const orc_op *op, const float *w, const float *b, const float *x,
+                          const float *x2, float *y, long oy) {
+    const size_t co = op->oc, P = 4;
+    size_t ox = 0;
+    while (ox < op->ow) {
+        if (row_interior(op, ox, P)) {
+            size_t o0 = 0;
+            for (; o0 + 24 <= co; o0 += 24) conv_tile_p4v3(op, w, b, x, x2, y, oy, ox, o0);
+            for (; o0 + 16 <= co; o0 += 16) conv_tile_p4v2(op, w, b, x, x2, y, oy, ox, o0);
+            for (; o0 + 8 <= co; o0 += 8) conv_tile_p4v1(op, w, b, x, x2, y, oy, ox, o0);
+            tail(y + ((size_t)oy * op->ow + ox) * co, P * co, op->fused);
+            ox += P;
+        } else {
+            conv_pixel(p, op, x, x2, y, oy, ox);
+            ox++;
+        }
+    }
+}
+
+/* The timed path's dense convolution, rows over the threads. With `mean`
+ * (the convolution feeds a channel mean), each finished row is added to
+ * the mean's f64 sums in row order while it is still in the cache of the
+ * thread that wrote it, the reference's fused mean (layers.rs:408-431):
+ * mean()'s sums, in mean()'s order. */
+static void conv_fast(const orc_plan *p, const orc_op *op, const float *x, const float *x2, float *y, float *mean) {
     const float *w = W(p, op->w0), *b = op->b1 ? W(p, op->b0) : NULL;
     const size_t co = op->oc;
     long rows = (long)op->oh;
-    const size_t P = 4;
+    if (!mean) {
 #pragma omp parallel for schedule(static)
+        for (long oy = 0; oy < rows; oy++) conv_fast_row(p, op, w, b, x, x2, y, oy);
+        return;
+    }
+    double *sums = calloc(co, sizeof(double));
+#pragma omp parallel for schedule(static, 1) ordered
     for (long oy = 0; oy < rows; oy++) {
-        size_t ox = 0;
-        while (ox < op->ow) {
-            if (row_interior(op, ox, P)) {
-                size_t o0 = 0;
-                for (; o0 + 24 <= co; o0 += 24) conv_tile_p4v3(op, w, b, x, x2, y, oy, ox, o0);
-                for (; o0 + 16 <= co; o0 += 16) conv_tile_p4v2(op, w, b, x, x2, y, oy, ox, o0);
-                for (; o0 + 8 <= co; o0 += 8) conv_tile_p4v1(op, w, b, x, x2, y, oy, ox, o0);
-                tail(y + ((size_t)oy * op->ow + ox) * co, P * co, op->fused);
-                ox += P;
-            } else {
-                conv_pixel(p, op, x, x2, y, oy, ox);
-                ox++;
-            }
+        conv_fast_row(p, op, w, b, x, x2, y, oy);
+#pragma omp ordered
+        {
+            const float *r = y + (size_t)oy * op->ow * co;
+            for (size_t px = 0; px < op->ow; px++)
+                for (size_t k = 0; k < co; k++) sums[k] += (double)r[px * co + k];
         }
     }
+    const size_t pixels = op->oh * op->ow;
+    for (size_t k = 0; k < co; k++) mean[k] = (float)(sums[k] / (double)pixels);
+    free(sums);
 }
 
 /* Dense convolution of any window over the channel concatenation of x (ic
@@ -729,7 +756,7 @@ static void conv_pixel(const orc_plan *p, const orc_op *op, const float *x, cons
 
 static void conv(const orc_plan *p, const orc_op *op, const float *x, const float *x2, float *y) {
     if (g_fast && op->oc % 8 == 0) {
-        conv_fast(p, op, x, x2, y);
+        conv_fast(p, op, x, x2, y, NULL);
         return;
     }
     long rows = (long)op->oh;
@@ -1326,7 +1353,16 @@ int orc_run(orc_plan *p, const float *input, float *const *outputs, int threads)
         float *y = buf[op->y];
         size_t n = op->oh * op->ow * op->oc;
         switch (op->kind) {
-        case K_CONV: conv(p, op, x, x2, y); break;
+        case K_CONV:
+            if (g_fast && op->oc % 8 == 0 && i + 1 < p->nops && p->ops[i + 1].kind == K_MEAN &&
+                p->ops[i + 1].x == op->y && p->ops[i + 1].y != op->y && p->ops[i + 1].ic == op->oc &&
+                p->ops[i + 1].ih == op->oh && p->ops[i + 1].iw == op->ow) {
+                conv_fast(p, op, x, x2, y, buf[p->ops[i + 1].y]); /* and the mean after it */
+                i++;
+                break;
+            }
+            conv(p, op, x, x2, y);
+            break;
         case K_DWCONV: dwconv(p, op, x, y); break;
         case K_ADD: /* conv.rs:74-79 */
 #pragma omp parallel for schedule(static)

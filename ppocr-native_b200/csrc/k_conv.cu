@@ -507,13 +507,16 @@ __global__ void __launch_bounds__(256) stem_rows_kernel(const ConvArgs a) {
         for (int j = 0; j < HALF; j++) acc[j] = bs[h * HALF + j];
 #pragma unroll
         for (int k = 0; k < 27; k++) {
+            const float2 xk = make_float2(in[k], in[k]);
 #pragma unroll
             for (int j = 0; j < HALF; j += 4) {
                 const float4 w4 = *reinterpret_cast<const float4 *>(ws + k * NB + h * HALF + j);  // broadcast
-                acc[j] = ffma(w4.x, in[k], acc[j]);
-                acc[j + 1] = ffma(w4.y, in[k], acc[j + 1]);
-                acc[j + 2] = ffma(w4.z, in[k], acc[j + 2]);
-                acc[j + 3] = ffma(w4.w, in[k], acc[j + 3]);
+                const float2 lo = ffma2(make_float2(w4.x, w4.y), xk, make_float2(acc[j], acc[j + 1]));
+                const float2 hi = ffma2(make_float2(w4.z, w4.w), xk, make_float2(acc[j + 2], acc[j + 3]));
+                acc[j] = lo.x;
+                acc[j + 1] = lo.y;
+                acc[j + 2] = hi.x;
+                acc[j + 3] = hi.y;
             }
         }
         float *out = yout + p * OS + h * HALF;

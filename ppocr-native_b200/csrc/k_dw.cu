@@ -176,10 +176,9 @@ __global__ void __launch_bounds__(256, DwWeights<K, S>::MIN_BLOCKS) dw_row_kerne
                 for (int j = 0; j < DW_RUN; j++) {
                     if (!(cols >> (j * S + kx) & 1u)) continue;
                     const float4 q = win[j * S + kx];
-                    v[j].x = ffma(g.x, q.x, v[j].x);
-                    v[j].y = ffma(g.y, q.y, v[j].y);
-                    v[j].z = ffma(g.z, q.z, v[j].z);
-                    v[j].w = ffma(g.w, q.w, v[j].w);
+                    const float2 lo = ffma2(make_float2(g.x, g.y), make_float2(q.x, q.y), make_float2(v[j].x, v[j].y));
+                    const float2 hi = ffma2(make_float2(g.z, g.w), make_float2(q.z, q.w), make_float2(v[j].z, v[j].w));
+                    v[j] = make_float4(lo.x, lo.y, hi.x, hi.y);
                 }
             }
         }

@@ -434,12 +434,22 @@ __global__ void __launch_bounds__(128) stem_kernel(const ConvArgs a) {
 // A 3x3 stride-2 RGB stem by row segments: a block computes STEM_SEG
 // consecutive outputs of one output row (grid y: the row over all lanes,
 // grid x: the segment). The three input rows under the segment are staged
-// in shared memory with coalesced loads (zeros outside the image), each
-// thread computes NB / 2 outputs of one pixel (bias first, then the 27 terms
-// in increasing k = (ky * 3 + kx) * 3 + c, padded taps as zeros: the same
-// bits as stem_kernel), and the segment's outputs, contiguous in the packed
-// output, leave through shared memory as coalesced 16-byte stores.
+// in shared memory with coalesced loads (zeros outside the image; each row
+// padded to a multiple of four floats, so that a pixel's nine values of a
+// kernel row read as four 8-byte loads and one 4-byte load, conflict free),
+// each thread computes STEM_CH channels of one or two pixels (stem_px; bias
+// first, then the 27 terms in increasing k = (ky * 3 + kx) * 3 + c, padded
+// taps as zeros: the same bits as stem_kernel; the channel pairs go through
+// packed FMAs), and the segment's
+// outputs, contiguous in the packed output, leave through shared memory as
+// coalesced 16-byte stores.
 constexpr int STEM_SEG = 128;
+constexpr int STEM_CH = 12;  // channels per thread
+// Pixels per thread: two for the 48-channel stem (a weight float4 then
+// serves both), one for the 24-channel one (which measured faster with 256
+// threads a block than with 128); 256 threads either way.
+__host__ __device__ constexpr int stem_px(int nb) { return nb >= 48 ? 2 : 1; }
+__host__ __device__ constexpr int stem_threads(int nb) { return STEM_SEG / stem_px(nb) * (nb / STEM_CH); }
 
 template <int N, int ACT, bool QUICK>
 __device__ __forceinline__ void stem_activate(const float acc[N], float *out) {
@@ -452,12 +462,15 @@ __device__ __forceinline__ void stem_activate(const float acc[N], float *out) {
 
 template <int NB, bool QUICK>
 __global__ void __launch_bounds__(256) stem_rows_kernel(const ConvArgs a) {
-    constexpr int SPAN = 2 * STEM_SEG + 1;  // staged input columns
-    constexpr int OS = NB + 4;              // padded smem output row (conflict-free 16-byte stores)
-    constexpr int HALF = NB / 2;
+    static_assert(NB % STEM_CH == 0, "whole channel groups");
+    constexpr int PX = stem_px(NB), THREADS = stem_threads(NB);
+    constexpr int SPAN = 2 * STEM_SEG + 1;        // staged input columns
+    constexpr int RF = 3 * SPAN;                  // floats of one staged row
+    constexpr int RS = (RF + 3) / 4 * 4;          // padded row stride
+    constexpr int OS = NB + 4;                    // padded smem output row (conflict-free 16-byte stores)
     __shared__ __align__(16) float ws[27 * NB];
     __shared__ float bs[NB];
-    __shared__ float xin[3 * SPAN * 3];
+    __shared__ __align__(16) float xin[3 * RS];
     __shared__ __align__(16) float yout[STEM_SEG * OS];
     const int tid = threadIdx.x;
     const LaneInfo &L = a.lanes[find_row_lane(a.lanes, a.nl, blockIdx.y)];
@@ -466,13 +479,13 @@ __global__ void __launch_bounds__(256) stem_rows_kernel(const ConvArgs a) {
     const int ox0 = int(blockIdx.x) * STEM_SEG;
     if (ox0 >= ow) return;  // a narrower lane's row
     const int cnt = ow - ox0 < STEM_SEG ? ow - ox0 : STEM_SEG;
-    for (int e = tid; e < 27 * NB; e += 256) ws[e] = __ldg(a.w + e);
-    for (int e = tid; e < NB; e += 256) bs[e] = a.b ? __ldg(a.b + e) : 0.0f;
+    for (int e = tid; e < 27 * NB; e += THREADS) ws[e] = __ldg(a.w + e);
+    for (int e = tid; e < NB; e += THREADS) bs[e] = a.b ? __ldg(a.b + e) : 0.0f;
     const float *xl = a.src[0].p + __ldg(&L.ipix0) * 3;
     const int iy0 = oy * 2 - a.pt, ix0 = ox0 * 2 - a.pl;
-    // each staged row is one run of 3 * SPAN floats of the input row (zeros
-    // outside the image): all twelve loads of a thread in flight at once
-    constexpr int RF = 3 * SPAN, PER = (RF + 255) / 256;
+    // each staged row is one run of RF floats of the input row (zeros
+    // outside the image): all of a thread's loads in flight at once
+    constexpr int PER = (RF + THREADS - 1) / THREADS;
     const int lo = (ix0 < 0 ? -ix0 : 0) * 3, hi = (iw - ix0 < SPAN ? iw - ix0 : SPAN) * 3;
     float v[3][PER];
 #pragma unroll
@@ -481,7 +494,7 @@ __global__ void __launch_bounds__(256) stem_rows_kernel(const ConvArgs a) {
         const float *src = xl + ((long)(iy0 + r) * iw + ix0) * 3;
 #pragma unroll
         for (int u = 0; u < PER; u++) {
-            const int j = tid + u * 256;
+            const int j = tid + u * THREADS;
             v[r][u] = (row_ok && j >= lo && j < hi) ? __ldg(src + j) : 0.0f;
         }
     }
@@ -489,52 +502,73 @@ __global__ void __launch_bounds__(256) stem_rows_kernel(const ConvArgs a) {
     for (int r = 0; r < 3; r++)
 #pragma unroll
         for (int u = 0; u < PER; u++) {
-            const int j = tid + u * 256;
-            if (j < RF) xin[r * RF + j] = v[r][u];
+            const int j = tid + u * THREADS;
+            if (j < RS) xin[r * RS + j] = j < RF ? v[r][u] : 0.0f;
         }
     __syncthreads();
-    const int p = tid % STEM_SEG, h = tid / STEM_SEG;
-    if (p < cnt) {
-        float in[27];
+    constexpr int GAP = STEM_SEG / PX;  // a thread's pixels: q, q + GAP, ...
+    const int q = tid % GAP, g = tid / GAP;
+    if (q < cnt) {
+        float acc[PX][STEM_CH];
 #pragma unroll
-        for (int ky = 0; ky < 3; ky++)
+        for (int i = 0; i < PX; i++)
 #pragma unroll
-            for (int kx = 0; kx < 3; kx++)
+            for (int j = 0; j < STEM_CH; j++) acc[i][j] = bs[g * STEM_CH + j];
 #pragma unroll
-                for (int c = 0; c < 3; c++) in[(ky * 3 + kx) * 3 + c] = xin[(ky * SPAN + 2 * p + kx) * 3 + c];
-        float acc[HALF];
+        for (int ky = 0; ky < 3; ky++) {
+            // the nine values (kx, c) of kernel row ky under each pixel
+            float in[PX][9];
 #pragma unroll
-        for (int j = 0; j < HALF; j++) acc[j] = bs[h * HALF + j];
+            for (int i = 0; i < PX; i++) {
+                const float *r = xin + ky * RS + 6 * (q + i * GAP);
 #pragma unroll
-        for (int k = 0; k < 27; k++) {
-            const float2 xk = make_float2(in[k], in[k]);
+                for (int e = 0; e < 8; e += 2) {
+                    const float2 t = *reinterpret_cast<const float2 *>(r + e);
+                    in[i][e] = t.x;
+                    in[i][e + 1] = t.y;
+                }
+                in[i][8] = r[8];
+            }
 #pragma unroll
-            for (int j = 0; j < HALF; j += 4) {
-                const float4 w4 = *reinterpret_cast<const float4 *>(ws + k * NB + h * HALF + j);  // broadcast
-                const float2 lo = ffma2(make_float2(w4.x, w4.y), xk, make_float2(acc[j], acc[j + 1]));
-                const float2 hi = ffma2(make_float2(w4.z, w4.w), xk, make_float2(acc[j + 2], acc[j + 3]));
-                acc[j] = lo.x;
-                acc[j + 1] = lo.y;
-                acc[j + 2] = hi.x;
-                acc[j + 3] = hi.y;
+            for (int t = 0; t < 9; t++) {
+                const int k = ky * 9 + t;
+#pragma unroll
+                for (int j = 0; j < STEM_CH; j += 4) {
+                    const float4 w4 = *reinterpret_cast<const float4 *>(ws + k * NB + g * STEM_CH + j);  // broadcast
+                    const float2 wa = make_float2(w4.x, w4.y), wb = make_float2(w4.z, w4.w);
+#pragma unroll
+                    for (int i = 0; i < PX; i++) {
+                        const float2 xv = make_float2(in[i][t], in[i][t]);
+                        float2 r = ffma2(wa, xv, make_float2(acc[i][j], acc[i][j + 1]));
+                        acc[i][j] = r.x;
+                        acc[i][j + 1] = r.y;
+                        r = ffma2(wb, xv, make_float2(acc[i][j + 2], acc[i][j + 3]));
+                        acc[i][j + 2] = r.x;
+                        acc[i][j + 3] = r.y;
+                    }
+                }
             }
         }
-        float *out = yout + p * OS + h * HALF;
         // one branch on the activation per thread, not per value
-        switch (a.act) {
-        case 1: stem_activate<HALF, 1, QUICK>(acc, out); break;
-        case 2: stem_activate<HALF, 2, QUICK>(acc, out); break;
-        case 3: stem_activate<HALF, 3, QUICK>(acc, out); break;
-        case 4: stem_activate<HALF, 4, QUICK>(acc, out); break;
-        case 5: stem_activate<HALF, 5, QUICK>(acc, out); break;
-        case 6: stem_activate<HALF, 6, QUICK>(acc, out); break;
-        case 7: stem_activate<HALF, 7, QUICK>(acc, out); break;
-        default: stem_activate<HALF, 0, QUICK>(acc, out); break;
+#pragma unroll
+        for (int i = 0; i < PX; i++) {
+            if (q + i * GAP >= cnt) break;
+            float *out = yout + (q + i * GAP) * OS + g * STEM_CH;
+            switch (a.act) {
+            case 1: stem_activate<STEM_CH, 1, QUICK>(acc[i], out); break;
+            case 2: stem_activate<STEM_CH, 2, QUICK>(acc[i], out); break;
+            case 3: stem_activate<STEM_CH, 3, QUICK>(acc[i], out); break;
+            case 4: stem_activate<STEM_CH, 4, QUICK>(acc[i], out); break;
+            case 5: stem_activate<STEM_CH, 5, QUICK>(acc[i], out); break;
+            case 6: stem_activate<STEM_CH, 6, QUICK>(acc[i], out); break;
+            case 7: stem_activate<STEM_CH, 7, QUICK>(acc[i], out); break;
+            default: stem_activate<STEM_CH, 0, QUICK>(acc[i], out); break;
+            }
         }
     }
     __syncthreads();
     float *dst = a.y + (__ldg(&L.pix0) + (long)oy * ow + ox0) * NB;
-    for (int e = tid; e < cnt * (NB / 4); e += 256) {
+    for (int e = tid; e < cnt * (NB / 4); e += THREADS) {
         const int px = e / (NB / 4), c4 = e - px * (NB / 4);
         reinterpret_cast<float4 *>(dst)[e] = *reinterpret_cast<const float4 *>(yout + px * OS + 4 * c4);
     }
@@ -543,10 +577,11 @@ __global__ void __launch_bounds__(256) stem_rows_kernel(const ConvArgs a) {
 template <int NB>
 void run_stem_rows(const ConvArgs &a, cudaStream_t s) {
     const dim3 grid(unsigned((a.max_ow + STEM_SEG - 1) / STEM_SEG), unsigned(a.out_rows));
+    constexpr int THREADS = stem_threads(NB);
     if (a.quick)
-        stem_rows_kernel<NB, true><<<grid, 256, 0, s>>>(a);
+        stem_rows_kernel<NB, true><<<grid, THREADS, 0, s>>>(a);
     else
-        stem_rows_kernel<NB, false><<<grid, 256, 0, s>>>(a);
+        stem_rows_kernel<NB, false><<<grid, THREADS, 0, s>>>(a);
 }
 
 template <int TM, int TN, int TX, int TY, int BK>

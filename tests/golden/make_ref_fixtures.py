@@ -1,6 +1,6 @@
 """Copy the reference's own parity fixtures into tests/golden/ref/.
 
-    python tests/golden/make_ref_fixtures.py [REFERENCE_ROOT]
+    python tests/golden/make_ref_fixtures.py REFERENCE_ROOT
 
 ppocr-native's `tests/fixtures/` holds the outputs of the libraries its host
 page steps reproduce (OpenCV 5.0, pyclipper 1.4, RapidOCR 3.9, numpy 2.5),
@@ -36,4 +36,6 @@ def main(root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_ref_fixtures.py REFERENCE_ROOT")
+    main(sys.argv[1])

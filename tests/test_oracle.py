@@ -402,6 +402,19 @@ def test_timed_path_gives_the_plain_loops_bits(oracle_mod):
              (synth.rec_plan(seed=3, std=None, vocab=700), (48, 328)),
              (synth.rec_plan(seed=3, std=None, vocab=300, logits=True), (48, 100)),
              (synth.fused_layer_plan(seed=0, h=23, w=31), (23, 31))]
+    # dense convolutions whose widths reach the 16- and 8-column tiles (the
+    # networks' widths are all multiples of 24), bias first and last, one
+    # over a second input, one strided
+    h, w, c1, c2 = 13, 29, 5, 7
+    for oc, fused, two, stride in [(40, "swish", False, 1), (32, "relu", True, 1), (16, "none", False, 2)]:
+        taps, ch = 9, c1 + (c2 if two else 0)
+        first = window(Op("conv", x=0, y=1, ic=c1, oc=c2, w=(0, c1 * c2), b=(c1 * c2, c2)), (1, 1), 1, 0, 0)
+        at = c1 * c2 + c2
+        conv = window(Op("conv", x=0, y=2, ic=c1, oc=oc, fused=fused, x2=1 if two else 0, n2=c2 if two else 0),
+                      (3, 3), stride, 1, 1)
+        conv.w, conv.b = (at, taps * ch * oc), (at + taps * ch * oc, oc)
+        weights = noise(at + taps * ch * oc + oc, 9 + oc, 0.4)
+        cases.append((encode((0, h, w, c1), 3, [2], [first, conv], weights), (h, w)))
     for oc, fused in [(1, "sigmoid"), (4, "relu"), (8, "swish")]:  # 4-, 16- and 32-column blocks
         w = noise(5 * 4 * oc, 3, 0.5)
         bias = noise(4 * oc, 4, 0.5)

@@ -7,6 +7,8 @@
 // as Rust's std calls them.
 #include "page.hpp"
 
+#include <emmintrin.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -49,6 +51,20 @@ inline uint64_t nonzero_bytes(uint64_t w) { return (w + 0x7f7f7f7f7f7f7f7full) &
 // and after `end`.
 size_t next_start(const uint8_t *row, size_t from, size_t end) {
     size_t i = from;
+    // sixteen at a time (SSE2, every x86-64): a byte's nonzero bit from a
+    // compare with zero, the same test as below
+    const __m128i zero = _mm_setzero_si128();
+    while (i + 16 <= end) {
+        const __m128i w = _mm_loadu_si128(reinterpret_cast<const __m128i *>(row + i));
+        const __m128i wl = _mm_loadu_si128(reinterpret_cast<const __m128i *>(row + i - 1));
+        const __m128i wr = _mm_loadu_si128(reinterpret_cast<const __m128i *>(row + i + 1));
+        const unsigned nz = ~unsigned(_mm_movemask_epi8(_mm_cmpeq_epi8(w, zero))) & 0xffffu;
+        const unsigned nzl = ~unsigned(_mm_movemask_epi8(_mm_cmpeq_epi8(wl, zero))) & 0xffffu;
+        const unsigned nzr = ~unsigned(_mm_movemask_epi8(_mm_cmpeq_epi8(wr, zero))) & 0xffffu;
+        const unsigned cand = nz & ~(nzl & nzr);
+        if (cand) return i + size_t(__builtin_ctz(cand));
+        i += 16;
+    }
     while (i + 9 <= end + 1) {
         uint64_t w, wl, wr;
         std::memcpy(&w, row + i, 8);

@@ -133,10 +133,13 @@ void find_contours(const uint8_t *mask, size_t width, size_t height, Contours &o
                     corners.push_back(point(start));
                 } else {
                     const size_t last = start + off[last_dir];
-                    s.chain_at.clear();
-                    s.chain_dir.clear();
-                    size_t cur = start;
-                    int back = last_dir;
+                    // CHAIN_APPROX_SIMPLE on the fly: a point is kept where
+                    // the step leaving it turns from the step before; the
+                    // first point's turn (against the last step) is known at
+                    // the end, and it then leads the list
+                    const size_t at = corners.size();
+                    size_t cur = start, first_at = start;
+                    int back = last_dir, first_dir = -1, prev_dir = -1;
                     for (;;) {
                         bool east_bg = false;
                         int next_dir = back;
@@ -152,26 +155,19 @@ void find_contours(const uint8_t *mask, size_t width, size_t height, Contours &o
                             state[cur] = MARKED_EAST;
                         else if (state[cur] == UNSEEN)
                             state[cur] = MARKED;
-                        s.chain_at.push_back(cur);
-                        s.chain_dir.push_back(uint8_t(next_dir));
+                        if (first_dir < 0) {
+                            first_dir = next_dir;
+                            first_at = cur;
+                        } else if (next_dir != prev_dir) {
+                            corners.push_back(point(cur));
+                        }
+                        prev_dir = next_dir;
                         const size_t next = cur + off[next_dir];
                         if (next == start && cur == last) break;
                         back = (next_dir + 4) & 7;
                         cur = next;
                     }
-                    const size_t n = s.chain_at.size();
-                    const auto turns = [&](size_t i) { return s.chain_dir[i] != s.chain_dir[(i + n - 1) % n]; };
-                    size_t first = 0;
-                    for (size_t i = 0; i < n; i++)
-                        if (turns(i)) {
-                            first = i;
-                            break;
-                        }
-                    const size_t at = corners.size();
-                    for (size_t j = 0; j < n; j++) {
-                        const size_t i = (first + j) % n;
-                        if (turns(i)) corners.push_back(point(s.chain_at[i]));
-                    }
+                    if (first_dir != prev_dir) corners.insert(corners.begin() + long(at), point(first_at));
                     found.emplace_back(at, corners.size() - at);
                 }
             }

@@ -34,11 +34,9 @@ struct Contours {
     size_t len(size_t i) const { return start[i + 1] - start[i]; }
 };
 
-// Scan state reused between calls (the frame of background and the chain).
+// Scan state reused between calls (the image inside a frame of background).
 struct ContourScratch {
     std::vector<uint8_t> state;
-    std::vector<size_t> chain_at;
-    std::vector<uint8_t> chain_dir;
 };
 
 void find_contours(const uint8_t *mask, size_t width, size_t height, Contours &out, ContourScratch &scratch);

@@ -104,6 +104,20 @@ def test_contours_and_boxes_match_the_oracle(oracle_mod, seed):
         assert cuda.contour_mean(prob, c) == oracle_mod.contour_mean(prob, c)
 
 
+@pytest.mark.parametrize("seed", range(6))
+def test_wide_mask_contours_match_the_oracle(oracle_mod, seed):
+    """Rows long enough for the sixteen-byte start scan, with borders at
+    every offset within a block and at the row ends: blobs, a checkerboard,
+    all foreground, single rows and columns."""
+    rng = np.random.default_rng(200 + seed)
+    h, w = int(rng.integers(1, 40)), int(rng.integers(16, 700))
+    masks = [blob_mask(rng, h, w, int(rng.integers(1, 12))), np.ones((h, w), np.uint8),
+             (np.indices((h, w)).sum(axis=0) % 2).astype(np.uint8), np.ones((1, w), np.uint8),
+             np.ones((h, 1), np.uint8), (rng.random((h, w)) < 0.5).astype(np.uint8)]
+    for m in masks:
+        assert cuda.find_contours(m) == oracle_mod.find_contours(m)
+
+
 @pytest.mark.parametrize("seed", range(8))
 def test_geometry_matches_the_oracle(oracle_mod, seed):
     rng = np.random.default_rng(100 + seed)

@@ -1075,7 +1075,12 @@ static inline __attribute__((always_inline)) void head_panel(const float *panel,
         __m256 second = _mm256_cmp_ps(a1, a0, _CMP_GT_OQ);
         __m256 top = _mm256_blendv_ps(a1, a0, _mm256_cmp_ps(a0, a1, _CMP_GT_OQ));
         __m256 grown = _mm256_blendv_ps(top, mm, _mm256_cmp_ps(mm, top, _CMP_GT_OQ));
-        __m256 sn = _mm256_mul_ps(sum, exp_neg8(_mm256_sub_ps(mm, grown)));
+        /* where no lane's maximum moved (and each is finite) the rescale is
+         * exp_neg(+-0) = 1 exactly, so the sum is kept as it is */
+        const __m256 kept = _mm256_and_ps(_mm256_cmp_ps(grown, mm, _CMP_EQ_OQ),
+                                          _mm256_cmp_ps(_mm256_andnot_ps(_mm256_set1_ps(-0.0f), mm),
+                                                        _mm256_set1_ps(INFINITY), _CMP_LT_OQ));
+        __m256 sn = _mm256_movemask_ps(kept) == 0xff ? sum : _mm256_mul_ps(sum, exp_neg8(_mm256_sub_ps(mm, grown)));
         sn = _mm256_add_ps(sn, exp_neg8(_mm256_sub_ps(a0, grown)));
         sn = _mm256_add_ps(sn, exp_neg8(_mm256_sub_ps(a1, grown)));
         __m256 c = _mm256_add_ps(col, _mm256_and_ps(second, _mm256_set1_ps(8.0f)));
